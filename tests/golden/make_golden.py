@@ -1,0 +1,173 @@
+"""Generate golden fixtures from the reference ThetaScan package.
+
+Run in the build container, where the reference project is importable:
+
+    PYTHONPATH=<reference>/src python tests/golden/make_golden.py <out_dir>
+
+It writes ``scan_cases.pt``, ``feature_cases.pt`` and ``mixer_cases.pt`` into
+``<out_dir>`` (default: this directory).  Everything is computed by the
+reference's own public module and core ops in float64 with fixed seeds, so the
+fixtures pin both the CPU oracle (``oracle/``) and the CUDA path.  The GPU box
+never runs this script; it only reads the fixtures.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import torch
+
+
+def _seeded(seed, *shape, dtype=torch.float64):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g, dtype=dtype)
+
+
+def scan_cases():
+    from thetascan._core.ops import scan_chunk, scan_cumsum, scan_naive
+
+    cases = []
+    B, H, T, Dk, Dv = 2, 3, 37, 5, 4
+    q, k, v = (_seeded(s, B, H, T, d) for s, d in ((1, Dk), (2, Dk), (3, Dv)))
+    log_alpha = torch.tensor([-0.05, -0.4, -2.0], dtype=torch.float64)
+    stream = -_seeded(4, B, H, T, 1).abs() * 0.3
+    for name, retention in (("sum", None), ("static", log_alpha), ("stream", stream)):
+        leaves = [x.clone().requires_grad_(True) for x in (q, k, v)]
+        ret = None if retention is None else retention.clone().requires_grad_(True)
+        if retention is None:
+            out = scan_chunk.linattn(*leaves, chunk=8)
+        elif retention.ndim == 1:
+            out = scan_chunk.linattn(*leaves, chunk=8, log_alpha=ret)
+        else:
+            out = scan_chunk.linattn(*leaves, ret, chunk=8)
+        out.square().sum().backward()
+        naive = scan_naive.linattn(q, k, v, None if retention is None else (
+            retention.view(1, H, 1, 1).expand(B, H, T, 1) if retention.ndim == 1 else retention))
+        cases.append({
+            "name": name, "q": q, "k": k, "v": v, "retention": retention, "chunk": 8,
+            "out": out.detach(), "naive": naive,
+            "grads": [x.grad for x in leaves] + [None if ret is None else ret.grad],
+        })
+    cumsum = scan_cumsum.linattn(q, k, v)
+    views = scan_chunk.linattn_views(q, k, v, (None, log_alpha, log_alpha * 3.0), chunk=16)
+    return {"cases": cases, "cumsum_sum": cumsum, "views": views,
+            "views_inputs": (q, k, v, log_alpha)}
+
+
+def feature_cases():
+    from thetascan._core.ops import kernel_features as kf
+
+    pre = _seeded(10, 2, 3, 17, 16)
+    thr = torch.tensor([0.0, 0.3, -0.2], dtype=torch.float64)
+    bias = _seeded(11, 3, 16) * 0.1
+    gain = torch.tensor([8.0, 4.0, 12.0], dtype=torch.float64)
+    spline_pre = _seeded(12, 2, 3, 17, 4) * 2.0
+    edge = torch.tensor([-3.5, -3.0, -1.0, 0.0, 1e-9, 1.0, 2.999, 3.0, 7.0], dtype=torch.float64)
+    return {
+        "pre": pre, "thr": thr, "bias": bias, "gain": gain, "spline_pre": spline_pre, "edge": edge,
+        "relu2": kf.relu2_ridge_features(pre, score_bias=None, relu2_threshold=thr, eps=1e-6),
+        "relu2_bias": kf.relu2_ridge_features(pre, score_bias=bias, eps=1e-6),
+        "relu2_dead": kf.relu2_ridge_features(-pre.abs() - 1.0, score_bias=None, eps=1e-6),
+        "softmax": kf.softmax_partition_features(
+            pre, gain=gain, fallback_gain=8.0, score_bias=bias, sparsity="none",
+            relative_threshold=None, threshold_temperature=0.25, eps=1e-6),
+        "bspline": kf.projected_bspline_features(
+            spline_pre, n_basis=8, degree=3, bound=3.0, scale=None, fallback_scale=1.0),
+        "bspline16": kf.projected_bspline_features(
+            spline_pre, n_basis=16, degree=3, bound=3.0, scale=None, fallback_scale=1.0),
+        "bspline_edge": kf.open_uniform_bspline_basis(edge, n_basis=8, degree=3, bound=3.0),
+    }
+
+
+MIXER_CONFIGS = {
+    # Config-1 family at a fixture-sized shape: softmax partition, bank (fast).
+    "softmax_bank_fast": dict(
+        d_model=64, n_heads=2, memory_multiplier=1, family="kernel",
+        kernel=dict(feature_map="softmax_partition"),
+        temporal=dict(mode="bank", retention_init=0.95), B=2, T=40),
+    # Config-2 family: relu2 ridge, 2x expansion, partial RoPE, bank.
+    "relu2_expanded_rope": dict(
+        d_model=64, n_heads=2, memory_multiplier=4, feature_expansion=2, family="kernel",
+        kernel=dict(feature_map="relu2_ridge", relu2_threshold_mode="learned_per_head"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", recency_branches=2,
+                                                               retention_inits=(0.9, 0.99)),
+        B=2, T=40),
+    # Config-4 family: projected B-spline with a stale bank.
+    "bspline_stale": dict(
+        d_model=64, n_heads=2, memory_multiplier=2, family="kernel",
+        kernel=dict(feature_map="projected_bspline", bspline_basis_count=16),
+        temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=2, T=40),
+    # Plain sum with per-feature mass normalization.
+    "softmax_sum_feature_mass": dict(
+        d_model=64, n_heads=2, memory_multiplier=1, family="kernel",
+        kernel=dict(feature_map="softmax_partition", read_normalization="feature_mass"),
+        B=2, T=40),
+    # Kernel-tile-shaped case (head_dim 64, ragged T) for the CUDA path.
+    "relu2_d64_ragged": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, family="kernel",
+        kernel=dict(feature_map="relu2_ridge"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32"),
+}
+
+
+def mixer_cases():
+    from thetascan import (KernelConfig, RoPEConfig, TemporalConfig, ThetaScan,
+                           ThetaScanConfig)
+
+    out = {}
+    for name, spec in MIXER_CONFIGS.items():
+        spec = dict(spec)
+        B, T = spec.pop("B"), spec.pop("T")
+        dtype = getattr(torch, spec.pop("dtype", "float64"))
+        kernel = KernelConfig(**spec.pop("kernel", {}))
+        rope = RoPEConfig(**spec.pop("rope", {}))
+        temporal = TemporalConfig(**spec.pop("temporal", {}))
+        cfg = ThetaScanConfig(kernel=kernel, rope=rope, temporal=temporal, **spec)
+        torch.manual_seed(0)
+        module = ThetaScan(cfg).to(torch.float64)
+        core = module._core
+        # Nonzero W2 and blends so every branch of the read carries gradient.
+        with torch.no_grad():
+            for p in core.W2:
+                p.copy_(_seeded(5, *p.shape) * 0.2)
+            if core.fade_eta is not None:
+                core.fade_eta.copy_(_seeded(6, *core.fade_eta.shape) * 0.5)
+            if getattr(core, "kernel_relu2_threshold", None) is not None:
+                core.kernel_relu2_threshold.copy_(_seeded(7, *core.kernel_relu2_threshold.shape) * 0.1)
+        x = _seeded(8, B, T, cfg.d_model).requires_grad_(True)
+        y = module(x)
+        weight = _seeded(9, *y.shape)
+        (y * weight).sum().backward()
+        params = {n: t.detach().to(dtype) for n, t in core.state_dict(keep_vars=True).items()
+                  if t is not None}
+        for n, buf in core.named_buffers():
+            if buf is not None and n not in params:
+                params[n] = buf.detach().to(dtype)
+        grads = {n: p.grad.detach().to(dtype) for n, p in core.named_parameters() if p.grad is not None}
+        core_cfg = module._core_config
+        out[name] = {
+            "public_config": cfg.to_dict(), "B": B, "T": T,
+            "core": {k: getattr(core_cfg, k) for k in (
+                "d_model", "n_heads", "head_dim", "mem_hidden", "feature_expansion", "expansion_key",
+                "kernel_kind", "softmax_gain", "bspline_basis_count", "bspline_bound", "bspline_scale",
+                "rope", "rope_frac", "rope_base", "read_fade", "read_fade_mode", "fade_blend_mode",
+                "read_norm", "read_norm_mode", "eps", "scan_chunk", "share_kq", "key_value_heads")},
+            "params": params, "x": x.detach().to(dtype), "y": y.detach().to(dtype),
+            "out_weight": weight.to(dtype), "x_grad": x.grad.detach().to(dtype), "grads": grads,
+        }
+    return out
+
+
+def main():
+    target = sys.argv[1] if len(sys.argv) > 1 else os.path.dirname(os.path.abspath(__file__))
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    torch.save(scan_cases(), os.path.join(target, "scan_cases.pt"))
+    torch.save(feature_cases(), os.path.join(target, "feature_cases.pt"))
+    torch.save(mixer_cases(), os.path.join(target, "mixer_cases.pt"))
+    print("golden fixtures written to", target)
+
+
+if __name__ == "__main__":
+    main()
