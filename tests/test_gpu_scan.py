@@ -1,0 +1,194 @@
+"""GPU parity of the tensor-core building blocks and the multi-view scan.
+
+The CUDA path is checked against the float64 CPU oracle (``oracle.scan``),
+which is itself pinned to the reference by tests/test_oracle_golden.py.
+Tolerance (SURVEY parity gate, bf16 streams with f32 state):
+``max|got - ref| / max|ref| <= 2e-2`` on outputs and gradients.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import pytest
+import torch
+
+from oracle import scan as oscan
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 2e-2
+
+
+def rel_err(got, want):
+    got = got.detach().to("cpu", torch.float64)
+    want = want.detach().to("cpu", torch.float64)
+    scale = want.abs().max().clamp_min(1e-30)
+    return float((got - want).abs().max() / scale)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from thetascan_b200 import _lib
+    return _lib
+
+
+# ----------------------------------------------------------------- tcgen05 self-test
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("N,K", [(16, 16), (64, 64), (80, 128), (128, 256), (256, 64), (144, 32)])
+def test_tcgen05_tile_product_matches_matmul(lib, a_mn, b_mn, N, K):
+    g = torch.Generator(device="cuda").manual_seed(N * 1000 + K)
+    A = torch.randn(128, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(K, N, device="cuda", generator=g).to(torch.bfloat16)
+    D = torch.empty(128, N, device="cuda", dtype=torch.float32)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lib.check(lib.load().ts_b200_selftest_mma(A.data_ptr(), B.data_ptr(), D.data_ptr(), N, K, a_mn, b_mn, s))
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    want = A.double() @ B.double()
+    assert rel_err(D, want) < 1e-3
+
+
+# ----------------------------------------------------------------- scan forward/backward
+
+def _streams(B, H, T, Dk, Dv, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(B, H, T, Dk, generator=g) / math.sqrt(Dk)).to(torch.bfloat16)
+    k = (torch.randn(B, H, T, Dk, generator=g) / math.sqrt(Dk)).to(torch.bfloat16)
+    v = torch.randn(B, H, T, Dv, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+def _alphas(H, lo, hi, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.log(lo + (hi - lo) * torch.rand(H, generator=g, dtype=torch.float64)).to(torch.float32)
+
+
+CASES = [
+    # B, H, T,   Dk,  Dv, n_decayed_views, with_sum
+    (2, 3, 37, 5, 4, 1, True),
+    (1, 2, 128, 64, 64, 1, True),
+    (2, 2, 300, 64, 65, 2, True),
+    (1, 2, 520, 128, 80, 3, True),
+    (1, 2, 384, 256, 64, 1, True),
+    (1, 1, 1030, 32, 16, 1, False),
+]
+
+
+def _retentions(H, n_decayed, with_sum):
+    rets = [None] if with_sum else []
+    for j in range(n_decayed):
+        rets.append(_alphas(H, 0.85 + 0.04 * j, 0.999, seed=j))
+    return rets
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_scan_forward_matches_oracle(lib, case):
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv, nd, with_sum = case
+    q, k, v = _streams(B, H, T, Dk, Dv)
+    rets = _retentions(H, nd, with_sum)
+    got = scan.linattn_views(q.cuda(), k.cuda(), v.cuda(), tuple(None if r is None else r.cuda() for r in rets),
+                             chunk=64)
+    want = oscan.linattn_chunk_views(q.double(), k.double(), v.double(),
+                                     tuple(None if r is None else r.double() for r in rets), chunk=64)
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for g_, w_ in zip(got, want):
+        assert g_.dtype == torch.bfloat16 and g_.shape == w_.shape
+        assert rel_err(g_, w_) < BF16_TOL
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_scan_backward_matches_oracle(lib, case):
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv, nd, with_sum = case
+    q, k, v = _streams(B, H, T, Dk, Dv, seed=1)
+    rets = _retentions(H, nd, with_sum)
+    g = torch.Generator().manual_seed(7)
+    weights = [torch.randn(B, H, T, Dv, generator=g, dtype=torch.float64) for _ in rets]
+
+    def run(qq, kk, vv, rr, fn):
+        outs = fn(qq, kk, vv, rr)
+        return sum((o.double() * w.to(o.device)).sum() for o, w in zip(outs, weights))
+
+    leaves = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    rleaves = [None if r is None else r.cuda().requires_grad_(True) for r in rets]
+    run(*leaves, tuple(rleaves), lambda a, b, c, r: scan.linattn_views(a, b, c, r, chunk=64)).backward()
+    oleaves = [x.double().requires_grad_(True) for x in (q, k, v)]
+    orets = [None if r is None else r.double().requires_grad_(True) for r in rets]
+    run(*oleaves, tuple(orets), lambda a, b, c, r: oscan.linattn_chunk_views(a, b, c, r, chunk=64)).backward()
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for name, got, want in zip("qkv", leaves, oleaves):
+        assert rel_err(got.grad, want.grad) < BF16_TOL, name
+    for got, want in zip(rleaves, orets):
+        if got is not None:
+            assert rel_err(got.grad, want.grad) < BF16_TOL
+
+
+def test_scan_append_unit_equals_explicit_unit_column(lib):
+    from thetascan_b200 import scan
+    q, k, v = (x.cuda() for x in _streams(1, 2, 200, 64, 64, seed=3))
+    la = _alphas(2, 0.9, 0.99, seed=4).cuda()
+    fused = scan.linattn_views(q, k, v, (None, la), append_unit=True)
+    unit = torch.cat([v, torch.ones_like(v[..., :1])], dim=-1)
+    explicit = scan.linattn_views(q, k, unit, (None, la))
+    for a, b in zip(fused, explicit):
+        assert torch.equal(a, b)
+
+
+def test_geometric_series_known_answer(lib):
+    """All-ones stream: out_t = (1 - alpha^(t+1)) / (1 - alpha)
+    (reference tests/test_scan_chunk.py:140-165)."""
+    from thetascan_b200 import scan
+    alpha, T = 0.9, 600
+    ones = torch.ones(1, 1, T, 1, dtype=torch.bfloat16, device="cuda")
+    la = torch.tensor([math.log(alpha)], device="cuda")
+    out = scan.linattn(ones, ones, ones, chunk=512, log_alpha=la).float().flatten().cpu()
+    pos = torch.arange(1, T + 1, dtype=torch.float64)
+    want = (1.0 - alpha ** pos) / (1.0 - alpha)
+    assert float((out - want).abs().max()) < 0.1
+
+
+def test_retention_gradient_closed_form(lib):
+    """d out_{T-1} / d log(alpha) = sum_p p alpha^p for an all-ones stream
+    (reference tests/test_scan_chunk.py:303-340)."""
+    from thetascan_b200 import scan
+    alpha, T = 0.9, 512
+    ones = torch.ones(1, 1, T, 1, dtype=torch.bfloat16, device="cuda")
+    la = torch.tensor([math.log(alpha)], device="cuda", requires_grad=True)
+    out = scan.linattn(ones, ones, ones, chunk=512, log_alpha=la)
+    out[0, 0, -1, 0].float().backward()
+    want = sum(p * alpha ** p for p in range(1, T + 1))
+    assert abs(float(la.grad) - want) / want < 5e-3
+
+
+@pytest.mark.parametrize("cut", [1, 9, 130, 200])
+def test_scan_is_exactly_causal(lib, cut):
+    """A later key or value never moves an earlier output, not even by rounding
+    (reference tests/test_scan_chunk.py:236-268)."""
+    from thetascan_b200 import scan
+    q, k, v = (x.cuda() for x in _streams(1, 2, 260, 32, 16, seed=5))
+    la = _alphas(2, 0.8, 0.95, seed=6).cuda()
+    base = scan.linattn_views(q, k, v, (None, la))
+    k2, v2 = k.clone(), v.clone()
+    k2[:, :, cut:] += 2.0
+    v2[:, :, cut:] += 2.0
+    moved = scan.linattn_views(q, k2, v2, (None, la))
+    for a, b in zip(base, moved):
+        assert torch.equal(a[:, :, :cut], b[:, :, :cut])
+
+
+def test_scan_errors_follow_the_reference_contract(lib):
+    from thetascan_b200 import scan
+    q, k, v = (x.cuda() for x in _streams(1, 2, 16, 8, 8))
+    with pytest.raises(ValueError):
+        scan.linattn(q, k, v, chunk=0)
+    with pytest.raises(ValueError):
+        scan.linattn(q, k, v, log_alpha=torch.zeros(3, device="cuda"))
+    with pytest.raises(NotImplementedError):
+        scan.linattn(q, k, v, -torch.rand(1, 2, 16, 8, device="cuda"))
+    with pytest.raises(NotImplementedError):
+        scan.linattn(q.float(), k.float(), v.float())
+    with pytest.raises(RuntimeError):
+        scan.linattn(q.cpu(), k.cpu(), v.cpu())

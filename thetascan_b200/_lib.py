@@ -1,0 +1,115 @@
+"""ctypes binding of the C ABI in ``include/thetascan_b200.h``.
+
+The shared library is built in-tree (``thetascan_b200/libthetascan_b200.so``,
+see :mod:`thetascan_b200.build`).  There is no fallback: if the library is
+missing or cannot be loaded, every CUDA entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libthetascan_b200.so")
+
+TS_OK, TS_ERR_VALUE, TS_ERR_NOT_IMPLEMENTED, TS_ERR_CUDA, TS_ERR_DEVICE = range(5)
+TS_DTYPE_F32, TS_DTYPE_BF16 = 0, 1
+MAX_RETENTIONS = 4
+
+c_int64_3 = ctypes.c_int64 * 3
+c_ptr4 = ctypes.c_void_p * MAX_RETENTIONS
+
+
+class ScanArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int),
+        ("dk", ctypes.c_int), ("dv", ctypes.c_int),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("q_strides", c_int64_3), ("k_strides", c_int64_3), ("v_strides", c_int64_3),
+        ("v_append_unit", ctypes.c_int),
+        ("n_retentions", ctypes.c_int),
+        ("log_alpha", c_ptr4),
+        ("out", c_ptr4),
+        ("out_dtype", ctypes.c_int),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class ScanGradArgs(ctypes.Structure):
+    _fields_ = [
+        ("dout", c_ptr4),
+        ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p),
+        ("grad_dtype", ctypes.c_int),
+        ("dlog_alpha", c_ptr4),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Every exported symbol declared in include/thetascan_b200.h, with its ctypes
+# signature (restype, argtypes).  tests/test_capi_symbols.py checks this table
+# against the header.
+SIGNATURES = {
+    "ts_b200_version": (ctypes.c_char_p, []),
+    "ts_b200_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
+    "ts_b200_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "ts_b200_selftest_mma": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "ts_b200_scan_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScanArgs)]),
+    "ts_b200_scan_fwd": (ctypes.c_int, [ctypes.POINTER(ScanArgs), ctypes.c_void_p]),
+    "ts_b200_scan_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScanArgs)]),
+    "ts_b200_scan_bwd": (ctypes.c_int, [ctypes.POINTER(ScanArgs), ctypes.POINTER(ScanGradArgs),
+                                        ctypes.c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class ThetaScanB200Error(RuntimeError):
+    """A CUDA-side failure reported by the library."""
+
+
+def load():
+    """Load the shared library (once) and bind every declared symbol."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"thetascan_b200: {LIB_PATH} is missing; build it with "
+                    "`python -m thetascan_b200.build` (nvcc, sm_100a)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def last_error() -> tuple[int, str]:
+    buf = ctypes.create_string_buffer(512)
+    code = load().ts_b200_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(code: int) -> None:
+    """Raise the Python exception matching a nonzero return code."""
+    if code == TS_OK:
+        return
+    _, message = last_error()
+    if code == TS_ERR_VALUE:
+        raise ValueError(message)
+    if code == TS_ERR_NOT_IMPLEMENTED:
+        raise NotImplementedError(message)
+    raise ThetaScanB200Error(message)
+
+
+def device_status(stream_handle: int) -> int:
+    """Synchronize the stream and return (and clear) the device status word."""
+    status = ctypes.c_int(0)
+    code = load().ts_b200_device_status(stream_handle, ctypes.byref(status))
+    if code not in (TS_OK, TS_ERR_DEVICE):
+        check(code)
+    return status.value

@@ -1,0 +1,6 @@
+// Single translation unit for the shared library: the kernels reference one
+// device-status word, so they are compiled together (no relocatable device code).
+#include "capi.cu"
+#include "selftest.cu"
+#include "scan_fwd.cu"
+#include "scan_bwd.cu"

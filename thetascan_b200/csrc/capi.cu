@@ -1,0 +1,183 @@
+// C-ABI entry points: argument validation, workspace sizing and launches.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "capi_internal.h"
+#include "scan.cuh"
+
+namespace ts {
+
+namespace {
+thread_local int g_last_code = TS_OK;
+thread_local char g_last_msg[512] = "";
+constexpr size_t kMaxSmem = 232448;  // 227 KB opt-in per block on sm_100
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  g_last_code = code;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_msg, sizeof(g_last_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return TS_OK;
+}
+
+int launch_scan_fwd(const ScanParams& p, cudaStream_t s);
+int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s);
+size_t scan_state_smem(const ScanParams& p);
+size_t scan_out_smem(const ScanParams& p);
+size_t scan_bwd_max_smem(const ScanParams& p);
+
+static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static size_t states_bytes(const ScanParams& p) {
+  return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * p.DkM * p.DvP * sizeof(float));
+}
+static size_t images_bytes(const ScanParams& p) {
+  return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * p.DvP * p.DkP * 2);
+}
+
+// Validate `a` and fill `p` (workspace pointers left null).
+static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
+  if (!a) return set_error(TS_ERR_VALUE, "scan: null arguments");
+  if (a->batch < 1 || a->heads < 1 || a->tokens < 1)
+    return set_error(TS_ERR_VALUE, "scan: batch, heads and tokens must be >= 1");
+  if (a->dk < 1 || a->dk > 256)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: key width %d outside 1..256", a->dk);
+  if (a->dv < 1 + a->v_append_unit || a->dv > 128)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: payload width %d outside 1..128", a->dv);
+  if (a->n_retentions < 1 || a->n_retentions > TS_MAX_RETENTIONS)
+    return set_error(TS_ERR_VALUE, "scan: n_retentions must be in 1..%d", TS_MAX_RETENTIONS);
+  if (!a->q || !a->k || !a->v) return set_error(TS_ERR_VALUE, "scan: null stream pointer");
+  if (a->out_dtype != TS_DTYPE_F32 && a->out_dtype != TS_DTYPE_BF16)
+    return set_error(TS_ERR_VALUE, "scan: out_dtype must be TS_DTYPE_F32 or TS_DTYPE_BF16");
+  std::memset(p, 0, sizeof(*p));
+  p->B = a->batch;
+  p->H = a->heads;
+  p->T = a->tokens;
+  p->Dk = a->dk;
+  p->Dv = a->dv;
+  p->DkP = round_up(a->dk, 16);
+  p->DkM = round_up(a->dk, 128);
+  p->DvP = round_up(a->dv, 16);
+  p->NT = ceil_div(a->tokens, 128);
+  p->R = a->n_retentions;
+  p->q = static_cast<const __nv_bfloat16*>(a->q);
+  p->k = static_cast<const __nv_bfloat16*>(a->k);
+  p->v = static_cast<const __nv_bfloat16*>(a->v);
+  for (int i = 0; i < 3; ++i) {
+    p->qs[i] = a->q_strides[i];
+    p->ks[i] = a->k_strides[i];
+    p->vs[i] = a->v_strides[i];
+  }
+  p->v_unit = a->v_append_unit ? 1 : 0;
+  for (int r = 0; r < p->R; ++r) {
+    p->la[r] = a->log_alpha[r];
+    p->out[r] = a->out[r];
+    if (!a->out[r]) return set_error(TS_ERR_VALUE, "scan: null output pointer for retention %d", r);
+  }
+  p->out_bf16 = a->out_dtype == TS_DTYPE_BF16;
+  const int mblocks = p->DkM / 128;
+  if (p->R * mblocks * p->DvP > 512 || 128 + p->R * p->DvP > 512)
+    return set_error(TS_ERR_NOT_IMPLEMENTED,
+                     "scan: %d retentions of a %dx%d state exceed the 512 tensor-memory columns of one CTA",
+                     p->R, p->Dk, p->Dv);
+  if (scan_state_smem(*p) > kMaxSmem || scan_out_smem(*p) > kMaxSmem || scan_bwd_max_smem(*p) > kMaxSmem)
+    return set_error(TS_ERR_NOT_IMPLEMENTED,
+                     "scan: key width %d with payload width %d exceeds the shared-memory budget of one CTA",
+                     p->Dk, p->Dv);
+  return TS_OK;
+}
+
+}  // namespace ts
+
+using namespace ts;
+
+extern "C" {
+
+const char* ts_b200_version(void) { return "thetascan_b200 0.1.0 (sm_100a)"; }
+
+int ts_b200_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    std::strncpy(buf, g_last_msg, len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_last_code;
+}
+
+int ts_b200_device_status(ts_stream_t stream, int* status) {
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+  int value = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&value, g_device_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+  if (status) *status = value;
+  if (value) return set_error(TS_ERR_DEVICE, "a kernel gave up on a bounded wait (code %d)", value);
+  return TS_OK;
+}
+
+int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                         ts_stream_t stream) {
+  return selftest_mma(A, B, D, N, K, a_mn, b_mn, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
+  ScanParams p;
+  if (build_scan_params(args, &p) != TS_OK) return 0;
+  return states_bytes(p) + images_bytes(p);
+}
+
+size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* args) {
+  ScanParams p;
+  if (build_scan_params(args, &p) != TS_OK) return 0;
+  return states_bytes(p) + images_bytes(p);
+}
+
+int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
+  ScanParams p;
+  if (int e = build_scan_params(args, &p)) return e;
+  const size_t need = states_bytes(p) + images_bytes(p);
+  if (!args->workspace || args->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_fwd: workspace of %zu bytes needed", need);
+  p.states = static_cast<float*>(args->workspace);
+  p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
+  return launch_scan_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts_stream_t stream) {
+  ScanParams p;
+  if (int e = build_scan_params(args, &p)) return e;
+  if (!grad) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient arguments");
+  const size_t need = states_bytes(p) + images_bytes(p);
+  if (!args->workspace || args->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_bwd: the forward workspace (%zu bytes) is required", need);
+  if (!grad->workspace || grad->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need);
+  if (!grad->dq || !grad->dk || !grad->dv) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
+  p.states = static_cast<float*>(args->workspace);
+  p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
+  ScanGradParams g;
+  std::memset(&g, 0, sizeof(g));
+  for (int r = 0; r < p.R; ++r) {
+    g.dout[r] = static_cast<const __nv_bfloat16*>(grad->dout[r]);
+    if (!g.dout[r]) return set_error(TS_ERR_VALUE, "scan_bwd: null dout for retention %d", r);
+    g.dla[r] = grad->dlog_alpha[r];
+  }
+  g.dq = grad->dq;
+  g.dk = grad->dk;
+  g.dv = grad->dv;
+  g.grad_bf16 = grad->grad_dtype == TS_DTYPE_BF16;
+  g.gstates = static_cast<float*>(grad->workspace);
+  g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));
+  return launch_scan_bwd(p, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

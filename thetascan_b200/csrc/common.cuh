@@ -1,0 +1,386 @@
+// Shared device helpers for the sm_100a ThetaScan kernels.
+//
+// Tensor-core work uses the 5th-generation MMA (tcgen05.mma, kind::f16,
+// bf16 x bf16 -> f32) with accumulators in Tensor Memory (TMEM).  Operands are
+// staged in shared memory as "core-matrix tiles":
+//
+//   a tile of R rows x C columns of bf16 (R, C multiples of 8) stores element
+//   (r, c) at byte  (c/8)*R*16 + (r/8)*128 + (r%8)*16 + (c%8)*2,
+//
+// i.e. every 8x8 block ("core matrix", 8 rows of 16 contiguous bytes) is one
+// 128-byte line, blocks of one 8-column chunk are stacked down the rows, and
+// chunks follow each other.  The same bytes can be read by the MMA either as a
+// K-major operand (tile rows = M or N, tile columns = K) or as an MN-major
+// operand (tile rows = K, tile columns = M or N); only the two strides of the
+// shared-memory descriptor differ.  That lets one staged copy of, say, a key
+// tile serve both the score product q.k^T and the state update k^T.v.
+//
+// Every wait on an mbarrier is bounded.  On timeout the kernel records an
+// error code in a device flag that the host reads back (ts_b200_device_status)
+// and stops issuing work; nothing traps or spins forever.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace ts {
+
+constexpr int kTile = 128;          // tokens per tile (= MMA M)
+constexpr int kThreads = 128;       // one thread per tile row
+
+// Error codes written to the device status word.
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrMmaTimeout = 1,
+  kErrCopyTimeout = 2,
+};
+
+// Device status word (the library is one translation unit; see all.cu).
+__device__ int g_device_status = 0;
+
+__device__ __forceinline__ void record_error(int code) {
+  atomicCAS(&g_device_status, 0, code);
+}
+
+__device__ __forceinline__ bool device_failed() {
+  return *(volatile int*)&g_device_status != 0;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up after about
+// one second (or 2^24 polls), records `code` and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (globaltimer_ns() - start > 1000000000ull) break;
+      if (device_failed()) return false;
+    }
+  }
+  record_error(code);
+  return false;
+}
+
+// ------------------------------------------------------------------ tcgen05
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (the tensor core reads operands through it).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Warp-wide: allocate `ncols` TMEM columns (power of two >= 32); the base
+// address is written to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Instruction descriptor for kind::f16 with bf16 A/B and an f32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                                  // D format: f32
+         | (1u << 7)                                // A format: bf16
+         | (1u << 10)                               // B format: bf16
+         | (static_cast<uint32_t>(a_mn_major) << 15)
+         | (static_cast<uint32_t>(b_mn_major) << 16)
+         | (static_cast<uint32_t>(N >> 3) << 17)
+         | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor, no swizzle (layout type 0), sm_100 version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every MMA previously issued by this thread completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// Warp-collective: 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Warp-collective: write 16 consecutive 32-bit TMEM columns of this lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// TMEM address of (lane, column): lane in bits 31:16, column in 15:0.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int lane, int col) {
+  return base + (static_cast<uint32_t>(lane) << 16) + static_cast<uint32_t>(col);
+}
+
+// ------------------------------------------------------------------ tiles
+
+struct Tile {
+  uint32_t saddr;  // shared-memory byte address (16-byte aligned)
+  int rows;        // multiple of 8
+  int cols;        // multiple of 8
+};
+
+__device__ __forceinline__ uint32_t tile_off(const Tile& t, int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * t.rows * 16 + (r >> 3) * 128 + (r & 7) * 16 + (c & 7) * 2);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// 16 bytes = columns c8*8 .. c8*8+7 of row r.
+__device__ __forceinline__ void tile_st16(const Tile& t, int r, int c8, uint4 v) {
+  st_shared_v4(t.saddr + tile_off(t, r, c8 * 8), v);
+}
+__device__ __forceinline__ uint4 tile_ld16(const Tile& t, int r, int c8) {
+  return ld_shared_v4(t.saddr + tile_off(t, r, c8 * 8));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
+  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
+  return __bfloat1622float2(h);
+}
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]),
+                    pack_bf16(f[6], f[7]));
+}
+__device__ __forceinline__ void unpack8(uint4 u, float* f) {
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), c = unpack_bf16(u.z), d = unpack_bf16(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+// Operand views of a tile for the descriptor.  `r0`/`c0` select a sub-block
+// (r0 multiple of 8, c0 multiple of 8).
+//
+// K-major view: MMA rows (M or N) = tile rows, K = tile columns.
+//   LBO = stride between 8-column K groups = rows*16, SBO = 128.
+// MN-major view: K = tile rows, MMA rows/cols (M or N) = tile columns.
+//   SBO = stride between 8-column MN groups = rows*16, LBO = 128.
+struct OperandView {
+  uint32_t start;
+  uint32_t lbo, sbo;
+  uint32_t kstep;  // bytes to advance per K step of 16
+  bool mn_major;
+};
+
+__device__ __forceinline__ OperandView kmajor(const Tile& t, int r0 = 0, int c0 = 0) {
+  OperandView v;
+  v.start = t.saddr + tile_off(t, r0, c0);
+  v.lbo = static_cast<uint32_t>(t.rows * 16);
+  v.sbo = 128u;
+  v.kstep = static_cast<uint32_t>(2 * t.rows * 16);
+  v.mn_major = false;
+  return v;
+}
+__device__ __forceinline__ OperandView mnmajor(const Tile& t, int r0 = 0, int c0 = 0) {
+  OperandView v;
+  v.start = t.saddr + tile_off(t, r0, c0);
+  v.lbo = 128u;
+  v.sbo = static_cast<uint32_t>(t.rows * 16);
+  v.kstep = 256u;
+  v.mn_major = true;
+  return v;
+}
+
+// D[128 x N] (+)= A[128 x K] . B[K x N]; issue from ONE thread.  K multiple
+// of 16, N multiple of 16 in [16, 256].
+__device__ __forceinline__ void gemm_issue(uint32_t d_tmem, const OperandView& a, const OperandView& b, int N,
+                                           int K, bool accumulate) {
+  const uint32_t id = idesc_bf16(128, N, a.mn_major, b.mn_major);
+  for (int s = 0; s < K / 16; ++s) {
+    const uint64_t ad = smem_desc(a.start + s * a.kstep, a.lbo, a.sbo);
+    const uint64_t bd = smem_desc(b.start + s * b.kstep, b.lbo, b.sbo);
+    mma_bf16(d_tmem, ad, bd, id, (accumulate || s > 0) ? 1u : 0u);
+  }
+}
+
+// ------------------------------------------------------------------ loads
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// Cooperative copy of a row-major bf16 matrix (rows_valid x cols_valid,
+// leading dimension `ld` elements) into `t`, zero-filling the rest of the
+// tile.  Consecutive threads cover 8 rows of one 8-column chunk, so the shared
+// stores are conflict-free and each row is read in 64-byte runs.  If
+// `unit_col` >= 0, column `unit_col` of every valid row is set to 1.
+__device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __restrict__ src, long ld,
+                                          int rows_valid, int cols_valid, int unit_col = -1) {
+  const int chunks = t.cols / 8;
+  const int total = t.rows * chunks;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && ((ld & 7) == 0);
+  for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    const int r8 = it & 7;
+    const int rest = it >> 3;
+    const int j = rest % chunks;
+    const int r = (rest / chunks) * 8 + r8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < rows_valid) {
+      const int c0 = j * 8;
+      if (vec_ok && c0 + 8 <= cols_valid) {
+        v = __ldg(reinterpret_cast<const uint4*>(src + r * ld + c0));
+      } else {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = c0 + e;
+          f[e] = (c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
+        }
+        v = pack8(f);
+      }
+      if (unit_col >= c0 && unit_col < c0 + 8) {
+        float f[8];
+        unpack8(v, f);
+        f[unit_col - c0] = 1.f;
+        v = pack8(f);
+      }
+    }
+    tile_st16(t, r, j, v);
+  }
+}
+
+// Copy a pre-arranged tile image (already in core-matrix order, `bytes` long)
+// from global memory.
+__device__ __forceinline__ void load_image(const Tile& t, const void* __restrict__ src, int bytes) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) st_shared_v4(t.saddr + i * 16, __ldg(s + i));
+}
+
+__device__ __forceinline__ void zero_tile(const Tile& t) {
+  for (int i = threadIdx.x; i < t.rows * t.cols / 8; i += blockDim.x)
+    st_shared_v4(t.saddr + i * 16, make_uint4(0, 0, 0, 0));
+}
+
+// Block-wide sum (blockDim.x == 128) via shared scratch of 4 floats.
+__device__ __forceinline__ float block_sum128(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = scratch[0] + scratch[1] + scratch[2] + scratch[3];
+  __syncthreads();
+  return s;
+}
+
+// ------------------------------------------------------------------ CTA context
+
+// Per-CTA MMA context: TMEM base, one completion barrier and its parity.
+struct MmaCtx {
+  uint64_t* bar;
+  uint32_t tmem;
+  uint32_t phase;
+  bool ok;
+
+  // Everybody: make staged operands visible, then thread 0 issues `issue()`,
+  // commits, and all threads wait for completion.
+  template <class F>
+  __device__ __forceinline__ void run(F issue) {
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+      issue();
+      mma_commit(bar);
+    }
+    if (ok) ok = mbar_wait(bar, phase, kErrMmaTimeout);
+    phase ^= 1u;
+    tc_fence_after();
+  }
+};
+
+}  // namespace ts

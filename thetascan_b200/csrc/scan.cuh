@@ -1,0 +1,97 @@
+// Shared definitions of the multi-view chunked scan kernels.
+//
+// Sequence tiles are 128 tokens.  For retention r with static per-head
+// log-retention la (la = 0 for the plain sum) and local position i in a tile:
+//   intra weight  w(i, j) = exp(la * (i - j))      (j <= i)
+//   carry         c(i)    = exp(la * (i + 1))      (weight of the entering state)
+//   key weight    u(j)    = exp(la * (127 - j))    (weight in the leaving state)
+//   closing       exp(128 * la)                    (state decay across a tile)
+// which is the tile algebra of the reference chunk backend
+// (src/thetascan/_core/ops/scan_chunk.py:102-119, 170-212, 322-336) with a
+// 128-token tile; every exponent is <= 0, so no reciprocal decay is formed.
+#pragma once
+
+#include "common.cuh"
+
+namespace ts {
+
+struct ScanParams {
+  int B, H, T;
+  int Dk, Dv;     // logical widths (Dv includes the unit column)
+  int DkP;        // Dk rounded up to 16 (MMA K of the score / read)
+  int DkM;        // Dk rounded up to 128 (MMA M of the state update)
+  int DvP;        // Dv rounded up to 16
+  int NT, R;
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  long long qs[3], ks[3], vs[3];
+  int v_unit;                // 1: column Dv-1 of the payload is the constant 1
+  const float* la[4];        // nullptr = plain sum
+  void* out[4];
+  int out_bf16;
+  float* states;             // [B,H,NT,R,DkM,DvP] f32: dS, then S_in in place
+  __nv_bfloat16* images;     // [B,H,NT,R] images of S_in (DvP rows x DkP cols)
+};
+
+struct ScanGradParams {
+  const __nv_bfloat16* dout[4];
+  void* dq;
+  void* dk;
+  void* dv;
+  int grad_bf16;
+  float* dla[4];
+  float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place
+  __nv_bfloat16* gimages;    // [B,H,NT,R] images of G (DvP rows x DkP cols)
+};
+
+__device__ __forceinline__ float head_la(const ScanParams& p, int r, int h) {
+  return p.la[r] ? __ldg(p.la[r] + h) : 0.f;
+}
+
+__device__ __forceinline__ size_t state_index(const ScanParams& p, int b, int h, int n, int r) {
+  return ((static_cast<size_t>(b) * p.H + h) * p.NT + n) * p.R + r;
+}
+
+__device__ __forceinline__ int image_bytes(const ScanParams& p) { return p.DvP * p.DkP * 2; }
+
+__device__ __forceinline__ void store_out(void* base, bool bf16, size_t idx, float v) {
+  if (bf16) {
+    reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<float*>(base)[idx] = v;
+  }
+}
+
+// Build a tile whose row t is `scale(t) * row_t(src)` for a bf16 row-major
+// source, thread t handling row t (blockDim.x == 128).  Rows >= rows_valid and
+// columns >= cols_valid are zero; `unit_col` (if >= 0) is 1 before scaling.
+template <class Scale>
+__device__ __forceinline__ void load_scaled_rows(const Tile& t, const __nv_bfloat16* __restrict__ src, long long ld,
+                                                 int rows_valid, int cols_valid, int unit_col, Scale scale) {
+  const int r = threadIdx.x;
+  const float s = scale(r);
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && ((ld & 7) == 0);
+  for (int j = 0; j < t.cols / 8; ++j) {
+    float f[8];
+    const int c0 = j * 8;
+    if (r < rows_valid && vec_ok && c0 + 8 <= cols_valid) {
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(src + r * ld + c0));
+      unpack8(u, f);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = c0 + e;
+        f[e] = (r < rows_valid && c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (r < rows_valid && c0 + e == unit_col) f[e] = 1.f;
+      f[e] *= s;
+    }
+    tile_st16(t, r, j, pack8(f));
+  }
+}
+
+}  // namespace ts

@@ -1,0 +1,449 @@
+// Backward of the multi-view chunked scan.  With g_r = dout_r . v^T, the
+// per-tile gradients are
+//   dq = ds . k + sum_r (c_r o dout_r) S_in,r^T
+//   dk = ds^T . q + sum_r (u_r o v) G_r^T
+//   dv = sum_r [ P_r^T dout_r + (u_r o k) G_r ]
+// where ds = sum_r w_r o causal o g_r, P_r = w_r o causal o (q.k^T), S_in,r is
+// the forward state entering the tile and G_r the gradient of the state leaving
+// it, obtained by a reverse exclusive scan of the local terms
+// sum_t c_r(t) q_t^T dout_r[t].  The log-retention gradient uses
+//   d/d la_r = sum_t (t - c) dout_r[t].out_r[t] - sum_j (j - c) v_j.dv_j^(r)
+// for any constant c (each pair (t, j) contributes (t - j) w s g), so it needs
+// no per-pair work beyond what dq and dv already do.  Kernels:
+//   scan_bwd_state_kernel  local dS per tile                     (tcgen05)
+//   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
+//   scan_bwd_dq_kernel     ds (accumulated in TMEM), dq, e-term  (tcgen05)
+//   scan_bwd_dk_kernel     ds, dk                                (tcgen05)
+//   scan_bwd_dv_kernel     P_r, dv, f-term                       (tcgen05)
+#include "capi_internal.h"
+#include "scan.cuh"
+
+namespace ts {
+
+namespace {
+
+__device__ __forceinline__ const __nv_bfloat16* dout_rows(const ScanParams& p, const ScanGradParams& g, int r,
+                                                          int b, int h, int t0) {
+  return g.dout[r] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
+}
+
+__device__ __forceinline__ float out_value(const ScanParams& p, int r, size_t idx) {
+  return p.out_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.out[r])[idx])
+                    : reinterpret_cast<const float*>(p.out[r])[idx];
+}
+
+// ds_acc (TMEM, 128 columns at t_ds) = sum_r w_r o causal o (dout_r . v^T).
+// Uses tiles td (dout staging) and tv (payload), TMEM columns t_g for g_r.
+// Also accumulates the e-term of the log-retention gradient when `eterm`.
+__device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile& td,
+                              const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows,
+                              bool eterm, float* red) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int r = 0; r < p.R; ++r) {
+    const __nv_bfloat16* dp = dout_rows(p, g, r, b, h, t0);
+    load_tile(td, dp, p.Dv, rows, p.Dv);
+    ctx.run([&] { gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false); });
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    for (int c = 0; c < kTile; c += 16) {
+      float gv[16], acc[16];
+      tmem_ld16(tmem_addr(t_g, warp * 32, c), gv);
+      if (r > 0) tmem_ld16(tmem_addr(t_ds, warp * 32, c), acc);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = c + e;
+        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
+        const float term = (j <= tid) ? w * gv[e] : 0.f;
+        acc[e] = (r > 0) ? acc[e] + term : term;
+      }
+      tmem_st16(tmem_addr(t_ds, warp * 32, c), acc);
+    }
+    if (eterm && decayed && g.dla[r] != nullptr) {
+      float e_t = 0.f;
+      if (tid < rows) {
+        const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
+        for (int c = 0; c < p.Dv; ++c) e_t += __bfloat162float(dp[tid * p.Dv + c]) * out_value(p, r, row + c);
+      }
+      const float center = 0.5f * static_cast<float>(p.T - 1);
+      const float s = block_sum128((static_cast<float>(t0 + tid) - center) * e_t, red);
+      if (tid == 0) atomicAdd(g.dla[r] + h, s);
+    }
+  }
+}
+
+// Move the f32 ds accumulator (TMEM) into a bf16 tile, row tid.
+__device__ __forceinline__ void ds_to_tile(uint32_t t_ds, const Tile& tds) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int c = 0; c < kTile; c += 16) {
+    float v[16];
+    tmem_ld16(tmem_addr(t_ds, warp * 32, c), v);
+    tile_st16(tds, tid, c / 8, pack8(v));
+    tile_st16(tds, tid, c / 8 + 1, pack8(v + 8));
+  }
+}
+
+__device__ __forceinline__ void store_grad_rows(void* dst, bool bf16, size_t row0, int width, uint32_t taddr,
+                                                int ncols_padded, bool valid) {
+  for (int c = 0; c < ncols_padded; c += 16) {
+    float v[16];
+    tmem_ld16(taddr + c, v);
+    if (valid) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c + e < width) store_out(dst, bf16, row0 + c + e, v[e]);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t tmem_cols_for(int n) {
+  return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ local dS
+
+__global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int n = blockIdx.x + 1, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tq{base, kTile, p.DkM};
+  Tile tw{tq.saddr + kTile * p.DkM * 2, kTile, p.DvP};
+  const int mblocks = p.DkM / kTile;
+  const uint32_t ncols = tmem_cols_for(p.R * mblocks * p.DvP);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+  const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
+  load_tile(tq, qp, p.qs[2], rows, p.Dk);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    load_scaled_rows(tw, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
+                     [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
+    ctx.run([&] {
+      for (int mb = 0; mb < mblocks; ++mb)
+        gemm_issue(ctx.tmem + static_cast<uint32_t>((r * mblocks + mb) * p.DvP), mnmajor(tq, 0, mb * kTile),
+                   mnmajor(tw), p.DvP, kTile, false);
+    });
+  }
+  for (int r = 0; r < p.R; ++r) {
+    float* dst_base = g.gstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+    for (int mb = 0; mb < mblocks; ++mb) {
+      float* dst = dst_base + static_cast<size_t>(mb * kTile + tid) * p.DvP;
+      for (int c = 0; c < p.DvP; c += 16) {
+        float v[16];
+        tmem_ld16(tmem_addr(ctx.tmem, warp * 32, (r * mblocks + mb) * p.DvP + c), v);
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          *reinterpret_cast<float4*>(dst + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ reverse prefix
+
+__global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, ScanGradParams g) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y;
+  const int bh = blockIdx.z;
+  const int b = bh / p.H, h = bh % p.H;
+  if (e >= p.DkM * p.DvP) return;
+  const int f = e / p.DvP, c = e % p.DvP;
+  const float la = head_la(p, r, h);
+  const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const bool in_image = f < p.DkP;
+  const Tile img{0u, p.DvP, p.DkP};
+  const uint32_t img_off = in_image ? tile_off(img, c, f) : 0u;
+  float G = 0.f;
+  for (int n = p.NT - 1; n >= 0; --n) {
+    const size_t si = state_index(p, b, h, n, r);
+    float* ptr = g.gstates + si * p.DkM * p.DvP + e;
+    const float local = (n >= 1) ? *ptr : 0.f;
+    *ptr = G;
+    if (in_image) {
+      uint8_t* img_base = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p));
+      *reinterpret_cast<__nv_bfloat16*>(img_base + img_off) = __float2bfloat16_rn(G);
+    }
+    G = G * closing + local;
+  }
+}
+
+// ------------------------------------------------------------------ dq
+
+__global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float red[4];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tv{base, kTile, p.DvP};
+  Tile td{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
+  Tile tds{td.saddr + kTile * p.DvP * 2, kTile, kTile};
+  Tile tk{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
+  Tile ts{tk.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
+  const uint32_t ncols = 512;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+  const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_tile(tk, kp, p.ks[2], rows, p.Dk);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dq = ctx.tmem + 256;
+
+  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows, true, red);
+  ds_to_tile(t_ds, tds);
+  ctx.run([&] { gemm_issue(t_dq, kmajor(tds), mnmajor(tk), p.DkP, kTile, false); });
+  if (n > 0) {
+    for (int r = 0; r < p.R; ++r) {
+      const float la = head_la(p, r, h);
+      const bool decayed = p.la[r] != nullptr;
+      load_scaled_rows(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
+                       [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
+      const size_t si = state_index(p, b, h, n, r);
+      load_image(ts, reinterpret_cast<const uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)),
+                 image_bytes(p));
+      ctx.run([&] { gemm_issue(t_dq, kmajor(td), mnmajor(ts), p.DkP, p.DvP, true); });
+    }
+  }
+  const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dk;
+  store_grad_rows(g.dq, g.grad_bf16, row, p.Dk, tmem_addr(t_dq, warp * 32, 0), p.DkP, tid < rows);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ dk
+
+__global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tv{base, kTile, p.DvP};
+  Tile td{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
+  Tile tds{td.saddr + kTile * p.DvP * 2, kTile, kTile};
+  Tile tq{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
+  Tile tg{tq.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
+  const uint32_t ncols = 512;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+  const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
+  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_tile(tq, qp, p.qs[2], rows, p.Dk);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dk = ctx.tmem + 256;
+
+  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows, false, nullptr);
+  ds_to_tile(t_ds, tds);
+  ctx.run([&] { gemm_issue(t_dk, mnmajor(tds), mnmajor(tq), p.DkP, kTile, false); });
+  if (n + 1 < p.NT) {
+    for (int r = 0; r < p.R; ++r) {
+      const float la = head_la(p, r, h);
+      const bool decayed = p.la[r] != nullptr;
+      // (u_r o v) rows: reuse the dout staging tile.
+      for (int j = 0; j < p.DvP / 8; ++j) {
+        float f[8];
+        unpack8(tile_ld16(tv, tid, j), f);
+        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - tid)) : 1.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= u;
+        tile_st16(td, tid, j, pack8(f));
+      }
+      const size_t si = state_index(p, b, h, n, r);
+      load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
+                 image_bytes(p));
+      ctx.run([&] { gemm_issue(t_dk, kmajor(td), mnmajor(tg), p.DkP, p.DvP, true); });
+    }
+  }
+  const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dk;
+  store_grad_rows(g.dk, g.grad_bf16, row, p.Dk, tmem_addr(t_dk, warp * 32, 0), p.DkP, tid < rows);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ dv
+
+__global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float red[4];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tq{base, kTile, p.DkP};                          // q, then (u_r o k)
+  Tile tk{tq.saddr + kTile * p.DkP * 2, kTile, p.DkP};  // k, then G image
+  Tile tg{tk.saddr, p.DvP, p.DkP};
+  Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
+  Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
+  Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
+  const uint32_t ncols = tmem_cols_for(kTile + p.R * p.DvP);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+  const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
+  const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  load_tile(tq, qp, p.qs[2], rows, p.Dk);
+  load_tile(tk, kp, p.ks[2], rows, p.Dk);
+  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_s = ctx.tmem;
+  ctx.run([&] { gemm_issue(t_s, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
+
+  const bool cross = n + 1 < p.NT;
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    for (int c = 0; c < kTile; c += 16) {
+      float s[16], f[16];
+      tmem_ld16(tmem_addr(t_s, warp * 32, c), s);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = c + e;
+        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
+        f[e] = (j <= tid) ? w * s[e] : 0.f;
+      }
+      tile_st16(tp, tid, c / 8, pack8(f));
+      tile_st16(tp, tid, c / 8 + 1, pack8(f + 8));
+    }
+    load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+    if (cross) {
+      load_scaled_rows(tq, kp, p.ks[2], rows, p.Dk, -1, [&](int t) {
+        return decayed ? __expf(la * static_cast<float>(kTile - 1 - t)) : 1.f;
+      });
+      const size_t si = state_index(p, b, h, n, r);
+      load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
+                 image_bytes(p));
+    }
+    const uint32_t t_dv = ctx.tmem + static_cast<uint32_t>(kTile + r * p.DvP);
+    ctx.run([&] {
+      gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, false);
+      if (cross) gemm_issue(t_dv, kmajor(tq), kmajor(tg), p.DvP, p.DkP, true);
+    });
+  }
+
+  // dv = sum_r dv_r; f-term of the log-retention gradient per retention.
+  const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
+  const float center = 0.5f * static_cast<float>(p.T - 1);
+  for (int c = 0; c < p.DvP; c += 16) {
+    float acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+    for (int r = 0; r < p.R; ++r) {
+      float v[16];
+      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] += v[e];
+    }
+    if (tid < rows) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c + e < p.Dv) store_out(g.dv, g.grad_bf16, row + c + e, acc[e]);
+    }
+  }
+  for (int r = 0; r < p.R; ++r) {
+    if (p.la[r] == nullptr || g.dla[r] == nullptr) continue;
+    float f_j = 0.f;
+    for (int c = 0; c < p.DvP; c += 16) {
+      float v[16], x[8], y[8];
+      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
+      unpack8(tile_ld16(tv, tid, c / 8), x);
+      unpack8(tile_ld16(tv, tid, c / 8 + 1), y);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f_j += x[e] * v[e] + y[e] * v[e + 8];
+    }
+    if (tid >= rows) f_j = 0.f;
+    const float s = block_sum128((static_cast<float>(t0 + tid) - center) * f_j, red);
+    if (tid == 0) atomicAdd(g.dla[r] + h, -s);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ host launch
+
+static size_t dq_smem(const ScanParams& p) {
+  return static_cast<size_t>(kTile) * (2 * p.DvP + kTile + p.DkP) * 2 + static_cast<size_t>(p.DvP) * p.DkP * 2;
+}
+static size_t dv_smem(const ScanParams& p) {
+  return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2;
+}
+static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (p.DkM + p.DvP) * 2; }
+
+size_t scan_bwd_max_smem(const ScanParams& p) {
+  size_t m = dq_smem(p);
+  if (dv_smem(p) > m) m = dv_smem(p);
+  if (bstate_smem(p) > m) m = bstate_smem(p);
+  return m;
+}
+
+int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s) {
+  const size_t s_state = bstate_smem(p), s_dq = dq_smem(p), s_dv = dv_smem(p);
+  cudaFuncSetAttribute(scan_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_state));
+  cudaFuncSetAttribute(scan_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dq));
+  cudaFuncSetAttribute(scan_bwd_dk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dq));
+  cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
+  if (p.NT > 1) {
+    scan_bwd_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, s_state, s>>>(p, g);
+    if (int e = check_launch("scan_bwd_state_kernel")) return e;
+  }
+  scan_bwd_prefix_kernel<<<dim3(ceil_div(p.DkM * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p, g);
+  if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
+  const dim3 grid(p.NT, p.H, p.B);
+  scan_bwd_dq_kernel<<<grid, kThreads, s_dq, s>>>(p, g);
+  if (int e = check_launch("scan_bwd_dq_kernel")) return e;
+  scan_bwd_dk_kernel<<<grid, kThreads, s_dq, s>>>(p, g);
+  if (int e = check_launch("scan_bwd_dk_kernel")) return e;
+  scan_bwd_dv_kernel<<<grid, kThreads, s_dv, s>>>(p, g);
+  return check_launch("scan_bwd_dv_kernel");
+}
+
+}  // namespace ts

@@ -1,0 +1,230 @@
+// Forward of the multi-view chunked scan (reference scan_chunk.linattn_views,
+// src/thetascan/_core/ops/scan_chunk.py:246-339), in three kernels:
+//   1. scan_state_kernel   per tile: dS_r = k^T (u_r * v)          (tcgen05)
+//   2. scan_prefix_kernel  per (b,h,r): exclusive scan of the tile states
+//                           S_in(n) = e^{128 la} S_in(n-1) + dS(n-1)  (f32)
+//   3. scan_out_kernel     per tile: score q.k^T once, then per retention
+//                           out_r = (w_r o causal o score) v + (c_r q) S_in  (tcgen05)
+#include "capi_internal.h"
+#include "scan.cuh"
+
+namespace ts {
+
+// ------------------------------------------------------------------ 1. tile states
+
+__global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+
+  const uint32_t base = smem_u32(smem);
+  Tile tk{base, kTile, p.DkM};
+  Tile tv{tk.saddr + kTile * p.DkM * 2, kTile, p.DvP};
+  Tile tw{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
+
+  const int mblocks = p.DkM / kTile;
+  const int cols_needed = p.R * mblocks * p.DvP;
+  const uint32_t ncols = cols_needed <= 32 ? 32 : cols_needed <= 64 ? 64 : cols_needed <= 128 ? 128
+                         : cols_needed <= 256 ? 256 : 512;
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+
+  const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  load_tile(tk, kp, p.ks[2], rows, p.Dk);
+  const int vcols = p.Dv - p.v_unit;
+  load_tile(tv, vp, p.vs[2], rows, vcols, p.v_unit ? p.Dv - 1 : -1);
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    // u_r(j) = exp(la (127 - j)): this tile's key weights in the leaving state.
+    const float u = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile - 1 - tid)) : 1.f;
+    for (int j = 0; j < p.DvP / 8; ++j) {
+      float f[8];
+      unpack8(tile_ld16(tv, tid, j), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= u;
+      tile_st16(tw, tid, j, pack8(f));
+    }
+    ctx.run([&] {
+      for (int mb = 0; mb < mblocks; ++mb) {
+        const uint32_t d = ctx.tmem + static_cast<uint32_t>((r * mblocks + mb) * p.DvP);
+        gemm_issue(d, mnmajor(tk, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+      }
+    });
+  }
+
+  // Epilogue: row f of block mb is feature mb*128 + tid.
+  for (int r = 0; r < p.R; ++r) {
+    float* dst_base = p.states + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+    for (int mb = 0; mb < mblocks; ++mb) {
+      float* dst = dst_base + static_cast<size_t>(mb * kTile + tid) * p.DvP;
+      for (int c = 0; c < p.DvP; c += 16) {
+        float v[16];
+        tmem_ld16(tmem_addr(ctx.tmem, warp * 32, (r * mblocks + mb) * p.DvP + c), v);
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          *reinterpret_cast<float4*>(dst + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ 2. prefix over tiles
+
+__global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y;
+  const int bh = blockIdx.z;
+  const int b = bh / p.H, h = bh % p.H;
+  if (e >= p.DkM * p.DvP) return;
+  const int f = e / p.DvP, c = e % p.DvP;
+  const float la = head_la(p, r, h);
+  const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const bool in_image = f < p.DkP;
+  const Tile img{0u, p.DvP, p.DkP};
+  const uint32_t img_off = in_image ? tile_off(img, c, f) : 0u;
+  float S = 0.f;
+  for (int n = 0; n < p.NT; ++n) {
+    const size_t si = state_index(p, b, h, n, r);
+    float* ptr = p.states + si * p.DkM * p.DvP + e;
+    const float upd = (n + 1 < p.NT) ? *ptr : 0.f;
+    *ptr = S;
+    if (in_image) {
+      uint8_t* img_base = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p));
+      *reinterpret_cast<__nv_bfloat16*>(img_base + img_off) = __float2bfloat16_rn(S);
+    }
+    S = S * closing + upd;
+  }
+}
+
+// ------------------------------------------------------------------ 3. tile outputs
+
+__global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+
+  const uint32_t base = smem_u32(smem);
+  Tile tq{base, kTile, p.DkP};
+  Tile tk{tq.saddr + kTile * p.DkP * 2, kTile, p.DkP};
+  Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
+  Tile tv{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
+  Tile ts{tv.saddr + kTile * p.DvP * 2, p.DvP, p.DkP};
+
+  const int cols_needed = kTile + p.R * p.DvP;
+  const uint32_t ncols = cols_needed <= 256 ? 256 : 512;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+
+  const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
+  const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  load_tile(tq, qp, p.qs[2], rows, p.Dk);
+  load_tile(tk, kp, p.ks[2], rows, p.Dk);
+  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_score = ctx.tmem;
+  ctx.run([&] { gemm_issue(t_score, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
+
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    // P_r row tid: w(tid, j) * score(tid, j) on the causal triangle.
+    for (int c = 0; c < kTile; c += 16) {
+      float s[16];
+      tmem_ld16(tmem_addr(t_score, warp * 32, c), s);
+      float f[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = c + e;
+        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
+        f[e] = (j <= tid) ? w * s[e] : 0.f;
+      }
+      tile_st16(tp, tid, c / 8, pack8(f));
+      tile_st16(tp, tid, c / 8 + 1, pack8(f + 8));
+    }
+    const bool cross = n > 0;
+    if (cross) {
+      const size_t si = state_index(p, b, h, n, r);
+      load_image(ts, reinterpret_cast<const uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)),
+                 image_bytes(p));
+      const float carry_la = la;
+      load_scaled_rows(tq, qp, p.qs[2], rows, p.Dk, -1, [&](int t) {
+        return decayed ? __expf(carry_la * static_cast<float>(t + 1)) : 1.f;
+      });
+    }
+    const uint32_t t_out = ctx.tmem + static_cast<uint32_t>(kTile + r * p.DvP);
+    ctx.run([&] {
+      gemm_issue(t_out, kmajor(tp), mnmajor(tv), p.DvP, kTile, false);
+      if (cross) gemm_issue(t_out, kmajor(tq), kmajor(ts), p.DvP, p.DkP, true);
+    });
+  }
+
+  // tcgen05.ld is warp-collective: every lane loads, only valid rows store.
+  for (int r = 0; r < p.R; ++r) {
+    const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
+    for (int c = 0; c < p.DvP; c += 16) {
+      float v[16];
+      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
+      if (tid < rows) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (c + e < p.Dv) store_out(p.out[r], p.out_bf16, row + c + e, v[e]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
+// ------------------------------------------------------------------ host launch
+
+size_t scan_state_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (p.DkM + 2 * p.DvP) * 2; }
+size_t scan_out_smem(const ScanParams& p) {
+  return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + p.DvP) * 2 + static_cast<size_t>(p.DvP) * p.DkP * 2;
+}
+
+int launch_scan_fwd(const ScanParams& p, cudaStream_t s) {
+  const size_t sm1 = scan_state_smem(p), sm3 = scan_out_smem(p);
+  cudaFuncSetAttribute(scan_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm1));
+  cudaFuncSetAttribute(scan_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm3));
+  if (p.NT > 1) {
+    scan_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, sm1, s>>>(p);
+    if (int e = check_launch("scan_state_kernel")) return e;
+  }
+  scan_prefix_kernel<<<dim3(ceil_div(p.DkM * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p);
+  if (int e = check_launch("scan_prefix_kernel")) return e;
+  scan_out_kernel<<<dim3(p.NT, p.H, p.B), kThreads, sm3, s>>>(p);
+  return check_launch("scan_out_kernel");
+}
+
+}  // namespace ts

@@ -1,0 +1,169 @@
+"""The ``b200`` scan backend: drop-in for the reference chunk scan.
+
+Mirrors ``thetascan._core.ops.scan_chunk`` (src/thetascan/_core/ops/
+scan_chunk.py:86, 246-358): same function names, argument meaning, output
+dtype and errors, computed by the sm_100a kernels behind the C ABI
+(``ts_b200_scan_fwd`` / ``ts_b200_scan_bwd``).  ``chunk`` is validated like the
+reference's but does not change the result: the kernels tile the sequence in
+128-token tiles internally, and the chunked algebra is exact for any tile.
+
+Supported: bf16 streams on a CUDA device, the plain causal sum (``None``) and
+static per-head log-retentions (``[H]``), up to four retentions per call,
+``Dk <= 256`` and ``Dv <= 128``.  Per-token retention streams (``[B,H,T,1]``)
+and float32 streams raise ``NotImplementedError``; a non-CUDA tensor raises
+``RuntimeError``.  Nothing falls back to a CPU implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+DEFAULT_CHUNK = 512
+
+
+def _strides3(x: torch.Tensor):
+    s = x.stride()
+    if s[3] != 1:
+        raise ValueError("b200 scan: the innermost dimension must be contiguous")
+    return _lib.c_int64_3(s[0], s[1], s[2])
+
+
+def _ptr(x):
+    return ctypes.c_void_p(0 if x is None else x.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _build_args(q, k, v, las, outs, append_unit, workspace=None):
+    B, H, T, Dk = q.shape
+    a = _lib.ScanArgs()
+    a.batch, a.heads, a.tokens, a.dk = B, H, T, Dk
+    a.dv = v.shape[-1] + (1 if append_unit else 0)
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    a.q_strides, a.k_strides, a.v_strides = _strides3(q), _strides3(k), _strides3(v)
+    a.v_append_unit = 1 if append_unit else 0
+    a.n_retentions = len(las)
+    for i, la in enumerate(las):
+        a.log_alpha[i] = None if la is None else la.data_ptr()
+        if outs is not None:
+            a.out[i] = outs[i].data_ptr()
+    a.out_dtype = _lib.TS_DTYPE_BF16 if (outs is not None and outs[0].dtype == torch.bfloat16) else _lib.TS_DTYPE_F32
+    if workspace is not None:
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    return a
+
+
+def _workspace(lib, fn, args, device):
+    nbytes = fn(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.last_error()[0] or _lib.TS_ERR_VALUE)
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+class _ScanViews(torch.autograd.Function):
+    """Autograd wrapper of the multi-view scan kernels."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, append_unit, out_dtype, *retentions):
+        lib = _lib.load()
+        las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+        B, H, T, _ = q.shape
+        dv = v.shape[-1] + (1 if append_unit else 0)
+        outs = [torch.empty(B, H, T, dv, dtype=out_dtype, device=q.device) for _ in las]
+        args = _build_args(q, k, v, las, outs, append_unit)
+        ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
+        ctx.append_unit = append_unit
+        ctx.n_ret = len(las)
+        ctx.ret_present = [r is not None for r in retentions]
+        ctx.ret_dtypes = [None if r is None else r.dtype for r in retentions]
+        ctx.ret_shapes = [None if r is None else r.shape for r in retentions]
+        saved_las = [la if la is not None else torch.empty(0, device=q.device) for la in las]
+        ctx.save_for_backward(q, k, v, ws, *outs, *saved_las)
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *douts):
+        lib = _lib.load()
+        n = ctx.n_ret
+        saved = ctx.saved_tensors
+        q, k, v, ws = saved[:4]
+        outs = list(saved[4:4 + n])
+        las = [la if present else None for la, present in zip(saved[4 + n:4 + 2 * n], ctx.ret_present)]
+        B, H, T, Dk = q.shape
+        dv_width = outs[0].shape[-1]
+        dgrads = [torch.zeros(B, H, T, dv_width, dtype=torch.bfloat16, device=q.device) if d is None
+                  else d.to(torch.bfloat16).contiguous() for d in douts]
+        args = _build_args(q, k, v, las, outs, ctx.append_unit, ws)
+        g = _lib.ScanGradArgs()
+        dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
+        dk = torch.empty_like(dq)
+        dvv = torch.empty(B, H, T, dv_width, dtype=torch.float32, device=q.device)
+        dlas = [None if la is None else torch.zeros(H, dtype=torch.float32, device=q.device) for la in las]
+        for i in range(n):
+            g.dout[i] = dgrads[i].data_ptr()
+            g.dlog_alpha[i] = None if dlas[i] is None else dlas[i].data_ptr()
+        g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dvv.data_ptr()
+        g.grad_dtype = _lib.TS_DTYPE_F32
+        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, args, q.device)
+        g.workspace, g.workspace_bytes = gws.data_ptr(), gws.numel()
+        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(args), ctypes.byref(g), _stream()))
+        if ctx.append_unit:
+            dvv = dvv[..., :-1]
+        ret_grads = []
+        for dla, dtype, shape in zip(dlas, ctx.ret_dtypes, ctx.ret_shapes):
+            ret_grads.append(None if dla is None else dla.to(dtype).reshape(shape))
+        return (dq.to(q.dtype), dk.to(k.dtype), dvv.to(v.dtype), None, None, *ret_grads)
+
+
+def _check_inputs(q, k, v, retentions, chunk):
+    if chunk < 1:
+        raise ValueError("chunk backend: chunk must be >= 1")
+    for x in (q, k, v):
+        if not x.is_cuda:
+            raise RuntimeError("b200 backend requires CUDA tensors")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise NotImplementedError(
+            "b200 backend: bf16 streams only (float32 needs the split-precision tensor-core path)")
+    H = q.shape[1]
+    for r in retentions:
+        if r is None:
+            continue
+        if r.ndim == 4:
+            if r.shape[-1] != 1:
+                raise NotImplementedError("chunk backend: scalar decay only (v1)")
+            raise NotImplementedError("b200 backend: per-token retention streams are not supported yet")
+        if r.numel() != H:
+            raise ValueError(
+                "chunk backend: a static retention needs one entry per head, "
+                f"got {tuple(r.shape)} for q {tuple(q.shape)}")
+
+
+def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_unit: bool = False):
+    """Scan one stream set through several retentions (scan_chunk.py:246-339).
+
+    ``append_unit=True`` treats the payload as ``[v | 1]`` without
+    materialising it (the key-mass read of engine.py:430); the outputs then have
+    ``Dv + 1`` columns, the last being the retention-weighted score mass.
+    """
+    if not retentions:
+        return ()
+    _check_inputs(q, k, v, retentions, chunk)
+    outs = []
+    # The kernels take at most four retentions per call; longer tuples are split.
+    for start in range(0, len(retentions), _lib.MAX_RETENTIONS):
+        group = tuple(retentions[start:start + _lib.MAX_RETENTIONS])
+        outs.extend(_ScanViews.apply(q, k, v, append_unit, q.dtype, *group))
+    return tuple(outs)
+
+
+def linattn(q, k, v, decay=None, chunk: int = DEFAULT_CHUNK, log_alpha=None):
+    """One-view scan (scan_chunk.py:342-358); ``log_alpha`` takes precedence."""
+    retention = log_alpha if log_alpha is not None else decay
+    return linattn_views(q, k, v, (retention,), chunk)[0]
