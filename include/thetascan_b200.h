@@ -124,6 +124,101 @@ typedef struct ts_scan_grad_args {
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* fwd);
 int ts_b200_scan_bwd(const ts_scan_args* fwd, const ts_scan_grad_args* grad, ts_stream_t stream);
 
+
+/* ------------------------------------------------------------------ feature maps
+ *
+ * Kernel-family write/read features, per token and head:
+ *   a = W1 x, pre = RMSNorm(a), phi = map(pre)
+ * for x = k (write keys) and x = q (read queries), and for q also the slow
+ * decode plus residual y0 = q + W2 phi(q).  Stands in for the feature chain of
+ *   engine._block_forward / dual_read_views.features
+ *   (src/thetascan/_core/ops/engine.py:117-158, 369-395, 522-526),
+ *   norms.rmsnorm (src/thetascan/_core/modules/norms.py:5-8) and
+ *   kernel_features.feature_map (src/thetascan/_core/ops/kernel_features.py:233-273).
+ */
+enum { TS_FEATURE_RELU2 = 0, TS_FEATURE_SOFTMAX = 1, TS_FEATURE_BSPLINE = 2 };
+
+typedef struct ts_feature_args {
+  int batch, heads, tokens;
+  int head_dim;             /* d, 1..128 */
+  int projections;          /* P = rows of W1, 1..256 */
+  int kind;                 /* TS_FEATURE_* */
+  int basis;                /* B-spline basis count per projection (multiple of 8, <= 16) */
+  float bound;              /* B-spline coordinate bound */
+  float eps;                /* RMSNorm / relu2 mass epsilon (core config eps) */
+  const void* k;            /* bf16 [B,H,T,d] */
+  const void* q;            /* bf16 [B,H,T,d] or NULL */
+  int64_t k_strides[3];
+  int64_t q_strides[3];
+  const void* w1;           /* bf16 [H, P, d] effective (expanded) projection, contiguous */
+  const void* w2;           /* bf16 [H, d, m] effective decode, contiguous, or NULL */
+  const float* score_bias;  /* f32 [H, m] or NULL (relu2 / softmax) */
+  const float* threshold;   /* f32 [H] or NULL (relu2) */
+  const float* gain;        /* f32 [H] or [H, m] or NULL (softmax) */
+  int gain_per_feature;     /* 1: gain is [H, m] */
+  float gain_scalar;        /* used when gain is NULL */
+  const float* spline_scale; /* f32 [H] or NULL (B-spline) */
+  float spline_scale_scalar;
+  void* phi_k;              /* bf16 [B,H,T,m] out */
+  void* phi_q;              /* bf16 [B,H,T,m] out (if q) */
+  float* y0;                /* f32 [B,H,T,d] out: q + W2 phi(q) (if q and w2), or NULL */
+} ts_feature_args;
+
+int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream);
+
+typedef struct ts_feature_grad_args {
+  const void* dphi_k;       /* [B,H,T,m] (grad_dtype of dphi_dtype) */
+  const void* dphi_q;       /* [B,H,T,m] or NULL */
+  int dphi_dtype;           /* TS_DTYPE_F32 or TS_DTYPE_BF16 */
+  const float* dy0;         /* f32 [B,H,T,d] gradient of y0, or NULL */
+  float* dk;                /* f32 [B,H,T,d] out */
+  float* dq;                /* f32 [B,H,T,d] out (includes dy0 through the residual) */
+  float* dw1;               /* f32 [H,P,d], ACCUMULATED */
+  float* dw2;               /* f32 [H,d,m], ACCUMULATED, or NULL */
+  float* dscore_bias;       /* f32 [H,m], ACCUMULATED, or NULL */
+  float* dthreshold;        /* f32 [H], ACCUMULATED, or NULL */
+  float* dgain;             /* f32 like gain, ACCUMULATED, or NULL */
+  float* dspline_scale;     /* f32 [H], ACCUMULATED, or NULL */
+} ts_feature_grad_args;
+
+int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream);
+
+/* ------------------------------------------------------------------ key-mass read
+ *
+ * Normalized read and temporal-view blend of the kernel family: from the
+ * augmented scan reads [N_s | D_s] of every retention slot (slot 0 = plain
+ * sum, slot 1+j = recency branch j) compute
+ *   y = y0 + sum_views c_view N_view / (D_view + eps)
+ * for the plain sum, a fast bank or a stale bank.  Stands in for
+ *   engine.dual_read_views.memory key_mass (src/thetascan/_core/ops/engine.py:419-442)
+ *   and ThetaScan.forward.read_with_temporal (src/thetascan/_core/modules/block.py:667-718).
+ * y is written token-major, [B,T,H,d], ready for the output gate/projection.
+ */
+enum { TS_VIEWS_SUM = 0, TS_VIEWS_FAST = 1, TS_VIEWS_STALE = 2 };
+
+typedef struct ts_kread_args {
+  int batch, heads, tokens, head_dim;
+  int mode;                 /* TS_VIEWS_* */
+  int branches;             /* J recency branches, 0..TS_MAX_RETENTIONS-1 */
+  float eps;
+  const float* slots[TS_MAX_RETENTIONS]; /* f32 [B,H,T,d+1] */
+  const float* eta;         /* f32 [J,H] blend (after any tanh), or NULL if J == 0 */
+  const float* y0;          /* f32 [B,H,T,d] */
+  void* y;                  /* bf16 [B,T,H,d] out */
+} ts_kread_args;
+
+int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream);
+
+typedef struct ts_kread_grad_args {
+  const void* dy;           /* [B,T,H,d] */
+  int dy_dtype;             /* TS_DTYPE_F32 or TS_DTYPE_BF16 */
+  void* dslots[TS_MAX_RETENTIONS]; /* bf16 [B,H,T,d+1] out: gradients of the scan reads */
+  float* dy0;               /* f32 [B,H,T,d] out */
+  float* deta;              /* f32 [J,H], ACCUMULATED, or NULL */
+} ts_kread_grad_args;
+
+int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad, ts_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -62,6 +62,59 @@ SIGNATURES = {
                                         ctypes.c_void_p]),
 }
 
+
+class FeatureArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int),
+        ("head_dim", ctypes.c_int), ("projections", ctypes.c_int), ("kind", ctypes.c_int),
+        ("basis", ctypes.c_int), ("bound", ctypes.c_float), ("eps", ctypes.c_float),
+        ("k", ctypes.c_void_p), ("q", ctypes.c_void_p),
+        ("k_strides", c_int64_3), ("q_strides", c_int64_3),
+        ("w1", ctypes.c_void_p), ("w2", ctypes.c_void_p),
+        ("score_bias", ctypes.c_void_p), ("threshold", ctypes.c_void_p), ("gain", ctypes.c_void_p),
+        ("gain_per_feature", ctypes.c_int), ("gain_scalar", ctypes.c_float),
+        ("spline_scale", ctypes.c_void_p), ("spline_scale_scalar", ctypes.c_float),
+        ("phi_k", ctypes.c_void_p), ("phi_q", ctypes.c_void_p), ("y0", ctypes.c_void_p),
+    ]
+
+
+class FeatureGradArgs(ctypes.Structure):
+    _fields_ = [
+        ("dphi_k", ctypes.c_void_p), ("dphi_q", ctypes.c_void_p), ("dphi_dtype", ctypes.c_int),
+        ("dy0", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dq", ctypes.c_void_p),
+        ("dw1", ctypes.c_void_p), ("dw2", ctypes.c_void_p),
+        ("dscore_bias", ctypes.c_void_p), ("dthreshold", ctypes.c_void_p), ("dgain", ctypes.c_void_p),
+        ("dspline_scale", ctypes.c_void_p),
+    ]
+
+
+class KReadArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("mode", ctypes.c_int), ("branches", ctypes.c_int), ("eps", ctypes.c_float),
+        ("slots", c_ptr4), ("eta", ctypes.c_void_p), ("y0", ctypes.c_void_p), ("y", ctypes.c_void_p),
+    ]
+
+
+class KReadGradArgs(ctypes.Structure):
+    _fields_ = [
+        ("dy", ctypes.c_void_p), ("dy_dtype", ctypes.c_int), ("dslots", c_ptr4),
+        ("dy0", ctypes.c_void_p), ("deta", ctypes.c_void_p),
+    ]
+
+
+TS_FEATURE_RELU2, TS_FEATURE_SOFTMAX, TS_FEATURE_BSPLINE = 0, 1, 2
+TS_VIEWS_SUM, TS_VIEWS_FAST, TS_VIEWS_STALE = 0, 1, 2
+
+SIGNATURES.update({
+    "ts_b200_feature_fwd": (ctypes.c_int, [ctypes.POINTER(FeatureArgs), ctypes.c_void_p]),
+    "ts_b200_feature_bwd": (ctypes.c_int, [ctypes.POINTER(FeatureArgs), ctypes.POINTER(FeatureGradArgs),
+                                           ctypes.c_void_p]),
+    "ts_b200_kread_fwd": (ctypes.c_int, [ctypes.POINTER(KReadArgs), ctypes.c_void_p]),
+    "ts_b200_kread_bwd": (ctypes.c_int, [ctypes.POINTER(KReadArgs), ctypes.POINTER(KReadGradArgs),
+                                         ctypes.c_void_p]),
+})
+
 _lock = threading.Lock()
 _lib = None
 

@@ -4,3 +4,6 @@
 #include "selftest.cu"
 #include "scan_fwd.cu"
 #include "scan_bwd.cu"
+#include "feature.cu"
+#include "kread.cu"
+#include "capi_kernel.cu"

@@ -1,0 +1,165 @@
+// C-ABI entry points of the kernel-family feature and key-mass-read kernels.
+#include <cstring>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ts {
+
+struct FeatParams;
+struct ReadParams;
+int launch_feature_fwd(const FeatParams& p, cudaStream_t s);
+int launch_feature_bwd(const FeatParams& p, cudaStream_t s);
+size_t feature_fwd_smem(const FeatParams& p);
+size_t feature_bwd_smem(const FeatParams& p);
+int launch_kread_fwd(const ReadParams& p, cudaStream_t s);
+int launch_kread_bwd(const ReadParams& p, cudaStream_t s);
+
+namespace {
+constexpr size_t kMaxSmemBlock = 232448;
+
+int build_feature_params(const ts_feature_args* a, FeatParams* p) {
+  if (!a) return set_error(TS_ERR_VALUE, "feature: null arguments");
+  if (a->batch < 1 || a->heads < 1 || a->tokens < 1)
+    return set_error(TS_ERR_VALUE, "feature: batch, heads and tokens must be >= 1");
+  if (a->head_dim < 1 || a->head_dim > 128)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "feature: head_dim %d outside 1..128", a->head_dim);
+  if (a->projections < 1 || a->projections > 256)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "feature: %d projections outside 1..256", a->projections);
+  if (a->kind < TS_FEATURE_RELU2 || a->kind > TS_FEATURE_BSPLINE)
+    return set_error(TS_ERR_VALUE, "feature: unknown kind %d", a->kind);
+  if (!a->k || !a->w1 || !a->phi_k) return set_error(TS_ERR_VALUE, "feature: null k, w1 or phi_k");
+  if (a->q && !a->phi_q) return set_error(TS_ERR_VALUE, "feature: phi_q is required with q");
+  std::memset(p, 0, sizeof(*p));
+  p->B = a->batch;
+  p->H = a->heads;
+  p->T = a->tokens;
+  p->d = a->head_dim;
+  p->dP = round_up(a->head_dim, 16);
+  p->P = a->projections;
+  p->PP = round_up(a->projections, 16);
+  p->PM = round_up(a->projections, 128);
+  p->kind = a->kind;
+  p->nb = a->kind == TS_FEATURE_BSPLINE ? a->basis : 1;
+  if (a->kind == TS_FEATURE_BSPLINE) {
+    if (a->basis < 8 || a->basis > 16 || a->basis % 8)
+      return set_error(TS_ERR_NOT_IMPLEMENTED, "feature: B-spline basis count %d must be 8 or 16", a->basis);
+    if (!(a->bound > 0.f)) return set_error(TS_ERR_VALUE, "feature: B-spline bound must be positive");
+  }
+  p->m = p->P * p->nb;
+  if (p->m > 256) return set_error(TS_ERR_NOT_IMPLEMENTED, "feature: feature width %d exceeds 256", p->m);
+  p->mP = round_up(p->m, 16);
+  p->mM = round_up(p->m, 128);
+  p->eps = a->eps;
+  p->bound = a->bound;
+  p->x[0] = static_cast<const __nv_bfloat16*>(a->k);
+  p->x[1] = static_cast<const __nv_bfloat16*>(a->q);
+  for (int i = 0; i < 3; ++i) {
+    p->xs[0][i] = a->k_strides[i];
+    p->xs[1][i] = a->q_strides[i];
+  }
+  p->W1 = static_cast<const __nv_bfloat16*>(a->w1);
+  p->W2 = static_cast<const __nv_bfloat16*>(a->w2);
+  p->bias = a->score_bias;
+  p->thr = a->threshold;
+  p->gain = a->gain;
+  p->gain_mode = a->gain ? (a->gain_per_feature ? 2 : 1) : 0;
+  p->gain_scalar = a->gain_scalar;
+  p->scale = a->spline_scale;
+  p->scale_scalar = a->spline_scale_scalar;
+  p->phi[0] = static_cast<__nv_bfloat16*>(a->phi_k);
+  p->phi[1] = static_cast<__nv_bfloat16*>(a->phi_q);
+  p->y0 = a->y0;
+  p->nsel = a->q ? 2 : 1;
+  p->sel0 = 0;
+  return TS_OK;
+}
+
+int build_read_params(const ts_kread_args* a, ReadParams* p) {
+  if (!a) return set_error(TS_ERR_VALUE, "kread: null arguments");
+  if (a->batch < 1 || a->heads < 1 || a->tokens < 1 || a->head_dim < 1)
+    return set_error(TS_ERR_VALUE, "kread: sizes must be >= 1");
+  if (a->mode < TS_VIEWS_SUM || a->mode > TS_VIEWS_STALE) return set_error(TS_ERR_VALUE, "kread: unknown mode");
+  const int J = a->mode == TS_VIEWS_SUM ? 0 : a->branches;
+  if (J < 0 || J > TS_MAX_RETENTIONS - 1)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "kread: %d recency branches (at most %d)", J, TS_MAX_RETENTIONS - 1);
+  if (a->mode != TS_VIEWS_SUM && J < 1) return set_error(TS_ERR_VALUE, "kread: a bank needs >= 1 branch");
+  if (J > 0 && !a->eta) return set_error(TS_ERR_VALUE, "kread: eta is required with recency branches");
+  for (int s = 0; s <= J; ++s)
+    if (!a->slots[s]) return set_error(TS_ERR_VALUE, "kread: null slot %d", s);
+  if (!a->y0) return set_error(TS_ERR_VALUE, "kread: null y0");
+  std::memset(p, 0, sizeof(*p));
+  p->B = a->batch;
+  p->H = a->heads;
+  p->T = a->tokens;
+  p->d = a->head_dim;
+  p->J = J;
+  p->mode = a->mode;
+  p->eps = a->eps;
+  for (int s = 0; s <= J; ++s) p->out[s] = a->slots[s];
+  p->eta = a->eta;
+  p->y0 = a->y0;
+  p->y = static_cast<__nv_bfloat16*>(a->y);
+  return TS_OK;
+}
+}  // namespace
+
+}  // namespace ts
+
+using namespace ts;
+
+extern "C" {
+
+int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream) {
+  FeatParams p;
+  if (int e = build_feature_params(args, &p)) return e;
+  if (feature_fwd_smem(p) > kMaxSmemBlock)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "feature: shapes exceed the shared-memory budget of one CTA");
+  return launch_feature_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream) {
+  FeatParams p;
+  if (int e = build_feature_params(args, &p)) return e;
+  if (!grad || !grad->dphi_k || !grad->dk || !grad->dw1)
+    return set_error(TS_ERR_VALUE, "feature_bwd: dphi_k, dk and dw1 are required");
+  if (args->q && (!grad->dphi_q || !grad->dq)) return set_error(TS_ERR_VALUE, "feature_bwd: dphi_q and dq are required");
+  if (feature_bwd_smem(p) > kMaxSmemBlock)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "feature_bwd: shapes exceed the shared-memory budget of one CTA");
+  p.dphi[0] = grad->dphi_k;
+  p.dphi[1] = grad->dphi_q;
+  p.dphi_bf16 = grad->dphi_dtype == TS_DTYPE_BF16;
+  p.dy = grad->dy0;
+  p.dx[0] = grad->dk;
+  p.dx[1] = grad->dq;
+  p.dW1 = grad->dw1;
+  p.dW2 = grad->dw2;
+  p.dbias = grad->dscore_bias;
+  p.dthr = grad->dthreshold;
+  p.dgain = grad->dgain;
+  p.dscale = grad->dspline_scale;
+  return launch_feature_bwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream) {
+  ReadParams p;
+  if (int e = build_read_params(args, &p)) return e;
+  if (!args->y) return set_error(TS_ERR_VALUE, "kread: null y");
+  return launch_kread_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad, ts_stream_t stream) {
+  ReadParams p;
+  if (int e = build_read_params(args, &p)) return e;
+  if (!grad || !grad->dy || !grad->dy0) return set_error(TS_ERR_VALUE, "kread_bwd: dy and dy0 are required");
+  for (int s = 0; s <= p.J; ++s)
+    if (!grad->dslots[s]) return set_error(TS_ERR_VALUE, "kread_bwd: null dslot %d", s);
+  p.dy = grad->dy;
+  p.dy_bf16 = grad->dy_dtype == TS_DTYPE_BF16;
+  for (int s = 0; s <= p.J; ++s) p.dout[s] = static_cast<__nv_bfloat16*>(grad->dslots[s]);
+  p.dy0 = grad->dy0;
+  p.deta = grad->deta;
+  return launch_kread_bwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

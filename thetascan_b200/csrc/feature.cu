@@ -1,0 +1,655 @@
+// Per-token feature maps of the kernel-family write and read, fused around a
+// tcgen05 projection.  Forward, per 128-token tile of x in {k, q}:
+//   a   = x W1^T                       (tcgen05, TMEM, f32)
+//   pre = a * rsqrt(mean(a^2) + eps)   (RMSNorm, reference norms.py:5-8)
+//   phi = map(pre)                     (kernel_features.py:116-135 relu2 ridge,
+//                                       :73-113 softmax partition,
+//                                       :138-230 projected cubic B-spline)
+// and for q additionally y0 = q + W2 phi (the slow decode of engine.py:524 plus
+// the residual of engine.py:526).  The backward recomputes a and phi and
+// produces dx = dA W1 (+ dy for q), dW1 += dA^T x, dW2 += dy^T phi and the
+// gradients of the per-head / per-feature controls.
+//
+// One thread owns one token row: the 32x32b TMEM load pattern hands every
+// thread its own accumulator row, so all row reductions stay in registers.
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ts {
+
+enum FeatureKind { kRelu2 = 0, kSoftmax = 1, kBspline = 2 };
+constexpr int kMaxBasis = 16;
+
+struct FeatParams {
+  int B, H, T;
+  int d, dP;          // head width, padded to 16
+  int P, PP, PM;      // projections, padded to 16 and to 128
+  int m, mP, mM;      // feature width, padded to 16 and to 128
+  int kind;
+  float eps;
+  int nsel, sel0;     // selections processed (0 = k, 1 = q)
+  const __nv_bfloat16* x[2];
+  long long xs[2][3];
+  const __nv_bfloat16* W1;  // [H, P, d]
+  const __nv_bfloat16* W2;  // [H, d, m] (may be null)
+  const float* bias;        // [H, m] or null
+  const float* thr;         // [H] or null
+  const float* gain;        // [H] or [H, m] or null
+  int gain_mode;            // 0 scalar, 1 per head, 2 per feature
+  float gain_scalar;
+  const float* scale;       // [H] or null
+  float scale_scalar;
+  int nb;
+  float bound;
+  // forward outputs
+  __nv_bfloat16* phi[2];    // [B, H, T, m]
+  float* y0;                // [B, H, T, d] or null (q only)
+  // backward
+  const void* dphi[2];      // [B, H, T, m], f32 or bf16
+  int dphi_bf16;
+  const float* dy;          // [B, H, T, d] (q only) or null
+  float* dx[2];             // [B, H, T, d]
+  float* dW1;               // [H, P, d]
+  float* dW2;               // [H, d, m]
+  float* dbias;             // [H, m]
+  float* dthr;              // [H]
+  float* dgain;             // [H] or [H, m]
+  float* dscale;            // [H]
+};
+
+__device__ __forceinline__ float ctl_bias(const FeatParams& p, int h, int i) {
+  return p.bias ? __ldg(p.bias + h * p.m + i) : 0.f;
+}
+__device__ __forceinline__ float ctl_gain(const FeatParams& p, int h, int i) {
+  return p.gain_mode == 0 ? p.gain_scalar : p.gain_mode == 1 ? __ldg(p.gain + h) : __ldg(p.gain + h * p.m + i);
+}
+__device__ __forceinline__ float ctl_scale(const FeatParams& p, int h) {
+  return p.scale ? __ldg(p.scale + h) : p.scale_scalar;
+}
+
+// Cubic (degree-3) open-uniform B-spline basis at x with its derivative,
+// by the Cox--de Boor recursion on knots [-b]*4, uniform interior, [b]*4
+// (reference kernel_features.py:138-205: half-open spans, zero-width spans
+// dropped, clamp to [-b, nextafter(b, -b)], negatives clamped, renormalised).
+// `inside` is false when the coordinate was clamped (zero derivative).
+__device__ __forceinline__ void bspline_eval(float c, int nb, float bound, float* val, float* der, bool& inside) {
+  const float hi = nextafterf(bound, -bound);
+  inside = (c >= -bound) && (c <= bound);
+  float x = fminf(fmaxf(c, -bound), bound);
+  if (x > hi) {
+    x = hi;
+  }
+  float knot[kMaxBasis + 4];
+  const float step = 2.f * bound / static_cast<float>(nb - 3);
+#pragma unroll
+  for (int i = 0; i < kMaxBasis + 4; ++i) {
+    float kv;
+    if (i <= 3) kv = -bound;
+    else if (i >= nb) kv = bound;
+    else kv = -bound + static_cast<float>(i - 3) * step;
+    knot[i] = kv;
+  }
+  float B[kMaxBasis + 3], D[kMaxBasis + 3];
+#pragma unroll
+  for (int i = 0; i < kMaxBasis + 3; ++i) {
+    B[i] = (i < nb + 3 && x >= knot[i] && x < knot[i + 1]) ? 1.f : 0.f;
+    D[i] = 0.f;
+  }
+#pragma unroll
+  for (int o = 1; o <= 3; ++o) {
+#pragma unroll
+    for (int i = 0; i < kMaxBasis + 3 - o; ++i) {
+      if (i >= nb + 3 - o) continue;
+      const float dl = knot[i + o] - knot[i];
+      const float dr = knot[i + o + 1] - knot[i + 1];
+      const float L = dl > 0.f ? (x - knot[i]) / dl : 0.f;
+      const float R = dr > 0.f ? (knot[i + o + 1] - x) / dr : 0.f;
+      const float dL = dl > 0.f ? 1.f / dl : 0.f;
+      const float dR = dr > 0.f ? -1.f / dr : 0.f;
+      const float nb_ = L * B[i] + R * B[i + 1];
+      const float nd_ = dL * B[i] + L * D[i] + dR * B[i + 1] + R * D[i + 1];
+      B[i] = nb_;
+      D[i] = nd_;
+    }
+  }
+  float S = 0.f, dS = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxBasis; ++i) {
+    if (i < nb) {
+      if (B[i] < 0.f) {
+        B[i] = 0.f;
+        D[i] = 0.f;
+      }
+      S += B[i];
+      dS += D[i];
+    }
+  }
+  S = fmaxf(S, 1.17549435e-38f);
+#pragma unroll
+  for (int i = 0; i < kMaxBasis; ++i) {
+    if (i < nb) {
+      val[i] = B[i] / S;
+      der[i] = (D[i] * S - B[i] * dS) / (S * S);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ shared tile setup
+
+struct FeatTiles {
+  Tile x, w1, phi, w2, dy, da;
+};
+
+__device__ __forceinline__ void load_weight_rows(const Tile& t, const __nv_bfloat16* __restrict__ src, int rows,
+                                                 int cols) {
+  load_tile(t, src, cols, rows, cols);
+}
+
+// a = x W1^T for this tile into TMEM columns [t_a, t_a + PP).
+__device__ __forceinline__ void project(const FeatParams& p, MmaCtx& ctx, const FeatTiles& tl, uint32_t t_a) {
+  ctx.run([&] { gemm_issue(t_a, kmajor(tl.x), kmajor(tl.w1), p.PP, p.dP, false); });
+}
+
+// Row statistics of the feature map for this thread's row.
+struct RowState {
+  float inv;   // 1 / rms(a)
+  float mass;  // relu2: sum of squared ReLU; softmax: sum of exp
+  float mx;    // softmax: max logit
+};
+
+__device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h) {
+  RowState s{0.f, 0.f, -INFINITY};
+  float ss = 0.f;
+  for (int c = 0; c < p.PP; c += 16) {
+    float a[16];
+    tmem_ld16(ta_row + c, a);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss += a[e] * a[e];
+  }
+  s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
+  if (p.kind == kRelu2) {
+    const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+    float M = 0.f;
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        if (i < p.P) {
+          const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i) - thr, 0.f);
+          M += u * u;
+        }
+      }
+    }
+    s.mass = M;
+  } else if (p.kind == kSoftmax) {
+    float mx = -INFINITY;
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        if (i < p.P) mx = fmaxf(mx, ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)));
+      }
+    }
+    float E = 0.f;
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        if (i < p.P) E += __expf(ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) - mx);
+      }
+    }
+    s.mx = mx;
+    s.mass = E;
+  }
+  return s;
+}
+
+// phi values for columns [c, c+16) of the (relu2 / softmax) feature row.
+__device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s, const float* a, int c, int h,
+                                          float* out) {
+  if (p.kind == kRelu2) {
+    const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+    const bool live = s.mass > p.eps;
+    const float inv_mass = 1.f / fmaxf(s.mass, p.eps);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int i = c + e;
+      const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i < p.P ? i : 0) - thr, 0.f);
+      out[e] = i < p.P ? (live ? u * u * inv_mass : 1.f / static_cast<float>(p.m)) : 0.f;
+    }
+  } else {
+    const float inv_E = 1.f / s.mass;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int i = c + e;
+      out[e] = i < p.P ? __expf(ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) - s.mx) * inv_E : 0.f;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ forward
+
+__global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int n = blockIdx.x, h = blockIdx.y;
+  const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const bool decode = sel == 1 && p.y0 != nullptr && p.W2 != nullptr;
+
+  const uint32_t base = smem_u32(smem);
+  FeatTiles tl;
+  tl.x = Tile{base, kTile, p.dP};
+  tl.w1 = Tile{tl.x.saddr + kTile * p.dP * 2, p.PP, p.dP};
+  tl.phi = Tile{tl.w1.saddr + p.PP * p.dP * 2, kTile, p.mP};
+  tl.w2 = Tile{tl.phi.saddr + kTile * p.mP * 2, p.dP, p.mP};
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  const __nv_bfloat16* xp = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(t0) * p.xs[sel][2];
+  load_tile(tl.x, xp, p.xs[sel][2], rows, p.d);
+  load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
+  if (decode) load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_a = ctx.tmem, t_y = ctx.tmem + 256;
+  project(p, ctx, tl, t_a);
+
+  const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
+  const RowState st = row_stats(p, ta_row, h);
+  __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.m;
+  const bool valid = tid < rows;
+  if (p.kind == kBspline) {
+    const float sc = ctl_scale(p, h);
+    const float invP = 1.f / static_cast<float>(p.P);
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+      for (int e = 0; e < 16; ++e) {
+        const int pj = c + e;
+        if (pj >= p.P) break;
+        float val[kMaxBasis], der[kMaxBasis];
+        bool inside;
+        bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
+        for (int i = 0; i < p.nb; i += 8) {
+          float f[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) f[q] = (i + q < p.nb) ? val[i + q] * invP : 0.f;
+          const int col = pj * p.nb + i;
+          const uint4 u = pack8(f);
+          if (valid) {
+            if (p.nb - i >= 8) {
+              *reinterpret_cast<uint4*>(out + col) = u;
+            } else {
+              for (int q = 0; q < p.nb - i; ++q) out[col + q] = __float2bfloat16_rn(f[q]);
+            }
+          }
+          if (decode) {
+            // The decode tile wants 8-aligned chunks; nb is a multiple of 8 when decoding.
+            tile_st16(tl.phi, tid, col / 8, u);
+          }
+        }
+      }
+    }
+  } else {
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16], f[16];
+      tmem_ld16(ta_row + c, a);
+      phi_chunk(p, st, a, c, h, f);
+      const uint4 u0 = pack8(f), u1 = pack8(f + 8);
+      if (valid) {
+        if (c + 16 <= p.m) {
+          *reinterpret_cast<uint4*>(out + c) = u0;
+          *reinterpret_cast<uint4*>(out + c + 8) = u1;
+        } else {
+          for (int e = 0; e < 16 && c + e < p.m; ++e) out[c + e] = __float2bfloat16_rn(f[e]);
+        }
+      }
+      if (decode) {
+        tile_st16(tl.phi, tid, c / 8, u0);
+        tile_st16(tl.phi, tid, c / 8 + 1, u1);
+      }
+    }
+  }
+  if (decode) {
+    // Padding rows past the sequence end hold valid features of zero input;
+    // they only produce y0 rows that are not stored.
+    ctx.run([&] { gemm_issue(t_y, kmajor(tl.phi), kmajor(tl.w2), p.dP, p.mP, false); });
+    float* yrow = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.d;
+    for (int c = 0; c < p.dP; c += 16) {
+      float v[16];
+      tmem_ld16(tmem_addr(t_y, warp * 32, c), v);
+      if (valid) {
+        for (int e = 0; e < 16 && c + e < p.d; ++e) yrow[c + e] = v[e] + bf2f(xp[tid * p.xs[sel][2] + c + e]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
+// ------------------------------------------------------------------ backward
+
+__device__ __forceinline__ float dphi_at(const FeatParams& p, int sel, size_t idx) {
+  return p.dphi_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.dphi[sel])[idx])
+                     : reinterpret_cast<const float*>(p.dphi[sel])[idx];
+}
+
+__global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float red[4];
+  const int n = blockIdx.x, h = blockIdx.y;
+  const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const bool valid = tid < rows;
+  const bool decode = sel == 1 && p.dy != nullptr && p.W2 != nullptr;
+
+  const uint32_t base = smem_u32(smem);
+  FeatTiles tl;
+  tl.x = Tile{base, kTile, p.dP};
+  tl.w1 = Tile{tl.x.saddr + kTile * p.dP * 2, p.PP, p.dP};
+  tl.da = Tile{tl.w1.saddr + p.PP * p.dP * 2, kTile, p.PM};
+  tl.phi = Tile{tl.da.saddr + kTile * p.PM * 2, kTile, p.mM};
+  tl.dy = Tile{tl.phi.saddr + kTile * p.mM * 2, kTile, p.dP};
+  tl.w2 = Tile{tl.dy.saddr + kTile * p.dP * 2, p.dP, p.mP};
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  const size_t rowbase = (static_cast<size_t>(b) * p.H + h) * p.T + t0;
+  const __nv_bfloat16* xp = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(t0) * p.xs[sel][2];
+  load_tile(tl.x, xp, p.xs[sel][2], rows, p.d);
+  load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
+  if (decode) {
+    load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
+    // dy rows (f32 in global) -> bf16 tile.
+    for (int j = 0; j < p.dP / 8; ++j) {
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = j * 8 + e;
+        f[e] = (valid && c < p.d) ? p.dy[(rowbase + tid) * p.d + c] : 0.f;
+      }
+      tile_st16(tl.dy, tid, j, pack8(f));
+    }
+  }
+  // Zero the padding columns of the dA / phi tiles once (M-blocks of 128).
+  for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
+  if (decode)
+    for (int j = p.mP / 8; j < p.mM / 8; ++j) tile_st16(tl.phi, tid, j, make_uint4(0, 0, 0, 0));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_a = ctx.tmem, t_hi = ctx.tmem + 256;
+  ctx.run([&] {
+    gemm_issue(t_a, kmajor(tl.x), kmajor(tl.w1), p.PP, p.dP, false);
+    if (decode) gemm_issue(t_hi, kmajor(tl.dy), mnmajor(tl.w2), p.mP, p.dP, false);
+  });
+
+  const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
+  const uint32_t tb_row = tmem_addr(t_hi, warp * 32, 0);
+  const RowState st = row_stats(p, ta_row, h);
+  const size_t prow = (rowbase + tid) * p.m;
+
+  // Gradient of the feature map -> dpre (kept in the dA tile as f32 is not
+  // possible; dpre is recomputed chunk by chunk in two sweeps instead).
+  float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
+  float dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
+  auto total_dphi = [&](int i, const float* dhi, int e) {
+    float g = valid && i < p.m ? dphi_at(p, sel, prow + i) : 0.f;
+    if (decode) g += dhi[e];
+    return g;
+  };
+  if (p.kind != kBspline) {
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16], f[16], dhi[16];
+      tmem_ld16(ta_row + c, a);
+      if (decode) tmem_ld16(tb_row + c, dhi);
+      phi_chunk(p, st, a, c, h, f);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) dot_phi += total_dphi(c + e, dhi, e) * f[e];
+    }
+  }
+  // dpre for columns [c, c+16) (projection index for B-splines).
+  auto dpre_chunk = [&](int c, const float* a, const float* dhi, float* dp) {
+    if (p.kind == kRelu2) {
+      const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+      const bool live = st.mass > p.eps;
+      const float inv_mass = 1.f / fmaxf(st.mass, p.eps);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        float g = 0.f;
+        if (i < p.P && live) {
+          const float u = fmaxf(a[e] * st.inv + ctl_bias(p, h, i) - thr, 0.f);
+          const float dz = (total_dphi(i, dhi, e) - dot_phi) * inv_mass;
+          g = dz * 2.f * u;
+        }
+        dp[e] = g;
+      }
+    } else if (p.kind == kSoftmax) {
+      const float inv_E = 1.f / st.mass;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        float g = 0.f;
+        if (i < p.P) {
+          const float gain = ctl_gain(p, h, i);
+          const float sc = a[e] * st.inv + ctl_bias(p, h, i);
+          const float ph = __expf(gain * sc - st.mx) * inv_E;
+          const float dl = ph * (total_dphi(i, dhi, e) - dot_phi);
+          g = gain * dl;
+        }
+        dp[e] = g;
+      }
+    } else {
+      const float sc = ctl_scale(p, h);
+      const float invP = 1.f / static_cast<float>(p.P);
+#pragma unroll 1
+      for (int e = 0; e < 16; ++e) {
+        const int pj = c + e;
+        float g = 0.f;
+        if (pj < p.P) {
+          float val[kMaxBasis], der[kMaxBasis];
+          bool inside;
+          bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
+          float dc = 0.f;
+          for (int i = 0; i < p.nb; ++i) {
+            const int col = pj * p.nb + i;
+            float gphi = valid ? dphi_at(p, sel, prow + col) : 0.f;
+            if (decode) {
+              float tmp[16];
+              tmem_ld16(tb_row + (col & ~15), tmp);
+              gphi += tmp[col & 15];
+            }
+            dc += gphi * der[i] * invP;
+          }
+          if (!inside) dc = 0.f;
+          g = dc * sc;
+        }
+        dp[e] = g;
+      }
+    }
+  };
+
+  // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
+  float dot_a = 0.f;
+  for (int c = 0; c < p.PP; c += 16) {
+    float a[16], dhi[16], dp[16];
+    tmem_ld16(ta_row + c, a);
+    if (decode && p.kind != kBspline) tmem_ld16(tb_row + c, dhi);
+    dpre_chunk(c, a, dhi, dp);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      dot_a += dp[e] * a[e];
+      if (p.kind == kRelu2) dthr -= dp[e];
+      if (p.kind == kSoftmax && c + e < p.P) {
+        const float gain = ctl_gain(p, h, c + e);
+        const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
+        // d gain = dl * score = dpre * score / gain
+        if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
+        if (p.gain_mode == 2 && valid) atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / gain);
+      }
+      if (p.kind == kBspline && c + e < p.P) {
+        const float sc = ctl_scale(p, h);
+        dscale += dp[e] * a[e] * st.inv / sc;
+      }
+      if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P) {
+        float db = dp[e];
+        if (p.kind == kSoftmax) db = dp[e];
+        atomicAdd(p.dbias + h * p.m + c + e, db);
+      }
+    }
+  }
+  if (!valid) {
+    dot_a = 0.f;
+    dthr = dscale = dgain_head = 0.f;
+  }
+  // Sweep 2: dA = inv * dpre - a * inv^3 * dot_a / P -> bf16 tile; phi -> tile.
+  const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
+  for (int c = 0; c < p.PP; c += 16) {
+    float a[16], dhi[16], dp[16], da[16];
+    tmem_ld16(ta_row + c, a);
+    if (decode && p.kind != kBspline) tmem_ld16(tb_row + c, dhi);
+    dpre_chunk(c, a, dhi, dp);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
+    tile_st16(tl.da, tid, c / 8, pack8(da));
+    tile_st16(tl.da, tid, c / 8 + 1, pack8(da + 8));
+    if (decode) {
+      if (p.kind != kBspline) {
+        float f[16];
+        phi_chunk(p, st, a, c, h, f);
+        if (!valid) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = 0.f;
+        }
+        tile_st16(tl.phi, tid, c / 8, pack8(f));
+        tile_st16(tl.phi, tid, c / 8 + 1, pack8(f + 8));
+      } else {
+        const float sc = ctl_scale(p, h);
+        const float invP = 1.f / static_cast<float>(p.P);
+        for (int e = 0; e < 16 && c + e < p.P; ++e) {
+          float val[kMaxBasis], der[kMaxBasis];
+          bool inside;
+          bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
+          for (int i = 0; i < p.nb; i += 8) {
+            float f[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f[q] = (valid && i + q < p.nb) ? val[i + q] * invP : 0.f;
+            tile_st16(tl.phi, tid, ((c + e) * p.nb + i) / 8, pack8(f));
+          }
+        }
+      }
+    }
+  }
+  {
+    const float s1 = block_sum128(dthr, red);
+    const float s2 = block_sum128(dscale, red);
+    const float s3 = block_sum128(dgain_head, red);
+    if (tid == 0) {
+      if (p.kind == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
+      if (p.kind == kBspline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
+      if (p.kind == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
+    }
+  }
+
+  // dx = dA W1 (+ dy for q); dW1 += dA^T x; dW2^T += phi^T dy.
+  const int pblocks = p.PM / kTile, mblocks = p.mM / kTile;
+  ctx.run([&] {
+    gemm_issue(t_hi, kmajor(tl.da), mnmajor(tl.w1), p.dP, p.PP, false);
+    for (int mb = 0; mb < pblocks; ++mb)
+      gemm_issue(t_a + mb * p.dP, mnmajor(tl.da, 0, mb * kTile), mnmajor(tl.x), p.dP, kTile, false);
+    if (decode)
+      for (int mb = 0; mb < mblocks; ++mb)
+        gemm_issue(t_a + (pblocks + mb) * p.dP, mnmajor(tl.phi, 0, mb * kTile), mnmajor(tl.dy), p.dP, kTile,
+                   false);
+  });
+  float* dxrow = p.dx[sel] + (rowbase + tid) * p.d;
+  for (int c = 0; c < p.dP; c += 16) {
+    float v[16];
+    tmem_ld16(tmem_addr(t_hi, warp * 32, c), v);
+    if (valid) {
+      for (int e = 0; e < 16 && c + e < p.d; ++e) {
+        float g = v[e];
+        if (decode) g += p.dy[(rowbase + tid) * p.d + c + e];
+        dxrow[c + e] = g;
+      }
+    }
+  }
+  for (int mb = 0; mb < pblocks; ++mb) {
+    const int prj = mb * kTile + tid;
+    for (int c = 0; c < p.dP; c += 16) {
+      float v[16];
+      tmem_ld16(tmem_addr(t_a + mb * p.dP, warp * 32, c), v);
+      if (prj < p.P && p.dW1) {
+        for (int e = 0; e < 16 && c + e < p.d; ++e) atomicAdd(p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d + c + e, v[e]);
+      }
+    }
+  }
+  if (decode) {
+    for (int mb = 0; mb < mblocks; ++mb) {
+      const int fi = mb * kTile + tid;
+      for (int c = 0; c < p.dP; c += 16) {
+        float v[16];
+        tmem_ld16(tmem_addr(t_a + (pblocks + mb) * p.dP, warp * 32, c), v);
+        if (fi < p.m && p.dW2) {
+          for (int e = 0; e < 16 && c + e < p.d; ++e)
+            atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.d + c + e) * p.m + fi, v[e]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
+// ------------------------------------------------------------------ host launch
+
+size_t feature_fwd_smem(const FeatParams& p) {
+  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.mP + p.dP * p.mP) * 2;
+}
+size_t feature_bwd_smem(const FeatParams& p) {
+  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.PM + kTile * p.mM + kTile * p.dP + p.dP * p.mP) * 2;
+}
+
+int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
+  const size_t sm = feature_fwd_smem(p);
+  cudaFuncSetAttribute(feature_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  const int NT = ceil_div(p.T, kTile);
+  feature_fwd_kernel<<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  return check_launch("feature_fwd_kernel");
+}
+
+int launch_feature_bwd(const FeatParams& p, cudaStream_t s) {
+  const size_t sm = feature_bwd_smem(p);
+  cudaFuncSetAttribute(feature_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  const int NT = ceil_div(p.T, kTile);
+  feature_bwd_kernel<<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  return check_launch("feature_bwd_kernel");
+}
+
+}  // namespace ts

@@ -6,10 +6,18 @@
 // where ds = sum_r w_r o causal o g_r, P_r = w_r o causal o (q.k^T), S_in,r is
 // the forward state entering the tile and G_r the gradient of the state leaving
 // it, obtained by a reverse exclusive scan of the local terms
-// sum_t c_r(t) q_t^T dout_r[t].  The log-retention gradient uses
-//   d/d la_r = sum_t (t - c) dout_r[t].out_r[t] - sum_j (j - c) v_j.dv_j^(r)
-// for any constant c (each pair (t, j) contributes (t - j) w s g), so it needs
-// no per-pair work beyond what dq and dv already do.  Kernels:
+// sum_t c_r(t) q_t^T dout_r[t].
+//
+// Log-retention gradient.  Every pair (t, j), j <= t, contributes
+// (t - j) w s g with g = dout_r[t].v_j.  Writing t - j with tile-local,
+// tile-centred positions (i - 63.5) - (j' - 63.5) plus 128 per tile boundary
+// the pair crosses, and noting that the pairs crossing boundary n sum to
+// <G_n, S_in(n+1)>, gives
+//   d/d la_r = sum_tiles [ sum_t (i_t - 63.5) dout_r[t].out_r[t]
+//                        - sum_j (j'_j - 63.5) v_j.dv_j^(r) ]
+//            + 128 sum_n <G_n, S_in(n+1)>,
+// local sums of bounded weight plus an f32 state contraction, so no large
+// terms cancel.  Kernels:
 //   scan_bwd_state_kernel  local dS per tile                     (tcgen05)
 //   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
 //   scan_bwd_dq_kernel     ds (accumulated in TMEM), dq, e-term  (tcgen05)
@@ -64,8 +72,7 @@ __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaC
         const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
         for (int c = 0; c < p.Dv; ++c) e_t += __bfloat162float(dp[tid * p.Dv + c]) * out_value(p, r, row + c);
       }
-      const float center = 0.5f * static_cast<float>(p.T - 1);
-      const float s = block_sum128((static_cast<float>(t0 + tid) - center) * e_t, red);
+      const float s = block_sum128((static_cast<float>(tid) - 63.5f) * e_t, red);
       if (tid == 0) atomicAdd(g.dla[r] + h, s);
     }
   }
@@ -104,7 +111,7 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int n) {
 // ------------------------------------------------------------------ local dS
 
 __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, ScanGradParams g) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x + 1, h = blockIdx.y, b = blockIdx.z;
@@ -163,15 +170,15 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
   const int r = blockIdx.y;
   const int bh = blockIdx.z;
   const int b = bh / p.H, h = bh % p.H;
-  if (e >= p.DkM * p.DvP) return;
-  const int f = e / p.DvP, c = e % p.DvP;
+  const bool active = e < p.DkM * p.DvP;
+  const int f = active ? e / p.DvP : 0, c = active ? e % p.DvP : 0;
   const float la = head_la(p, r, h);
   const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
-  const bool in_image = f < p.DkP;
+  const bool in_image = active && f < p.DkP;
   const Tile img{0u, p.DvP, p.DkP};
   const uint32_t img_off = in_image ? tile_off(img, c, f) : 0u;
-  float G = 0.f;
-  for (int n = p.NT - 1; n >= 0; --n) {
+  float G = 0.f, boundary = 0.f;
+  for (int n = p.NT - 1; n >= 0 && active; --n) {
     const size_t si = state_index(p, b, h, n, r);
     float* ptr = g.gstates + si * p.DkM * p.DvP + e;
     const float local = (n >= 1) ? *ptr : 0.f;
@@ -180,14 +187,29 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
       uint8_t* img_base = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p));
       *reinterpret_cast<__nv_bfloat16*>(img_base + img_off) = __float2bfloat16_rn(G);
     }
+    // <G_n, S_in(n+1)>: every pair crossing the boundary after tile n.
+    if (n + 1 < p.NT) boundary += G * p.states[state_index(p, b, h, n + 1, r) * p.DkM * p.DvP + e];
     G = G * closing + local;
+  }
+  if (p.la[r] != nullptr && g.dla[r] != nullptr) {
+    __shared__ float red[8];
+    float v = boundary * static_cast<float>(kTile);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red[w];
+      atomicAdd(g.dla[r] + h, s);
+    }
   }
 }
 
 // ------------------------------------------------------------------ dq
 
 __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, ScanGradParams g) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   __shared__ float red[4];
@@ -242,7 +264,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
 // ------------------------------------------------------------------ dk
 
 __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, ScanGradParams g) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -303,7 +325,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
 // ------------------------------------------------------------------ dv
 
 __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, ScanGradParams g) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   __shared__ float red[4];
@@ -371,7 +393,6 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
 
   // dv = sum_r dv_r; f-term of the log-retention gradient per retention.
   const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
-  const float center = 0.5f * static_cast<float>(p.T - 1);
   for (int c = 0; c < p.DvP; c += 16) {
     float acc[16];
 #pragma unroll
@@ -400,7 +421,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
       for (int e = 0; e < 8; ++e) f_j += x[e] * v[e] + y[e] * v[e + 8];
     }
     if (tid >= rows) f_j = 0.f;
-    const float s = block_sum128((static_cast<float>(t0 + tid) - center) * f_j, red);
+    const float s = block_sum128((static_cast<float>(tid) - 63.5f) * f_j, red);
     if (tid == 0) atomicAdd(g.dla[r] + h, -s);
   }
   tc_fence_before();

@@ -13,7 +13,7 @@ namespace ts {
 // ------------------------------------------------------------------ 1. tile states
 
 __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
 // ------------------------------------------------------------------ 3. tile outputs
 
 __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;

@@ -12,7 +12,7 @@ __global__ void __launch_bounds__(kThreads) selftest_mma_kernel(const __nv_bfloa
                                                                 const __nv_bfloat16* __restrict__ B,
                                                                 float* __restrict__ D, int N, int K,
                                                                 int a_mn, int b_mn) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
 

@@ -74,7 +74,9 @@ class _ScanViews(torch.autograd.Function):
         las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
         B, H, T, _ = q.shape
         dv = v.shape[-1] + (1 if append_unit else 0)
-        outs = [torch.empty(B, H, T, dv, dtype=out_dtype, device=q.device) for _ in las]
+        # The kernels write f32 reads; the backward's log-retention term uses
+        # them unrounded, and the caller gets them in the stream dtype.
+        outs = [torch.empty(B, H, T, dv, dtype=torch.float32, device=q.device) for _ in las]
         args = _build_args(q, k, v, las, outs, append_unit)
         ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
         args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -86,7 +88,7 @@ class _ScanViews(torch.autograd.Function):
         ctx.ret_shapes = [None if r is None else r.shape for r in retentions]
         saved_las = [la if la is not None else torch.empty(0, device=q.device) for la in las]
         ctx.save_for_backward(q, k, v, ws, *outs, *saved_las)
-        return tuple(outs)
+        return tuple(o.to(out_dtype) for o in outs)
 
     @staticmethod
     def backward(ctx, *douts):
