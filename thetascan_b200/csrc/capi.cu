@@ -138,7 +138,7 @@ size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* args) {
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;
-  return states_bytes(p) + images_bytes(p);
+  return 2 * states_bytes(p) + images_bytes(p);
 }
 
 int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
@@ -159,8 +159,9 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   const size_t need = states_bytes(p) + images_bytes(p);
   if (!args->workspace || args->workspace_bytes < need)
     return set_error(TS_ERR_VALUE, "scan_bwd: the forward workspace (%zu bytes) is required", need);
-  if (!grad->workspace || grad->workspace_bytes < need)
-    return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need);
+  const size_t need_bwd = 2 * states_bytes(p) + images_bytes(p);
+  if (!grad->workspace || grad->workspace_bytes < need_bwd)
+    return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need_bwd);
   if (!grad->dq || !grad->dk || !grad->dv) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
   p.states = static_cast<float*>(args->workspace);
   p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
@@ -177,6 +178,7 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   g.grad_bf16 = grad->grad_dtype == TS_DTYPE_BF16;
   g.gstates = static_cast<float*>(grad->workspace);
   g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));
+  g.pstates = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p) + images_bytes(p));
   return launch_scan_bwd(p, g, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -42,6 +42,7 @@ struct ScanGradParams {
   int grad_bf16;
   float* dla[4];
   float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place
+  float* pstates;            // [B,H,NT,R,DkM,DvP] f32: key-weight derivative of each tile's state
   __nv_bfloat16* gimages;    // [B,H,NT,R] images of G (DvP rows x DkP cols)
 };
 

@@ -8,16 +8,15 @@
 // it, obtained by a reverse exclusive scan of the local terms
 // sum_t c_r(t) q_t^T dout_r[t].
 //
-// Log-retention gradient.  Every pair (t, j), j <= t, contributes
-// (t - j) w s g with g = dout_r[t].v_j.  Writing t - j with tile-local,
-// tile-centred positions (i - 63.5) - (j' - 63.5) plus 128 per tile boundary
-// the pair crosses, and noting that the pairs crossing boundary n sum to
-// <G_n, S_in(n+1)>, gives
-//   d/d la_r = sum_tiles [ sum_t (i_t - 63.5) dout_r[t].out_r[t]
-//                        - sum_j (j'_j - 63.5) v_j.dv_j^(r) ]
-//            + 128 sum_n <G_n, S_in(n+1)>,
-// local sums of bounded weight plus an f32 state contraction, so no large
-// terms cancel.  Kernels:
+// Log-retention gradient, by reverse mode through the tile recursion
+//   S_in(n+1) = e^{128 la} S_in(n) + sum_j e^{la (127-j)} k_j^T v_j,
+//   out_t     = intra_t + e^{la (i+1)} q_t S_in(n):
+//   d/d la_r = sum_tiles sum_{i>=j} (i-j) w s g                 (intra pairs)
+//            + sum_n <S_in(n), sum_t (i+1) c(i) q_t^T dout_t>     (carries)
+//            + sum_n <G_n, sum_j (127-j) u(j) k_j^T v_j>         (key weights)
+//            + 128 sum_n e^{128 la} <G_n, S_in(n)>              (tile closings)
+// with g = dout . v^T.  Every term is a natural sum of positive-weight
+// contractions (no two large terms cancel), evaluated in f32.  Kernels:
 //   scan_bwd_state_kernel  local dS per tile                     (tcgen05)
 //   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
 //   scan_bwd_dq_kernel     ds (accumulated in TMEM), dq, e-term  (tcgen05)
@@ -35,17 +34,10 @@ __device__ __forceinline__ const __nv_bfloat16* dout_rows(const ScanParams& p, c
   return g.dout[r] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
 }
 
-__device__ __forceinline__ float out_value(const ScanParams& p, int r, size_t idx) {
-  return p.out_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.out[r])[idx])
-                    : reinterpret_cast<const float*>(p.out[r])[idx];
-}
-
 // ds_acc (TMEM, 128 columns at t_ds) = sum_r w_r o causal o (dout_r . v^T).
 // Uses tiles td (dout staging) and tv (payload), TMEM columns t_g for g_r.
-// Also accumulates the e-term of the log-retention gradient when `eterm`.
 __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile& td,
-                              const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows,
-                              bool eterm, float* red) {
+                              const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows) {
   const int tid = threadIdx.x, warp = tid >> 5;
   for (int r = 0; r < p.R; ++r) {
     const __nv_bfloat16* dp = dout_rows(p, g, r, b, h, t0);
@@ -65,15 +57,6 @@ __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaC
         acc[e] = (r > 0) ? acc[e] + term : term;
       }
       tmem_st16(tmem_addr(t_ds, warp * 32, c), acc);
-    }
-    if (eterm && decayed && g.dla[r] != nullptr) {
-      float e_t = 0.f;
-      if (tid < rows) {
-        const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
-        for (int c = 0; c < p.Dv; ++c) e_t += __bfloat162float(dp[tid * p.Dv + c]) * out_value(p, r, row + c);
-      }
-      const float s = block_sum128((static_cast<float>(tid) - 63.5f) * e_t, red);
-      if (tid == 0) atomicAdd(g.dla[r] + h, s);
     }
   }
 }
@@ -110,19 +93,30 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int n) {
 
 // ------------------------------------------------------------------ local dS
 
+// Per tile n and retention r:
+//   dSloc(n) = sum_t c(i) q_t^T dout_t                       -> gstates (n >= 1)
+// and, when the log-retention gradient is wanted,
+//   <S_in(n), sum_t (i+1) c(i) q_t^T dout_t>                 -> dla (n >= 1)
+//   B'(n)    = sum_j (127-j) u(j) k_j^T v_j                  -> pstates (n <= NT-2)
 __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, ScanGradParams g) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
-  const int n = blockIdx.x + 1, h = blockIdx.y, b = blockIdx.z;
+  __shared__ float red[4];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
   Tile tq{base, kTile, p.DkM};
   Tile tw{tq.saddr + kTile * p.DkM * 2, kTile, p.DvP};
+  Tile tk{tw.saddr + kTile * p.DvP * 2, kTile, p.DkM};
+  Tile tv{tk.saddr + kTile * p.DkM * 2, kTile, p.DvP};
   const int mblocks = p.DkM / kTile;
-  const uint32_t ncols = tmem_cols_for(p.R * mblocks * p.DvP);
+  const int region = mblocks * p.DvP;
+  const uint32_t ncols = tmem_cols_for(2 * region);
+  bool any_dla = false;
+  for (int r = 0; r < p.R; ++r) any_dla |= (p.la[r] != nullptr && g.dla[r] != nullptr);
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
@@ -130,31 +124,90 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   if (warp == 0) tmem_alloc(&tmem_base, ncols);
   const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
+  if (any_dla && n + 1 < p.NT) {
+    const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+    const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+    load_tile(tk, kp, p.ks[2], rows, p.Dk);
+    load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_d = ctx.tmem, t_x = ctx.tmem + static_cast<uint32_t>(region);
+
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
-    load_scaled_rows(tw, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
-                     [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
-    ctx.run([&] {
-      for (int mb = 0; mb < mblocks; ++mb)
-        gemm_issue(ctx.tmem + static_cast<uint32_t>((r * mblocks + mb) * p.DvP), mnmajor(tq, 0, mb * kTile),
-                   mnmajor(tw), p.DvP, kTile, false);
-    });
-  }
-  for (int r = 0; r < p.R; ++r) {
-    float* dst_base = g.gstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
-    for (int mb = 0; mb < mblocks; ++mb) {
-      float* dst = dst_base + static_cast<size_t>(mb * kTile + tid) * p.DvP;
-      for (int c = 0; c < p.DvP; c += 16) {
-        float v[16];
-        tmem_ld16(tmem_addr(ctx.tmem, warp * 32, (r * mblocks + mb) * p.DvP + c), v);
+    const bool want = decayed && g.dla[r] != nullptr;
+    if (n >= 1) {
+      // dSloc (region d) and, for the gradient, the (i+1)-weighted copy (region x).
+      load_scaled_rows(tw, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
+                       [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
+      ctx.run([&] {
+        for (int mb = 0; mb < mblocks; ++mb)
+          gemm_issue(t_d + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+      });
+      if (want) {
+        for (int j = 0; j < p.DvP / 8; ++j) {
+          float f[8];
+          unpack8(tile_ld16(tw, tid, j), f);
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          *reinterpret_cast<float4*>(dst + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          for (int e = 0; e < 8; ++e) f[e] *= static_cast<float>(tid + 1);
+          tile_st16(tw, tid, j, pack8(f));
+        }
+        ctx.run([&] {
+          for (int mb = 0; mb < mblocks; ++mb)
+            gemm_issue(t_x + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+        });
+      }
+      float carry_dot = 0.f;
+      const size_t si = state_index(p, b, h, n, r) * p.DkM * p.DvP;
+      for (int mb = 0; mb < mblocks; ++mb) {
+        const size_t frow = static_cast<size_t>(mb * kTile + tid) * p.DvP;
+        for (int c = 0; c < p.DvP; c += 16) {
+          float v[16];
+          tmem_ld16(tmem_addr(t_d, warp * 32, mb * p.DvP + c), v);
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(g.gstates + si + frow + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          if (want) {
+            float x[16];
+            tmem_ld16(tmem_addr(t_x, warp * 32, mb * p.DvP + c), x);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) carry_dot += x[e] * p.states[si + frow + c + e];
+          }
+        }
+      }
+      if (want) {
+        const float sum = block_sum128(carry_dot, red);
+        if (tid == 0) atomicAdd(g.dla[r] + h, sum);
+      }
+    }
+    if (want && n + 1 < p.NT) {
+      // B'(n): key-weight derivative of the state this tile leaves behind.
+      for (int j = 0; j < p.DvP / 8; ++j) {
+        float f[8];
+        unpack8(tile_ld16(tv, tid, j), f);
+        const float wgt = static_cast<float>(kTile - 1 - tid) * __expf(la * static_cast<float>(kTile - 1 - tid));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= wgt;
+        tile_st16(tw, tid, j, pack8(f));
+      }
+      ctx.run([&] {
+        for (int mb = 0; mb < mblocks; ++mb)
+          gemm_issue(t_x + mb * p.DvP, mnmajor(tk, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+      });
+      float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+      for (int mb = 0; mb < mblocks; ++mb) {
+        float* row = dst + static_cast<size_t>(mb * kTile + tid) * p.DvP;
+        for (int c = 0; c < p.DvP; c += 16) {
+          float v[16];
+          tmem_ld16(tmem_addr(t_x, warp * 32, mb * p.DvP + c), v);
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(row + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        }
       }
     }
   }
@@ -165,6 +218,8 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
 
 // ------------------------------------------------------------------ reverse prefix
 
+// G(n) = e^{128 la} G(n+1) + dSloc(n+1), G(NT-1) = 0, per state element; and
+// the key-weight and closing terms of the log-retention gradient.
 __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, ScanGradParams g) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   const int r = blockIdx.y;
@@ -174,34 +229,35 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
   const int f = active ? e / p.DvP : 0, c = active ? e % p.DvP : 0;
   const float la = head_la(p, r, h);
   const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const bool want = p.la[r] != nullptr && g.dla[r] != nullptr;
   const bool in_image = active && f < p.DkP;
   const Tile img{0u, p.DvP, p.DkP};
   const uint32_t img_off = in_image ? tile_off(img, c, f) : 0u;
-  float G = 0.f, boundary = 0.f;
+  float G = 0.f, acc = 0.f;
   for (int n = p.NT - 1; n >= 0 && active; --n) {
-    const size_t si = state_index(p, b, h, n, r);
-    float* ptr = g.gstates + si * p.DkM * p.DvP + e;
-    const float local = (n >= 1) ? *ptr : 0.f;
-    *ptr = G;
+    const size_t si = state_index(p, b, h, n, r) * p.DkM * p.DvP + e;
+    const float local = (n >= 1) ? g.gstates[si] : 0.f;
+    g.gstates[si] = G;
     if (in_image) {
-      uint8_t* img_base = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p));
+      uint8_t* img_base = reinterpret_cast<uint8_t*>(g.gimages) +
+                          state_index(p, b, h, n, r) * static_cast<size_t>(image_bytes(p));
       *reinterpret_cast<__nv_bfloat16*>(img_base + img_off) = __float2bfloat16_rn(G);
     }
-    // <G_n, S_in(n+1)>: every pair crossing the boundary after tile n.
-    if (n + 1 < p.NT) boundary += G * p.states[state_index(p, b, h, n + 1, r) * p.DkM * p.DvP + e];
+    if (want && n + 1 < p.NT)
+      acc += G * (g.pstates[si] + static_cast<float>(kTile) * closing * p.states[si]);
     G = G * closing + local;
   }
-  if (p.la[r] != nullptr && g.dla[r] != nullptr) {
+  if (want) {
     __shared__ float red[8];
-    float v = boundary * static_cast<float>(kTile);
+    float v = acc;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     if (threadIdx.x == 0) {
-      float s = 0.f;
-      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red[w];
-      atomicAdd(g.dla[r] + h, s);
+      float sum = 0.f;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
+      atomicAdd(g.dla[r] + h, sum);
     }
   }
 }
@@ -212,7 +268,6 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
-  __shared__ float red[4];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t0 = n * kTile;
@@ -239,7 +294,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dq = ctx.tmem + 256;
 
-  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows, true, red);
+  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows);
   ds_to_tile(t_ds, tds);
   ctx.run([&] { gemm_issue(t_dq, kmajor(tds), mnmajor(tk), p.DkP, kTile, false); });
   if (n > 0) {
@@ -293,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dk = ctx.tmem + 256;
 
-  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows, false, nullptr);
+  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows);
   ds_to_tile(t_ds, tds);
   ctx.run([&] { gemm_issue(t_dk, mnmajor(tds), mnmajor(tq), p.DkP, kTile, false); });
   if (n + 1 < p.NT) {
@@ -324,6 +379,9 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
 
 // ------------------------------------------------------------------ dv
 
+// dv = sum_r [ P_r^T dout_r + (u_r o k) G_r ], accumulated in one TMEM region,
+// plus the intra-tile pairs of the log-retention gradient,
+// sum_{i>=j} (i-j) w s g with g = dout_r . v^T.
 __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, ScanGradParams g) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
@@ -340,7 +398,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
   Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
-  const uint32_t ncols = tmem_cols_for(kTile + p.R * p.DvP);
+  const uint32_t ncols = tmem_cols_for(2 * kTile + p.DvP);
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
@@ -356,13 +414,14 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   __syncthreads();
   tc_fence_after();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
-  const uint32_t t_s = ctx.tmem;
+  const uint32_t t_s = ctx.tmem, t_g = ctx.tmem + kTile, t_dv = ctx.tmem + 2 * kTile;
   ctx.run([&] { gemm_issue(t_s, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
 
   const bool cross = n + 1 < p.NT;
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
+    const bool want = decayed && g.dla[r] != nullptr;
     for (int c = 0; c < kTile; c += 16) {
       float s[16], f[16];
       tmem_ld16(tmem_addr(t_s, warp * 32, c), s);
@@ -384,45 +443,38 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
       load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
                  image_bytes(p));
     }
-    const uint32_t t_dv = ctx.tmem + static_cast<uint32_t>(kTile + r * p.DvP);
     ctx.run([&] {
-      gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, false);
+      gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, r > 0);
       if (cross) gemm_issue(t_dv, kmajor(tq), kmajor(tg), p.DvP, p.DkP, true);
+      if (want) gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false);
     });
+    if (want) {
+      float acc = 0.f;
+      for (int c = 0; c < kTile; c += 16) {
+        float s[16], gv[16];
+        tmem_ld16(tmem_addr(t_s, warp * 32, c), s);
+        tmem_ld16(tmem_addr(t_g, warp * 32, c), gv);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int j = c + e;
+          const float lag = static_cast<float>(tid - j);
+          if (j <= tid) acc += lag * __expf(la * lag) * s[e] * gv[e];
+        }
+      }
+      const float sum = block_sum128(acc, red);
+      if (tid == 0) atomicAdd(g.dla[r] + h, sum);
+    }
   }
 
-  // dv = sum_r dv_r; f-term of the log-retention gradient per retention.
   const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
   for (int c = 0; c < p.DvP; c += 16) {
-    float acc[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = 0.f;
-    for (int r = 0; r < p.R; ++r) {
-      float v[16];
-      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[e] += v[e];
-    }
+    float v[16];
+    tmem_ld16(tmem_addr(t_dv, warp * 32, c), v);
     if (tid < rows) {
 #pragma unroll
       for (int e = 0; e < 16; ++e)
-        if (c + e < p.Dv) store_out(g.dv, g.grad_bf16, row + c + e, acc[e]);
+        if (c + e < p.Dv) store_out(g.dv, g.grad_bf16, row + c + e, v[e]);
     }
-  }
-  for (int r = 0; r < p.R; ++r) {
-    if (p.la[r] == nullptr || g.dla[r] == nullptr) continue;
-    float f_j = 0.f;
-    for (int c = 0; c < p.DvP; c += 16) {
-      float v[16], x[8], y[8];
-      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
-      unpack8(tile_ld16(tv, tid, c / 8), x);
-      unpack8(tile_ld16(tv, tid, c / 8 + 1), y);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f_j += x[e] * v[e] + y[e] * v[e + 8];
-    }
-    if (tid >= rows) f_j = 0.f;
-    const float s = block_sum128((static_cast<float>(tid) - 63.5f) * f_j, red);
-    if (tid == 0) atomicAdd(g.dla[r] + h, -s);
   }
   tc_fence_before();
   __syncthreads();
@@ -437,7 +489,7 @@ static size_t dq_smem(const ScanParams& p) {
 static size_t dv_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2;
 }
-static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (p.DkM + p.DvP) * 2; }
+static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (2 * p.DkM + 2 * p.DvP) * 2; }
 
 size_t scan_bwd_max_smem(const ScanParams& p) {
   size_t m = dq_smem(p);
@@ -453,7 +505,7 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
   cudaFuncSetAttribute(scan_bwd_dk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dq));
   cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
   if (p.NT > 1) {
-    scan_bwd_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, s_state, s>>>(p, g);
+    scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
     if (int e = check_launch("scan_bwd_state_kernel")) return e;
   }
   scan_bwd_prefix_kernel<<<dim3(ceil_div(p.DkM * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p, g);

@@ -226,4 +226,8 @@ def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias
             raise ValueError("b200 backend: streams need a contiguous innermost dimension")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core: log_alphas are required exactly for a bank (mode fast/stale)")
+    if spec.mode == "stale":
+        raise NotImplementedError(
+            "b200 backend: the stale bank reads a difference of two scans whose mass can vanish; "
+            "its dedicated retention kind is not built yet (fast banks are supported)")
     return _KernelCore.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas)
