@@ -1,0 +1,416 @@
+"""Benchmark: ThetaScan mixer forward+backward tokens/s on B200.
+
+Default workload (N=1): config 2 of the baseline -- kernel family, ReLU^2
+ridge features, m = 256 from 2x random feature expansion, partial RoPE, a
+one-branch fast recency bank with per-head alpha ~ U(0.9, 0.999), output gate,
+B=8, T=4096, d_model=1024, H=16, d=64, bf16 activations with f32 state.
+A step is one forward + backward of the whole mixer (projections included)
+on synthetic x ~ N(0,1) with loss = mean(y^2).
+
+With --gpus N (torchrun, one rank per GPU) every rank runs its own batch of
+the same shape (weak scaling: independent (batch, head) units) and the ranks
+all-reduce the mixer's parameter gradients over NCCL, as a data-parallel
+step does.  ``--impl reference`` times the reference's CPU implementation
+(the float32 oracle restatement of its chunk backend) on the host cores.
+
+One JSON line is printed by rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "mixer fwd+bwd tokens/s at T=4K/32K, 1/2/4/8 B200, % of tensor roofline"
+CONFIGS = {
+    # name: (B, T, d_model, H, memory_multiplier, expansion, feature_map, rope, J)
+    "c2": dict(B=8, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+    "small": dict(B=2, T=1024, D=512, H=8, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+}
+
+
+# --------------------------------------------------------------------------- workload
+
+def build_module(cfg, device):
+    from thetascan_b200.config import KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+    config = ThetaScanConfig(
+        d_model=cfg["D"], n_heads=cfg["H"], memory_multiplier=cfg["mult"], feature_expansion=cfg["expansion"],
+        family="kernel", kernel=KernelConfig(feature_map=cfg["fmap"]),
+        rope=RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=TemporalConfig(mode="bank", retention_init=0.95))
+    torch.manual_seed(0)
+    module = ThetaScan(config)
+    with torch.no_grad():
+        alphas = 0.9 + 0.099 * torch.rand(cfg["H"], generator=torch.Generator().manual_seed(0))
+        module._core.fade_alpha.copy_(torch.log(alphas / (1.0 - alphas)))
+    return module.to(device), config
+
+
+def flops_per_token(cfg):
+    """Algorithmic FLOPs per token, forward+backward (= 3x forward).
+
+    Fixed counting convention: reference chunk C=64 with causal-half score,
+    elementwise work counted as zero.  Returns (core, full mixer, per-phase
+    forward FLOPs per token)."""
+    H, d = cfg["H"], cfg["D"] // cfg["H"]
+    m = cfg["mult"] * d
+    P, C, V = m, 64, 1 + cfg["J"]
+    feature = 4 * P * d + 2 * d * m
+    scan = C * m + V * (C * (d + 1) + 4 * m * (d + 1))
+    D, Hd = cfg["D"], H * d
+    proj = 2 * D * 3 * Hd + 2 * Hd * D + 2 * D * Hd
+    core = 3 * H * (feature + scan)
+    return core, core + 3 * proj, {"feature": H * feature, "scan": H * scan}
+
+
+# --------------------------------------------------------------------------- measurement helpers
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+class PhaseTimer:
+    """Time each C-ABI entry point with CUDA events on the launching stream.
+
+    Wraps the bound ctypes functions of the library; counts our kernel
+    launches per entry point."""
+
+    KERNELS = {"ts_b200_feature_fwd": 1, "ts_b200_scan_fwd": 3, "ts_b200_kread_fwd": 1,
+               "ts_b200_kread_bwd": 1, "ts_b200_scan_bwd": 5, "ts_b200_feature_bwd": 1}
+
+    def __init__(self, lib):
+        self.lib = lib
+        self.saved = {}
+        self.events = {name: [] for name in self.KERNELS}
+        self.calls = {name: 0 for name in self.KERNELS}
+        self.timing = False
+
+    def install(self):
+        for name in self.KERNELS:
+            fn = getattr(self.lib, name)
+            self.saved[name] = fn
+
+            def wrapper(*a, _fn=fn, _name=name):
+                self.calls[_name] += 1
+                if not self.timing:
+                    return _fn(*a)
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                rc = _fn(*a)
+                end.record()
+                self.events[_name].append((start, end))
+                return rc
+            setattr(self.lib, name, wrapper)
+
+    def uninstall(self):
+        for name, fn in self.saved.items():
+            setattr(self.lib, name, fn)
+
+    def launches(self):
+        return sum(self.calls[n] * k for n, k in self.KERNELS.items())
+
+    def mean_ms(self):
+        torch.cuda.synchronize()
+        return {n: statistics.mean(s.elapsed_time(e) for s, e in ev) for n, ev in self.events.items() if ev}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+        return peaks.get("bf16_tflops_sustained", 1403.9), peaks.get("bf16_tflops", 1638.2), "measured"
+    return 1400.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------------------------- CPU reference
+
+def cpu_reference_step(cfg, T, view_set):
+    """One forward+backward of the reference CPU algorithm (oracle restatement).
+
+    ``view_set="bank"`` runs the chunk form with the full bank (the
+    reference's fastest CPU path); ``"sum"`` runs the prefix-sum (cumsum)
+    backend, which the reference restricts to the plain sum view."""
+    from oracle import mixer as omixer
+    from oracle import scan as oscan
+
+    module, _ = build_module(cfg, torch.device("cpu"))
+    params = {n: t.detach().float().requires_grad_(True) for n, t in module._core.named_parameters()}
+    for n, t in module._core.named_buffers():
+        if n.startswith("_expand_"):
+            params[n] = t.float()
+    d = cfg["D"] // cfg["H"]
+    core_cfg = {"n_heads": cfg["H"], "head_dim": d, "feature_expansion": cfg["expansion"],
+                "kernel_kind": cfg["fmap"], "rope": cfg["rope"], "rope_frac": 0.5, "rope_base": 10000.0,
+                "read_fade": view_set == "bank", "read_fade_mode": "fast", "read_norm": "key_mass", "eps": 1e-6,
+                "scan_chunk": 512}
+    if view_set == "sum":
+        scan_fn = lambda q, k, v, rets: tuple(oscan.linattn_cumsum(q, k, v) for _ in rets)
+    else:
+        scan_fn = None
+    x = torch.randn(1, T, cfg["D"], generator=torch.Generator().manual_seed(0))
+    t0 = time.perf_counter()
+    y = omixer.mixer_forward(params, core_cfg, x, scan_fn=scan_fn)
+    y.square().mean().backward()
+    return time.perf_counter() - t0
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    T = args.ref_tokens
+    cpu_reference_step(cfg, 128, "bank")  # warm-up of the allocator and kernels
+    times = [cpu_reference_step(cfg, T, "bank") for _ in range(max(1, args.steps))]
+    per_step = statistics.median(times)
+    value = T / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": len(times), "warmup": 1, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config 2 per-token shape, bounded CPU sample B=1 T={T}", "model": "ThetaScan-Kernel",
+                   "global_batch": 1, "seq_len": T, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"B=1, T={T}, full bank, chunk form of the reference (float32 oracle restatement), "
+                                   f"forward+backward, median of {len(times)}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def run_b200(args, cfg):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    from thetascan_b200 import _lib
+
+    module, config = build_module(cfg, device)
+    params = [p for p in module.parameters() if p.requires_grad]
+    B, T = cfg["B"], cfg["T"]
+    gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
+    x_host = torch.randn(B, T, cfg["D"], generator=gen).to(torch.bfloat16).pin_memory()
+    x = x_host.to(device)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step(inp):
+        for p in params:
+            p.grad = None
+        y = module(inp)
+        loss = y.float().square().mean()
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1) for p in params])
+            dist.all_reduce(flat)
+            flat.div_(world)
+            offset = 0
+            for p in params:
+                n = p.numel()
+                p.grad.copy_(flat[offset:offset + n].view_as(p.grad))
+                offset += n
+        return loss
+
+    lib = _lib.load()
+    timer = PhaseTimer(lib)
+    timer.install()
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    timer.calls = {n: 0 for n in timer.calls}
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(float(i))  # evict L2 (256 MB > 126 MB) outside the timed interval
+            starts[i].record()
+            step(x)
+            ends[i].record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        wall = time.perf_counter() - wall0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    launches = timer.launches() // max(1, args.steps)
+    mean_ms = statistics.mean(step_ms)
+    if world > 1:
+        t = torch.tensor([mean_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mean_ms = float(t)
+    status = _lib.device_status(torch.cuda.current_stream().cuda_stream)
+
+    # Per-entry-point device times (one extra profiled step, not part of the timed region).
+    timer.timing = True
+    flush.fill_(0.5)
+    step(x)
+    phase_ms = timer.mean_ms()
+    timer.timing = False
+    timer.uninstall()
+
+    # End-to-end: pinned host input -> device, fwd+bwd, loss back to the host.
+    e2e_ms = []
+    for i in range(max(2, min(args.steps, 5))):
+        flush.fill_(float(i))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        xin = x_host.to(device, non_blocking=True)
+        loss = step(xin)
+        loss_host = loss.detach().to("cpu", non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+        _ = float(loss_host)
+    e2e = statistics.mean(e2e_ms)
+    if world > 1:
+        t = torch.tensor([e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = float(t)
+
+    core_flops, mixer_flops, phase_flops = flops_per_token(cfg)
+    tokens = B * T * world
+    value = tokens / (mean_ms / 1e3)
+    peak_sus, peak_burst, peak_kind = load_peaks()
+    # Dominant entry point of ours and its algorithmic FLOPs per launch.
+    per_token = {"ts_b200_feature_fwd": phase_flops["feature"], "ts_b200_scan_fwd": phase_flops["scan"],
+                 "ts_b200_scan_bwd": 2 * phase_flops["scan"], "ts_b200_feature_bwd": 2 * phase_flops["feature"],
+                 "ts_b200_kread_fwd": 0, "ts_b200_kread_bwd": 0}
+    dominant = max(phase_ms, key=phase_ms.get)
+    achieved = per_token[dominant] * B * T / (phase_ms[dominant] / 1e3) / 1e12
+    mixer_tflops = mixer_flops * value / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic x ~ N(0,1), seeded random-init weights",
+        "config": {"workload": "config 2: ThetaScan-Kernel relu2 ridge m=256 (2x expansion), partial RoPE, "
+                               "1-branch fast bank, output gate; fwd+bwd, loss=mean(y^2)",
+                   "model": "ThetaScan-Kernel mixer", "global_batch": B * world, "seq_len": T,
+                   "d_model": cfg["D"], "heads": cfg["H"], "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "256 MB buffer written before every timed step"},
+        "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_sus,
+                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained"},
+        "mixer_roofline": {"achieved": mixer_tflops, "peak": peak_sus, "unit": "TFLOP/s",
+                           "frac": mixer_tflops / peak_sus, "flop_per_token": mixer_flops,
+                           "core_flop_per_token": core_flops},
+        "phase_ms": {k.replace("ts_b200_", ""): round(v, 4) for k, v in phase_ms.items()},
+        "e2e": {"value": tokens / (e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(), "d2h_bytes_per_step": 4},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks.summary(),
+        "wall_s": wall,
+        "device_status": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        T_cpu = args.ref_tokens
+        secs = cpu_reference_step(cfg, T_cpu, "sum")
+        line["cpu_baseline"] = {"value": T_cpu / secs, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"reference cumsum backend (float32 oracle restatement), config 2 "
+                                          f"per-token shape, B=1, T={T_cpu}, plain-sum view (cumsum rejects banks), "
+                                          f"one forward+backward"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--ref-tokens", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

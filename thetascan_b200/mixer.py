@@ -1,0 +1,336 @@
+"""The ThetaScan token mixer on the B200 path.
+
+``ThetaScan(config)`` mirrors the reference public module (src/thetascan/
+api.py:13-48): ``x [B,T,D] -> [B,T,D]``, ``zero_output_projection_()``,
+``regularization_loss()``, and a ``_core`` submodule whose parameter and
+buffer names, shapes and initialisation order follow the reference core
+module (src/thetascan/_core/modules/block.py:142-333), so a reference
+state dict loads unchanged and the same seed gives the same weights.
+
+The forward of the kernel family (block.py:573-724) runs the projections as
+cuBLAS GEMMs, RoPE and L2 norm as PyTorch elementwise ops, and the hot path
+(feature maps, multi-view scan, normalized read and bank blend) as the
+sm_100a kernels of :mod:`thetascan_b200.kernel`.  Streams are bf16; a float32
+input is computed with bf16 streams and returned in float32.
+"""
+from __future__ import annotations
+
+import hashlib
+import math
+from copy import deepcopy
+from functools import lru_cache
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .config import ThetaScanConfig
+from .kernel import KernelSpec, kernel_core
+
+EXPANSION_DOMAIN = "thetascan-expansion-v1"
+FINGERPRINT_MAGIC = b"TSXF"
+FINGERPRINT_SCHEMA = 1
+
+
+def _inverse_softplus(value: float) -> float:
+    return value + math.log(-math.expm1(-value))
+
+
+def _domain(shape, key, role) -> bytes:
+    """Versioned identity of one sign stream (block.py:67-74)."""
+    return f"{EXPANSION_DOMAIN}\0{key}\0{role}\0{','.join(str(s) for s in shape)}".encode("utf-8")
+
+
+def key_signs(shape, *, key: str, role: str) -> torch.Tensor:
+    """+-1 signs from the low bits of SHAKE-256 over the domain (block.py:49-64)."""
+    raw = bytearray(hashlib.shake_256(_domain(shape, key, role)).digest(math.prod(shape)))
+    bits = torch.frombuffer(raw, dtype=torch.uint8).clone()
+    return bits.bitwise_and(1).to(torch.float32).mul_(2.0).sub_(1.0).reshape(shape)
+
+
+def unit_row_map(shape, *, key: str, role: str) -> torch.Tensor:
+    """Uncentred sign rows scaled to unit L2 norm (block.py:117-133, center_rows=False)."""
+    matrix = key_signs(shape, key=key, role=role)
+    fallback = key_signs(shape, key=key, role=f"{role}-fallback")
+    matrix = torch.where(matrix.norm(dim=-1, keepdim=True) > 0.0, matrix, fallback)
+    return matrix / matrix.norm(dim=-1, keepdim=True)
+
+
+def expansion_fingerprint(*, key: str, effective: int, expansion: int, depth: int) -> torch.Tensor:
+    """40-byte persistent identity of the derived expansion maps (block.py:77-114)."""
+    base = effective // expansion
+    digest = hashlib.sha256()
+    digest.update(b"thetascan-expansion-checkpoint\0")
+    digest.update(EXPANSION_DOMAIN.encode("ascii"))
+    for layer in range(depth):
+        for shape, role in (((1, effective, base), f"w1-expand-layer-{layer}"),
+                            ((1, base, effective), f"w2-expand-layer-{layer}")):
+            descriptor = _domain(shape, key, role)
+            digest.update(len(descriptor).to_bytes(8, "big"))
+            digest.update(descriptor)
+    encoded = FINGERPRINT_MAGIC + FINGERPRINT_SCHEMA.to_bytes(4, "big") + digest.digest()
+    return torch.tensor(tuple(encoded), dtype=torch.uint8)
+
+
+class _HeadLinear(nn.Module):
+    """``d_model -> [B,H,T,out]`` gate projection (gates.py:6-17)."""
+
+    def __init__(self, d_model, n_heads, out, bias_init):
+        super().__init__()
+        self.h, self.o = n_heads, out
+        self.lin = nn.Linear(d_model, n_heads * out, bias=True)
+        nn.init.zeros_(self.lin.weight)
+        nn.init.constant_(self.lin.bias, bias_init)
+
+
+class _OutGate(nn.Module):
+    """SiLU output gate; parameters at ``ogate.g.lin`` (gates.py:34-40)."""
+
+    def __init__(self, d_model, n_heads, d):
+        super().__init__()
+        self.g = _HeadLinear(d_model, n_heads, d, bias_init=1.0)
+
+
+@lru_cache(maxsize=32)
+def _rope_tables(T: int, rot: int, base: float, device: str):
+    inv = 1.0 / (base ** (torch.arange(0, rot, 2, dtype=torch.float32, device=device) / rot))
+    angles = torch.outer(torch.arange(T, dtype=torch.float32, device=device), inv)
+    return angles.cos(), angles.sin()
+
+
+def _rope_width(d: int, mode: str, frac: float) -> int:
+    if mode == "none":
+        return 0
+    max_rot = d // 2 * 2
+    if max_rot == 0:
+        return 0
+    return max_rot if mode == "full" else min(max_rot, max(2, int(d * frac) // 2 * 2))
+
+
+def _rope(x: torch.Tensor, rot: int, base: float) -> torch.Tensor:
+    """Adjacent-pair rotation of the first ``rot`` channels with f32 phases (rope.py:57-72)."""
+    if rot == 0:
+        return x
+    cos, sin = _rope_tables(x.shape[2], rot, float(base), str(x.device))
+    even, odd = x[..., 0:rot:2], x[..., 1:rot:2]
+    rotated = torch.stack((even * cos - odd * sin, even * sin + odd * cos), dim=-1).flatten(-2)
+    return torch.cat((rotated, x[..., rot:]), dim=-1)
+
+
+class ThetaScanCore(nn.Module):
+    """Parameters and forward of one mixer (reference block.ThetaScan)."""
+
+    def __init__(self, cfg: ThetaScanConfig):
+        super().__init__()
+        self.cfg = cfg
+        reason = cfg.unsupported_reason()
+        if reason is not None:
+            raise NotImplementedError(f"thetascan_b200: {reason}")
+        D, H, d = cfg.d_model, cfg.n_heads, cfg.resolved_head_dim
+        m = cfg.memory_width
+        k = cfg.kernel
+        self.n_heads, self.head_dim, self.mem_hidden = H, d, m
+        # Control parameters, in the reference's construction order.
+        if k.kernel_sharpness_mode == "learned_per_head":
+            self.kernel_sharpness_raw = nn.Parameter(torch.full((H,), _inverse_softplus(float(k.kernel_sharpness))))
+        elif k.kernel_sharpness_mode == "learned_per_feature":
+            self.kernel_sharpness_raw = nn.Parameter(
+                torch.full((H, m), _inverse_softplus(float(k.kernel_sharpness))))
+        else:
+            self.register_parameter("kernel_sharpness_raw", None)
+        self.kernel_score_bias = nn.Parameter(torch.zeros(H, m)) if k.score_bias else None
+        if k.relu2_threshold_mode == "learned_per_head":
+            self.kernel_relu2_threshold = nn.Parameter(torch.zeros(H))
+        else:
+            self.register_parameter("kernel_relu2_threshold", None)
+        if k.bspline_scale_mode == "learned_per_head":
+            self.bspline_scale_raw = nn.Parameter(torch.full((H,), _inverse_softplus(float(k.bspline_scale))))
+        else:
+            self.register_parameter("bspline_scale_raw", None)
+        # Projections (block.py:186-207).
+        if cfg.key_value_heads is not None:
+            G = cfg.key_value_heads
+            self.proj_qkv = None
+            self.proj_q = nn.Linear(D, H * d, bias=False)
+            self.proj_k = nn.Linear(D, G * d, bias=False)
+            self.proj_v = nn.Linear(D, G * d, bias=False)
+        elif cfg.share_key_query:
+            self.proj_qkv = None
+            self.proj_q1 = nn.Linear(D, d, bias=False)
+            self.proj_k1 = nn.Linear(D, d, bias=False)
+            self.proj_v = nn.Linear(D, H * d, bias=False)
+            self.kq_bias = nn.Parameter(torch.zeros(2, H, d))
+        else:
+            self.proj_qkv = nn.Linear(D, 3 * H * d, bias=False)
+        self.proj_out = nn.Linear(H * d, D, bias=False)
+        # Memory net theta0 (block.py:210-301).
+        projections = m // k.bspline_basis_count if k.feature_map == "projected_bspline" else m
+        self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, projections, d) / math.sqrt(d))])
+        self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, m))])
+        self.Wg = None
+        self.register_buffer("_expansion_fingerprint", None)
+        self._expanded = cfg.feature_expansion > 1
+        if self._expanded:
+            b = m // cfg.feature_expansion
+            self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, b, d) / math.sqrt(d))])
+            self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, b))])
+            self.register_buffer("_expand_w1_0", unit_row_map((1, m, b), key=cfg.expansion_key,
+                                                               role="w1-expand-layer-0"), persistent=False)
+            self.register_buffer("_expand_w2_0", unit_row_map((1, b, m), key=cfg.expansion_key,
+                                                               role="w2-expand-layer-0"), persistent=False)
+            self._expansion_fingerprint = expansion_fingerprint(
+                key=cfg.expansion_key, effective=m, expansion=cfg.feature_expansion, depth=cfg.depth)
+        self.vmlp_in = self.vmlp_out = None
+        if k.value_representation == "value_mlp":
+            vh = max(1, int(k.value_mlp_multiplier * d))
+            self.vmlp_in = nn.Linear(d, vh)
+            self.vmlp_out = nn.Linear(vh, d)
+            nn.init.zeros_(self.vmlp_out.weight)
+            nn.init.zeros_(self.vmlp_out.bias)
+        self.ogate = _OutGate(D, H, d) if cfg.output_gate else None
+        # Temporal bank (block.py:313-330).
+        t = cfg.temporal
+        self.branches = t.recency_branches if t.mode == "bank" else 0
+        if t.mode == "bank":
+            alphas = t.resolved_retentions()
+            if t.recency_branches == 1:
+                self.fade_alpha = nn.Parameter(torch.full((H,), math.log(alphas[0] / (1.0 - alphas[0]))))
+                self.fade_eta = nn.Parameter(torch.zeros(H))
+            else:
+                raw = [math.log(a / (1.0 - a)) for a in alphas]
+                self.fade_alpha = nn.Parameter(torch.tensor(raw).view(-1, 1).expand(-1, H).clone())
+                self.fade_eta = nn.Parameter(torch.zeros(t.recency_branches, H))
+        else:
+            self.fade_alpha = None
+            self.fade_eta = None
+        self.spec = KernelSpec(
+            kind=k.feature_map, mode=("sum" if t.mode == "sum" else t.bank_mode),
+            eps=1e-6, gain=float(k.kernel_sharpness), basis=k.bspline_basis_count,
+            bound=float(k.bspline_bound), spline_scale=float(k.bspline_scale))
+        self._rot = _rope_width(d, cfg.rope.mode, cfg.rope.fraction)
+
+    # -------------------------------------------------------------- helpers
+
+    def effective_weights(self):
+        """``U W1`` and ``W2 D`` (block.py:546-567)."""
+        W1, W2 = self.W1[0], self.W2[0]
+        if self._expanded:
+            W1 = torch.matmul(self._expand_w1_0, W1)
+            W2 = torch.matmul(W2, self._expand_w2_0)
+        return W1, W2
+
+    def fade(self):
+        """Per-branch ``log_alpha = -softplus(-raw)`` and blends, ``[J,H]``."""
+        if self.fade_alpha is None:
+            return None, None
+        raw, eta = self.fade_alpha, self.fade_eta
+        if raw.ndim == 1:
+            raw, eta = raw.unsqueeze(0), eta.unsqueeze(0)
+        if self.cfg.temporal.blend_mode == "tanh":
+            eta = torch.tanh(eta)
+        return -F.softplus(-raw), eta
+
+    def kernel_controls(self):
+        gain = None if self.kernel_sharpness_raw is None else \
+            F.softplus(self.kernel_sharpness_raw).clamp_min(torch.finfo(torch.float32).tiny)
+        scale = None if self.bspline_scale_raw is None else \
+            F.softplus(self.bspline_scale_raw).clamp_min(torch.finfo(torch.float32).tiny)
+        return dict(threshold=self.kernel_relu2_threshold, score_bias=self.kernel_score_bias, gain=gain,
+                    spline_scale=scale)
+
+    def project(self, x):
+        """q, k, v ``[B,H,T,d]`` in the stream dtype (block.py:577-594)."""
+        cfg = self.cfg
+        B, T, _ = x.shape
+        H, d = self.n_heads, self.head_dim
+        dt = x.dtype
+        if cfg.key_value_heads is not None:
+            G = cfg.key_value_heads
+            q = F.linear(x, self.proj_q.weight.to(dt)).view(B, T, H, d).transpose(1, 2)
+            k = F.linear(x, self.proj_k.weight.to(dt)).view(B, T, G, d).transpose(1, 2)
+            v = F.linear(x, self.proj_v.weight.to(dt)).view(B, T, G, d).transpose(1, 2)
+            return q, k.repeat_interleave(H // G, dim=1), v.repeat_interleave(H // G, dim=1)
+        if cfg.share_key_query:
+            bias = self.kq_bias.to(dt)
+            q = F.linear(x, self.proj_q1.weight.to(dt)).unsqueeze(1) + bias[0][None, :, None, :]
+            k = F.linear(x, self.proj_k1.weight.to(dt)).unsqueeze(1) + bias[1][None, :, None, :]
+            v = F.linear(x, self.proj_v.weight.to(dt)).view(B, T, H, d).transpose(1, 2)
+            return q, k, v
+        qkv = F.linear(x, self.proj_qkv.weight.to(dt))
+        q, k, v = qkv.view(B, T, 3, H, d).permute(2, 0, 3, 1, 4)
+        return q, k, v
+
+    def prepare_qk(self, x):
+        """RoPE then L2 norm with f32 arithmetic, back to bf16 (block.py:595-599)."""
+        x = _rope(x.float(), self._rot, self.cfg.rope.base)
+        return (x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)).to(torch.bfloat16).contiguous()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("thetascan_b200 requires a CUDA input")
+        B, T, _ = x.shape
+        H, d = self.n_heads, self.head_dim
+        out_dtype = x.dtype
+        xb = x.to(torch.bfloat16)
+        q, k, v = self.project(xb)
+        q, k = self.prepare_qk(q), self.prepare_qk(k)
+        if self.vmlp_in is not None:
+            v = v + self.vmlp_out(F.silu(self.vmlp_in(v.float()))).to(v.dtype)
+        v = v.contiguous()
+        W1, W2 = self.effective_weights()
+        log_alphas, etas = self.fade()
+        y = kernel_core(q, k, v, W1, W2, self.spec, log_alphas=log_alphas, etas=etas, **self.kernel_controls())
+        if self.ogate is not None:
+            lin = self.ogate.g.lin
+            gate = F.linear(xb, lin.weight.to(torch.bfloat16), lin.bias.to(torch.bfloat16))
+            y = y * F.silu(gate.view(B, T, H, d))
+        y = F.linear(y.reshape(B, T, H * d), self.proj_out.weight.to(torch.bfloat16))
+        return y.to(out_dtype)
+
+
+class ThetaScan(nn.Module):
+    """Public mixer: ``x [B,T,D] -> [B,T,D]`` (reference api.py:13-48)."""
+
+    def __init__(self, config: ThetaScanConfig):
+        super().__init__()
+        self.config = deepcopy(config)
+        self.config.validate()
+        self._core = ThetaScanCore(self.config)
+        if self.config.family == "kernel" and not self.config.kernel.feature_parameters_trainable:
+            for p in (self._core.W1[0], self._core.kernel_sharpness_raw, self._core.kernel_score_bias,
+                      self._core.kernel_relu2_threshold, self._core.bspline_scale_raw):
+                if p is not None:
+                    p.requires_grad_(False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self._core(x)
+
+    def zero_output_projection_(self) -> "ThetaScan":
+        nn.init.zeros_(self._core.proj_out.weight)
+        return self
+
+    def regularization_loss(self) -> torch.Tensor:
+        """Optional decorrelation penalty of theta0 (block.py:496-544)."""
+        cfg = self.config.regularization
+        out = torch.zeros((), device=self._core.W2[0].device)
+        mats = [self._core.W1[0], self._core.W2[0]]
+        if cfg.feature_weight:
+            acc = 0.0
+            eligible = [W for W in mats if W.shape[-2] > 1]
+            for W in eligible:
+                Wn = W / W.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+                G = Wn @ Wn.transpose(-1, -2)
+                r = G.shape[-1]
+                acc = acc + (G * (1.0 - torch.eye(r, device=G.device))).square().sum() / (G.shape[0] * r * (r - 1))
+            if eligible:
+                out = out + cfg.feature_weight * acc / len(eligible)
+        if cfg.head_weight and self.config.n_heads > 1:
+            acc = 0.0
+            for W in mats:
+                V = W.flatten(1)
+                Vn = V / V.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+                Gh = Vn @ Vn.t()
+                n = Gh.shape[0]
+                acc = acc + (Gh * (1.0 - torch.eye(n, device=Gh.device))).square().sum() / (n * (n - 1))
+            out = out + cfg.head_weight * acc / len(mats)
+        return out
