@@ -124,6 +124,26 @@ typedef struct ts_scan_grad_args {
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* fwd);
 int ts_b200_scan_bwd(const ts_scan_args* fwd, const ts_scan_grad_args* grad, ts_stream_t stream);
 
+/* Forward of the multi-view scan without any caller workspace.  No
+ * counterpart in the reference: it exists for hosts that cannot allocate
+ * device memory for this library -- a runtime whose allocator owns all device
+ * memory and lends none to plug-ins, or a serving loop that forbids cudaMalloc
+ * once it is running.  Same inputs, outputs and results as ts_b200_scan_fwd;
+ * args->workspace and args->workspace_bytes are ignored.
+ *  - Scratch is one fixed device array of TS_STATIC_SCRATCH_BYTES inside the
+ *    library, held by every GPU that loads it until the process exits.  A
+ *    shape needing more (ts_b200_scan_workspace_bytes > the limit) is
+ *    rejected with TS_ERR_VALUE before anything is launched.
+ *  - The first call on each device resolves the array's device address with
+ *    that device current; make that first call before any stream capture.
+ *  - All calls on one GPU share that GPU's copy of the array, which keeps
+ *    the last call's contents: calls that overlap on the same GPU (say, on
+ *    two streams) race, so serialize them.  Nothing in it needs clearing:
+ *    each call writes every scratch element before reading it.
+ *  - Forward only: the chunk states are not kept for ts_b200_scan_bwd. */
+#define TS_STATIC_SCRATCH_BYTES (16u << 20)
+int ts_b200_scan_fwd_static(const ts_scan_args* args, ts_stream_t stream);
+
 
 /* ------------------------------------------------------------------ feature maps
  *

@@ -60,7 +60,9 @@ SIGNATURES = {
     "ts_b200_scan_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScanArgs)]),
     "ts_b200_scan_bwd": (ctypes.c_int, [ctypes.POINTER(ScanArgs), ctypes.POINTER(ScanGradArgs),
                                         ctypes.c_void_p]),
+    "ts_b200_scan_fwd_static": (ctypes.c_int, [ctypes.POINTER(ScanArgs), ctypes.c_void_p]),
 }
+STATIC_SCRATCH_BYTES = 16 << 20
 
 
 class FeatureArgs(ctypes.Structure):

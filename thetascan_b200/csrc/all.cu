@@ -7,3 +7,4 @@
 #include "feature.cu"
 #include "kread.cu"
 #include "capi_kernel.cu"
+#include "capi_static.cu"

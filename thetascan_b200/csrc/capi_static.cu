@@ -1,0 +1,66 @@
+// Forward scan on library-owned scratch, for callers that cannot allocate.
+//
+// ts_b200_scan_fwd needs a caller workspace for the per-tile chunk states.
+// Some hosts cannot hand one over: a runtime that owns all device memory
+// through its own allocator and exposes none of it to plug-ins, or a serving
+// loop that forbids cudaMalloc after start-up (and inside captured streams).
+// For them this variant keeps its scratch in a fixed file-scope device array
+// of TS_STATIC_SCRATCH_BYTES that every GPU loading the library holds until
+// exit; the caller still passes inputs and outputs.
+#include <mutex>
+
+#include "capi_internal.h"
+#include "scan.cuh"
+
+namespace ts {
+
+static __device__ __align__(256) unsigned char g_scan_scratch[TS_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_scan_scratch on the current device.  Resolved once per
+// device, with that device current, on the first call there; the symbol name
+// itself is only a host-side handle and must never reach a kernel.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "scan_fwd_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(TS_ERR_VALUE, "scan_fwd_static: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_address[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_scan_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return set_error(TS_ERR_CUDA, "scan_fwd_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_address[dev] = ptr;
+  }
+  *out = g_scratch_address[dev];
+  return TS_OK;
+}
+
+}  // namespace
+}  // namespace ts
+
+extern "C" int ts_b200_scan_fwd_static(const ts_scan_args* args, ts_stream_t stream) {
+  using namespace ts;
+  ScanParams p;
+  if (int e = build_scan_params(args, &p)) return e;
+  const size_t need = states_bytes(p) + images_bytes(p);
+  if (need > static_cast<size_t>(TS_STATIC_SCRATCH_BYTES))
+    return set_error(TS_ERR_VALUE,
+                     "scan_fwd_static: this shape needs %zu bytes of scratch but the static scratch holds %zu; "
+                     "use ts_b200_scan_fwd with a caller workspace",
+                     need, static_cast<size_t>(TS_STATIC_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  if (int e = scratch_address(&scratch)) return e;
+  // Every scratch element the kernels read is written earlier in the same
+  // call (tile updates before the prefix, state images before the reads), so
+  // nothing has to be cleared between calls.
+  p.states = static_cast<float*>(scratch);
+  p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + states_bytes(p));
+  return launch_scan_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
