@@ -332,6 +332,97 @@ __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __
   }
 }
 
+// Cooperative, coalesced copy of a tile back to a row-major bf16 matrix
+// (rows_valid x cols_valid, leading dimension `ld`): the inverse of load_tile.
+__device__ __forceinline__ void store_tile(const Tile& t, __nv_bfloat16* __restrict__ dst, long ld, int rows_valid,
+                                           int cols_valid) {
+  const int chunks = t.cols / 8;
+  const int total = t.rows * chunks;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) && ((ld & 7) == 0);
+  for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    const int r8 = it & 7;
+    const int rest = it >> 3;
+    const int j = rest % chunks;
+    const int r = (rest / chunks) * 8 + r8;
+    const int c0 = j * 8;
+    if (r >= rows_valid || c0 >= cols_valid) continue;
+    const uint4 v = tile_ld16(t, r, j);
+    if (vec_ok && c0 + 8 <= cols_valid) {
+      *reinterpret_cast<uint4*>(dst + r * ld + c0) = v;
+    } else {
+      float f[8];
+      unpack8(v, f);
+      for (int e = 0; e < 8 && c0 + e < cols_valid; ++e) dst[r * ld + c0 + e] = __float2bfloat16_rn(f[e]);
+    }
+  }
+}
+
+// Coalesced store of per-thread accumulator rows.  Thread t owns row t of a
+// TMEM accumulator (columns [0, ncols) at `trow`, the address of this warp's
+// lane quadrant); rows [0, rows_valid) and columns [0, width) go to the
+// row-major matrix `dst` with leading dimension `ld` (f32 or bf16).  Every 16
+// columns pass through a small padded shared buffer (`stage`, >= 128*17
+// floats) so that global stores are full 32-byte sectors instead of one row
+// per lane.  `transform(row, col, value)` may adjust each value.
+template <class Transform>
+__device__ __forceinline__ void store_rows(uint32_t trow, int ncols, int width, int rows_valid, void* dst, long ld,
+                                           bool bf16, float* stage, Transform transform,
+                                           const float* __restrict__ addend = nullptr) {
+  const int tid = threadIdx.x;
+  for (int c = 0; c < ncols; c += 16) {
+    float v[16];
+    tmem_ld16(trow + c, v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) stage[tid * 17 + e] = transform(tid, c + e, v[e]);
+    __syncthreads();
+    const int cols = min(16, width - c);
+    if (cols > 0) {
+      for (int i = tid; i < rows_valid * 16; i += blockDim.x) {
+        const int r = i >> 4, e = i & 15;
+        if (e < cols) {
+          float x = stage[r * 17 + e];
+          if (addend != nullptr) x += addend[r * ld + c + e];
+          if (bf16) {
+            reinterpret_cast<__nv_bfloat16*>(dst)[r * ld + c + e] = __float2bfloat16_rn(x);
+          } else {
+            reinterpret_cast<float*>(dst)[r * ld + c + e] = x;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+struct Identity {
+  __device__ __forceinline__ float operator()(int, int, float v) const { return v; }
+};
+
+// load_tile for an f32 or bf16 source (f32 values are rounded to bf16).
+__device__ __forceinline__ void load_tile_any(const Tile& t, const void* __restrict__ src, long ld, int rows_valid,
+                                              int cols_valid, bool src_bf16) {
+  if (src_bf16) {
+    load_tile(t, static_cast<const __nv_bfloat16*>(src), ld, rows_valid, cols_valid);
+    return;
+  }
+  const float* s = static_cast<const float*>(src);
+  const int chunks = t.cols / 8;
+  const int total = t.rows * chunks;
+  for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    const int r8 = it & 7;
+    const int rest = it >> 3;
+    const int j = rest % chunks;
+    const int r = (rest / chunks) * 8 + r8;
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = j * 8 + e;
+      f[e] = (r < rows_valid && c < cols_valid) ? __ldg(s + r * ld + c) : 0.f;
+    }
+    tile_st16(t, r, j, pack8(f));
+  }
+}
+
 // Copy a pre-arranged tile image (already in core-matrix order, `bytes` long)
 // from global memory.
 __device__ __forceinline__ void load_image(const Tile& t, const void* __restrict__ src, int bytes) {

@@ -235,6 +235,53 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
 
 // ------------------------------------------------------------------ forward
 
+__device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
+  unsigned short u;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(u) : "r"(t.saddr + tile_off(t, r, c)));
+  return __bfloat162float(__ushort_as_bfloat16(u));
+}
+
+constexpr int kStageFloats = kTile * 17;
+
+// phi for this thread's row into the phi tile (bf16), all kinds.
+__device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
+                                                const Tile& tphi, bool zero_row) {
+  const int tid = threadIdx.x;
+  if (p.kind == kBspline) {
+    const float sc = ctl_scale(p, h);
+    const float invP = 1.f / static_cast<float>(p.P);
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+      for (int e = 0; e < 16; ++e) {
+        const int pj = c + e;
+        if (pj >= p.P) break;
+        float val[kMaxBasis], der[kMaxBasis];
+        bool inside;
+        bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
+        for (int i = 0; i < p.nb; i += 8) {
+          float f[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) f[q] = (!zero_row && i + q < p.nb) ? val[i + q] * invP : 0.f;
+          tile_st16(tphi, tid, (pj * p.nb + i) / 8, pack8(f));
+        }
+      }
+    }
+  } else {
+    for (int c = 0; c < p.PP; c += 16) {
+      float a[16], f[16];
+      tmem_ld16(ta_row + c, a);
+      phi_chunk(p, st, a, c, h, f);
+      if (zero_row) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[e] = 0.f;
+      }
+      tile_st16(tphi, tid, c / 8, pack8(f));
+      tile_st16(tphi, tid, c / 8 + 1, pack8(f + 8));
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
@@ -252,6 +299,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   tl.w1 = Tile{tl.x.saddr + kTile * p.dP * 2, p.PP, p.dP};
   tl.phi = Tile{tl.w1.saddr + p.PP * p.dP * 2, kTile, p.mP};
   tl.w2 = Tile{tl.phi.saddr + kTile * p.mP * 2, p.dP, p.mP};
+  float* stage = reinterpret_cast<float*>(smem + (tl.w2.saddr + p.dP * p.mP * 2 - base));
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -271,72 +319,18 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
 
   const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
   const RowState st = row_stats(p, ta_row, h);
-  __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.m;
-  const bool valid = tid < rows;
-  if (p.kind == kBspline) {
-    const float sc = ctl_scale(p, h);
-    const float invP = 1.f / static_cast<float>(p.P);
-    for (int c = 0; c < p.PP; c += 16) {
-      float a[16];
-      tmem_ld16(ta_row + c, a);
-      for (int e = 0; e < 16; ++e) {
-        const int pj = c + e;
-        if (pj >= p.P) break;
-        float val[kMaxBasis], der[kMaxBasis];
-        bool inside;
-        bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
-        for (int i = 0; i < p.nb; i += 8) {
-          float f[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) f[q] = (i + q < p.nb) ? val[i + q] * invP : 0.f;
-          const int col = pj * p.nb + i;
-          const uint4 u = pack8(f);
-          if (valid) {
-            if (p.nb - i >= 8) {
-              *reinterpret_cast<uint4*>(out + col) = u;
-            } else {
-              for (int q = 0; q < p.nb - i; ++q) out[col + q] = __float2bfloat16_rn(f[q]);
-            }
-          }
-          if (decode) {
-            // The decode tile wants 8-aligned chunks; nb is a multiple of 8 when decoding.
-            tile_st16(tl.phi, tid, col / 8, u);
-          }
-        }
-      }
-    }
-  } else {
-    for (int c = 0; c < p.PP; c += 16) {
-      float a[16], f[16];
-      tmem_ld16(ta_row + c, a);
-      phi_chunk(p, st, a, c, h, f);
-      const uint4 u0 = pack8(f), u1 = pack8(f + 8);
-      if (valid) {
-        if (c + 16 <= p.m) {
-          *reinterpret_cast<uint4*>(out + c) = u0;
-          *reinterpret_cast<uint4*>(out + c + 8) = u1;
-        } else {
-          for (int e = 0; e < 16 && c + e < p.m; ++e) out[c + e] = __float2bfloat16_rn(f[e]);
-        }
-      }
-      if (decode) {
-        tile_st16(tl.phi, tid, c / 8, u0);
-        tile_st16(tl.phi, tid, c / 8 + 1, u1);
-      }
-    }
-  }
+  // Rows past the sequence end get zero features, so the decode below and the
+  // stored tile are exact zeros there.
+  phi_row_to_tile(p, st, ta_row, h, tl.phi, tid >= rows);
+  __syncthreads();
+  __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
+  store_tile(tl.phi, out, p.m, rows, p.m);
   if (decode) {
-    // Padding rows past the sequence end hold valid features of zero input;
-    // they only produce y0 rows that are not stored.
     ctx.run([&] { gemm_issue(t_y, kmajor(tl.phi), kmajor(tl.w2), p.dP, p.mP, false); });
-    float* yrow = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.d;
-    for (int c = 0; c < p.dP; c += 16) {
-      float v[16];
-      tmem_ld16(tmem_addr(t_y, warp * 32, c), v);
-      if (valid) {
-        for (int e = 0; e < 16 && c + e < p.d; ++e) yrow[c + e] = v[e] + bf2f(xp[tid * p.xs[sel][2] + c + e]);
-      }
-    }
+    float* y0 = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.d;
+    const Tile tx = tl.x;
+    store_rows(tmem_addr(t_y, warp * 32, 0), p.dP, p.d, rows, y0, p.d, false, stage,
+               [&](int row, int col, float v) { return col < p.d ? v + tile_elem(tx, row, col) : v; });
   }
   tc_fence_before();
   __syncthreads();
@@ -344,11 +338,6 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
 }
 
 // ------------------------------------------------------------------ backward
-
-__device__ __forceinline__ float dphi_at(const FeatParams& p, int sel, size_t idx) {
-  return p.dphi_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.dphi[sel])[idx])
-                     : reinterpret_cast<const float*>(p.dphi[sel])[idx];
-}
 
 __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -362,6 +351,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   const int rows = min(kTile, p.T - t0);
   const bool valid = tid < rows;
   const bool decode = sel == 1 && p.dy != nullptr && p.W2 != nullptr;
+  const bool spline = p.kind == kBspline;
 
   const uint32_t base = smem_u32(smem);
   FeatTiles tl;
@@ -371,6 +361,10 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   tl.phi = Tile{tl.da.saddr + kTile * p.PM * 2, kTile, p.mM};
   tl.dy = Tile{tl.phi.saddr + kTile * p.mM * 2, kTile, p.dP};
   tl.w2 = Tile{tl.dy.saddr + kTile * p.dP * 2, p.dP, p.mP};
+  // dphi: in place of dA for relu2 / softmax (column j of both is feature j,
+  // and each thread overwrites a chunk only after reading it); separate for
+  // B-splines, whose dphi columns are (projection, basis) pairs.
+  const Tile tdphi = spline ? Tile{tl.w2.saddr + p.dP * p.mP * 2, kTile, p.mP} : Tile{tl.da.saddr, kTile, p.PM};
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -381,23 +375,16 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   const __nv_bfloat16* xp = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(t0) * p.xs[sel][2];
   load_tile(tl.x, xp, p.xs[sel][2], rows, p.d);
   load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
+  const void* dphi_src = p.dphi_bf16
+      ? static_cast<const void*>(static_cast<const __nv_bfloat16*>(p.dphi[sel]) + rowbase * p.m)
+      : static_cast<const void*>(static_cast<const float*>(p.dphi[sel]) + rowbase * p.m);
+  load_tile_any(tdphi, dphi_src, p.m, rows, p.m, p.dphi_bf16 != 0);
   if (decode) {
     load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
-    // dy rows (f32 in global) -> bf16 tile.
-    for (int j = 0; j < p.dP / 8; ++j) {
-      float f[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int c = j * 8 + e;
-        f[e] = (valid && c < p.d) ? p.dy[(rowbase + tid) * p.d + c] : 0.f;
-      }
-      tile_st16(tl.dy, tid, j, pack8(f));
-    }
+    load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
   }
-  // Zero the padding columns of the dA / phi tiles once (M-blocks of 128).
-  for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
-  if (decode)
-    for (int j = p.mP / 8; j < p.mM / 8; ++j) tile_st16(tl.phi, tid, j, make_uint4(0, 0, 0, 0));
+  if (!spline)
+    for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -411,58 +398,64 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
   const uint32_t tb_row = tmem_addr(t_hi, warp * 32, 0);
   const RowState st = row_stats(p, ta_row, h);
-  const size_t prow = (rowbase + tid) * p.m;
 
-  // Gradient of the feature map -> dpre (kept in the dA tile as f32 is not
-  // possible; dpre is recomputed chunk by chunk in two sweeps instead).
-  float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
-  float dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
-  auto total_dphi = [&](int i, const float* dhi, int e) {
-    float g = valid && i < p.m ? dphi_at(p, sel, prow + i) : 0.f;
-    if (decode) g += dhi[e];
-    return g;
+  // Total gradient of 16 feature columns [c, c+16) of this row: staged dphi
+  // plus the slow-decode contribution dy W2 (TMEM).
+  auto grad16 = [&](int c, float* g) {
+    unpack8(tile_ld16(tdphi, tid, c / 8), g);
+    unpack8(tile_ld16(tdphi, tid, c / 8 + 1), g + 8);
+    if (decode) {
+      float dhi[16];
+      tmem_ld16(tb_row + c, dhi);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) g[e] += dhi[e];
+    }
   };
-  if (p.kind != kBspline) {
+
+  float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
+  if (!spline) {
     for (int c = 0; c < p.PP; c += 16) {
-      float a[16], f[16], dhi[16];
+      float a[16], f[16], g[16];
       tmem_ld16(ta_row + c, a);
-      if (decode) tmem_ld16(tb_row + c, dhi);
+      grad16(c, g);
       phi_chunk(p, st, a, c, h, f);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) dot_phi += total_dphi(c + e, dhi, e) * f[e];
+      for (int e = 0; e < 16; ++e) dot_phi += g[e] * f[e];
     }
   }
   // dpre for columns [c, c+16) (projection index for B-splines).
-  auto dpre_chunk = [&](int c, const float* a, const float* dhi, float* dp) {
+  auto dpre_chunk = [&](int c, const float* a, float* dp) {
     if (p.kind == kRelu2) {
+      float g[16];
+      grad16(c, g);
       const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
       const bool live = st.mass > p.eps;
       const float inv_mass = 1.f / fmaxf(st.mass, p.eps);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        float g = 0.f;
+        float d = 0.f;
         if (i < p.P && live) {
           const float u = fmaxf(a[e] * st.inv + ctl_bias(p, h, i) - thr, 0.f);
-          const float dz = (total_dphi(i, dhi, e) - dot_phi) * inv_mass;
-          g = dz * 2.f * u;
+          d = (g[e] - dot_phi) * inv_mass * 2.f * u;
         }
-        dp[e] = g;
+        dp[e] = d;
       }
     } else if (p.kind == kSoftmax) {
+      float g[16];
+      grad16(c, g);
       const float inv_E = 1.f / st.mass;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        float g = 0.f;
+        float d = 0.f;
         if (i < p.P) {
           const float gain = ctl_gain(p, h, i);
           const float sc = a[e] * st.inv + ctl_bias(p, h, i);
           const float ph = __expf(gain * sc - st.mx) * inv_E;
-          const float dl = ph * (total_dphi(i, dhi, e) - dot_phi);
-          g = gain * dl;
+          d = gain * ph * (g[e] - dot_phi);
         }
-        dp[e] = g;
+        dp[e] = d;
       }
     } else {
       const float sc = ctl_scale(p, h);
@@ -470,37 +463,38 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 #pragma unroll 1
       for (int e = 0; e < 16; ++e) {
         const int pj = c + e;
-        float g = 0.f;
+        float d = 0.f;
         if (pj < p.P) {
           float val[kMaxBasis], der[kMaxBasis];
           bool inside;
           bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
           float dc = 0.f;
-          for (int i = 0; i < p.nb; ++i) {
-            const int col = pj * p.nb + i;
-            float gphi = valid ? dphi_at(p, sel, prow + col) : 0.f;
-            if (decode) {
-              float tmp[16];
-              tmem_ld16(tb_row + (col & ~15), tmp);
-              gphi += tmp[col & 15];
+          for (int i0 = 0; i0 < p.nb; i0 += 16) {
+            const int col = pj * p.nb + i0;   // multiple of 8
+            float g[16];
+            const int cbase = col & ~15;
+            grad16(cbase, g);
+            const int off = col - cbase;
+            for (int i = 0; i < 16 - off && i0 + i < p.nb; ++i) dc += g[off + i] * der[i0 + i] * invP;
+            if (off && i0 + 16 - off < p.nb) {
+              float g2[16];
+              grad16(cbase + 16, g2);
+              for (int i = 16 - off; i0 + i < p.nb && i < 16; ++i) dc += g2[i - (16 - off)] * der[i0 + i] * invP;
             }
-            dc += gphi * der[i] * invP;
           }
-          if (!inside) dc = 0.f;
-          g = dc * sc;
+          d = inside ? dc * sc : 0.f;
         }
-        dp[e] = g;
+        dp[e] = d;
       }
     }
   };
 
   // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
-  float dot_a = 0.f;
+  float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
   for (int c = 0; c < p.PP; c += 16) {
-    float a[16], dhi[16], dp[16];
+    float a[16], dp[16];
     tmem_ld16(ta_row + c, a);
-    if (decode && p.kind != kBspline) tmem_ld16(tb_row + c, dhi);
-    dpre_chunk(c, a, dhi, dp);
+    dpre_chunk(c, a, dp);
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       dot_a += dp[e] * a[e];
@@ -508,70 +502,40 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
       if (p.kind == kSoftmax && c + e < p.P) {
         const float gain = ctl_gain(p, h, c + e);
         const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
-        // d gain = dl * score = dpre * score / gain
         if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
         if (p.gain_mode == 2 && valid) atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / gain);
       }
-      if (p.kind == kBspline && c + e < p.P) {
-        const float sc = ctl_scale(p, h);
-        dscale += dp[e] * a[e] * st.inv / sc;
-      }
-      if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P) {
-        float db = dp[e];
-        if (p.kind == kSoftmax) db = dp[e];
-        atomicAdd(p.dbias + h * p.m + c + e, db);
-      }
+      if (spline && c + e < p.P) dscale += dp[e] * a[e] * st.inv / ctl_scale(p, h);
+      if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P)
+        atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
     }
   }
   if (!valid) {
     dot_a = 0.f;
     dthr = dscale = dgain_head = 0.f;
   }
-  // Sweep 2: dA = inv * dpre - a * inv^3 * dot_a / P -> bf16 tile; phi -> tile.
+  // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
+  // For B-splines phi is written first (its tile does not alias dphi).
+  if (decode) phi_row_to_tile(p, st, ta_row, h, tl.phi, !valid);
   const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
   for (int c = 0; c < p.PP; c += 16) {
-    float a[16], dhi[16], dp[16], da[16];
+    float a[16], dp[16], da[16];
     tmem_ld16(ta_row + c, a);
-    if (decode && p.kind != kBspline) tmem_ld16(tb_row + c, dhi);
-    dpre_chunk(c, a, dhi, dp);
+    dpre_chunk(c, a, dp);
 #pragma unroll
     for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
     tile_st16(tl.da, tid, c / 8, pack8(da));
     tile_st16(tl.da, tid, c / 8 + 1, pack8(da + 8));
-    if (decode) {
-      if (p.kind != kBspline) {
-        float f[16];
-        phi_chunk(p, st, a, c, h, f);
-        if (!valid) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) f[e] = 0.f;
-        }
-        tile_st16(tl.phi, tid, c / 8, pack8(f));
-        tile_st16(tl.phi, tid, c / 8 + 1, pack8(f + 8));
-      } else {
-        const float sc = ctl_scale(p, h);
-        const float invP = 1.f / static_cast<float>(p.P);
-        for (int e = 0; e < 16 && c + e < p.P; ++e) {
-          float val[kMaxBasis], der[kMaxBasis];
-          bool inside;
-          bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
-          for (int i = 0; i < p.nb; i += 8) {
-            float f[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) f[q] = (valid && i + q < p.nb) ? val[i + q] * invP : 0.f;
-            tile_st16(tl.phi, tid, ((c + e) * p.nb + i) / 8, pack8(f));
-          }
-        }
-      }
-    }
   }
+  if (spline)
+    for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
   {
     const float s1 = block_sum128(dthr, red);
     const float s2 = block_sum128(dscale, red);
     const float s3 = block_sum128(dgain_head, red);
     if (tid == 0) {
       if (p.kind == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
-      if (p.kind == kBspline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
+      if (spline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
       if (p.kind == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
     }
   }
@@ -587,25 +551,23 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
         gemm_issue(t_a + (pblocks + mb) * p.dP, mnmajor(tl.phi, 0, mb * kTile), mnmajor(tl.dy), p.dP, kTile,
                    false);
   });
-  float* dxrow = p.dx[sel] + (rowbase + tid) * p.d;
-  for (int c = 0; c < p.dP; c += 16) {
-    float v[16];
-    tmem_ld16(tmem_addr(t_hi, warp * 32, c), v);
-    if (valid) {
-      for (int e = 0; e < 16 && c + e < p.d; ++e) {
-        float g = v[e];
-        if (decode) g += p.dy[(rowbase + tid) * p.d + c + e];
-        dxrow[c + e] = g;
-      }
-    }
-  }
+  float* stage = reinterpret_cast<float*>(smem);  // x tile region, idle after the MMAs
+  store_rows(tmem_addr(t_hi, warp * 32, 0), p.dP, p.d, rows, p.dx[sel] + rowbase * p.d, p.d, false, stage,
+             Identity{}, decode ? p.dy + rowbase * p.d : nullptr);
   for (int mb = 0; mb < pblocks; ++mb) {
     const int prj = mb * kTile + tid;
     for (int c = 0; c < p.dP; c += 16) {
       float v[16];
       tmem_ld16(tmem_addr(t_a + mb * p.dP, warp * 32, c), v);
       if (prj < p.P && p.dW1) {
-        for (int e = 0; e < 16 && c + e < p.d; ++e) atomicAdd(p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d + c + e, v[e]);
+        float* row = p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d;
+        for (int e = 0; e < 16 && c + e < p.d; e += 4) {
+          if (c + e + 4 <= p.d && (p.d & 3) == 0) {
+            atomicAdd(reinterpret_cast<float4*>(row + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+          } else {
+            for (int q = 0; q < 4 && c + e + q < p.d; ++q) atomicAdd(row + c + e + q, v[e + q]);
+          }
+        }
       }
     }
   }
@@ -630,10 +592,13 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 // ------------------------------------------------------------------ host launch
 
 size_t feature_fwd_smem(const FeatParams& p) {
-  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.mP + p.dP * p.mP) * 2;
+  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.mP + p.dP * p.mP) * 2 + kStageFloats * 4;
 }
 size_t feature_bwd_smem(const FeatParams& p) {
-  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.PM + kTile * p.mM + kTile * p.dP + p.dP * p.mP) * 2;
+  size_t bytes = static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.PM + kTile * p.mM + kTile * p.dP +
+                                     p.dP * p.mP) * 2;
+  if (p.kind == kBspline) bytes += static_cast<size_t>(kTile) * p.mP * 2;
+  return bytes;
 }
 
 int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {

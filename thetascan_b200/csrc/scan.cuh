@@ -65,32 +65,22 @@ __device__ __forceinline__ void store_out(void* base, bool bf16, size_t idx, flo
 }
 
 // Build a tile whose row t is `scale(t) * row_t(src)` for a bf16 row-major
-// source, thread t handling row t (blockDim.x == 128).  Rows >= rows_valid and
-// columns >= cols_valid are zero; `unit_col` (if >= 0) is 1 before scaling.
+// source: a cooperative, coalesced copy (load_tile), then thread t rescales
+// its own row in shared memory (conflict-free in the core-matrix layout).
+// Rows >= rows_valid and columns >= cols_valid are zero; `unit_col` (if >= 0)
+// is 1 before scaling.  Requires blockDim.x == 128 == t.rows.
 template <class Scale>
 __device__ __forceinline__ void load_scaled_rows(const Tile& t, const __nv_bfloat16* __restrict__ src, long long ld,
                                                  int rows_valid, int cols_valid, int unit_col, Scale scale) {
+  load_tile(t, src, ld, rows_valid, cols_valid, unit_col);
+  __syncthreads();
   const int r = threadIdx.x;
   const float s = scale(r);
-  const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && ((ld & 7) == 0);
   for (int j = 0; j < t.cols / 8; ++j) {
     float f[8];
-    const int c0 = j * 8;
-    if (r < rows_valid && vec_ok && c0 + 8 <= cols_valid) {
-      uint4 u = __ldg(reinterpret_cast<const uint4*>(src + r * ld + c0));
-      unpack8(u, f);
-    } else {
+    unpack8(tile_ld16(t, r, j), f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int c = c0 + e;
-        f[e] = (r < rows_valid && c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (r < rows_valid && c0 + e == unit_col) f[e] = 1.f;
-      f[e] *= s;
-    }
+    for (int e = 0; e < 8; ++e) f[e] *= s;
     tile_st16(t, r, j, pack8(f));
   }
 }

@@ -67,17 +67,17 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
     });
   }
 
-  // Epilogue: row f of block mb is feature mb*128 + tid.
+  // Epilogue: row f of block mb is feature mb*128 + tid; states are stored
+  // value-major ([DvP][DkM]), so lanes of a warp write consecutive features.
   for (int r = 0; r < p.R; ++r) {
     float* dst_base = p.states + state_index(p, b, h, n, r) * p.DkM * p.DvP;
     for (int mb = 0; mb < mblocks; ++mb) {
-      float* dst = dst_base + static_cast<size_t>(mb * kTile + tid) * p.DvP;
+      float* dst = dst_base + mb * kTile + tid;
       for (int c = 0; c < p.DvP; c += 16) {
         float v[16];
         tmem_ld16(tmem_addr(ctx.tmem, warp * 32, (r * mblocks + mb) * p.DvP + c), v);
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          *reinterpret_cast<float4*>(dst + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        for (int e = 0; e < 16; ++e) dst[static_cast<size_t>(c + e) * p.DkM] = v[e];
       }
     }
   }
@@ -89,28 +89,39 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
 // ------------------------------------------------------------------ 2. prefix over tiles
 
 __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  // Thread <-> (8 consecutive features f8*8.., one value column c), c fastest:
+  // each step moves two float4 of state and writes one 16-byte image chunk,
+  // and consecutive threads write consecutive image chunks.
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int r = blockIdx.y;
   const int bh = blockIdx.z;
   const int b = bh / p.H, h = bh % p.H;
-  if (e >= p.DkM * p.DvP) return;
-  const int f = e / p.DvP, c = e % p.DvP;
+  if (idx >= (p.DkM / 8) * p.DvP) return;
+  const int c = idx % p.DvP, f8 = idx / p.DvP;
   const float la = head_la(p, r, h);
   const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
-  const bool in_image = f < p.DkP;
-  const Tile img{0u, p.DvP, p.DkP};
-  const uint32_t img_off = in_image ? tile_off(img, c, f) : 0u;
-  float S = 0.f;
+  const bool in_image = f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(f8) * p.DvP * 16 + static_cast<size_t>(c) * 16;
+  float S[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) S[e] = 0.f;
   for (int n = 0; n < p.NT; ++n) {
     const size_t si = state_index(p, b, h, n, r);
-    float* ptr = p.states + si * p.DkM * p.DvP + e;
-    const float upd = (n + 1 < p.NT) ? *ptr : 0.f;
-    *ptr = S;
-    if (in_image) {
-      uint8_t* img_base = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p));
-      *reinterpret_cast<__nv_bfloat16*>(img_base + img_off) = __float2bfloat16_rn(S);
+    float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + static_cast<size_t>(c) * p.DkM + f8 * 8);
+    float4 u0 = make_float4(0.f, 0.f, 0.f, 0.f), u1 = u0;
+    if (n + 1 < p.NT) {
+      u0 = ptr[0];
+      u1 = ptr[1];
     }
-    S = S * closing + upd;
+    ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
+    ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
+    if (in_image) {
+      uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+      *reinterpret_cast<uint4*>(img) = pack8(S);
+    }
+    const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) S[e] = S[e] * closing + u[e];
   }
 }
 
@@ -188,18 +199,14 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
     });
   }
 
-  // tcgen05.ld is warp-collective: every lane loads, only valid rows store.
+  // Coalesced stores through a stage on the (now idle) P tile.
+  float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
   for (int r = 0; r < p.R; ++r) {
-    const size_t row = ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + tid) * p.Dv;
-    for (int c = 0; c < p.DvP; c += 16) {
-      float v[16];
-      tmem_ld16(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP + c), v);
-      if (tid < rows) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (c + e < p.Dv) store_out(p.out[r], p.out_bf16, row + c + e, v[e]);
-      }
-    }
+    const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
+    void* dst = p.out_bf16 ? static_cast<void*>(reinterpret_cast<__nv_bfloat16*>(p.out[r]) + row0)
+                           : static_cast<void*>(reinterpret_cast<float*>(p.out[r]) + row0);
+    store_rows(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP), p.DvP, p.Dv, rows, dst, p.Dv, p.out_bf16 != 0,
+               stage, Identity{});
   }
   tc_fence_before();
   __syncthreads();
@@ -221,7 +228,7 @@ int launch_scan_fwd(const ScanParams& p, cudaStream_t s) {
     scan_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, sm1, s>>>(p);
     if (int e = check_launch("scan_state_kernel")) return e;
   }
-  scan_prefix_kernel<<<dim3(ceil_div(p.DkM * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p);
+  scan_prefix_kernel<<<dim3(ceil_div((p.DkM / 8) * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p);
   if (int e = check_launch("scan_prefix_kernel")) return e;
   scan_out_kernel<<<dim3(p.NT, p.H, p.B), kThreads, sm3, s>>>(p);
   return check_launch("scan_out_kernel");

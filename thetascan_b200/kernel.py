@@ -168,15 +168,16 @@ class _KernelCore(torch.autograd.Function):
         sa = _build_args(phi_q, phi_k, v, las, slots, True, ws)
         sg = _lib.ScanGradArgs()
         m = phi_q.shape[-1]
-        dphi_q = torch.empty(B, H, T, m, dtype=torch.float32, device=dev)
+        # bf16 hand-over: the feature backward stages dphi as a bf16 tile.
+        dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
         dphi_k = torch.empty_like(dphi_q)
-        dvaug = torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev)
+        dvaug = torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev)
         dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
         for i in range(n):
             sg.dout[i] = dslots[i].data_ptr()
             sg.dlog_alpha[i] = _ptr(dlas[i])
         sg.dq, sg.dk, sg.dv = dphi_q.data_ptr(), dphi_k.data_ptr(), dvaug.data_ptr()
-        sg.grad_dtype = _lib.TS_DTYPE_F32
+        sg.grad_dtype = _lib.TS_DTYPE_BF16
         gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
         sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
         _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
@@ -186,7 +187,7 @@ class _KernelCore(torch.autograd.Function):
         ctl = {"thr": thr, "bias": bias, "gain": gain, "scale": scale}
         fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, None)
         fg = _lib.FeatureGradArgs()
-        fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_F32
+        fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
         fg.dy0 = dy0.data_ptr()
         dk = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
         dq = torch.empty_like(dk)
