@@ -27,7 +27,14 @@
 namespace ts {
 
 constexpr int kTile = 128;          // tokens per tile (= MMA M)
-constexpr int kThreads = 128;       // one thread per tile row
+constexpr int kThreads = 256;       // two threads per tile row (column halves)
+
+// Thread <-> (tile row, column half).  Warps w and w+4 read the same TMEM
+// lane quadrant (w % 4), so threads t and t+128 own the same accumulator row
+// and split its columns into alternating 16-column chunks.
+__device__ __forceinline__ int my_row() { return threadIdx.x & (kTile - 1); }
+__device__ __forceinline__ int my_half() { return threadIdx.x >> 7; }
+__device__ __forceinline__ int my_quad() { return (threadIdx.x >> 5) & 3; }
 
 // Error codes written to the device status word.
 enum DeviceError : int {
@@ -357,30 +364,36 @@ __device__ __forceinline__ void store_tile(const Tile& t, __nv_bfloat16* __restr
   }
 }
 
-// Coalesced store of per-thread accumulator rows.  Thread t owns row t of a
-// TMEM accumulator (columns [0, ncols) at `trow`, the address of this warp's
-// lane quadrant); rows [0, rows_valid) and columns [0, width) go to the
-// row-major matrix `dst` with leading dimension `ld` (f32 or bf16).  Every 16
-// columns pass through a small padded shared buffer (`stage`, >= 128*17
-// floats) so that global stores are full 32-byte sectors instead of one row
-// per lane.  `transform(row, col, value)` may adjust each value.
+// Coalesced store of accumulator rows.  The two threads of row r (r, r+128)
+// own row r of a TMEM accumulator (columns [0, ncols) starting at column
+// `tcol` of `tbase`); rows [0, rows_valid) and columns [0, width) go to the
+// row-major matrix `dst` with leading dimension `ld` (f32 or bf16).  Every 32
+// columns pass through a padded shared stage (>= 128*33 floats) so that global
+// stores are whole 32-byte sectors.  `transform(row, col, value)` may adjust
+// each value; `addend` (same layout as dst, f32) is added on the way out.
 template <class Transform>
-__device__ __forceinline__ void store_rows(uint32_t trow, int ncols, int width, int rows_valid, void* dst, long ld,
-                                           bool bf16, float* stage, Transform transform,
+__device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, int width, int rows_valid, void* dst,
+                                           long ld, bool bf16, float* stage, Transform transform,
                                            const float* __restrict__ addend = nullptr) {
-  const int tid = threadIdx.x;
-  for (int c = 0; c < ncols; c += 16) {
-    float v[16];
-    tmem_ld16(trow + c, v);
+  const int row = my_row(), half = my_half();
+  const uint32_t trow = tmem_addr(tbase, my_quad() * 32, tcol);
+  for (int c = 0; c < ncols; c += 32) {
+    const int cc = c + 16 * half;
+    if (cc < ncols) {
+      float v[16];
+      tmem_ld16(trow + cc, v);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) stage[tid * 17 + e] = transform(tid, c + e, v[e]);
+      for (int e = 0; e < 16; ++e) stage[row * 33 + 16 * half + e] = transform(row, cc + e, v[e]);
+    } else {
+      // Keep the warp-collective load pattern uniform: nothing to load here.
+    }
     __syncthreads();
-    const int cols = min(16, width - c);
+    const int cols = min(32, width - c);
     if (cols > 0) {
-      for (int i = tid; i < rows_valid * 16; i += blockDim.x) {
-        const int r = i >> 4, e = i & 15;
+      for (int i = threadIdx.x; i < rows_valid * 32; i += blockDim.x) {
+        const int r = i >> 5, e = i & 31;
         if (e < cols) {
-          float x = stage[r * 17 + e];
+          float x = stage[r * 33 + e];
           if (addend != nullptr) x += addend[r * ld + c + e];
           if (bf16) {
             reinterpret_cast<__nv_bfloat16*>(dst)[r * ld + c + e] = __float2bfloat16_rn(x);
@@ -435,14 +448,33 @@ __device__ __forceinline__ void zero_tile(const Tile& t) {
     st_shared_v4(t.saddr + i * 16, make_uint4(0, 0, 0, 0));
 }
 
-// Block-wide sum (blockDim.x == 128) via shared scratch of 4 floats.
-__device__ __forceinline__ float block_sum128(float v, float* scratch) {
+// Block-wide sum; `scratch` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
   __syncthreads();
-  float s = scratch[0] + scratch[1] + scratch[2] + scratch[3];
+  float s = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += scratch[w];
+  __syncthreads();
+  return s;
+}
+
+// Sum of a per-thread value over the two threads that own one row.
+__device__ __forceinline__ float row_pair_sum(float v, float* pair /* >= 256 floats */) {
+  __syncthreads();
+  pair[threadIdx.x] = v;
+  __syncthreads();
+  const float s = pair[my_row()] + pair[my_row() + kTile];
+  __syncthreads();
+  return s;
+}
+__device__ __forceinline__ float row_pair_max(float v, float* pair) {
+  __syncthreads();
+  pair[threadIdx.x] = v;
+  __syncthreads();
+  const float s = fmaxf(pair[my_row()], pair[my_row() + kTile]);
   __syncthreads();
   return s;
 }

@@ -157,20 +157,24 @@ struct RowState {
   float mx;    // softmax: max logit
 };
 
-__device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h) {
+// Row statistics of the feature map; the two threads of a row each reduce
+// their column chunks and combine through `pair` (256 floats of shared memory).
+__device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair) {
+  const int half = my_half();
   RowState s{0.f, 0.f, -INFINITY};
   float ss = 0.f;
-  for (int c = 0; c < p.PP; c += 16) {
+  for (int c = 16 * half; c < p.PP; c += 32) {
     float a[16];
     tmem_ld16(ta_row + c, a);
 #pragma unroll
     for (int e = 0; e < 16; ++e) ss += a[e] * a[e];
   }
+  ss = row_pair_sum(ss, pair);
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
   if (p.kind == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
     float M = 0.f;
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -182,10 +186,10 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
         }
       }
     }
-    s.mass = M;
+    s.mass = row_pair_sum(M, pair);
   } else if (p.kind == kSoftmax) {
     float mx = -INFINITY;
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -194,8 +198,9 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
         if (i < p.P) mx = fmaxf(mx, ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)));
       }
     }
+    mx = row_pair_max(mx, pair);
     float E = 0.f;
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -205,7 +210,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
       }
     }
     s.mx = mx;
-    s.mass = E;
+    s.mass = row_pair_sum(E, pair);
   }
   return s;
 }
@@ -241,16 +246,16 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
   return __bfloat162float(__ushort_as_bfloat16(u));
 }
 
-constexpr int kStageFloats = kTile * 17;
+constexpr int kStageFloats = kTile * 33;
 
-// phi for this thread's row into the phi tile (bf16), all kinds.
+// phi of this thread's row and column chunks into the phi tile (bf16).
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
                                                 const Tile& tphi, bool zero_row) {
-  const int tid = threadIdx.x;
+  const int row = my_row(), half = my_half();
   if (p.kind == kBspline) {
     const float sc = ctl_scale(p, h);
     const float invP = 1.f / static_cast<float>(p.P);
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16];
       tmem_ld16(ta_row + c, a);
       for (int e = 0; e < 16; ++e) {
@@ -263,12 +268,12 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
           float f[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) f[q] = (!zero_row && i + q < p.nb) ? val[i + q] * invP : 0.f;
-          tile_st16(tphi, tid, (pj * p.nb + i) / 8, pack8(f));
+          tile_st16(tphi, row, (pj * p.nb + i) / 8, pack8(f));
         }
       }
     }
   } else {
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16], f[16];
       tmem_ld16(ta_row + c, a);
       phi_chunk(p, st, a, c, h, f);
@@ -276,8 +281,8 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
 #pragma unroll
         for (int e = 0; e < 16; ++e) f[e] = 0.f;
       }
-      tile_st16(tphi, tid, c / 8, pack8(f));
-      tile_st16(tphi, tid, c / 8 + 1, pack8(f + 8));
+      tile_st16(tphi, row, c / 8, pack8(f));
+      tile_st16(tphi, row, c / 8 + 1, pack8(f + 8));
     }
   }
 }
@@ -286,9 +291,11 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
+  __shared__ float pair[kThreads];
   const int n = blockIdx.x, h = blockIdx.y;
   const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const bool decode = sel == 1 && p.y0 != nullptr && p.W2 != nullptr;
@@ -301,7 +308,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   tl.w2 = Tile{tl.phi.saddr + kTile * p.mP * 2, p.dP, p.mP};
   float* stage = reinterpret_cast<float*>(smem + (tl.w2.saddr + p.dP * p.mP * 2 - base));
 
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -317,11 +324,11 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   const uint32_t t_a = ctx.tmem, t_y = ctx.tmem + 256;
   project(p, ctx, tl, t_a);
 
-  const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
-  const RowState st = row_stats(p, ta_row, h);
+  const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
+  const RowState st = row_stats(p, ta_row, h, pair);
   // Rows past the sequence end get zero features, so the decode below and the
   // stored tile are exact zeros there.
-  phi_row_to_tile(p, st, ta_row, h, tl.phi, tid >= rows);
+  phi_row_to_tile(p, st, ta_row, h, tl.phi, row >= rows);
   __syncthreads();
   __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
   store_tile(tl.phi, out, p.m, rows, p.m);
@@ -329,8 +336,8 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
     ctx.run([&] { gemm_issue(t_y, kmajor(tl.phi), kmajor(tl.w2), p.dP, p.mP, false); });
     float* y0 = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.d;
     const Tile tx = tl.x;
-    store_rows(tmem_addr(t_y, warp * 32, 0), p.dP, p.d, rows, y0, p.d, false, stage,
-               [&](int row, int col, float v) { return col < p.d ? v + tile_elem(tx, row, col) : v; });
+    store_rows(t_y, 0, p.dP, p.d, rows, y0, p.d, false, stage,
+               [&](int r, int col, float v) { return col < p.d ? v + tile_elem(tx, r, col) : v; });
   }
   tc_fence_before();
   __syncthreads();
@@ -343,13 +350,15 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
-  __shared__ float red[4];
+  __shared__ float red[32];
+  __shared__ float pair[kThreads];
   const int n = blockIdx.x, h = blockIdx.y;
   const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
-  const bool valid = tid < rows;
+  const bool valid = row < rows;
   const bool decode = sel == 1 && p.dy != nullptr && p.W2 != nullptr;
   const bool spline = p.kind == kBspline;
 
@@ -362,11 +371,11 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   tl.dy = Tile{tl.phi.saddr + kTile * p.mM * 2, kTile, p.dP};
   tl.w2 = Tile{tl.dy.saddr + kTile * p.dP * 2, p.dP, p.mP};
   // dphi: in place of dA for relu2 / softmax (column j of both is feature j,
-  // and each thread overwrites a chunk only after reading it); separate for
-  // B-splines, whose dphi columns are (projection, basis) pairs.
+  // and each thread overwrites one of its own chunks only after reading it);
+  // separate for B-splines, whose dphi columns are (projection, basis) pairs.
   const Tile tdphi = spline ? Tile{tl.w2.saddr + p.dP * p.mP * 2, kTile, p.mP} : Tile{tl.da.saddr, kTile, p.PM};
 
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -384,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
   }
   if (!spline)
-    for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
+    for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -395,15 +404,15 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     if (decode) gemm_issue(t_hi, kmajor(tl.dy), mnmajor(tl.w2), p.mP, p.dP, false);
   });
 
-  const uint32_t ta_row = tmem_addr(t_a, warp * 32, 0);
-  const uint32_t tb_row = tmem_addr(t_hi, warp * 32, 0);
-  const RowState st = row_stats(p, ta_row, h);
+  const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
+  const uint32_t tb_row = tmem_addr(t_hi, quad * 32, 0);
+  const RowState st = row_stats(p, ta_row, h, pair);
 
   // Total gradient of 16 feature columns [c, c+16) of this row: staged dphi
   // plus the slow-decode contribution dy W2 (TMEM).
   auto grad16 = [&](int c, float* g) {
-    unpack8(tile_ld16(tdphi, tid, c / 8), g);
-    unpack8(tile_ld16(tdphi, tid, c / 8 + 1), g + 8);
+    unpack8(tile_ld16(tdphi, row, c / 8), g);
+    unpack8(tile_ld16(tdphi, row, c / 8 + 1), g + 8);
     if (decode) {
       float dhi[16];
       tmem_ld16(tb_row + c, dhi);
@@ -414,7 +423,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 
   float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
   if (!spline) {
-    for (int c = 0; c < p.PP; c += 16) {
+    for (int c = 16 * half; c < p.PP; c += 32) {
       float a[16], f[16], g[16];
       tmem_ld16(ta_row + c, a);
       grad16(c, g);
@@ -422,6 +431,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) dot_phi += g[e] * f[e];
     }
+    dot_phi = row_pair_sum(dot_phi, pair);
   }
   // dpre for columns [c, c+16) (projection index for B-splines).
   auto dpre_chunk = [&](int c, const float* a, float* dp) {
@@ -491,7 +501,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 
   // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
   float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
-  for (int c = 0; c < p.PP; c += 16) {
+  for (int c = 16 * half; c < p.PP; c += 32) {
     float a[16], dp[16];
     tmem_ld16(ta_row + c, a);
     dpre_chunk(c, a, dp);
@@ -510,30 +520,31 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
         atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
     }
   }
+  dot_a = row_pair_sum(dot_a, pair);
   if (!valid) {
     dot_a = 0.f;
     dthr = dscale = dgain_head = 0.f;
   }
   // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
-  // For B-splines phi is written first (its tile does not alias dphi).
   if (decode) phi_row_to_tile(p, st, ta_row, h, tl.phi, !valid);
   const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
-  for (int c = 0; c < p.PP; c += 16) {
+  for (int c = 16 * half; c < p.PP; c += 32) {
     float a[16], dp[16], da[16];
     tmem_ld16(ta_row + c, a);
     dpre_chunk(c, a, dp);
 #pragma unroll
     for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
-    tile_st16(tl.da, tid, c / 8, pack8(da));
-    tile_st16(tl.da, tid, c / 8 + 1, pack8(da + 8));
+    if (spline) __syncwarp();
+    tile_st16(tl.da, row, c / 8, pack8(da));
+    tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
   }
   if (spline)
-    for (int j = p.PP / 8; j < p.PM / 8; ++j) tile_st16(tl.da, tid, j, make_uint4(0, 0, 0, 0));
+    for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   {
-    const float s1 = block_sum128(dthr, red);
-    const float s2 = block_sum128(dscale, red);
-    const float s3 = block_sum128(dgain_head, red);
-    if (tid == 0) {
+    const float s1 = block_sum(dthr, red);
+    const float s2 = block_sum(dscale, red);
+    const float s3 = block_sum(dgain_head, red);
+    if (threadIdx.x == 0) {
       if (p.kind == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
       if (spline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
       if (p.kind == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
@@ -551,21 +562,21 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
         gemm_issue(t_a + (pblocks + mb) * p.dP, mnmajor(tl.phi, 0, mb * kTile), mnmajor(tl.dy), p.dP, kTile,
                    false);
   });
-  float* stage = reinterpret_cast<float*>(smem);  // x tile region, idle after the MMAs
-  store_rows(tmem_addr(t_hi, warp * 32, 0), p.dP, p.d, rows, p.dx[sel] + rowbase * p.d, p.d, false, stage,
-             Identity{}, decode ? p.dy + rowbase * p.d : nullptr);
+  float* stage = reinterpret_cast<float*>(smem + (tl.da.saddr - base));  // idle after the MMAs
+  store_rows(t_hi, 0, p.dP, p.d, rows, p.dx[sel] + rowbase * p.d, p.d, false, stage, Identity{},
+             decode ? p.dy + rowbase * p.d : nullptr);
   for (int mb = 0; mb < pblocks; ++mb) {
-    const int prj = mb * kTile + tid;
-    for (int c = 0; c < p.dP; c += 16) {
+    const int prj = mb * kTile + row;
+    for (int c = 16 * half; c < p.dP; c += 32) {
       float v[16];
-      tmem_ld16(tmem_addr(t_a + mb * p.dP, warp * 32, c), v);
+      tmem_ld16(tmem_addr(t_a + mb * p.dP, quad * 32, c), v);
       if (prj < p.P && p.dW1) {
-        float* row = p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d;
+        float* wrow = p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d;
         for (int e = 0; e < 16 && c + e < p.d; e += 4) {
           if (c + e + 4 <= p.d && (p.d & 3) == 0) {
-            atomicAdd(reinterpret_cast<float4*>(row + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+            atomicAdd(reinterpret_cast<float4*>(wrow + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
           } else {
-            for (int q = 0; q < 4 && c + e + q < p.d; ++q) atomicAdd(row + c + e + q, v[e + q]);
+            for (int q = 0; q < 4 && c + e + q < p.d; ++q) atomicAdd(wrow + c + e + q, v[e + q]);
           }
         }
       }
@@ -573,10 +584,10 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   }
   if (decode) {
     for (int mb = 0; mb < mblocks; ++mb) {
-      const int fi = mb * kTile + tid;
-      for (int c = 0; c < p.dP; c += 16) {
+      const int fi = mb * kTile + row;
+      for (int c = 16 * half; c < p.dP; c += 32) {
         float v[16];
-        tmem_ld16(tmem_addr(t_a + (pblocks + mb) * p.dP, warp * 32, c), v);
+        tmem_ld16(tmem_addr(t_a + (pblocks + mb) * p.dP, quad * 32, c), v);
         if (fi < p.m && p.dW2) {
           for (int e = 0; e < 16 && c + e < p.d; ++e)
             atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.d + c + e) * p.m + fi, v[e]);

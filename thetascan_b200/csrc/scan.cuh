@@ -74,9 +74,9 @@ __device__ __forceinline__ void load_scaled_rows(const Tile& t, const __nv_bfloa
                                                  int rows_valid, int cols_valid, int unit_col, Scale scale) {
   load_tile(t, src, ld, rows_valid, cols_valid, unit_col);
   __syncthreads();
-  const int r = threadIdx.x;
+  const int r = my_row();
   const float s = scale(r);
-  for (int j = 0; j < t.cols / 8; ++j) {
+  for (int j = my_half(); j < t.cols / 8; j += 2) {
     float f[8];
     unpack8(tile_ld16(t, r, j), f);
 #pragma unroll

@@ -38,37 +38,37 @@ __device__ __forceinline__ const __nv_bfloat16* dout_rows(const ScanParams& p, c
 // Uses tiles td (dout staging) and tv (payload), TMEM columns t_g for g_r.
 __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile& td,
                               const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows) {
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
   for (int r = 0; r < p.R; ++r) {
     const __nv_bfloat16* dp = dout_rows(p, g, r, b, h, t0);
     load_tile(td, dp, p.Dv, rows, p.Dv);
     ctx.run([&] { gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false); });
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
-    for (int c = 0; c < kTile; c += 16) {
+    for (int c = 16 * half; c < kTile; c += 32) {
       float gv[16], acc[16];
-      tmem_ld16(tmem_addr(t_g, warp * 32, c), gv);
-      if (r > 0) tmem_ld16(tmem_addr(t_ds, warp * 32, c), acc);
+      tmem_ld16(tmem_addr(t_g, quad * 32, c), gv);
+      if (r > 0) tmem_ld16(tmem_addr(t_ds, quad * 32, c), acc);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
-        const float term = (j <= tid) ? w * gv[e] : 0.f;
+        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
+        const float term = (j <= row) ? w * gv[e] : 0.f;
         acc[e] = (r > 0) ? acc[e] + term : term;
       }
-      tmem_st16(tmem_addr(t_ds, warp * 32, c), acc);
+      tmem_st16(tmem_addr(t_ds, quad * 32, c), acc);
     }
   }
 }
 
-// Move the f32 ds accumulator (TMEM) into a bf16 tile, row tid.
+// Move the f32 ds accumulator (TMEM) into a bf16 tile.
 __device__ __forceinline__ void ds_to_tile(uint32_t t_ds, const Tile& tds) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  for (int c = 0; c < kTile; c += 16) {
+  const int row = my_row();
+  for (int c = 16 * my_half(); c < kTile; c += 32) {
     float v[16];
-    tmem_ld16(tmem_addr(t_ds, warp * 32, c), v);
-    tile_st16(tds, tid, c / 8, pack8(v));
-    tile_st16(tds, tid, c / 8 + 1, pack8(v + 8));
+    tmem_ld16(tmem_addr(t_ds, my_quad() * 32, c), v);
+    tile_st16(tds, row, c / 8, pack8(v));
+    tile_st16(tds, row, c / 8 + 1, pack8(v + 8));
   }
 }
 
@@ -94,9 +94,10 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
-  __shared__ float red[4];
+  __shared__ float red[32];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   const uint32_t ncols = tmem_cols_for(2 * region);
   bool any_dla = false;
   for (int r = 0; r < p.R; ++r) any_dla |= (p.la[r] != nullptr && g.dla[r] != nullptr);
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -141,12 +142,12 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
           gemm_issue(t_d + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
       });
       if (want) {
-        for (int j = 0; j < p.DvP / 8; ++j) {
+        for (int j = half; j < p.DvP / 8; j += 2) {
           float f[8];
-          unpack8(tile_ld16(tw, tid, j), f);
+          unpack8(tile_ld16(tw, row, j), f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= static_cast<float>(tid + 1);
-          tile_st16(tw, tid, j, pack8(f));
+          for (int e = 0; e < 8; ++e) f[e] *= static_cast<float>(row + 1);
+          tile_st16(tw, row, j, pack8(f));
         }
         ctx.run([&] {
           for (int mb = 0; mb < mblocks; ++mb)
@@ -156,34 +157,34 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
       float carry_dot = 0.f;
       const size_t si = state_index(p, b, h, n, r) * p.DkM * p.DvP;
       for (int mb = 0; mb < mblocks; ++mb) {
-        const size_t f = static_cast<size_t>(mb * kTile + tid);  // value-major [DvP][DkM]
-        for (int c = 0; c < p.DvP; c += 16) {
+        const size_t f = static_cast<size_t>(mb * kTile + row);  // value-major [DvP][DkM]
+        for (int c = 16 * half; c < p.DvP; c += 32) {
           float v[16];
-          tmem_ld16(tmem_addr(t_d, warp * 32, mb * p.DvP + c), v);
+          tmem_ld16(tmem_addr(t_d, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
           for (int e = 0; e < 16; ++e) g.gstates[si + static_cast<size_t>(c + e) * p.DkM + f] = v[e];
           if (want) {
             float x[16];
-            tmem_ld16(tmem_addr(t_x, warp * 32, mb * p.DvP + c), x);
+            tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), x);
 #pragma unroll
             for (int e = 0; e < 16; ++e) carry_dot += x[e] * p.states[si + static_cast<size_t>(c + e) * p.DkM + f];
           }
         }
       }
       if (want) {
-        const float sum = block_sum128(carry_dot, red);
-        if (tid == 0) atomicAdd(g.dla[r] + h, sum);
+        const float sum = block_sum(carry_dot, red);
+        if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
       }
     }
     if (want && n + 1 < p.NT) {
       // B'(n): key-weight derivative of the state this tile leaves behind.
-      for (int j = 0; j < p.DvP / 8; ++j) {
+      for (int j = half; j < p.DvP / 8; j += 2) {
         float f[8];
-        unpack8(tile_ld16(tv, tid, j), f);
-        const float wgt = static_cast<float>(kTile - 1 - tid) * __expf(la * static_cast<float>(kTile - 1 - tid));
+        unpack8(tile_ld16(tv, row, j), f);
+        const float wgt = static_cast<float>(kTile - 1 - row) * __expf(la * static_cast<float>(kTile - 1 - row));
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] *= wgt;
-        tile_st16(tw, tid, j, pack8(f));
+        tile_st16(tw, row, j, pack8(f));
       }
       ctx.run([&] {
         for (int mb = 0; mb < mblocks; ++mb)
@@ -191,10 +192,10 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
       });
       float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
       for (int mb = 0; mb < mblocks; ++mb) {
-        float* col = dst + mb * kTile + tid;
-        for (int c = 0; c < p.DvP; c += 16) {
+        float* col = dst + mb * kTile + row;
+        for (int c = 16 * half; c < p.DvP; c += 32) {
           float v[16];
-          tmem_ld16(tmem_addr(t_x, warp * 32, mb * p.DvP + c), v);
+          tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
           for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = v[e];
         }
@@ -279,7 +280,8 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   Tile tk{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
   Tile ts{tk.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
   const uint32_t ncols = 512;
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   }
   const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
   float* stage = reinterpret_cast<float*>(smem + (tds.saddr - base));
-  store_rows(tmem_addr(t_dq, warp * 32, 0), p.DkP, p.Dk, rows, grad_ptr(g.dq, g.grad_bf16, row0), p.Dk,
+  store_rows(t_dq, 0, p.DkP, p.Dk, rows, grad_ptr(g.dq, g.grad_bf16, row0), p.Dk,
              g.grad_bf16 != 0, stage, Identity{});
   tc_fence_before();
   __syncthreads();
@@ -335,7 +337,8 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   Tile tq{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
   Tile tg{tq.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
   const uint32_t ncols = 512;
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -368,13 +371,13 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
       const float la = head_la(p, r, h);
       const bool decayed = p.la[r] != nullptr;
       // (u_r o v) rows: reuse the dout staging tile.
-      for (int j = 0; j < p.DvP / 8; ++j) {
+      for (int j = half; j < p.DvP / 8; j += 2) {
         float f[8];
-        unpack8(tile_ld16(tv, tid, j), f);
-        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - tid)) : 1.f;
+        unpack8(tile_ld16(tv, row, j), f);
+        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] *= u;
-        tile_st16(td, tid, j, pack8(f));
+        tile_st16(td, row, j, pack8(f));
       }
       const size_t si = state_index(p, b, h, n, r);
       load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   }
   const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
   float* stage = reinterpret_cast<float*>(smem + (tds.saddr - base));
-  store_rows(tmem_addr(t_dk, warp * 32, 0), p.DkP, p.Dk, rows, grad_ptr(g.dk, g.grad_bf16, row0), p.Dk,
+  store_rows(t_dk, 0, p.DkP, p.Dk, rows, grad_ptr(g.dk, g.grad_bf16, row0), p.Dk,
              g.grad_bf16 != 0, stage, Identity{});
   tc_fence_before();
   __syncthreads();
@@ -400,9 +403,10 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
-  __shared__ float red[4];
+  __shared__ float red[32];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
@@ -413,7 +417,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
   const uint32_t ncols = tmem_cols_for(2 * kTile + p.DvP);
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -436,17 +440,17 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
     const bool want = decayed && g.dla[r] != nullptr;
-    for (int c = 0; c < kTile; c += 16) {
+    for (int c = 16 * half; c < kTile; c += 32) {
       float s[16], f[16];
-      tmem_ld16(tmem_addr(t_s, warp * 32, c), s);
+      tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
-        f[e] = (j <= tid) ? w * s[e] : 0.f;
+        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
+        f[e] = (j <= row) ? w * s[e] : 0.f;
       }
-      tile_st16(tp, tid, c / 8, pack8(f));
-      tile_st16(tp, tid, c / 8 + 1, pack8(f + 8));
+      tile_st16(tp, row, c / 8, pack8(f));
+      tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
     }
     load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     if (cross) {
@@ -464,25 +468,25 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     });
     if (want) {
       float acc = 0.f;
-      for (int c = 0; c < kTile; c += 16) {
+      for (int c = 16 * half; c < kTile; c += 32) {
         float s[16], gv[16];
-        tmem_ld16(tmem_addr(t_s, warp * 32, c), s);
-        tmem_ld16(tmem_addr(t_g, warp * 32, c), gv);
+        tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
+        tmem_ld16(tmem_addr(t_g, quad * 32, c), gv);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int j = c + e;
-          const float lag = static_cast<float>(tid - j);
-          if (j <= tid) acc += lag * __expf(la * lag) * s[e] * gv[e];
+          const float lag = static_cast<float>(row - j);
+          if (j <= row) acc += lag * __expf(la * lag) * s[e] * gv[e];
         }
       }
-      const float sum = block_sum128(acc, red);
-      if (tid == 0) atomicAdd(g.dla[r] + h, sum);
+      const float sum = block_sum(acc, red);
+      if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
     }
   }
 
   const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
   float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
-  store_rows(tmem_addr(t_dv, warp * 32, 0), p.DvP, p.Dv, rows, grad_ptr(g.dv, g.grad_bf16, row0), p.Dv,
+  store_rows(t_dv, 0, p.DvP, p.Dv, rows, grad_ptr(g.dv, g.grad_bf16, row0), p.Dv,
              g.grad_bf16 != 0, stage, Identity{});
   tc_fence_before();
   __syncthreads();

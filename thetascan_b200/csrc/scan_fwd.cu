@@ -5,6 +5,8 @@
 //                           S_in(n) = e^{128 la} S_in(n-1) + dS(n-1)  (f32)
 //   3. scan_out_kernel     per tile: score q.k^T once, then per retention
 //                           out_r = (w_r o causal o score) v + (c_r q) S_in  (tcgen05)
+// Tile kernels run 256 threads: the two threads of token row r (r, r+128)
+// split its columns into alternating 16-column chunks.
 #include "capi_internal.h"
 #include "scan.cuh"
 
@@ -17,7 +19,8 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
 
@@ -31,7 +34,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   const uint32_t ncols = cols_needed <= 32 ? 32 : cols_needed <= 64 ? 64 : cols_needed <= 128 ? 128
                          : cols_needed <= 256 ? 256 : 512;
 
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -40,8 +43,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
-  const int vcols = p.Dv - p.v_unit;
-  load_tile(tv, vp, p.vs[2], rows, vcols, p.v_unit ? p.Dv - 1 : -1);
+  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
 
   tc_fence_before();
   __syncthreads();
@@ -51,13 +53,13 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     // u_r(j) = exp(la (127 - j)): this tile's key weights in the leaving state.
-    const float u = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile - 1 - tid)) : 1.f;
-    for (int j = 0; j < p.DvP / 8; ++j) {
+    const float u = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
+    for (int j = half; j < p.DvP / 8; j += 2) {
       float f[8];
-      unpack8(tile_ld16(tv, tid, j), f);
+      unpack8(tile_ld16(tv, row, j), f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] *= u;
-      tile_st16(tw, tid, j, pack8(f));
+      tile_st16(tw, row, j, pack8(f));
     }
     ctx.run([&] {
       for (int mb = 0; mb < mblocks; ++mb) {
@@ -67,15 +69,15 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
     });
   }
 
-  // Epilogue: row f of block mb is feature mb*128 + tid; states are stored
-  // value-major ([DvP][DkM]), so lanes of a warp write consecutive features.
+  // Epilogue: accumulator row of block mb is feature mb*128 + row; states are
+  // stored value-major ([DvP][DkM]), so lanes of a warp write consecutive features.
   for (int r = 0; r < p.R; ++r) {
     float* dst_base = p.states + state_index(p, b, h, n, r) * p.DkM * p.DvP;
     for (int mb = 0; mb < mblocks; ++mb) {
-      float* dst = dst_base + mb * kTile + tid;
-      for (int c = 0; c < p.DvP; c += 16) {
+      float* dst = dst_base + mb * kTile + row;
+      for (int c = 16 * half; c < p.DvP; c += 32) {
         float v[16];
-        tmem_ld16(tmem_addr(ctx.tmem, warp * 32, (r * mblocks + mb) * p.DvP + c), v);
+        tmem_ld16(tmem_addr(ctx.tmem, quad * 32, (r * mblocks + mb) * p.DvP + c), v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) dst[static_cast<size_t>(c + e) * p.DkM] = v[e];
       }
@@ -132,7 +134,8 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
 
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
 
   const int cols_needed = kTile + p.R * p.DvP;
   const uint32_t ncols = cols_needed <= 256 ? 256 : 512;
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
@@ -168,19 +171,19 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
-    // P_r row tid: w(tid, j) * score(tid, j) on the causal triangle.
-    for (int c = 0; c < kTile; c += 16) {
+    // P_r row: w(row, j) * score(row, j) on the causal triangle.
+    for (int c = 16 * half; c < kTile; c += 32) {
       float s[16];
-      tmem_ld16(tmem_addr(t_score, warp * 32, c), s);
+      tmem_ld16(tmem_addr(t_score, quad * 32, c), s);
       float f[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(tid - j)) : 1.f;
-        f[e] = (j <= tid) ? w * s[e] : 0.f;
+        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
+        f[e] = (j <= row) ? w * s[e] : 0.f;
       }
-      tile_st16(tp, tid, c / 8, pack8(f));
-      tile_st16(tp, tid, c / 8 + 1, pack8(f + 8));
+      tile_st16(tp, row, c / 8, pack8(f));
+      tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
     }
     const bool cross = n > 0;
     if (cross) {
@@ -205,8 +208,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
     const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
     void* dst = p.out_bf16 ? static_cast<void*>(reinterpret_cast<__nv_bfloat16*>(p.out[r]) + row0)
                            : static_cast<void*>(reinterpret_cast<float*>(p.out[r]) + row0);
-    store_rows(tmem_addr(ctx.tmem, warp * 32, kTile + r * p.DvP), p.DvP, p.Dv, rows, dst, p.Dv, p.out_bf16 != 0,
-               stage, Identity{});
+    store_rows(ctx.tmem, kTile + r * p.DvP, p.DvP, p.Dv, rows, dst, p.Dv, p.out_bf16 != 0, stage, Identity{});
   }
   tc_fence_before();
   __syncthreads();

@@ -8,7 +8,7 @@
 
 namespace ts {
 
-__global__ void __launch_bounds__(kThreads) selftest_mma_kernel(const __nv_bfloat16* __restrict__ A,
+__global__ void __launch_bounds__(128) selftest_mma_kernel(const __nv_bfloat16* __restrict__ A,
                                                                 const __nv_bfloat16* __restrict__ B,
                                                                 float* __restrict__ D, int N, int K,
                                                                 int a_mn, int b_mn) {
@@ -64,7 +64,7 @@ int selftest_mma(const void* A, const void* B, float* D, int N, int K, int a_mn,
   }
   const size_t smem = static_cast<size_t>(128 * K + K * N) * 2;
   cudaFuncSetAttribute(selftest_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  selftest_mma_kernel<<<1, kThreads, smem, s>>>(static_cast<const __nv_bfloat16*>(A),
+  selftest_mma_kernel<<<1, 128, smem, s>>>(static_cast<const __nv_bfloat16*>(A),
                                                 static_cast<const __nv_bfloat16*>(B), D, N, K, a_mn, b_mn);
   return check_launch("selftest_mma");
 }
