@@ -39,6 +39,8 @@ CONFIGS = {
     # name: (B, T, d_model, H, memory_multiplier, expansion, feature_map, rope, J)
     "c2": dict(B=8, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
     "small": dict(B=2, T=1024, D=512, H=8, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+    # config-2 shapes at batch 2: inputs still larger than L2, for profiler captures
+    "c2b2": dict(B=2, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
 }
 
 

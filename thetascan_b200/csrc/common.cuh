@@ -299,11 +299,23 @@ __device__ __forceinline__ void gemm_issue(uint32_t d_tmem, const OperandView& a
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
+// 16-byte asynchronous global -> shared copy (LDGSTS, L1 bypassed).  Many
+// can be in flight per thread; cp_async_wait_all() waits for this thread's.
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Cooperative copy of a row-major bf16 matrix (rows_valid x cols_valid,
 // leading dimension `ld` elements) into `t`, zero-filling the rest of the
 // tile.  Consecutive threads cover 8 rows of one 8-column chunk, so the shared
 // stores are conflict-free and each row is read in 64-byte runs.  If
 // `unit_col` >= 0, column `unit_col` of every valid row is set to 1.
+// Whole in-range 16-byte chunks are copied with cp.async, so a thread has all
+// of its copies in flight at once; the tile is complete after
+// cp_async_wait_all() (MmaCtx::run and tiles_ready() do that) and a barrier.
 __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __restrict__ src, long ld,
                                           int rows_valid, int cols_valid, int unit_col = -1) {
   const int chunks = t.cols / 8;
@@ -314,26 +326,22 @@ __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __
     const int rest = it >> 3;
     const int j = rest % chunks;
     const int r = (rest / chunks) * 8 + r8;
+    const int c0 = j * 8;
+    const bool has_unit = unit_col >= c0 && unit_col < c0 + 8;
+    if (r < rows_valid && vec_ok && c0 + 8 <= cols_valid && !has_unit) {
+      cp_async16(t.saddr + tile_off(t, r, c0), src + r * ld + c0);
+      continue;
+    }
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < rows_valid) {
-      const int c0 = j * 8;
-      if (vec_ok && c0 + 8 <= cols_valid) {
-        v = __ldg(reinterpret_cast<const uint4*>(src + r * ld + c0));
-      } else {
-        float f[8];
+      float f[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = c0 + e;
-          f[e] = (c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
-        }
-        v = pack8(f);
+      for (int e = 0; e < 8; ++e) {
+        const int c = c0 + e;
+        f[e] = (c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
       }
-      if (unit_col >= c0 && unit_col < c0 + 8) {
-        float f[8];
-        unpack8(v, f);
-        f[unit_col - c0] = 1.f;
-        v = pack8(f);
-      }
+      if (has_unit) f[unit_col - c0] = 1.f;
+      v = pack8(f);
     }
     tile_st16(t, r, j, v);
   }
@@ -421,26 +429,50 @@ __device__ __forceinline__ void load_tile_any(const Tile& t, const void* __restr
   const float* s = static_cast<const float*>(src);
   const int chunks = t.cols / 8;
   const int total = t.rows * chunks;
-  for (int it = threadIdx.x; it < total; it += blockDim.x) {
-    const int r8 = it & 7;
-    const int rest = it >> 3;
-    const int j = rest % chunks;
-    const int r = (rest / chunks) * 8 + r8;
-    float f[8];
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && ((ld & 3) == 0);
+  // Four chunks per thread per pass: all loads are issued before any convert.
+  constexpr int kBatch = 4;
+  for (int it0 = threadIdx.x; it0 < total; it0 += kBatch * blockDim.x) {
+    float f[kBatch][8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int c = j * 8 + e;
-      f[e] = (r < rows_valid && c < cols_valid) ? __ldg(s + r * ld + c) : 0.f;
+    for (int q = 0; q < kBatch; ++q) {
+      const int it = it0 + q * blockDim.x;
+      const int r8 = it & 7;
+      const int rest = it >> 3;
+      const int j = rest % chunks;
+      const int r = (rest / chunks) * 8 + r8;
+      const int c0 = j * 8;
+      if (it < total && r < rows_valid && vec_ok && c0 + 8 <= cols_valid) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(s + r * ld + c0));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(s + r * ld + c0 + 4));
+        f[q][0] = a.x; f[q][1] = a.y; f[q][2] = a.z; f[q][3] = a.w;
+        f[q][4] = b.x; f[q][5] = b.y; f[q][6] = b.z; f[q][7] = b.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = c0 + e;
+          f[q][e] = (it < total && r < rows_valid && c < cols_valid) ? __ldg(s + r * ld + c) : 0.f;
+        }
+      }
     }
-    tile_st16(t, r, j, pack8(f));
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int it = it0 + q * blockDim.x;
+      if (it >= total) break;
+      const int r8 = it & 7;
+      const int rest = it >> 3;
+      const int j = rest % chunks;
+      const int r = (rest / chunks) * 8 + r8;
+      tile_st16(t, r, j, pack8(f[q]));
+    }
   }
 }
 
-// Copy a pre-arranged tile image (already in core-matrix order, `bytes` long)
-// from global memory.
+// Copy a pre-arranged tile image (already in core-matrix order, `bytes` long,
+// 16-byte aligned) from global memory, asynchronously like load_tile.
 __device__ __forceinline__ void load_image(const Tile& t, const void* __restrict__ src, int bytes) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) st_shared_v4(t.saddr + i * 16, __ldg(s + i));
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) cp_async16(t.saddr + i * 16, s + i * 16);
 }
 
 __device__ __forceinline__ void zero_tile(const Tile& t) {
@@ -481,6 +513,17 @@ __device__ __forceinline__ float row_pair_max(float v, float* pair) {
 
 // ------------------------------------------------------------------ CTA context
 
+// Barrier after the staging loads of a kernel's prologue: this thread's
+// cp.async copies have landed, all threads' tiles are visible to every thread
+// and to the tensor core, and TMEM allocation is ordered before later use.
+__device__ __forceinline__ void tiles_ready() {
+  cp_async_wait_all();
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
 // Per-CTA MMA context: TMEM base, one completion barrier and its parity.
 struct MmaCtx {
   uint64_t* bar;
@@ -492,6 +535,7 @@ struct MmaCtx {
   // commits, and all threads wait for completion.
   template <class F>
   __device__ __forceinline__ void run(F issue) {
+    cp_async_wait_all();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();

@@ -317,9 +317,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   load_tile(tl.x, xp, p.xs[sel][2], rows, p.d);
   load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
   if (decode) load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_a = ctx.tmem, t_y = ctx.tmem + 256;
   project(p, ctx, tl, t_a);
@@ -394,9 +392,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   }
   if (!spline)
     for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_a = ctx.tmem, t_hi = ctx.tmem + 256;
   ctx.run([&] {

@@ -56,6 +56,33 @@ __device__ __forceinline__ size_t state_index(const ScanParams& p, int b, int h,
 
 __device__ __forceinline__ int image_bytes(const ScanParams& p) { return p.DvP * p.DkP * 2; }
 
+// Thread mapping of the tile-prefix kernels.  A thread carries 8 consecutive
+// features (f8*8 ..) of one value column c of one state through the tiles.
+// Lanes 0-7 take 8 consecutive value columns and lanes 8 apart consecutive
+// feature groups, so a warp touches whole 128-byte lines both in the f32
+// states (value-major: 4 feature groups x 32 B per column) and in the bf16
+// images (core-matrix order: 8 columns x 16 B per feature group).
+// Grid: x = feature-group blocks of 32, y = R * (DvP / 8), z = B * H.
+struct PrefixLane {
+  int f8, c, r, b, h;
+  bool active;
+};
+__device__ __forceinline__ PrefixLane prefix_lane(const ScanParams& p) {
+  PrefixLane l;
+  const int cblocks = p.DvP / 8;
+  l.r = blockIdx.y / cblocks;
+  l.c = (blockIdx.y % cblocks) * 8 + (threadIdx.x & 7);
+  l.f8 = blockIdx.x * 32 + (threadIdx.x >> 3);
+  l.b = blockIdx.z / p.H;
+  l.h = blockIdx.z % p.H;
+  l.active = l.f8 < p.DkM / 8;
+  return l;
+}
+__host__ __device__ inline dim3 prefix_grid(int DkM, int DvP, int R, int BH) {
+  return dim3((DkM / 8 + 31) / 32, R * (DvP / 8), BH);
+}
+constexpr int kPrefixBatch = 8;   // tiles whose states are loaded together
+
 __device__ __forceinline__ void store_out(void* base, bool bf16, size_t idx, float v) {
   if (bf16) {
     reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
@@ -68,11 +95,12 @@ __device__ __forceinline__ void store_out(void* base, bool bf16, size_t idx, flo
 // source: a cooperative, coalesced copy (load_tile), then thread t rescales
 // its own row in shared memory (conflict-free in the core-matrix layout).
 // Rows >= rows_valid and columns >= cols_valid are zero; `unit_col` (if >= 0)
-// is 1 before scaling.  Requires blockDim.x == 128 == t.rows.
+// is 1 before scaling.  Requires blockDim.x == kThreads and t.rows == kTile.
 template <class Scale>
 __device__ __forceinline__ void load_scaled_rows(const Tile& t, const __nv_bfloat16* __restrict__ src, long long ld,
                                                  int rows_valid, int cols_valid, int unit_col, Scale scale) {
   load_tile(t, src, ld, rows_valid, cols_valid, unit_col);
+  cp_async_wait_all();
   __syncthreads();
   const int r = my_row();
   const float s = scale(r);

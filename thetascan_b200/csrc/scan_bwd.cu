@@ -123,9 +123,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
     load_tile(tk, kp, p.ks[2], rows, p.Dk);
     load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_d = ctx.tmem, t_x = ctx.tmem + static_cast<uint32_t>(region);
 
@@ -212,51 +210,65 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
 // G(n) = e^{128 la} G(n+1) + dSloc(n+1), G(NT-1) = 0, per state element; and
 // the key-weight and closing terms of the log-retention gradient.
 __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, ScanGradParams g) {
-  // Same thread mapping as the forward prefix: 8 features x 1 value column.
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  const int r = blockIdx.y;
-  const int bh = blockIdx.z;
-  const int b = bh / p.H, h = bh % p.H;
-  const bool active = idx < (p.DkM / 8) * p.DvP;
-  const int c = active ? idx % p.DvP : 0, f8 = active ? idx / p.DvP : 0;
-  const float la = head_la(p, r, h);
+  const PrefixLane l = prefix_lane(p);
+  const int r = l.r;
+  const float la = head_la(p, r, l.h);
   const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
   const bool want = p.la[r] != nullptr && g.dla[r] != nullptr;
-  const bool in_image = active && f8 * 8 < p.DkP;
-  const size_t img_off = static_cast<size_t>(f8) * p.DvP * 16 + static_cast<size_t>(c) * 16;
-  const size_t elem = static_cast<size_t>(c) * p.DkM + f8 * 8;
+  const bool in_image = l.active && l.f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  const float k128 = static_cast<float>(kTile) * closing;
   float G[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) G[e] = 0.f;
   float acc = 0.f;
-  for (int n = p.NT - 1; n >= 0 && active; --n) {
-    const size_t si = state_index(p, b, h, n, r);
-    const size_t base = si * p.DkM * p.DvP + elem;
-    float4* gp = reinterpret_cast<float4*>(g.gstates + base);
-    float4 l0 = make_float4(0.f, 0.f, 0.f, 0.f), l1 = l0;
-    if (n >= 1) {
-      l0 = gp[0];
-      l1 = gp[1];
-    }
-    gp[0] = make_float4(G[0], G[1], G[2], G[3]);
-    gp[1] = make_float4(G[4], G[5], G[6], G[7]);
-    if (in_image) {
-      uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
-      *reinterpret_cast<uint4*>(img) = pack8(G);
-    }
-    if (want && n + 1 < p.NT) {
-      const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
-      const float4* sp = reinterpret_cast<const float4*>(p.states + base);
-      const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1 = sp[1];
-      const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      const float k128 = static_cast<float>(kTile) * closing;
+  constexpr int kB = kPrefixBatch / 2;
+  // Reverse over tiles, a batch of tiles' inputs loaded together.
+  for (int n0 = p.NT - 1; n0 >= 0 && l.active; n0 -= kB) {
+    float4 ld[kB][2], pw[kB][2];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc += G[e] * (pv[e] + k128 * sv[e]);
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0 - k;
+      ld[k][0] = ld[k][1] = pw[k][0] = pw[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n < 0) continue;
+      const size_t base = state_index(p, l.b, l.h, n, r) * p.DkM * p.DvP + elem;
+      if (n >= 1) {
+        const float4* gp = reinterpret_cast<const float4*>(g.gstates + base);
+        ld[k][0] = gp[0];
+        ld[k][1] = gp[1];
+      }
+      if (want && n + 1 < p.NT) {
+        // pstates + 128 e^{128 la} S_in: the weight of G(n) in d la.
+        const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
+        const float4* sp = reinterpret_cast<const float4*>(p.states + base);
+        const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1 = sp[1];
+        pw[k][0] = make_float4(p0.x + k128 * s0.x, p0.y + k128 * s0.y, p0.z + k128 * s0.z, p0.w + k128 * s0.w);
+        pw[k][1] = make_float4(p1.x + k128 * s1.x, p1.y + k128 * s1.y, p1.z + k128 * s1.z, p1.w + k128 * s1.w);
+      }
     }
-    const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) G[e] = G[e] * closing + lv[e];
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0 - k;
+      if (n < 0) break;
+      const size_t si = state_index(p, l.b, l.h, n, r);
+      float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
+      gp[0] = make_float4(G[0], G[1], G[2], G[3]);
+      gp[1] = make_float4(G[4], G[5], G[6], G[7]);
+      if (in_image) {
+        uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+        *reinterpret_cast<uint4*>(img) = pack8(G);
+      }
+      const float pv[8] = {pw[k][0].x, pw[k][0].y, pw[k][0].z, pw[k][0].w,
+                           pw[k][1].x, pw[k][1].y, pw[k][1].z, pw[k][1].w};
+      const float lv[8] = {ld[k][0].x, ld[k][0].y, ld[k][0].z, ld[k][0].w,
+                           ld[k][1].x, ld[k][1].y, ld[k][1].z, ld[k][1].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc += G[e] * pv[e];
+        G[e] = G[e] * closing + lv[e];
+      }
+    }
   }
   if (want) {
     __shared__ float red[8];
@@ -268,7 +280,7 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
     if (threadIdx.x == 0) {
       float sum = 0.f;
       for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
-      atomicAdd(g.dla[r] + h, sum);
+      atomicAdd(g.dla[r] + l.h, sum);
     }
   }
 }
@@ -300,9 +312,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dq = ctx.tmem + 256;
 
@@ -357,9 +367,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dk = ctx.tmem + 256;
 
@@ -428,9 +436,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_s = ctx.tmem, t_g = ctx.tmem + kTile, t_dv = ctx.tmem + 2 * kTile;
   ctx.run([&] { gemm_issue(t_s, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
@@ -520,7 +526,7 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
     scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
     if (int e = check_launch("scan_bwd_state_kernel")) return e;
   }
-  scan_bwd_prefix_kernel<<<dim3(ceil_div((p.DkM / 8) * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p, g);
+  scan_bwd_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p, g);
   if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
   const dim3 grid(p.NT, p.H, p.B);
   scan_bwd_dq_kernel<<<grid, kThreads, s_dq, s>>>(p, g);

@@ -45,9 +45,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
 
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
 
   for (int r = 0; r < p.R; ++r) {
@@ -91,39 +89,48 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
 // ------------------------------------------------------------------ 2. prefix over tiles
 
 __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
-  // Thread <-> (8 consecutive features f8*8.., one value column c), c fastest:
-  // each step moves two float4 of state and writes one 16-byte image chunk,
-  // and consecutive threads write consecutive image chunks.
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  const int r = blockIdx.y;
-  const int bh = blockIdx.z;
-  const int b = bh / p.H, h = bh % p.H;
-  if (idx >= (p.DkM / 8) * p.DvP) return;
-  const int c = idx % p.DvP, f8 = idx / p.DvP;
-  const float la = head_la(p, r, h);
-  const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
-  const bool in_image = f8 * 8 < p.DkP;
-  const size_t img_off = static_cast<size_t>(f8) * p.DvP * 16 + static_cast<size_t>(c) * 16;
+  const PrefixLane l = prefix_lane(p);
+  if (!l.active) return;
+  const float la = head_la(p, l.r, l.h);
+  const float closing = (p.la[l.r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const bool in_image = l.f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
   float S[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) S[e] = 0.f;
-  for (int n = 0; n < p.NT; ++n) {
-    const size_t si = state_index(p, b, h, n, r);
-    float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + static_cast<size_t>(c) * p.DkM + f8 * 8);
-    float4 u0 = make_float4(0.f, 0.f, 0.f, 0.f), u1 = u0;
-    if (n + 1 < p.NT) {
-      u0 = ptr[0];
-      u1 = ptr[1];
-    }
-    ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
-    ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
-    if (in_image) {
-      uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
-      *reinterpret_cast<uint4*>(img) = pack8(S);
-    }
-    const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  // Loads of a batch of tiles are issued together (the in-place writes of a
+  // batch touch only tiles whose values were already read), so the serial
+  // chain pays one memory latency per batch rather than per tile.
+  for (int n0 = 0; n0 < p.NT; n0 += kPrefixBatch) {
+    float4 u[kPrefixBatch][2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) S[e] = S[e] * closing + u[e];
+    for (int k = 0; k < kPrefixBatch; ++k) {
+      const int n = n0 + k;
+      u[k][0] = u[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n + 1 < p.NT) {
+        const float4* ptr = reinterpret_cast<const float4*>(
+            p.states + state_index(p, l.b, l.h, n, l.r) * p.DkM * p.DvP + elem);
+        u[k][0] = ptr[0];
+        u[k][1] = ptr[1];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPrefixBatch; ++k) {
+      const int n = n0 + k;
+      if (n >= p.NT) break;
+      const size_t si = state_index(p, l.b, l.h, n, l.r);
+      float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + elem);
+      ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
+      ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
+      if (in_image) {
+        uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+        *reinterpret_cast<uint4*>(img) = pack8(S);
+      }
+      const float v[8] = {u[k][0].x, u[k][0].y, u[k][0].z, u[k][0].w, u[k][1].x, u[k][1].y, u[k][1].z, u[k][1].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) S[e] = S[e] * closing + v[e];
+    }
   }
 }
 
@@ -161,9 +168,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
 
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_score = ctx.tmem;
   ctx.run([&] { gemm_issue(t_score, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
@@ -230,7 +235,7 @@ int launch_scan_fwd(const ScanParams& p, cudaStream_t s) {
     scan_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, sm1, s>>>(p);
     if (int e = check_launch("scan_state_kernel")) return e;
   }
-  scan_prefix_kernel<<<dim3(ceil_div((p.DkM / 8) * p.DvP, 256), p.R, p.B * p.H), 256, 0, s>>>(p);
+  scan_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p);
   if (int e = check_launch("scan_prefix_kernel")) return e;
   scan_out_kernel<<<dim3(p.NT, p.H, p.B), kThreads, sm3, s>>>(p);
   return check_launch("scan_out_kernel");

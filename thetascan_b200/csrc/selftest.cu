@@ -37,9 +37,7 @@ __global__ void __launch_bounds__(128) selftest_mma_kernel(const __nv_bfloat16* 
     fence_mbar_init();
   }
   if (tid < 32) tmem_alloc(&tmem_base, 256);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  tiles_ready();
 
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const OperandView av = a_mn ? mnmajor(ta) : kmajor(ta);
