@@ -119,6 +119,11 @@ typedef struct ts_scan_grad_args {
   float* dlog_alpha[TS_MAX_RETENTIONS];
   void* workspace; /* ts_b200_scan_bwd_workspace_bytes(fwd) bytes */
   size_t workspace_bytes;
+  /* All zero: dv is contiguous [B,H,T,dv].  Otherwise element strides
+   * (batch, head, token) of a [B,H,T,dv - v_append_unit] view that receives
+   * the payload gradient (the unit column's gradient is not written), for
+   * instance the v slot of the gradient of a fused qkv projection. */
+  int64_t dv_strides[3];
 } ts_scan_grad_args;
 
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* fwd);
@@ -182,6 +187,20 @@ typedef struct ts_feature_args {
   void* phi_k;              /* bf16 [B,H,T,m] out */
   void* phi_q;              /* bf16 [B,H,T,m] out (if q) */
   float* y0;                /* f32 [B,H,T,d] out: q + W2 phi(q) (if q and w2), or NULL */
+  /* Optional fused prologue; all zero = k and q rows are used as given.
+   * Otherwise k and q are the RAW projections: each row is rotated (channel
+   * pairs (2i, 2i+1), i < rope_rot/2, by the f32 tables rope_cos / rope_sin
+   * [rope_pos0 + tokens, rope_rot/2] at row rope_pos0 + t) and, with l2norm,
+   * divided by max(||row||_2, l2norm_eps), in f32, then rounded to bf16:
+   * reference rope.py:57-72 (apply_rope) then norms.py:11-12 (l2norm), as
+   * block.py:595-599 applies them to q and k.  y0 is then qhat + W2 phi(qhat),
+   * and the backward returns gradients of the raw rows. */
+  int rope_rot;             /* even, <= head_dim; 0 = no rotation */
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_pos0;            /* sequence position of token 0 (sequence shards) */
+  int l2norm;               /* 1 = L2-normalize each row after the rotation */
+  float l2norm_eps;
 } ts_feature_args;
 
 int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream);
@@ -199,6 +218,13 @@ typedef struct ts_feature_grad_args {
   float* dthreshold;        /* f32 [H], ACCUMULATED, or NULL */
   float* dgain;             /* f32 like gain, ACCUMULATED, or NULL */
   float* dspline_scale;     /* f32 [H], ACCUMULATED, or NULL */
+  /* Optional bf16 outputs of the row gradients in place of dk / dq (which are
+   * then NULL): element strides (batch, head, token) of [B,H,T,d] views, for
+   * instance the k and q slots of the gradient of a fused qkv projection. */
+  void* dk_bf16;
+  void* dq_bf16;
+  int64_t dk_strides[3];
+  int64_t dq_strides[3];
 } ts_feature_grad_args;
 
 int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream);

@@ -121,3 +121,77 @@ def test_stale_bank_is_rejected_explicitly(dev):
     with pytest.raises(NotImplementedError):
         kernel_core(q, q, q, W1, W2, KernelSpec(kind="softmax_partition", mode="stale"),
                     log_alphas=torch.zeros(1, 2, device=dev), etas=torch.zeros(1, 2, device=dev))
+
+
+PROLOGUE_CASES = {
+    # name: (kind, P, basis, mode, J, B, H, T, d, rot)
+    "relu2_partial_rope": ("relu2_ridge", 256, 1, "fast", 1, 2, 2, 300, 64, 32),
+    "softmax_d40_rope20": ("softmax_partition", 64, 1, "sum", 0, 1, 3, 129, 40, 20),
+    "bspline_full_rope": ("projected_bspline", 8, 16, "fast", 2, 1, 2, 200, 64, 64),
+    "relu2_norm_only": ("relu2_ridge", 128, 1, "sum", 0, 2, 1, 77, 64, 0),
+}
+
+
+@pytest.mark.parametrize("name", list(PROLOGUE_CASES))
+def test_fused_prologue_matches_torch_prologue(dev, name):
+    """RoPE + L2 norm inside the feature kernels (``kernel_core_qkv``) against
+    the same transforms as f32 PyTorch ops in front of ``kernel_core``: output,
+    d qkv (all three slots) and the weight gradients.  Both run bf16 streams;
+    they differ by one bf16 rounding of the q/k gradient (the unfused chain
+    rounds it before the norm backward) and the order of the norm's sum."""
+    from thetascan_b200.kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv
+    from thetascan_b200.mixer import _rope, _rope_tables
+
+    kind, P, basis, mode, J, B, H, T, d, rot = PROLOGUE_CASES[name]
+    g = torch.Generator().manual_seed(sum(map(ord, name)))
+    qkv = (torch.randn(B, T, 3 * H * d, generator=g) * 0.7).to(torch.bfloat16)
+    m = P * basis
+    W1 = torch.randn(H, P, d, generator=g) / math.sqrt(d)
+    W2 = torch.randn(H, d, m, generator=g) * 0.2
+    thr = torch.randn(H, generator=g) * 0.1 if kind == "relu2_ridge" else None
+    gain = 4.0 + 8.0 * torch.rand(H, generator=g) if kind == "softmax_partition" else None
+    scale = 0.5 + torch.rand(H, generator=g) if kind == "projected_bspline" else None
+    las = etas = None
+    if J:
+        las = (0.9 + 0.099 * torch.rand(J, H, generator=g)).log()
+        etas = torch.randn(J, H, generator=g) * 0.5
+    w_out = torch.randn(B, T, H, d, generator=g).to(dev)
+    spec = KernelSpec(kind=kind, mode=mode, basis=basis)
+
+    def leaves():
+        return [None if x is None else x.to(dev).clone().requires_grad_(True)
+                for x in (qkv, W1, W2, thr, gain, scale, las, etas)]
+
+    def ctl(t, gn, sc):
+        return dict(threshold=t, gain=gn, spline_scale=sc)
+
+    # fused
+    a = leaves()
+    cos = sin = None
+    if rot:
+        cos, sin = _rope_tables(T, rot, 10000.0, str(dev))
+    y_f = kernel_core_qkv(a[0], H, a[1], a[2], spec, Prologue(rot, cos, sin, 1e-6), log_alphas=a[6],
+                          etas=a[7], **ctl(a[3], a[4], a[5]))
+    (y_f.float() * w_out).sum().backward()
+
+    # unfused: torch prologue in f32, then the plain entry point
+    b = leaves()
+    q, k, v = b[0].view(B, T, 3, H, d).permute(2, 0, 3, 1, 4)
+
+    def prep(x):
+        x = _rope(x.float(), rot, 10000.0)
+        return (x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)).to(torch.bfloat16).contiguous()
+
+    y_u = kernel_core(prep(q), prep(k), v.contiguous(), b[1], b[2], spec, log_alphas=b[6], etas=b[7],
+                      **ctl(b[3], b[4], b[5]))
+    (y_u.float() * w_out).sum().backward()
+
+    assert rel_err(y_f, y_u) < 1e-2
+    dq_f, dk_f, dv_f = a[0].grad.view(B, T, 3, H, d).unbind(2)
+    dq_u, dk_u, dv_u = b[0].grad.view(B, T, 3, H, d).unbind(2)
+    for label, got, want in (("dq", dq_f, dq_u), ("dk", dk_f, dk_u), ("dv", dv_f, dv_u),
+                             ("W1", a[1].grad, b[1].grad), ("W2", a[2].grad, b[2].grad)):
+        assert rel_err(got, want) < 1e-2, label
+    for i in range(3, 8):
+        if a[i] is not None:
+            assert rel_err(a[i].grad, b[i].grad) < 1e-2, i

@@ -43,6 +43,7 @@ class ScanGradArgs(ctypes.Structure):
         ("grad_dtype", ctypes.c_int),
         ("dlog_alpha", c_ptr4),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("dv_strides", c_int64_3),
     ]
 
 
@@ -77,6 +78,8 @@ class FeatureArgs(ctypes.Structure):
         ("gain_per_feature", ctypes.c_int), ("gain_scalar", ctypes.c_float),
         ("spline_scale", ctypes.c_void_p), ("spline_scale_scalar", ctypes.c_float),
         ("phi_k", ctypes.c_void_p), ("phi_q", ctypes.c_void_p), ("y0", ctypes.c_void_p),
+        ("rope_rot", ctypes.c_int), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
+        ("rope_pos0", ctypes.c_int), ("l2norm", ctypes.c_int), ("l2norm_eps", ctypes.c_float),
     ]
 
 
@@ -87,6 +90,8 @@ class FeatureGradArgs(ctypes.Structure):
         ("dw1", ctypes.c_void_p), ("dw2", ctypes.c_void_p),
         ("dscore_bias", ctypes.c_void_p), ("dthreshold", ctypes.c_void_p), ("dgain", ctypes.c_void_p),
         ("dspline_scale", ctypes.c_void_p),
+        ("dk_bf16", ctypes.c_void_p), ("dq_bf16", ctypes.c_void_p),
+        ("dk_strides", c_int64_3), ("dq_strides", c_int64_3),
     ]
 
 

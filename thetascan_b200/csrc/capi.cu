@@ -175,6 +175,8 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   g.dq = grad->dq;
   g.dk = grad->dk;
   g.dv = grad->dv;
+  for (int i = 0; i < 3; ++i) g.dvs[i] = grad->dv_strides[i];
+  g.dv_strided = (grad->dv_strides[0] | grad->dv_strides[1] | grad->dv_strides[2]) != 0;
   g.grad_bf16 = grad->grad_dtype == TS_DTYPE_BF16;
   g.gstates = static_cast<float*>(grad->workspace);
   g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));

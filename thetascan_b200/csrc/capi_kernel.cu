@@ -72,6 +72,18 @@ int build_feature_params(const ts_feature_args* a, FeatParams* p) {
   p->y0 = a->y0;
   p->nsel = a->q ? 2 : 1;
   p->sel0 = 0;
+  if (a->rope_rot < 0 || a->rope_rot % 2 || a->rope_rot > a->head_dim)
+    return set_error(TS_ERR_VALUE, "feature: rope_rot %d must be even and within 0..head_dim", a->rope_rot);
+  if (a->rope_rot > 0 && (!a->rope_cos || !a->rope_sin))
+    return set_error(TS_ERR_VALUE, "feature: rope_cos and rope_sin are required with rope_rot");
+  if (a->rope_pos0 < 0) return set_error(TS_ERR_VALUE, "feature: rope_pos0 must be >= 0");
+  if (a->l2norm && !(a->l2norm_eps > 0.f)) return set_error(TS_ERR_VALUE, "feature: l2norm_eps must be positive");
+  p->rot = a->rope_rot;
+  p->rcos = a->rope_cos;
+  p->rsin = a->rope_sin;
+  p->pos0 = a->rope_pos0;
+  p->l2norm = a->l2norm ? 1 : 0;
+  p->neps = a->l2norm_eps;
   return TS_OK;
 }
 
@@ -121,9 +133,11 @@ int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream) {
 int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream) {
   FeatParams p;
   if (int e = build_feature_params(args, &p)) return e;
-  if (!grad || !grad->dphi_k || !grad->dk || !grad->dw1)
-    return set_error(TS_ERR_VALUE, "feature_bwd: dphi_k, dk and dw1 are required");
-  if (args->q && (!grad->dphi_q || !grad->dq)) return set_error(TS_ERR_VALUE, "feature_bwd: dphi_q and dq are required");
+  if (!grad || !grad->dphi_k || !grad->dw1) return set_error(TS_ERR_VALUE, "feature_bwd: dphi_k and dw1 are required");
+  if ((grad->dk == nullptr) == (grad->dk_bf16 == nullptr))
+    return set_error(TS_ERR_VALUE, "feature_bwd: exactly one of dk and dk_bf16 is required");
+  if (args->q && (!grad->dphi_q || (grad->dq == nullptr) == (grad->dq_bf16 == nullptr)))
+    return set_error(TS_ERR_VALUE, "feature_bwd: dphi_q and exactly one of dq and dq_bf16 are required");
   if (feature_bwd_smem(p) > kMaxSmemBlock)
     return set_error(TS_ERR_NOT_IMPLEMENTED, "feature_bwd: shapes exceed the shared-memory budget of one CTA");
   p.dphi[0] = grad->dphi_k;
@@ -132,6 +146,12 @@ int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args*
   p.dy = grad->dy0;
   p.dx[0] = grad->dk;
   p.dx[1] = grad->dq;
+  p.dxb[0] = static_cast<__nv_bfloat16*>(grad->dk_bf16);
+  p.dxb[1] = static_cast<__nv_bfloat16*>(grad->dq_bf16);
+  for (int i = 0; i < 3; ++i) {
+    p.dxs[0][i] = grad->dk_strides[i];
+    p.dxs[1][i] = grad->dq_strides[i];
+  }
   p.dW1 = grad->dw1;
   p.dW2 = grad->dw2;
   p.dbias = grad->dscore_bias;

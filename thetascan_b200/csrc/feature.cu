@@ -10,8 +10,9 @@
 // produces dx = dA W1 (+ dy for q), dW1 += dA^T x, dW2 += dy^T phi and the
 // gradients of the per-head / per-feature controls.
 //
-// One thread owns one token row: the 32x32b TMEM load pattern hands every
-// thread its own accumulator row, so all row reductions stay in registers.
+// Two threads own one token row (threads t and t+128 read the same TMEM lane
+// quadrant and split the row's columns into alternating 16-column chunks);
+// row reductions combine the two halves through shared memory.
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -55,6 +56,14 @@ struct FeatParams {
   float* dthr;              // [H]
   float* dgain;             // [H] or [H, m]
   float* dscale;            // [H]
+  // fused row prologue (raw projections in x): rotation tables [pos0 + T, rot/2]
+  int rot, pos0, l2norm;
+  float neps;
+  const float* rcos;
+  const float* rsin;
+  // bf16 strided row-gradient outputs in place of the f32 dx
+  __nv_bfloat16* dxb[2];
+  long long dxs[2][3];
 };
 
 __device__ __forceinline__ float ctl_bias(const FeatParams& p, int h, int i) {
@@ -238,6 +247,167 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
   }
 }
 
+// ------------------------------------------------------------------ row prologue
+
+// Adjacent-pair rotation of 16 consecutive channels [c, c+16) of the row at
+// sequence position `t`, in f32 with separately rounded products as the
+// reference's elementwise tensor ops round them (rope.py:69-70).  `inverse`
+// applies the transpose (the backward of the rotation).
+__device__ __forceinline__ void rotate16(const FeatParams& p, int t, int c, float* f, bool inverse) {
+  const int hr = p.rot >> 1;
+#pragma unroll
+  for (int e = 0; e < 16; e += 2) {
+    const int col = c + e;
+    if (col >= p.rot) break;
+    const float cs = __ldg(p.rcos + static_cast<size_t>(t) * hr + (col >> 1));
+    const float sn = __ldg(p.rsin + static_cast<size_t>(t) * hr + (col >> 1));
+    const float x1 = f[e], x2 = f[e + 1];
+    if (!inverse) {
+      f[e] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      f[e + 1] = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+    } else {
+      f[e] = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      f[e + 1] = __fsub_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+    }
+  }
+}
+
+constexpr int kMaxRowChunks = 4;  // 16-column chunks per thread for d <= 128
+
+// In place on the staged x tile: rotate each valid row, L2-normalize it
+// (row / max(||row||, eps)) and round to bf16, so that the projection and the
+// y0 residual see the reference's post-RoPE, post-norm rows.  `row_norm[r]`
+// keeps the divisor of row r for the backward, negated when the eps clamp was
+// active (then the norm passes no gradient).  Needs the tile complete and
+// visible (after tiles_ready()); ends with the tile rewritten but no barrier.
+__device__ void prepare_rows(const FeatParams& p, const Tile& tx, int t0, int rows, float* row_norm, float* pair) {
+  const int row = my_row(), half = my_half();
+  const bool valid = row < rows;
+  const int t = p.pos0 + t0 + row;
+  float v[kMaxRowChunks][16];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxRowChunks; ++k) {
+    const int c = 16 * half + 32 * k;
+    if (c >= p.dP) break;
+    unpack8(tile_ld16(tx, row, c / 8), v[k]);
+    unpack8(tile_ld16(tx, row, c / 8 + 1), v[k] + 8);
+    if (valid && p.rot > 0) rotate16(p, t, c, v[k], false);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+  }
+  float N = 1.f;
+  if (p.l2norm) {
+    ss = row_pair_sum(ss, pair);
+    const float n = sqrtf(ss);
+    N = fmaxf(n, p.neps);
+    if (half == 0) row_norm[row] = n >= p.neps ? N : -N;
+  }
+  if (!valid) return;
+#pragma unroll
+  for (int k = 0; k < kMaxRowChunks; ++k) {
+    const int c = 16 * half + 32 * k;
+    if (c >= p.dP) break;
+    if (p.l2norm) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[k][e] = __fdiv_rn(v[k][e], N);
+    }
+    tile_st16(tx, row, c / 8, pack8(v[k]));
+    tile_st16(tx, row, c / 8 + 1, pack8(v[k] + 8));
+  }
+}
+
+// 16 raw channels [c, c+16) of row t0 + row of selection `sel` (zero past d).
+__device__ __forceinline__ void load_raw16(const FeatParams& p, int sel, int b, int h, int tok, int c, float* f) {
+  const __nv_bfloat16* src = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(tok) * p.xs[sel][2];
+  const bool vec = ((reinterpret_cast<uintptr_t>(src + c) & 15) == 0) && c + 16 <= p.d;
+  if (vec) {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(src + c)), f);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(src + c + 8)), f + 8);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = c + e < p.d ? bf2f(src[c + e]) : 0.f;
+  }
+}
+
+// Row-gradient epilogue of the backward.  TMEM columns [0, dP) at `t_dx` hold
+// the gradient of the rows as the projection saw them (plus `addend`, f32
+// [rows, d] row-major, when given).  With the fused prologue it is carried
+// back through the normalization and the rotation to the raw rows.  Written
+// as f32 rows of p.dx[sel] (contiguous) or bf16 rows of p.dxb[sel] (strided).
+__device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int b, int h, int t0, int rows,
+                                const float* __restrict__ addend, const float* row_norm, float* pair) {
+  const int row = my_row(), half = my_half(), quad = my_quad();
+  const bool valid = row < rows;
+  const int tok = t0 + row;
+  const int t = p.pos0 + tok;
+  float g[kMaxRowChunks][16];
+#pragma unroll
+  for (int k = 0; k < kMaxRowChunks; ++k) {
+    const int c = 16 * half + 32 * k;
+    if (c >= p.dP) break;
+    tmem_ld16(tmem_addr(t_dx, quad * 32, c), g[k]);
+    if (addend != nullptr && valid) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c + e < p.d) g[k][e] += addend[static_cast<size_t>(row) * p.d + c + e];
+    }
+  }
+  if (p.l2norm) {
+    // d raw = (g - xhat (xhat . g)) / N, or g / N where the eps clamp held.
+    const float Ns = valid ? row_norm[row] : 1.f;
+    const float N = fabsf(Ns);
+    float xh[kMaxRowChunks][16];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxRowChunks; ++k) {
+      const int c = 16 * half + 32 * k;
+      if (c >= p.dP) break;
+      if (valid) {
+        load_raw16(p, sel, b, h, tok, c, xh[k]);
+        if (p.rot > 0) rotate16(p, t, c, xh[k], false);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xh[k][e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        xh[k][e] = __fdiv_rn(xh[k][e], N);
+        dot = fmaf(xh[k][e], g[k][e], dot);
+      }
+    }
+    dot = row_pair_sum(dot, pair);
+    const float proj = Ns > 0.f ? dot : 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxRowChunks; ++k) {
+      const int c = 16 * half + 32 * k;
+      if (c >= p.dP) break;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) g[k][e] = (g[k][e] - xh[k][e] * proj) / N;
+    }
+  }
+  if (!valid) return;
+  const bool bf16 = p.dxb[sel] != nullptr;
+#pragma unroll
+  for (int k = 0; k < kMaxRowChunks; ++k) {
+    const int c = 16 * half + 32 * k;
+    if (c >= p.dP) break;
+    if (p.rot > 0) rotate16(p, t, c, g[k], true);
+    if (bf16) {
+      __nv_bfloat16* dst = p.dxb[sel] + b * p.dxs[sel][0] + h * p.dxs[sel][1] + static_cast<long long>(tok) * p.dxs[sel][2];
+      if (((reinterpret_cast<uintptr_t>(dst + c) & 15) == 0) && c + 16 <= p.d) {
+        *reinterpret_cast<uint4*>(dst + c) = pack8(g[k]);
+        *reinterpret_cast<uint4*>(dst + c + 8) = pack8(g[k] + 8);
+      } else {
+        for (int e = 0; e < 16 && c + e < p.d; ++e) dst[c + e] = __float2bfloat16_rn(g[k][e]);
+      }
+    } else {
+      float* dst = p.dx[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + tok) * p.d;
+      for (int e = 0; e < 16 && c + e < p.d; ++e) dst[c + e] = g[k][e];
+    }
+  }
+}
+
 // ------------------------------------------------------------------ forward
 
 __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
@@ -292,6 +462,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   __shared__ float pair[kThreads];
+  __shared__ float row_norm[kTile];
   const int n = blockIdx.x, h = blockIdx.y;
   const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
   const int row = my_row(), quad = my_quad();
@@ -318,6 +489,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
   if (decode) load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
   tiles_ready();
+  if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_a = ctx.tmem, t_y = ctx.tmem + 256;
   project(p, ctx, tl, t_a);
@@ -350,6 +522,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   __shared__ uint32_t tmem_base;
   __shared__ float red[32];
   __shared__ float pair[kThreads];
+  __shared__ float row_norm[kTile];
   const int n = blockIdx.x, h = blockIdx.y;
   const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
   const int row = my_row(), half = my_half(), quad = my_quad();
@@ -393,6 +566,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   if (!spline)
     for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   tiles_ready();
+  if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_a = ctx.tmem, t_hi = ctx.tmem + 256;
   ctx.run([&] {
@@ -558,9 +732,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
         gemm_issue(t_a + (pblocks + mb) * p.dP, mnmajor(tl.phi, 0, mb * kTile), mnmajor(tl.dy), p.dP, kTile,
                    false);
   });
-  float* stage = reinterpret_cast<float*>(smem + (tl.da.saddr - base));  // idle after the MMAs
-  store_rows(t_hi, 0, p.dP, p.d, rows, p.dx[sel] + rowbase * p.d, p.d, false, stage, Identity{},
-             decode ? p.dy + rowbase * p.d : nullptr);
+  store_row_grads(p, t_hi, sel, b, h, t0, rows, decode ? p.dy + rowbase * p.d : nullptr, row_norm, pair);
   for (int mb = 0; mb < pblocks; ++mb) {
     const int prj = mb * kTile + row;
     for (int c = 16 * half; c < p.dP; c += 32) {

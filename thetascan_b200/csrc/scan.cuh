@@ -39,6 +39,8 @@ struct ScanGradParams {
   void* dq;
   void* dk;
   void* dv;
+  long long dvs[3];          // element strides of a [B,H,T,Dv - v_unit] view when dv_strided
+  int dv_strided;
   int grad_bf16;
   float* dla[4];
   float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place

@@ -490,10 +490,16 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     }
   }
 
-  const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
   float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
-  store_rows(t_dv, 0, p.DvP, p.Dv, rows, grad_ptr(g.dv, g.grad_bf16, row0), p.Dv,
-             g.grad_bf16 != 0, stage, Identity{});
+  if (g.dv_strided) {
+    const long long off = b * g.dvs[0] + h * g.dvs[1] + static_cast<long long>(t0) * g.dvs[2];
+    store_rows(t_dv, 0, p.DvP, p.Dv - p.v_unit, rows, grad_ptr(g.dv, g.grad_bf16, off), g.dvs[2],
+               g.grad_bf16 != 0, stage, Identity{});
+  } else {
+    const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
+    store_rows(t_dv, 0, p.DvP, p.Dv, rows, grad_ptr(g.dv, g.grad_bf16, row0), p.Dv,
+               g.grad_bf16 != 0, stage, Identity{});
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_base, ncols);

@@ -87,125 +87,219 @@ def _kread_args(spec, slots, eta, y0, y):
     return a
 
 
+@dataclass(frozen=True)
+class Prologue:
+    """Row transform fused into the feature kernels: RoPE tables and L2 norm."""
+
+    rot: int
+    cos: torch.Tensor | None   # f32 [T, rot/2]
+    sin: torch.Tensor | None
+    l2norm_eps: float | None   # None: no normalization
+
+
+def _set_prologue(fa, prologue):
+    if prologue is None:
+        return
+    fa.rope_rot = prologue.rot
+    if prologue.rot:
+        fa.rope_cos, fa.rope_sin = prologue.cos.data_ptr(), prologue.sin.data_ptr()
+    if prologue.l2norm_eps is not None:
+        fa.l2norm, fa.l2norm_eps = 1, prologue.l2norm_eps
+
+
+def _controls(thr, bias, gain, scale):
+    return {"thr": _f32(thr), "bias": _f32(bias), "gain": _f32(gain), "scale": _f32(scale)}
+
+
+def _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue):
+    """Feature, scan and read kernels; returns y and what the backward needs."""
+    lib = _lib.load()
+    B, H, T, d = q.shape
+    W1b = W1.detach().to(torch.bfloat16).contiguous()
+    W2b = W2.detach().to(torch.bfloat16).contiguous()
+    m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
+    dev = q.device
+    phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
+    phi_q = torch.empty_like(phi_k)
+    y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+    fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
+    _set_prologue(fa, prologue)
+    _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
+
+    las = [None] + ([] if log_alphas is None else
+                    [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
+    slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
+    sa = _build_args(phi_q, phi_k, v, las, slots, True)
+    ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
+    sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
+
+    eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
+    y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=dev)
+    ra = _kread_args(spec, slots, eta, y0, y)
+    _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
+    state = dict(W1b=W1b, W2b=W2b, phi_q=phi_q, phi_k=phi_k, ws=ws, slots=slots, las=las, eta=eta, y0=y0)
+    return y, state
+
+
+def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out):
+    """Backward of the three stages.  ``dq_out``/``dk_out``/``dv_out`` are either
+    ``None`` (fresh f32 dq, dk and a bf16 [.., d+1] dv are returned) or bf16
+    strided views that receive the gradients in place."""
+    lib = _lib.load()
+    slots, las, eta, y0 = st["slots"], st["las"], st["eta"], st["y0"]
+    W1b, W2b, phi_q, phi_k = st["W1b"], st["W2b"], st["phi_q"], st["phi_k"]
+    n = len(slots)
+    B, H, T, d = q.shape
+    dev = q.device
+    dy = dy.contiguous()
+    if dy.dtype not in (torch.bfloat16, torch.float32):
+        dy = dy.float()
+
+    # 1. read epilogue
+    ra = _kread_args(spec, slots, eta, y0, None)
+    ga = _lib.KReadGradArgs()
+    ga.dy = dy.data_ptr()
+    ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
+    dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
+    for i, s in enumerate(dslots):
+        ga.dslots[i] = s.data_ptr()
+    dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+    ga.dy0 = dy0.data_ptr()
+    deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
+    ga.deta = _ptr(deta)
+    _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
+
+    # 2. scan
+    sa = _build_args(phi_q, phi_k, v, las, slots, True, st["ws"])
+    sg = _lib.ScanGradArgs()
+    m = phi_q.shape[-1]
+    # bf16 hand-over: the feature backward stages dphi as a bf16 tile.
+    dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
+    dphi_k = torch.empty_like(dphi_q)
+    if dv_out is None:
+        dvaug = torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev)
+        sg.dv = dvaug.data_ptr()
+    else:
+        dvaug = None
+        sg.dv = dv_out.data_ptr()
+        sg.dv_strides = _lib.c_int64_3(*dv_out.stride()[:3])
+    dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
+    for i in range(n):
+        sg.dout[i] = dslots[i].data_ptr()
+        sg.dlog_alpha[i] = _ptr(dlas[i])
+    sg.dq, sg.dk = dphi_q.data_ptr(), dphi_k.data_ptr()
+    sg.grad_dtype = _lib.TS_DTYPE_BF16
+    gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+    sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
+    _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
+    del gws
+
+    # 3. features
+    fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, None)
+    _set_prologue(fa, prologue)
+    fg = _lib.FeatureGradArgs()
+    fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
+    fg.dy0 = dy0.data_ptr()
+    dq = dk = None
+    if dq_out is None:
+        dk = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        dq = torch.empty_like(dk)
+        fg.dk, fg.dq = dk.data_ptr(), dq.data_ptr()
+    else:
+        fg.dk_bf16, fg.dq_bf16 = dk_out.data_ptr(), dq_out.data_ptr()
+        fg.dk_strides = _lib.c_int64_3(*dk_out.stride()[:3])
+        fg.dq_strides = _lib.c_int64_3(*dq_out.stride()[:3])
+    dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
+    dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+    grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
+             for key in ("thr", "bias", "gain", "scale")}
+    fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+    fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
+    fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
+    _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+    dla = None if n == 1 else torch.stack(dlas[1:])
+    return dict(dq=dq, dk=dk, dvaug=dvaug, dW1=dW1, dW2=dW2, dla=dla, deta=deta, **grads)
+
+
 class _KernelCore(torch.autograd.Function):
     @staticmethod
     def forward(ctx, spec, q, k, v, W1, W2, thr, bias, gain, scale, log_alphas, etas):
-        lib = _lib.load()
-        B, H, T, d = q.shape
-        W1b = W1.detach().to(torch.bfloat16).contiguous()
-        W2b = W2.detach().to(torch.bfloat16).contiguous()
-        ctl = {"thr": _f32(thr), "bias": _f32(bias), "gain": _f32(gain), "scale": _f32(scale)}
-        m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
-        dev = q.device
-        phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
-        phi_q = torch.empty_like(phi_k)
-        y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
-        _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
-
-        las = [None] + ([] if log_alphas is None else
-                        [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
-        slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
-        sa = _build_args(phi_q, phi_k, v, las, slots, True)
-        ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
-        sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
-        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
-
-        eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
-        y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=dev)
-        ra = _kread_args(spec, slots, eta, y0, y)
-        _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
-
-        ctx.spec = spec
-        ctx.has = (thr is not None, bias is not None, gain is not None, scale is not None,
-                   log_alphas is not None)
+        ctl = _controls(thr, bias, gain, scale)
+        y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, None)
+        ctx.spec, ctx.st, ctx.ctl = spec, st, ctl
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, W1.dtype, W2.dtype)
-        saved_las = [la for la in las[1:]]
-        ctx.save_for_backward(q, k, v, W1b, W2b, phi_q, phi_k, ws, *slots, *saved_las,
-                              *[t if t is not None else torch.empty(0, device=dev) for t in
-                                (ctl["thr"], ctl["bias"], ctl["gain"], ctl["scale"], eta, y0)])
-        ctx.n_slots = len(slots)
+        ctx.save_for_backward(q, k, v)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        lib = _lib.load()
-        spec = ctx.spec
-        n = ctx.n_slots
-        saved = ctx.saved_tensors
-        q, k, v, W1b, W2b, phi_q, phi_k, ws = saved[:8]
-        slots = list(saved[8:8 + n])
-        las = [None] + list(saved[8 + n:8 + 2 * n - 1])
-        thr, bias, gain, scale, eta, y0 = saved[8 + 2 * n - 1:]
-        has_thr, has_bias, has_gain, has_scale, has_la = ctx.has
-        thr = thr if has_thr else None
-        bias = bias if has_bias else None
-        gain = gain if has_gain else None
-        scale = scale if has_scale else None
-        eta = eta if has_la else None
-        B, H, T, d = q.shape
-        dev = q.device
-        dy = dy.contiguous()
-
-        # 1. read epilogue
-        ra = _kread_args(spec, slots, eta, y0, None)
-        ga = _lib.KReadGradArgs()
-        ga.dy = dy.data_ptr()
-        ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
-        if dy.dtype not in (torch.bfloat16, torch.float32):
-            dy = dy.float()
-            ga.dy, ga.dy_dtype = dy.data_ptr(), _lib.TS_DTYPE_F32
-        dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
-        for i, s in enumerate(dslots):
-            ga.dslots[i] = s.data_ptr()
-        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-        ga.dy0 = dy0.data_ptr()
-        deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
-        ga.deta = _ptr(deta)
-        _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
-
-        # 2. scan
-        sa = _build_args(phi_q, phi_k, v, las, slots, True, ws)
-        sg = _lib.ScanGradArgs()
-        m = phi_q.shape[-1]
-        # bf16 hand-over: the feature backward stages dphi as a bf16 tile.
-        dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
-        dphi_k = torch.empty_like(dphi_q)
-        dvaug = torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev)
-        dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
-        for i in range(n):
-            sg.dout[i] = dslots[i].data_ptr()
-            sg.dlog_alpha[i] = _ptr(dlas[i])
-        sg.dq, sg.dk, sg.dv = dphi_q.data_ptr(), dphi_k.data_ptr(), dvaug.data_ptr()
-        sg.grad_dtype = _lib.TS_DTYPE_BF16
-        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
-        sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
-        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
-        del gws
-
-        # 3. features
-        ctl = {"thr": thr, "bias": bias, "gain": gain, "scale": scale}
-        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, None)
-        fg = _lib.FeatureGradArgs()
-        fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
-        fg.dy0 = dy0.data_ptr()
-        dk = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-        dq = torch.empty_like(dk)
-        dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
-        dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
-        dthr = torch.zeros_like(thr) if thr is not None else None
-        dbias = torch.zeros_like(bias) if bias is not None else None
-        dgain = torch.zeros_like(gain) if gain is not None else None
-        dscale = torch.zeros_like(scale) if scale is not None else None
-        fg.dk, fg.dq, fg.dw1, fg.dw2 = dk.data_ptr(), dq.data_ptr(), dW1.data_ptr(), dW2.data_ptr()
-        fg.dscore_bias, fg.dthreshold = _ptr(dbias), _ptr(dthr)
-        fg.dgain, fg.dspline_scale = _ptr(dgain), _ptr(dscale)
-        _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
-
+        q, k, v = ctx.saved_tensors
+        g = _core_backward(ctx.spec, q, k, v, ctx.st, ctx.ctl, dy, None, None, None, None)
         qd, kd, vd, w1d, w2d = ctx.dtypes
-        dla = None if n == 1 else torch.stack(dlas[1:])
-        return (None, dq.to(qd), dk.to(kd), dvaug[..., :d].to(vd), dW1.to(w1d), dW2.to(w2d),
-                dthr, dbias, dgain, dscale, dla, deta)
+        d = q.shape[-1]
+        return (None, g["dq"].to(qd), g["dk"].to(kd), g["dvaug"][..., :d].to(vd), g["dW1"].to(w1d),
+                g["dW2"].to(w2d), g["thr"], g["bias"], g["gain"], g["scale"], g["dla"], g["deta"])
+
+
+def _qkv_views(qkv, H, d):
+    B, T = qkv.shape[:2]
+    q, k, v = qkv.view(B, T, 3, H, d).permute(2, 0, 3, 1, 4)
+    return q, k, v
+
+
+class _KernelCoreQKV(torch.autograd.Function):
+    """The hot path from the raw fused projection ``qkv [B,T,3Hd]``: RoPE and
+    L2 norm run inside the feature kernels, v is read in place, and the
+    backward writes the q, k and v gradients straight into ``d qkv``."""
+
+    @staticmethod
+    def forward(ctx, spec, prologue, H, qkv, W1, W2, thr, bias, gain, scale, log_alphas, etas):
+        d = qkv.shape[-1] // (3 * H)
+        q, k, v = _qkv_views(qkv, H, d)
+        ctl = _controls(thr, bias, gain, scale)
+        y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue)
+        ctx.spec, ctx.prologue, ctx.H, ctx.st, ctx.ctl = spec, prologue, H, st, ctl
+        ctx.dtypes = (W1.dtype, W2.dtype)
+        ctx.save_for_backward(qkv)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (qkv,) = ctx.saved_tensors
+        H = ctx.H
+        d = qkv.shape[-1] // (3 * H)
+        q, k, v = _qkv_views(qkv, H, d)
+        dqkv = torch.empty_like(qkv)
+        dq, dk, dv = _qkv_views(dqkv, H, d)
+        g = _core_backward(ctx.spec, q, k, v, ctx.st, ctx.ctl, dy, ctx.prologue, dq, dk, dv)
+        w1d, w2d = ctx.dtypes
+        return (None, None, None, dqkv, g["dW1"].to(w1d), g["dW2"].to(w2d), g["thr"], g["bias"], g["gain"],
+                g["scale"], g["dla"], g["deta"])
+
+
+def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,
+                    score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None):
+    """Hot path from the raw fused projection; returns ``y`` token-major ``[B,T,H,d]``.
+
+    ``qkv``: bf16 ``[B,T,3*H*d]`` output of the fused q/k/v projection
+    (block.py:593-594 layout: q, k, v blocks of ``H*d``).  ``prologue``
+    applies RoPE and the L2 norm to q and k inside the feature kernels, as
+    block.py:595-599 does before the mixer core."""
+    if not qkv.is_cuda:
+        raise RuntimeError("b200 backend requires CUDA tensors")
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 3 or not qkv.is_contiguous():
+        raise ValueError("kernel_core_qkv: qkv must be a contiguous bf16 [B,T,3*H*d] tensor")
+    if qkv.shape[-1] % (3 * H):
+        raise ValueError("kernel_core_qkv: last dimension must be 3*H*d")
+    if (log_alphas is None) != (spec.mode == "sum"):
+        raise ValueError("kernel_core_qkv: log_alphas are required exactly for a bank (mode fast/stale)")
+    if spec.mode == "stale":
+        raise NotImplementedError(
+            "b200 backend: the stale bank reads a difference of two scans whose mass can vanish; "
+            "its dedicated retention kind is not built yet (fast banks are supported)")
+    return _KernelCoreQKV.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale,
+                                log_alphas, etas)
 
 
 def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias=None, gain=None,

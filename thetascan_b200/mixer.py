@@ -8,9 +8,11 @@ module (src/thetascan/_core/modules/block.py:142-333), so a reference
 state dict loads unchanged and the same seed gives the same weights.
 
 The forward of the kernel family (block.py:573-724) runs the projections as
-cuBLAS GEMMs, RoPE and L2 norm as PyTorch elementwise ops, and the hot path
-(feature maps, multi-view scan, normalized read and bank blend) as the
-sm_100a kernels of :mod:`thetascan_b200.kernel`.  Streams are bf16; a float32
+cuBLAS GEMMs and the hot path (feature maps, multi-view scan, normalized read
+and bank blend) as the sm_100a kernels of :mod:`thetascan_b200.kernel`.  With
+the fused q/k/v projection, RoPE and the L2 norm of q and k run inside the
+feature kernels (and their backward inside the feature backward); the other
+projection layouts apply them as PyTorch f32 elementwise ops.  Streams are bf16; a float32
 input is computed with bf16 streams and returned in float32.
 """
 from __future__ import annotations
@@ -25,7 +27,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .config import ThetaScanConfig
-from .kernel import KernelSpec, kernel_core
+from .kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv
 
 EXPANSION_DOMAIN = "thetascan-expansion-v1"
 FINGERPRINT_MAGIC = b"TSXF"
@@ -272,14 +274,26 @@ class ThetaScanCore(nn.Module):
         H, d = self.n_heads, self.head_dim
         out_dtype = x.dtype
         xb = x.to(torch.bfloat16)
-        q, k, v = self.project(xb)
-        q, k = self.prepare_qk(q), self.prepare_qk(k)
-        if self.vmlp_in is not None:
-            v = v + self.vmlp_out(F.silu(self.vmlp_in(v.float()))).to(v.dtype)
-        v = v.contiguous()
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
-        y = kernel_core(q, k, v, W1, W2, self.spec, log_alphas=log_alphas, etas=etas, **self.kernel_controls())
+        if self.proj_qkv is not None and self.vmlp_in is None:
+            # Fused projection layout: RoPE and the L2 norm run inside the
+            # feature kernels, v is read from the projection in place.
+            qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
+            cos = sin = None
+            if self._rot:
+                cos, sin = _rope_tables(T, self._rot, float(self.cfg.rope.base), str(x.device))
+            prologue = Prologue(self._rot, cos, sin, 1e-6)
+            y = kernel_core_qkv(qkv, H, W1, W2, self.spec, prologue, log_alphas=log_alphas, etas=etas,
+                                **self.kernel_controls())
+        else:
+            q, k, v = self.project(xb)
+            q, k = self.prepare_qk(q), self.prepare_qk(k)
+            if self.vmlp_in is not None:
+                v = v + self.vmlp_out(F.silu(self.vmlp_in(v.float()))).to(v.dtype)
+            v = v.contiguous()
+            y = kernel_core(q, k, v, W1, W2, self.spec, log_alphas=log_alphas, etas=etas,
+                            **self.kernel_controls())
         if self.ogate is not None:
             lin = self.ogate.g.lin
             gate = F.linear(xb, lin.weight.to(torch.bfloat16), lin.bias.to(torch.bfloat16))
