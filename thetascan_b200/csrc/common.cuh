@@ -26,14 +26,17 @@
 
 namespace ts {
 
-constexpr int kTile = 128;          // tokens per tile (= MMA M)
-constexpr int kThreads = 256;       // two threads per tile row (column halves)
+constexpr int kTile = 128;            // tokens per tile (= MMA M)
+constexpr int kThreads = 512;         // threads of a tile CTA
+constexpr int kParts = kThreads / kTile;  // threads per tile row
+constexpr int kChunkStep = 16 * kParts;   // column stride between a thread's 16-column chunks
 
-// Thread <-> (tile row, column half).  Warps w and w+4 read the same TMEM
-// lane quadrant (w % 4), so threads t and t+128 own the same accumulator row
-// and split its columns into alternating 16-column chunks.
+// Thread <-> (tile row, part).  Warps w, w+4, w+8 and w+12 read the same TMEM
+// lane quadrant (w % 4), so threads t + 128 j (j < kParts) own the same
+// accumulator row and split its columns into 16-column chunks dealt out in
+// turn: part j takes chunks j, j + kParts, ...
 __device__ __forceinline__ int my_row() { return threadIdx.x & (kTile - 1); }
-__device__ __forceinline__ int my_half() { return threadIdx.x >> 7; }
+__device__ __forceinline__ int my_part() { return threadIdx.x >> 7; }
 __device__ __forceinline__ int my_quad() { return (threadIdx.x >> 5) & 3; }
 
 // Error codes written to the device status word.
@@ -372,36 +375,40 @@ __device__ __forceinline__ void store_tile(const Tile& t, __nv_bfloat16* __restr
   }
 }
 
-// Coalesced store of accumulator rows.  The two threads of row r (r, r+128)
-// own row r of a TMEM accumulator (columns [0, ncols) starting at column
-// `tcol` of `tbase`); rows [0, rows_valid) and columns [0, width) go to the
-// row-major matrix `dst` with leading dimension `ld` (f32 or bf16).  Every 32
-// columns pass through a padded shared stage (>= 128*33 floats) so that global
-// stores are whole 32-byte sectors.  `transform(row, col, value)` may adjust
-// each value; `addend` (same layout as dst, f32) is added on the way out.
+// Coalesced store of accumulator rows.  The kParts threads of row r own row
+// r of a TMEM accumulator (columns [0, ncols) starting at column `tcol` of
+// `tbase`); rows [0, rows_valid) and columns [0, width) go to the row-major
+// matrix `dst` with leading dimension `ld` (f32 or bf16).  Every kChunkStep
+// columns pass through a shared stage of kTile * kChunkStep floats (32 KB),
+// XOR-swizzled so that both the row-wise writes and the column-wise reads are
+// free of bank conflicts, and leave as whole 32-byte sectors.
+// `transform(row, col, value)` may adjust each value; `addend` (same layout as
+// dst, f32) is added on the way out.
+constexpr int kStageFloats = kTile * kChunkStep;
+
+__device__ __forceinline__ int stage_idx(int r, int c) { return r * kChunkStep + (c ^ (r & 31)); }
+
 template <class Transform>
 __device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, int width, int rows_valid, void* dst,
                                            long ld, bool bf16, float* stage, Transform transform,
                                            const float* __restrict__ addend = nullptr) {
-  const int row = my_row(), half = my_half();
+  const int row = my_row(), part = my_part();
   const uint32_t trow = tmem_addr(tbase, my_quad() * 32, tcol);
-  for (int c = 0; c < ncols; c += 32) {
-    const int cc = c + 16 * half;
+  for (int c = 0; c < ncols; c += kChunkStep) {
+    const int cc = c + 16 * part;
     if (cc < ncols) {
       float v[16];
       tmem_ld16(trow + cc, v);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) stage[row * 33 + 16 * half + e] = transform(row, cc + e, v[e]);
-    } else {
-      // Keep the warp-collective load pattern uniform: nothing to load here.
+      for (int e = 0; e < 16; ++e) stage[stage_idx(row, 16 * part + e)] = transform(row, cc + e, v[e]);
     }
     __syncthreads();
-    const int cols = min(32, width - c);
+    const int cols = min(kChunkStep, width - c);
     if (cols > 0) {
-      for (int i = threadIdx.x; i < rows_valid * 32; i += blockDim.x) {
-        const int r = i >> 5, e = i & 31;
+      for (int i = threadIdx.x; i < rows_valid * kChunkStep; i += blockDim.x) {
+        const int r = i / kChunkStep, e = i % kChunkStep;
         if (e < cols) {
-          float x = stage[r * 33 + e];
+          float x = stage[stage_idx(r, e)];
           if (addend != nullptr) x += addend[r * ld + c + e];
           if (bf16) {
             reinterpret_cast<__nv_bfloat16*>(dst)[r * ld + c + e] = __float2bfloat16_rn(x);
@@ -493,12 +500,15 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return s;
 }
 
-// Sum of a per-thread value over the two threads that own one row.
-__device__ __forceinline__ float row_pair_sum(float v, float* pair /* >= 256 floats */) {
+// Sum / max of a per-thread value over the kParts threads that own one row;
+// `pair` holds kThreads floats of shared memory.
+__device__ __forceinline__ float row_pair_sum(float v, float* pair) {
   __syncthreads();
   pair[threadIdx.x] = v;
   __syncthreads();
-  const float s = pair[my_row()] + pair[my_row() + kTile];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kParts; ++j) s += pair[my_row() + kTile * j];
   __syncthreads();
   return s;
 }
@@ -506,7 +516,9 @@ __device__ __forceinline__ float row_pair_max(float v, float* pair) {
   __syncthreads();
   pair[threadIdx.x] = v;
   __syncthreads();
-  const float s = fmaxf(pair[my_row()], pair[my_row() + kTile]);
+  float s = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kParts; ++j) s = fmaxf(s, pair[my_row() + kTile * j]);
   __syncthreads();
   return s;
 }

@@ -169,10 +169,10 @@ struct RowState {
 // Row statistics of the feature map; the two threads of a row each reduce
 // their column chunks and combine through `pair` (256 floats of shared memory).
 __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair) {
-  const int half = my_half();
+  const int part = my_part();
   RowState s{0.f, 0.f, -INFINITY};
   float ss = 0.f;
-  for (int c = 16 * half; c < p.PP; c += 32) {
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16];
     tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -183,7 +183,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   if (p.kind == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
     float M = 0.f;
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -198,7 +198,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
     s.mass = row_pair_sum(M, pair);
   } else if (p.kind == kSoftmax) {
     float mx = -INFINITY;
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -209,7 +209,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
     }
     mx = row_pair_max(mx, pair);
     float E = 0.f;
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
@@ -272,7 +272,7 @@ __device__ __forceinline__ void rotate16(const FeatParams& p, int t, int c, floa
   }
 }
 
-constexpr int kMaxRowChunks = 4;  // 16-column chunks per thread for d <= 128
+constexpr int kMaxRowChunks = 128 / kChunkStep;  // 16-column chunks per thread for d <= 128
 
 // In place on the staged x tile: rotate each valid row, L2-normalize it
 // (row / max(||row||, eps)) and round to bf16, so that the projection and the
@@ -281,14 +281,14 @@ constexpr int kMaxRowChunks = 4;  // 16-column chunks per thread for d <= 128
 // active (then the norm passes no gradient).  Needs the tile complete and
 // visible (after tiles_ready()); ends with the tile rewritten but no barrier.
 __device__ void prepare_rows(const FeatParams& p, const Tile& tx, int t0, int rows, float* row_norm, float* pair) {
-  const int row = my_row(), half = my_half();
+  const int row = my_row(), part = my_part();
   const bool valid = row < rows;
   const int t = p.pos0 + t0 + row;
   float v[kMaxRowChunks][16];
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxRowChunks; ++k) {
-    const int c = 16 * half + 32 * k;
+    const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
     unpack8(tile_ld16(tx, row, c / 8), v[k]);
     unpack8(tile_ld16(tx, row, c / 8 + 1), v[k] + 8);
@@ -301,12 +301,12 @@ __device__ void prepare_rows(const FeatParams& p, const Tile& tx, int t0, int ro
     ss = row_pair_sum(ss, pair);
     const float n = sqrtf(ss);
     N = fmaxf(n, p.neps);
-    if (half == 0) row_norm[row] = n >= p.neps ? N : -N;
+    if (part == 0) row_norm[row] = n >= p.neps ? N : -N;
   }
   if (!valid) return;
 #pragma unroll
   for (int k = 0; k < kMaxRowChunks; ++k) {
-    const int c = 16 * half + 32 * k;
+    const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
     if (p.l2norm) {
 #pragma unroll
@@ -337,14 +337,14 @@ __device__ __forceinline__ void load_raw16(const FeatParams& p, int sel, int b, 
 // as f32 rows of p.dx[sel] (contiguous) or bf16 rows of p.dxb[sel] (strided).
 __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int b, int h, int t0, int rows,
                                 const float* __restrict__ addend, const float* row_norm, float* pair) {
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const bool valid = row < rows;
   const int tok = t0 + row;
   const int t = p.pos0 + tok;
   float g[kMaxRowChunks][16];
 #pragma unroll
   for (int k = 0; k < kMaxRowChunks; ++k) {
-    const int c = 16 * half + 32 * k;
+    const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
     tmem_ld16(tmem_addr(t_dx, quad * 32, c), g[k]);
     if (addend != nullptr && valid) {
@@ -361,7 +361,7 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxRowChunks; ++k) {
-      const int c = 16 * half + 32 * k;
+      const int c = 16 * part + kChunkStep * k;
       if (c >= p.dP) break;
       if (valid) {
         load_raw16(p, sel, b, h, tok, c, xh[k]);
@@ -380,7 +380,7 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
     const float proj = Ns > 0.f ? dot : 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxRowChunks; ++k) {
-      const int c = 16 * half + 32 * k;
+      const int c = 16 * part + kChunkStep * k;
       if (c >= p.dP) break;
 #pragma unroll
       for (int e = 0; e < 16; ++e) g[k][e] = (g[k][e] - xh[k][e] * proj) / N;
@@ -390,7 +390,7 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
   const bool bf16 = p.dxb[sel] != nullptr;
 #pragma unroll
   for (int k = 0; k < kMaxRowChunks; ++k) {
-    const int c = 16 * half + 32 * k;
+    const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
     if (p.rot > 0) rotate16(p, t, c, g[k], true);
     if (bf16) {
@@ -416,16 +416,14 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
   return __bfloat162float(__ushort_as_bfloat16(u));
 }
 
-constexpr int kStageFloats = kTile * 33;
-
 // phi of this thread's row and column chunks into the phi tile (bf16).
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
                                                 const Tile& tphi, bool zero_row) {
-  const int row = my_row(), half = my_half();
+  const int row = my_row(), part = my_part();
   if (p.kind == kBspline) {
     const float sc = ctl_scale(p, h);
     const float invP = 1.f / static_cast<float>(p.P);
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16];
       tmem_ld16(ta_row + c, a);
       for (int e = 0; e < 16; ++e) {
@@ -443,7 +441,7 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
       }
     }
   } else {
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], f[16];
       tmem_ld16(ta_row + c, a);
       phi_chunk(p, st, a, c, h, f);
@@ -525,7 +523,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   __shared__ float row_norm[kTile];
   const int n = blockIdx.x, h = blockIdx.y;
   const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -564,7 +562,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
   }
   if (!spline)
-    for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
+    for (int j = p.PP / 8 + part; j < p.PM / 8; j += kParts) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   tiles_ready();
   if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
   MmaCtx ctx{&bar, tmem_base, 0u, true};
@@ -593,7 +591,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 
   float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
   if (!spline) {
-    for (int c = 16 * half; c < p.PP; c += 32) {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], f[16], g[16];
       tmem_ld16(ta_row + c, a);
       grad16(c, g);
@@ -671,7 +669,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 
   // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
   float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
-  for (int c = 16 * half; c < p.PP; c += 32) {
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16], dp[16];
     tmem_ld16(ta_row + c, a);
     dpre_chunk(c, a, dp);
@@ -698,7 +696,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
   if (decode) phi_row_to_tile(p, st, ta_row, h, tl.phi, !valid);
   const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
-  for (int c = 16 * half; c < p.PP; c += 32) {
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16], dp[16], da[16];
     tmem_ld16(ta_row + c, a);
     dpre_chunk(c, a, dp);
@@ -709,7 +707,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
   }
   if (spline)
-    for (int j = p.PP / 8 + half; j < p.PM / 8; j += 2) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
+    for (int j = p.PP / 8 + part; j < p.PM / 8; j += kParts) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   {
     const float s1 = block_sum(dthr, red);
     const float s2 = block_sum(dscale, red);
@@ -735,7 +733,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   store_row_grads(p, t_hi, sel, b, h, t0, rows, decode ? p.dy + rowbase * p.d : nullptr, row_norm, pair);
   for (int mb = 0; mb < pblocks; ++mb) {
     const int prj = mb * kTile + row;
-    for (int c = 16 * half; c < p.dP; c += 32) {
+    for (int c = 16 * part; c < p.dP; c += kChunkStep) {
       float v[16];
       tmem_ld16(tmem_addr(t_a + mb * p.dP, quad * 32, c), v);
       if (prj < p.P && p.dW1) {
@@ -753,7 +751,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   if (decode) {
     for (int mb = 0; mb < mblocks; ++mb) {
       const int fi = mb * kTile + row;
-      for (int c = 16 * half; c < p.dP; c += 32) {
+      for (int c = 16 * part; c < p.dP; c += kChunkStep) {
         float v[16];
         tmem_ld16(tmem_addr(t_a + (pblocks + mb) * p.dP, quad * 32, c), v);
         if (fi < p.m && p.dW2) {

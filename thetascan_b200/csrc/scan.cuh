@@ -106,7 +106,7 @@ __device__ __forceinline__ void load_scaled_rows(const Tile& t, const __nv_bfloa
   __syncthreads();
   const int r = my_row();
   const float s = scale(r);
-  for (int j = my_half(); j < t.cols / 8; j += 2) {
+  for (int j = my_part(); j < t.cols / 8; j += kParts) {
     float f[8];
     unpack8(tile_ld16(t, r, j), f);
 #pragma unroll

@@ -38,14 +38,14 @@ __device__ __forceinline__ const __nv_bfloat16* dout_rows(const ScanParams& p, c
 // Uses tiles td (dout staging) and tv (payload), TMEM columns t_g for g_r.
 __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile& td,
                               const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows) {
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   for (int r = 0; r < p.R; ++r) {
     const __nv_bfloat16* dp = dout_rows(p, g, r, b, h, t0);
     load_tile(td, dp, p.Dv, rows, p.Dv);
     ctx.run([&] { gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false); });
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
-    for (int c = 16 * half; c < kTile; c += 32) {
+    for (int c = 16 * part; c < kTile; c += kChunkStep) {
       float gv[16], acc[16];
       tmem_ld16(tmem_addr(t_g, quad * 32, c), gv);
       if (r > 0) tmem_ld16(tmem_addr(t_ds, quad * 32, c), acc);
@@ -64,7 +64,7 @@ __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaC
 // Move the f32 ds accumulator (TMEM) into a bf16 tile.
 __device__ __forceinline__ void ds_to_tile(uint32_t t_ds, const Tile& tds) {
   const int row = my_row();
-  for (int c = 16 * my_half(); c < kTile; c += 32) {
+  for (int c = 16 * my_part(); c < kTile; c += kChunkStep) {
     float v[16];
     tmem_ld16(tmem_addr(t_ds, my_quad() * 32, c), v);
     tile_st16(tds, row, c / 8, pack8(v));
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   __shared__ uint32_t tmem_base;
   __shared__ float red[32];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
           gemm_issue(t_d + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
       });
       if (want) {
-        for (int j = half; j < p.DvP / 8; j += 2) {
+        for (int j = part; j < p.DvP / 8; j += kParts) {
           float f[8];
           unpack8(tile_ld16(tw, row, j), f);
 #pragma unroll
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
       const size_t si = state_index(p, b, h, n, r) * p.DkM * p.DvP;
       for (int mb = 0; mb < mblocks; ++mb) {
         const size_t f = static_cast<size_t>(mb * kTile + row);  // value-major [DvP][DkM]
-        for (int c = 16 * half; c < p.DvP; c += 32) {
+        for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
           float v[16];
           tmem_ld16(tmem_addr(t_d, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
     }
     if (want && n + 1 < p.NT) {
       // B'(n): key-weight derivative of the state this tile leaves behind.
-      for (int j = half; j < p.DvP / 8; j += 2) {
+      for (int j = part; j < p.DvP / 8; j += kParts) {
         float f[8];
         unpack8(tile_ld16(tv, row, j), f);
         const float wgt = static_cast<float>(kTile - 1 - row) * __expf(la * static_cast<float>(kTile - 1 - row));
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
       float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
       for (int mb = 0; mb < mblocks; ++mb) {
         float* col = dst + mb * kTile + row;
-        for (int c = 16 * half; c < p.DvP; c += 32) {
+        for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
           float v[16];
           tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, Sca
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, Sca
       const float la = head_la(p, r, h);
       const bool decayed = p.la[r] != nullptr;
       // (u_r o v) rows: reuse the dout staging tile.
-      for (int j = half; j < p.DvP / 8; j += 2) {
+      for (int j = part; j < p.DvP / 8; j += kParts) {
         float f[8];
         unpack8(tile_ld16(tv, row, j), f);
         const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   __shared__ uint32_t tmem_base;
   __shared__ float red[32];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
     const bool want = decayed && g.dla[r] != nullptr;
-    for (int c = 16 * half; c < kTile; c += 32) {
+    for (int c = 16 * part; c < kTile; c += kChunkStep) {
       float s[16], f[16];
       tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
 #pragma unroll
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     });
     if (want) {
       float acc = 0.f;
-      for (int c = 16 * half; c < kTile; c += 32) {
+      for (int c = 16 * part; c < kTile; c += kChunkStep) {
         float s[16], gv[16];
         tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
         tmem_ld16(tmem_addr(t_g, quad * 32, c), gv);

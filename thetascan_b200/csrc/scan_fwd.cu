@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
     const float la = head_la(p, r, h);
     // u_r(j) = exp(la (127 - j)): this tile's key weights in the leaving state.
     const float u = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
-    for (int j = half; j < p.DvP / 8; j += 2) {
+    for (int j = part; j < p.DvP / 8; j += kParts) {
       float f[8];
       unpack8(tile_ld16(tv, row, j), f);
 #pragma unroll
@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
     float* dst_base = p.states + state_index(p, b, h, n, r) * p.DkM * p.DvP;
     for (int mb = 0; mb < mblocks; ++mb) {
       float* dst = dst_base + mb * kTile + row;
-      for (int c = 16 * half; c < p.DvP; c += 32) {
+      for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
         float v[16];
         tmem_ld16(tmem_addr(ctx.tmem, quad * 32, (r * mblocks + mb) * p.DvP + c), v);
 #pragma unroll
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), half = my_half(), quad = my_quad();
+  const int row = my_row(), part = my_part(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
     // P_r row: w(row, j) * score(row, j) on the causal triangle.
-    for (int c = 16 * half; c < kTile; c += 32) {
+    for (int c = 16 * part; c < kTile; c += kChunkStep) {
       float s[16];
       tmem_ld16(tmem_addr(t_score, quad * 32, c), s);
       float f[16];
