@@ -37,7 +37,11 @@ CASES = {
     "relu2_m128_sum": ("relu2_ridge", 128, 1, "sum", 0, 1, 2, 200, 64),
     "softmax_m64_fast2": ("softmax_partition", 64, 1, "fast", 2, 2, 2, 257, 64),
     "bspline_p8x16_fast3": ("projected_bspline", 8, 16, "fast", 3, 1, 2, 384, 64),
+    # per-feature controls: score bias with a threshold, per-feature sharpness with a bias
+    "relu2_bias_threshold": ("relu2_ridge", 128, 1, "fast", 1, 1, 2, 200, 64),
+    "softmax_feature_gain_bias": ("softmax_partition", 64, 1, "sum", 0, 1, 2, 150, 64),
 }
+WITH_BIAS = {"relu2_bias_threshold", "softmax_feature_gain_bias"}
 
 
 def _case_tensors(name):
@@ -47,15 +51,21 @@ def _case_tensors(name):
     k = F.normalize(torch.randn(B, H, T, d, generator=g), dim=-1).to(torch.bfloat16)
     v = torch.randn(B, H, T, d, generator=g).to(torch.bfloat16)
     m = P * basis
-    W1 = torch.randn(H, P, d, generator=g) / math.sqrt(d)
-    W2 = torch.randn(H, d, m, generator=g) * 0.2
+    # Weights are bf16-representable: the kernels take bf16 projection
+    # operands, so the oracle sees the same values (rounding W1 to bf16 moves
+    # the logits of a sharp softmax by up to gain * |a| * 2^-9).
+    W1 = (torch.randn(H, P, d, generator=g) / math.sqrt(d)).bfloat16().float()
+    W2 = (torch.randn(H, d, m, generator=g) * 0.2).bfloat16().float()
     ctl = {}
     if kind == "relu2_ridge":
         ctl["threshold"] = torch.randn(H, generator=g) * 0.1
     elif kind == "softmax_partition":
-        ctl["gain"] = 4.0 + 8.0 * torch.rand(H, generator=g)
+        shape = (H, m) if name in WITH_BIAS else (H,)
+        ctl["gain"] = 4.0 + 8.0 * torch.rand(*shape, generator=g)
     else:
         ctl["spline_scale"] = 0.5 + torch.rand(H, generator=g)
+    if name in WITH_BIAS:
+        ctl["score_bias"] = torch.randn(H, m, generator=g) * 0.2
     log_alphas = etas = None
     if J:
         alphas = torch.empty(J, H)
@@ -82,7 +92,8 @@ def test_kernel_core_matches_oracle_forward_and_backward(dev, name):
     gctl = {key: leaf(val) for key, val in ctl.items()}
     gla, geta = leaf(las), leaf(etas)
     y = kernel_core(gq, gk, gv, gW1, gW2, spec, threshold=gctl.get("threshold"), gain=gctl.get("gain"),
-                    spline_scale=gctl.get("spline_scale"), log_alphas=gla, etas=geta)
+                    spline_scale=gctl.get("spline_scale"), score_bias=gctl.get("score_bias"), log_alphas=gla,
+                    etas=geta)
     (y.double() * w_out.to(dev)).sum().backward()
     assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
 
@@ -98,6 +109,8 @@ def test_kernel_core_matches_oracle_forward_and_backward(dev, name):
         spec_dict["gain"] = octl["gain"]
     else:
         spec_dict.update(n_basis=basis, scale=octl["spline_scale"])
+    if "score_bias" in octl:
+        spec_dict["score_bias"] = octl["score_bias"]
     want = omixer.kernel_core(oq, ok_, ov, oW1, oW2, spec_dict, log_alphas=ola, etas=oeta, mode=mode,
                               chunk=64)
     (want.transpose(1, 2) * w_out).sum().backward()

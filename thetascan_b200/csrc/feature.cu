@@ -164,13 +164,24 @@ struct RowState {
   float inv;   // 1 / rms(a)
   float mass;  // relu2: sum of squared ReLU; softmax: sum of exp
   float mx;    // softmax: max logit
+  float dphi;  // with a gradient: sum_j g_j phi_j (relu2 / softmax)
 };
 
-// Row statistics of the feature map; the two threads of a row each reduce
-// their column chunks and combine through `pair` (256 floats of shared memory).
-__device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair) {
+struct NoGrad {
+  __device__ __forceinline__ void operator()(int, float*) const {}
+};
+
+// Row statistics of the feature map; the kParts threads of a row each reduce
+// their column chunks and combine through `pair` (kThreads floats of shared
+// memory).  relu2: ss pass, then mass (and sum g u^2) pass.  softmax: ss
+// pass, then one online pass for the max, the partition sum E and sum g e
+// (each part rescales its running sums when its max grows; the parts are
+// combined at the common max).  With kWithGrad, `grad16(c, g)` supplies the
+// feature gradient of columns [c, c+16) and dphi = sum_j g_j phi_j.
+template <bool kWithGrad, class Grad>
+__device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
   const int part = my_part();
-  RowState s{0.f, 0.f, -INFINITY};
+  RowState s{0.f, 0.f, -INFINITY, 0.f};
   float ss = 0.f;
   for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16];
@@ -182,44 +193,58 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
   if (p.kind == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
-    float M = 0.f;
+    float M = 0.f, Sg = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-      float a[16];
+      float a[16], g[16];
       tmem_ld16(ta_row + c, a);
+      if (kWithGrad) grad16(c, g);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
         if (i < p.P) {
           const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i) - thr, 0.f);
           M += u * u;
+          if (kWithGrad) Sg += g[e] * u * u;
         }
       }
     }
     s.mass = row_pair_sum(M, pair);
+    if (kWithGrad) {
+      Sg = row_pair_sum(Sg, pair);
+      s.dphi = s.mass > p.eps ? Sg / s.mass : 0.f;
+    }
   } else if (p.kind == kSoftmax) {
-    float mx = -INFINITY;
+    float m = -INFINITY, E = 0.f, Sg = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-      float a[16];
+      float a[16], g[16], l[16];
       tmem_ld16(ta_row + c, a);
+      if (kWithGrad) grad16(c, g);
+      float cm = -INFINITY;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        if (i < p.P) mx = fmaxf(mx, ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)));
+        l[e] = i < p.P ? ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) : -INFINITY;
+        cm = fmaxf(cm, l[e]);
       }
-    }
-    mx = row_pair_max(mx, pair);
-    float E = 0.f;
-    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-      float a[16];
-      tmem_ld16(ta_row + c, a);
+      if (cm > m) {
+        const float r = __expf(m - cm);
+        E *= r;
+        Sg *= r;
+        m = cm;
+      }
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        const int i = c + e;
-        if (i < p.P) E += __expf(ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) - mx);
+        if (c + e < p.P) {
+          const float w = __expf(l[e] - m);
+          E += w;
+          if (kWithGrad) Sg += g[e] * w;
+        }
       }
     }
-    s.mx = mx;
-    s.mass = row_pair_sum(E, pair);
+    s.mx = row_pair_max(m, pair);
+    const float r = __expf(m - s.mx);  // 0 for a part without columns (m = -inf)
+    s.mass = row_pair_sum(E * r, pair);
+    if (kWithGrad) s.dphi = row_pair_sum(Sg * r, pair) / s.mass;
   }
   return s;
 }
@@ -493,7 +518,7 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   project(p, ctx, tl, t_a);
 
   const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
-  const RowState st = row_stats(p, ta_row, h, pair);
+  const RowState st = row_stats<false>(p, ta_row, h, pair, NoGrad{});
   // Rows past the sequence end get zero features, so the decode below and the
   // stored tile are exact zeros there.
   phi_row_to_tile(p, st, ta_row, h, tl.phi, row >= rows);
@@ -574,8 +599,6 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 
   const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
   const uint32_t tb_row = tmem_addr(t_hi, quad * 32, 0);
-  const RowState st = row_stats(p, ta_row, h, pair);
-
   // Total gradient of 16 feature columns [c, c+16) of this row: staged dphi
   // plus the slow-decode contribution dy W2 (TMEM).
   auto grad16 = [&](int c, float* g) {
@@ -589,18 +612,9 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     }
   };
 
-  float dot_phi = 0.f;  // sum_j dphi_j phi_j (relu2 / softmax Jacobians)
-  if (!spline) {
-    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-      float a[16], f[16], g[16];
-      tmem_ld16(ta_row + c, a);
-      grad16(c, g);
-      phi_chunk(p, st, a, c, h, f);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) dot_phi += g[e] * f[e];
-    }
-    dot_phi = row_pair_sum(dot_phi, pair);
-  }
+  const RowState st = spline ? row_stats<false>(p, ta_row, h, pair, NoGrad{})
+                             : row_stats<true>(p, ta_row, h, pair, grad16);
+  const float dot_phi = st.dphi;  // sum_j g_j phi_j (relu2 / softmax Jacobians)
   // dpre for columns [c, c+16) (projection index for B-splines).
   auto dpre_chunk = [&](int c, const float* a, float* dp) {
     if (p.kind == kRelu2) {
