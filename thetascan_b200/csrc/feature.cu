@@ -178,7 +178,7 @@ struct NoGrad {
 // (each part rescales its running sums when its max grows; the parts are
 // combined at the common max).  With kWithGrad, `grad16(c, g)` supplies the
 // feature gradient of columns [c, c+16) and dphi = sum_j g_j phi_j.
-template <bool kWithGrad, class Grad>
+template <int KIND, bool kWithGrad, class Grad>
 __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
   const int part = my_part();
   RowState s{0.f, 0.f, -INFINITY, 0.f};
@@ -191,7 +191,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   }
   ss = row_pair_sum(ss, pair);
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
-  if (p.kind == kRelu2) {
+  if constexpr (KIND == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
     float M = 0.f, Sg = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
@@ -213,7 +213,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
       Sg = row_pair_sum(Sg, pair);
       s.dphi = s.mass > p.eps ? Sg / s.mass : 0.f;
     }
-  } else if (p.kind == kSoftmax) {
+  } else if constexpr (KIND == kSoftmax) {
     float m = -INFINITY, E = 0.f, Sg = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], g[16], l[16];
@@ -250,9 +250,10 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
 }
 
 // phi values for columns [c, c+16) of the (relu2 / softmax) feature row.
+template <int KIND>
 __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s, const float* a, int c, int h,
                                           float* out) {
-  if (p.kind == kRelu2) {
+  if constexpr (KIND == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
     const bool live = s.mass > p.eps;
     const float inv_mass = 1.f / fmaxf(s.mass, p.eps);
@@ -442,10 +443,11 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
 }
 
 // phi of this thread's row and column chunks into the phi tile (bf16).
+template <int KIND>
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
                                                 const Tile& tphi, bool zero_row) {
   const int row = my_row(), part = my_part();
-  if (p.kind == kBspline) {
+  if constexpr (KIND == kBspline) {
     const float sc = ctl_scale(p, h);
     const float invP = 1.f / static_cast<float>(p.P);
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
@@ -469,7 +471,7 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], f[16];
       tmem_ld16(ta_row + c, a);
-      phi_chunk(p, st, a, c, h, f);
+      phi_chunk<KIND>(p, st, a, c, h, f);
       if (zero_row) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) f[e] = 0.f;
@@ -480,7 +482,8 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
   }
 }
 
-__global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
@@ -518,10 +521,10 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
   project(p, ctx, tl, t_a);
 
   const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
-  const RowState st = row_stats<false>(p, ta_row, h, pair, NoGrad{});
+  const RowState st = row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{});
   // Rows past the sequence end get zero features, so the decode below and the
   // stored tile are exact zeros there.
-  phi_row_to_tile(p, st, ta_row, h, tl.phi, row >= rows);
+  phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows);
   __syncthreads();
   __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
   store_tile(tl.phi, out, p.m, rows, p.m);
@@ -539,7 +542,8 @@ __global__ void __launch_bounds__(kThreads) feature_fwd_kernel(FeatParams p) {
 
 // ------------------------------------------------------------------ backward
 
-__global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
@@ -554,7 +558,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
   const int rows = min(kTile, p.T - t0);
   const bool valid = row < rows;
   const bool decode = sel == 1 && p.dy != nullptr && p.W2 != nullptr;
-  const bool spline = p.kind == kBspline;
+  constexpr bool spline = KIND == kBspline;
 
   const uint32_t base = smem_u32(smem);
   FeatTiles tl;
@@ -612,12 +616,12 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     }
   };
 
-  const RowState st = spline ? row_stats<false>(p, ta_row, h, pair, NoGrad{})
-                             : row_stats<true>(p, ta_row, h, pair, grad16);
+  const RowState st = spline ? row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{})
+                             : row_stats<KIND, true>(p, ta_row, h, pair, grad16);
   const float dot_phi = st.dphi;  // sum_j g_j phi_j (relu2 / softmax Jacobians)
   // dpre for columns [c, c+16) (projection index for B-splines).
   auto dpre_chunk = [&](int c, const float* a, float* dp) {
-    if (p.kind == kRelu2) {
+    if constexpr (KIND == kRelu2) {
       float g[16];
       grad16(c, g);
       const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
@@ -633,7 +637,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
         }
         dp[e] = d;
       }
-    } else if (p.kind == kSoftmax) {
+    } else if constexpr (KIND == kSoftmax) {
       float g[16];
       grad16(c, g);
       const float inv_E = 1.f / st.mass;
@@ -690,8 +694,8 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       dot_a += dp[e] * a[e];
-      if (p.kind == kRelu2) dthr -= dp[e];
-      if (p.kind == kSoftmax && c + e < p.P) {
+      if (KIND == kRelu2) dthr -= dp[e];
+      if (KIND == kSoftmax && c + e < p.P) {
         const float gain = ctl_gain(p, h, c + e);
         const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
         if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
@@ -708,7 +712,7 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     dthr = dscale = dgain_head = 0.f;
   }
   // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
-  if (decode) phi_row_to_tile(p, st, ta_row, h, tl.phi, !valid);
+  if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
   const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
   for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16], dp[16], da[16];
@@ -727,9 +731,9 @@ __global__ void __launch_bounds__(kThreads) feature_bwd_kernel(FeatParams p) {
     const float s2 = block_sum(dscale, red);
     const float s3 = block_sum(dgain_head, red);
     if (threadIdx.x == 0) {
-      if (p.kind == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
+      if (KIND == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
       if (spline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
-      if (p.kind == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
+      if (KIND == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
     }
   }
 
@@ -792,20 +796,40 @@ size_t feature_bwd_smem(const FeatParams& p) {
   return bytes;
 }
 
-int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
+// One instantiation per feature kind: the kind decides the per-element code
+// of every sweep, and specialising keeps each kind's locals in registers.
+template <int KIND>
+static int launch_feature_fwd_kind(const FeatParams& p, cudaStream_t s) {
   const size_t sm = feature_fwd_smem(p);
-  cudaFuncSetAttribute(feature_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  cudaFuncSetAttribute(feature_fwd_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   const int NT = ceil_div(p.T, kTile);
-  feature_fwd_kernel<<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  feature_fwd_kernel<KIND><<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
   return check_launch("feature_fwd_kernel");
 }
 
-int launch_feature_bwd(const FeatParams& p, cudaStream_t s) {
+template <int KIND>
+static int launch_feature_bwd_kind(const FeatParams& p, cudaStream_t s) {
   const size_t sm = feature_bwd_smem(p);
-  cudaFuncSetAttribute(feature_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  cudaFuncSetAttribute(feature_bwd_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   const int NT = ceil_div(p.T, kTile);
-  feature_bwd_kernel<<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  feature_bwd_kernel<KIND><<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
   return check_launch("feature_bwd_kernel");
+}
+
+int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
+  switch (p.kind) {
+    case kRelu2: return launch_feature_fwd_kind<kRelu2>(p, s);
+    case kSoftmax: return launch_feature_fwd_kind<kSoftmax>(p, s);
+    default: return launch_feature_fwd_kind<kBspline>(p, s);
+  }
+}
+
+int launch_feature_bwd(const FeatParams& p, cudaStream_t s) {
+  switch (p.kind) {
+    case kRelu2: return launch_feature_bwd_kind<kRelu2>(p, s);
+    case kSoftmax: return launch_feature_bwd_kind<kSoftmax>(p, s);
+    default: return launch_feature_bwd_kind<kBspline>(p, s);
+  }
 }
 
 }  // namespace ts
