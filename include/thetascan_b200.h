@@ -225,6 +225,11 @@ typedef struct ts_feature_grad_args {
   void* dq_bf16;
   int64_t dk_strides[3];
   int64_t dq_strides[3];
+  /* Optional bf16 gradient of y0 in place of dy0 (which is then NULL):
+   * element strides (batch, head, token) of a [B,H,T,d] view, for instance the
+   * token-major gradient of the read output, whose y0 part is the identity. */
+  const void* dy0_bf16;
+  int64_t dy0_strides[3];
 } ts_feature_grad_args;
 
 int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream);
@@ -259,7 +264,7 @@ typedef struct ts_kread_grad_args {
   const void* dy;           /* [B,T,H,d] */
   int dy_dtype;             /* TS_DTYPE_F32 or TS_DTYPE_BF16 */
   void* dslots[TS_MAX_RETENTIONS]; /* bf16 [B,H,T,d+1] out: gradients of the scan reads */
-  float* dy0;               /* f32 [B,H,T,d] out */
+  float* dy0;               /* f32 [B,H,T,d] out (a copy of dy, head-major), or NULL */
   float* deta;              /* f32 [J,H], ACCUMULATED, or NULL */
 } ts_kread_grad_args;
 

@@ -144,6 +144,9 @@ int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args*
   p.dphi[1] = grad->dphi_q;
   p.dphi_bf16 = grad->dphi_dtype == TS_DTYPE_BF16;
   p.dy = grad->dy0;
+  p.dyb = static_cast<const __nv_bfloat16*>(grad->dy0_bf16);
+  for (int i = 0; i < 3; ++i) p.dys[i] = grad->dy0_strides[i];
+  if (p.dy && p.dyb) return set_error(TS_ERR_VALUE, "feature_bwd: give at most one of dy0 and dy0_bf16");
   p.dx[0] = grad->dk;
   p.dx[1] = grad->dq;
   p.dxb[0] = static_cast<__nv_bfloat16*>(grad->dk_bf16);
@@ -171,7 +174,7 @@ int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream) {
 int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad, ts_stream_t stream) {
   ReadParams p;
   if (int e = build_read_params(args, &p)) return e;
-  if (!grad || !grad->dy || !grad->dy0) return set_error(TS_ERR_VALUE, "kread_bwd: dy and dy0 are required");
+  if (!grad || !grad->dy) return set_error(TS_ERR_VALUE, "kread_bwd: dy is required");
   for (int s = 0; s <= p.J; ++s)
     if (!grad->dslots[s]) return set_error(TS_ERR_VALUE, "kread_bwd: null dslot %d", s);
   p.dy = grad->dy;

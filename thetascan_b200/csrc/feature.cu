@@ -49,6 +49,8 @@ struct FeatParams {
   const void* dphi[2];      // [B, H, T, m], f32 or bf16
   int dphi_bf16;
   const float* dy;          // [B, H, T, d] (q only) or null
+  const __nv_bfloat16* dyb; // or bf16 strided view of it
+  long long dys[3];
   float* dx[2];             // [B, H, T, d]
   float* dW1;               // [H, P, d]
   float* dW2;               // [H, d, m]
@@ -275,18 +277,47 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
 
 // ------------------------------------------------------------------ row prologue
 
-// Adjacent-pair rotation of 16 consecutive channels [c, c+16) of the row at
-// sequence position `t`, in f32 with separately rounded products as the
-// reference's elementwise tensor ops round them (rope.py:69-70).  `inverse`
-// applies the transpose (the backward of the rotation).
-__device__ __forceinline__ void rotate16(const FeatParams& p, int t, int c, float* f, bool inverse) {
+// Rotation factors of the 8 channel pairs of columns [c, c+16) at sequence
+// position t (zero-extended past rot): one vector load per table when the
+// tables allow it.
+struct Rot8 {
+  float cs[8], sn[8];
+};
+__device__ __forceinline__ Rot8 load_rot8(const FeatParams& p, int t, int c) {
+  Rot8 r;
   const int hr = p.rot >> 1;
+  const size_t base = static_cast<size_t>(t) * hr + (c >> 1);
+  if (c + 16 <= p.rot && (hr & 3) == 0) {
+    const float4* pc = reinterpret_cast<const float4*>(p.rcos + base);
+    const float4* ps = reinterpret_cast<const float4*>(p.rsin + base);
+    const float4 c0 = __ldg(pc), c1 = __ldg(pc + 1), s0 = __ldg(ps), s1 = __ldg(ps + 1);
+    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r.cs[i] = cv[i];
+      r.sn[i] = sv[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const bool in = c + 2 * i < p.rot;
+      r.cs[i] = in ? __ldg(p.rcos + base + i) : 1.f;
+      r.sn[i] = in ? __ldg(p.rsin + base + i) : 0.f;
+    }
+  }
+  return r;
+}
+
+// Adjacent-pair rotation of 16 consecutive channels [c, c+16) of the row, in
+// f32 with separately rounded products as the reference's elementwise tensor
+// ops round them (rope.py:69-70); channels past rot are left as they are.
+// `inverse` applies the transpose (the backward of the rotation).
+__device__ __forceinline__ void rotate16(const FeatParams& p, const Rot8& r, int c, float* f, bool inverse) {
 #pragma unroll
   for (int e = 0; e < 16; e += 2) {
-    const int col = c + e;
-    if (col >= p.rot) break;
-    const float cs = __ldg(p.rcos + static_cast<size_t>(t) * hr + (col >> 1));
-    const float sn = __ldg(p.rsin + static_cast<size_t>(t) * hr + (col >> 1));
+    if (c + e >= p.rot) break;
+    const float cs = r.cs[e >> 1], sn = r.sn[e >> 1];
     const float x1 = f[e], x2 = f[e + 1];
     if (!inverse) {
       f[e] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
@@ -318,7 +349,7 @@ __device__ void prepare_rows(const FeatParams& p, const Tile& tx, int t0, int ro
     if (c >= p.dP) break;
     unpack8(tile_ld16(tx, row, c / 8), v[k]);
     unpack8(tile_ld16(tx, row, c / 8 + 1), v[k] + 8);
-    if (valid && p.rot > 0) rotate16(p, t, c, v[k], false);
+    if (valid && c < p.rot) rotate16(p, load_rot8(p, t, c), c, v[k], false);
 #pragma unroll
     for (int e = 0; e < 16; ++e) ss = fmaf(v[k][e], v[k][e], ss);
   }
@@ -343,17 +374,21 @@ __device__ void prepare_rows(const FeatParams& p, const Tile& tx, int t0, int ro
   }
 }
 
-// 16 raw channels [c, c+16) of row t0 + row of selection `sel` (zero past d).
-__device__ __forceinline__ void load_raw16(const FeatParams& p, int sel, int b, int h, int tok, int c, float* f) {
-  const __nv_bfloat16* src = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(tok) * p.xs[sel][2];
-  const bool vec = ((reinterpret_cast<uintptr_t>(src + c) & 15) == 0) && c + 16 <= p.d;
+// 16 bf16 values [c, c+16) of the row at `src` as floats (zero past width).
+__device__ __forceinline__ void load_row16(const __nv_bfloat16* src, int c, int width, float* f) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(src + c) & 15) == 0) && c + 16 <= width;
   if (vec) {
     unpack8(__ldg(reinterpret_cast<const uint4*>(src + c)), f);
     unpack8(__ldg(reinterpret_cast<const uint4*>(src + c + 8)), f + 8);
   } else {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) f[e] = c + e < p.d ? bf2f(src[c + e]) : 0.f;
+    for (int e = 0; e < 16; ++e) f[e] = c + e < width ? bf2f(src[c + e]) : 0.f;
   }
+}
+
+// 16 raw channels [c, c+16) of row t0 + row of selection `sel` (zero past d).
+__device__ __forceinline__ void load_raw16(const FeatParams& p, int sel, int b, int h, int tok, int c, float* f) {
+  load_row16(p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(tok) * p.xs[sel][2], c, p.d, f);
 }
 
 // Row-gradient epilogue of the backward.  TMEM columns [0, dP) at `t_dx` hold
@@ -362,43 +397,54 @@ __device__ __forceinline__ void load_raw16(const FeatParams& p, int sel, int b, 
 // back through the normalization and the rotation to the raw rows.  Written
 // as f32 rows of p.dx[sel] (contiguous) or bf16 rows of p.dxb[sel] (strided).
 __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int b, int h, int t0, int rows,
-                                const float* __restrict__ addend, const float* row_norm, float* pair) {
+                                bool add_dy, size_t rowbase, const float* row_norm, float* pair) {
   const int row = my_row(), part = my_part(), quad = my_quad();
   const bool valid = row < rows;
   const int tok = t0 + row;
   const int t = p.pos0 + tok;
+  // Global inputs first, so that their latencies overlap: the raw row and the
+  // rotation factors (for the normalization backward) and the addend.
+  float xh[kMaxRowChunks][16];
+  Rot8 rot[kMaxRowChunks];
   float g[kMaxRowChunks][16];
 #pragma unroll
   for (int k = 0; k < kMaxRowChunks; ++k) {
     const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
+    if (p.l2norm && valid) load_raw16(p, sel, b, h, tok, c, xh[k]);
+    if (valid && c < p.rot) rot[k] = load_rot8(p, t, c);
     tmem_ld16(tmem_addr(t_dx, quad * 32, c), g[k]);
-    if (addend != nullptr && valid) {
+    if (add_dy && valid) {
+      float dy[16];
+      if (p.dyb != nullptr) {
+        load_row16(p.dyb + b * p.dys[0] + h * p.dys[1] + static_cast<long long>(tok) * p.dys[2], c, p.d, dy);
+      } else {
+        const float* src = p.dy + (rowbase + row) * p.d;
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (c + e < p.d) g[k][e] += addend[static_cast<size_t>(row) * p.d + c + e];
+        for (int e = 0; e < 16; ++e) dy[e] = c + e < p.d ? __ldg(src + c + e) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) g[k][e] += dy[e];
     }
   }
   if (p.l2norm) {
     // d raw = (g - xhat (xhat . g)) / N, or g / N where the eps clamp held.
     const float Ns = valid ? row_norm[row] : 1.f;
-    const float N = fabsf(Ns);
-    float xh[kMaxRowChunks][16];
+    const float invN = 1.f / fabsf(Ns);
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxRowChunks; ++k) {
       const int c = 16 * part + kChunkStep * k;
       if (c >= p.dP) break;
       if (valid) {
-        load_raw16(p, sel, b, h, tok, c, xh[k]);
-        if (p.rot > 0) rotate16(p, t, c, xh[k], false);
+        if (c < p.rot) rotate16(p, rot[k], c, xh[k], false);
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) xh[k][e] = 0.f;
       }
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        xh[k][e] = __fdiv_rn(xh[k][e], N);
+        xh[k][e] *= invN;
         dot = fmaf(xh[k][e], g[k][e], dot);
       }
     }
@@ -409,7 +455,7 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
       const int c = 16 * part + kChunkStep * k;
       if (c >= p.dP) break;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) g[k][e] = (g[k][e] - xh[k][e] * proj) / N;
+      for (int e = 0; e < 16; ++e) g[k][e] = (g[k][e] - xh[k][e] * proj) * invN;
     }
   }
   if (!valid) return;
@@ -418,7 +464,7 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
   for (int k = 0; k < kMaxRowChunks; ++k) {
     const int c = 16 * part + kChunkStep * k;
     if (c >= p.dP) break;
-    if (p.rot > 0) rotate16(p, t, c, g[k], true);
+    if (c < p.rot) rotate16(p, rot[k], c, g[k], true);
     if (bf16) {
       __nv_bfloat16* dst = p.dxb[sel] + b * p.dxs[sel][0] + h * p.dxs[sel][1] + static_cast<long long>(tok) * p.dxs[sel][2];
       if (((reinterpret_cast<uintptr_t>(dst + c) & 15) == 0) && c + 16 <= p.d) {
@@ -557,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const bool valid = row < rows;
-  const bool decode = sel == 1 && p.dy != nullptr && p.W2 != nullptr;
+  const bool decode = sel == 1 && (p.dy != nullptr || p.dyb != nullptr) && p.W2 != nullptr;
   constexpr bool spline = KIND == kBspline;
 
   const uint32_t base = smem_u32(smem);
@@ -588,7 +634,12 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
   load_tile_any(tdphi, dphi_src, p.m, rows, p.m, p.dphi_bf16 != 0);
   if (decode) {
     load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
-    load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
+    if (p.dyb != nullptr) {
+      load_tile(tl.dy, p.dyb + b * p.dys[0] + h * p.dys[1] + static_cast<long long>(t0) * p.dys[2], p.dys[2], rows,
+                p.d);
+    } else {
+      load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
+    }
   }
   if (!spline)
     for (int j = p.PP / 8 + part; j < p.PM / 8; j += kParts) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
@@ -748,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
         gemm_issue(t_a + (pblocks + mb) * p.dP, mnmajor(tl.phi, 0, mb * kTile), mnmajor(tl.dy), p.dP, kTile,
                    false);
   });
-  store_row_grads(p, t_hi, sel, b, h, t0, rows, decode ? p.dy + rowbase * p.d : nullptr, row_norm, pair);
+  store_row_grads(p, t_hi, sel, b, h, t0, rows, decode, rowbase, row_norm, pair);
   for (int mb = 0; mb < pblocks; ++mb) {
     const int prj = mb * kTile + row;
     for (int c = 16 * part; c < p.dP; c += kChunkStep) {

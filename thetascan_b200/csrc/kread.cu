@@ -29,7 +29,7 @@ struct ReadParams {
   const void* dy;              // [B, T, H, d]
   int dy_bf16;
   __nv_bfloat16* dout[5];      // [B, H, T, d+1]
-  float* dy0;                  // [B, H, T, d]
+  float* dy0;                  // [B, H, T, d] or null
   float* deta;                 // [J, H] (accumulated)
 };
 
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p
         if (vs.slot_b[k] >= 0) g[vs.slot_b[k]] -= val;
       }
       for (int s = 0; s < nslots; ++s) p.dout[s][row * (p.d + 1) + c] = __float2bfloat16_rn(g[s]);
-      if (c < p.d) p.dy0[row * p.d + c] = dyc;
+      if (c < p.d && p.dy0 != nullptr) p.dy0[row * p.d + c] = dyc;
     }
     // fast: d eta_j = dy.mem(1+j) - dy.mem(0); stale: d eta_j = -dy.mem(stale_j)
     for (int j = 0; j < p.J; ++j) deta[j] += (p.mode == 1) ? dymem[1 + j] - dymem[0] : -dymem[1 + j];

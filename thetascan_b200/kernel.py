@@ -164,8 +164,13 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
     for i, s in enumerate(dslots):
         ga.dslots[i] = s.data_ptr()
-    dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-    ga.dy0 = dy0.data_ptr()
+    # y0 enters y with coefficient 1, so its gradient is dy itself: a bf16 dy
+    # is handed to the feature backward as a head-major view, an f32 one as the
+    # head-major copy the read backward writes.
+    dy0 = None
+    if dy.dtype != torch.bfloat16:
+        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        ga.dy0 = dy0.data_ptr()
     deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
     ga.deta = _ptr(deta)
     _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
@@ -200,7 +205,12 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     _set_prologue(fa, prologue)
     fg = _lib.FeatureGradArgs()
     fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
-    fg.dy0 = dy0.data_ptr()
+    if dy0 is None:
+        dyv = dy.permute(0, 2, 1, 3)
+        fg.dy0_bf16 = dyv.data_ptr()
+        fg.dy0_strides = _lib.c_int64_3(*dyv.stride()[:3])
+    else:
+        fg.dy0 = dy0.data_ptr()
     dq = dk = None
     if dq_out is None:
         dk = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
