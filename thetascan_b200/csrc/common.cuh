@@ -310,6 +310,15 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+// Close the current group of this thread's cp.async copies / wait until at
+// most the newest `N` committed groups are still in flight.
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Cooperative copy of a row-major bf16 matrix (rows_valid x cols_valid,
 // leading dimension `ld` elements) into `t`, zero-filling the rest of the
@@ -405,15 +414,36 @@ __device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, 
     __syncthreads();
     const int cols = min(kChunkStep, width - c);
     if (cols > 0) {
-      for (int i = threadIdx.x; i < rows_valid * kChunkStep; i += blockDim.x) {
-        const int r = i / kChunkStep, e = i % kChunkStep;
-        if (e < cols) {
-          float x = stage[stage_idx(r, e)];
-          if (addend != nullptr) x += addend[r * ld + c + e];
-          if (bf16) {
-            reinterpret_cast<__nv_bfloat16*>(dst)[r * ld + c + e] = __float2bfloat16_rn(x);
+      // 8 consecutive columns per thread: one 16-byte store (bf16) or two (f32)
+      // where the row segment is whole and aligned, element stores otherwise.
+      constexpr int kGroups = kChunkStep / 8;
+      for (int i = threadIdx.x; i < rows_valid * kGroups; i += blockDim.x) {
+        const int r = i / kGroups, e0 = (i % kGroups) * 8;
+        if (e0 >= cols) continue;
+        float x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) x[q] = stage[stage_idx(r, e0 + q)];
+        const long off = r * ld + c + e0;
+        const bool whole = e0 + 8 <= cols;
+        if (addend != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (whole || e0 + q < cols) x[q] += addend[off + q];
+        }
+        if (bf16) {
+          __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst) + off;
+          if (whole && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            *reinterpret_cast<uint4*>(d) = pack8(x);
           } else {
-            reinterpret_cast<float*>(dst)[r * ld + c + e] = x;
+            for (int q = 0; q < 8 && e0 + q < cols; ++q) d[q] = __float2bfloat16_rn(x[q]);
+          }
+        } else {
+          float* d = reinterpret_cast<float*>(dst) + off;
+          if (whole && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            reinterpret_cast<float4*>(d)[0] = make_float4(x[0], x[1], x[2], x[3]);
+            reinterpret_cast<float4*>(d)[1] = make_float4(x[4], x[5], x[6], x[7]);
+          } else {
+            for (int q = 0; q < 8 && e0 + q < cols; ++q) d[q] = x[q];
           }
         }
       }
@@ -548,6 +578,24 @@ struct MmaCtx {
   template <class F>
   __device__ __forceinline__ void run(F issue) {
     cp_async_wait_all();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+      issue();
+      mma_commit(bar);
+    }
+    if (ok) ok = mbar_wait(bar, phase, kErrMmaTimeout);
+    phase ^= 1u;
+    tc_fence_after();
+  }
+
+  // As run(), but this thread's newest committed cp.async group may stay in
+  // flight (it must not feed this MMA).
+  template <class F>
+  __device__ __forceinline__ void run_keep_newest(F issue) {
+    cp_async_wait_group<1>();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();

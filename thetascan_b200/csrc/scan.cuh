@@ -58,6 +58,17 @@ __device__ __forceinline__ size_t state_index(const ScanParams& p, int b, int h,
 
 __device__ __forceinline__ int image_bytes(const ScanParams& p) { return p.DvP * p.DkP * 2; }
 
+// Decay powers exp(la_r k), k = 0..kTile-1, of every retention of head h into
+// shared memory (`tab`: R * kTile floats), so that the intra-tile weight is a
+// lookup: w_r(i, j) = tab[r * kTile + i - j] for j <= i.  Visible after the
+// next barrier.
+__device__ __forceinline__ void fill_decay(const ScanParams& p, int h, float* tab) {
+  for (int i = threadIdx.x; i < p.R * kTile; i += blockDim.x) {
+    const int r = i / kTile, k = i % kTile;
+    tab[i] = p.la[r] != nullptr ? __expf(head_la(p, r, h) * static_cast<float>(k)) : 1.f;
+  }
+}
+
 // Thread mapping of the tile-prefix kernels.  A thread carries 8 consecutive
 // features (f8*8 ..) of one value column c of one state through the tiles.
 // Lanes 0-7 take 8 consecutive value columns and lanes 8 apart consecutive

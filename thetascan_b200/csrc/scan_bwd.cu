@@ -19,8 +19,7 @@
 // contractions (no two large terms cancel), evaluated in f32.  Kernels:
 //   scan_bwd_state_kernel  local dS per tile                     (tcgen05)
 //   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
-//   scan_bwd_dq_kernel     ds (accumulated in TMEM), dq, e-term  (tcgen05)
-//   scan_bwd_dk_kernel     ds, dk                                (tcgen05)
+//   scan_bwd_dqk_kernel    ds (summed over retentions), then dq or dk (tcgen05)
 //   scan_bwd_dv_kernel     P_r, dv, f-term                       (tcgen05)
 #include "capi_internal.h"
 #include "scan.cuh"
@@ -34,41 +33,42 @@ __device__ __forceinline__ const __nv_bfloat16* dout_rows(const ScanParams& p, c
   return g.dout[r] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
 }
 
-// ds_acc (TMEM, 128 columns at t_ds) = sum_r w_r o causal o (dout_r . v^T).
-// Uses tiles td (dout staging) and tv (payload), TMEM columns t_g for g_r.
-__device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile& td,
-                              const Tile& tv, uint32_t t_g, uint32_t t_ds, int b, int h, int t0, int rows) {
+// ds = sum_r w_r o causal o (dout_r . v^T) into the bf16 tile `tds`.  The
+// dout tile of retention r is td[r] when `staged` (all loaded in the
+// prologue), else it is loaded into td[0] here.  g_r goes through TMEM
+// columns t_g; the sum over retentions stays in registers (this thread's two
+// 16-column chunks of its row).
+__device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaCtx& ctx, const Tile* td,
+                              bool staged, const Tile& tv, uint32_t t_g, const Tile& tds, int b, int h, int t0,
+                              int rows, const float* decay) {
   const int row = my_row(), part = my_part(), quad = my_quad();
+  constexpr int kChunks = kTile / kChunkStep;
+  float acc[kChunks][16];
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[k][e] = 0.f;
   for (int r = 0; r < p.R; ++r) {
-    const __nv_bfloat16* dp = dout_rows(p, g, r, b, h, t0);
-    load_tile(td, dp, p.Dv, rows, p.Dv);
-    ctx.run([&] { gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false); });
-    const float la = head_la(p, r, h);
-    const bool decayed = p.la[r] != nullptr;
-    for (int c = 16 * part; c < kTile; c += kChunkStep) {
-      float gv[16], acc[16];
+    const Tile& t = staged ? td[r] : td[0];
+    if (!staged) load_tile(t, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+    ctx.run([&] { gemm_issue(t_g, kmajor(t), kmajor(tv), kTile, p.DvP, false); });
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int c = 16 * part + kChunkStep * k;
+      float gv[16];
       tmem_ld16(tmem_addr(t_g, quad * 32, c), gv);
-      if (r > 0) tmem_ld16(tmem_addr(t_ds, quad * 32, c), acc);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
-        const float term = (j <= row) ? w * gv[e] : 0.f;
-        acc[e] = (r > 0) ? acc[e] + term : term;
+        if (j <= row) acc[k][e] += decay[r * kTile + row - j] * gv[e];
       }
-      tmem_st16(tmem_addr(t_ds, quad * 32, c), acc);
     }
   }
-}
-
-// Move the f32 ds accumulator (TMEM) into a bf16 tile.
-__device__ __forceinline__ void ds_to_tile(uint32_t t_ds, const Tile& tds) {
-  const int row = my_row();
-  for (int c = 16 * my_part(); c < kTile; c += kChunkStep) {
-    float v[16];
-    tmem_ld16(tmem_addr(t_ds, my_quad() * 32, c), v);
-    tile_st16(tds, row, c / 8, pack8(v));
-    tile_st16(tds, row, c / 8 + 1, pack8(v + 8));
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = 16 * part + kChunkStep * k;
+    tile_st16(tds, row, c / 8, pack8(acc[k]));
+    tile_st16(tds, row, c / 8 + 1, pack8(acc[k] + 8));
   }
 }
 
@@ -285,121 +285,108 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
   }
 }
 
-// ------------------------------------------------------------------ dq
+// ------------------------------------------------------------------ dq, dk
 
-__global__ void __launch_bounds__(kThreads) scan_bwd_dq_kernel(ScanParams p, ScanGradParams g) {
+// One kernel for both (kDq selects):
+//   dq = ds . k    + sum_r (c_r o dout_r) S_in,r^T   (tiles n >= 1 carry a state)
+//   dk = ds^T . q  + sum_r (u_r o v) G_r^T           (tiles n <= NT-2 feed one)
+// Prologue: v, the k (or q) tile and, when they fit (`nbuf` == R), every
+// retention's dout tile, plus the first state image.  The cross terms then
+// run with the image of retention r+1 loading (into the k/q region, free
+// after the ds product) while retention r multiplies.
+template <bool kDq>
+__global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, ScanGradParams g, int nbuf) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
+  __shared__ float decay[4 * kTile];
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), part = my_part(), quad = my_quad();
+  const int row = my_row(), part = my_part();
   const int warp = threadIdx.x >> 5;
   const int t0 = n * kTile;
   const int rows = min(kTile, p.T - t0);
   const uint32_t base = smem_u32(smem);
   Tile tv{base, kTile, p.DvP};
-  Tile td{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
-  Tile tds{td.saddr + kTile * p.DvP * 2, kTile, kTile};
-  Tile tk{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
-  Tile ts{tk.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
-  const uint32_t ncols = 512;
+  Tile tx{tv.saddr + kTile * p.DvP * 2, kTile, p.DkP};          // k (dq) or q (dk)
+  Tile tds{tx.saddr + kTile * p.DkP * 2, kTile, kTile};
+  Tile ts0{tds.saddr + kTile * kTile * 2, p.DvP, p.DkP};         // state image buffer 0
+  Tile ts1{tx.saddr, p.DvP, p.DkP};                               // buffer 1: the k/q region
+  Tile td[4];
+  for (int i = 0; i < 4; ++i) td[i] = Tile{ts0.saddr + p.DvP * p.DkP * 2 + i * kTile * p.DvP * 2, kTile, p.DvP};
+  const bool staged = nbuf >= p.R;
+  const bool cross = kDq ? n > 0 : n + 1 < p.NT;
+  const __nv_bfloat16* images = kDq ? p.images : g.gimages;
+  auto image_of = [&](int r) {
+    return reinterpret_cast<const uint8_t*>(images) + state_index(p, b, h, n, r) * static_cast<size_t>(image_bytes(p));
+  };
+  fill_decay(p, h, decay);
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, ncols);
-  const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  const __nv_bfloat16* xp = kDq ? p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2]
+                                : p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
   load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
-  load_tile(tk, kp, p.ks[2], rows, p.Dk);
+  load_tile(tx, xp, kDq ? p.ks[2] : p.qs[2], rows, p.Dk);
+  if (staged)
+    for (int r = 0; r < p.R; ++r) load_tile(td[r], dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+  if (cross) load_image(ts0, image_of(0), image_bytes(p));
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
-  const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dq = ctx.tmem + 256;
+  const uint32_t t_g = ctx.tmem, t_acc = ctx.tmem + 256;
 
-  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows);
-  ds_to_tile(t_ds, tds);
-  ctx.run([&] { gemm_issue(t_dq, kmajor(tds), mnmajor(tk), p.DkP, kTile, false); });
-  if (n > 0) {
+  accumulate_ds(p, g, ctx, td, staged, tv, t_g, tds, b, h, t0, rows, decay);
+  ctx.run([&] {
+    if (kDq) gemm_issue(t_acc, kmajor(tds), mnmajor(tx), p.DkP, kTile, false);
+    else gemm_issue(t_acc, mnmajor(tds), mnmajor(tx), p.DkP, kTile, false);
+  });
+  if (cross) {
     for (int r = 0; r < p.R; ++r) {
+      const Tile& img = (r & 1) ? ts1 : ts0;
+      // The buffer of retention r+1 was read by the product of r-1 (done).
+      if (r + 1 < p.R) load_image((r & 1) ? ts0 : ts1, image_of(r + 1), image_bytes(p));
+      cp_async_commit();
       const float la = head_la(p, r, h);
       const bool decayed = p.la[r] != nullptr;
-      load_scaled_rows(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
-                       [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
-      const size_t si = state_index(p, b, h, n, r);
-      load_image(ts, reinterpret_cast<const uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)),
-                 image_bytes(p));
-      ctx.run([&] { gemm_issue(t_dq, kmajor(td), mnmajor(ts), p.DkP, p.DvP, true); });
-    }
-  }
-  const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
-  float* stage = reinterpret_cast<float*>(smem + (tds.saddr - base));
-  store_rows(t_dq, 0, p.DkP, p.Dk, rows, grad_ptr(g.dq, g.grad_bf16, row0), p.Dk,
-             g.grad_bf16 != 0, stage, Identity{});
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem_base, ncols);
-}
-
-// ------------------------------------------------------------------ dk
-
-__global__ void __launch_bounds__(kThreads) scan_bwd_dk_kernel(ScanParams p, ScanGradParams g) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bar;
-  __shared__ uint32_t tmem_base;
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row = my_row(), part = my_part(), quad = my_quad();
-  const int warp = threadIdx.x >> 5;
-  const int t0 = n * kTile;
-  const int rows = min(kTile, p.T - t0);
-  const uint32_t base = smem_u32(smem);
-  Tile tv{base, kTile, p.DvP};
-  Tile td{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
-  Tile tds{td.saddr + kTile * p.DvP * 2, kTile, kTile};
-  Tile tq{tds.saddr + kTile * kTile * 2, kTile, p.DkP};
-  Tile tg{tq.saddr + kTile * p.DkP * 2, p.DvP, p.DkP};
-  const uint32_t ncols = 512;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) tmem_alloc(&tmem_base, ncols);
-  const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
-  const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
-  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
-  load_tile(tq, qp, p.qs[2], rows, p.Dk);
-  tiles_ready();
-  MmaCtx ctx{&bar, tmem_base, 0u, true};
-  const uint32_t t_g = ctx.tmem, t_ds = ctx.tmem + 128, t_dk = ctx.tmem + 256;
-
-  accumulate_ds(p, g, ctx, td, tv, t_g, t_ds, b, h, t0, rows);
-  ds_to_tile(t_ds, tds);
-  ctx.run([&] { gemm_issue(t_dk, mnmajor(tds), mnmajor(tq), p.DkP, kTile, false); });
-  if (n + 1 < p.NT) {
-    for (int r = 0; r < p.R; ++r) {
-      const float la = head_la(p, r, h);
-      const bool decayed = p.la[r] != nullptr;
-      // (u_r o v) rows: reuse the dout staging tile.
-      for (int j = part; j < p.DvP / 8; j += kParts) {
-        float f[8];
-        unpack8(tile_ld16(tv, row, j), f);
-        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
+      const Tile& ta = staged ? td[r] : td[0];
+      if (kDq) {
+        // rows of c_r o dout_r, c_r(i) = e^{la (i+1)}
+        const float c = decayed ? __expf(la * static_cast<float>(row + 1)) : 1.f;
+        if (!staged) {
+          load_tile(ta, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+          cp_async_wait_all();
+          __syncthreads();
+        }
+        for (int j = part; j < p.DvP / 8; j += kParts) {
+          float f[8];
+          unpack8(tile_ld16(ta, row, j), f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] *= u;
-        tile_st16(td, row, j, pack8(f));
+          for (int e = 0; e < 8; ++e) f[e] *= c;
+          tile_st16(ta, row, j, pack8(f));
+        }
+      } else {
+        // rows of u_r o v, u_r(i) = e^{la (127-i)}
+        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
+        for (int j = part; j < p.DvP / 8; j += kParts) {
+          float f[8];
+          unpack8(tile_ld16(tv, row, j), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= u;
+          tile_st16(ta, row, j, pack8(f));
+        }
       }
-      const size_t si = state_index(p, b, h, n, r);
-      load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
-                 image_bytes(p));
-      ctx.run([&] { gemm_issue(t_dk, kmajor(td), mnmajor(tg), p.DkP, p.DvP, true); });
+      ctx.run_keep_newest([&] { gemm_issue(t_acc, kmajor(ta), mnmajor(img), p.DkP, p.DvP, true); });
     }
   }
   const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
   float* stage = reinterpret_cast<float*>(smem + (tds.saddr - base));
-  store_rows(t_dk, 0, p.DkP, p.Dk, rows, grad_ptr(g.dk, g.grad_bf16, row0), p.Dk,
+  store_rows(t_acc, 0, p.DkP, p.Dk, rows, grad_ptr(kDq ? g.dq : g.dk, g.grad_bf16, row0), p.Dk,
              g.grad_bf16 != 0, stage, Identity{});
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+  if (warp == 0) tmem_dealloc(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ dv
@@ -425,6 +412,8 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
   const uint32_t ncols = tmem_cols_for(2 * kTile + p.DvP);
+  __shared__ float decay[4 * kTile];
+  fill_decay(p, h, decay);
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
@@ -452,8 +441,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
-        f[e] = (j <= row) ? w * s[e] : 0.f;
+        f[e] = (j <= row) ? decay[r * kTile + row - j] * s[e] : 0.f;
       }
       tile_st16(tp, row, c / 8, pack8(f));
       tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
@@ -481,8 +469,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int j = c + e;
-          const float lag = static_cast<float>(row - j);
-          if (j <= row) acc += lag * __expf(la * lag) * s[e] * gv[e];
+          if (j <= row) acc += static_cast<float>(row - j) * decay[r * kTile + row - j] * s[e] * gv[e];
         }
       }
       const float sum = block_sum(acc, red);
@@ -507,26 +494,33 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
 
 // ------------------------------------------------------------------ host launch
 
-static size_t dq_smem(const ScanParams& p) {
-  return static_cast<size_t>(kTile) * (2 * p.DvP + kTile + p.DkP) * 2 + static_cast<size_t>(p.DvP) * p.DkP * 2;
+// Dynamic shared memory of the dq/dk kernel with `nbuf` staged dout tiles.
+static size_t dqk_smem(const ScanParams& p, int nbuf) {
+  return static_cast<size_t>(kTile) * (p.DvP + p.DkP + kTile + nbuf * p.DvP) * 2 +
+         static_cast<size_t>(p.DvP) * p.DkP * 2;
 }
+// Budget for the dynamic part: the opt-in maximum per block less room for
+// the kernels' static shared memory.
+constexpr size_t kDynSmemBudget = 232448 - 4096;
+static int dqk_buffers(const ScanParams& p) { return dqk_smem(p, p.R) <= kDynSmemBudget ? p.R : 1; }
 static size_t dv_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2;
 }
 static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (2 * p.DkM + 2 * p.DvP) * 2; }
 
 size_t scan_bwd_max_smem(const ScanParams& p) {
-  size_t m = dq_smem(p);
+  size_t m = dqk_smem(p, dqk_buffers(p));
   if (dv_smem(p) > m) m = dv_smem(p);
   if (bstate_smem(p) > m) m = bstate_smem(p);
   return m;
 }
 
 int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s) {
-  const size_t s_state = bstate_smem(p), s_dq = dq_smem(p), s_dv = dv_smem(p);
+  const int nbuf = dqk_buffers(p);
+  const size_t s_state = bstate_smem(p), s_dqk = dqk_smem(p, nbuf), s_dv = dv_smem(p);
   cudaFuncSetAttribute(scan_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_state));
-  cudaFuncSetAttribute(scan_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dq));
-  cudaFuncSetAttribute(scan_bwd_dk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dq));
+  cudaFuncSetAttribute(scan_bwd_dqk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
+  cudaFuncSetAttribute(scan_bwd_dqk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
   if (p.NT > 1) {
     scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
@@ -535,9 +529,9 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
   scan_bwd_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p, g);
   if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
   const dim3 grid(p.NT, p.H, p.B);
-  scan_bwd_dq_kernel<<<grid, kThreads, s_dq, s>>>(p, g);
+  scan_bwd_dqk_kernel<true><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
   if (int e = check_launch("scan_bwd_dq_kernel")) return e;
-  scan_bwd_dk_kernel<<<grid, kThreads, s_dq, s>>>(p, g);
+  scan_bwd_dqk_kernel<false><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
   if (int e = check_launch("scan_bwd_dk_kernel")) return e;
   scan_bwd_dv_kernel<<<grid, kThreads, s_dv, s>>>(p, g);
   return check_launch("scan_bwd_dv_kernel");

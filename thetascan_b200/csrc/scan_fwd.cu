@@ -152,6 +152,8 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
   Tile tv{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile ts{tv.saddr + kTile * p.DvP * 2, p.DvP, p.DkP};
+  __shared__ float decay[4 * kTile];
+  fill_decay(p, h, decay);
 
   const int cols_needed = kTile + p.R * p.DvP;
   const uint32_t ncols = cols_needed <= 256 ? 256 : 512;
@@ -184,8 +186,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c + e;
-        const float w = decayed ? __expf(la * static_cast<float>(row - j)) : 1.f;
-        f[e] = (j <= row) ? w * s[e] : 0.f;
+        f[e] = (j <= row) ? decay[r * kTile + row - j] * s[e] : 0.f;
       }
       tile_st16(tp, row, c / 8, pack8(f));
       tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
