@@ -182,12 +182,41 @@ class PhaseTimer:
 
 
 def load_peaks():
+    """(sustained bf16 TFLOP/s, burst bf16 TFLOP/s, HBM GB/s, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
             peaks = json.load(f)
-        return peaks.get("bf16_tflops_sustained", 1403.9), peaks.get("bf16_tflops", 1638.2), "measured"
-    return 1400.0, 1590.0, "fallback"
+        return (peaks.get("bf16_tflops_sustained", 1403.9), peaks.get("bf16_tflops", 1638.2),
+                peaks.get("hbm_gbs", 6650.0), "measured")
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+def bytes_per_token(cfg):
+    """Compulsory HBM bytes per token of each entry point: its inputs read and
+    outputs written once (bf16 streams, f32 reads / y0; chunk states and other
+    scratch excluded).  Per head: x = d-wide q/k rows, m-wide features, R
+    retention slots of width d+1."""
+    H, d = cfg["H"], cfg["D"] // cfg["H"]
+    m = cfg["mult"] * d
+    R = 1 + cfg["J"]
+    return {
+        "ts_b200_feature_fwd": H * (2 * d * 2 + 2 * m * 2 + d * 4),               # q,k in; phi q,k, y0 out
+        "ts_b200_feature_bwd": H * (2 * d * 2 + 2 * m * 2 + d * 2 + 2 * d * 2),   # q,k, dphi q,k, dy in; dq,dk out
+        "ts_b200_scan_fwd": H * (2 * m * 2 + d * 2 + R * (d + 1) * 4),            # phi q,k, v in; slots out
+        "ts_b200_scan_bwd": H * (2 * m * 2 + d * 2 + R * (d + 1) * 2 + 2 * m * 2 + d * 2),
+        "ts_b200_kread_fwd": H * (R * (d + 1) * 4 + d * 4 + d * 2),
+        "ts_b200_kread_bwd": H * (R * (d + 1) * 4 + d * 2 + R * (d + 1) * 2),
+    }
+
+
+# DRAM bytes (read + write) of one launch measured by ncu, from the summaries
+# under profiles/ (config-2 shapes at batch 2), scaled to a launch of the
+# timed config by its number of token rows (traffic grows with B * T).
+MEASURED_TRAFFIC = {
+    # entry point: (bytes per launch at the profiled size, tokens of that launch, source)
+    "ts_b200_feature_bwd": (189.9e6 + 27.0e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+}
 
 
 # --------------------------------------------------------------------------- CPU reference
@@ -348,13 +377,33 @@ def run_b200(args, cfg):
     core_flops, mixer_flops, phase_flops = flops_per_token(cfg)
     tokens = B * T * world
     value = tokens / (mean_ms / 1e3)
-    peak_sus, peak_burst, peak_kind = load_peaks()
-    # Dominant entry point of ours and its algorithmic FLOPs per launch.
+    peak_sus, peak_burst, peak_hbm, peak_kind = load_peaks()
+    # Dominant entry point of ours: algorithmic FLOPs and compulsory bytes per
+    # launch; its roofline is the one its arithmetic intensity falls under.
     per_token = {"ts_b200_feature_fwd": phase_flops["feature"], "ts_b200_scan_fwd": phase_flops["scan"],
                  "ts_b200_scan_bwd": 2 * phase_flops["scan"], "ts_b200_feature_bwd": 2 * phase_flops["feature"],
                  "ts_b200_kread_fwd": 0, "ts_b200_kread_bwd": 0}
     dominant = max(phase_ms, key=phase_ms.get)
-    achieved = per_token[dominant] * B * T / (phase_ms[dominant] / 1e3) / 1e12
+    launch_s = phase_ms[dominant] / 1e3
+    flops_launch = per_token[dominant] * B * T
+    bytes_launch = bytes_per_token(cfg)[dominant] * B * T
+    ridge = peak_sus * 1e12 / (peak_hbm * 1e9)
+    traffic = None
+    if dominant in MEASURED_TRAFFIC and args.config in ("c2", "c2b2"):
+        tb, ttok, _ = MEASURED_TRAFFIC[dominant]
+        traffic = tb * (B * T) / ttok
+    if flops_launch / max(bytes_launch, 1) < ridge:
+        achieved = bytes_launch / launch_s / 1e9
+        roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
+                    "frac": achieved / peak_hbm, "traffic": traffic, "bytes_per_launch": bytes_launch,
+                    "flops_per_launch": flops_launch, "tflops": flops_launch / launch_s / 1e12,
+                    "peak_source": f"{peak_kind} hbm_gbs"}
+    else:
+        achieved = flops_launch / launch_s / 1e12
+        roofline = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_sus,
+                    "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": traffic,
+                    "bytes_per_launch": bytes_launch, "flops_per_launch": flops_launch,
+                    "peak_source": f"{peak_kind} bf16_tflops_sustained"}
     mixer_tflops = mixer_flops * value / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -365,9 +414,7 @@ def run_b200(args, cfg):
                    "model": "ThetaScan-Kernel mixer", "global_batch": B * world, "seq_len": T,
                    "d_model": cfg["D"], "heads": cfg["H"], "parallelism": f"dp{world}" if world > 1 else "single",
                    "l2": "256 MB buffer written before every timed step"},
-        "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_sus,
-                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": None,
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained"},
+        "roofline": roofline,
         "mixer_roofline": {"achieved": mixer_tflops, "peak": peak_sus, "unit": "TFLOP/s",
                            "frac": mixer_tflops / peak_sus, "flop_per_token": mixer_flops,
                            "core_flop_per_token": core_flops},
