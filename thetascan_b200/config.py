@@ -182,8 +182,10 @@ class TemporalConfig:
             raise ValueError(f"unknown bank mode: {self.bank_mode!r}")
         if not 0.0 < self.retention_init < 1.0:
             raise ValueError("TemporalConfig.retention_init must be in (0, 1)")
-        if self.recency_branches not in (1, 2):
-            raise ValueError("TemporalConfig.recency_branches must be 1 or 2")
+        # The reference accepts 1 or 2 branches; 3 (explicit initializers only)
+        # is this package's extension for the four-view bank of config 4.
+        if self.recency_branches not in (1, 2, 3):
+            raise ValueError("TemporalConfig.recency_branches must be 1, 2 or 3")
         if self.blend_mode not in ("free", "tanh"):
             raise ValueError("TemporalConfig.blend_mode must be 'free' or 'tanh'")
         if self.retention_inits is not None and self.half_life_inits is not None:
@@ -200,8 +202,8 @@ class TemporalConfig:
             raise ValueError("retention/half-life initializers must contain exactly recency_branches values")
         if any(not 0.0 < x < 1.0 for x in retentions):
             raise ValueError("retentions must be in (0, 1)")
-        if self.recency_branches == 2 and retentions[0] == retentions[1]:
-            raise ValueError("two recency branches require distinct initial timescales")
+        if self.recency_branches >= 2 and len(set(retentions)) != len(retentions):
+            raise ValueError("recency branches require distinct initial timescales")
 
 
 @dataclass

@@ -92,15 +92,17 @@ class Prologue:
     """Row transform fused into the feature kernels: RoPE tables and L2 norm."""
 
     rot: int
-    cos: torch.Tensor | None   # f32 [T, rot/2]
+    cos: torch.Tensor | None   # f32 [pos0 + T, rot/2]
     sin: torch.Tensor | None
     l2norm_eps: float | None   # None: no normalization
+    pos0: int = 0              # sequence position of token 0 (sequence shards)
 
 
 def _set_prologue(fa, prologue):
     if prologue is None:
         return
     fa.rope_rot = prologue.rot
+    fa.rope_pos0 = prologue.pos0
     if prologue.rot:
         fa.rope_cos, fa.rope_sin = prologue.cos.data_ptr(), prologue.sin.data_ptr()
     if prologue.l2norm_eps is not None:
@@ -286,6 +288,172 @@ class _KernelCoreQKV(torch.autograd.Function):
         w1d, w2d = ctx.dtypes
         return (None, None, None, dqkv, g["dW1"].to(w1d), g["dW2"].to(w2d), g["thr"], g["bias"], g["gain"],
                 g["scale"], g["dla"], g["deta"])
+
+
+class _FeatScan(torch.autograd.Function):
+    """Features and scan of the fused-projection path as one autograd stage
+    whose outputs (phi_q, phi_k, y0 and the retention slots) stay visible, so
+    that code between the scan and the read -- the state exchange of sequence
+    shards -- differentiates through them."""
+
+    @staticmethod
+    def forward(ctx, spec, prologue, H, qkv, W1, W2, thr, bias, gain, scale, log_alphas):
+        lib = _lib.load()
+        d = qkv.shape[-1] // (3 * H)
+        q, k, v = _qkv_views(qkv, H, d)
+        B, _, T, _ = q.shape
+        ctl = _controls(thr, bias, gain, scale)
+        W1b = W1.detach().to(torch.bfloat16).contiguous()
+        W2b = W2.detach().to(torch.bfloat16).contiguous()
+        m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
+        dev = q.device
+        phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
+        phi_q = torch.empty_like(phi_k)
+        y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
+        _set_prologue(fa, prologue)
+        _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
+        las = [None] + ([] if log_alphas is None else
+                        [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
+        slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
+        sa = _build_args(phi_q, phi_k, v, las, slots, True)
+        ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
+        sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
+        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
+        ctx.spec, ctx.prologue, ctx.H, ctx.ctl = spec, prologue, H, ctl
+        ctx.st = dict(W1b=W1b, W2b=W2b, phi_q=phi_q, phi_k=phi_k, ws=ws, slots=slots, las=las)
+        ctx.dtypes = (W1.dtype, W2.dtype)
+        ctx.save_for_backward(qkv)
+        return (phi_q, phi_k, y0, *slots)
+
+    @staticmethod
+    def backward(ctx, dphi_q_out, dphi_k_out, dy0, *dslots):
+        lib = _lib.load()
+        (qkv,) = ctx.saved_tensors
+        H, st, spec = ctx.H, ctx.st, ctx.spec
+        d = qkv.shape[-1] // (3 * H)
+        q, k, v = _qkv_views(qkv, H, d)
+        B, _, T, _ = q.shape
+        dev = q.device
+        slots, las = st["slots"], st["las"]
+        n = len(slots)
+        dqkv = torch.empty_like(qkv)
+        dq, dk, dv = _qkv_views(dqkv, H, d)
+        # scan
+        douts = [torch.zeros(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) if g is None
+                 else g.to(torch.bfloat16).contiguous() for g in dslots]
+        sa = _build_args(st["phi_q"], st["phi_k"], v, las, slots, True, st["ws"])
+        sg = _lib.ScanGradArgs()
+        m = st["phi_q"].shape[-1]
+        dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
+        dphi_k = torch.empty_like(dphi_q)
+        sg.dv = dv.data_ptr()
+        sg.dv_strides = _lib.c_int64_3(*dv.stride()[:3])
+        dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
+        for i in range(n):
+            sg.dout[i] = douts[i].data_ptr()
+            sg.dlog_alpha[i] = _ptr(dlas[i])
+        sg.dq, sg.dk = dphi_q.data_ptr(), dphi_k.data_ptr()
+        sg.grad_dtype = _lib.TS_DTYPE_BF16
+        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+        sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
+        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
+        del gws
+        # gradients that reached phi directly (not through the scan)
+        if dphi_q_out is not None:
+            dphi_q = (dphi_q.float() + dphi_q_out.float()).to(torch.bfloat16)
+        if dphi_k_out is not None:
+            dphi_k = (dphi_k.float() + dphi_k_out.float()).to(torch.bfloat16)
+        # features
+        fa = _feature_args(spec, q, k, st["W1b"], st["W2b"], ctx.ctl, st["phi_k"], st["phi_q"], None)
+        _set_prologue(fa, ctx.prologue)
+        fg = _lib.FeatureGradArgs()
+        fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
+        if dy0 is None:
+            dy0 = torch.zeros(B, H, T, d, dtype=torch.float32, device=dev)
+        dy0 = dy0.float().contiguous()
+        fg.dy0 = dy0.data_ptr()
+        fg.dk_bf16, fg.dq_bf16 = dk.data_ptr(), dq.data_ptr()
+        fg.dk_strides = _lib.c_int64_3(*dk.stride()[:3])
+        fg.dq_strides = _lib.c_int64_3(*dq.stride()[:3])
+        W1b, W2b, ctl = st["W1b"], st["W2b"], ctx.ctl
+        dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
+        dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+        grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
+                 for key in ("thr", "bias", "gain", "scale")}
+        fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+        fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
+        fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
+        _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+        w1d, w2d = ctx.dtypes
+        dla = None if n == 1 else torch.stack(dlas[1:])
+        return (None, None, None, dqkv, dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"], grads["gain"],
+                grads["scale"], dla)
+
+
+class _KRead(torch.autograd.Function):
+    """Key-mass read and bank blend as one autograd stage: y0 and the slots
+    in, token-major y out."""
+
+    @staticmethod
+    def forward(ctx, spec, y0, etas, *slots):
+        lib = _lib.load()
+        B, H, T, d = y0.shape
+        eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
+        slots = [s.contiguous() for s in slots]
+        y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=y0.device)
+        ra = _kread_args(spec, slots, eta, y0.contiguous(), y)
+        _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
+        ctx.spec, ctx.eta, ctx.has_eta = spec, eta, etas is not None
+        ctx.save_for_backward(y0, *slots)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _lib.load()
+        y0, *slots = ctx.saved_tensors
+        B, H, T, d = y0.shape
+        dev = y0.device
+        dy = dy.contiguous()
+        if dy.dtype not in (torch.bfloat16, torch.float32):
+            dy = dy.float()
+        ra = _kread_args(ctx.spec, list(slots), ctx.eta, y0.contiguous(), None)
+        ga = _lib.KReadGradArgs()
+        ga.dy = dy.data_ptr()
+        ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
+        dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
+        for i, s in enumerate(dslots):
+            ga.dslots[i] = s.data_ptr()
+        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        ga.dy0 = dy0.data_ptr()
+        n = len(slots)
+        deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
+        ga.deta = _ptr(deta)
+        _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
+        return (None, dy0, deta if ctx.has_eta else None, *dslots)
+
+
+def kernel_core_staged(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,
+                       score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None,
+                       between=None):
+    """The hot path of :func:`kernel_core_qkv` as two autograd stages with a
+    hook between them: ``between(phi_q, phi_k, v, slots) -> slots`` may add to
+    the retention slots (the entering-state terms of a sequence shard) with
+    differentiable torch code.  Without a hook it equals ``kernel_core_qkv``."""
+    if not qkv.is_cuda:
+        raise RuntimeError("b200 backend requires CUDA tensors")
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 3 or not qkv.is_contiguous():
+        raise ValueError("kernel_core_staged: qkv must be a contiguous bf16 [B,T,3*H*d] tensor")
+    if (log_alphas is None) != (spec.mode == "sum"):
+        raise ValueError("kernel_core_staged: log_alphas are required exactly for a bank (mode fast/stale)")
+    if spec.mode == "stale":
+        raise NotImplementedError("b200 backend: the stale bank is not built yet (fast banks are supported)")
+    out = _FeatScan.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas)
+    phi_q, phi_k, y0, slots = out[0], out[1], out[2], list(out[3:])
+    if between is not None:
+        d = qkv.shape[-1] // (3 * H)
+        slots = list(between(phi_q, phi_k, _qkv_views(qkv, H, d)[2], slots))
+    return _KRead.apply(spec, y0, etas, *slots)
 
 
 def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,

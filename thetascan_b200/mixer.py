@@ -27,7 +27,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .config import ThetaScanConfig
-from .kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv
+from .kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv, kernel_core_staged
 
 EXPANSION_DOMAIN = "thetascan-expansion-v1"
 FINGERPRINT_MAGIC = b"TSXF"
@@ -267,7 +267,10 @@ class ThetaScanCore(nn.Module):
         x = _rope(x.float(), self._rot, self.cfg.rope.base)
         return (x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)).to(torch.bfloat16).contiguous()
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, shard=None) -> torch.Tensor:
+        """``x [B,T,D]``; with ``shard`` (a :class:`thetascan_b200.seqpar.SeqShard`)
+        ``x`` is this rank's contiguous T-slice of longer sequences, and the
+        chunk states of the earlier slices arrive through one exchange."""
         if not x.is_cuda:
             raise RuntimeError("thetascan_b200 requires a CUDA input")
         B, T, _ = x.shape
@@ -276,7 +279,20 @@ class ThetaScanCore(nn.Module):
         xb = x.to(torch.bfloat16)
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
-        if self.proj_qkv is not None and self.vmlp_in is None:
+        if shard is not None:
+            if self.proj_qkv is None or self.vmlp_in is not None:
+                raise NotImplementedError("sequence shards need the fused q/k/v projection without a value MLP")
+            from .seqpar import exchange
+            qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
+            pos0 = shard.rank * T
+            cos = sin = None
+            if self._rot:
+                cos, sin = _rope_tables(pos0 + T, self._rot, float(self.cfg.rope.base), str(x.device))
+            prologue = Prologue(self._rot, cos, sin, 1e-6, pos0)
+            las = [None] + ([] if log_alphas is None else [log_alphas[j] for j in range(log_alphas.shape[0])])
+            y = kernel_core_staged(qkv, H, W1, W2, self.spec, prologue, log_alphas=log_alphas, etas=etas,
+                                   between=exchange(shard, las), **self.kernel_controls())
+        elif self.proj_qkv is not None and self.vmlp_in is None:
             # Fused projection layout: RoPE and the L2 norm run inside the
             # feature kernels, v is read from the projection in place.
             qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
@@ -316,8 +332,8 @@ class ThetaScan(nn.Module):
                 if p is not None:
                     p.requires_grad_(False)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self._core(x)
+    def forward(self, x: torch.Tensor, shard=None) -> torch.Tensor:
+        return self._core(x, shard)
 
     def zero_output_projection_(self) -> "ThetaScan":
         nn.init.zeros_(self._core.proj_out.weight)
