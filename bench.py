@@ -10,7 +10,10 @@ on synthetic x ~ N(0,1) with loss = mean(y^2).
 With --gpus N (torchrun, one rank per GPU) every rank runs its own batch of
 the same shape (weak scaling: independent (batch, head) units) and the ranks
 all-reduce the mixer's parameter gradients over NCCL, as a data-parallel
-step does.  ``--impl reference`` times the reference's CPU implementation
+step does.  ``--config c4`` (config 4: T = 32768, B-spline features, four
+views) instead splits the sequences into N contiguous shards, one per rank,
+that exchange their chunk states with one NCCL all-gather per step (strong
+scaling: the B x T tokens are fixed).  ``--impl reference`` times the reference's CPU implementation
 (the float32 oracle restatement of its chunk backend) on the host cores.
 
 One JSON line is printed by rank 0.
@@ -41,6 +44,19 @@ CONFIGS = {
     "small": dict(B=2, T=1024, D=512, H=8, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
     # config-2 shapes at batch 2: inputs still larger than L2, for profiler captures
     "c2b2": dict(B=2, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+    # config 4: B-spline features (16 basis functions, m = 2d = 128, P = 8
+    # projections), bank of three recency branches 0.9 / 0.99 / 0.999 plus the
+    # sum view; with --gpus N the 32K-token sequences are split into N shards.
+    "c4": dict(B=4, T=32768, D=1024, H=16, mult=2, expansion=1, fmap="projected_bspline", basis=16,
+               rope="partial", J=3, retentions=(0.9, 0.99, 0.999), seqpar=True),
+}
+
+WORKLOADS = {
+    "c2": "config 2: ThetaScan-Kernel relu2 ridge m=256 (2x expansion), partial RoPE, 1-branch fast bank, "
+          "output gate; fwd+bwd, loss=mean(y^2)",
+    "c4": "config 4: ThetaScan-Kernel projected B-spline (16 basis, m=128), partial RoPE, fast bank "
+          "0.9/0.99/0.999 + sum (4 views), output gate, T=32768; sequence-sharded over the GPUs; "
+          "fwd+bwd, loss=mean(y^2)",
 }
 
 
@@ -49,15 +65,21 @@ CONFIGS = {
 def build_module(cfg, device):
     from thetascan_b200.config import KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
     from thetascan_b200.mixer import ThetaScan
+    kernel = KernelConfig(feature_map=cfg["fmap"], bspline_basis_count=cfg.get("basis", 8))
+    if cfg["J"] == 1:
+        temporal = TemporalConfig(mode="bank", retention_init=0.95)
+    else:
+        temporal = TemporalConfig(mode="bank", recency_branches=cfg["J"], retention_inits=cfg["retentions"])
     config = ThetaScanConfig(
         d_model=cfg["D"], n_heads=cfg["H"], memory_multiplier=cfg["mult"], feature_expansion=cfg["expansion"],
-        family="kernel", kernel=KernelConfig(feature_map=cfg["fmap"]),
-        rope=RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=TemporalConfig(mode="bank", retention_init=0.95))
+        family="kernel", kernel=kernel, rope=RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=temporal)
     torch.manual_seed(0)
     module = ThetaScan(config)
-    with torch.no_grad():
-        alphas = 0.9 + 0.099 * torch.rand(cfg["H"], generator=torch.Generator().manual_seed(0))
-        module._core.fade_alpha.copy_(torch.log(alphas / (1.0 - alphas)))
+    if cfg["J"] == 1:
+        # per-head retentions alpha_h ~ U(0.9, 0.999), as the config-2 statement has them
+        with torch.no_grad():
+            alphas = 0.9 + 0.099 * torch.rand(cfg["H"], generator=torch.Generator().manual_seed(0))
+            module._core.fade_alpha.copy_(torch.log(alphas / (1.0 - alphas)))
     return module.to(device), config
 
 
@@ -69,7 +91,8 @@ def flops_per_token(cfg):
     forward FLOPs per token)."""
     H, d = cfg["H"], cfg["D"] // cfg["H"]
     m = cfg["mult"] * d
-    P, C, V = m, 64, 1 + cfg["J"]
+    P = m // cfg["basis"] if cfg["fmap"] == "projected_bspline" else m
+    C, V = 64, 1 + cfg["J"]
     feature = 4 * P * d + 2 * d * m
     scan = C * m + V * (C * (d + 1) + 4 * m * (d + 1))
     D, Hd = cfg["D"], H * d
@@ -290,16 +313,30 @@ def run_b200(args, cfg):
 
     module, config = build_module(cfg, device)
     params = [p for p in module.parameters() if p.requires_grad]
+    seqpar = bool(cfg.get("seqpar")) and world > 1
     B, T = cfg["B"], cfg["T"]
-    gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
-    x_host = torch.randn(B, T, cfg["D"], generator=gen).to(torch.bfloat16).pin_memory()
+    shard = None
+    if seqpar:
+        # every rank holds a contiguous T / world slice of the same sequences
+        from thetascan_b200.seqpar import nccl_shard
+        if T % world:
+            raise SystemExit(f"T={T} does not split into {world} shards")
+        shard = nccl_shard()
+        gen = torch.Generator(device="cpu").manual_seed(1000)
+        L = T // world
+        x_host = torch.randn(B, T, cfg["D"], generator=gen)[:, rank * L:(rank + 1) * L]
+        x_host = x_host.to(torch.bfloat16).contiguous().pin_memory()
+        T = L
+    else:
+        gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
+        x_host = torch.randn(B, T, cfg["D"], generator=gen).to(torch.bfloat16).pin_memory()
     x = x_host.to(device)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def step(inp):
         for p in params:
             p.grad = None
-        y = module(inp)
+        y = module(inp, shard)
         loss = y.float().square().mean()
         loss.backward()
         if world > 1:
@@ -407,12 +444,14 @@ def run_b200(args, cfg):
     mixer_tflops = mixer_flops * value / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True,
+        "scaling": "strong" if seqpar else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic x ~ N(0,1), seeded random-init weights",
-        "config": {"workload": "config 2: ThetaScan-Kernel relu2 ridge m=256 (2x expansion), partial RoPE, "
-                               "1-branch fast bank, output gate; fwd+bwd, loss=mean(y^2)",
-                   "model": "ThetaScan-Kernel mixer", "global_batch": B * world, "seq_len": T,
-                   "d_model": cfg["D"], "heads": cfg["H"], "parallelism": f"dp{world}" if world > 1 else "single",
+        "config": {"workload": WORKLOADS.get(args.config, f"{args.config}: {cfg}"),
+                   "model": "ThetaScan-Kernel mixer", "global_batch": B if seqpar else B * world,
+                   "seq_len": T * world if seqpar else T,
+                   "d_model": cfg["D"], "heads": cfg["H"],
+                   "parallelism": f"sp{world}" if seqpar else (f"dp{world}" if world > 1 else "single"),
                    "l2": "256 MB buffer written before every timed step"},
         "roofline": roofline,
         "mixer_roofline": {"achieved": mixer_tflops, "peak": peak_sus, "unit": "TFLOP/s",
@@ -426,7 +465,7 @@ def run_b200(args, cfg):
         "wall_s": wall,
         "device_status": status,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c2":
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
         T_cpu = args.ref_tokens

@@ -78,72 +78,79 @@ __device__ __forceinline__ float ctl_scale(const FeatParams& p, int h) {
   return p.scale ? __ldg(p.scale + h) : p.scale_scalar;
 }
 
-// Cubic (degree-3) open-uniform B-spline basis at x with its derivative,
-// by the Cox--de Boor recursion on knots [-b]*4, uniform interior, [b]*4
+// Cubic (degree-3) open-uniform B-spline basis at x with its derivative, by
+// the Cox--de Boor recursion on knots [-b]*4, uniform interior, [b]*4
 // (reference kernel_features.py:138-205: half-open spans, zero-width spans
 // dropped, clamp to [-b, nextafter(b, -b)], negatives clamped, renormalised).
+// At a coordinate in knot span j (knot[j] <= x < knot[j+1]) only the degree-3
+// functions j-3 .. j can be nonzero, so the recursion runs on that window of
+// four; every term it skips is an exact zero, which leaves the values, the
+// derivatives and the normalising sums what the recursion over all functions
+// gives.  Writes val/der of functions first .. first+3 (first = j - 3);
 // `inside` is false when the coordinate was clamped (zero derivative).
-__device__ __forceinline__ void bspline_eval(float c, int nb, float bound, float* val, float* der, bool& inside) {
+__device__ __forceinline__ float bspline_knot(int i, int nb, float bound, float step) {
+  return i <= 3 ? -bound : (i >= nb ? bound : -bound + static_cast<float>(i - 3) * step);
+}
+__device__ __forceinline__ void bspline_local(float c, int nb, float bound, float* val, float* der, int& first,
+                                              bool& inside) {
   const float hi = nextafterf(bound, -bound);
   inside = (c >= -bound) && (c <= bound);
   float x = fminf(fmaxf(c, -bound), bound);
-  if (x > hi) {
-    x = hi;
-  }
-  float knot[kMaxBasis + 4];
+  if (x > hi) x = hi;
   const float step = 2.f * bound / static_cast<float>(nb - 3);
-#pragma unroll
-  for (int i = 0; i < kMaxBasis + 4; ++i) {
-    float kv;
-    if (i <= 3) kv = -bound;
-    else if (i >= nb) kv = bound;
-    else kv = -bound + static_cast<float>(i - 3) * step;
-    knot[i] = kv;
-  }
-  float B[kMaxBasis + 3], D[kMaxBasis + 3];
-#pragma unroll
-  for (int i = 0; i < kMaxBasis + 3; ++i) {
-    B[i] = (i < nb + 3 && x >= knot[i] && x < knot[i + 1]) ? 1.f : 0.f;
-    D[i] = 0.f;
-  }
+  int j = 3 + static_cast<int>(floorf((x + bound) / step));
+  j = min(max(j, 3), nb - 1);
+  while (j > 3 && x < bspline_knot(j, nb, bound, step)) --j;
+  while (j < nb - 1 && x >= bspline_knot(j + 1, nb, bound, step)) ++j;
+  float B[4] = {0.f, 0.f, 0.f, 1.f}, D[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int o = 1; o <= 3; ++o) {
 #pragma unroll
-    for (int i = 0; i < kMaxBasis + 3 - o; ++i) {
-      if (i >= nb + 3 - o) continue;
-      const float dl = knot[i + o] - knot[i];
-      const float dr = knot[i + o + 1] - knot[i + 1];
-      const float L = dl > 0.f ? (x - knot[i]) / dl : 0.f;
-      const float R = dr > 0.f ? (knot[i + o + 1] - x) / dr : 0.f;
+    for (int s = 3 - o; s < 4; ++s) {
+      const int i = j - 3 + s;
+      const float ki = bspline_knot(i, nb, bound, step), ki1 = bspline_knot(i + 1, nb, bound, step);
+      const float kio = bspline_knot(i + o, nb, bound, step), kio1 = bspline_knot(i + o + 1, nb, bound, step);
+      const float dl = kio - ki;
+      const float dr = kio1 - ki1;
+      const float L = dl > 0.f ? (x - ki) / dl : 0.f;
+      const float R = dr > 0.f ? (kio1 - x) / dr : 0.f;
       const float dL = dl > 0.f ? 1.f / dl : 0.f;
       const float dR = dr > 0.f ? -1.f / dr : 0.f;
-      const float nb_ = L * B[i] + R * B[i + 1];
-      const float nd_ = dL * B[i] + L * D[i] + dR * B[i + 1] + R * D[i + 1];
-      B[i] = nb_;
-      D[i] = nd_;
+      const float b1 = s < 3 ? B[s + 1] : 0.f, d1 = s < 3 ? D[s + 1] : 0.f;
+      const float nb_ = L * B[s] + R * b1;
+      const float nd_ = dL * B[s] + L * D[s] + dR * b1 + R * d1;
+      B[s] = nb_;
+      D[s] = nd_;
     }
   }
   float S = 0.f, dS = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxBasis; ++i) {
-    if (i < nb) {
-      if (B[i] < 0.f) {
-        B[i] = 0.f;
-        D[i] = 0.f;
-      }
-      S += B[i];
-      dS += D[i];
+  for (int s = 0; s < 4; ++s) {
+    if (B[s] < 0.f) {
+      B[s] = 0.f;
+      D[s] = 0.f;
     }
+    S += B[s];
+    dS += D[s];
   }
   S = fmaxf(S, 1.17549435e-38f);
 #pragma unroll
-  for (int i = 0; i < kMaxBasis; ++i) {
-    if (i < nb) {
-      val[i] = B[i] / S;
-      der[i] = (D[i] * S - B[i] * dS) / (S * S);
-    }
+  for (int s = 0; s < 4; ++s) {
+    val[s] = B[s] / S;
+    der[s] = (D[s] * S - B[s] * dS) / (S * S);
   }
+  first = j - 3;
 }
+
+// Element idx (0..3) of a 4-vector by value selects (no local memory).
+__device__ __forceinline__ float pick4(const float* v, int idx) {
+  return idx == 0 ? v[0] : idx == 1 ? v[1] : idx == 2 ? v[2] : v[3];
+}
+
+// B-spline projections are dealt out to the kParts threads of a row: thread
+// part takes projections part, part + kParts, ... (P <= 32, two 16-column
+// chunks of the projection accumulator at most).
+constexpr int kMaxSplineOwn = 32 / kParts;
 
 // ------------------------------------------------------------------ shared tile setup
 
@@ -496,19 +503,27 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
   if constexpr (KIND == kBspline) {
     const float sc = ctl_scale(p, h);
     const float invP = 1.f / static_cast<float>(p.P);
-    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 16 * cc;
+      if (c >= p.PP) break;
       float a[16];
       tmem_ld16(ta_row + c, a);
+#pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int pj = c + e;
-        if (pj >= p.P) break;
-        float val[kMaxBasis], der[kMaxBasis];
+        if ((e % kParts) != part || pj >= p.P) continue;
+        float val[4], der[4];
+        int first;
         bool inside;
-        bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
+        bspline_local(a[e] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
         for (int i = 0; i < p.nb; i += 8) {
           float f[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) f[q] = (!zero_row && i + q < p.nb) ? val[i + q] * invP : 0.f;
+          for (int q = 0; q < 8; ++q) {
+            const int w = i + q - first;
+            f[q] = (!zero_row && w >= 0 && w < 4) ? pick4(val, w) * invP : 0.f;
+          }
           tile_st16(tphi, row, (pj * p.nb + i) / 8, pack8(f));
         }
       }
@@ -641,8 +656,9 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       load_tile_any(tl.dy, p.dy + rowbase * p.d, p.d, rows, p.d, false);
     }
   }
-  if (!spline)
-    for (int j = p.PP / 8 + part; j < p.PM / 8; j += kParts) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
+  // dA columns no sweep writes must be zero (the dW1 product reads PM of them).
+  for (int j = (spline ? 0 : p.PP / 8) + part; j < p.PM / 8; j += kParts)
+    tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   tiles_ready();
   if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
   MmaCtx ctx{&bar, tmem_base, 0u, true};
@@ -705,78 +721,106 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
         dp[e] = d;
       }
     } else {
-      const float sc = ctl_scale(p, h);
-      const float invP = 1.f / static_cast<float>(p.P);
-#pragma unroll 1
-      for (int e = 0; e < 16; ++e) {
-        const int pj = c + e;
-        float d = 0.f;
-        if (pj < p.P) {
-          float val[kMaxBasis], der[kMaxBasis];
-          bool inside;
-          bspline_eval(a[e] * st.inv * sc, p.nb, p.bound, val, der, inside);
-          float dc = 0.f;
-          for (int i0 = 0; i0 < p.nb; i0 += 16) {
-            const int col = pj * p.nb + i0;   // multiple of 8
-            float g[16];
-            const int cbase = col & ~15;
-            grad16(cbase, g);
-            const int off = col - cbase;
-            for (int i = 0; i < 16 - off && i0 + i < p.nb; ++i) dc += g[off + i] * der[i0 + i] * invP;
-            if (off && i0 + 16 - off < p.nb) {
-              float g2[16];
-              grad16(cbase + 16, g2);
-              for (int i = 16 - off; i0 + i < p.nb && i < 16; ++i) dc += g2[i - (16 - off)] * der[i0 + i] * invP;
-            }
-          }
-          d = inside ? dc * sc : 0.f;
-        }
-        dp[e] = d;
-      }
+      // B-splines run their own sweep (below).
+#pragma unroll
+      for (int e = 0; e < 16; ++e) dp[e] = 0.f;
     }
   };
 
-  // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
   float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
-  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-    float a[16], dp[16];
-    tmem_ld16(ta_row + c, a);
-    dpre_chunk(c, a, dp);
+  if constexpr (spline) {
+    // B-splines: this thread's projections pj = kParts * i + part.  dpre of a
+    // projection is sc * sum over the four live basis functions of
+    // g(pj, basis) * basis' / P (zero where the coordinate was clamped).
+    const float sc = ctl_scale(p, h);
+    const float invP = 1.f / static_cast<float>(p.P);
+    float a_own[kMaxSplineOwn], dp_own[kMaxSplineOwn];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      dot_a += dp[e] * a[e];
-      if (KIND == kRelu2) dthr -= dp[e];
-      if (KIND == kSoftmax && c + e < p.P) {
-        const float gain = ctl_gain(p, h, c + e);
-        const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
-        if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
-        if (p.gain_mode == 2 && valid) atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / gain);
+    for (int i = 0; i < kMaxSplineOwn; ++i) a_own[i] = dp_own[i] = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 16 * cc;
+      if (c >= p.PP) break;
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if ((e % kParts) == part) a_own[(c + e) / kParts] = a[e];
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxSplineOwn; ++i) {
+      const int pj = kParts * i + part;
+      if (pj >= p.P) break;
+      float val[4], der[4];
+      int first;
+      bool inside;
+      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
+      float g[16];
+      grad16(pj * p.nb, g);   // basis functions 0..15 of projection pj (nb <= 16)
+      float dc = 0.f;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int w = q - first;
+        if (w >= 0 && w < 4) dc += g[q] * pick4(der, w) * invP;
       }
-      if (spline && c + e < p.P) dscale += dp[e] * a[e] * st.inv / ctl_scale(p, h);
-      if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P)
-        atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
+      const float d = inside ? dc * sc : 0.f;
+      dp_own[i] = d;
+      dot_a += d * a_own[i];
+      dscale += d * a_own[i] * st.inv / sc;
+    }
+    dot_a = row_pair_sum(dot_a, pair);
+    if (!valid) dot_a = dscale = 0.f;
+    if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
+#pragma unroll
+    for (int i = 0; i < kMaxSplineOwn; ++i) {
+      const int pj = kParts * i + part;
+      if (pj >= p.P) break;
+      const float da = valid ? st.inv * dp_own[i] - a_own[i] * inv3 * dot_a : 0.f;
+      const __nv_bfloat16 v = __float2bfloat16_rn(da);
+      asm volatile("st.shared.u16 [%0], %1;" ::"r"(tl.da.saddr + tile_off(tl.da, row, pj)),
+                   "h"(__bfloat16_as_ushort(v))
+                   : "memory");
+    }
+  } else {
+    // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16], dp[16];
+      tmem_ld16(ta_row + c, a);
+      dpre_chunk(c, a, dp);
+  #pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        dot_a += dp[e] * a[e];
+        if (KIND == kRelu2) dthr -= dp[e];
+        if (KIND == kSoftmax && c + e < p.P) {
+          const float gain = ctl_gain(p, h, c + e);
+          const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
+          if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
+          if (p.gain_mode == 2 && valid) atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / gain);
+        }
+        if (spline && c + e < p.P) dscale += dp[e] * a[e] * st.inv / ctl_scale(p, h);
+        if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P)
+          atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
+      }
+    }
+    dot_a = row_pair_sum(dot_a, pair);
+    if (!valid) {
+      dot_a = 0.f;
+      dthr = dscale = dgain_head = 0.f;
+    }
+    // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
+    if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16], dp[16], da[16];
+      tmem_ld16(ta_row + c, a);
+      dpre_chunk(c, a, dp);
+  #pragma unroll
+      for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
+      tile_st16(tl.da, row, c / 8, pack8(da));
+      tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
     }
   }
-  dot_a = row_pair_sum(dot_a, pair);
-  if (!valid) {
-    dot_a = 0.f;
-    dthr = dscale = dgain_head = 0.f;
-  }
-  // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
-  if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
-  const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
-  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-    float a[16], dp[16], da[16];
-    tmem_ld16(ta_row + c, a);
-    dpre_chunk(c, a, dp);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
-    if (spline) __syncwarp();
-    tile_st16(tl.da, row, c / 8, pack8(da));
-    tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
-  }
-  if (spline)
-    for (int j = p.PP / 8 + part; j < p.PM / 8; j += kParts) tile_st16(tl.da, row, j, make_uint4(0, 0, 0, 0));
   {
     const float s1 = block_sum(dthr, red);
     const float s2 = block_sum(dscale, red);
