@@ -96,6 +96,22 @@ typedef struct ts_scan_args {
    * reads, so keep it unchanged between the two calls. */
   void* workspace;
   size_t workspace_bytes;
+  /* Optional boundary states of a sequence shard, f32 [B,H,R,dk,dv]
+   * (feature-major, payload column fastest; R = n_retentions):
+   *   init_state  the state entering token 0 (NULL = zero state);
+   *   final_state receives the state after the last token (NULL = not written).
+   * `stage` splits the forward around an exchange of shard states:
+   *   0  whole forward (init_state used, final_state written if given);
+   *   1  tile states of every tile and final_state from a ZERO initial state,
+   *      no outputs (final_state required);
+   *   2  the rest of the forward from init_state: carried states and the
+   *      outputs, reusing the tile states that stage 1 left in the workspace
+   *      (same workspace, same inputs).
+   * Sequence parallelism: stage 1 on every shard, exchange the final states,
+   * compose each shard's entering state, stage 2 on every shard. */
+  const float* init_state;
+  float* final_state;
+  int stage;
 } ts_scan_args;
 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args);
@@ -124,6 +140,20 @@ typedef struct ts_scan_grad_args {
    * the payload gradient (the unit column's gradient is not written), for
    * instance the v slot of the gradient of a fused qkv projection. */
   int64_t dv_strides[3];
+  /* Boundary gradients of a sequence shard (f32 [B,H,R,dk,dv]), and the
+   * backward split around their exchange:
+   *   dfinal_state gradient of the forward's final_state (NULL = zero);
+   *   dinit_state  receives the gradient of init_state (NULL = not written);
+   *   stage 0  whole backward;
+   *        1  local tile terms of every tile and dinit_state of the shard's own
+   *           outputs (dinit_state required; nothing else is written except the
+   *           log-retention terms of this stage);
+   *        2  the rest from dfinal_state, the gradient of stage 1's final
+   *           state (the zero-start total): dq, dk, dv and the remaining
+   *           log-retention terms (same workspaces as stage 1). */
+  const float* dfinal_state;
+  float* dinit_state;
+  int stage;
 } ts_scan_grad_args;
 
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* fwd);

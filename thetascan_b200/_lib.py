@@ -33,6 +33,7 @@ class ScanArgs(ctypes.Structure):
         ("out", c_ptr4),
         ("out_dtype", ctypes.c_int),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("init_state", ctypes.c_void_p), ("final_state", ctypes.c_void_p), ("stage", ctypes.c_int),
     ]
 
 
@@ -44,6 +45,7 @@ class ScanGradArgs(ctypes.Structure):
         ("dlog_alpha", c_ptr4),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("dv_strides", c_int64_3),
+        ("dfinal_state", ctypes.c_void_p), ("dinit_state", ctypes.c_void_p), ("stage", ctypes.c_int),
     ]
 
 

@@ -29,8 +29,8 @@ int check_launch(const char* what) {
   return TS_OK;
 }
 
-int launch_scan_fwd(const ScanParams& p, cudaStream_t s);
-int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s);
+int launch_scan_fwd(const ScanParams& p, cudaStream_t s, bool tile_states, bool outputs);
+int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s, bool tile_terms, bool grads);
 size_t scan_state_smem(const ScanParams& p);
 size_t scan_out_smem(const ScanParams& p);
 size_t scan_bwd_max_smem(const ScanParams& p);
@@ -84,6 +84,11 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
     if (!a->out[r]) return set_error(TS_ERR_VALUE, "scan: null output pointer for retention %d", r);
   }
   p->out_bf16 = a->out_dtype == TS_DTYPE_BF16;
+  if (a->stage < 0 || a->stage > 2) return set_error(TS_ERR_VALUE, "scan: stage must be 0, 1 or 2");
+  p->init = a->init_state;
+  p->final_state = a->final_state;
+  p->all_tiles = a->final_state != nullptr;
+  p->store = 1;
   const int mblocks = p->DkM / 128;
   if (p->R * mblocks * p->DvP > 512 || 128 + p->R * p->DvP > 512)
     return set_error(TS_ERR_NOT_IMPLEMENTED,
@@ -149,7 +154,16 @@ int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
     return set_error(TS_ERR_VALUE, "scan_fwd: workspace of %zu bytes needed", need);
   p.states = static_cast<float*>(args->workspace);
   p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
-  return launch_scan_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (args->stage == 1) {
+    // tile states of every tile and the final state from a zero initial state
+    if (!p.final_state) return set_error(TS_ERR_VALUE, "scan_fwd: stage 1 needs final_state");
+    p.init = nullptr;
+    p.store = 0;
+    p.all_tiles = 1;
+    return launch_scan_fwd(p, s, true, false);
+  }
+  return launch_scan_fwd(p, s, args->stage == 0, true);
 }
 
 int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts_stream_t stream) {
@@ -162,7 +176,8 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   const size_t need_bwd = 2 * states_bytes(p) + images_bytes(p);
   if (!grad->workspace || grad->workspace_bytes < need_bwd)
     return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need_bwd);
-  if (!grad->dq || !grad->dk || !grad->dv) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
+  if (grad->stage != 1 && (!grad->dq || !grad->dk || !grad->dv))
+    return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
   p.states = static_cast<float*>(args->workspace);
   p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
   ScanGradParams g;
@@ -178,10 +193,25 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   for (int i = 0; i < 3; ++i) g.dvs[i] = grad->dv_strides[i];
   g.dv_strided = (grad->dv_strides[0] | grad->dv_strides[1] | grad->dv_strides[2]) != 0;
   g.grad_bf16 = grad->grad_dtype == TS_DTYPE_BF16;
+  if (grad->stage < 0 || grad->stage > 2) return set_error(TS_ERR_VALUE, "scan_bwd: stage must be 0, 1 or 2");
+  g.dfinal = grad->dfinal_state;
+  g.dinit = grad->dinit_state;
+  g.store = 1;
+  g.all_tiles = (g.dfinal != nullptr || g.dinit != nullptr || p.init != nullptr || grad->stage != 0) ? 1 : 0;
   g.gstates = static_cast<float*>(grad->workspace);
   g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));
   g.pstates = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p) + images_bytes(p));
-  return launch_scan_bwd(p, g, reinterpret_cast<cudaStream_t>(stream));
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (grad->stage == 1) {
+    // local tile terms and the gradient of the initial state from this shard's outputs
+    if (!g.dinit) return set_error(TS_ERR_VALUE, "scan_bwd: stage 1 needs dinit_state");
+    g.dfinal = nullptr;
+    g.store = 0;
+    return launch_scan_bwd(p, g, s, true, false);
+  }
+  // stage 2 continues stage 1, whose final state started from zero
+  g.zero_start_final = grad->stage == 2;
+  return launch_scan_bwd(p, g, s, grad->stage == 0, true);
 }
 
 }  // extern "C"

@@ -49,6 +49,7 @@ extern "C" int ts_b200_scan_fwd_static(const ts_scan_args* args, ts_stream_t str
   using namespace ts;
   ScanParams p;
   if (int e = build_scan_params(args, &p)) return e;
+  if (args->stage != 0) return set_error(TS_ERR_VALUE, "scan_fwd_static: only the whole forward (stage 0)");
   const size_t need = states_bytes(p) + images_bytes(p);
   if (need > static_cast<size_t>(TS_STATIC_SCRATCH_BYTES))
     return set_error(TS_ERR_VALUE,
@@ -62,5 +63,5 @@ extern "C" int ts_b200_scan_fwd_static(const ts_scan_args* args, ts_stream_t str
   // nothing has to be cleared between calls.
   p.states = static_cast<float*>(scratch);
   p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + states_bytes(p));
-  return launch_scan_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+  return launch_scan_fwd(p, reinterpret_cast<cudaStream_t>(stream), true, true);
 }

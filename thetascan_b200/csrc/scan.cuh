@@ -32,6 +32,11 @@ struct ScanParams {
   int out_bf16;
   float* states;             // [B,H,NT,R,DkM,DvP] f32: dS, then S_in in place
   __nv_bfloat16* images;     // [B,H,NT,R] images of S_in (DvP rows x DkP cols)
+  // sequence-shard boundary states, f32 [B,H,R,Dk,Dv] (payload column fastest)
+  const float* init;         // state entering token 0, or null (zero)
+  float* final_state;        // state after the last token (written), or null
+  int all_tiles;             // tile states of every tile, the last one towards the final state
+  int store;                 // the prefix writes S_in and images (0: final state only)
 };
 
 struct ScanGradParams {
@@ -46,6 +51,11 @@ struct ScanGradParams {
   float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place
   float* pstates;            // [B,H,NT,R,DkM,DvP] f32: key-weight derivative of each tile's state
   __nv_bfloat16* gimages;    // [B,H,NT,R] images of G (DvP rows x DkP cols)
+  const float* dfinal;       // gradient of the final state (G of the last tile), or null
+  float* dinit;              // gradient of the initial state (written), or null
+  int all_tiles;             // local terms of every tile (the last one feeds the final state)
+  int store;                 // the reverse prefix writes G, images and its log-retention terms
+  int zero_start_final;      // dfinal is the gradient of the final state from a zero start
 };
 
 __device__ __forceinline__ float head_la(const ScanParams& p, int r, int h) {
@@ -57,6 +67,22 @@ __device__ __forceinline__ size_t state_index(const ScanParams& p, int b, int h,
 }
 
 __device__ __forceinline__ int image_bytes(const ScanParams& p) { return p.DvP * p.DkP * 2; }
+
+// Tokens in tile n (the last tile may be ragged).
+__device__ __forceinline__ int tile_len(const ScanParams& p, int n) { return min(kTile, p.T - n * kTile); }
+
+// Weight of row j of a tile of `len` tokens in the state that leaves it,
+// e^{la (len - 1 - j)} (1 for the plain sum), and 0 past the tile's end.
+__device__ __forceinline__ float key_weight(float la, bool decayed, int len, int j) {
+  if (j >= len) return 0.f;
+  return decayed ? __expf(la * static_cast<float>(len - 1 - j)) : 1.f;
+}
+
+// Index of state element (feature f, payload column c) of the boundary state
+// arrays [B,H,R,Dk,Dv].
+__device__ __forceinline__ size_t boundary_index(const ScanParams& p, int b, int h, int r, int f, int c) {
+  return ((((static_cast<size_t>(b) * p.H + h) * p.R + r) * p.Dk + f) * p.Dv) + c;
+}
 
 // Decay powers exp(la_r k), k = 0..kTile-1, of every retention of head h into
 // shared memory (`tab`: R * kTile floats), so that the intra-tile weight is a

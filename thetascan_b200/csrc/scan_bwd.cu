@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   if (warp == 0) tmem_alloc(&tmem_base, ncols);
   const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
-  if (any_dla && n + 1 < p.NT) {
+  if (any_dla && (n + 1 < p.NT || g.all_tiles)) {
     const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
     const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
     load_tile(tk, kp, p.ks[2], rows, p.Dk);
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
     const bool want = decayed && g.dla[r] != nullptr;
-    if (n >= 1) {
+    if (n >= 1 || g.all_tiles) {
       // dSloc (region d) and, for the gradient, the (i+1)-weighted copy (region x).
       load_scaled_rows(tw, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
                        [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
@@ -174,12 +174,12 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
         if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
       }
     }
-    if (want && n + 1 < p.NT) {
+    if (want && (n + 1 < p.NT || g.all_tiles)) {
       // B'(n): key-weight derivative of the state this tile leaves behind.
       for (int j = part; j < p.DvP / 8; j += kParts) {
         float f[8];
         unpack8(tile_ld16(tv, row, j), f);
-        const float wgt = static_cast<float>(kTile - 1 - row) * __expf(la * static_cast<float>(kTile - 1 - row));
+        const float wgt = row < rows ? static_cast<float>(rows - 1 - row) * key_weight(la, true, rows, row) : 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] *= wgt;
         tile_st16(tw, row, j, pack8(f));
@@ -213,18 +213,43 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
   const PrefixLane l = prefix_lane(p);
   const int r = l.r;
   const float la = head_la(p, r, l.h);
-  const float closing = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
-  const bool want = p.la[r] != nullptr && g.dla[r] != nullptr;
+  const bool decayed = p.la[r] != nullptr;
+  const int len_last = tile_len(p, p.NT - 1);
+  const float closing = decayed ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const float closing_last = decayed ? __expf(la * static_cast<float>(len_last)) : 1.f;
+  // log-retention terms are this stage's only when it stores G
+  const bool want = decayed && g.dla[r] != nullptr && g.store;
   const bool in_image = l.active && l.f8 * 8 < p.DkP;
   const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
   const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
-  const float k128 = static_cast<float>(kTile) * closing;
+  // G(NT-1): the gradient of the final state, or zero.
   float G[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) G[e] = 0.f;
+  for (int e = 0; e < 8; ++e) {
+    const int f = l.f8 * 8 + e;
+    G[e] = (l.active && g.dfinal != nullptr && f < p.Dk && l.c < p.Dv)
+               ? __ldg(g.dfinal + boundary_index(p, l.b, l.h, l.r, f, l.c)) : 0.f;
+  }
   float acc = 0.f;
+  if (want && g.zero_start_final && g.dfinal != nullptr && p.init != nullptr) {
+    // dfinal belongs to the total from a zero start, U, while the closing
+    // terms below see the states carried from init, whose final state is
+    // e^{la T} init + U: remove d/dla(e^{la T}) <dfinal, init>.
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = l.f8 * 8 + e;
+      if (f < p.Dk && l.c < p.Dv) dot += G[e] * __ldg(p.init + boundary_index(p, l.b, l.h, l.r, f, l.c));
+    }
+    acc -= static_cast<float>(p.T) * __expf(la * static_cast<float>(p.T)) * dot;
+  }
+  // Tiles whose leaving state carries gradient: all but the last, and the
+  // last too when the final state has one.
+  const int last_dla = g.dfinal != nullptr ? p.NT : p.NT - 1;
+  const int first_local = g.all_tiles ? 0 : 1;  // dSloc(0) is needed for the initial state only
   constexpr int kB = kPrefixBatch / 2;
-  // Reverse over tiles, a batch of tiles' inputs loaded together.
+  // Reverse over tiles, a batch of tiles' inputs loaded together:
+  // G(n-1) = C_n G(n) + dSloc(n), C_n the closing of tile n.
   for (int n0 = p.NT - 1; n0 >= 0 && l.active; n0 -= kB) {
     float4 ld[kB][2], pw[kB][2];
 #pragma unroll
@@ -233,18 +258,20 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
       ld[k][0] = ld[k][1] = pw[k][0] = pw[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (n < 0) continue;
       const size_t base = state_index(p, l.b, l.h, n, r) * p.DkM * p.DvP + elem;
-      if (n >= 1) {
+      if (n >= first_local) {
         const float4* gp = reinterpret_cast<const float4*>(g.gstates + base);
         ld[k][0] = gp[0];
         ld[k][1] = gp[1];
       }
-      if (want && n + 1 < p.NT) {
-        // pstates + 128 e^{128 la} S_in: the weight of G(n) in d la.
+      if (want && n < last_dla) {
+        // pstates + C'_n S_in: the weight of G(n) in d la (C' = d C / d la).
+        const float kc = n + 1 < p.NT ? static_cast<float>(kTile) * closing
+                                      : static_cast<float>(len_last) * closing_last;
         const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
         const float4* sp = reinterpret_cast<const float4*>(p.states + base);
         const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1 = sp[1];
-        pw[k][0] = make_float4(p0.x + k128 * s0.x, p0.y + k128 * s0.y, p0.z + k128 * s0.z, p0.w + k128 * s0.w);
-        pw[k][1] = make_float4(p1.x + k128 * s1.x, p1.y + k128 * s1.y, p1.z + k128 * s1.z, p1.w + k128 * s1.w);
+        pw[k][0] = make_float4(p0.x + kc * s0.x, p0.y + kc * s0.y, p0.z + kc * s0.z, p0.w + kc * s0.w);
+        pw[k][1] = make_float4(p1.x + kc * s1.x, p1.y + kc * s1.y, p1.z + kc * s1.z, p1.w + kc * s1.w);
       }
     }
 #pragma unroll
@@ -252,13 +279,16 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
       const int n = n0 - k;
       if (n < 0) break;
       const size_t si = state_index(p, l.b, l.h, n, r);
-      float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
-      gp[0] = make_float4(G[0], G[1], G[2], G[3]);
-      gp[1] = make_float4(G[4], G[5], G[6], G[7]);
-      if (in_image) {
-        uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
-        *reinterpret_cast<uint4*>(img) = pack8(G);
+      if (g.store) {
+        float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
+        gp[0] = make_float4(G[0], G[1], G[2], G[3]);
+        gp[1] = make_float4(G[4], G[5], G[6], G[7]);
+        if (in_image) {
+          uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+          *reinterpret_cast<uint4*>(img) = pack8(G);
+        }
       }
+      const float cl = n + 1 < p.NT ? closing : closing_last;
       const float pv[8] = {pw[k][0].x, pw[k][0].y, pw[k][0].z, pw[k][0].w,
                            pw[k][1].x, pw[k][1].y, pw[k][1].z, pw[k][1].w};
       const float lv[8] = {ld[k][0].x, ld[k][0].y, ld[k][0].z, ld[k][0].w,
@@ -266,8 +296,16 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         acc += G[e] * pv[e];
-        G[e] = G[e] * closing + lv[e];
+        G[e] = G[e] * cl + lv[e];
       }
+    }
+  }
+  // After tile 0, G is the gradient of the state entering the sequence.
+  if (g.dinit != nullptr && l.active && l.c < p.Dv) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = l.f8 * 8 + e;
+      if (f < p.Dk) g.dinit[boundary_index(p, l.b, l.h, l.r, f, l.c)] = G[e];
     }
   }
   if (want) {
@@ -314,7 +352,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   Tile td[4];
   for (int i = 0; i < 4; ++i) td[i] = Tile{ts0.saddr + p.DvP * p.DkP * 2 + i * kTile * p.DvP * 2, kTile, p.DvP};
   const bool staged = nbuf >= p.R;
-  const bool cross = kDq ? n > 0 : n + 1 < p.NT;
+  const bool cross = kDq ? (n > 0 || p.init != nullptr) : (n + 1 < p.NT || g.dfinal != nullptr);
   const __nv_bfloat16* images = kDq ? p.images : g.gimages;
   auto image_of = [&](int r) {
     return reinterpret_cast<const uint8_t*>(images) + state_index(p, b, h, n, r) * static_cast<size_t>(image_bytes(p));
@@ -368,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
         }
       } else {
         // rows of u_r o v, u_r(i) = e^{la (127-i)}
-        const float u = decayed ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
+        const float u = key_weight(la, decayed, rows, row);
         for (int j = part; j < p.DvP / 8; j += kParts) {
           float f[8];
           unpack8(tile_ld16(tv, row, j), f);
@@ -430,7 +468,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   const uint32_t t_s = ctx.tmem, t_g = ctx.tmem + kTile, t_dv = ctx.tmem + 2 * kTile;
   ctx.run([&] { gemm_issue(t_s, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
 
-  const bool cross = n + 1 < p.NT;
+  const bool cross = n + 1 < p.NT || g.dfinal != nullptr;
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
@@ -449,7 +487,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     if (cross) {
       load_scaled_rows(tq, kp, p.ks[2], rows, p.Dk, -1, [&](int t) {
-        return decayed ? __expf(la * static_cast<float>(kTile - 1 - t)) : 1.f;
+        return key_weight(la, decayed, rows, t);
       });
       const size_t si = state_index(p, b, h, n, r);
       load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
@@ -515,19 +553,23 @@ size_t scan_bwd_max_smem(const ScanParams& p) {
   return m;
 }
 
-int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s) {
+// The backward kernels; `tile_terms` runs the local per-tile terms, `grads`
+// the dq / dk / dv kernels (the stages of a sequence shard run them apart;
+// the reverse prefix runs in both).
+int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s, bool tile_terms, bool grads) {
   const int nbuf = dqk_buffers(p);
   const size_t s_state = bstate_smem(p), s_dqk = dqk_smem(p, nbuf), s_dv = dv_smem(p);
   cudaFuncSetAttribute(scan_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_state));
   cudaFuncSetAttribute(scan_bwd_dqk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dqk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
-  if (p.NT > 1) {
+  if (tile_terms && (p.NT > 1 || g.all_tiles)) {
     scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
     if (int e = check_launch("scan_bwd_state_kernel")) return e;
   }
   scan_bwd_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p, g);
   if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
+  if (!grads) return 0;
   const dim3 grid(p.NT, p.H, p.B);
   scan_bwd_dqk_kernel<true><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
   if (int e = check_launch("scan_bwd_dq_kernel")) return e;

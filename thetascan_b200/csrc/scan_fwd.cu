@@ -50,8 +50,8 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
 
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
-    // u_r(j) = exp(la (127 - j)): this tile's key weights in the leaving state.
-    const float u = (p.la[r] != nullptr) ? __expf(la * static_cast<float>(kTile - 1 - row)) : 1.f;
+    // u_r(j) = exp(la (len - 1 - j)): this tile's key weights in the leaving state.
+    const float u = key_weight(la, p.la[r] != nullptr, rows, row);
     for (int j = part; j < p.DvP / 8; j += kParts) {
       float f[8];
       unpack8(tile_ld16(tv, row, j), f);
@@ -92,23 +92,32 @@ __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
   const PrefixLane l = prefix_lane(p);
   if (!l.active) return;
   const float la = head_la(p, l.r, l.h);
-  const float closing = (p.la[l.r] != nullptr) ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const bool decayed = p.la[l.r] != nullptr;
+  const float closing = decayed ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const float closing_last = decayed ? __expf(la * static_cast<float>(tile_len(p, p.NT - 1))) : 1.f;
   const bool in_image = l.f8 * 8 < p.DkP;
   const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
   const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  // S_in(0): the initial state, or zero.
   float S[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) S[e] = 0.f;
+  for (int e = 0; e < 8; ++e) {
+    const int f = l.f8 * 8 + e;
+    S[e] = (p.init != nullptr && f < p.Dk && l.c < p.Dv) ? __ldg(p.init + boundary_index(p, l.b, l.h, l.r, f, l.c))
+                                                       : 0.f;
+  }
   // Loads of a batch of tiles are issued together (the in-place writes of a
   // batch touch only tiles whose values were already read), so the serial
-  // chain pays one memory latency per batch rather than per tile.
+  // chain pays one memory latency per batch rather than per tile.  The last
+  // tile's state only matters for the final state (all_tiles).
+  const int last_used = p.all_tiles ? p.NT : p.NT - 1;
   for (int n0 = 0; n0 < p.NT; n0 += kPrefixBatch) {
     float4 u[kPrefixBatch][2];
 #pragma unroll
     for (int k = 0; k < kPrefixBatch; ++k) {
       const int n = n0 + k;
       u[k][0] = u[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (n + 1 < p.NT) {
+      if (n < last_used) {
         const float4* ptr = reinterpret_cast<const float4*>(
             p.states + state_index(p, l.b, l.h, n, l.r) * p.DkM * p.DvP + elem);
         u[k][0] = ptr[0];
@@ -120,16 +129,26 @@ __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
       const int n = n0 + k;
       if (n >= p.NT) break;
       const size_t si = state_index(p, l.b, l.h, n, l.r);
-      float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + elem);
-      ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
-      ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
-      if (in_image) {
-        uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
-        *reinterpret_cast<uint4*>(img) = pack8(S);
+      if (p.store) {
+        float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + elem);
+        ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
+        ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
+        if (in_image) {
+          uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+          *reinterpret_cast<uint4*>(img) = pack8(S);
+        }
       }
+      const float cl = n + 1 < p.NT ? closing : closing_last;
       const float v[8] = {u[k][0].x, u[k][0].y, u[k][0].z, u[k][0].w, u[k][1].x, u[k][1].y, u[k][1].z, u[k][1].w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) S[e] = S[e] * closing + v[e];
+      for (int e = 0; e < 8; ++e) S[e] = S[e] * cl + v[e];
+    }
+  }
+  if (p.final_state != nullptr && l.c < p.Dv) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = l.f8 * 8 + e;
+      if (f < p.Dk) p.final_state[boundary_index(p, l.b, l.h, l.r, f, l.c)] = S[e];
     }
   }
 }
@@ -191,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
       tile_st16(tp, row, c / 8, pack8(f));
       tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
     }
-    const bool cross = n > 0;
+    const bool cross = n > 0 || p.init != nullptr;
     if (cross) {
       const size_t si = state_index(p, b, h, n, r);
       load_image(ts, reinterpret_cast<const uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)),
@@ -228,16 +247,20 @@ size_t scan_out_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + p.DvP) * 2 + static_cast<size_t>(p.DvP) * p.DkP * 2;
 }
 
-int launch_scan_fwd(const ScanParams& p, cudaStream_t s) {
+// The three forward kernels; `tile_states` / `outputs` select the parts that
+// run (the stages of a sequence shard run them separately).
+int launch_scan_fwd(const ScanParams& p, cudaStream_t s, bool tile_states, bool outputs) {
   const size_t sm1 = scan_state_smem(p), sm3 = scan_out_smem(p);
   cudaFuncSetAttribute(scan_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm1));
   cudaFuncSetAttribute(scan_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm3));
-  if (p.NT > 1) {
-    scan_state_kernel<<<dim3(p.NT - 1, p.H, p.B), kThreads, sm1, s>>>(p);
+  const int state_tiles = p.all_tiles ? p.NT : p.NT - 1;
+  if (tile_states && state_tiles > 0) {
+    scan_state_kernel<<<dim3(state_tiles, p.H, p.B), kThreads, sm1, s>>>(p);
     if (int e = check_launch("scan_state_kernel")) return e;
   }
   scan_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p);
   if (int e = check_launch("scan_prefix_kernel")) return e;
+  if (!outputs) return 0;
   scan_out_kernel<<<dim3(p.NT, p.H, p.B), kThreads, sm3, s>>>(p);
   return check_launch("scan_out_kernel");
 }

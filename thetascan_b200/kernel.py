@@ -290,82 +290,99 @@ class _KernelCoreQKV(torch.autograd.Function):
                 g["scale"], g["dla"], g["deta"])
 
 
-class _FeatScan(torch.autograd.Function):
-    """Features and scan of the fused-projection path as one autograd stage
-    whose outputs (phi_q, phi_k, y0 and the retention slots) stay visible, so
-    that code between the scan and the read -- the state exchange of sequence
-    shards -- differentiates through them."""
+class _ShardScan:
+    """What the two autograd stages of a sequence shard share: the scan
+    workspaces (forward and backward), the slots and the entering state."""
+
+
+def _features_fwd(spec, prologue, H, qkv, W1, W2, ctl):
+    lib = _lib.load()
+    d = qkv.shape[-1] // (3 * H)
+    q, k, v = _qkv_views(qkv, H, d)
+    B, _, T, _ = q.shape
+    W1b = W1.detach().to(torch.bfloat16).contiguous()
+    W2b = W2.detach().to(torch.bfloat16).contiguous()
+    m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
+    phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=q.device)
+    phi_q = torch.empty_like(phi_k)
+    y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=q.device)
+    fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
+    _set_prologue(fa, prologue)
+    _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
+    return (q, k, v), W1b, W2b, phi_q, phi_k, y0
+
+
+class _ShardStageA(torch.autograd.Function):
+    """Features and the first half of the scan of one sequence shard: every
+    tile's state and the shard total U (the state its tokens leave behind from
+    a zero start).  Its backward finishes the scan backward from dU, the
+    gradient the exchange hands back, then runs the feature backward."""
 
     @staticmethod
-    def forward(ctx, spec, prologue, H, qkv, W1, W2, thr, bias, gain, scale, log_alphas):
+    def forward(ctx, hold, spec, prologue, H, qkv, W1, W2, thr, bias, gain, scale, log_alphas):
         lib = _lib.load()
-        d = qkv.shape[-1] // (3 * H)
-        q, k, v = _qkv_views(qkv, H, d)
-        B, _, T, _ = q.shape
         ctl = _controls(thr, bias, gain, scale)
-        W1b = W1.detach().to(torch.bfloat16).contiguous()
-        W2b = W2.detach().to(torch.bfloat16).contiguous()
-        m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
+        (q, k, v), W1b, W2b, phi_q, phi_k, y0 = _features_fwd(spec, prologue, H, qkv, W1, W2, ctl)
+        B, _, T, d = q.shape
+        m = phi_q.shape[-1]
         dev = q.device
-        phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
-        phi_q = torch.empty_like(phi_k)
-        y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
-        _set_prologue(fa, prologue)
-        _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
         las = [None] + ([] if log_alphas is None else
                         [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
+        R = len(las)
         slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
+        U = torch.empty(B, H, R, m, d + 1, dtype=torch.float32, device=dev)
         sa = _build_args(phi_q, phi_k, v, las, slots, True)
         ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
         sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
+        sa.final_state, sa.stage = U.data_ptr(), 1
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
-        ctx.spec, ctx.prologue, ctx.H, ctx.ctl = spec, prologue, H, ctl
-        ctx.st = dict(W1b=W1b, W2b=W2b, phi_q=phi_q, phi_k=phi_k, ws=ws, slots=slots, las=las)
+        hold.ws, hold.slots, hold.las, hold.phi_q, hold.phi_k = ws, slots, las, phi_q, phi_k
+        hold.dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
+        ctx.hold, ctx.spec, ctx.prologue, ctx.H, ctx.ctl = hold, spec, prologue, H, ctl
+        ctx.W = (W1b, W2b)
         ctx.dtypes = (W1.dtype, W2.dtype)
         ctx.save_for_backward(qkv)
-        return (phi_q, phi_k, y0, *slots)
+        return phi_q, phi_k, y0, U
 
     @staticmethod
-    def backward(ctx, dphi_q_out, dphi_k_out, dy0, *dslots):
+    def backward(ctx, dphi_q_out, dphi_k_out, dy0, dU):
         lib = _lib.load()
         (qkv,) = ctx.saved_tensors
-        H, st, spec = ctx.H, ctx.st, ctx.spec
+        hold, H, spec = ctx.hold, ctx.H, ctx.spec
         d = qkv.shape[-1] // (3 * H)
         q, k, v = _qkv_views(qkv, H, d)
         B, _, T, _ = q.shape
         dev = q.device
-        slots, las = st["slots"], st["las"]
-        n = len(slots)
         dqkv = torch.empty_like(qkv)
         dq, dk, dv = _qkv_views(dqkv, H, d)
-        # scan
-        douts = [torch.zeros(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) if g is None
-                 else g.to(torch.bfloat16).contiguous() for g in dslots]
-        sa = _build_args(st["phi_q"], st["phi_k"], v, las, slots, True, st["ws"])
+        # scan, second half: reverse prefix from dU, then dq / dk / dv
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
         sg = _lib.ScanGradArgs()
-        m = st["phi_q"].shape[-1]
+        m = hold.phi_q.shape[-1]
         dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
         dphi_k = torch.empty_like(dphi_q)
         sg.dv = dv.data_ptr()
         sg.dv_strides = _lib.c_int64_3(*dv.stride()[:3])
-        dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
-        for i in range(n):
-            sg.dout[i] = douts[i].data_ptr()
-            sg.dlog_alpha[i] = _ptr(dlas[i])
+        for i in range(len(hold.las)):
+            sg.dout[i] = hold.douts[i].data_ptr()
+            sg.dlog_alpha[i] = _ptr(hold.dlas[i])
         sg.dq, sg.dk = dphi_q.data_ptr(), dphi_k.data_ptr()
         sg.grad_dtype = _lib.TS_DTYPE_BF16
-        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
-        sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
+        sg.workspace, sg.workspace_bytes = hold.gws.data_ptr(), hold.gws.numel()
+        dU = None if dU is None else dU.float().contiguous()
+        sg.dfinal_state = _ptr(dU)
+        sg.stage = 2
         _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
-        del gws
-        # gradients that reached phi directly (not through the scan)
+        del hold.gws
         if dphi_q_out is not None:
             dphi_q = (dphi_q.float() + dphi_q_out.float()).to(torch.bfloat16)
         if dphi_k_out is not None:
             dphi_k = (dphi_k.float() + dphi_k_out.float()).to(torch.bfloat16)
         # features
-        fa = _feature_args(spec, q, k, st["W1b"], st["W2b"], ctx.ctl, st["phi_k"], st["phi_q"], None)
+        W1b, W2b = ctx.W
+        ctl = ctx.ctl
+        fa = _feature_args(spec, q, k, W1b, W2b, ctl, hold.phi_k, hold.phi_q, None)
         _set_prologue(fa, ctx.prologue)
         fg = _lib.FeatureGradArgs()
         fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_BF16
@@ -376,7 +393,6 @@ class _FeatScan(torch.autograd.Function):
         fg.dk_bf16, fg.dq_bf16 = dk.data_ptr(), dq.data_ptr()
         fg.dk_strides = _lib.c_int64_3(*dk.stride()[:3])
         fg.dq_strides = _lib.c_int64_3(*dq.stride()[:3])
-        W1b, W2b, ctl = st["W1b"], st["W2b"], ctx.ctl
         dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
         dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
         grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
@@ -386,9 +402,52 @@ class _FeatScan(torch.autograd.Function):
         fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
         _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
         w1d, w2d = ctx.dtypes
-        dla = None if n == 1 else torch.stack(dlas[1:])
-        return (None, None, None, dqkv, dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"], grads["gain"],
-                grads["scale"], dla)
+        dla = None if len(hold.las) == 1 else torch.stack(hold.dlas[1:])
+        return (None, None, None, None, dqkv, dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"],
+                grads["gain"], grads["scale"], dla)
+
+
+class _ShardStageB(torch.autograd.Function):
+    """Second half of the scan forward of a shard: carried states from the
+    entering state S and the retention slots.  Its backward runs the first
+    half of the scan backward and returns dS, the gradient of the entering
+    state from this shard's own outputs."""
+
+    @staticmethod
+    def forward(ctx, hold, S, phi_q, phi_k, v):
+        lib = _lib.load()
+        hold.S = S.detach().float().contiguous()
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
+        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
+        ctx.hold = hold
+        ctx.save_for_backward(v)
+        return tuple(hold.slots)
+
+    @staticmethod
+    def backward(ctx, *dslots):
+        lib = _lib.load()
+        hold = ctx.hold
+        (v,) = ctx.saved_tensors
+        B, H, T = hold.phi_q.shape[:3]
+        d = v.shape[-1]
+        dev = v.device
+        hold.douts = [torch.zeros(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) if g is None
+                      else g.to(torch.bfloat16).contiguous() for g in dslots]
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
+        hold.gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+        sg = _lib.ScanGradArgs()
+        for i in range(len(hold.las)):
+            sg.dout[i] = hold.douts[i].data_ptr()
+            sg.dlog_alpha[i] = _ptr(hold.dlas[i])
+        # dq / dk / dv are written by the second half (stage A's backward)
+        sg.grad_dtype = _lib.TS_DTYPE_BF16
+        sg.workspace, sg.workspace_bytes = hold.gws.data_ptr(), hold.gws.numel()
+        dS = torch.empty_like(hold.S)
+        sg.dinit_state, sg.stage = dS.data_ptr(), 1
+        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
+        return None, dS, None, None, None
 
 
 class _KRead(torch.autograd.Function):
@@ -433,26 +492,38 @@ class _KRead(torch.autograd.Function):
         return (None, dy0, deta if ctx.has_eta else None, *dslots)
 
 
-def kernel_core_staged(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,
-                       score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None,
-                       between=None):
-    """The hot path of :func:`kernel_core_qkv` as two autograd stages with a
-    hook between them: ``between(phi_q, phi_k, v, slots) -> slots`` may add to
-    the retention slots (the entering-state terms of a sequence shard) with
-    differentiable torch code.  Without a hook it equals ``kernel_core_qkv``."""
+def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, shard, *, threshold=None,
+                        score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None):
+    """The hot path of :func:`kernel_core_qkv` on one contiguous shard of the
+    sequence (``prologue.pos0`` = its first position).  The scan runs in two
+    halves around one exchange of shard totals (``shard.gather``, an
+    all-gather on a process group): the first half leaves every tile's state
+    and the shard total U; the entering state S is the decayed exclusive
+    prefix of the earlier shards' totals (:func:`thetascan_b200.seqpar.entering_state`);
+    the second half carries the states from S and reads.  The backward mirrors
+    it: dS of every shard, the reverse exchange (all_gather's backward), then
+    dq / dk / dv from each shard's dU."""
+    from .seqpar import entering_state
     if not qkv.is_cuda:
         raise RuntimeError("b200 backend requires CUDA tensors")
     if qkv.dtype != torch.bfloat16 or qkv.dim() != 3 or not qkv.is_contiguous():
-        raise ValueError("kernel_core_staged: qkv must be a contiguous bf16 [B,T,3*H*d] tensor")
+        raise ValueError("kernel_core_sharded: qkv must be a contiguous bf16 [B,T,3*H*d] tensor")
     if (log_alphas is None) != (spec.mode == "sum"):
-        raise ValueError("kernel_core_staged: log_alphas are required exactly for a bank (mode fast/stale)")
+        raise ValueError("kernel_core_sharded: log_alphas are required exactly for a bank (mode fast/stale)")
     if spec.mode == "stale":
         raise NotImplementedError("b200 backend: the stale bank is not built yet (fast banks are supported)")
-    out = _FeatScan.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas)
-    phi_q, phi_k, y0, slots = out[0], out[1], out[2], list(out[3:])
-    if between is not None:
-        d = qkv.shape[-1] // (3 * H)
-        slots = list(between(phi_q, phi_k, _qkv_views(qkv, H, d)[2], slots))
+    hold = _ShardScan()
+    phi_q, phi_k, y0, U = _ShardStageA.apply(hold, spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain,
+                                             spline_scale, log_alphas)
+    totals = shard.gather(U)
+    las = [None] + ([] if log_alphas is None else [log_alphas[j] for j in range(log_alphas.shape[0])])
+    S = entering_state(totals, las, qkv.shape[1], shard.rank)
+    if shard.rank == 0:
+        # a zero state, but the graph must reach the gather: its backward is a
+        # collective every rank joins
+        S = S + 0.0 * totals[0]
+    d = qkv.shape[-1] // (3 * H)
+    slots = _ShardStageB.apply(hold, S, phi_q, phi_k, _qkv_views(qkv, H, d)[2])
     return _KRead.apply(spec, y0, etas, *slots)
 
 

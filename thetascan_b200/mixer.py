@@ -27,7 +27,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .config import ThetaScanConfig
-from .kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv, kernel_core_staged
+from .kernel import KernelSpec, Prologue, kernel_core, kernel_core_qkv, kernel_core_sharded
 
 EXPANSION_DOMAIN = "thetascan-expansion-v1"
 FINGERPRINT_MAGIC = b"TSXF"
@@ -282,16 +282,14 @@ class ThetaScanCore(nn.Module):
         if shard is not None:
             if self.proj_qkv is None or self.vmlp_in is not None:
                 raise NotImplementedError("sequence shards need the fused q/k/v projection without a value MLP")
-            from .seqpar import exchange
             qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
             pos0 = shard.rank * T
             cos = sin = None
             if self._rot:
                 cos, sin = _rope_tables(pos0 + T, self._rot, float(self.cfg.rope.base), str(x.device))
             prologue = Prologue(self._rot, cos, sin, 1e-6, pos0)
-            las = [None] + ([] if log_alphas is None else [log_alphas[j] for j in range(log_alphas.shape[0])])
-            y = kernel_core_staged(qkv, H, W1, W2, self.spec, prologue, log_alphas=log_alphas, etas=etas,
-                                   between=exchange(shard, las), **self.kernel_controls())
+            y = kernel_core_sharded(qkv, H, W1, W2, self.spec, prologue, shard, log_alphas=log_alphas, etas=etas,
+                                    **self.kernel_controls())
         elif self.proj_qkv is not None and self.vmlp_in is None:
             # Fused projection layout: RoPE and the L2 norm run inside the
             # feature kernels, v is read from the projection in place.

@@ -14,10 +14,16 @@ augmented payload [v | 1]:
 the same algebra as the tile states of the reference chunk backend
 (src/thetascan/_core/ops/scan_chunk.py:199-207) with shards in place of
 tiles.  Numerators and masses stay unnormalized until the read, so the
-division happens once, after the correction.  Everything here is
-differentiable torch code: autograd carries the gradients of phi_q, phi_k, v
-and la back through the exchange (all_gather's backward reduces the gradient
-of each shard total onto its owner).
+division happens once, after the correction.
+
+On the GPU the scan kernels produce U (the tile-prefix recursion carried one
+tile further) and apply S (as the initial state of the prefix, read through
+the cross term of every tile), in two halves around the exchange; see
+:func:`thetascan_b200.kernel.kernel_core_sharded`.  Only the exchange and
+:func:`entering_state` run here, as differentiable torch code on
+[B,H,R,m,d+1] states.  :func:`shard_totals`, :func:`add_entering` and
+:func:`exchange` state the whole algebra in torch for any scan (the CPU
+tests run it around the float64 oracle scan).
 """
 from __future__ import annotations
 
@@ -110,8 +116,9 @@ def add_entering(slots: Sequence[torch.Tensor], phi_q: torch.Tensor, S: torch.Te
 
 
 def exchange(shard: SeqShard, las: Sequence[torch.Tensor | None]):
-    """The hook between the scan and the read of one shard (see
-    :func:`thetascan_b200.kernel.kernel_core_staged`)."""
+    """The exchange applied to the zero-state reads ``slots`` of one shard:
+    ``between(phi_q, phi_k, v, slots)`` returns the reads of the shard
+    entering with the earlier shards' state (torch statement of the algebra)."""
 
     def between(phi_q, phi_k, v, slots):
         totals = shard.gather(shard_totals(phi_k, v, las))
