@@ -205,3 +205,33 @@ def test_scan_errors_follow_the_reference_contract(lib):
         scan.linattn(q.float(), k.float(), v.float())
     with pytest.raises(RuntimeError):
         scan.linattn(q.cpu(), k.cpu(), v.cpu())
+
+
+def test_streamed_segments_equal_one_call(lib):
+    """Scanning ragged segments one after another, each continuing from the
+    previous segment's state, gives the single-call outputs; the returned
+    state is sum_t e^{la (T-1-t)} k_t^T [v_t | 1] (float64 reference)."""
+    from thetascan_b200.scan import linattn_views, linattn_views_stream
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(21)
+    B, H, T, Dk, Dv = 2, 3, 528, 64, 32
+    q = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
+    k = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
+    v = torch.randn(B, H, T, Dv, generator=g).to(torch.bfloat16).to(dev)
+    la = [None] + [torch.log(0.9 + 0.09 * torch.rand(H, generator=g)).to(dev) for _ in range(2)]
+    full = linattn_views(q, k, v, tuple(la), append_unit=True)
+    state, pieces, t0 = None, [], 0
+    for seg in (100, 128, 300):
+        sl = slice(t0, t0 + seg)
+        outs, state = linattn_views_stream(q[:, :, sl], k[:, :, sl], v[:, :, sl], tuple(la), state, append_unit=True)
+        pieces.append(outs)
+        t0 += seg
+    for r in range(len(la)):
+        streamed = torch.cat([p[r] for p in pieces], dim=2)
+        assert rel_err(streamed, full[r]) < BF16_TOL, r
+    kk, vv = k.double().cpu(), torch.cat((v.double(), torch.ones(B, H, T, 1, dtype=torch.float64, device=dev)), -1).cpu()
+    back = (T - 1 - torch.arange(T, dtype=torch.float64))
+    for r, a in enumerate(la):
+        w = torch.ones(H, T, dtype=torch.float64) if a is None else torch.exp(a.double().cpu()[:, None] * back)
+        want = torch.einsum("bhtf,ht,bhtc->bhfc", kk, w, vv)
+        assert rel_err(state[:, :, r], want) < BF16_TOL, r

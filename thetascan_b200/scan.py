@@ -169,3 +169,38 @@ def linattn(q, k, v, decay=None, chunk: int = DEFAULT_CHUNK, log_alpha=None):
     """One-view scan (scan_chunk.py:342-358); ``log_alpha`` takes precedence."""
     retention = log_alpha if log_alpha is not None else decay
     return linattn_views(q, k, v, (retention,), chunk)[0]
+
+
+def linattn_views_stream(q, k, v, retentions, state=None, *, append_unit: bool = False):
+    """Streaming form of :func:`linattn_views` (forward only): scan this
+    segment of the sequence continuing from ``state`` and return
+    ``(outputs, new_state)``.
+
+    ``state`` is what the previous segment returned (``None`` for the start
+    of the sequence): f32 ``[B,H,R,Dk,Dv]`` with ``R = len(retentions)`` and
+    ``Dv`` the payload width (``+1`` with ``append_unit``), the carried chunk
+    state of every retention -- the persistent fast state of a decoder.
+    Scanning a sequence segment by segment gives the outputs of one call over
+    the whole sequence (to rounding), for segments of any lengths."""
+    if not retentions:
+        return (), state
+    _check_inputs(q, k, v, retentions, DEFAULT_CHUNK)
+    if len(retentions) > _lib.MAX_RETENTIONS:
+        raise NotImplementedError(f"b200 streaming scan: at most {_lib.MAX_RETENTIONS} retentions per call")
+    lib = _lib.load()
+    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    B, H, T, Dk = q.shape
+    dv = v.shape[-1] + (1 if append_unit else 0)
+    if state is not None:
+        if tuple(state.shape) != (B, H, len(las), Dk, dv) or state.dtype != torch.float32:
+            raise ValueError(f"b200 streaming scan: state must be f32 [{B},{H},{len(las)},{Dk},{dv}]")
+        state = state.contiguous()
+    outs = [torch.empty(B, H, T, dv, dtype=torch.float32, device=q.device) for _ in las]
+    new_state = torch.empty(B, H, len(las), Dk, dv, dtype=torch.float32, device=q.device)
+    args = _build_args(q, k, v, las, outs, append_unit)
+    ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    args.init_state = None if state is None else state.data_ptr()
+    args.final_state = new_state.data_ptr()
+    _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
+    return tuple(o.to(q.dtype) for o in outs), new_state
