@@ -211,7 +211,7 @@ def project_qkv(p, cfg, x):
 
 
 def mixer_forward(p, cfg, x, *, scan_fn=None):
-    """Full kernel-family mixer ``x [B,T,D] -> [B,T,D]`` (block.py:573-724).
+    """Full mixer ``x [B,T,D] -> [B,T,D]`` (block.py:573-724), kernel or GN family.
 
     ``p`` maps reference state-dict names (core module, no ``_core.`` prefix,
     plus the expansion buffers) to tensors; ``cfg`` holds the core flags.
@@ -226,9 +226,17 @@ def mixer_forward(p, cfg, x, *, scan_fn=None):
     q, k = features.l2norm(q, eps), features.l2norm(k, eps)
     W1, W2 = effective_weights(p, cfg)
     log_alphas, etas = fade_parameters(p, cfg, x.dtype)
-    y = kernel_core(q, k, v, W1, W2, feature_spec(p, cfg), log_alphas=log_alphas, etas=etas,
-                    mode=cfg.get("read_fade_mode", "fast"), read_norm=cfg.get("read_norm", "key_mass"),
-                    eps=eps, chunk=cfg.get("scan_chunk", 512), scan_fn=scan_fn)
+    if cfg.get("write_rule", "kernel") == "gn":
+        from .gn import gn_core
+        y = gn_core(q, k, v, W1, W2, p.get("Wg.0") if cfg.get("learn_thresh") else None,
+                    nonlin=cfg["nonlin"], read_norm=bool(cfg["read_norm"]),
+                    read_norm_w1=bool(cfg.get("read_norm_w1")), log_alphas=log_alphas, etas=etas,
+                    mode=cfg.get("read_fade_mode", "fast"), eps=eps, chunk=cfg.get("scan_chunk", 512),
+                    scan_fn=scan_fn)
+    else:
+        y = kernel_core(q, k, v, W1, W2, feature_spec(p, cfg), log_alphas=log_alphas, etas=etas,
+                        mode=cfg.get("read_fade_mode", "fast"), read_norm=cfg.get("read_norm", "key_mass"),
+                        eps=eps, chunk=cfg.get("scan_chunk", 512), scan_fn=scan_fn)
     if "ogate.g.lin.weight" in p:
         gate = F.linear(x, p["ogate.g.lin.weight"], p["ogate.g.lin.bias"])
         y = y * F.silu(gate.view(B, T, H, d).transpose(1, 2))

@@ -160,13 +160,99 @@ def mixer_cases():
     return out
 
 
+GN_CONFIGS = {
+    # Config-3 parity family: relu2, two-stage normalized read, one fast branch,
+    # shared k/q projection (the gn_reference_v0_1 preset at fixture size).
+    "gn_both_relu2_bank": dict(
+        d_model=64, n_heads=2, memory_multiplier=3, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9), B=2, T=40),
+    # gn_expanded_reference_v0_1 at fixture size: learned threshold, 2x expansion.
+    "gn_both_threshold_expanded": dict(
+        d_model=64, n_heads=2, memory_multiplier=6, feature_expansion=2, share_key_query=True,
+        output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2_threshold", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9), B=2, T=40),
+    # Normalized W2 read only, plain sum, output gate, per-head projections.
+    "gn_w2_relu2_sum": dict(
+        d_model=64, n_heads=2, memory_multiplier=2, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="w2_feature_mass"), B=2, T=40),
+    # Unnormalized read with silu and a two-branch fast bank.
+    "gn_none_silu_bank2": dict(
+        d_model=64, n_heads=2, memory_multiplier=2, family="gn",
+        gn=dict(nonlinearity="silu", read_normalization="none"),
+        temporal=dict(mode="bank", recency_branches=2, retention_inits=(0.9, 0.99)), B=2, T=40),
+    # Kernel-tile-shaped case for the CUDA path (head_dim 64, m = 128, ragged T).
+    "gn_d64_ragged": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32"),
+}
+
+GN_CORE_KEYS = (
+    "d_model", "n_heads", "head_dim", "mem_hidden", "feature_expansion", "expansion_key", "depth",
+    "write_rule", "nonlin", "learn_thresh", "write_iters", "fast_w1", "act_norm", "qk_norm",
+    "rope", "rope_frac", "rope_base", "read_fade", "read_fade_mode", "fade_blend_mode",
+    "read_norm", "read_norm_w1", "read_norm_mode", "eps", "scan_chunk", "share_kq", "key_value_heads")
+
+
+def gn_cases():
+    from thetascan import GNConfig, RoPEConfig, TemporalConfig, ThetaScan, ThetaScanConfig
+
+    out = {}
+    for name, spec in GN_CONFIGS.items():
+        spec = dict(spec)
+        B, T = spec.pop("B"), spec.pop("T")
+        dtype = getattr(torch, spec.pop("dtype", "float64"))
+        gn = GNConfig(**spec.pop("gn", {}))
+        rope = RoPEConfig(**spec.pop("rope", {}))
+        temporal = TemporalConfig(**spec.pop("temporal", {}))
+        cfg = ThetaScanConfig(gn=gn, rope=rope, temporal=temporal, **spec)
+        torch.manual_seed(0)
+        module = ThetaScan(cfg).to(torch.float64)
+        core = module._core
+        with torch.no_grad():
+            for p in core.W2:
+                p.copy_(_seeded(5, *p.shape) * 0.2)
+            if core.fade_eta is not None:
+                core.fade_eta.copy_(_seeded(6, *core.fade_eta.shape) * 0.5)
+            if core.Wg is not None:
+                for p in core.Wg:
+                    p.copy_(_seeded(7, *p.shape) * 0.1)
+            if getattr(core, "kq_bias", None) is not None:
+                core.kq_bias.copy_(_seeded(10, *core.kq_bias.shape) * 0.1)
+        x = _seeded(8, B, T, cfg.d_model).requires_grad_(True)
+        y = module(x)
+        weight = _seeded(9, *y.shape)
+        (y * weight).sum().backward()
+        params = {n: t.detach().to(dtype) for n, t in core.state_dict(keep_vars=True).items()
+                  if t is not None}
+        for n, buf in core.named_buffers():
+            if buf is not None and n not in params:
+                params[n] = buf.detach().to(dtype)
+        grads = {n: p.grad.detach().to(dtype) for n, p in core.named_parameters() if p.grad is not None}
+        core_cfg = module._core_config
+        out[name] = {
+            "public_config": cfg.to_dict(), "B": B, "T": T,
+            "core": {k: getattr(core_cfg, k) for k in GN_CORE_KEYS},
+            "params": params, "x": x.detach().to(dtype), "y": y.detach().to(dtype),
+            "out_weight": weight.to(dtype), "x_grad": x.grad.detach().to(dtype), "grads": grads,
+        }
+    return out
+
+
+GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases}
+
+
 def main():
+    # usage: make_golden.py [out_dir] [scan,feature,mixer,gn]
     target = sys.argv[1] if len(sys.argv) > 1 else os.path.dirname(os.path.abspath(__file__))
+    which = sys.argv[2].split(",") if len(sys.argv) > 2 else list(GENERATORS)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    torch.save(scan_cases(), os.path.join(target, "scan_cases.pt"))
-    torch.save(feature_cases(), os.path.join(target, "feature_cases.pt"))
-    torch.save(mixer_cases(), os.path.join(target, "mixer_cases.pt"))
-    print("golden fixtures written to", target)
+    for name in which:
+        torch.save(GENERATORS[name](), os.path.join(target, f"{name}_cases.pt"))
+    print("golden fixtures written to", target, which)
 
 
 if __name__ == "__main__":

@@ -130,3 +130,28 @@ def test_expansion_maps_match_reference_buffers():
     d = mixer.row_map((1, b, m), key=key, role="w2-expand-layer-0")
     assert torch.equal(u.to(torch.float64), case["params"]["_expand_w1_0"])
     assert torch.equal(d.to(torch.float64), case["params"]["_expand_w2_0"])
+
+
+GN_CASES = ["gn_both_relu2_bank", "gn_both_threshold_expanded", "gn_w2_relu2_sum", "gn_none_silu_bank2",
+            "gn_d64_ragged"]
+
+
+@pytest.mark.parametrize("name", GN_CASES)
+def test_gn_mixer_oracle_matches_reference_forward_and_backward(name):
+    """The GN restatement (oracle/gn.py) against the reference GN mixer: output,
+    input gradient and every parameter gradient."""
+    case = _load("gn_cases.pt")[name]
+    dtype = case["x"].dtype
+    params = {n: t.to(torch.float64).clone().requires_grad_(t.is_floating_point() and not n.startswith("_"))
+              for n, t in case["params"].items()}
+    x = case["x"].to(torch.float64).clone().requires_grad_(True)
+    cfg = dict(case["core"])
+    y = mixer.mixer_forward(params, cfg, x)
+    # The float32 fixture stores inputs rounded after the reference ran in
+    # float64; the lambda solve's division amplifies that rounding to ~6e-6.
+    tol = 1e-9 if dtype == torch.float64 else 2e-5
+    _close(y, case["y"].to(torch.float64), tol)
+    (y * case["out_weight"].to(torch.float64)).sum().backward()
+    _close(x.grad, case["x_grad"].to(torch.float64), tol)
+    for n, g in case["grads"].items():
+        _close(params[n].grad, g.to(torch.float64), tol)
