@@ -78,7 +78,7 @@ int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, i
 typedef struct ts_scan_args {
   int batch, heads, tokens;
   int dk;               /* key/query width, 1..256 */
-  int dv;               /* payload width incl. the unit column if v_append_unit, 1..128 */
+  int dv;               /* payload width incl. the unit column if v_append_unit, 1..256 (within the CTA budgets) */
   const void* q;        /* bf16 [B,H,T,dk] */
   const void* k;        /* bf16 [B,H,T,dk] */
   const void* v;        /* bf16 [B,H,T,dv - v_append_unit] */

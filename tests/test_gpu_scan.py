@@ -76,6 +76,9 @@ CASES = [
     (1, 2, 520, 128, 80, 3, True),
     (1, 2, 384, 256, 64, 1, True),
     (1, 1, 1030, 32, 16, 1, False),
+    # payloads wider than a tile (the GN streams [g | 1] and [lambda | 1])
+    (1, 2, 300, 128, 129, 1, True),
+    (1, 1, 200, 64, 160, 1, False),
 ]
 # Streams with random-sign scores whose log-retention gradient is a large
 # cancellation at alpha -> 1 (case 4, head 0: terms of 670 sum to 160, and

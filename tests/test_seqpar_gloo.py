@@ -66,6 +66,7 @@ def _worker(rank, port, out_dir):
         dist.all_reduce(dla)
         torch.save({"slots": [o.detach() for o in slots], "dq": qs.grad, "dk": ks.grad, "dv": vs.grad,
                     "dla": dla}, os.path.join(out_dir, f"rank{rank}.pt"))
+        dist.barrier()   # both ranks done with every collective before teardown
     finally:
         dist.destroy_process_group()
 

@@ -51,8 +51,8 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
     return set_error(TS_ERR_VALUE, "scan: batch, heads and tokens must be >= 1");
   if (a->dk < 1 || a->dk > 256)
     return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: key width %d outside 1..256", a->dk);
-  if (a->dv < 1 + a->v_append_unit || a->dv > 128)
-    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: payload width %d outside 1..128", a->dv);
+  if (a->dv < 1 + a->v_append_unit || a->dv > 256)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: payload width %d outside 1..256", a->dv);
   if (a->n_retentions < 1 || a->n_retentions > TS_MAX_RETENTIONS)
     return set_error(TS_ERR_VALUE, "scan: n_retentions must be in 1..%d", TS_MAX_RETENTIONS);
   if (!a->q || !a->k || !a->v) return set_error(TS_ERR_VALUE, "scan: null stream pointer");
@@ -90,7 +90,11 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
   p->all_tiles = a->final_state != nullptr;
   p->store = 1;
   const int mblocks = p->DkM / 128;
-  if (p->R * mblocks * p->DvP > 512 || 128 + p->R * p->DvP > 512)
+  // TMEM columns: tile updates of every retention (state kernel), score plus
+  // every retention's read (output kernel), the tile update and its
+  // (i+1)-weighted copy (backward state kernel), score, g and dv (dv kernel).
+  if (p->R * mblocks * p->DvP > 512 || 128 + p->R * p->DvP > 512 || 2 * mblocks * p->DvP > 512 ||
+      256 + p->DvP > 512)
     return set_error(TS_ERR_NOT_IMPLEMENTED,
                      "scan: %d retentions of a %dx%d state exceed the 512 tensor-memory columns of one CTA",
                      p->R, p->Dk, p->Dv);

@@ -348,7 +348,10 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   Tile tx{tv.saddr + kTile * p.DvP * 2, kTile, p.DkP};          // k (dq) or q (dk)
   Tile tds{tx.saddr + kTile * p.DkP * 2, kTile, kTile};
   Tile ts0{tds.saddr + kTile * kTile * 2, p.DvP, p.DkP};         // state image buffer 0
-  Tile ts1{tx.saddr, p.DvP, p.DkP};                               // buffer 1: the k/q region
+  // buffer 1: the k/q region (free after the ds product) when an image fits
+  // in it, else the images take turns in buffer 0
+  const bool two_images = p.DvP <= kTile;
+  Tile ts1 = two_images ? Tile{tx.saddr, p.DvP, p.DkP} : ts0;
   Tile td[4];
   for (int i = 0; i < 4; ++i) td[i] = Tile{ts0.saddr + p.DvP * p.DkP * 2 + i * kTile * p.DvP * 2, kTile, p.DvP};
   const bool staged = nbuf >= p.R;
@@ -383,8 +386,12 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   if (cross) {
     for (int r = 0; r < p.R; ++r) {
       const Tile& img = (r & 1) ? ts1 : ts0;
-      // The buffer of retention r+1 was read by the product of r-1 (done).
-      if (r + 1 < p.R) load_image((r & 1) ? ts0 : ts1, image_of(r + 1), image_bytes(p));
+      if (two_images) {
+        // The buffer of retention r+1 was read by the product of r-1 (done).
+        if (r + 1 < p.R) load_image((r & 1) ? ts0 : ts1, image_of(r + 1), image_bytes(p));
+      } else if (r > 0) {
+        load_image(ts0, image_of(r), image_bytes(p));   // buffer 0 is free again
+      }
       cp_async_commit();
       const float la = head_la(p, r, h);
       const bool decayed = p.la[r] != nullptr;
@@ -415,7 +422,11 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
           tile_st16(ta, row, j, pack8(f));
         }
       }
-      ctx.run_keep_newest([&] { gemm_issue(t_acc, kmajor(ta), mnmajor(img), p.DkP, p.DvP, true); });
+      if (two_images) {
+        ctx.run_keep_newest([&] { gemm_issue(t_acc, kmajor(ta), mnmajor(img), p.DkP, p.DvP, true); });
+      } else {
+        ctx.run([&] { gemm_issue(t_acc, kmajor(ta), mnmajor(img), p.DkP, p.DvP, true); });
+      }
     }
   }
   const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
@@ -445,7 +456,11 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   const uint32_t base = smem_u32(smem);
   Tile tq{base, kTile, p.DkP};                          // q, then (u_r o k)
   Tile tk{tq.saddr + kTile * p.DkP * 2, kTile, p.DkP};  // k, then G image
-  Tile tg{tk.saddr, p.DvP, p.DkP};
+  // The G image reuses the k region when it fits there (DvP <= 128), else it
+  // has its own region after the payload tile.
+  const Tile tg = p.DvP <= kTile ? Tile{tk.saddr, p.DvP, p.DkP}
+                                 : Tile{tk.saddr + kTile * p.DkP * 2 + kTile * kTile * 2 + 2 * kTile * p.DvP * 2,
+                                        p.DvP, p.DkP};
   Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
   Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
@@ -542,7 +557,8 @@ static size_t dqk_smem(const ScanParams& p, int nbuf) {
 constexpr size_t kDynSmemBudget = 232448 - 4096;
 static int dqk_buffers(const ScanParams& p) { return dqk_smem(p, p.R) <= kDynSmemBudget ? p.R : 1; }
 static size_t dv_smem(const ScanParams& p) {
-  return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2;
+  return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2 +
+         (p.DvP > kTile ? static_cast<size_t>(p.DvP) * p.DkP * 2 : 0);
 }
 static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (2 * p.DkM + 2 * p.DvP) * 2; }
 
