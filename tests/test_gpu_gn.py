@@ -1,0 +1,56 @@
+"""GPU parity of the GN (Gauss--Newton fast-weight) mixer.
+
+The module runs the GN write and features in f32 PyTorch and every sequence
+read on the scan kernels (bf16 streams, f32 states).  Each case is a golden
+fixture produced by the reference GN mixer itself (two-stage normalized read
+with and without the learned threshold and feature expansion, the normalized
+W2 read, the unnormalized silu read with a two-branch bank, and a
+head_dim-64 ragged-T case): output, input gradient and every parameter
+gradient.  Tolerance ``max|got - ref| / max|ref| <= 2e-2`` (bf16 streams).
+"""
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 2e-2
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+CASES = ["gn_both_relu2_bank", "gn_both_threshold_expanded", "gn_w2_relu2_sum", "gn_none_silu_bank2",
+         "gn_d64_ragged"]
+
+
+def rel_err(got, want):
+    got = got.detach().to("cpu", torch.float64)
+    want = want.detach().to("cpu", torch.float64)
+    return float((got - want).abs().max() / want.abs().max().clamp_min(1e-30))
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda")
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_gn_mixer_matches_reference_fixture(dev, name):
+    from thetascan_b200 import _lib
+    from thetascan_b200.config import ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+
+    case = torch.load(os.path.join(GOLDEN, "gn_cases.pt"), weights_only=False)[name]
+    module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    x = case["x"].float().to(dev).requires_grad_(True)
+    y = module(x)
+    (y.double() * case["out_weight"].to(dev)).sum().backward()
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    assert rel_err(y, case["y"]) < BF16_TOL
+    assert rel_err(x.grad, case["x_grad"]) < BF16_TOL
+    grads = dict(module._core.named_parameters())
+    for n, want in case["grads"].items():
+        assert rel_err(grads[n].grad, want) < BF16_TOL, n

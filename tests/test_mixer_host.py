@@ -54,8 +54,11 @@ def test_state_dict_and_seeded_init_match_reference(name):
 def test_presets_and_unsupported_configs():
     kernel = ThetaScanConfig.kernel_expanded_reference_v0_1(d_model=256, n_heads=4)
     ThetaScan(kernel)  # constructs on CPU; the forward needs CUDA
+    ThetaScan(ThetaScanConfig.gn_reference_v0_1(d_model=256, n_heads=4))
+    ThetaScan(ThetaScanConfig.gn_expanded_reference_v0_1(d_model=256, n_heads=4))
+    from thetascan_b200.config import GNConfig
     with pytest.raises(NotImplementedError):
-        ThetaScan(ThetaScanConfig.gn_reference_v0_1(d_model=256, n_heads=4))
+        ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn", gn=GNConfig(nonlinearity="swiglu")))
     stale = ThetaScanConfig.from_dict(_fixtures()["bspline_stale"]["public_config"])
     with pytest.raises(NotImplementedError):
         ThetaScan(stale)
@@ -69,3 +72,25 @@ def test_forward_requires_cuda():
     module = ThetaScan(cfg)
     with pytest.raises(RuntimeError):
         module(torch.zeros(1, 8, cfg.d_model))
+
+
+GN_OVERWRITTEN = {"W2.0", "fade_eta", "Wg.0", "kq_bias"}  # set by the fixture generator
+
+
+@pytest.mark.parametrize("name", ["gn_both_relu2_bank", "gn_both_threshold_expanded", "gn_w2_relu2_sum",
+                                  "gn_none_silu_bank2"])
+def test_gn_state_dict_and_seeded_init_match_reference(name):
+    """GN modules: the same parameter names and shapes as the reference's, and
+    (seed 0) the same initial values for everything the fixture generator did
+    not overwrite; the reference state dict loads unchanged."""
+    case = torch.load(os.path.join(GOLDEN, "gn_cases.pt"), weights_only=False)[name]
+    torch.manual_seed(0)
+    module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"]))
+    ours = {n: t for n, t in module._core.state_dict().items()}
+    theirs = {n: t for n, t in case["params"].items() if not n.startswith("_expand_")}
+    assert set(ours) == set(theirs)
+    for n, t in ours.items():
+        assert tuple(t.shape) == tuple(theirs[n].shape), n
+        if n not in GN_OVERWRITTEN:
+            assert torch.equal(t.to(theirs[n].dtype), theirs[n]), n
+    module.load_state_dict({"_core." + n: t.float() for n, t in theirs.items()})

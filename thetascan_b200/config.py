@@ -10,7 +10,7 @@ package executes that backend only (``"auto"`` resolves to it).
 
 Validation restates the reference's rules for the fields this package reads
 and raises ``NotImplementedError`` for configurations the GPU path does not
-cover yet (the GN family, EMA decay gates, stale banks, value anchors,
+cover yet (GN swiglu and two-step Jacobians, EMA decay gates, stale banks, value anchors,
 relative sparsity, feature-space RoPE).
 """
 from __future__ import annotations
@@ -410,10 +410,22 @@ class ThetaScanConfig:
 
     def unsupported_reason(self) -> str | None:
         """Why the B200 path cannot run this (validated) config, or None."""
-        if self.family != "kernel":
-            return "the GN family is not built on the B200 path yet"
         if self.runtime.backend not in ("auto", "b200"):
             return f"this package executes backend 'b200' only, not {self.runtime.backend!r}"
+        if self.temporal.mode == "ema":
+            return "the data-dependent EMA decay gate is not built"
+        if self.temporal.mode == "bank" and self.temporal.bank_mode == "stale":
+            return "the stale bank is not built"
+        if self.rope.mode != "none" and self.rope.placement == "feature":
+            return "feature-space RoPE is not built"
+        if self.family == "gn":
+            if self.gn.nonlinearity == "swiglu":
+                return "the GN swiglu nonlinearity is not built"
+            if self.gn.jacobian_steps != 1:
+                return "GN jacobian_steps=2 is not built"
+            if self.depth != 1:
+                return "GN depth > 1 is not built"
+            return None
         k = self.kernel
         if k.read_normalization != "key_mass":
             return f"kernel read_normalization={k.read_normalization!r} (only 'key_mass' is built)"
@@ -421,10 +433,4 @@ class ThetaScanConfig:
             return "kernel value_anchors are not built"
         if k.sparsity != "none":
             return "relative kernel sparsity is not built"
-        if self.temporal.mode == "ema":
-            return "the data-dependent EMA decay gate is not built"
-        if self.temporal.mode == "bank" and self.temporal.bank_mode == "stale":
-            return "the stale bank is not built"
-        if self.rope.mode != "none" and self.rope.placement == "feature":
-            return "feature-space RoPE is not built"
         return None

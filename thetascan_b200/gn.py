@@ -1,0 +1,153 @@
+"""Gauss--Newton (GN) fast-weight family on the B200 path.
+
+One memory block (depth 1) with one Jacobian step, as the reference runs
+``family="gn"`` (src/thetascan/config.py:745-756).  Per token, in f32 with
+autograd:
+
+  write (engine.py:161-340)  a = W1 k, pre = rmsnorm(a) [- tau], h = sigma(pre),
+                             o = k + W2 h, r = v - o,
+                             lambda = r / (||h||^2 + ||k||^2 (W2^2)(s^2) + eps),
+                             s = sigma'(pre) / rms(a),
+                             g = sigma'(pre) (W2^T lambda) / rms(a);
+  read (engine.py:455-528)   stage 1: pre_v = W1 q + [g-stream read of the view],
+                             stage 2: h_v = sigma(rmsnorm(pre_v) [- tau]),
+                             y_v = q + W2 h_v + [lambda-stream read of the view].
+
+Every read over the sequence -- the T-long part -- runs on the sm_100a
+multi-view scan kernels (``ts_b200_scan_fwd/bwd``) with bf16 streams, f32
+states and f32 reads: stage 1 once for all views (one score tile per view
+set), stage 2 once per view because each view's query differs
+(engine.py:355-361).  The read normalizations follow the reference:
+``both_feature_mass`` reads [g | 1] with the positive slow features
+h0 = relu2(rmsnorm(W1 q) [- tau]) against keys h and normalizes both stages
+by their mass column; ``w2_feature_mass`` reads g with q against k
+unnormalized and normalizes stage 2; ``none`` normalizes neither.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .scan import _ScanViews
+
+
+def _activation(nonlin, pre):
+    if nonlin == "relu2":
+        r = F.relu(pre)
+        return r * r
+    if nonlin == "silu":
+        return F.silu(pre)
+    raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
+
+
+def _activation_grad(nonlin, pre):
+    if nonlin == "relu2":
+        return 2.0 * F.relu(pre)
+    if nonlin == "silu":
+        s = torch.sigmoid(pre)
+        return s * (1 + pre * (1 - s))
+    raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
+
+
+def _rmsnorm(a, eps):
+    """``a * rsqrt(mean(a^2) + eps)`` and the factor (reference norms.py:5-8)."""
+    inv = torch.rsqrt(a.square().mean(-1, keepdim=True) + eps)
+    return a * inv, inv
+
+
+def _thresholded(pre, tau):
+    return pre if tau is None else pre - tau[..., 0].unsqueeze(0).unsqueeze(2).to(pre.dtype)
+
+
+def _views(mode, J):
+    """Retention slots of each view: slot 0 the plain sum, 1+j branch j (fast bank)."""
+    if mode != "fast" and J:
+        raise NotImplementedError("b200 GN: only the plain sum and fast banks are built")
+    return [0] + [1 + j for j in range(J)]
+
+
+def _piece_width(n_retentions, Dk):
+    """Payload columns (unit column included) one scan call takes within the
+    tensor-memory and shared-memory budget of its tile kernels."""
+    if n_retentions >= 4:
+        return 96
+    if n_retentions == 3 or Dk > 128:
+        return 128
+    return 144
+
+
+def _scan(query, keys, payload, append_unit, retentions):
+    """f32 reads of the multi-view scan kernels (bf16 streams).  The scan is
+    linear in the payload, so a payload wider than one call takes is read in
+    column pieces (the mass column rides on the last)."""
+    bf = torch.bfloat16
+    q, k = query.to(bf).contiguous(), keys.to(bf).contiguous()
+    width = payload.shape[-1]
+    step = _piece_width(len(retentions), q.shape[-1]) - 1
+    if width + (1 if append_unit else 0) <= step + 1:
+        return _ScanViews.apply(q, k, payload.to(bf).contiguous(), append_unit, torch.float32, *retentions)
+    parts = [[] for _ in retentions]
+    for start in range(0, width, step):
+        piece = payload[..., start:start + step].to(bf).contiguous()
+        last = start + step >= width
+        for i, read in enumerate(_ScanViews.apply(q, k, piece, append_unit and last, torch.float32, *retentions)):
+            parts[i].append(read)
+    return tuple(torch.cat(p, dim=-1) for p in parts)
+
+
+def gn_write(k, v, W1, W2, tau, nonlin, eps):
+    """(h, g, lambda) of every token, f32 (reference engine.py:161-340, depth 1)."""
+    a = torch.einsum("hmd,bhtd->bhtm", W1, k)
+    pre, inv = _rmsnorm(a, eps)
+    pre = _thresholded(pre, tau)
+    h = _activation(nonlin, pre)
+    o = k + torch.einsum("hdm,bhtm->bhtd", W2, h)
+    r = v - o
+    dsig = _activation_grad(nonlin, pre)
+    s = dsig * inv
+    rowsq = torch.einsum("hdm,bhtm->bhtd", W2 * W2, s * s)
+    diag = h.square().sum(-1, keepdim=True) + k.square().sum(-1, keepdim=True) * rowsq
+    lam = r / (diag + eps)
+    g = dsig * torch.einsum("hdm,bhtd->bhtm", W2, lam) * inv
+    return h, g, lam
+
+
+def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_norm_w1=True, log_alphas=None,
+            etas=None, mode="fast", eps=1e-6):
+    """GN mixer core ``[B,H,T,d]`` f32 from bf16 ``q, k, v`` after RoPE / L2 norm.
+
+    ``W1 [H,m,d]``, ``W2 [H,d,m]`` effective weights, ``tau [H,m,1]`` the learned
+    threshold of ``relu2_threshold`` (or None), ``log_alphas``/``etas``
+    ``[J,H]`` for a fast bank."""
+    for x in (q, k, v):
+        if not x.is_cuda:
+            raise RuntimeError("b200 backend requires CUDA tensors")
+    m, d = W1.shape[1], q.shape[-1]
+    qf, kf, vf = q.float(), k.float(), v.float()
+    W1f, W2f = W1.float(), W2.float()
+    tauf = None if tau is None else tau.float()
+    h_k, g, lam = gn_write(kf, vf, W1f, W2f, tauf, nonlin, eps)
+    J = 0 if log_alphas is None else log_alphas.shape[0]
+    las = [None] + [log_alphas[j].float() for j in range(J)]
+    slots = _views(mode, J)
+    a_q = torch.einsum("hmd,bhtd->bhtm", W1f, qf)
+    # stage 1, shared by all views: the correction of the hidden preactivation
+    if read_norm_w1:
+        h0 = _activation("relu2", _thresholded(_rmsnorm(a_q, eps)[0], tauf))
+        reads = _scan(h0, h_k, g, True, las)
+        pres = [a_q + reads[s][..., :m] / (reads[s][..., m:] + eps) for s in slots]
+    else:
+        reads = _scan(q, k, g, False, las)
+        pres = [a_q + reads[s] for s in slots]
+    # stage 2, one query per view
+    outs = []
+    for s, pre in zip(slots, pres):
+        hq = _activation(nonlin, _thresholded(_rmsnorm(pre, eps)[0], tauf))
+        base = torch.einsum("hdm,bhtm->bhtd", W2f, hq)
+        c = _scan(hq, h_k, lam, bool(read_norm), [las[s]])[0]
+        mem = c[..., :d] / (c[..., d:] + eps) if read_norm else c
+        outs.append(qf + base + mem)
+    y = outs[0]
+    for j in range(J):
+        y = y + etas[j].float().view(1, -1, 1, 1) * (outs[1 + j] - outs[0])
+    return y

@@ -119,6 +119,11 @@ def _rope(x: torch.Tensor, rot: int, base: float) -> torch.Tensor:
     return torch.cat((rotated, x[..., rot:]), dim=-1)
 
 
+def _l2(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """``x / max(||x||, eps)`` in the input's precision (norms.py:11-12)."""
+    return x / x.norm(dim=-1, keepdim=True).clamp_min(eps)
+
+
 class ThetaScanCore(nn.Module):
     """Parameters and forward of one mixer (reference block.ThetaScan)."""
 
@@ -132,20 +137,22 @@ class ThetaScanCore(nn.Module):
         m = cfg.memory_width
         k = cfg.kernel
         self.n_heads, self.head_dim, self.mem_hidden = H, d, m
-        # Control parameters, in the reference's construction order.
-        if k.kernel_sharpness_mode == "learned_per_head":
+        kernel = cfg.family == "kernel"
+        # Control parameters, in the reference's construction order (the GN
+        # family has none).
+        if kernel and k.kernel_sharpness_mode == "learned_per_head":
             self.kernel_sharpness_raw = nn.Parameter(torch.full((H,), _inverse_softplus(float(k.kernel_sharpness))))
-        elif k.kernel_sharpness_mode == "learned_per_feature":
+        elif kernel and k.kernel_sharpness_mode == "learned_per_feature":
             self.kernel_sharpness_raw = nn.Parameter(
                 torch.full((H, m), _inverse_softplus(float(k.kernel_sharpness))))
         else:
             self.register_parameter("kernel_sharpness_raw", None)
-        self.kernel_score_bias = nn.Parameter(torch.zeros(H, m)) if k.score_bias else None
-        if k.relu2_threshold_mode == "learned_per_head":
+        self.kernel_score_bias = nn.Parameter(torch.zeros(H, m)) if kernel and k.score_bias else None
+        if kernel and k.relu2_threshold_mode == "learned_per_head":
             self.kernel_relu2_threshold = nn.Parameter(torch.zeros(H))
         else:
             self.register_parameter("kernel_relu2_threshold", None)
-        if k.bspline_scale_mode == "learned_per_head":
+        if kernel and k.bspline_scale_mode == "learned_per_head":
             self.bspline_scale_raw = nn.Parameter(torch.full((H,), _inverse_softplus(float(k.bspline_scale))))
         else:
             self.register_parameter("bspline_scale_raw", None)
@@ -166,10 +173,14 @@ class ThetaScanCore(nn.Module):
             self.proj_qkv = nn.Linear(D, 3 * H * d, bias=False)
         self.proj_out = nn.Linear(H * d, D, bias=False)
         # Memory net theta0 (block.py:210-301).
-        projections = m // k.bspline_basis_count if k.feature_map == "projected_bspline" else m
+        projections = m // k.bspline_basis_count if kernel and k.feature_map == "projected_bspline" else m
         self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, projections, d) / math.sqrt(d))])
         self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, m))])
-        self.Wg = None
+        if not kernel and cfg.gn.nonlinearity == "relu2_threshold":
+            # GN learned threshold tau rides the Wg slot (block.py:231-235), zero-init
+            self.Wg = nn.ParameterList([nn.Parameter(torch.zeros(H, m, 1))])
+        else:
+            self.Wg = None
         self.register_buffer("_expansion_fingerprint", None)
         self._expanded = cfg.feature_expansion > 1
         if self._expanded:
@@ -212,6 +223,39 @@ class ThetaScanCore(nn.Module):
         self._rot = _rope_width(d, cfg.rope.mode, cfg.rope.fraction)
 
     # -------------------------------------------------------------- helpers
+
+    def _forward_gn(self, x, shard):
+        """GN family: the per-token write and features in f32 PyTorch, every
+        sequence read on the scan kernels (:mod:`thetascan_b200.gn`)."""
+        from .gn import gn_core
+        if shard is not None:
+            raise NotImplementedError("thetascan_b200: sequence shards of the GN family are not built")
+        B, T, _ = x.shape
+        H, d = self.n_heads, self.head_dim
+        # The write's solve divides by ||k||^2-weighted terms and amplifies
+        # rounding of its inputs (bf16 projections move the input gradient by
+        # ~3%), so projections, q/k preparation and the per-token math stay
+        # f32; only the scan streams are bf16.
+        xf = x.float()
+        q, k, v = self.project(xf)
+        rot, base = self._rot, self.cfg.rope.base
+        q, k = (_l2(_rope(t, rot, base)) for t in (q, k))
+        if self.vmlp_in is not None:
+            v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
+        W1, W2 = self.effective_weights()
+        log_alphas, etas = self.fade()
+        gn = self.cfg.gn
+        y = gn_core(q, k, v, W1, W2, None if self.Wg is None else self.Wg[0],
+                    nonlin="relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity,
+                    read_norm=gn.read_normalization != "none",
+                    read_norm_w1=gn.read_normalization == "both_feature_mass",
+                    log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum")
+        y = y.transpose(1, 2)
+        if self.ogate is not None:
+            lin = self.ogate.g.lin
+            y = y * F.silu(F.linear(xf, lin.weight.float(), lin.bias.float()).view(B, T, H, d))
+        y = F.linear(y.reshape(B, T, H * d), self.proj_out.weight.float())
+        return y.to(x.dtype)
 
     def effective_weights(self):
         """``U W1`` and ``W2 D`` (block.py:546-567)."""
@@ -273,6 +317,8 @@ class ThetaScanCore(nn.Module):
         chunk states of the earlier slices arrive through one exchange."""
         if not x.is_cuda:
             raise RuntimeError("thetascan_b200 requires a CUDA input")
+        if self.cfg.family == "gn":
+            return self._forward_gn(x, shard)
         B, T, _ = x.shape
         H, d = self.n_heads, self.head_dim
         out_dtype = x.dtype
