@@ -49,11 +49,17 @@ CONFIGS = {
     # sum view; with --gpus N the 32K-token sequences are split into N shards.
     "c4": dict(B=4, T=32768, D=1024, H=16, mult=2, expansion=1, fmap="projected_bspline", basis=16,
                rope="partial", J=3, retentions=(0.9, 0.99, 0.999), seqpar=True),
+    # config 3: Gauss-Newton fast weights, head_dim 128, m = 128, relu2, two-stage
+    # feature-mass read (both_feature_mass), one Jacobian step, the plain sum view.
+    "c3": dict(B=8, T=8192, D=1024, H=8, mult=1, expansion=1, family="gn", fmap="relu2",
+               gn_read="both_feature_mass", rope="partial", J=0),
 }
 
 WORKLOADS = {
     "c2": "config 2: ThetaScan-Kernel relu2 ridge m=256 (2x expansion), partial RoPE, 1-branch fast bank, "
           "output gate; fwd+bwd, loss=mean(y^2)",
+    "c3": "config 3: ThetaScan-GN relu2, head_dim 128, m=128, two-stage feature-mass read "
+          "(both_feature_mass), 1 Jacobian step, sum view, output gate; fwd+bwd, loss=mean(y^2)",
     "c4": "config 4: ThetaScan-Kernel projected B-spline (16 basis, m=128), partial RoPE, fast bank "
           "0.9/0.99/0.999 + sum (4 views), output gate, T=32768; sequence-sharded over the GPUs; "
           "fwd+bwd, loss=mean(y^2)",
@@ -63,8 +69,18 @@ WORKLOADS = {
 # --------------------------------------------------------------------------- workload
 
 def build_module(cfg, device):
-    from thetascan_b200.config import KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
+    from thetascan_b200.config import GNConfig, KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
     from thetascan_b200.mixer import ThetaScan
+    if cfg.get("family") == "gn":
+        config = ThetaScanConfig(
+            d_model=cfg["D"], n_heads=cfg["H"], memory_multiplier=cfg["mult"], family="gn",
+            gn=GNConfig(nonlinearity=cfg["fmap"], jacobian_steps=1, read_normalization=cfg["gn_read"]),
+            rope=RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=TemporalConfig(mode="sum"))
+        torch.manual_seed(0)
+        module = ThetaScan(config)
+        with torch.no_grad():
+            module._core.W2[0].normal_(0.0, 0.02)   # a trained-like slow W2 (zero-init makes the write trivial)
+        return module.to(device), config
     kernel = KernelConfig(feature_map=cfg["fmap"], bspline_basis_count=cfg.get("basis", 8))
     if cfg["J"] == 1:
         temporal = TemporalConfig(mode="bank", retention_init=0.95)
@@ -91,10 +107,16 @@ def flops_per_token(cfg):
     forward FLOPs per token)."""
     H, d = cfg["H"], cfg["D"] // cfg["H"]
     m = cfg["mult"] * d
-    P = m // cfg["basis"] if cfg["fmap"] == "projected_bspline" else m
     C, V = 64, 1 + cfg["J"]
-    feature = 4 * P * d + 2 * d * m
-    scan = C * m + V * (C * (d + 1) + 4 * m * (d + 1))
+    if cfg.get("family") == "gn":
+        # GN both_feature_mass: write 10 m d (W1 k, W2 h, W2^2 s^2, W2^T lambda; read W1 q),
+        # stage 1 and stage 2 scans per view, and the stage-2 slow decode 2 d m
+        feature = 10 * m * d
+        scan = C * m + V * (C * (m + 1) + 4 * m * (m + 1) + 2 * d * m + C * m + C * (d + 1) + 4 * m * (d + 1))
+    else:
+        P = m // cfg["basis"] if cfg["fmap"] == "projected_bspline" else m
+        feature = 4 * P * d + 2 * d * m
+        scan = C * m + V * (C * (d + 1) + 4 * m * (d + 1))
     D, Hd = cfg["D"], H * d
     proj = 2 * D * 3 * Hd + 2 * Hd * D + 2 * D * Hd
     core = 3 * H * (feature + scan)
@@ -225,6 +247,10 @@ def bytes_per_token(cfg):
     H, d = cfg["H"], cfg["D"] // cfg["H"]
     m = cfg["mult"] * d
     R = 1 + cfg["J"]
+    if cfg.get("family") == "gn":
+        # stage 1: h0, h, g in, [g|1] f32 out; stage 2: h_q, h, lambda in, [lambda|1] f32 out
+        fwd = H * R * ((3 * m) * 2 + (m + 1) * 4 + (2 * m + d) * 2 + (d + 1) * 4)
+        return {"ts_b200_scan_fwd": fwd, "ts_b200_scan_bwd": 2 * fwd}
     return {
         "ts_b200_feature_fwd": H * (2 * d * 2 + 2 * m * 2 + d * 4),               # q,k in; phi q,k, y0 out
         "ts_b200_feature_bwd": H * (2 * d * 2 + 2 * m * 2 + d * 2 + 2 * d * 2),   # q,k, dphi q,k, dy in; dq,dk out
