@@ -31,6 +31,58 @@ import torch.nn.functional as F
 from .scan import _ScanViews
 
 
+class _tf32:
+    """TF32 tensor-core GEMMs for f32 matmuls inside the block (10-bit
+    mantissa operands, f32 accumulation), restoring the caller's setting."""
+
+    def __enter__(self):
+        self.saved = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.saved
+
+
+class _PerToken(torch.autograd.Function):
+    """``fn(*tensors)`` with TF32 GEMMs in the forward and in the backward,
+    which recomputes ``fn`` under autograd (the per-token GN math is cheap next
+    to its f32 SIMT GEMMs, and recomputation keeps nothing but the inputs)."""
+
+    @staticmethod
+    def forward(ctx, fn, *tensors):
+        ctx.fn = fn
+        ctx.save_for_backward(*tensors)
+        with _tf32(), torch.no_grad():
+            out = fn(*tensors)
+        ctx.single = torch.is_tensor(out)
+        return out
+
+    @staticmethod
+    def backward(ctx, *grads):
+        inputs = [t.detach().requires_grad_(t.requires_grad) for t in ctx.saved_tensors]
+        with _tf32(), torch.enable_grad():
+            out = ctx.fn(*inputs)
+        outs = [out] if ctx.single else list(out)
+        pairs = [(o, g) for o, g in zip(outs, grads) if g is not None and o.requires_grad]
+        wanted = [t for t in inputs if t.requires_grad]
+        got = torch.autograd.grad([o for o, _ in pairs], wanted, [g for _, g in pairs], allow_unused=True) \
+            if pairs and wanted else [None] * len(wanted)
+        it = iter(got)
+        return (None, *[next(it) if t.requires_grad else None for t in inputs])
+
+
+def per_token(fn, *tensors):
+    """Run the per-token block ``fn`` on TF32 tensor cores (see _PerToken)."""
+    return _PerToken.apply(fn, *tensors)
+
+
+def per_token_f32(fn, *tensors):
+    """The same block in full f32: the write's solve and the features, whose
+    gradients (the log-retention one above all, a long sum over tokens) move
+    by ~2% when their operands are rounded to TF32."""
+    return fn(*tensors)
+
+
 def _activation(nonlin, pre):
     if nonlin == "relu2":
         r = F.relu(pre)
@@ -126,24 +178,37 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
     qf, kf, vf = q.float(), k.float(), v.float()
     W1f, W2f = W1.float(), W2.float()
     tauf = None if tau is None else tau.float()
-    h_k, g, lam = gn_write(kf, vf, W1f, W2f, tauf, nonlin, eps)
+    extra = () if tauf is None else (tauf,)
+
+    def write(kk, vv, w1, w2, *t):
+        return gn_write(kk, vv, w1, w2, t[0] if t else None, nonlin, eps)
+
+    h_k, g, lam = per_token_f32(write, kf, vf, W1f, W2f, *extra)
     J = 0 if log_alphas is None else log_alphas.shape[0]
     las = [None] + [log_alphas[j].float() for j in range(J)]
     slots = _views(mode, J)
-    a_q = torch.einsum("hmd,bhtd->bhtm", W1f, qf)
+
+    def query_pre(qq, w1, *t):
+        a = torch.einsum("hmd,bhtd->bhtm", w1, qq)
+        return a, _activation("relu2", _thresholded(_rmsnorm(a, eps)[0], t[0] if t else None))
+
+    a_q, h0 = per_token_f32(query_pre, qf, W1f, *extra)
     # stage 1, shared by all views: the correction of the hidden preactivation
     if read_norm_w1:
-        h0 = _activation("relu2", _thresholded(_rmsnorm(a_q, eps)[0], tauf))
         reads = _scan(h0, h_k, g, True, las)
         pres = [a_q + reads[s][..., :m] / (reads[s][..., m:] + eps) for s in slots]
     else:
         reads = _scan(q, k, g, False, las)
         pres = [a_q + reads[s] for s in slots]
+
+    def features(pre, w2, *t):
+        hq = _activation(nonlin, _thresholded(_rmsnorm(pre, eps)[0], t[0] if t else None))
+        return hq, torch.einsum("hdm,bhtm->bhtd", w2, hq)
+
     # stage 2, one query per view
     outs = []
     for s, pre in zip(slots, pres):
-        hq = _activation(nonlin, _thresholded(_rmsnorm(pre, eps)[0], tauf))
-        base = torch.einsum("hdm,bhtm->bhtd", W2f, hq)
+        hq, base = per_token_f32(features, pre, W2f, *extra)
         c = _scan(hq, h_k, lam, bool(read_norm), [las[s]])[0]
         mem = c[..., :d] / (c[..., d:] + eps) if read_norm else c
         outs.append(qf + base + mem)

@@ -119,6 +119,13 @@ def _rope(x: torch.Tensor, rot: int, base: float) -> torch.Tensor:
     return torch.cat((rotated, x[..., rot:]), dim=-1)
 
 
+def _set_param(module: nn.Module, name: str, value) -> None:
+    """Point ``module.<name>`` (dotted) at ``value`` without registering it."""
+    owner, _, leaf = name.rpartition(".")
+    target = module.get_submodule(owner) if owner else module
+    target._parameters[leaf] = value
+
+
 def _l2(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """``x / max(||x||, eps)`` in the input's precision (norms.py:11-12)."""
     return x / x.norm(dim=-1, keepdim=True).clamp_min(eps)
@@ -236,10 +243,26 @@ class ThetaScanCore(nn.Module):
         # rounding of its inputs (bf16 projections move the input gradient by
         # ~3%), so projections, q/k preparation and the per-token math stay
         # f32; only the scan streams are bf16.
+        from .gn import per_token
         xf = x.float()
-        q, k, v = self.project(xf)
+        names = [n for n, _ in self.named_parameters() if n.startswith("proj_") or n == "kq_bias"]
+        params = dict(self.named_parameters())
         rot, base = self._rot, self.cfg.rope.base
-        q, k = (_l2(_rope(t, rot, base)) for t in (q, k))
+
+        def qkv(xx, *ws):
+            # the module's projection with its weights passed in (so that the
+            # TF32 recomputation differentiates them)
+            saved = {n: params[n] for n in names}
+            try:
+                for n, w in zip(names, ws):
+                    _set_param(self, n, w)
+                q, k, v = self.project(xx)
+            finally:
+                for n in names:
+                    _set_param(self, n, saved[n])
+            return _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base)), v.contiguous()
+
+        q, k, v = per_token(qkv, xf, *[params[n] for n in names])
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         W1, W2 = self.effective_weights()
@@ -251,10 +274,14 @@ class ThetaScanCore(nn.Module):
                     read_norm_w1=gn.read_normalization == "both_feature_mass",
                     log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum")
         y = y.transpose(1, 2)
-        if self.ogate is not None:
-            lin = self.ogate.g.lin
-            y = y * F.silu(F.linear(xf, lin.weight.float(), lin.bias.float()).view(B, T, H, d))
-        y = F.linear(y.reshape(B, T, H * d), self.proj_out.weight.float())
+
+        def out(yy, xx, w_out, *gate):
+            if gate:
+                yy = yy * F.silu(F.linear(xx, gate[0], gate[1]).view(B, T, H, d))
+            return F.linear(yy.reshape(B, T, H * d), w_out)
+
+        gate = () if self.ogate is None else (self.ogate.g.lin.weight, self.ogate.g.lin.bias)
+        y = per_token(out, y, xf, self.proj_out.weight, *gate)
         return y.to(x.dtype)
 
     def effective_weights(self):
