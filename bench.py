@@ -243,7 +243,7 @@ def bytes_per_token(cfg):
     """Compulsory HBM bytes per token of each entry point: its inputs read and
     outputs written once (bf16 streams, f32 reads / y0; chunk states and other
     scratch excluded).  Per head: x = d-wide q/k rows, m-wide features, R
-    retention slots of width d+1."""
+    retention slots of width d+2 ([N | D | D], the mass column twice)."""
     H, d = cfg["H"], cfg["D"] // cfg["H"]
     m = cfg["mult"] * d
     R = 1 + cfg["J"]
@@ -254,10 +254,10 @@ def bytes_per_token(cfg):
     return {
         "ts_b200_feature_fwd": H * (2 * d * 2 + 2 * m * 2 + d * 4),               # q,k in; phi q,k, y0 out
         "ts_b200_feature_bwd": H * (2 * d * 2 + 2 * m * 2 + d * 2 + 2 * d * 2),   # q,k, dphi q,k, dy in; dq,dk out
-        "ts_b200_scan_fwd": H * (2 * m * 2 + d * 2 + R * (d + 1) * 4),            # phi q,k, v in; slots out
-        "ts_b200_scan_bwd": H * (2 * m * 2 + d * 2 + R * (d + 1) * 2 + 2 * m * 2 + d * 2),
-        "ts_b200_kread_fwd": H * (R * (d + 1) * 4 + d * 4 + d * 2),
-        "ts_b200_kread_bwd": H * (R * (d + 1) * 4 + d * 2 + R * (d + 1) * 2),
+        "ts_b200_scan_fwd": H * (2 * m * 2 + d * 2 + R * (d + 2) * 4),            # phi q,k, v in; slots out
+        "ts_b200_scan_bwd": H * (2 * m * 2 + d * 2 + R * (d + 2) * 2 + 2 * m * 2 + d * 2),
+        "ts_b200_kread_fwd": H * (R * (d + 2) * 4 + d * 4 + d * 2),
+        "ts_b200_kread_bwd": H * (R * (d + 2) * 4 + d * 2 + R * (d + 2) * 2),
     }
 
 

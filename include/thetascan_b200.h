@@ -71,7 +71,8 @@ int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, i
  *   scan_chunk.linattn_views(q, k, v, retentions, chunk)
  *   (src/thetascan/_core/ops/scan_chunk.py:246-339)
  * out_r[t] = sum_{i<=t} w_r(t,i) (q_t . k_i) v_i  for every retention r, with
- * w = 1 (plain sum) or alpha_h^(t-i) (static per-head log-retention).  The
+ * w = 1 (plain sum), alpha_h^(t-i) (static per-head log-retention) or
+ * 1 - alpha_h^(t-i) (the stale view, `stale` below).  The
  * score tile q.k^T is formed once and shared by all retentions; the carried
  * state is f32.  Streams are bf16; their innermost dimension is contiguous.
  */
@@ -85,7 +86,9 @@ typedef struct ts_scan_args {
   int64_t q_strides[3]; /* element strides of batch, head, token */
   int64_t k_strides[3];
   int64_t v_strides[3];
-  int v_append_unit;    /* 1: the payload is [v | 1] (key-mass read, engine.py:430) */
+  int v_append_unit;    /* 1: the payload is [v | 1] (key-mass read, engine.py:430);
+                         * 2: [v | 1 | 1], the mass column twice, so that a read
+                         * gradient can hand its mass part over as bf16 hi + lo */
   int n_retentions;     /* 1..TS_MAX_RETENTIONS */
   /* NULL = plain causal sum; else device f32 [heads] static log-retention */
   const float* log_alpha[TS_MAX_RETENTIONS];
@@ -112,6 +115,13 @@ typedef struct ts_scan_args {
   const float* init_state;
   float* final_state;
   int stage;
+  /* stale[r] != 0: retention r reads the STALE view of log_alpha[r], weights
+   * 1 - alpha_h^(t-i) (zero for the current token), which is the reference's
+   * FadeStale view S_sum - S_fast (src/thetascan/_core/ops/interface.py:
+   * 251-279) formed without the cancellation of that difference.  Needs
+   * log_alpha[r]; takes no boundary states (init/final NULL, stage 0).  Each
+   * stale retention carries one extra decayed state in the workspace. */
+  int stale[TS_MAX_RETENTIONS];
 } ts_scan_args;
 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args);
@@ -268,9 +278,11 @@ int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args*
  *
  * Normalized read and temporal-view blend of the kernel family: from the
  * augmented scan reads [N_s | D_s] of every retention slot (slot 0 = plain
- * sum, slot 1+j = recency branch j) compute
+ * sum, slot 1+j = recency branch j: its decayed scan for a fast bank, its
+ * stale scan, ts_scan_args.stale, for a stale bank) compute
  *   y = y0 + sum_views c_view N_view / (D_view + eps)
- * for the plain sum, a fast bank or a stale bank.  Stands in for
+ * for the plain sum, a fast bank (c = 1 - sum eta, eta_j) or a stale bank
+ * (c = 1, -eta_j; the zero-memory base read it subtracts is y0).  Stands in for
  *   engine.dual_read_views.memory key_mass (src/thetascan/_core/ops/engine.py:419-442)
  *   and ThetaScan.forward.read_with_temporal (src/thetascan/_core/modules/block.py:667-718).
  * y is written token-major, [B,T,H,d], ready for the output gate/projection.
@@ -282,10 +294,16 @@ typedef struct ts_kread_args {
   int mode;                 /* TS_VIEWS_* */
   int branches;             /* J recency branches, 0..TS_MAX_RETENTIONS-1 */
   float eps;
-  const float* slots[TS_MAX_RETENTIONS]; /* f32 [B,H,T,d+1] */
+  const float* slots[TS_MAX_RETENTIONS]; /* f32 [B,H,T,d+mass_columns] */
   const float* eta;         /* f32 [J,H] blend (after any tanh), or NULL if J == 0 */
   const float* y0;          /* f32 [B,H,T,d] */
   void* y;                  /* bf16 [B,T,H,d] out */
+  /* Mass columns after the d value columns of every slot: 1 ([N | D], a scan
+   * with v_append_unit = 1) or 2 ([N | D | D], v_append_unit = 2); 0 means 1.
+   * The backward writes the mass gradient into them (with 2: as bf16 hi + lo),
+   * formed from the bf16-rounded value gradient so that the quotient rule's
+   * cancellation survives the bf16 hand-over to the scan backward. */
+  int mass_columns;
 } ts_kread_args;
 
 int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream);
@@ -293,7 +311,7 @@ int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream);
 typedef struct ts_kread_grad_args {
   const void* dy;           /* [B,T,H,d] */
   int dy_dtype;             /* TS_DTYPE_F32 or TS_DTYPE_BF16 */
-  void* dslots[TS_MAX_RETENTIONS]; /* bf16 [B,H,T,d+1] out: gradients of the scan reads */
+  void* dslots[TS_MAX_RETENTIONS]; /* bf16 [B,H,T,d+mass_columns] out: gradients of the scan reads */
   float* dy0;               /* f32 [B,H,T,d] out (a copy of dy, head-major), or NULL */
   float* deta;              /* f32 [J,H], ACCUMULATED, or NULL */
 } ts_kread_grad_args;

@@ -40,8 +40,19 @@ CASES = {
     # per-feature controls: score bias with a threshold, per-feature sharpness with a bias
     "relu2_bias_threshold": ("relu2_ridge", 128, 1, "fast", 1, 1, 2, 200, 64),
     "softmax_feature_gain_bias": ("softmax_partition", 64, 1, "sum", 0, 1, 2, 150, 64),
+    # stale banks: slots 1..J are stale scans (weights 1 - alpha^(t-i))
+    "relu2_m256_stale": ("relu2_ridge", 256, 1, "stale", 1, 2, 2, 300, 64),
+    "softmax_m64_stale2": ("softmax_partition", 64, 1, "stale", 2, 1, 2, 257, 64),
+    "bspline_p8x16_stale3": ("projected_bspline", 8, 16, "stale", 3, 1, 2, 384, 64),
 }
 WITH_BIAS = {"relu2_bias_threshold", "softmax_feature_gain_bias"}
+# The stale view's log-retention gradient of this case is small by
+# cancellation (-1.8 against terms of ~30-50 in the fast cases): rounding the
+# read gradient handed to the scan to bf16 -- and nothing else -- moves the
+# float64 value by 2.3% (tests/test_conditioning.py), so no bf16 hand-over can
+# meet 2e-2 on it.  Its outputs and every other gradient are checked; the
+# stale log-retention gradient is checked on the other stale cases.
+ILL_CONDITIONED_RETENTION = {"relu2_m256_stale"}
 
 
 def _case_tensors(name):
@@ -119,21 +130,24 @@ def test_kernel_core_matches_oracle_forward_and_backward(dev, name):
     pairs = [("q", gq, oq), ("k", gk, ok_), ("v", gv, ov), ("W1", gW1, oW1), ("W2", gW2, oW2)]
     pairs += [(key, gctl[key], octl[key]) for key in ctl]
     if las is not None:
-        pairs += [("log_alpha", gla, ola), ("eta", geta, oeta)]
+        pairs += [("eta", geta, oeta)]
+        if name not in ILL_CONDITIONED_RETENTION:
+            pairs += [("log_alpha", gla, ola)]
     for label, got, ref in pairs:
         assert rel_err(got.grad, ref.grad) < BF16_TOL, label
 
 
-def test_stale_bank_is_rejected_explicitly(dev):
-    """The stale view is not implemented on the GPU path yet; it must raise,
-    never silently compute a low-precision difference of scans."""
-    from thetascan_b200.kernel import KernelSpec, kernel_core
-    q = torch.zeros(1, 2, 8, 64, dtype=torch.bfloat16, device=dev)
+def test_stale_bank_sequence_shards_are_rejected(dev):
+    """Stale scans take no boundary states, so a sharded stale bank must raise
+    rather than drop the earlier shards' memory."""
+    from thetascan_b200.kernel import KernelSpec, kernel_core_sharded
+    from thetascan_b200.seqpar import SeqShard
+    qkv = torch.zeros(1, 8, 3 * 2 * 64, dtype=torch.bfloat16, device=dev)
     W1 = torch.zeros(2, 64, 64, device=dev)
-    W2 = torch.zeros(2, 64, 64, device=dev)
     with pytest.raises(NotImplementedError):
-        kernel_core(q, q, q, W1, W2, KernelSpec(kind="softmax_partition", mode="stale"),
-                    log_alphas=torch.zeros(1, 2, device=dev), etas=torch.zeros(1, 2, device=dev))
+        kernel_core_sharded(qkv, 2, W1, W1, KernelSpec(kind="softmax_partition", mode="stale"), None,
+                            SeqShard(0, 1, lambda u: [u]), log_alphas=torch.zeros(1, 2, device=dev),
+                            etas=torch.zeros(1, 2, device=dev))
 
 
 PROLOGUE_CASES = {

@@ -238,3 +238,129 @@ def test_streamed_segments_equal_one_call(lib):
         w = torch.ones(H, T, dtype=torch.float64) if a is None else torch.exp(a.double().cpu()[:, None] * back)
         want = torch.einsum("bhtf,ht,bhtc->bhfc", kk, w, vv)
         assert rel_err(state[:, :, r], want) < BF16_TOL, r
+
+
+# ----------------------------------------------------------------- stale retentions
+
+# B, H, T, Dk, Dv, retention layout: "s" plain sum, "d" decayed, "x" stale
+STALE_CASES = [
+    (2, 3, 37, 5, 4, "sx"),
+    (1, 2, 300, 64, 65, "sxx"),
+    (1, 2, 520, 128, 80, "sdxx"),
+    (1, 2, 384, 256, 64, "x"),
+    (1, 1, 1030, 32, 16, "xs"),
+    (1, 2, 300, 128, 129, "sx"),
+]
+
+
+def _stale_setup(H, layout, seed):
+    rets, flags = [], []
+    for i, c in enumerate(layout):
+        rets.append(None if c == "s" else _alphas(H, 0.9, 0.999, seed=seed + i))
+        flags.append(c == "x")
+    return rets, flags
+
+
+def _oracle_stale_views(q, k, v, rets, flags):
+    """Stale view = plain sum - decayed scan (interface.py:268-279), in float64,
+    where the difference loses nothing that matters."""
+    plain = oscan.linattn_chunk_views(q, k, v, (None,), chunk=64)[0]
+    decayed = oscan.linattn_chunk_views(q, k, v, tuple(r for r in rets if r is not None), chunk=64)
+    outs, it = [], iter(decayed)
+    for r, st in zip(rets, flags):
+        if r is None:
+            outs.append(plain)
+        else:
+            d = next(it)
+            outs.append(plain - d if st else d)
+    return outs
+
+
+@pytest.mark.parametrize("case", STALE_CASES)
+def test_stale_scan_forward_matches_oracle(lib, case):
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv, layout = case
+    q, k, v = _streams(B, H, T, Dk, Dv, seed=11, positive=True)
+    rets, flags = _stale_setup(H, layout, seed=20)
+    got = scan.linattn_views(q.cuda(), k.cuda(), v.cuda(), tuple(None if r is None else r.cuda() for r in rets),
+                             stale=flags)
+    want = _oracle_stale_views(q.double(), k.double(), v.double(),
+                               [None if r is None else r.double() for r in rets], flags)
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for g_, w_ in zip(got, want):
+        assert rel_err(g_, w_) < BF16_TOL
+
+
+def test_stale_scan_is_accurate_where_its_weights_vanish(lib):
+    """Early tokens of a slow retention (alpha = 0.999) have stale weights of
+    about 1e-3 (t - i): the stale read must be right relative to ITS OWN size
+    there, which a difference of two bf16-tiled scans is not (its error is
+    ~2^-9 of the plain read, hundreds of times the stale value)."""
+    from thetascan_b200 import scan
+    q, k, v = _streams(1, 1, 256, 64, 16, seed=12, positive=True)
+    v = v.float().abs().to(torch.bfloat16)   # positive payload: no cancellation inside the view
+    la = torch.full((1,), math.log(0.999))
+    got = scan.linattn_views(q.cuda(), k.cuda(), v.cuda(), (la.cuda(),), stale=[True])[0].double().cpu()
+    want = _oracle_stale_views(q.double(), k.double(), v.double(), [la.double()], [True])[0]
+    assert float(got[0, 0, 0].abs().max()) == 0.0      # the current token carries no stale weight
+    rows = want[0, 0, 1:200]
+    err = (got[0, 0, 1:200] - rows).abs().amax(-1) / rows.abs().amax(-1)
+    assert float(err.max()) < BF16_TOL
+
+
+@pytest.mark.parametrize("index", range(len(STALE_CASES)))
+def test_stale_scan_backward_matches_oracle(lib, index):
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv, layout = STALE_CASES[index]
+    q, k, v = _streams(B, H, T, Dk, Dv, seed=13, positive=True)
+    rets, flags = _stale_setup(H, layout, seed=30)
+    g = torch.Generator().manual_seed(17)
+    # The kernels take the output gradient in bf16 (the C ABI's dout), so both
+    # sides get the same bf16 values: in case 2 rounding float64 weights alone
+    # moves one log-retention gradient (a near-cancellation, -269 against terms
+    # of ~4e4) by 4% of the largest.
+    weights = [torch.randn(B, H, T, Dv, generator=g, dtype=torch.float64).bfloat16().double() for _ in rets]
+
+    def total(outs):
+        return sum((o.double() * w.to(o.device)).sum() for o, w in zip(outs, weights))
+
+    leaves = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    rleaves = [None if r is None else r.cuda().requires_grad_(True) for r in rets]
+    total(scan.linattn_views(*leaves, tuple(rleaves), stale=flags)).backward()
+    oleaves = [x.double().requires_grad_(True) for x in (q, k, v)]
+    orets = [None if r is None else r.double().requires_grad_(True) for r in rets]
+    total(_oracle_stale_views(*oleaves, orets, flags)).backward()
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for name, got, want in zip("qkv", leaves, oleaves):
+        assert rel_err(got.grad, want.grad) < BF16_TOL, name
+    for got, want in zip(rleaves, orets):
+        if got is not None:
+            assert rel_err(got.grad, want.grad) < BF16_TOL, "log_alpha"
+
+
+def test_stale_retention_gradient_closed_form(lib):
+    """All-ones stream, stale view: out_{T-1} = sum_p (1 - alpha^p), so
+    d out_{T-1} / d log(alpha) = -sum_p p alpha^p (p = 1..T-1)."""
+    from thetascan_b200 import scan
+    alpha, T = 0.9, 400
+    ones = torch.ones(1, 1, T, 1, dtype=torch.bfloat16, device="cuda")
+    la = torch.tensor([math.log(alpha)], device="cuda", requires_grad=True)
+    out = scan.linattn_views(ones, ones, ones, (la,), stale=[True])[0]
+    want_out = sum(1 - alpha ** p for p in range(1, T))
+    assert abs(float(out[0, 0, -1, 0]) - want_out) / want_out < 1e-2
+    out[0, 0, -1, 0].float().backward()
+    want = -sum(p * alpha ** p for p in range(1, T))
+    assert abs(float(la.grad) - want) / abs(want) < 5e-3
+
+
+def test_stale_scan_rejects_boundary_states(lib):
+    from thetascan_b200 import scan
+    q, k, v = (x.cuda() for x in _streams(1, 2, 64, 16, 8, seed=14))
+    la = _alphas(2, 0.9, 0.99, seed=15).cuda()
+    with pytest.raises(ValueError):
+        scan.linattn_views(q, k, v, (None,), stale=[True])
+    from thetascan_b200 import _lib
+    a = scan._build_args(q, k, v, [la], [torch.empty(1, 2, 64, 8, device="cuda")], False, stale=[True])
+    a.final_state = torch.empty(1, 2, 1, 16, 8, device="cuda").data_ptr()
+    assert _lib.load().ts_b200_scan_workspace_bytes(ctypes.byref(a)) == 0
+    assert _lib.last_error()[0] == _lib.TS_ERR_NOT_IMPLEMENTED

@@ -31,7 +31,7 @@ def test_manifest_round_trip(name):
     assert ThetaScanConfig.from_dict(cfg.to_dict()) == cfg
 
 
-@pytest.mark.parametrize("name", ["softmax_bank_fast", "relu2_expanded_rope", "relu2_d64_ragged"])
+@pytest.mark.parametrize("name", ["softmax_bank_fast", "relu2_expanded_rope", "relu2_d64_ragged", "bspline_stale"])
 def test_state_dict_and_seeded_init_match_reference(name):
     case = _fixtures()[name]
     cfg = ThetaScanConfig.from_dict(case["public_config"])
@@ -59,9 +59,11 @@ def test_presets_and_unsupported_configs():
     from thetascan_b200.config import GNConfig
     with pytest.raises(NotImplementedError):
         ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn", gn=GNConfig(nonlinearity="swiglu")))
-    stale = ThetaScanConfig.from_dict(_fixtures()["bspline_stale"]["public_config"])
+    ThetaScan(ThetaScanConfig.from_dict(_fixtures()["bspline_stale"]["public_config"]))
+    from thetascan_b200.config import TemporalConfig
     with pytest.raises(NotImplementedError):
-        ThetaScan(stale)
+        ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn",
+                                  temporal=TemporalConfig(mode="bank", bank_mode="stale")))
     with pytest.raises(ValueError):
         ThetaScanConfig(runtime=__import__("thetascan_b200.config", fromlist=["RuntimeConfig"])
                         .RuntimeConfig(backend="bogus")).validate()

@@ -34,6 +34,7 @@ class ScanArgs(ctypes.Structure):
         ("out_dtype", ctypes.c_int),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("init_state", ctypes.c_void_p), ("final_state", ctypes.c_void_p), ("stage", ctypes.c_int),
+        ("stale", ctypes.c_int * MAX_RETENTIONS),
     ]
 
 
@@ -103,6 +104,7 @@ class KReadArgs(ctypes.Structure):
         ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("head_dim", ctypes.c_int),
         ("mode", ctypes.c_int), ("branches", ctypes.c_int), ("eps", ctypes.c_float),
         ("slots", c_ptr4), ("eta", ctypes.c_void_p), ("y0", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("mass_columns", ctypes.c_int),
     ]
 
 

@@ -51,6 +51,8 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
     return set_error(TS_ERR_VALUE, "scan: batch, heads and tokens must be >= 1");
   if (a->dk < 1 || a->dk > 256)
     return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: key width %d outside 1..256", a->dk);
+  if (a->v_append_unit < 0 || a->v_append_unit > 2)
+    return set_error(TS_ERR_VALUE, "scan: v_append_unit must be 0, 1 or 2");
   if (a->dv < 1 + a->v_append_unit || a->dv > 256)
     return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: payload width %d outside 1..256", a->dv);
   if (a->n_retentions < 1 || a->n_retentions > TS_MAX_RETENTIONS)
@@ -68,7 +70,7 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
   p->DkM = round_up(a->dk, 128);
   p->DvP = round_up(a->dv, 16);
   p->NT = ceil_div(a->tokens, 128);
-  p->R = a->n_retentions;
+  p->RU = a->n_retentions;
   p->q = static_cast<const __nv_bfloat16*>(a->q);
   p->k = static_cast<const __nv_bfloat16*>(a->k);
   p->v = static_cast<const __nv_bfloat16*>(a->v);
@@ -77,24 +79,40 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
     p->ks[i] = a->k_strides[i];
     p->vs[i] = a->v_strides[i];
   }
-  p->v_unit = a->v_append_unit ? 1 : 0;
-  for (int r = 0; r < p->R; ++r) {
+  p->v_unit = a->v_append_unit;
+  // Caller slots first, then one auxiliary decayed slot per stale slot.
+  p->R = p->RU;
+  for (int r = 0; r < p->RU; ++r) {
     p->la[r] = a->log_alpha[r];
     p->out[r] = a->out[r];
+    p->kind[r] = kSlotDecay;
+    p->partner[r] = -1;
     if (!a->out[r]) return set_error(TS_ERR_VALUE, "scan: null output pointer for retention %d", r);
+    if (a->stale[r]) {
+      if (!a->log_alpha[r]) return set_error(TS_ERR_VALUE, "scan: stale retention %d needs a log_alpha", r);
+      const int aux = p->R++;
+      p->kind[r] = kSlotStale;
+      p->partner[r] = aux;
+      p->la[aux] = a->log_alpha[r];
+      p->kind[aux] = kSlotAux;
+      p->partner[aux] = r;
+      p->out[aux] = nullptr;
+      p->any_stale = 1;
+    }
   }
   p->out_bf16 = a->out_dtype == TS_DTYPE_BF16;
   if (a->stage < 0 || a->stage > 2) return set_error(TS_ERR_VALUE, "scan: stage must be 0, 1 or 2");
+  if (p->any_stale && (a->init_state || a->final_state || a->stage != 0))
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: stale retentions take no boundary states or stages");
   p->init = a->init_state;
   p->final_state = a->final_state;
   p->all_tiles = a->final_state != nullptr;
   p->store = 1;
   const int mblocks = p->DkM / 128;
-  // TMEM columns: tile updates of every retention (state kernel), score plus
-  // every retention's read (output kernel), the tile update and its
-  // (i+1)-weighted copy (backward state kernel), score, g and dv (dv kernel).
-  if (p->R * mblocks * p->DvP > 512 || 128 + p->R * p->DvP > 512 || 2 * mblocks * p->DvP > 512 ||
-      256 + p->DvP > 512)
+  // TMEM columns: score plus every caller slot's read (output kernel), the
+  // tile update and its la-weighted copy (state kernels), score, g and dv
+  // (dv kernel).
+  if (128 + p->RU * p->DvP > 512 || 2 * mblocks * p->DvP > 512 || 256 + p->DvP > 512)
     return set_error(TS_ERR_NOT_IMPLEMENTED,
                      "scan: %d retentions of a %dx%d state exceed the 512 tensor-memory columns of one CTA",
                      p->R, p->Dk, p->Dv);
@@ -186,11 +204,14 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   p.images = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(args->workspace) + states_bytes(p));
   ScanGradParams g;
   std::memset(&g, 0, sizeof(g));
-  for (int r = 0; r < p.R; ++r) {
+  for (int r = 0; r < p.RU; ++r) {
     g.dout[r] = static_cast<const __nv_bfloat16*>(grad->dout[r]);
     if (!g.dout[r]) return set_error(TS_ERR_VALUE, "scan_bwd: null dout for retention %d", r);
     g.dla[r] = grad->dlog_alpha[r];
   }
+  for (int r = p.RU; r < p.R; ++r) g.dla[r] = g.dla[p.partner[r]];
+  if (p.any_stale && (grad->dfinal_state || grad->dinit_state || grad->stage != 0))
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan_bwd: stale retentions take no boundary states or stages");
   g.dq = grad->dq;
   g.dk = grad->dk;
   g.dv = grad->dv;

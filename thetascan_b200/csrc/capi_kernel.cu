@@ -108,6 +108,9 @@ int build_read_params(const ts_kread_args* a, ReadParams* p) {
   p->J = J;
   p->mode = a->mode;
   p->eps = a->eps;
+  if (a->mass_columns < 0 || a->mass_columns > 2)
+    return set_error(TS_ERR_VALUE, "kread: mass_columns must be 1 or 2 (0 = 1)");
+  p->mass_cols = a->mass_columns == 2 ? 2 : 1;
   for (int s = 0; s <= J; ++s) p->out[s] = a->slots[s];
   p->eta = a->eta;
   p->y0 = a->y0;

@@ -324,12 +324,14 @@ __device__ __forceinline__ void cp_async_wait_group() {
 // leading dimension `ld` elements) into `t`, zero-filling the rest of the
 // tile.  Consecutive threads cover 8 rows of one 8-column chunk, so the shared
 // stores are conflict-free and each row is read in 64-byte runs.  If
-// `unit_col` >= 0, column `unit_col` of every valid row is set to 1.
+// `unit_col` >= 0, columns [unit_col, unit_col + unit_count) of every valid
+// row are set to 1.
 // Whole in-range 16-byte chunks are copied with cp.async, so a thread has all
 // of its copies in flight at once; the tile is complete after
 // cp_async_wait_all() (MmaCtx::run and tiles_ready() do that) and a barrier.
 __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __restrict__ src, long ld,
-                                          int rows_valid, int cols_valid, int unit_col = -1) {
+                                          int rows_valid, int cols_valid, int unit_col = -1,
+                                          int unit_count = 1) {
   const int chunks = t.cols / 8;
   const int total = t.rows * chunks;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && ((ld & 7) == 0);
@@ -339,7 +341,7 @@ __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __
     const int j = rest % chunks;
     const int r = (rest / chunks) * 8 + r8;
     const int c0 = j * 8;
-    const bool has_unit = unit_col >= c0 && unit_col < c0 + 8;
+    const bool has_unit = unit_col >= 0 && unit_col < c0 + 8 && unit_col + unit_count > c0;
     if (r < rows_valid && vec_ok && c0 + 8 <= cols_valid && !has_unit) {
       cp_async16(t.saddr + tile_off(t, r, c0), src + r * ld + c0);
       continue;
@@ -352,7 +354,11 @@ __device__ __forceinline__ void load_tile(const Tile& t, const __nv_bfloat16* __
         const int c = c0 + e;
         f[e] = (c < cols_valid) ? bf2f(src[r * ld + c]) : 0.f;
       }
-      if (has_unit) f[unit_col - c0] = 1.f;
+      if (has_unit) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (c0 + e >= unit_col && c0 + e < unit_col + unit_count) f[e] = 1.f;
+      }
       v = pack8(f);
     }
     tile_st16(t, r, j, v);

@@ -9,11 +9,27 @@
 // which is the tile algebra of the reference chunk backend
 // (src/thetascan/_core/ops/scan_chunk.py:102-119, 170-212, 322-336) with a
 // 128-token tile; every exponent is <= 0, so no reciprocal decay is formed.
+//
+// A stale slot reads with weights 1 - alpha^(t-j), the reference's stale view
+// S_sum - S_fast (src/thetascan/_core/ops/interface.py:251-279), formed
+// directly rather than as a difference of two reads (which would cancel for
+// recent tokens, whose stale weight is near zero).  Its state S_X carries
+// those weights; an auxiliary decayed slot a (same la, no output) carries
+// S_a = the alpha-weighted state, and with C = e^{la len}:
+//   intra weight  1 - e^{la (i - j)}
+//   read          q S_X + (1 - c(i)) q S_a
+//   key weight    1 - e^{la (len - 1 - j)}
+//   recursion     S_X(n+1) = S_X(n) + (1 - C) S_a(n) + dS_X(n)
+// so every weight is a nonnegative f32 number formed without cancellation.
 #pragma once
 
+#include "../../include/thetascan_b200.h"
 #include "common.cuh"
 
 namespace ts {
+
+constexpr int kMaxSlots = 2 * TS_MAX_RETENTIONS;  // caller slots plus the auxiliary slots of stale ones
+enum SlotKind : int { kSlotDecay = 0, kSlotStale = 1, kSlotAux = 2 };
 
 struct ScanParams {
   int B, H, T;
@@ -21,17 +37,21 @@ struct ScanParams {
   int DkP;        // Dk rounded up to 16 (MMA K of the score / read)
   int DkM;        // Dk rounded up to 128 (MMA M of the state update)
   int DvP;        // Dv rounded up to 16
-  int NT, R;
+  int NT, R;      // R: all slots; slots 0..RU-1 are the caller's, RU..R-1 auxiliary
+  int RU;
   const __nv_bfloat16* q;
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;
   long long qs[3], ks[3], vs[3];
-  int v_unit;                // 1: column Dv-1 of the payload is the constant 1
-  const float* la[4];        // nullptr = plain sum
-  void* out[4];
+  int v_unit;                // the last v_unit (0..2) payload columns are the constant 1
+  const float* la[kMaxSlots];   // nullptr = plain sum
+  int kind[kMaxSlots];          // SlotKind
+  int partner[kMaxSlots];       // stale slot <-> its auxiliary slot, else -1
+  void* out[kMaxSlots];         // caller slots only
   int out_bf16;
   float* states;             // [B,H,NT,R,DkM,DvP] f32: dS, then S_in in place
   __nv_bfloat16* images;     // [B,H,NT,R] images of S_in (DvP rows x DkP cols)
+  int any_stale;
   // sequence-shard boundary states, f32 [B,H,R,Dk,Dv] (payload column fastest)
   const float* init;         // state entering token 0, or null (zero)
   float* final_state;        // state after the last token (written), or null
@@ -40,14 +60,14 @@ struct ScanParams {
 };
 
 struct ScanGradParams {
-  const __nv_bfloat16* dout[4];
+  const __nv_bfloat16* dout[kMaxSlots];   // caller slots only
   void* dq;
   void* dk;
   void* dv;
   long long dvs[3];          // element strides of a [B,H,T,Dv - v_unit] view when dv_strided
   int dv_strided;
   int grad_bf16;
-  float* dla[4];
+  float* dla[kMaxSlots];     // an auxiliary slot shares its stale slot's
   float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place
   float* pstates;            // [B,H,NT,R,DkM,DvP] f32: key-weight derivative of each tile's state
   __nv_bfloat16* gimages;    // [B,H,NT,R] images of G (DvP rows x DkP cols)
@@ -78,20 +98,38 @@ __device__ __forceinline__ float key_weight(float la, bool decayed, int len, int
   return decayed ? __expf(la * static_cast<float>(len - 1 - j)) : 1.f;
 }
 
+// 1 - e^{x} for x <= 0 without cancellation.
+__device__ __forceinline__ float one_minus_exp(float x) { return -expm1f(x); }
+
+// Key weight of slot r: the stale slot's is 1 - e^{la (len - 1 - j)}.
+__device__ __forceinline__ float slot_key_weight(const ScanParams& p, int r, float la, int len, int j) {
+  if (p.kind[r] == kSlotStale) return j < len ? one_minus_exp(la * static_cast<float>(len - 1 - j)) : 0.f;
+  return key_weight(la, p.la[r] != nullptr, len, j);
+}
+
+// d/d la of slot r's key weight of row j.
+__device__ __forceinline__ float slot_key_weight_dla(const ScanParams& p, int r, float la, int len, int j) {
+  if (j >= len) return 0.f;
+  const float k = static_cast<float>(len - 1 - j);
+  const float dw = k * __expf(la * k);
+  return p.kind[r] == kSlotStale ? -dw : dw;
+}
+
 // Index of state element (feature f, payload column c) of the boundary state
 // arrays [B,H,R,Dk,Dv].
 __device__ __forceinline__ size_t boundary_index(const ScanParams& p, int b, int h, int r, int f, int c) {
   return ((((static_cast<size_t>(b) * p.H + h) * p.R + r) * p.Dk + f) * p.Dv) + c;
 }
 
-// Decay powers exp(la_r k), k = 0..kTile-1, of every retention of head h into
-// shared memory (`tab`: R * kTile floats), so that the intra-tile weight is a
-// lookup: w_r(i, j) = tab[r * kTile + i - j] for j <= i.  Visible after the
-// next barrier.
+// Intra-tile weights of every caller slot of head h at distances k =
+// 0..kTile-1 into shared memory (`tab`: RU * kTile floats): exp(la_r k), or
+// 1 - exp(la_r k) for a stale slot, so that w_r(i, j) = tab[r * kTile + i - j]
+// for j <= i.  Visible after the next barrier.
 __device__ __forceinline__ void fill_decay(const ScanParams& p, int h, float* tab) {
-  for (int i = threadIdx.x; i < p.R * kTile; i += blockDim.x) {
+  for (int i = threadIdx.x; i < p.RU * kTile; i += blockDim.x) {
     const int r = i / kTile, k = i % kTile;
-    tab[i] = p.la[r] != nullptr ? __expf(head_la(p, r, h) * static_cast<float>(k)) : 1.f;
+    const float x = head_la(p, r, h) * static_cast<float>(k);
+    tab[i] = p.la[r] == nullptr ? 1.f : p.kind[r] == kSlotStale ? one_minus_exp(x) : __expf(x);
   }
 }
 
@@ -121,6 +159,11 @@ __host__ __device__ inline dim3 prefix_grid(int DkM, int DvP, int R, int BH) {
   return dim3((DkM / 8 + 31) / 32, R * (DvP / 8), BH);
 }
 constexpr int kPrefixBatch = 8;   // tiles whose states are loaded together
+
+// The payload tile of a tile's rows: v, then the v_unit constant columns.
+__device__ __forceinline__ void load_payload(const ScanParams& p, const Tile& t, const __nv_bfloat16* src, int rows) {
+  load_tile(t, src, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - p.v_unit : -1, p.v_unit);
+}
 
 __device__ __forceinline__ void store_out(void* base, bool bf16, size_t idx, float v) {
   if (bf16) {

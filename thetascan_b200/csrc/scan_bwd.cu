@@ -21,6 +21,11 @@
 //   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
 //   scan_bwd_dqk_kernel    ds (summed over retentions), then dq or dk (tcgen05)
 //   scan_bwd_dv_kernel     P_r, dv, f-term                       (tcgen05)
+// A stale slot X and its auxiliary slot a (scan.cuh) enter the same sums with
+// their own weights: dout_X reaches S_X with carry 1 and S_a with 1 - c(i),
+// and the reverse recursion couples them,
+//   G_X(n-1) = G_X(n) + dSloc_X(n),
+//   G_a(n-1) = C_n G_a(n) + (1 - C_n) G_X(n) + dSloc_a(n).
 #include "capi_internal.h"
 #include "scan.cuh"
 
@@ -48,7 +53,7 @@ __device__ void accumulate_ds(const ScanParams& p, const ScanGradParams& g, MmaC
   for (int k = 0; k < kChunks; ++k)
 #pragma unroll
     for (int e = 0; e < 16; ++e) acc[k][e] = 0.f;
-  for (int r = 0; r < p.R; ++r) {
+  for (int r = 0; r < p.RU; ++r) {
     const Tile& t = staged ? td[r] : td[0];
     if (!staged) load_tile(t, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     ctx.run([&] { gemm_issue(t_g, kmajor(t), kmajor(tv), kTile, p.DvP, false); });
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
     const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
     const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
     load_tile(tk, kp, p.ks[2], rows, p.Dk);
-    load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+    load_payload(p, tv, vp, rows);
   }
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
@@ -130,22 +135,37 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
+    const int kind = p.kind[r];
     const bool want = decayed && g.dla[r] != nullptr;
+    // the stale slot's own carry is 1: only its key weights depend on la
+    const bool want_carry = want && kind != kSlotStale;
+    // an auxiliary slot is read through its stale slot's dout
+    const __nv_bfloat16* dsrc = dout_rows(p, g, kind == kSlotAux ? p.partner[r] : r, b, h, t0);
     if (n >= 1 || g.all_tiles) {
-      // dSloc (region d) and, for the gradient, the (i+1)-weighted copy (region x).
-      load_scaled_rows(tw, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv, -1,
-                       [&](int t) { return decayed ? __expf(la * static_cast<float>(t + 1)) : 1.f; });
+      // dSloc (region d) and, for the gradient, the la-derivative of the
+      // carry-weighted copy (region x).
+      load_scaled_rows(tw, dsrc, p.Dv, rows, p.Dv, -1, [&](int t) {
+        const float x = la * static_cast<float>(t + 1);
+        return kind == kSlotAux ? one_minus_exp(x) : (decayed && kind != kSlotStale) ? __expf(x) : 1.f;
+      });
       ctx.run([&] {
         for (int mb = 0; mb < mblocks; ++mb)
           gemm_issue(t_d + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
       });
-      if (want) {
-        for (int j = part; j < p.DvP / 8; j += kParts) {
-          float f[8];
-          unpack8(tile_ld16(tw, row, j), f);
+      if (want_carry) {
+        if (kind == kSlotAux) {
+          // d/dla (1 - e^{la (i+1)}) = -(i+1) e^{la (i+1)}
+          load_scaled_rows(tw, dsrc, p.Dv, rows, p.Dv, -1, [&](int t) {
+            return -static_cast<float>(t + 1) * __expf(la * static_cast<float>(t + 1));
+          });
+        } else {
+          for (int j = part; j < p.DvP / 8; j += kParts) {
+            float f[8];
+            unpack8(tile_ld16(tw, row, j), f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= static_cast<float>(row + 1);
-          tile_st16(tw, row, j, pack8(f));
+            for (int e = 0; e < 8; ++e) f[e] *= static_cast<float>(row + 1);
+            tile_st16(tw, row, j, pack8(f));
+          }
         }
         ctx.run([&] {
           for (int mb = 0; mb < mblocks; ++mb)
@@ -161,7 +181,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
           tmem_ld16(tmem_addr(t_d, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
           for (int e = 0; e < 16; ++e) g.gstates[si + static_cast<size_t>(c + e) * p.DkM + f] = v[e];
-          if (want) {
+          if (want_carry) {
             float x[16];
             tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), x);
 #pragma unroll
@@ -169,17 +189,39 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
           }
         }
       }
-      if (want) {
+      if (want_carry) {
         const float sum = block_sum(carry_dot, red);
         if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
       }
+      if (want && kind == kSlotStale) {
+        // dSloc_delta(n) = sum_t c(i) q_t^T dout_X[t]: the local term of
+        // G_delta = G_X - G_a, which the reverse prefix carries on its own
+        // (the stale slot's key-weight derivative is not needed: it is
+        // -B'_a), so this tile's pstates hold it.
+        load_scaled_rows(tw, dsrc, p.Dv, rows, p.Dv, -1,
+                         [&](int t) { return __expf(la * static_cast<float>(t + 1)); });
+        ctx.run([&] {
+          for (int mb = 0; mb < mblocks; ++mb)
+            gemm_issue(t_x + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+        });
+        float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+        for (int mb = 0; mb < mblocks; ++mb) {
+          float* col = dst + mb * kTile + row;
+          for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
+            float v[16];
+            tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = v[e];
+          }
+        }
+      }
     }
-    if (want && (n + 1 < p.NT || g.all_tiles)) {
+    if (want && kind != kSlotStale && (n + 1 < p.NT || g.all_tiles)) {
       // B'(n): key-weight derivative of the state this tile leaves behind.
+      const float wgt = slot_key_weight_dla(p, r, la, rows, row);
       for (int j = part; j < p.DvP / 8; j += kParts) {
         float f[8];
         unpack8(tile_ld16(tv, row, j), f);
-        const float wgt = row < rows ? static_cast<float>(rows - 1 - row) * key_weight(la, true, rows, row) : 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] *= wgt;
         tile_st16(tw, row, j, pack8(f));
@@ -207,11 +249,105 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
 
 // ------------------------------------------------------------------ reverse prefix
 
+// Sum over the block's threads of `acc`, added to dla[h] by thread 0.
+__device__ __forceinline__ void add_block_dla(float acc, float* dla, int h) {
+  __shared__ float red[8];
+  float v = acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
+    atomicAdd(dla + h, sum);
+  }
+}
+
+// Reverse recursion of a stale slot X and its auxiliary slot a in one lane
+// (no boundary states):
+//   G_X(n-1) = G_X(n) + dSloc_X(n)
+//   G_a(n-1) = C_n G_a(n) + (1 - C_n) G_X(n) + dSloc_a(n)
+// whose images feed dk and dv.  The log-retention terms of the pair,
+//   <G_X(n), B'_X(n) - C'_n S_a(n)> + <G_a(n), B'_a(n) + C'_n S_a(n)>,
+// with B'_X = -B'_a and C'_n = len_n C_n, are -<G_delta(n), B'_a(n) + C'_n S_a(n)>
+// for G_delta = G_X - G_a.  That difference is small where the stale weights
+// are, so it is carried by its own recursion from its own local terms
+// (held in the stale slot's pstates) rather than formed from G_X and G_a:
+//   G_delta(n-1) = C_n G_delta(n) + dSloc_delta(n),  dSloc_delta = sum_t c(i) q_t^T dout_X[t].
+__device__ __forceinline__ void stale_reverse_prefix(const ScanParams& p, const ScanGradParams& g,
+                                                     const PrefixLane& l) {
+  const int r = l.r, a = p.partner[r];
+  const float la = head_la(p, r, l.h);
+  const int len_last = tile_len(p, p.NT - 1);
+  const float closing = __expf(la * static_cast<float>(kTile));
+  const float closing_last = __expf(la * static_cast<float>(len_last));
+  const float open = one_minus_exp(la * static_cast<float>(kTile));
+  const float open_last = one_minus_exp(la * static_cast<float>(len_last));
+  const bool want = g.dla[r] != nullptr;
+  const bool in_image = l.active && l.f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  float GX[8], GA[8], GD[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) GX[e] = GA[e] = GD[e] = 0.f;
+  float acc = 0.f;
+  auto store8 = [&](int slot, int n, const float* G) {
+    const size_t si = state_index(p, l.b, l.h, n, slot);
+    float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
+    gp[0] = make_float4(G[0], G[1], G[2], G[3]);
+    gp[1] = make_float4(G[4], G[5], G[6], G[7]);
+    if (in_image) {
+      uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+      *reinterpret_cast<uint4*>(img) = pack8(G);
+    }
+  };
+  auto load8 = [&](const float* base, int slot, int n, float* out) {
+    const float4* ptr = reinterpret_cast<const float4*>(base + state_index(p, l.b, l.h, n, slot) * p.DkM * p.DvP + elem);
+    const float4 x0 = ptr[0], x1 = ptr[1];
+    out[0] = x0.x; out[1] = x0.y; out[2] = x0.z; out[3] = x0.w;
+    out[4] = x1.x; out[5] = x1.y; out[6] = x1.z; out[7] = x1.w;
+  };
+  for (int n = p.NT - 1; n >= 0 && l.active; --n) {
+    float lx[8] = {}, lA[8] = {}, lD[8] = {}, pa[8] = {}, sa[8] = {};
+    if (n >= 1) {
+      load8(g.gstates, r, n, lx);
+      load8(g.gstates, a, n, lA);
+      if (want) load8(g.pstates, r, n, lD);
+    }
+    const bool terms = want && n + 1 < p.NT;
+    if (terms) {
+      load8(g.pstates, a, n, pa);
+      load8(p.states, a, n, sa);
+    }
+    store8(r, n, GX);
+    store8(a, n, GA);
+    const float cl = n + 1 < p.NT ? closing : closing_last;
+    const float op = n + 1 < p.NT ? open : open_last;
+    const float kc = n + 1 < p.NT ? static_cast<float>(kTile) * closing : static_cast<float>(len_last) * closing_last;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (terms) acc -= GD[e] * (pa[e] + kc * sa[e]);
+      const float gx = GX[e];
+      GX[e] = gx + lx[e];
+      GA[e] = GA[e] * cl + op * gx + lA[e];
+      GD[e] = GD[e] * cl + lD[e];
+    }
+  }
+  if (want) add_block_dla(acc, g.dla[r], l.h);
+}
+
 // G(n) = e^{128 la} G(n+1) + dSloc(n+1), G(NT-1) = 0, per state element; and
 // the key-weight and closing terms of the log-retention gradient.
 __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, ScanGradParams g) {
   const PrefixLane l = prefix_lane(p);
   const int r = l.r;
+  // every lane of a block has the same slot, so these exits are block-uniform
+  if (p.kind[r] == kSlotAux) return;     // carried by its stale slot's lane
+  if (p.kind[r] == kSlotStale) {
+    stale_reverse_prefix(p, g, l);
+    return;
+  }
   const float la = head_la(p, r, l.h);
   const bool decayed = p.la[r] != nullptr;
   const int len_last = tile_len(p, p.NT - 1);
@@ -308,19 +444,7 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
       if (f < p.Dk) g.dinit[boundary_index(p, l.b, l.h, l.r, f, l.c)] = G[e];
     }
   }
-  if (want) {
-    __shared__ float red[8];
-    float v = acc;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float sum = 0.f;
-      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
-      atomicAdd(g.dla[r] + l.h, sum);
-    }
-  }
+  if (want) add_block_dla(acc, g.dla[r], l.h);
 }
 
 // ------------------------------------------------------------------ dq, dk
@@ -354,7 +478,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   Tile ts1 = two_images ? Tile{tx.saddr, p.DvP, p.DkP} : ts0;
   Tile td[4];
   for (int i = 0; i < 4; ++i) td[i] = Tile{ts0.saddr + p.DvP * p.DkP * 2 + i * kTile * p.DvP * 2, kTile, p.DvP};
-  const bool staged = nbuf >= p.R;
+  const bool staged = nbuf >= p.RU;
   const bool cross = kDq ? (n > 0 || p.init != nullptr) : (n + 1 < p.NT || g.dfinal != nullptr);
   const __nv_bfloat16* images = kDq ? p.images : g.gimages;
   auto image_of = [&](int r) {
@@ -369,10 +493,10 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   const __nv_bfloat16* xp = kDq ? p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2]
                                 : p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
-  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_payload(p, tv, vp, rows);
   load_tile(tx, xp, kDq ? p.ks[2] : p.qs[2], rows, p.Dk);
   if (staged)
-    for (int r = 0; r < p.R; ++r) load_tile(td[r], dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+    for (int r = 0; r < p.RU; ++r) load_tile(td[r], dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
   if (cross) load_image(ts0, image_of(0), image_bytes(p));
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
@@ -395,25 +519,33 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
       cp_async_commit();
       const float la = head_la(p, r, h);
       const bool decayed = p.la[r] != nullptr;
-      const Tile& ta = staged ? td[r] : td[0];
+      const int kind = p.kind[r];
+      // the row operand: a caller slot's staged dout tile (scaled in place),
+      // an auxiliary slot's stale partner's (its own scaling is 1, so the
+      // tile still holds dout), or scratch tile 0
+      const int src = kind == kSlotAux ? p.partner[r] : r;
+      const Tile& ta = (staged && (kDq || r < p.RU)) ? td[kDq ? src : r] : td[0];
       if (kDq) {
-        // rows of c_r o dout_r, c_r(i) = e^{la (i+1)}
-        const float c = decayed ? __expf(la * static_cast<float>(row + 1)) : 1.f;
+        // rows of c o dout: c(i) = e^{la (i+1)} (decayed), 1 (stale), 1 - e^{la (i+1)} (auxiliary)
+        const float x = la * static_cast<float>(row + 1);
+        const float c = kind == kSlotAux ? one_minus_exp(x) : (decayed && kind != kSlotStale) ? __expf(x) : 1.f;
         if (!staged) {
-          load_tile(ta, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+          load_tile(ta, dout_rows(p, g, src, b, h, t0), p.Dv, rows, p.Dv);
           cp_async_wait_all();
           __syncthreads();
         }
-        for (int j = part; j < p.DvP / 8; j += kParts) {
-          float f[8];
-          unpack8(tile_ld16(ta, row, j), f);
+        if (c != 1.f || kind == kSlotAux) {
+          for (int j = part; j < p.DvP / 8; j += kParts) {
+            float f[8];
+            unpack8(tile_ld16(ta, row, j), f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= c;
-          tile_st16(ta, row, j, pack8(f));
+            for (int e = 0; e < 8; ++e) f[e] *= c;
+            tile_st16(ta, row, j, pack8(f));
+          }
         }
       } else {
-        // rows of u_r o v, u_r(i) = e^{la (127-i)}
-        const float u = key_weight(la, decayed, rows, row);
+        // rows of u_r o v
+        const float u = slot_key_weight(p, r, la, rows, row);
         for (int j = part; j < p.DvP / 8; j += kParts) {
           float f[8];
           unpack8(tile_ld16(tv, row, j), f);
@@ -477,7 +609,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
-  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_payload(p, tv, vp, rows);
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_s = ctx.tmem, t_g = ctx.tmem + kTile, t_dv = ctx.tmem + 2 * kTile;
@@ -487,33 +619,39 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
-    const bool want = decayed && g.dla[r] != nullptr;
-    for (int c = 16 * part; c < kTile; c += kChunkStep) {
-      float s[16], f[16];
-      tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
+    const bool caller = r < p.RU;            // auxiliary slots have no dout
+    if (!caller && !cross) continue;
+    const bool want = caller && decayed && g.dla[r] != nullptr;
+    if (caller) {
+      for (int c = 16 * part; c < kTile; c += kChunkStep) {
+        float s[16], f[16];
+        tmem_ld16(tmem_addr(t_s, quad * 32, c), s);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int j = c + e;
-        f[e] = (j <= row) ? decay[r * kTile + row - j] * s[e] : 0.f;
+        for (int e = 0; e < 16; ++e) {
+          const int j = c + e;
+          f[e] = (j <= row) ? decay[r * kTile + row - j] * s[e] : 0.f;
+        }
+        tile_st16(tp, row, c / 8, pack8(f));
+        tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
       }
-      tile_st16(tp, row, c / 8, pack8(f));
-      tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
+      load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     }
-    load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     if (cross) {
       load_scaled_rows(tq, kp, p.ks[2], rows, p.Dk, -1, [&](int t) {
-        return key_weight(la, decayed, rows, t);
+        return slot_key_weight(p, r, la, rows, t);
       });
       const size_t si = state_index(p, b, h, n, r);
       load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
                  image_bytes(p));
     }
     ctx.run([&] {
-      gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, r > 0);
+      if (caller) gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, r > 0);
       if (cross) gemm_issue(t_dv, kmajor(tq), kmajor(tg), p.DvP, p.DkP, true);
       if (want) gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false);
     });
     if (want) {
+      // d w / d la at distance k: k e^{la k}, or -k e^{la k} = -k (1 - w) for a stale slot
+      const bool stale = p.kind[r] == kSlotStale;
       float acc = 0.f;
       for (int c = 16 * part; c < kTile; c += kChunkStep) {
         float s[16], gv[16];
@@ -522,7 +660,11 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int j = c + e;
-          if (j <= row) acc += static_cast<float>(row - j) * decay[r * kTile + row - j] * s[e] * gv[e];
+          if (j <= row) {
+            const float w = decay[r * kTile + row - j];
+            const float dw = stale ? -(1.f - w) : w;
+            acc += static_cast<float>(row - j) * dw * s[e] * gv[e];
+          }
         }
       }
       const float sum = block_sum(acc, red);
@@ -555,7 +697,7 @@ static size_t dqk_smem(const ScanParams& p, int nbuf) {
 // Budget for the dynamic part: the opt-in maximum per block less room for
 // the kernels' static shared memory.
 constexpr size_t kDynSmemBudget = 232448 - 4096;
-static int dqk_buffers(const ScanParams& p) { return dqk_smem(p, p.R) <= kDynSmemBudget ? p.R : 1; }
+static int dqk_buffers(const ScanParams& p) { return dqk_smem(p, p.RU) <= kDynSmemBudget ? p.RU : 1; }
 static size_t dv_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2 +
          (p.DvP > kTile ? static_cast<size_t>(p.DvP) * p.DkP * 2 : 0);

@@ -5,8 +5,10 @@
 //                           S_in(n) = e^{128 la} S_in(n-1) + dS(n-1)  (f32)
 //   3. scan_out_kernel     per tile: score q.k^T once, then per retention
 //                           out_r = (w_r o causal o score) v + (c_r q) S_in  (tcgen05)
-// Tile kernels run 256 threads: the two threads of token row r (r, r+128)
-// split its columns into alternating 16-column chunks.
+// Tile kernels run kThreads = 512 threads: the kParts threads of token row r
+// (r, r+128, ...) split its columns into 16-column chunks.  A stale slot
+// (weights 1 - alpha^(t-j)) is carried with its auxiliary decayed slot (see
+// scan.cuh).
 #include "capi_internal.h"
 #include "scan.cuh"
 
@@ -30,7 +32,7 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   Tile tw{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};
 
   const int mblocks = p.DkM / kTile;
-  const int cols_needed = p.R * mblocks * p.DvP;
+  const int cols_needed = mblocks * p.DvP;
   const uint32_t ncols = cols_needed <= 32 ? 32 : cols_needed <= 64 ? 64 : cols_needed <= 128 ? 128
                          : cols_needed <= 256 ? 256 : 512;
 
@@ -43,15 +45,18 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
   const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
-  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_payload(p, tv, vp, rows);
 
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
 
+  // One slot at a time through one TMEM region: the update, then its store
+  // (accumulator row of block mb is feature mb*128 + row; states are stored
+  // value-major, [DvP][DkM], so lanes of a warp write consecutive features).
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
-    // u_r(j) = exp(la (len - 1 - j)): this tile's key weights in the leaving state.
-    const float u = key_weight(la, p.la[r] != nullptr, rows, row);
+    // u_r(j): this tile's key weights in the leaving state.
+    const float u = slot_key_weight(p, r, la, rows, row);
     for (int j = part; j < p.DvP / 8; j += kParts) {
       float f[8];
       unpack8(tile_ld16(tv, row, j), f);
@@ -61,21 +66,16 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
     }
     ctx.run([&] {
       for (int mb = 0; mb < mblocks; ++mb) {
-        const uint32_t d = ctx.tmem + static_cast<uint32_t>((r * mblocks + mb) * p.DvP);
+        const uint32_t d = ctx.tmem + static_cast<uint32_t>(mb * p.DvP);
         gemm_issue(d, mnmajor(tk, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
       }
     });
-  }
-
-  // Epilogue: accumulator row of block mb is feature mb*128 + row; states are
-  // stored value-major ([DvP][DkM]), so lanes of a warp write consecutive features.
-  for (int r = 0; r < p.R; ++r) {
     float* dst_base = p.states + state_index(p, b, h, n, r) * p.DkM * p.DvP;
     for (int mb = 0; mb < mblocks; ++mb) {
       float* dst = dst_base + mb * kTile + row;
       for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
         float v[16];
-        tmem_ld16(tmem_addr(ctx.tmem, quad * 32, (r * mblocks + mb) * p.DvP + c), v);
+        tmem_ld16(tmem_addr(ctx.tmem, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) dst[static_cast<size_t>(c + e) * p.DkM] = v[e];
       }
@@ -88,9 +88,80 @@ __global__ void __launch_bounds__(kThreads) scan_state_kernel(ScanParams p) {
 
 // ------------------------------------------------------------------ 2. prefix over tiles
 
+// The lane of a stale slot X carries its auxiliary slot a too:
+//   S_X(n+1) = S_X(n) + (1 - C_n) S_a(n) + dS_X(n),  S_a(n+1) = C_n S_a(n) + dS_a(n)
+// from zero states (stale slots take no boundary states).
+__device__ __forceinline__ void stale_prefix(const ScanParams& p, const PrefixLane& l) {
+  const int a = p.partner[l.r];
+  const float la = head_la(p, l.r, l.h);
+  const float closing = __expf(la * static_cast<float>(kTile));
+  const float closing_last = __expf(la * static_cast<float>(tile_len(p, p.NT - 1)));
+  const float open = one_minus_exp(la * static_cast<float>(kTile));
+  const float open_last = one_minus_exp(la * static_cast<float>(tile_len(p, p.NT - 1)));
+  const bool in_image = l.f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  float X[8], A[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) X[e] = A[e] = 0.f;
+  constexpr int kB = kPrefixBatch / 2;
+  const int last_used = p.NT - 1;
+  auto store8 = [&](int slot, int n, const float* S) {
+    const size_t si = state_index(p, l.b, l.h, n, slot);
+    float4* ptr = reinterpret_cast<float4*>(p.states + si * p.DkM * p.DvP + elem);
+    ptr[0] = make_float4(S[0], S[1], S[2], S[3]);
+    ptr[1] = make_float4(S[4], S[5], S[6], S[7]);
+    if (in_image) {
+      uint8_t* img = reinterpret_cast<uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+      *reinterpret_cast<uint4*>(img) = pack8(S);
+    }
+  };
+  for (int n0 = 0; n0 < p.NT; n0 += kB) {
+    float4 ux[kB][2], ua[kB][2];
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0 + k;
+      ux[k][0] = ux[k][1] = ua[k][0] = ua[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n < last_used) {
+        const float4* px = reinterpret_cast<const float4*>(
+            p.states + state_index(p, l.b, l.h, n, l.r) * p.DkM * p.DvP + elem);
+        const float4* pa = reinterpret_cast<const float4*>(
+            p.states + state_index(p, l.b, l.h, n, a) * p.DkM * p.DvP + elem);
+        ux[k][0] = px[0];
+        ux[k][1] = px[1];
+        ua[k][0] = pa[0];
+        ua[k][1] = pa[1];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0 + k;
+      if (n >= p.NT) break;
+      store8(l.r, n, X);
+      store8(a, n, A);
+      const float cl = n + 1 < p.NT ? closing : closing_last;
+      const float op = n + 1 < p.NT ? open : open_last;
+      const float vx[8] = {ux[k][0].x, ux[k][0].y, ux[k][0].z, ux[k][0].w,
+                           ux[k][1].x, ux[k][1].y, ux[k][1].z, ux[k][1].w};
+      const float va[8] = {ua[k][0].x, ua[k][0].y, ua[k][0].z, ua[k][0].w,
+                           ua[k][1].x, ua[k][1].y, ua[k][1].z, ua[k][1].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        X[e] = X[e] + op * A[e] + vx[e];
+        A[e] = A[e] * cl + va[e];
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) scan_prefix_kernel(ScanParams p) {
   const PrefixLane l = prefix_lane(p);
   if (!l.active) return;
+  if (p.kind[l.r] == kSlotAux) return;   // carried by its stale slot's lane
+  if (p.kind[l.r] == kSlotStale) {
+    stale_prefix(p, l);
+    return;
+  }
   const float la = head_la(p, l.r, l.h);
   const bool decayed = p.la[l.r] != nullptr;
   const float closing = decayed ? __expf(la * static_cast<float>(kTile)) : 1.f;
@@ -174,7 +245,7 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   __shared__ float decay[4 * kTile];
   fill_decay(p, h, decay);
 
-  const int cols_needed = kTile + p.R * p.DvP;
+  const int cols_needed = kTile + p.RU * p.DvP;
   const uint32_t ncols = cols_needed <= 256 ? 256 : 512;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
@@ -187,16 +258,17 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
-  load_tile(tv, vp, p.vs[2], rows, p.Dv - p.v_unit, p.v_unit ? p.Dv - 1 : -1);
+  load_payload(p, tv, vp, rows);
 
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_score = ctx.tmem;
   ctx.run([&] { gemm_issue(t_score, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
 
-  for (int r = 0; r < p.R; ++r) {
+  for (int r = 0; r < p.RU; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
+    const bool stale = p.kind[r] == kSlotStale;
     // P_r row: w(row, j) * score(row, j) on the causal triangle.
     for (int c = 16 * part; c < kTile; c += kChunkStep) {
       float s[16];
@@ -211,13 +283,16 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
       tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
     }
     const bool cross = n > 0 || p.init != nullptr;
+    auto image_of = [&](int slot) {
+      return reinterpret_cast<const uint8_t*>(p.images) +
+             state_index(p, b, h, n, slot) * static_cast<size_t>(image_bytes(p));
+    };
     if (cross) {
-      const size_t si = state_index(p, b, h, n, r);
-      load_image(ts, reinterpret_cast<const uint8_t*>(p.images) + si * static_cast<size_t>(image_bytes(p)),
-                 image_bytes(p));
+      load_image(ts, image_of(r), image_bytes(p));
+      // carry c(i) = e^{la (i+1)}; a stale slot reads its own state with weight 1
       const float carry_la = la;
       load_scaled_rows(tq, qp, p.qs[2], rows, p.Dk, -1, [&](int t) {
-        return decayed ? __expf(carry_la * static_cast<float>(t + 1)) : 1.f;
+        return decayed && !stale ? __expf(carry_la * static_cast<float>(t + 1)) : 1.f;
       });
     }
     const uint32_t t_out = ctx.tmem + static_cast<uint32_t>(kTile + r * p.DvP);
@@ -225,11 +300,21 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
       gemm_issue(t_out, kmajor(tp), mnmajor(tv), p.DvP, kTile, false);
       if (cross) gemm_issue(t_out, kmajor(tq), kmajor(ts), p.DvP, p.DkP, true);
     });
+    if (cross && stale) {
+      // + (1 - c(i)) q S_a: the auxiliary state, whose weights have not yet
+      // reached the stale ones by the distance i + 1 into this tile
+      load_image(ts, image_of(p.partner[r]), image_bytes(p));
+      const float carry_la = la;
+      load_scaled_rows(tq, qp, p.qs[2], rows, p.Dk, -1, [&](int t) {
+        return one_minus_exp(carry_la * static_cast<float>(t + 1));
+      });
+      ctx.run([&] { gemm_issue(t_out, kmajor(tq), kmajor(ts), p.DvP, p.DkP, true); });
+    }
   }
 
   // Coalesced stores through a stage on the (now idle) P tile.
   float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
-  for (int r = 0; r < p.R; ++r) {
+  for (int r = 0; r < p.RU; ++r) {
     const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
     void* dst = p.out_bf16 ? static_cast<void*>(reinterpret_cast<__nv_bfloat16*>(p.out[r]) + row0)
                            : static_cast<void*>(reinterpret_cast<float*>(p.out[r]) + row0);

@@ -128,7 +128,7 @@ def _piece_width(n_retentions, Dk):
     return 144
 
 
-def _scan(query, keys, payload, append_unit, retentions):
+def _scan(query, keys, payload, append_unit, retentions, stale=None):
     """f32 reads of the multi-view scan kernels (bf16 streams).  The scan is
     linear in the payload, so a payload wider than one call takes is read in
     column pieces (the mass column rides on the last)."""
@@ -137,12 +137,13 @@ def _scan(query, keys, payload, append_unit, retentions):
     width = payload.shape[-1]
     step = _piece_width(len(retentions), q.shape[-1]) - 1
     if width + (1 if append_unit else 0) <= step + 1:
-        return _ScanViews.apply(q, k, payload.to(bf).contiguous(), append_unit, torch.float32, *retentions)
+        return _ScanViews.apply(q, k, payload.to(bf).contiguous(), append_unit, torch.float32, stale, *retentions)
     parts = [[] for _ in retentions]
     for start in range(0, width, step):
         piece = payload[..., start:start + step].to(bf).contiguous()
         last = start + step >= width
-        for i, read in enumerate(_ScanViews.apply(q, k, piece, append_unit and last, torch.float32, *retentions)):
+        for i, read in enumerate(_ScanViews.apply(q, k, piece, append_unit and last, torch.float32, stale,
+                                                  *retentions)):
             parts[i].append(read)
     return tuple(torch.cat(p, dim=-1) for p in parts)
 

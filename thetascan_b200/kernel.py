@@ -24,6 +24,10 @@ import torch
 from . import _lib
 from .scan import _build_args, _stream, _workspace
 
+# Mass columns of every scan read [N | D | D]: the read backward hands the
+# mass gradient to the scan as bf16 hi + lo (see ts_kread_args.mass_columns).
+MASS_COLS = 2
+
 KINDS = {"relu2_ridge": _lib.TS_FEATURE_RELU2, "softmax_partition": _lib.TS_FEATURE_SOFTMAX,
          "projected_bspline": _lib.TS_FEATURE_BSPLINE}
 MODES = {"sum": _lib.TS_VIEWS_SUM, "fast": _lib.TS_VIEWS_FAST, "stale": _lib.TS_VIEWS_STALE}
@@ -84,6 +88,7 @@ def _kread_args(spec, slots, eta, y0, y):
     for i, s in enumerate(slots):
         a.slots[i] = s.data_ptr()
     a.eta, a.y0, a.y = _ptr(eta), y0.data_ptr(), _ptr(y)
+    a.mass_columns = MASS_COLS
     return a
 
 
@@ -113,6 +118,11 @@ def _controls(thr, bias, gain, scale):
     return {"thr": _f32(thr), "bias": _f32(bias), "gain": _f32(gain), "scale": _f32(scale)}
 
 
+def _stale_flags(spec, n_slots):
+    """Slots 1..J of a stale bank are stale scans (the view S_sum - S_fast_j)."""
+    return [False] + [True] * (n_slots - 1) if spec.mode == "stale" else None
+
+
 def _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue):
     """Feature, scan and read kernels; returns y and what the backward needs."""
     lib = _lib.load()
@@ -130,8 +140,8 @@ def _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue):
 
     las = [None] + ([] if log_alphas is None else
                     [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
-    slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
-    sa = _build_args(phi_q, phi_k, v, las, slots, True)
+    slots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.float32, device=dev) for _ in las]
+    sa = _build_args(phi_q, phi_k, v, las, slots, MASS_COLS, stale=_stale_flags(spec, len(las)))
     ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
     sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
@@ -163,7 +173,7 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     ga = _lib.KReadGradArgs()
     ga.dy = dy.data_ptr()
     ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
-    dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
+    dslots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev) for _ in slots]
     for i, s in enumerate(dslots):
         ga.dslots[i] = s.data_ptr()
     # y0 enters y with coefficient 1, so its gradient is dy itself: a bf16 dy
@@ -178,14 +188,14 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
 
     # 2. scan
-    sa = _build_args(phi_q, phi_k, v, las, slots, True, st["ws"])
+    sa = _build_args(phi_q, phi_k, v, las, slots, MASS_COLS, st["ws"], stale=_stale_flags(spec, n))
     sg = _lib.ScanGradArgs()
     m = phi_q.shape[-1]
     # bf16 hand-over: the feature backward stages dphi as a bf16 tile.
     dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
     dphi_k = torch.empty_like(dphi_q)
     if dv_out is None:
-        dvaug = torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev)
+        dvaug = torch.empty(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev)
         sg.dv = dvaug.data_ptr()
     else:
         dvaug = None
@@ -329,9 +339,9 @@ class _ShardStageA(torch.autograd.Function):
         las = [None] + ([] if log_alphas is None else
                         [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
         R = len(las)
-        slots = [torch.empty(B, H, T, d + 1, dtype=torch.float32, device=dev) for _ in las]
-        U = torch.empty(B, H, R, m, d + 1, dtype=torch.float32, device=dev)
-        sa = _build_args(phi_q, phi_k, v, las, slots, True)
+        slots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.float32, device=dev) for _ in las]
+        U = torch.empty(B, H, R, m, d + MASS_COLS, dtype=torch.float32, device=dev)
+        sa = _build_args(phi_q, phi_k, v, las, slots, MASS_COLS)
         ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
         sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
         sa.final_state, sa.stage = U.data_ptr(), 1
@@ -356,7 +366,7 @@ class _ShardStageA(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         dq, dk, dv = _qkv_views(dqkv, H, d)
         # scan, second half: reverse prefix from dU, then dq / dk / dv
-        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
         sa.init_state, sa.stage = hold.S.data_ptr(), 2
         sg = _lib.ScanGradArgs()
         m = hold.phi_q.shape[-1]
@@ -417,7 +427,7 @@ class _ShardStageB(torch.autograd.Function):
     def forward(ctx, hold, S, phi_q, phi_k, v):
         lib = _lib.load()
         hold.S = S.detach().float().contiguous()
-        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
         sa.init_state, sa.stage = hold.S.data_ptr(), 2
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
         ctx.hold = hold
@@ -432,9 +442,9 @@ class _ShardStageB(torch.autograd.Function):
         B, H, T = hold.phi_q.shape[:3]
         d = v.shape[-1]
         dev = v.device
-        hold.douts = [torch.zeros(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) if g is None
+        hold.douts = [torch.zeros(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev) if g is None
                       else g.to(torch.bfloat16).contiguous() for g in dslots]
-        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, True, hold.ws)
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
         sa.init_state, sa.stage = hold.S.data_ptr(), 2
         hold.gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
         sg = _lib.ScanGradArgs()
@@ -480,7 +490,7 @@ class _KRead(torch.autograd.Function):
         ga = _lib.KReadGradArgs()
         ga.dy = dy.data_ptr()
         ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
-        dslots = [torch.empty(B, H, T, d + 1, dtype=torch.bfloat16, device=dev) for _ in slots]
+        dslots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev) for _ in slots]
         for i, s in enumerate(dslots):
             ga.dslots[i] = s.data_ptr()
         dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
@@ -511,7 +521,8 @@ def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | N
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core_sharded: log_alphas are required exactly for a bank (mode fast/stale)")
     if spec.mode == "stale":
-        raise NotImplementedError("b200 backend: the stale bank is not built yet (fast banks are supported)")
+        raise NotImplementedError("b200 backend: sequence shards of a stale bank are not built (stale scans take "
+                                  "no boundary states); fast banks and the plain sum shard")
     hold = _ShardScan()
     phi_q, phi_k, y0, U = _ShardStageA.apply(hold, spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain,
                                              spline_scale, log_alphas)
@@ -543,10 +554,6 @@ def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None,
         raise ValueError("kernel_core_qkv: last dimension must be 3*H*d")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core_qkv: log_alphas are required exactly for a bank (mode fast/stale)")
-    if spec.mode == "stale":
-        raise NotImplementedError(
-            "b200 backend: the stale bank reads a difference of two scans whose mass can vanish; "
-            "its dedicated retention kind is not built yet (fast banks are supported)")
     return _KernelCoreQKV.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale,
                                 log_alphas, etas)
 
@@ -570,8 +577,4 @@ def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias
             raise ValueError("b200 backend: streams need a contiguous innermost dimension")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core: log_alphas are required exactly for a bank (mode fast/stale)")
-    if spec.mode == "stale":
-        raise NotImplementedError(
-            "b200 backend: the stale bank reads a difference of two scans whose mass can vanish; "
-            "its dedicated retention kind is not built yet (fast banks are supported)")
     return _KernelCore.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas)

@@ -39,17 +39,19 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def _build_args(q, k, v, las, outs, append_unit, workspace=None):
+def _build_args(q, k, v, las, outs, append_unit, workspace=None, stale=None):
     B, H, T, Dk = q.shape
     a = _lib.ScanArgs()
     a.batch, a.heads, a.tokens, a.dk = B, H, T, Dk
-    a.dv = v.shape[-1] + (1 if append_unit else 0)
+    n_unit = int(append_unit)   # False/True/2: constant columns after v
+    a.dv = v.shape[-1] + n_unit
     a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
     a.q_strides, a.k_strides, a.v_strides = _strides3(q), _strides3(k), _strides3(v)
-    a.v_append_unit = 1 if append_unit else 0
+    a.v_append_unit = n_unit
     a.n_retentions = len(las)
     for i, la in enumerate(las):
         a.log_alpha[i] = None if la is None else la.data_ptr()
+        a.stale[i] = 1 if (stale and stale[i]) else 0
         if outs is not None:
             a.out[i] = outs[i].data_ptr()
     a.out_dtype = _lib.TS_DTYPE_BF16 if (outs is not None and outs[0].dtype == torch.bfloat16) else _lib.TS_DTYPE_F32
@@ -69,7 +71,7 @@ class _ScanViews(torch.autograd.Function):
     """Autograd wrapper of the multi-view scan kernels."""
 
     @staticmethod
-    def forward(ctx, q, k, v, append_unit, out_dtype, *retentions):
+    def forward(ctx, q, k, v, append_unit, out_dtype, stale, *retentions):
         lib = _lib.load()
         las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
         B, H, T, _ = q.shape
@@ -77,11 +79,12 @@ class _ScanViews(torch.autograd.Function):
         # The kernels write f32 reads; the backward's log-retention term uses
         # them unrounded, and the caller gets them in the stream dtype.
         outs = [torch.empty(B, H, T, dv, dtype=torch.float32, device=q.device) for _ in las]
-        args = _build_args(q, k, v, las, outs, append_unit)
+        args = _build_args(q, k, v, las, outs, append_unit, stale=stale)
         ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
         args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
         ctx.append_unit = append_unit
+        ctx.stale = stale
         ctx.n_ret = len(las)
         ctx.ret_present = [r is not None for r in retentions]
         ctx.ret_dtypes = [None if r is None else r.dtype for r in retentions]
@@ -102,7 +105,7 @@ class _ScanViews(torch.autograd.Function):
         dv_width = outs[0].shape[-1]
         dgrads = [torch.zeros(B, H, T, dv_width, dtype=torch.bfloat16, device=q.device) if d is None
                   else d.to(torch.bfloat16).contiguous() for d in douts]
-        args = _build_args(q, k, v, las, outs, ctx.append_unit, ws)
+        args = _build_args(q, k, v, las, outs, ctx.append_unit, ws, stale=ctx.stale)
         g = _lib.ScanGradArgs()
         dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
         dk = torch.empty_like(dq)
@@ -121,7 +124,7 @@ class _ScanViews(torch.autograd.Function):
         ret_grads = []
         for dla, dtype, shape in zip(dlas, ctx.ret_dtypes, ctx.ret_shapes):
             ret_grads.append(None if dla is None else dla.to(dtype).reshape(shape))
-        return (dq.to(q.dtype), dk.to(k.dtype), dvv.to(v.dtype), None, None, *ret_grads)
+        return (dq.to(q.dtype), dk.to(k.dtype), dvv.to(v.dtype), None, None, None, *ret_grads)
 
 
 def _check_inputs(q, k, v, retentions, chunk):
@@ -147,21 +150,31 @@ def _check_inputs(q, k, v, retentions, chunk):
                 f"got {tuple(r.shape)} for q {tuple(q.shape)}")
 
 
-def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_unit: bool = False):
+def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_unit: bool = False, stale=None):
     """Scan one stream set through several retentions (scan_chunk.py:246-339).
 
     ``append_unit=True`` treats the payload as ``[v | 1]`` without
     materialising it (the key-mass read of engine.py:430); the outputs then have
     ``Dv + 1`` columns, the last being the retention-weighted score mass.
+    ``stale`` (one flag per retention) reads a static retention's stale view,
+    weights ``1 - alpha^(t-i)``: the reference's ``FadeStale`` difference
+    ``S_sum - S_fast`` (interface.py:251-279), formed inside the kernels.
     """
     if not retentions:
         return ()
     _check_inputs(q, k, v, retentions, chunk)
+    stale = tuple(bool(x) for x in stale) if stale is not None else (False,) * len(retentions)
+    if len(stale) != len(retentions):
+        raise ValueError("b200 scan: one stale flag per retention")
+    for r, st in zip(retentions, stale):
+        if st and r is None:
+            raise ValueError("b200 scan: a stale view needs a retention")
     outs = []
     # The kernels take at most four retentions per call; longer tuples are split.
     for start in range(0, len(retentions), _lib.MAX_RETENTIONS):
         group = tuple(retentions[start:start + _lib.MAX_RETENTIONS])
-        outs.extend(_ScanViews.apply(q, k, v, append_unit, q.dtype, *group))
+        flags = stale[start:start + _lib.MAX_RETENTIONS]
+        outs.extend(_ScanViews.apply(q, k, v, append_unit, q.dtype, flags if any(flags) else None, *group))
     return tuple(outs)
 
 
