@@ -241,6 +241,9 @@ typedef struct ts_feature_args {
   int rope_pos0;            /* sequence position of token 0 (sequence shards) */
   int l2norm;               /* 1 = L2-normalize each row after the rotation */
   float l2norm_eps;
+  /* Optional f32 [B,H,T,m] copy of phi(q) before its bf16 rounding (16-byte
+   * aligned), for the feature-mass read, which divides it by the key mass. */
+  float* phi_q_f32;
 } ts_feature_args;
 
 int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream);
@@ -304,6 +307,11 @@ typedef struct ts_kread_args {
    * formed from the bf16-rounded value gradient so that the quotient rule's
    * cancellation survives the bf16 hand-over to the scan backward. */
   int mass_columns;
+  /* Nonzero: unnormalized blend, mem(s) = N_s, slots f32 [B,H,T,d] (no mass
+   * column): the unnormalized read (engine.py:402-416) and the feature-mass
+   * read (engine.py:443-456), whose normalization happened on the query side
+   * (ts_b200_mass_query_fwd).  mass_columns is then ignored. */
+  int unnormalized;
 } ts_kread_args;
 
 int ts_b200_kread_fwd(const ts_kread_args* args, ts_stream_t stream);
@@ -317,6 +325,45 @@ typedef struct ts_kread_grad_args {
 } ts_kread_grad_args;
 
 int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad, ts_stream_t stream);
+
+/* ------------------------------------------------------------------ feature mass
+ *
+ * Query side of the feature-mass read (engine.dual_read_views.memory,
+ * src/thetascan/_core/ops/engine.py:443-456): each temporal view divides the
+ * query features by its own cumulative key-feature mass
+ *   mass_t[f] = sum_{i<=t} w(t-i) phi_k[i][f]
+ * (view.mass_cum: causal_prefix_sum, ema_cumsum or their stale difference,
+ * src/thetascan/_core/ops/interface.py:58-107, 216-230, 278-279, 306-307)
+ * before an unnormalized scan of that view:
+ *   q_scaled = phi_q / (mass + eps)   (bf16)
+ * w = 1 (log_alpha NULL), alpha_h^(t-i), or 1 - alpha_h^(t-i) (stale != 0).
+ */
+typedef struct ts_mass_args {
+  int batch, heads, tokens, width;  /* width m: even, 2..512 */
+  const void* phi_k;        /* bf16 [B,H,T,m] contiguous */
+  const void* phi_q;        /* bf16 [B,H,T,m] contiguous */
+  const float* log_alpha;   /* f32 [H] of the view, or NULL (plain prefix sum) */
+  int stale;                /* the stale view's mass */
+  float eps;
+  void* q_scaled;           /* bf16 [B,H,T,m] out (forward) */
+  const float* phi_q_f32;   /* f32 [B,H,T,m] phi(q), read instead of phi_q when set
+                             * (ts_feature_args.phi_q_f32: one rounding, of the quotient) */
+} ts_mass_args;
+
+int ts_b200_mass_query_fwd(const ts_mass_args* args, ts_stream_t stream);
+
+typedef struct ts_mass_grad_args {
+  const void* dq_scaled;    /* [B,H,T,m] gradient of q_scaled */
+  int dq_dtype;             /* TS_DTYPE_F32 or TS_DTYPE_BF16 */
+  float* dphi_q;            /* f32 [B,H,T,m], ACCUMULATED into */
+  float* dphi_k;            /* f32 [B,H,T,m], ACCUMULATED into (the mass path only) */
+  float* dlog_alpha;        /* f32 [H], ACCUMULATED, or NULL */
+  void* workspace;          /* ts_b200_mass_query_bwd_workspace_bytes(args) bytes */
+  size_t workspace_bytes;
+} ts_mass_grad_args;
+
+size_t ts_b200_mass_query_bwd_workspace_bytes(const ts_mass_args* args);
+int ts_b200_mass_query_bwd(const ts_mass_args* args, const ts_mass_grad_args* grad, ts_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -3,8 +3,8 @@
 1. Against the committed golden fixtures produced by the reference module
    itself (relu2 ridge with partial RoPE and a fast bank at ragged T=160;
    projected B-spline with a stale bank; softmax partition with a fast bank;
-   expanded relu2 with two recency branches): output, input gradient and
-   every parameter gradient.
+   expanded relu2 with two recency branches; softmax partition with the
+   feature-mass read): output, input gradient and every parameter gradient.
 2. Against the float64 oracle mixer on a config-2-shaped module (relu2 ridge
    with 2x random feature expansion, m=256, partial RoPE, fast bank).
 Tolerance: ``max|got - ref| / max|ref| <= 2e-2`` (bf16 streams).
@@ -38,7 +38,8 @@ def dev():
     return torch.device("cuda")
 
 
-GOLDEN_CASES = ["relu2_d64_ragged", "bspline_stale", "softmax_bank_fast", "relu2_expanded_rope"]
+GOLDEN_CASES = ["relu2_d64_ragged", "bspline_stale", "softmax_bank_fast", "relu2_expanded_rope",
+                "softmax_sum_feature_mass"]
 # The sharp-softmax fixture's blend gradient (-1.19, 0.93) is a sum over 40
 # tokens of differences between its fast and plain reads; its absolute error
 # on the GPU (~0.02) is the noise level of the same gradient in the random
@@ -53,11 +54,27 @@ def _bf16(t):
     return t.to(torch.bfloat16).to(t.dtype)
 
 
+def _straight(t):
+    return t + (_bf16(t) - t).detach()
+
+
 def _oracle_at_bf16_inputs(case):
     """The float64 oracle mixer (pinned to these fixtures by
-    tests/test_oracle_golden.py) on the bf16 values of x and the weights that
-    the GPU path consumes; gradients pass the rounding straight through."""
+    tests/test_oracle_golden.py) on the bf16 values that the GPU path reads:
+    x, the weights, the q/k/v projections and the L2-normalized q/k streams;
+    gradients pass the rounding straight through."""
+    from oracle import features as ofeatures
     from test_oracle_golden import _core_cfg
+    project, l2norm = omixer.project_qkv, ofeatures.l2norm
+    omixer.project_qkv = lambda p, cfg, x: tuple(_straight(t) for t in project(p, cfg, x))
+    ofeatures.l2norm = lambda x, eps: _straight(l2norm(x, eps))
+    try:
+        return _oracle_rounded(case, _core_cfg)
+    finally:
+        omixer.project_qkv, ofeatures.l2norm = project, l2norm
+
+
+def _oracle_rounded(case, _core_cfg):
     params = {}
     for n, t in case["params"].items():
         t = t.to(torch.float64).clone()
@@ -66,9 +83,9 @@ def _oracle_at_bf16_inputs(case):
             continue
         t.requires_grad_(True)
         params[n] = t
-    used = {n: (t + (_bf16(t) - t).detach() if n in BF16_INPUTS else t) for n, t in params.items()}
+    used = {n: (_straight(t) if n in BF16_INPUTS else t) for n, t in params.items()}
     x = case["x"].to(torch.float64).clone().requires_grad_(True)
-    y = omixer.mixer_forward(used, _core_cfg(case), x + (_bf16(x) - x).detach())
+    y = omixer.mixer_forward(used, _core_cfg(case), _straight(x))
     (y * case["out_weight"].to(torch.float64)).sum().backward()
     return y.detach(), x.grad, {n: t.grad for n, t in params.items() if t.requires_grad}
 

@@ -16,7 +16,7 @@ from thetascan_b200.config import ThetaScanConfig
 from thetascan_b200.mixer import ThetaScan
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-CASES = ["softmax_bank_fast", "relu2_expanded_rope", "bspline_stale", "relu2_d64_ragged"]
+CASES = ["softmax_bank_fast", "relu2_expanded_rope", "bspline_stale", "relu2_d64_ragged", "softmax_sum_feature_mass"]
 # Parameters the fixture generator overwrote after construction.
 OVERWRITTEN = ("W2.0", "fade_eta", "kernel_relu2_threshold")
 
@@ -31,7 +31,8 @@ def test_manifest_round_trip(name):
     assert ThetaScanConfig.from_dict(cfg.to_dict()) == cfg
 
 
-@pytest.mark.parametrize("name", ["softmax_bank_fast", "relu2_expanded_rope", "relu2_d64_ragged", "bspline_stale"])
+@pytest.mark.parametrize("name", ["softmax_bank_fast", "relu2_expanded_rope", "relu2_d64_ragged", "bspline_stale",
+                                  "softmax_sum_feature_mass"])
 def test_state_dict_and_seeded_init_match_reference(name):
     case = _fixtures()[name]
     cfg = ThetaScanConfig.from_dict(case["public_config"])

@@ -83,6 +83,7 @@ class FeatureArgs(ctypes.Structure):
         ("phi_k", ctypes.c_void_p), ("phi_q", ctypes.c_void_p), ("y0", ctypes.c_void_p),
         ("rope_rot", ctypes.c_int), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
         ("rope_pos0", ctypes.c_int), ("l2norm", ctypes.c_int), ("l2norm_eps", ctypes.c_float),
+        ("phi_q_f32", ctypes.c_void_p),
     ]
 
 
@@ -104,7 +105,7 @@ class KReadArgs(ctypes.Structure):
         ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("head_dim", ctypes.c_int),
         ("mode", ctypes.c_int), ("branches", ctypes.c_int), ("eps", ctypes.c_float),
         ("slots", c_ptr4), ("eta", ctypes.c_void_p), ("y0", ctypes.c_void_p), ("y", ctypes.c_void_p),
-        ("mass_columns", ctypes.c_int),
+        ("mass_columns", ctypes.c_int), ("unnormalized", ctypes.c_int),
     ]
 
 
@@ -112,6 +113,23 @@ class KReadGradArgs(ctypes.Structure):
     _fields_ = [
         ("dy", ctypes.c_void_p), ("dy_dtype", ctypes.c_int), ("dslots", c_ptr4),
         ("dy0", ctypes.c_void_p), ("deta", ctypes.c_void_p),
+    ]
+
+
+class MassArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("width", ctypes.c_int),
+        ("phi_k", ctypes.c_void_p), ("phi_q", ctypes.c_void_p), ("log_alpha", ctypes.c_void_p),
+        ("stale", ctypes.c_int), ("eps", ctypes.c_float), ("q_scaled", ctypes.c_void_p),
+        ("phi_q_f32", ctypes.c_void_p),
+    ]
+
+
+class MassGradArgs(ctypes.Structure):
+    _fields_ = [
+        ("dq_scaled", ctypes.c_void_p), ("dq_dtype", ctypes.c_int),
+        ("dphi_q", ctypes.c_void_p), ("dphi_k", ctypes.c_void_p), ("dlog_alpha", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -125,6 +143,10 @@ SIGNATURES.update({
     "ts_b200_kread_fwd": (ctypes.c_int, [ctypes.POINTER(KReadArgs), ctypes.c_void_p]),
     "ts_b200_kread_bwd": (ctypes.c_int, [ctypes.POINTER(KReadArgs), ctypes.POINTER(KReadGradArgs),
                                          ctypes.c_void_p]),
+    "ts_b200_mass_query_fwd": (ctypes.c_int, [ctypes.POINTER(MassArgs), ctypes.c_void_p]),
+    "ts_b200_mass_query_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MassArgs)]),
+    "ts_b200_mass_query_bwd": (ctypes.c_int, [ctypes.POINTER(MassArgs), ctypes.POINTER(MassGradArgs),
+                                              ctypes.c_void_p]),
 })
 
 _lock = threading.Lock()

@@ -427,8 +427,6 @@ class ThetaScanConfig:
                 return "the GN stale bank is not built"
             return None
         k = self.kernel
-        if k.read_normalization != "key_mass":
-            return f"kernel read_normalization={k.read_normalization!r} (only 'key_mass' is built)"
         if k.value_representation == "value_anchors":
             return "kernel value_anchors are not built"
         if k.sparsity != "none":

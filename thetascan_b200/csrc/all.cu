@@ -6,5 +6,6 @@
 #include "scan_bwd.cu"
 #include "feature.cu"
 #include "kread.cu"
+#include "mass.cu"
 #include "capi_kernel.cu"
 #include "capi_static.cu"

@@ -8,12 +8,15 @@ namespace ts {
 
 struct FeatParams;
 struct ReadParams;
+struct MassParams;
 int launch_feature_fwd(const FeatParams& p, cudaStream_t s);
 int launch_feature_bwd(const FeatParams& p, cudaStream_t s);
 size_t feature_fwd_smem(const FeatParams& p);
 size_t feature_bwd_smem(const FeatParams& p);
 int launch_kread_fwd(const ReadParams& p, cudaStream_t s);
 int launch_kread_bwd(const ReadParams& p, cudaStream_t s);
+int launch_mass_fwd(const MassParams& p, cudaStream_t s);
+int launch_mass_bwd(const MassParams& p, cudaStream_t s);
 
 namespace {
 constexpr size_t kMaxSmemBlock = 232448;
@@ -69,6 +72,9 @@ int build_feature_params(const ts_feature_args* a, FeatParams* p) {
   p->scale_scalar = a->spline_scale_scalar;
   p->phi[0] = static_cast<__nv_bfloat16*>(a->phi_k);
   p->phi[1] = static_cast<__nv_bfloat16*>(a->phi_q);
+  p->phi_q32 = a->q ? a->phi_q_f32 : nullptr;
+  if (p->phi_q32 && (reinterpret_cast<uintptr_t>(p->phi_q32) & 15))
+    return set_error(TS_ERR_VALUE, "feature: phi_q_f32 must be 16-byte aligned");
   p->y0 = a->y0;
   p->nsel = a->q ? 2 : 1;
   p->sel0 = 0;
@@ -110,11 +116,35 @@ int build_read_params(const ts_kread_args* a, ReadParams* p) {
   p->eps = a->eps;
   if (a->mass_columns < 0 || a->mass_columns > 2)
     return set_error(TS_ERR_VALUE, "kread: mass_columns must be 1 or 2 (0 = 1)");
-  p->mass_cols = a->mass_columns == 2 ? 2 : 1;
+  p->mass_cols = a->unnormalized ? 0 : a->mass_columns == 2 ? 2 : 1;
   for (int s = 0; s <= J; ++s) p->out[s] = a->slots[s];
   p->eta = a->eta;
   p->y0 = a->y0;
   p->y = static_cast<__nv_bfloat16*>(a->y);
+  return TS_OK;
+}
+int build_mass_params(const ts_mass_args* a, MassParams* p) {
+  if (!a) return set_error(TS_ERR_VALUE, "mass: null arguments");
+  if (a->batch < 1 || a->heads < 1 || a->tokens < 1) return set_error(TS_ERR_VALUE, "mass: sizes must be >= 1");
+  if (a->width < 2 || a->width > 512 || (a->width & 1))
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "mass: feature width %d must be even and in 2..512", a->width);
+  if (!a->phi_k || (!a->phi_q && !a->phi_q_f32)) return set_error(TS_ERR_VALUE, "mass: null phi_k or phi_q");
+  if (a->stale && !a->log_alpha) return set_error(TS_ERR_VALUE, "mass: the stale mass needs a log_alpha");
+  if ((reinterpret_cast<uintptr_t>(a->phi_k) | reinterpret_cast<uintptr_t>(a->phi_q)) & 3)
+    return set_error(TS_ERR_VALUE, "mass: phi_k and phi_q must be 4-byte aligned");
+  std::memset(p, 0, sizeof(*p));
+  p->B = a->batch;
+  p->H = a->heads;
+  p->T = a->tokens;
+  p->m = a->width;
+  p->phi_k = static_cast<const __nv_bfloat16*>(a->phi_k);
+  p->phi_q32 = a->phi_q_f32;
+  if (reinterpret_cast<uintptr_t>(a->phi_q_f32) & 7) return set_error(TS_ERR_VALUE, "mass: phi_q_f32 must be 8-byte aligned");
+  p->phi_q = static_cast<const __nv_bfloat16*>(a->phi_q);
+  p->la = a->log_alpha;
+  p->stale = a->stale ? 1 : 0;
+  p->eps = a->eps;
+  p->qs = static_cast<__nv_bfloat16*>(a->q_scaled);
   return TS_OK;
 }
 }  // namespace
@@ -186,6 +216,40 @@ int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad,
   p.dy0 = grad->dy0;
   p.deta = grad->deta;
   return launch_kread_bwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_mass_query_fwd(const ts_mass_args* args, ts_stream_t stream) {
+  MassParams p;
+  if (int e = build_mass_params(args, &p)) return e;
+  if (!p.qs) return set_error(TS_ERR_VALUE, "mass: null q_scaled");
+  return launch_mass_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ts_b200_mass_query_bwd_workspace_bytes(const ts_mass_args* args) {
+  MassParams p;
+  if (build_mass_params(args, &p) != TS_OK) return 0;
+  return static_cast<size_t>(p.B) * p.H * p.T * p.m * sizeof(float);
+}
+
+int ts_b200_mass_query_bwd(const ts_mass_args* args, const ts_mass_grad_args* grad, ts_stream_t stream) {
+  MassParams p;
+  if (int e = build_mass_params(args, &p)) return e;
+  if (!grad || !grad->dq_scaled || !grad->dphi_q || !grad->dphi_k)
+    return set_error(TS_ERR_VALUE, "mass_bwd: dq_scaled, dphi_q and dphi_k are required");
+  const size_t need = static_cast<size_t>(p.B) * p.H * p.T * p.m * sizeof(float);
+  if (!grad->workspace || grad->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "mass_bwd: workspace of %zu bytes needed", need);
+  if (((reinterpret_cast<uintptr_t>(grad->dphi_q) | reinterpret_cast<uintptr_t>(grad->dphi_k) |
+        reinterpret_cast<uintptr_t>(grad->workspace)) & 7) ||
+      (reinterpret_cast<uintptr_t>(grad->dq_scaled) & (grad->dq_dtype == TS_DTYPE_BF16 ? 3 : 7)))
+    return set_error(TS_ERR_VALUE, "mass_bwd: misaligned gradient buffers");
+  p.dqs = grad->dq_scaled;
+  p.dqs_bf16 = grad->dq_dtype == TS_DTYPE_BF16;
+  p.dphi_q = grad->dphi_q;
+  p.dphi_k = grad->dphi_k;
+  p.dla = grad->dlog_alpha;
+  p.dmass = static_cast<float*>(grad->workspace);
+  return launch_mass_bwd(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

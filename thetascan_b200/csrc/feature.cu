@@ -44,6 +44,7 @@ struct FeatParams {
   float bound;
   // forward outputs
   __nv_bfloat16* phi[2];    // [B, H, T, m]
+  float* phi_q32;           // [B, H, T, m] f32 copy of phi_q, or null
   float* y0;                // [B, H, T, d] or null (q only)
   // backward
   const void* dphi[2];      // [B, H, T, m], f32 or bf16
@@ -498,7 +499,7 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
 // phi of this thread's row and column chunks into the phi tile (bf16).
 template <int KIND>
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
-                                                const Tile& tphi, bool zero_row) {
+                                                const Tile& tphi, bool zero_row, float* row32 = nullptr) {
   const int row = my_row(), part = my_part();
   if constexpr (KIND == kBspline) {
     const float sc = ctl_scale(p, h);
@@ -525,6 +526,11 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
             f[q] = (!zero_row && w >= 0 && w < 4) ? pick4(val, w) * invP : 0.f;
           }
           tile_st16(tphi, row, (pj * p.nb + i) / 8, pack8(f));
+          if (row32 != nullptr && !zero_row) {
+            float4* dst = reinterpret_cast<float4*>(row32 + pj * p.nb + i);
+            dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+            dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+          }
         }
       }
     }
@@ -539,6 +545,9 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
       }
       tile_st16(tphi, row, c / 8, pack8(f));
       tile_st16(tphi, row, c / 8 + 1, pack8(f + 8));
+      if (row32 != nullptr && !zero_row) {
+        for (int e = 0; e < 16 && c + e < p.m; ++e) row32[c + e] = f[e];
+      }
     }
   }
 }
@@ -585,7 +594,9 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
   const RowState st = row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{});
   // Rows past the sequence end get zero features, so the decode below and the
   // stored tile are exact zeros there.
-  phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows);
+  float* row32 = (sel == 1 && p.phi_q32 != nullptr && row < rows)
+                    ? p.phi_q32 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + row) * p.m : nullptr;
+  phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows, row32);
   __syncthreads();
   __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
   store_tile(tl.phi, out, p.m, rows, p.m);

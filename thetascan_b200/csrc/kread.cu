@@ -1,4 +1,6 @@
-// Key-mass normalized read and temporal-view blend of the kernel family.
+// Key-mass normalized read and temporal-view blend of the kernel family
+// (also the unnormalized blend, mass_cols = 0: mem(s) = N_s, for the
+// unnormalized and feature-mass reads, engine.py:402-416, 443-456).
 //
 // The scans deliver, per retention slot s, the augmented read
 // out_s = [N_s | D_s] (numerator and score mass, reference engine.py:430-442),
@@ -31,7 +33,7 @@ struct ReadParams {
   int B, H, T, d;
   int J;                       // recency branches (slots 1..J)
   int mode;                    // 0 sum, 1 fast, 2 stale
-  int mass_cols;               // mass columns after the d value columns (1 or 2)
+  int mass_cols;               // mass columns after the d value columns (1 or 2; 0: unnormalized read)
   float eps;
   const float* out[5];         // slot outputs [B, H, T, d + mass_cols] f32
   const float* eta;            // [J, H] f32
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_fwd_kernel(ReadParams p
     if (t >= p.T) break;
     const size_t row = bh * p.T + t;  // [B, H, T] row index
     float scale[5];
-    for (int s = 0; s < n; ++s) scale[s] = coef[s] / (slot_val(p, s, row, p.d) + p.eps);
+    for (int s = 0; s < n; ++s) scale[s] = p.mass_cols ? coef[s] / (slot_val(p, s, row, p.d) + p.eps) : coef[s];
     __nv_bfloat16* yrow = p.y + ((static_cast<size_t>(b) * p.T + t) * p.H + h) * p.d;
     for (int c = lane; c < p.d; c += 32) {
       float acc = __ldg(p.y0 + row * p.d + c);
@@ -119,6 +121,17 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p
     };
     float dymem[5];
     for (int s = 0; s < n; ++s) {
+      if (p.mass_cols == 0) {
+        // unnormalized read: mem_s = N_s
+        float dot = 0.f;
+        for (int c = lane; c < p.d; c += 32) {
+          const float dyc = dy_at(c);
+          p.dout[s][row * width + c] = __float2bfloat16_rn(coef[s] * dyc);
+          dot += dyc * slot_val(p, s, row, c);
+        }
+        dymem[s] = warp_sum(dot);
+        continue;
+      }
       const float inv = 1.f / (slot_val(p, s, row, p.d) + p.eps);
       float exact = 0.f, consistent = 0.f;
       for (int c = lane; c < p.d; c += 32) {

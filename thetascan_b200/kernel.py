@@ -44,6 +44,7 @@ class KernelSpec:
     basis: int = 8              # B-spline basis per projection
     bound: float = 3.0
     spline_scale: float = 1.0   # fixed B-spline scale when no learned scale
+    read: str = "key_mass"      # key_mass | feature_mass | none (engine.py:402-456)
 
 
 def _ptr(t):
@@ -89,7 +90,13 @@ def _kread_args(spec, slots, eta, y0, y):
         a.slots[i] = s.data_ptr()
     a.eta, a.y0, a.y = _ptr(eta), y0.data_ptr(), _ptr(y)
     a.mass_columns = MASS_COLS
+    a.unnormalized = 0 if spec.read == "key_mass" else 1
     return a
+
+
+def _slot_width(spec, d):
+    """Columns of a scan read: [N | D | D] for the key-mass read, N otherwise."""
+    return d + MASS_COLS if spec.read == "key_mass" else d
 
 
 @dataclass(frozen=True)
@@ -460,9 +467,210 @@ class _ShardStageB(torch.autograd.Function):
         return None, dS, None, None, None
 
 
+class _MassQuery(torch.autograd.Function):
+    """``phi_q / (mass + eps)`` of one view (``ts_b200_mass_query_fwd``), the
+    query of that view's unnormalized scan in the feature-mass read."""
+
+    @staticmethod
+    def _args(phi_k, phi_q, la, stale, eps, out):
+        """``phi_q`` bf16, or f32 (read instead, one rounding less)."""
+        B, H, T, m = phi_k.shape
+        a = _lib.MassArgs()
+        a.batch, a.heads, a.tokens, a.width = B, H, T, m
+        a.phi_k = phi_k.data_ptr()
+        if phi_q.dtype == torch.float32:
+            a.phi_q_f32 = phi_q.data_ptr()
+        else:
+            a.phi_q = phi_q.data_ptr()
+        a.log_alpha = _ptr(la)
+        a.stale, a.eps = 1 if stale else 0, eps
+        a.q_scaled = _ptr(out)
+        return a
+
+    @staticmethod
+    def forward(ctx, phi_k, phi_q, la, stale, eps):
+        lib = _lib.load()
+        la32 = None if la is None else la.detach().reshape(-1).to(torch.float32).contiguous()
+        qn = torch.empty_like(phi_q)
+        a = _MassQuery._args(phi_k, phi_q, la32, stale, eps, qn)
+        _lib.check(lib.ts_b200_mass_query_fwd(ctypes.byref(a), _stream()))
+        ctx.stale, ctx.eps, ctx.la32 = stale, eps, la32
+        ctx.la_meta = None if la is None else (la.dtype, la.shape)
+        ctx.save_for_backward(phi_k, phi_q)
+        return qn
+
+    @staticmethod
+    def backward(ctx, dqn):
+        lib = _lib.load()
+        phi_k, phi_q = ctx.saved_tensors
+        a = _MassQuery._args(phi_k, phi_q, ctx.la32, ctx.stale, ctx.eps, None)
+        dqn = dqn.contiguous()
+        if dqn.dtype not in (torch.bfloat16, torch.float32):
+            dqn = dqn.float()
+        dphi_q = torch.zeros(phi_q.shape, dtype=torch.float32, device=phi_q.device)
+        dphi_k = torch.zeros_like(dphi_q)
+        dla = None if ctx.la32 is None else torch.zeros_like(ctx.la32)
+        ws = _workspace(lib, lib.ts_b200_mass_query_bwd_workspace_bytes, a, phi_q.device)
+        g = _lib.MassGradArgs()
+        g.dq_scaled = dqn.data_ptr()
+        g.dq_dtype = _lib.TS_DTYPE_BF16 if dqn.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
+        g.dphi_q, g.dphi_k, g.dlog_alpha = dphi_q.data_ptr(), dphi_k.data_ptr(), _ptr(dla)
+        g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
+        _lib.check(lib.ts_b200_mass_query_bwd(ctypes.byref(a), ctypes.byref(g), _stream()))
+        if dla is not None:
+            dla = dla.to(ctx.la_meta[0]).reshape(ctx.la_meta[1])
+        return dphi_k, dphi_q, dla, None, None
+
+
+class _KernelCoreViews(torch.autograd.Function):
+    """Unnormalized and feature-mass reads (engine.py:402-416, 443-456) in one
+    autograd stage, so that the gradients of phi_q and phi_k -- whose scan and
+    mass parts nearly cancel under the feature-mass quotient -- are summed in
+    f32 before the feature backward:
+
+    forward   features -> [per view: phi_q / (mass_v + eps)] -> unnormalized
+              scans (f32 reads) -> unnormalized blend
+    backward  blend -> scans (f32 dq, dk, dv) -> mass backward -> features
+    """
+
+    @staticmethod
+    def forward(ctx, spec, q, k, v, W1, W2, thr, bias, gain, scale, log_alphas, etas):
+        lib = _lib.load()
+        B, H, T, d = q.shape
+        dev = q.device
+        ctl = _controls(thr, bias, gain, scale)
+        W1b = W1.detach().to(torch.bfloat16).contiguous()
+        W2b = W2.detach().to(torch.bfloat16).contiguous()
+        m = W1.shape[1] * (spec.basis if spec.kind == "projected_bspline" else 1)
+        phi_k = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
+        phi_q = torch.empty_like(phi_k)
+        y0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, y0)
+        # the feature-mass quotient reads phi(q) before its bf16 rounding
+        phi_q32 = torch.empty(B, H, T, m, dtype=torch.float32, device=dev) if spec.read == "feature_mass" else None
+        fa.phi_q_f32 = _ptr(phi_q32)
+        _lib.check(lib.ts_b200_feature_fwd(ctypes.byref(fa), _stream()))
+        J = 0 if log_alphas is None else log_alphas.shape[0]
+        las = [None] + [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(J)]
+        flags = [False] + [spec.mode == "stale"] * J
+        slots = [torch.empty(B, H, T, d, dtype=torch.float32, device=dev) for _ in las]
+        if spec.read == "none":
+            groups = [(phi_q, list(range(len(las))))]
+        else:
+            groups = []
+            for i, la in enumerate(las):
+                qn = torch.empty_like(phi_q)
+                ma = _MassQuery._args(phi_k, phi_q32, la, flags[i], spec.eps, qn)
+                _lib.check(lib.ts_b200_mass_query_fwd(ctypes.byref(ma), _stream()))
+                groups.append((qn, [i]))
+        scans = []
+        for query, idx in groups:
+            sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0,
+                             stale=[flags[i] for i in idx])
+            ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
+            sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
+            _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
+            scans.append((query, idx, ws))
+        eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
+        y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=dev)
+        ra = _kread_args(spec, slots, eta, y0, y)
+        _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
+        ctx.spec, ctx.ctl, ctx.W, ctx.las, ctx.flags = spec, ctl, (W1b, W2b), las, flags
+        ctx.scans, ctx.slots, ctx.eta, ctx.y0 = scans, slots, eta, y0
+        ctx.phi = (phi_q, phi_k, phi_q32)
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype, W1.dtype, W2.dtype)
+        ctx.has_eta = etas is not None
+        ctx.save_for_backward(q, k, v)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _lib.load()
+        q, k, v = ctx.saved_tensors
+        spec, las, flags, slots = ctx.spec, ctx.las, ctx.flags, ctx.slots
+        phi_q, phi_k, phi_q32 = ctx.phi
+        W1b, W2b = ctx.W
+        B, H, T, d = q.shape
+        m = phi_q.shape[-1]
+        dev = q.device
+        dy = dy.contiguous()
+        if dy.dtype not in (torch.bfloat16, torch.float32):
+            dy = dy.float()
+        # 1. blend
+        ra = _kread_args(spec, slots, ctx.eta, ctx.y0, None)
+        ga = _lib.KReadGradArgs()
+        ga.dy = dy.data_ptr()
+        ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
+        dslots = [torch.empty(B, H, T, d, dtype=torch.bfloat16, device=dev) for _ in slots]
+        for i, t in enumerate(dslots):
+            ga.dslots[i] = t.data_ptr()
+        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        ga.dy0 = dy0.data_ptr()
+        n = len(slots)
+        deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
+        ga.deta = _ptr(deta)
+        _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
+        # 2. scans (f32 gradients), then the mass of each view
+        dphi_q = torch.zeros(B, H, T, m, dtype=torch.float32, device=dev)
+        dphi_k = torch.zeros_like(dphi_q)
+        dv = torch.zeros(B, H, T, d, dtype=torch.float32, device=dev)
+        dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
+        for query, idx, ws in ctx.scans:
+            sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0, ws,
+                             stale=[flags[i] for i in idx])
+            sg = _lib.ScanGradArgs()
+            dq_s = torch.empty(B, H, T, m, dtype=torch.float32, device=dev)
+            dk_s = torch.empty_like(dq_s)
+            dv_s = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+            for j, i in enumerate(idx):
+                sg.dout[j] = dslots[i].data_ptr()
+                sg.dlog_alpha[j] = _ptr(dlas[i])
+            sg.dq, sg.dk, sg.dv = dq_s.data_ptr(), dk_s.data_ptr(), dv_s.data_ptr()
+            sg.grad_dtype = _lib.TS_DTYPE_F32
+            gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+            sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
+            _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
+            del gws
+            dphi_k += dk_s
+            dv += dv_s
+            if spec.read == "none":
+                dphi_q += dq_s
+                continue
+            i = idx[0]
+            ma = _MassQuery._args(phi_k, phi_q32, las[i], flags[i], spec.eps, None)
+            mg = _lib.MassGradArgs()
+            mg.dq_scaled, mg.dq_dtype = dq_s.data_ptr(), _lib.TS_DTYPE_F32
+            mg.dphi_q, mg.dphi_k, mg.dlog_alpha = dphi_q.data_ptr(), dphi_k.data_ptr(), _ptr(dlas[i])
+            mws = _workspace(lib, lib.ts_b200_mass_query_bwd_workspace_bytes, ma, dev)
+            mg.workspace, mg.workspace_bytes = mws.data_ptr(), mws.numel()
+            _lib.check(lib.ts_b200_mass_query_bwd(ctypes.byref(ma), ctypes.byref(mg), _stream()))
+        # 3. features
+        ctl = ctx.ctl
+        fa = _feature_args(spec, q, k, W1b, W2b, ctl, phi_k, phi_q, None)
+        fg = _lib.FeatureGradArgs()
+        fg.dphi_k, fg.dphi_q, fg.dphi_dtype = dphi_k.data_ptr(), dphi_q.data_ptr(), _lib.TS_DTYPE_F32
+        fg.dy0 = dy0.data_ptr()
+        dk = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        dq = torch.empty_like(dk)
+        fg.dk, fg.dq = dk.data_ptr(), dq.data_ptr()
+        dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
+        dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+        grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
+                 for key in ("thr", "bias", "gain", "scale")}
+        fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+        fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
+        fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
+        _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+        qd, kd, vd, w1d, w2d = ctx.dtypes
+        dla = None if n == 1 else torch.stack(dlas[1:])
+        return (None, dq.to(qd), dk.to(kd), dv.to(vd), dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"],
+                grads["gain"], grads["scale"], dla, deta if ctx.has_eta else None)
+
+
 class _KRead(torch.autograd.Function):
-    """Key-mass read and bank blend as one autograd stage: y0 and the slots
-    in, token-major y out."""
+    """Read and bank blend as one autograd stage (key-mass normalized, or
+    unnormalized for the unnormalized and feature-mass reads): y0 and the
+    slots in, token-major y out."""
 
     @staticmethod
     def forward(ctx, spec, y0, etas, *slots):
@@ -490,7 +698,7 @@ class _KRead(torch.autograd.Function):
         ga = _lib.KReadGradArgs()
         ga.dy = dy.data_ptr()
         ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
-        dslots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev) for _ in slots]
+        dslots = [torch.empty(B, H, T, _slot_width(ctx.spec, d), dtype=torch.bfloat16, device=dev) for _ in slots]
         for i, s in enumerate(dslots):
             ga.dslots[i] = s.data_ptr()
         dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
@@ -523,6 +731,8 @@ def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | N
     if spec.mode == "stale":
         raise NotImplementedError("b200 backend: sequence shards of a stale bank are not built (stale scans take "
                                   "no boundary states); fast banks and the plain sum shard")
+    if spec.read != "key_mass":
+        raise NotImplementedError("b200 backend: sequence shards read with key mass only")
     hold = _ShardScan()
     phi_q, phi_k, y0, U = _ShardStageA.apply(hold, spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain,
                                              spline_scale, log_alphas)
@@ -554,6 +764,8 @@ def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None,
         raise ValueError("kernel_core_qkv: last dimension must be 3*H*d")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core_qkv: log_alphas are required exactly for a bank (mode fast/stale)")
+    if spec.read != "key_mass":
+        raise NotImplementedError("kernel_core_qkv: the fused projection path reads with key mass; use kernel_core")
     return _KernelCoreQKV.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale,
                                 log_alphas, etas)
 
@@ -577,4 +789,9 @@ def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias
             raise ValueError("b200 backend: streams need a contiguous innermost dimension")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core: log_alphas are required exactly for a bank (mode fast/stale)")
+    if spec.read not in ("key_mass", "feature_mass", "none"):
+        raise ValueError(f"kernel_core: unknown read normalization {spec.read!r}")
+    if spec.read != "key_mass":
+        return _KernelCoreViews.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale,
+                                      log_alphas, etas)
     return _KernelCore.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas)

@@ -226,7 +226,7 @@ class ThetaScanCore(nn.Module):
         self.spec = KernelSpec(
             kind=k.feature_map, mode=("sum" if t.mode == "sum" else t.bank_mode),
             eps=1e-6, gain=float(k.kernel_sharpness), basis=k.bspline_basis_count,
-            bound=float(k.bspline_bound), spline_scale=float(k.bspline_scale))
+            bound=float(k.bspline_bound), spline_scale=float(k.bspline_scale), read=k.read_normalization)
         self._rot = _rope_width(d, cfg.rope.mode, cfg.rope.fraction)
 
     # -------------------------------------------------------------- helpers
@@ -353,8 +353,9 @@ class ThetaScanCore(nn.Module):
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
         if shard is not None:
-            if self.proj_qkv is None or self.vmlp_in is not None:
-                raise NotImplementedError("sequence shards need the fused q/k/v projection without a value MLP")
+            if self.proj_qkv is None or self.vmlp_in is not None or self.spec.read != "key_mass":
+                raise NotImplementedError("sequence shards need the fused q/k/v projection without a value MLP "
+                                          "and the key-mass read")
             qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
             pos0 = shard.rank * T
             cos = sin = None
@@ -363,7 +364,7 @@ class ThetaScanCore(nn.Module):
             prologue = Prologue(self._rot, cos, sin, 1e-6, pos0)
             y = kernel_core_sharded(qkv, H, W1, W2, self.spec, prologue, shard, log_alphas=log_alphas, etas=etas,
                                     **self.kernel_controls())
-        elif self.proj_qkv is not None and self.vmlp_in is None:
+        elif self.proj_qkv is not None and self.vmlp_in is None and self.spec.read == "key_mass":
             # Fused projection layout: RoPE and the L2 norm run inside the
             # feature kernels, v is read from the projection in place.
             qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
