@@ -19,7 +19,9 @@ read (engine.dual_read_views.layer, engine.py:455-528), per temporal view:
   h_q = sigma(rmsnorm(pre) [- tau]), base = W2 h_q,
   mem = scan(h_q; h, [lambda | 1]) normalized (read_norm) or scan(h_q; h, lambda),
   y_view = q + base + mem;
-views blended like the kernel family (block.py:676-718).
+views blended like the kernel family (block.py:676-718); a stale bank
+subtracts eta_j (y_stale_j - y_base), y_base the zero-memory read
+q + W2 sigma(rmsnorm(W1 q) [- tau]) (block.py:697-718).
 """
 from __future__ import annotations
 
@@ -117,5 +119,8 @@ def gn_core(q, k, v, W1, W2, tau, *, nonlin: str, read_norm: bool, read_norm_w1:
             mem = _combine(scan_fn(hq.to(h_k.dtype), h_k, lam, retentions), view)
         outs.append(q + base + mem)
     if J and mode == "stale":
-        raise NotImplementedError("GN oracle: stale banks are not restated")
+        # the zero-memory read of the stale blend (NullAccumulator, interface.py:
+        # 310-327): every scan is zero, so pre = W1 q and mem = 0
+        h_base = activation(nonlin, _thresholded(features.rmsnorm(a, eps)[0], tau))
+        base_out = q + torch.einsum("hdm,bhtm->bhtd", W2, h_base)
     return blend_outputs(outs, base_out, mode, etas) if J else outs[0]

@@ -109,6 +109,12 @@ MIXER_CONFIGS = {
         kernel=dict(feature_map="relu2_ridge"),
         rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
         B=1, T=160, dtype="float32"),
+    # The same shape with a stale bank (the zero-memory base read in the blend).
+    "gn_d64_stale": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5),
+        temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=1, T=160, dtype="float32"),
 }
 
 
@@ -188,6 +194,12 @@ GN_CONFIGS = {
         gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
         rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
         B=1, T=160, dtype="float32"),
+    # The same shape with a stale bank (the zero-memory base read in the blend).
+    "gn_d64_stale": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5),
+        temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=1, T=160, dtype="float32"),
 }
 
 GN_CORE_KEYS = (

@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 BF16_TOL = 2e-2
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 CASES = ["gn_both_relu2_bank", "gn_both_threshold_expanded", "gn_w2_relu2_sum", "gn_none_silu_bank2",
-         "gn_d64_ragged"]
+         "gn_d64_ragged", "gn_d64_stale"]
 
 
 def rel_err(got, want):

@@ -62,9 +62,10 @@ def test_presets_and_unsupported_configs():
         ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn", gn=GNConfig(nonlinearity="swiglu")))
     ThetaScan(ThetaScanConfig.from_dict(_fixtures()["bspline_stale"]["public_config"]))
     from thetascan_b200.config import TemporalConfig
+    ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn",
+                              temporal=TemporalConfig(mode="bank", bank_mode="stale")))
     with pytest.raises(NotImplementedError):
-        ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn",
-                                  temporal=TemporalConfig(mode="bank", bank_mode="stale")))
+        ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, temporal=TemporalConfig(mode="ema")))
     with pytest.raises(ValueError):
         ThetaScanConfig(runtime=__import__("thetascan_b200.config", fromlist=["RuntimeConfig"])
                         .RuntimeConfig(backend="bogus")).validate()

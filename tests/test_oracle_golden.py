@@ -133,7 +133,7 @@ def test_expansion_maps_match_reference_buffers():
 
 
 GN_CASES = ["gn_both_relu2_bank", "gn_both_threshold_expanded", "gn_w2_relu2_sum", "gn_none_silu_bank2",
-            "gn_d64_ragged"]
+            "gn_d64_ragged", "gn_d64_stale"]
 
 
 @pytest.mark.parametrize("name", GN_CASES)

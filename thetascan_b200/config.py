@@ -10,7 +10,7 @@ package executes that backend only (``"auto"`` resolves to it).
 
 Validation restates the reference's rules for the fields this package reads
 and raises ``NotImplementedError`` for configurations the GPU path does not
-cover yet (GN swiglu and two-step Jacobians, EMA decay gates, GN stale banks, value anchors,
+cover yet (GN swiglu and two-step Jacobians, EMA decay gates, value anchors,
 relative sparsity, feature-space RoPE).
 """
 from __future__ import annotations
@@ -423,8 +423,6 @@ class ThetaScanConfig:
                 return "GN jacobian_steps=2 is not built"
             if self.depth != 1:
                 return "GN depth > 1 is not built"
-            if self.temporal.mode == "bank" and self.temporal.bank_mode == "stale":
-                return "the GN stale bank is not built"
             return None
         k = self.kernel
         if k.value_representation == "value_anchors":

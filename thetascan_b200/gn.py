@@ -112,9 +112,10 @@ def _thresholded(pre, tau):
 
 
 def _views(mode, J):
-    """Retention slots of each view: slot 0 the plain sum, 1+j branch j (fast bank)."""
-    if mode != "fast" and J:
-        raise NotImplementedError("b200 GN: only the plain sum and fast banks are built")
+    """Retention slots of each view: slot 0 the plain sum, 1+j branch j (its
+    decayed scan for a fast bank, its stale scan for a stale bank)."""
+    if J and mode not in ("fast", "stale"):
+        raise ValueError(f"b200 GN: unknown bank mode {mode!r}")
     return [0] + [1 + j for j in range(J)]
 
 
@@ -188,6 +189,8 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
     J = 0 if log_alphas is None else log_alphas.shape[0]
     las = [None] + [log_alphas[j].float() for j in range(J)]
     slots = _views(mode, J)
+    stale = [False] + [mode == "stale"] * J
+    flags = stale if any(stale) else None
 
     def query_pre(qq, w1, *t):
         a = torch.einsum("hmd,bhtd->bhtm", w1, qq)
@@ -196,10 +199,10 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
     a_q, h0 = per_token_f32(query_pre, qf, W1f, *extra)
     # stage 1, shared by all views: the correction of the hidden preactivation
     if read_norm_w1:
-        reads = _scan(h0, h_k, g, True, las)
+        reads = _scan(h0, h_k, g, True, las, flags)
         pres = [a_q + reads[s][..., :m] / (reads[s][..., m:] + eps) for s in slots]
     else:
-        reads = _scan(q, k, g, False, las)
+        reads = _scan(q, k, g, False, las, flags)
         pres = [a_q + reads[s] for s in slots]
 
     def features(pre, w2, *t):
@@ -210,10 +213,17 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
     outs = []
     for s, pre in zip(slots, pres):
         hq, base = per_token_f32(features, pre, W2f, *extra)
-        c = _scan(hq, h_k, lam, bool(read_norm), [las[s]])[0]
+        c = _scan(hq, h_k, lam, bool(read_norm), [las[s]], [True] if stale[s] else None)[0]
         mem = c[..., :d] / (c[..., d:] + eps) if read_norm else c
         outs.append(qf + base + mem)
     y = outs[0]
+    if J and mode == "stale":
+        # y - sum_j eta_j (y_stale_j - y_base), y_base the zero-memory read
+        # (pre = W1 q, no memory term; block.py:697-718)
+        y_base = qf + per_token_f32(features, a_q, W2f, *extra)[1]
+        for j in range(J):
+            y = y - etas[j].float().view(1, -1, 1, 1) * (outs[1 + j] - y_base)
+        return y
     for j in range(J):
         y = y + etas[j].float().view(1, -1, 1, 1) * (outs[1 + j] - outs[0])
     return y
