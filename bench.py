@@ -44,6 +44,9 @@ CONFIGS = {
     "small": dict(B=2, T=1024, D=512, H=8, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
     # config-2 shapes at batch 2: inputs still larger than L2, for profiler captures
     "c2b2": dict(B=2, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+    # config 4 at batch 1 (profiling captures of its tile kernels)
+    "c4b1": dict(B=1, T=32768, D=1024, H=16, mult=2, expansion=1, fmap="projected_bspline", basis=16,
+                 rope="partial", J=3, retentions=(0.9, 0.99, 0.999)),
     # config 4: B-spline features (16 basis functions, m = 2d = 128, P = 8
     # projections), bank of three recency branches 0.9 / 0.99 / 0.999 plus the
     # sum view; with --gpus N the 32K-token sequences are split into N shards.

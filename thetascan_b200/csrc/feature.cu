@@ -504,6 +504,11 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
   if constexpr (KIND == kBspline) {
     const float sc = ctl_scale(p, h);
     const float invP = 1.f / static_cast<float>(p.P);
+    // This thread's projections pj = kParts * i + part, gathered first so that
+    // the basis evaluation below is one compact loop (one copy of its code).
+    float a_own[kMaxSplineOwn];
+#pragma unroll
+    for (int i = 0; i < kMaxSplineOwn; ++i) a_own[i] = 0.f;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const int c = 16 * cc;
@@ -511,26 +516,29 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
       float a[16];
       tmem_ld16(ta_row + c, a);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int pj = c + e;
-        if ((e % kParts) != part || pj >= p.P) continue;
-        float val[4], der[4];
-        int first;
-        bool inside;
-        bspline_local(a[e] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
-        for (int i = 0; i < p.nb; i += 8) {
-          float f[8];
+      for (int e = 0; e < 16; ++e)
+        if ((e % kParts) == part) a_own[(c + e) / kParts] = a[e];
+    }
+#pragma unroll 1
+    for (int i = 0; i < kMaxSplineOwn; ++i) {
+      const int pj = kParts * i + part;
+      if (pj >= p.P) break;
+      float val[4], der[4];
+      int first;
+      bool inside;
+      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
+      for (int ii = 0; ii < p.nb; ii += 8) {
+        float f[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int w = i + q - first;
-            f[q] = (!zero_row && w >= 0 && w < 4) ? pick4(val, w) * invP : 0.f;
-          }
-          tile_st16(tphi, row, (pj * p.nb + i) / 8, pack8(f));
-          if (row32 != nullptr && !zero_row) {
-            float4* dst = reinterpret_cast<float4*>(row32 + pj * p.nb + i);
-            dst[0] = make_float4(f[0], f[1], f[2], f[3]);
-            dst[1] = make_float4(f[4], f[5], f[6], f[7]);
-          }
+        for (int q = 0; q < 8; ++q) {
+          const int w = ii + q - first;
+          f[q] = (!zero_row && w >= 0 && w < 4) ? pick4(val, w) * invP : 0.f;
+        }
+        tile_st16(tphi, row, (pj * p.nb + ii) / 8, pack8(f));
+        if (row32 != nullptr && !zero_row) {
+          float4* dst = reinterpret_cast<float4*>(row32 + pj * p.nb + ii);
+          dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+          dst[1] = make_float4(f[4], f[5], f[6], f[7]);
         }
       }
     }
@@ -552,6 +560,17 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
   }
 }
 
+// Persistent over tiles: CTA (c, h) owns head h's tiles c, c + G, c + 2G, ...
+// of the (b, sel, n) tiles of that head (G = gridDim.x), so W1 and W2 are
+// staged once, TMEM and the barrier are set up once, and the next tile's rows
+// are copied in (cp.async, a second x buffer) while this tile computes.
+__device__ __forceinline__ void feature_tile_coords(const FeatParams& p, int i, int NT, int& b, int& sel, int& n) {
+  n = i % NT;
+  const int rest = i / NT;
+  sel = p.sel0 + rest % p.nsel;
+  b = rest / p.nsel;
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -559,18 +578,19 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
   __shared__ uint32_t tmem_base;
   __shared__ float pair[kThreads];
   __shared__ float row_norm[kTile];
-  const int n = blockIdx.x, h = blockIdx.y;
-  const int b = blockIdx.z / p.nsel, sel = p.sel0 + blockIdx.z % p.nsel;
+  const int h = blockIdx.y;
   const int row = my_row(), quad = my_quad();
   const int warp = threadIdx.x >> 5;
-  const int t0 = n * kTile;
-  const int rows = min(kTile, p.T - t0);
-  const bool decode = sel == 1 && p.y0 != nullptr && p.W2 != nullptr;
+  const int NT = (p.T + kTile - 1) / kTile;
+  const int ntiles = p.B * p.nsel * NT;
+  const bool any_decode = p.sel0 + p.nsel > 1 && p.y0 != nullptr && p.W2 != nullptr;
 
   const uint32_t base = smem_u32(smem);
   FeatTiles tl;
-  tl.x = Tile{base, kTile, p.dP};
-  tl.w1 = Tile{tl.x.saddr + kTile * p.dP * 2, p.PP, p.dP};
+  Tile xbuf[2];
+  xbuf[0] = Tile{base, kTile, p.dP};
+  xbuf[1] = Tile{xbuf[0].saddr + kTile * p.dP * 2, kTile, p.dP};
+  tl.w1 = Tile{xbuf[1].saddr + kTile * p.dP * 2, p.PP, p.dP};
   tl.phi = Tile{tl.w1.saddr + p.PP * p.dP * 2, kTile, p.mP};
   tl.w2 = Tile{tl.phi.saddr + kTile * p.mP * 2, p.dP, p.mP};
   float* stage = reinterpret_cast<float*>(smem + (tl.w2.saddr + p.dP * p.mP * 2 - base));
@@ -580,33 +600,61 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
-  const __nv_bfloat16* xp = p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(t0) * p.xs[sel][2];
-  load_tile(tl.x, xp, p.xs[sel][2], rows, p.d);
+  auto load_x = [&](int i, const Tile& dst) {
+    int b, sel, n;
+    feature_tile_coords(p, i, NT, b, sel, n);
+    const int t0 = n * kTile;
+    const __nv_bfloat16* xp =
+        p.x[sel] + b * p.xs[sel][0] + h * p.xs[sel][1] + static_cast<long long>(t0) * p.xs[sel][2];
+    load_tile(dst, xp, p.xs[sel][2], min(kTile, p.T - t0), p.d);
+  };
   load_tile(tl.w1, p.W1 + static_cast<size_t>(h) * p.P * p.d, p.d, p.P, p.d);
-  if (decode) load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
+  if (any_decode) load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
+  if (static_cast<int>(blockIdx.x) < ntiles) load_x(blockIdx.x, xbuf[0]);
   tiles_ready();
-  if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_a = ctx.tmem, t_y = ctx.tmem + 256;
-  project(p, ctx, tl, t_a);
-
   const uint32_t ta_row = tmem_addr(t_a, quad * 32, 0);
-  const RowState st = row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{});
-  // Rows past the sequence end get zero features, so the decode below and the
-  // stored tile are exact zeros there.
-  float* row32 = (sel == 1 && p.phi_q32 != nullptr && row < rows)
-                    ? p.phi_q32 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + row) * p.m : nullptr;
-  phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows, row32);
-  __syncthreads();
-  __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
-  store_tile(tl.phi, out, p.m, rows, p.m);
-  if (decode) {
-    ctx.run([&] { gemm_issue(t_y, kmajor(tl.phi), kmajor(tl.w2), p.dP, p.mP, false); });
-    float* y0 = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.d;
-    const Tile tx = tl.x;
-    store_rows(t_y, 0, p.dP, p.d, rows, y0, p.d, false, stage,
-               [&](int r, int col, float v) { return col < p.d ? v + tile_elem(tx, r, col) : v; });
+
+  int k = 0;
+  for (int i = blockIdx.x; i < ntiles; i += gridDim.x, ++k) {
+    int b, sel, n;
+    feature_tile_coords(p, i, NT, b, sel, n);
+    const int t0 = n * kTile;
+    const int rows = min(kTile, p.T - t0);
+    const bool decode = sel == 1 && any_decode;
+    tl.x = xbuf[k & 1];
+    // the next tile's rows stream in while this one computes
+    if (i + static_cast<int>(gridDim.x) < ntiles) load_x(i + gridDim.x, xbuf[(k + 1) & 1]);
+    cp_async_commit();
+    cp_async_wait_group<1>();
+    __syncthreads();
+    if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
+    ctx.run_keep_newest([&] { gemm_issue(t_a, kmajor(tl.x), kmajor(tl.w1), p.PP, p.dP, false); });
+
+    const RowState st = row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{});
+    // Rows past the sequence end get zero features, so the decode below and
+    // the stored tile are exact zeros there.
+    float* row32 = (sel == 1 && p.phi_q32 != nullptr && row < rows)
+                      ? p.phi_q32 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + row) * p.m : nullptr;
+    phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows, row32);
+    __syncthreads();
+    __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
+    store_tile(tl.phi, out, p.m, rows, p.m);
+    if (decode) {
+      ctx.run_keep_newest([&] { gemm_issue(t_y, kmajor(tl.phi), kmajor(tl.w2), p.dP, p.mP, false); });
+      float* y0 = p.y0 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.d;
+      const Tile tx = tl.x;
+      store_rows(t_y, 0, p.dP, p.d, rows, y0, p.d, false, stage,
+                 [&](int r, int col, float v) { return col < p.d ? v + tile_elem(tx, r, col) : v; });
+    }
+    // everything of this tile (x, phi, stage, TMEM) is consumed before the
+    // next iteration refills it
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
   }
+  cp_async_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_base, 512);
@@ -758,7 +806,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       for (int e = 0; e < 16; ++e)
         if ((e % kParts) == part) a_own[(c + e) / kParts] = a[e];
     }
-#pragma unroll
+#pragma unroll 1
     for (int i = 0; i < kMaxSplineOwn; ++i) {
       const int pj = kParts * i + part;
       if (pj >= p.P) break;
@@ -893,7 +941,19 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
 // ------------------------------------------------------------------ host launch
 
 size_t feature_fwd_smem(const FeatParams& p) {
-  return static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.mP + p.dP * p.mP) * 2 + kStageFloats * 4;
+  return static_cast<size_t>(2 * kTile * p.dP + p.PP * p.dP + kTile * p.mP + p.dP * p.mP) * 2 + kStageFloats * 4;
+}
+
+// CTAs per head of the persistent kernels: about one CTA per SM in all.
+static int persistent_ctas_per_head(const FeatParams& p, int ntiles) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  const int g = sms / p.H;
+  return max(1, min(ntiles, g));
 }
 size_t feature_bwd_smem(const FeatParams& p) {
   size_t bytes = static_cast<size_t>(kTile * p.dP + p.PP * p.dP + kTile * p.PM + kTile * p.mM + kTile * p.dP +
@@ -909,7 +969,8 @@ static int launch_feature_fwd_kind(const FeatParams& p, cudaStream_t s) {
   const size_t sm = feature_fwd_smem(p);
   cudaFuncSetAttribute(feature_fwd_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   const int NT = ceil_div(p.T, kTile);
-  feature_fwd_kernel<KIND><<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  const int G = persistent_ctas_per_head(p, p.B * p.nsel * NT);
+  feature_fwd_kernel<KIND><<<dim3(G, p.H), kThreads, sm, s>>>(p);
   return check_launch("feature_fwd_kernel");
 }
 
