@@ -79,6 +79,9 @@ CASES = [
     # payloads wider than a tile (the GN streams [g | 1] and [lambda | 1])
     (1, 2, 300, 128, 129, 1, True),
     (1, 1, 200, 64, 160, 1, False),
+    # long sequences: the two-level tile prefix (more than 32 tiles)
+    (1, 2, 4200, 64, 65, 2, True),
+    (1, 1, 8300, 32, 16, 1, True),
 ]
 # Streams with random-sign scores whose log-retention gradient is a large
 # cancellation at alpha -> 1 (case 4, head 0: terms of 670 sum to 160, and
@@ -122,7 +125,10 @@ def test_scan_backward_matches_oracle(lib, index, positive):
     q, k, v = _streams(B, H, T, Dk, Dv, seed=1, positive=positive)
     rets = _retentions(H, nd, with_sum)
     g = torch.Generator().manual_seed(7)
-    weights = [torch.randn(B, H, T, Dv, generator=g, dtype=torch.float64) for _ in rets]
+    # Both sides get the bf16 output gradient the C ABI takes: at T = 8300
+    # rounding float64 weights alone moves a log-retention gradient (a sum of
+    # ~3e7 pair terms of both signs) by 1.2%.
+    weights = [torch.randn(B, H, T, Dv, generator=g, dtype=torch.float64).bfloat16().double() for _ in rets]
 
     def run(qq, kk, vv, rr, fn):
         outs = fn(qq, kk, vv, rr)
@@ -210,21 +216,23 @@ def test_scan_errors_follow_the_reference_contract(lib):
         scan.linattn(q.cpu(), k.cpu(), v.cpu())
 
 
-def test_streamed_segments_equal_one_call(lib):
+@pytest.mark.parametrize("segments", [(100, 128, 300), (4500, 4300)])
+def test_streamed_segments_equal_one_call(lib, segments):
     """Scanning ragged segments one after another, each continuing from the
     previous segment's state, gives the single-call outputs; the returned
-    state is sum_t e^{la (T-1-t)} k_t^T [v_t | 1] (float64 reference)."""
+    state is sum_t e^{la (T-1-t)} k_t^T [v_t | 1] (float64 reference).  The
+    long segments run the two-level tile prefix with boundary states."""
     from thetascan_b200.scan import linattn_views, linattn_views_stream
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(21)
-    B, H, T, Dk, Dv = 2, 3, 528, 64, 32
+    B, H, T, Dk, Dv = 2, 3, sum(segments), 64, 32
     q = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
     k = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
     v = torch.randn(B, H, T, Dv, generator=g).to(torch.bfloat16).to(dev)
     la = [None] + [torch.log(0.9 + 0.09 * torch.rand(H, generator=g)).to(dev) for _ in range(2)]
     full = linattn_views(q, k, v, tuple(la), append_unit=True)
     state, pieces, t0 = None, [], 0
-    for seg in (100, 128, 300):
+    for seg in segments:
         sl = slice(t0, t0 + seg)
         outs, state = linattn_views_stream(q[:, :, sl], k[:, :, sl], v[:, :, sl], tuple(la), state, append_unit=True)
         pieces.append(outs)

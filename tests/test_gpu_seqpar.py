@@ -54,7 +54,8 @@ def _module(kind, dev):
     return module
 
 
-@pytest.mark.parametrize("kind,P,T", [("bspline", 4, 512), ("relu2", 2, 384)])
+# the last case runs the two-level tile prefix in every stage (4352-token shards)
+@pytest.mark.parametrize("kind,P,T", [("bspline", 4, 512), ("relu2", 2, 384), ("relu2", 2, 8704)])
 def test_sharded_mixer_matches_unsharded(dev, kind, P, T):
     from thetascan_b200.seqpar import SequentialShards
     module = _module(kind, dev)

@@ -43,6 +43,10 @@ static size_t states_bytes(const ScanParams& p) {
 static size_t images_bytes(const ScanParams& p) {
   return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * p.DvP * p.DkP * 2);
 }
+// Segment totals of the backward's two-level tile prefix (zero when unused).
+static size_t segs_bytes(const ScanParams& p) {
+  return align256(static_cast<size_t>(p.B) * p.H * p.R * p.NS * p.DkM * p.DvP * sizeof(float));
+}
 
 // Validate `a` and fill `p` (workspace pointers left null).
 static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
@@ -102,6 +106,7 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
   }
   p->out_bf16 = a->out_dtype == TS_DTYPE_BF16;
   if (a->stage < 0 || a->stage > 2) return set_error(TS_ERR_VALUE, "scan: stage must be 0, 1 or 2");
+  p->NS = prefix_segments(p->NT, p->any_stale != 0);
   if (p->any_stale && (a->init_state || a->final_state || a->stage != 0))
     return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: stale retentions take no boundary states or stages");
   p->init = a->init_state;
@@ -165,7 +170,7 @@ size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* args) {
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;
-  return 2 * states_bytes(p) + images_bytes(p);
+  return 2 * states_bytes(p) + images_bytes(p) + segs_bytes(p);
 }
 
 int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
@@ -195,7 +200,7 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   const size_t need = states_bytes(p) + images_bytes(p);
   if (!args->workspace || args->workspace_bytes < need)
     return set_error(TS_ERR_VALUE, "scan_bwd: the forward workspace (%zu bytes) is required", need);
-  const size_t need_bwd = 2 * states_bytes(p) + images_bytes(p);
+  const size_t need_bwd = 2 * states_bytes(p) + images_bytes(p) + segs_bytes(p);
   if (!grad->workspace || grad->workspace_bytes < need_bwd)
     return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need_bwd);
   if (grad->stage != 1 && (!grad->dq || !grad->dk || !grad->dv))
@@ -226,6 +231,7 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   g.gstates = static_cast<float*>(grad->workspace);
   g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));
   g.pstates = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p) + images_bytes(p));
+  g.gsegs = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + 2 * states_bytes(p) + images_bytes(p));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (grad->stage == 1) {
     // local tile terms and the gradient of the initial state from this shard's outputs

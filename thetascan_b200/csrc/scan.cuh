@@ -52,6 +52,9 @@ struct ScanParams {
   float* states;             // [B,H,NT,R,DkM,DvP] f32: dS, then S_in in place
   __nv_bfloat16* images;     // [B,H,NT,R] images of S_in (DvP rows x DkP cols)
   int any_stale;
+  // Two-level reverse tile prefix of the backward (long sequences): NS
+  // segments of kSegTiles tiles (NS = 0: one serial chain per state element).
+  int NS;
   // sequence-shard boundary states, f32 [B,H,R,Dk,Dv] (payload column fastest)
   const float* init;         // state entering token 0, or null (zero)
   float* final_state;        // state after the last token (written), or null
@@ -76,6 +79,7 @@ struct ScanGradParams {
   int all_tiles;             // local terms of every tile (the last one feeds the final state)
   int store;                 // the reverse prefix writes G, images and its log-retention terms
   int zero_start_final;      // dfinal is the gradient of the final state from a zero start
+  float* gsegs;              // [B,H,R,NS,DkM,DvP] f32: segment totals of the reverse prefix (NS > 0)
 };
 
 __device__ __forceinline__ float head_la(const ScanParams& p, int r, int h) {
@@ -159,6 +163,43 @@ __host__ __device__ inline dim3 prefix_grid(int DkM, int DvP, int R, int BH) {
   return dim3((DkM / 8 + 31) / 32, R * (DvP / 8), BH);
 }
 constexpr int kPrefixBatch = 8;   // tiles whose states are loaded together
+constexpr int kSegTiles = 16;     // tiles per segment of the two-level prefix
+
+// Segments of the backward's two-level prefix: used for sequences of more
+// than two segments without stale slots (whose paired lanes run the serial
+// chain).
+__host__ __device__ inline int prefix_segments(int NT, bool any_stale) {
+  return (!any_stale && NT > 2 * kSegTiles) ? (NT + kSegTiles - 1) / kSegTiles : 0;
+}
+
+// Lane of a two-level prefix kernel: as prefix_lane, with the segment in
+// blockIdx.z (z = bh * NS + s) and blocks of min(256, DkM) threads.
+struct SegLane {
+  PrefixLane l;
+  int s;
+};
+__device__ __forceinline__ SegLane seg_lane(const ScanParams& p) {
+  SegLane o;
+  const int cblocks = p.DvP / 8;
+  const int per_block = blockDim.x >> 3;    // feature groups per block
+  o.l.r = blockIdx.y / cblocks;
+  o.l.c = (blockIdx.y % cblocks) * 8 + (threadIdx.x & 7);
+  o.l.f8 = blockIdx.x * per_block + (threadIdx.x >> 3);
+  const int bh = blockIdx.z / p.NS;
+  o.s = blockIdx.z % p.NS;
+  o.l.b = bh / p.H;
+  o.l.h = bh % p.H;
+  o.l.active = o.l.f8 < p.DkM / 8;
+  return o;
+}
+__host__ __device__ inline int seg_threads(int DkM) { return DkM < 256 ? DkM : 256; }
+__host__ __device__ inline dim3 seg_grid(int DkM, int DvP, int R, int BH, int NS) {
+  const int per_block = seg_threads(DkM) / 8;
+  return dim3((DkM / 8 + per_block - 1) / per_block, R * (DvP / 8), BH * NS);
+}
+__device__ __forceinline__ size_t seg_index(const ScanParams& p, int b, int h, int r, int s) {
+  return (((static_cast<size_t>(b) * p.H + h) * p.R + r) * p.NS + s);
+}
 
 // The payload tile of a tile's rows: v, then the v_unit constant columns.
 __device__ __forceinline__ void load_payload(const ScanParams& p, const Tile& t, const __nv_bfloat16* src, int rows) {

@@ -447,6 +447,177 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
   if (want) add_block_dla(acc, g.dla[r], l.h);
 }
 
+// ------------------------------------------------------------------ two-level reverse prefix
+
+// Long sequences: the reverse chain over NT tiles streams three inputs per
+// tile (local terms, key-weight derivatives, forward states) and is latency
+// bound as one serial chain per state element, so the tiles are cut into NS
+// segments of kSegTiles.  Pass 1 gives each segment's zero-start total U_s
+// (the gradient its tiles' local terms leave at the state entering the
+// segment); pass 2 folds the later segments' totals into the gradient leaving
+// the segment's last tile,
+//   G(end of s) = C_{s+1} G(end of s+1) + U_{s+1}   (C_s = e^{la * tokens of s}),
+// then replays the segment's tiles as the one-level kernel does, with their
+// log-retention terms.  One more read of the local terms buys NS-fold shorter
+// dependency chains.
+
+__device__ __forceinline__ void bload8(const float* base, size_t elem, float* out) {
+  const float4* ptr = reinterpret_cast<const float4*>(base + elem);
+  const float4 a = ptr[0], b = ptr[1];
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+__global__ void __launch_bounds__(256) scan_bwd_prefix_seg_kernel(ScanParams p, ScanGradParams g) {
+  const SegLane sl = seg_lane(p);
+  const PrefixLane& l = sl.l;
+  if (!l.active) return;
+  const float la = head_la(p, l.r, l.h);
+  const bool decayed = p.la[l.r] != nullptr;
+  const float closing = decayed ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const float closing_last = decayed ? __expf(la * static_cast<float>(tile_len(p, p.NT - 1))) : 1.f;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  const int n0 = sl.s * kSegTiles, n1 = min(p.NT, n0 + kSegTiles);
+  const int first_local = g.all_tiles ? 0 : 1;
+  constexpr int kB = kPrefixBatch;
+  float U[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int nt = n1 - 1; nt >= n0; nt -= kB) {
+    float ld[kB][8];
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = nt - k;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ld[k][e] = 0.f;
+      if (n >= n0 && n >= first_local)
+        bload8(g.gstates + state_index(p, l.b, l.h, n, l.r) * p.DkM * p.DvP, elem, ld[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = nt - k;
+      if (n < n0) break;
+      const float cl = n + 1 < p.NT ? closing : closing_last;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) U[e] = U[e] * cl + ld[k][e];
+    }
+  }
+  float4* dst = reinterpret_cast<float4*>(g.gsegs + seg_index(p, l.b, l.h, l.r, sl.s) * p.DkM * p.DvP + elem);
+  dst[0] = make_float4(U[0], U[1], U[2], U[3]);
+  dst[1] = make_float4(U[4], U[5], U[6], U[7]);
+}
+
+__global__ void __launch_bounds__(256) scan_bwd_prefix_apply_kernel(ScanParams p, ScanGradParams g) {
+  const SegLane sl = seg_lane(p);
+  const PrefixLane& l = sl.l;
+  const int r = l.r;
+  const float la = head_la(p, r, l.h);
+  const bool decayed = p.la[r] != nullptr;
+  const int len_last = tile_len(p, p.NT - 1);
+  const float closing = decayed ? __expf(la * static_cast<float>(kTile)) : 1.f;
+  const float closing_last = decayed ? __expf(la * static_cast<float>(len_last)) : 1.f;
+  const bool want = decayed && g.dla[r] != nullptr && g.store;
+  // only segment 0 produces dinit when nothing is stored (block-uniform)
+  const bool work = g.store || sl.s == 0;
+  const bool in_image = l.active && l.f8 * 8 < p.DkP;
+  const size_t img_off = static_cast<size_t>(l.f8) * p.DvP * 16 + static_cast<size_t>(l.c) * 16;
+  const size_t elem = static_cast<size_t>(l.c) * p.DkM + l.f8 * 8;
+  const int n0 = sl.s * kSegTiles, n1 = min(p.NT, n0 + kSegTiles);
+  float G[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int f = l.f8 * 8 + e;
+    G[e] = (l.active && g.dfinal != nullptr && f < p.Dk && l.c < p.Dv)
+               ? __ldg(g.dfinal + boundary_index(p, l.b, l.h, l.r, f, l.c)) : 0.f;
+  }
+  float acc = 0.f;
+  if (want && sl.s == p.NS - 1 && l.active && g.zero_start_final && g.dfinal != nullptr && p.init != nullptr) {
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = l.f8 * 8 + e;
+      if (f < p.Dk && l.c < p.Dv) dot += G[e] * __ldg(p.init + boundary_index(p, l.b, l.h, l.r, f, l.c));
+    }
+    acc -= static_cast<float>(p.T) * __expf(la * static_cast<float>(p.T)) * dot;
+  }
+  // fold the later segments: the last one may be short, the others are full
+  const float seg_closing = decayed ? __expf(la * static_cast<float>(kSegTiles * kTile)) : 1.f;
+  const int last_tokens = p.T - (p.NS - 1) * kSegTiles * kTile;
+  const float last_seg_closing = decayed ? __expf(la * static_cast<float>(last_tokens)) : 1.f;
+  for (int s1 = p.NS - 1; s1 > sl.s && l.active && work; s1 -= kPrefixBatch) {
+    float u[kPrefixBatch][8];
+#pragma unroll
+    for (int k = 0; k < kPrefixBatch; ++k)
+      if (s1 - k > sl.s) bload8(g.gsegs + seg_index(p, l.b, l.h, l.r, s1 - k) * p.DkM * p.DvP, elem, u[k]);
+#pragma unroll
+    for (int k = 0; k < kPrefixBatch; ++k) {
+      const int ss = s1 - k;
+      if (ss <= sl.s) break;
+      const float cs = ss == p.NS - 1 ? last_seg_closing : seg_closing;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) G[e] = G[e] * cs + u[k][e];
+    }
+  }
+  const int last_dla = g.dfinal != nullptr ? p.NT : p.NT - 1;
+  const int first_local = g.all_tiles ? 0 : 1;
+  constexpr int kB = kPrefixBatch / 2;
+  for (int n0b = n1 - 1; n0b >= n0 && l.active && work; n0b -= kB) {
+    float4 ld[kB][2], pw[kB][2];
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0b - k;
+      ld[k][0] = ld[k][1] = pw[k][0] = pw[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n < n0) continue;
+      const size_t base = state_index(p, l.b, l.h, n, r) * p.DkM * p.DvP + elem;
+      if (n >= first_local) {
+        const float4* gp = reinterpret_cast<const float4*>(g.gstates + base);
+        ld[k][0] = gp[0];
+        ld[k][1] = gp[1];
+      }
+      if (want && n < last_dla) {
+        const float kc = n + 1 < p.NT ? static_cast<float>(kTile) * closing
+                                      : static_cast<float>(len_last) * closing_last;
+        const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
+        const float4* sp = reinterpret_cast<const float4*>(p.states + base);
+        const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1v = sp[1];
+        pw[k][0] = make_float4(p0.x + kc * s0.x, p0.y + kc * s0.y, p0.z + kc * s0.z, p0.w + kc * s0.w);
+        pw[k][1] = make_float4(p1.x + kc * s1v.x, p1.y + kc * s1v.y, p1.z + kc * s1v.z, p1.w + kc * s1v.w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int n = n0b - k;
+      if (n < n0) break;
+      const size_t si = state_index(p, l.b, l.h, n, r);
+      if (g.store) {
+        float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
+        gp[0] = make_float4(G[0], G[1], G[2], G[3]);
+        gp[1] = make_float4(G[4], G[5], G[6], G[7]);
+        if (in_image) {
+          uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
+          *reinterpret_cast<uint4*>(img) = pack8(G);
+        }
+      }
+      const float cl = n + 1 < p.NT ? closing : closing_last;
+      const float pv[8] = {pw[k][0].x, pw[k][0].y, pw[k][0].z, pw[k][0].w,
+                           pw[k][1].x, pw[k][1].y, pw[k][1].z, pw[k][1].w};
+      const float lv[8] = {ld[k][0].x, ld[k][0].y, ld[k][0].z, ld[k][0].w,
+                           ld[k][1].x, ld[k][1].y, ld[k][1].z, ld[k][1].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc += G[e] * pv[e];
+        G[e] = G[e] * cl + lv[e];
+      }
+    }
+  }
+  if (sl.s == 0 && g.dinit != nullptr && l.active && l.c < p.Dv) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = l.f8 * 8 + e;
+      if (f < p.Dk) g.dinit[boundary_index(p, l.b, l.h, l.r, f, l.c)] = G[e];
+    }
+  }
+  if (want) add_block_dla(acc, g.dla[r], l.h);
+}
+
 // ------------------------------------------------------------------ dq, dk
 
 // One kernel for both (kDq selects):
@@ -725,8 +896,16 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
     scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
     if (int e = check_launch("scan_bwd_state_kernel")) return e;
   }
-  scan_bwd_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p, g);
-  if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
+  if (p.NS > 0) {
+    const dim3 grid = seg_grid(p.DkM, p.DvP, p.R, p.B * p.H, p.NS);
+    scan_bwd_prefix_seg_kernel<<<grid, seg_threads(p.DkM), 0, s>>>(p, g);
+    if (int e = check_launch("scan_bwd_prefix_seg_kernel")) return e;
+    scan_bwd_prefix_apply_kernel<<<grid, seg_threads(p.DkM), 0, s>>>(p, g);
+    if (int e = check_launch("scan_bwd_prefix_apply_kernel")) return e;
+  } else {
+    scan_bwd_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p, g);
+    if (int e = check_launch("scan_bwd_prefix_kernel")) return e;
+  }
   if (!grads) return 0;
   const dim3 grid(p.NT, p.H, p.B);
   scan_bwd_dqk_kernel<true><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);

@@ -343,6 +343,10 @@ int launch_scan_fwd(const ScanParams& p, cudaStream_t s, bool tile_states, bool 
     scan_state_kernel<<<dim3(state_tiles, p.H, p.B), kThreads, sm1, s>>>(p);
     if (int e = check_launch("scan_state_kernel")) return e;
   }
+  // One serial chain per state element: the forward chain streams one input
+  // and two outputs per tile at about half of HBM bandwidth already (a
+  // two-level version, measured, was slower for its second read of the tile
+  // states); the backward's three inputs per tile take the two-level form.
   scan_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p);
   if (int e = check_launch("scan_prefix_kernel")) return e;
   if (!outputs) return 0;
