@@ -273,6 +273,10 @@ typedef struct ts_feature_grad_args {
    * token-major gradient of the read output, whose y0 part is the identity. */
   const void* dy0_bf16;
   int64_t dy0_strides[3];
+  /* 1: dw2 is f32 [H,m,d] (the transpose of W2's layout), accumulated with
+   * vector atomics; 0: [H,d,m].  When ts_feature_args.phi_q is given to the
+   * backward it is read as the forward's phi(q) for dw2 (else rebuilt). */
+  int dw2_transposed;
 } ts_feature_grad_args;
 
 int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream);

@@ -97,6 +97,7 @@ class FeatureGradArgs(ctypes.Structure):
         ("dk_bf16", ctypes.c_void_p), ("dq_bf16", ctypes.c_void_p),
         ("dk_strides", c_int64_3), ("dq_strides", c_int64_3),
         ("dy0_bf16", ctypes.c_void_p), ("dy0_strides", c_int64_3),
+        ("dw2_transposed", ctypes.c_int),
     ]
 
 

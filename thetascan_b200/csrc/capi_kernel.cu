@@ -189,6 +189,7 @@ int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args*
     p.dxs[1][i] = grad->dq_strides[i];
   }
   p.dW1 = grad->dw1;
+  p.dW2_t = grad->dw2_transposed ? 1 : 0;
   p.dW2 = grad->dw2;
   p.dbias = grad->dscore_bias;
   p.dthr = grad->dthreshold;

@@ -45,6 +45,7 @@ struct FeatParams {
   // forward outputs
   __nv_bfloat16* phi[2];    // [B, H, T, m]
   float* phi_q32;           // [B, H, T, m] f32 copy of phi_q, or null
+  int dW2_t;                // backward: dW2 accumulated as [H, m, d] (vector atomics)
   float* y0;                // [B, H, T, d] or null (q only)
   // backward
   const void* dphi[2];      // [B, H, T, m], f32 or bf16
@@ -706,6 +707,10 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       ? static_cast<const void*>(static_cast<const __nv_bfloat16*>(p.dphi[sel]) + rowbase * p.m)
       : static_cast<const void*>(static_cast<const float*>(p.dphi[sel]) + rowbase * p.m);
   load_tile_any(tdphi, dphi_src, p.m, rows, p.m, p.dphi_bf16 != 0);
+  // The decode gradient dW2 += phi(q)^T dy reads the forward's phi(q) when it
+  // is given (instead of rebuilding it in the second sweep).
+  const bool phi_stored = decode && p.phi[1] != nullptr;
+  if (phi_stored) load_tile(tl.phi, p.phi[1] + rowbase * p.m, p.m, rows, p.m);
   if (decode) {
     load_tile(tl.w2, p.W2 + static_cast<size_t>(h) * p.d * p.m, p.m, p.d, p.m);
     if (p.dyb != nullptr) {
@@ -829,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
     dot_a = row_pair_sum(dot_a, pair);
     if (!valid) dot_a = dscale = 0.f;
-    if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    if (decode && !phi_stored) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
 #pragma unroll
     for (int i = 0; i < kMaxSplineOwn; ++i) {
@@ -867,8 +872,8 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       dot_a = 0.f;
       dthr = dscale = dgain_head = 0.f;
     }
-    // Sweep 2: phi -> tile (for dW2) and dA = inv * dpre - a * inv^3 * dot_a / P.
-    if (decode) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    // Sweep 2: (phi -> tile for dW2 unless stored) and dA = inv * dpre - a * inv^3 * dot_a / P.
+    if (decode && !phi_stored) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], dp[16], da[16];
@@ -927,8 +932,18 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
         float v[16];
         tmem_ld16(tmem_addr(t_a + (pblocks + mb) * p.dP, quad * 32, c), v);
         if (fi < p.m && p.dW2) {
-          for (int e = 0; e < 16 && c + e < p.d; ++e)
-            atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.d + c + e) * p.m + fi, v[e]);
+          if (p.dW2_t && (p.d & 3) == 0) {
+            // [H, m, d]: this row's d values are contiguous
+            float* wrow = p.dW2 + (static_cast<size_t>(h) * p.m + fi) * p.d;
+            for (int e = 0; e < 16 && c + e < p.d; e += 4)
+              atomicAdd(reinterpret_cast<float4*>(wrow + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+          } else if (p.dW2_t) {
+            for (int e = 0; e < 16 && c + e < p.d; ++e)
+              atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.m + fi) * p.d + c + e, v[e]);
+          } else {
+            for (int e = 0; e < 16 && c + e < p.d; ++e)
+              atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.d + c + e) * p.m + fi, v[e]);
+          }
         }
       }
     }

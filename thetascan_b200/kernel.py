@@ -240,13 +240,14 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
         fg.dk_strides = _lib.c_int64_3(*dk_out.stride()[:3])
         fg.dq_strides = _lib.c_int64_3(*dq_out.stride()[:3])
     dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
-    dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+    dW2t = torch.zeros(W2b.shape[0], W2b.shape[2], W2b.shape[1], dtype=torch.float32, device=dev)
     grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
              for key in ("thr", "bias", "gain", "scale")}
-    fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+    fg.dw1, fg.dw2, fg.dw2_transposed = dW1.data_ptr(), dW2t.data_ptr(), 1
     fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
     fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
     _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+    dW2 = dW2t.transpose(1, 2)
     dla = None if n == 1 else torch.stack(dlas[1:])
     return dict(dq=dq, dk=dk, dvaug=dvaug, dW1=dW1, dW2=dW2, dla=dla, deta=deta, **grads)
 
@@ -411,13 +412,14 @@ class _ShardStageA(torch.autograd.Function):
         fg.dk_strides = _lib.c_int64_3(*dk.stride()[:3])
         fg.dq_strides = _lib.c_int64_3(*dq.stride()[:3])
         dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
-        dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+        dW2t = torch.zeros(W2b.shape[0], W2b.shape[2], W2b.shape[1], dtype=torch.float32, device=dev)
         grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
                  for key in ("thr", "bias", "gain", "scale")}
-        fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+        fg.dw1, fg.dw2, fg.dw2_transposed = dW1.data_ptr(), dW2t.data_ptr(), 1
         fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
         fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
         _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+        dW2 = dW2t.transpose(1, 2)
         w1d, w2d = ctx.dtypes
         dla = None if len(hold.las) == 1 else torch.stack(hold.dlas[1:])
         return (None, None, None, None, dqkv, dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"],
@@ -654,13 +656,14 @@ class _KernelCoreViews(torch.autograd.Function):
         dq = torch.empty_like(dk)
         fg.dk, fg.dq = dk.data_ptr(), dq.data_ptr()
         dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
-        dW2 = torch.zeros(W2b.shape, dtype=torch.float32, device=dev)
+        dW2t = torch.zeros(W2b.shape[0], W2b.shape[2], W2b.shape[1], dtype=torch.float32, device=dev)
         grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
                  for key in ("thr", "bias", "gain", "scale")}
-        fg.dw1, fg.dw2 = dW1.data_ptr(), dW2.data_ptr()
+        fg.dw1, fg.dw2, fg.dw2_transposed = dW1.data_ptr(), dW2t.data_ptr(), 1
         fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
         fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
         _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
+        dW2 = dW2t.transpose(1, 2)
         qd, kd, vd, w1d, w2d = ctx.dtypes
         dla = None if n == 1 else torch.stack(dlas[1:])
         return (None, dq.to(qd), dk.to(kd), dv.to(vd), dW1.to(w1d), dW2.to(w2d), grads["thr"], grads["bias"],
