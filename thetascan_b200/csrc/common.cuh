@@ -398,7 +398,9 @@ __device__ __forceinline__ void store_tile(const Tile& t, __nv_bfloat16* __restr
 // XOR-swizzled so that both the row-wise writes and the column-wise reads are
 // free of bank conflicts, and leave as whole 32-byte sectors.
 // `transform(row, col, value)` may adjust each value; `addend` (same layout as
-// dst, f32) is added on the way out.
+// dst, f32) is added on the way out.  With tcol_b >= 0 the value is
+// A + scale_b * B, B the accumulator at TMEM column tcol_b and scale_b this
+// thread's row factor.
 constexpr int kStageFloats = kTile * kChunkStep;
 
 __device__ __forceinline__ int stage_idx(int r, int c) { return r * kChunkStep + (c ^ (r & 31)); }
@@ -406,14 +408,23 @@ __device__ __forceinline__ int stage_idx(int r, int c) { return r * kChunkStep +
 template <class Transform>
 __device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, int width, int rows_valid, void* dst,
                                            long ld, bool bf16, float* stage, Transform transform,
-                                           const float* __restrict__ addend = nullptr) {
+                                           const float* __restrict__ addend = nullptr, int tcol_b = -1,
+                                           float scale_b = 0.f) {
   const int row = my_row(), part = my_part();
   const uint32_t trow = tmem_addr(tbase, my_quad() * 32, tcol);
+  const uint32_t trow_b = tmem_addr(tbase, my_quad() * 32, tcol_b < 0 ? 0 : tcol_b);
   for (int c = 0; c < ncols; c += kChunkStep) {
     const int cc = c + 16 * part;
     if (cc < ncols) {
       float v[16];
       tmem_ld16(trow + cc, v);
+      if (tcol_b >= 0) {
+        // a second accumulator of the same shape, scaled per row (this thread's)
+        float w[16];
+        tmem_ld16(trow_b + cc, w);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = fmaf(scale_b, w[e], v[e]);
+      }
 #pragma unroll
       for (int e = 0; e < 16; ++e) stage[stage_idx(row, 16 * part + e)] = transform(row, cc + e, v[e]);
     }

@@ -245,7 +245,16 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   __shared__ float decay[4 * kTile];
   fill_decay(p, h, decay);
 
-  const int cols_needed = kTile + p.RU * p.DvP;
+  // Fold mode (payloads up to a tile wide): q is loaded once and stays
+  // unscaled.  A slot's read is P_r v + q S_r with carry 1 (plain sum, the
+  // stale slot's own state) straight into its accumulator, and the decayed
+  // cross term c_r(i) (q S_r) -- or the stale slot's (1 - c(i)) (q S_a) -- in
+  // a second accumulator scaled per row on the way out.  Each slot is stored
+  // right after its products (the P tile doubles as the store stage), and the
+  // next slot's state image streams into the key tile's region, free after
+  // the score, meanwhile.
+  const bool fold = p.DvP <= kTile && kTile + 2 * p.DvP <= 512;
+  const int cols_needed = fold ? kTile + 2 * p.DvP : kTile + p.RU * p.DvP;
   const uint32_t ncols = cols_needed <= 256 ? 256 : 512;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
@@ -256,14 +265,73 @@ __global__ void __launch_bounds__(kThreads) scan_out_kernel(ScanParams p) {
   const __nv_bfloat16* qp = p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2];
   const __nv_bfloat16* kp = p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2];
   const __nv_bfloat16* vp = p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2];
+  const bool cross_any = n > 0 || p.init != nullptr;
+  auto image_at = [&](int slot) {
+    return reinterpret_cast<const uint8_t*>(p.images) +
+           state_index(p, b, h, n, slot) * static_cast<size_t>(image_bytes(p));
+  };
   load_tile(tq, qp, p.qs[2], rows, p.Dk);
   load_tile(tk, kp, p.ks[2], rows, p.Dk);
   load_payload(p, tv, vp, rows);
+  if (fold && cross_any) load_image(ts, image_at(0), image_bytes(p));
 
   tiles_ready();
   MmaCtx ctx{&bar, tmem_base, 0u, true};
   const uint32_t t_score = ctx.tmem;
   ctx.run([&] { gemm_issue(t_score, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
+
+  if (fold) {
+    const Tile img[2] = {ts, Tile{tk.saddr, p.DvP, p.DkP}};
+    const uint32_t c_out = kTile, c_x = kTile + p.DvP;
+    float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
+    const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
+    for (int r = 0; r < p.RU; ++r) {
+      const float la = head_la(p, r, h);
+      const bool decayed = p.la[r] != nullptr;
+      const bool stale = p.kind[r] == kSlotStale;
+      // image r+1 into the buffer slot r-1 read (its products are done)
+      if (cross_any && r + 1 < p.RU) load_image(img[(r + 1) & 1], image_at(r + 1), image_bytes(p));
+      cp_async_commit();
+      for (int c = 16 * part; c < kTile; c += kChunkStep) {
+        float sc[16], f[16];
+        tmem_ld16(tmem_addr(t_score, quad * 32, c), sc);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int j = c + e;
+          f[e] = (j <= row) ? decay[r * kTile + row - j] * sc[e] : 0.f;
+        }
+        tile_st16(tp, row, c / 8, pack8(f));
+        tile_st16(tp, row, c / 8 + 1, pack8(f + 8));
+      }
+      const Tile& im = img[r & 1];
+      // the carry-1 state (plain sum, stale) accumulates into the read itself
+      const bool direct = cross_any && (!decayed || stale);
+      const bool scaled = cross_any && decayed && !stale;
+      ctx.run_keep_newest([&] {
+        gemm_issue(ctx.tmem + c_out, kmajor(tp), mnmajor(tv), p.DvP, kTile, false);
+        if (direct) gemm_issue(ctx.tmem + c_out, kmajor(tq), kmajor(im), p.DvP, p.DkP, true);
+        if (scaled) gemm_issue(ctx.tmem + c_x, kmajor(tq), kmajor(im), p.DvP, p.DkP, false);
+      });
+      bool second = scaled;
+      if (cross_any && stale) {
+        // + (1 - c(i)) q S_a: the auxiliary image into the buffer just read
+        load_image(im, image_at(p.partner[r]), image_bytes(p));
+        ctx.run([&] { gemm_issue(ctx.tmem + c_x, kmajor(tq), kmajor(im), p.DvP, p.DkP, false); });
+        second = true;
+      }
+      const float x = la * static_cast<float>(row + 1);
+      const float row_scale = stale ? one_minus_exp(x) : __expf(x);
+      void* dst = p.out_bf16 ? static_cast<void*>(reinterpret_cast<__nv_bfloat16*>(p.out[r]) + row0)
+                             : static_cast<void*>(reinterpret_cast<float*>(p.out[r]) + row0);
+      store_rows(ctx.tmem, c_out, p.DvP, p.Dv, rows, dst, p.Dv, p.out_bf16 != 0, stage, Identity{}, nullptr,
+                 second ? static_cast<int>(c_x) : -1, row_scale);
+    }
+    cp_async_wait_all();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem_base, ncols);
+    return;
+  }
 
   for (int r = 0; r < p.RU; ++r) {
     const float la = head_la(p, r, h);
