@@ -767,7 +767,14 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   Tile tp{tk.saddr + kTile * p.DkP * 2, kTile, kTile};
   Tile td{tp.saddr + kTile * kTile * 2, kTile, p.DvP};
   Tile tv{td.saddr + kTile * p.DvP * 2, kTile, p.DvP};
-  const uint32_t ncols = tmem_cols_for(2 * kTile + p.DvP);
+  // Fold mode (payloads up to a tile wide): k stays in its tile, unscaled;
+  // G images go to the q region (free after the score), and the key-weighted
+  // cross term u_r(j) (k G_r)_j of every slot is formed in its own
+  // accumulator and summed per row in registers, so k is not reloaded and
+  // rescaled per slot.
+  const bool fold = p.DvP <= kTile;
+  const Tile tgf{tq.saddr, p.DvP, p.DkP};
+  const uint32_t ncols = tmem_cols_for(2 * kTile + (fold ? 2 : 1) * p.DvP);
   __shared__ float decay[4 * kTile];
   fill_decay(p, h, decay);
   if (threadIdx.x == 0) {
@@ -787,6 +794,12 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
   ctx.run([&] { gemm_issue(t_s, kmajor(tq), kmajor(tk), kTile, p.DkP, false); });
 
   const bool cross = n + 1 < p.NT || g.dfinal != nullptr;
+  const uint32_t t_x = t_dv + p.DvP;          // fold: this slot's k G_r
+  float xacc[2][16];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) xacc[k][e] = 0.f;
   for (int r = 0; r < p.R; ++r) {
     const float la = head_la(p, r, h);
     const bool decayed = p.la[r] != nullptr;
@@ -808,18 +821,35 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
       load_tile(td, dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
     }
     if (cross) {
-      load_scaled_rows(tq, kp, p.ks[2], rows, p.Dk, -1, [&](int t) {
-        return slot_key_weight(p, r, la, rows, t);
-      });
       const size_t si = state_index(p, b, h, n, r);
-      load_image(tg, reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)),
-                 image_bytes(p));
+      const uint8_t* gimg = reinterpret_cast<const uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p));
+      if (fold) {
+        load_image(tgf, gimg, image_bytes(p));
+      } else {
+        load_scaled_rows(tq, kp, p.ks[2], rows, p.Dk, -1, [&](int t) {
+          return slot_key_weight(p, r, la, rows, t);
+        });
+        load_image(tg, gimg, image_bytes(p));
+      }
     }
     ctx.run([&] {
       if (caller) gemm_issue(t_dv, mnmajor(tp), mnmajor(td), p.DvP, kTile, r > 0);
-      if (cross) gemm_issue(t_dv, kmajor(tq), kmajor(tg), p.DvP, p.DkP, true);
+      if (cross && fold) gemm_issue(t_x, kmajor(tk), kmajor(tgf), p.DvP, p.DkP, false);
+      if (cross && !fold) gemm_issue(t_dv, kmajor(tq), kmajor(tg), p.DvP, p.DkP, true);
       if (want) gemm_issue(t_g, kmajor(td), kmajor(tv), kTile, p.DvP, false);
     });
+    if (cross && fold) {
+      const float u = slot_key_weight(p, r, la, rows, row);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = 16 * part + kChunkStep * k;
+        if (c >= p.DvP) break;
+        float v[16];
+        tmem_ld16(tmem_addr(t_x, quad * 32, c), v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xacc[k][e] = fmaf(u, v[e], xacc[k][e]);
+      }
+    }
     if (want) {
       // d w / d la at distance k: k e^{la k}, or -k e^{la k} = -k (1 - w) for a stale slot
       const bool stale = p.kind[r] == kSlotStale;
@@ -843,15 +873,28 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     }
   }
 
+  // fold: the summed cross terms back into TMEM beside dv, added on the way out
+  const int xcol = (fold && cross) ? p.DvP : -1;
+  if (fold && cross) {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int c = 16 * part + kChunkStep * k;
+      if (c >= p.DvP) break;
+      tmem_st16(tmem_addr(t_x, quad * 32, c), xacc[k]);
+    }
+  }
   float* stage = reinterpret_cast<float*>(smem + (tp.saddr - base));
   if (g.dv_strided) {
     const long long off = b * g.dvs[0] + h * g.dvs[1] + static_cast<long long>(t0) * g.dvs[2];
     store_rows(t_dv, 0, p.DvP, p.Dv - p.v_unit, rows, grad_ptr(g.dv, g.grad_bf16, off), g.dvs[2],
-               g.grad_bf16 != 0, stage, Identity{});
+               g.grad_bf16 != 0, stage, Identity{}, nullptr, xcol, 1.f);
   } else {
     const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dv;
     store_rows(t_dv, 0, p.DvP, p.Dv, rows, grad_ptr(g.dv, g.grad_bf16, row0), p.Dv,
-               g.grad_bf16 != 0, stage, Identity{});
+               g.grad_bf16 != 0, stage, Identity{}, nullptr, xcol, 1.f);
   }
   tc_fence_before();
   __syncthreads();
