@@ -193,11 +193,30 @@ class PhaseTimer:
     KERNELS = {"ts_b200_feature_fwd": 1, "ts_b200_scan_fwd": 3, "ts_b200_kread_fwd": 1,
                "ts_b200_kread_bwd": 1, "ts_b200_scan_bwd": 5, "ts_b200_feature_bwd": 1}
 
+    @staticmethod
+    def scan_kernels(name, args):
+        """Kernels one scan call launches (the launch logic of the C ABI:
+        csrc/scan_fwd.cu launch_scan_fwd, csrc/scan_bwd.cu launch_scan_bwd)."""
+        a = args[0]._obj
+        nt = -(-a.tokens // 128)
+        stale = any(a.stale[i] for i in range(a.n_retentions))
+        if name == "ts_b200_scan_fwd":
+            stage = a.stage
+            state = 1 if (stage != 2 and (nt > 1 or a.final_state or stage == 1)) else 0
+            return state + 1 + (0 if stage == 1 else 1)
+        g = args[1]._obj
+        two_level = (not stale) and nt >= 32
+        all_tiles = bool(g.dfinal_state or g.dinit_state or a.init_state or g.stage != 0)
+        state = 1 if (g.stage != 2 and (nt > 1 or all_tiles)) else 0
+        prefix = 2 if two_level else 1
+        return state + prefix + (0 if g.stage == 1 else 3)
+
     def __init__(self, lib):
         self.lib = lib
         self.saved = {}
         self.events = {name: [] for name in self.KERNELS}
         self.calls = {name: 0 for name in self.KERNELS}
+        self.scan_launches = 0
         self.timing = False
 
     def install(self):
@@ -207,6 +226,8 @@ class PhaseTimer:
 
             def wrapper(*a, _fn=fn, _name=name):
                 self.calls[_name] += 1
+                if _name in ("ts_b200_scan_fwd", "ts_b200_scan_bwd"):
+                    self.scan_launches += self.scan_kernels(_name, a)
                 if not self.timing:
                     return _fn(*a)
                 start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -222,7 +243,8 @@ class PhaseTimer:
             setattr(self.lib, name, fn)
 
     def launches(self):
-        return sum(self.calls[n] * k for n, k in self.KERNELS.items())
+        return self.scan_launches + sum(self.calls[n] * k for n, k in self.KERNELS.items()
+                                        if n not in ("ts_b200_scan_fwd", "ts_b200_scan_bwd"))
 
     def total_ms(self):
         """Device time of each entry point summed over the timed calls (a
@@ -269,7 +291,9 @@ def bytes_per_token(cfg):
 # timed config by its number of token rows (traffic grows with B * T).
 MEASURED_TRAFFIC = {
     # entry point: (bytes per launch at the profiled size, tokens of that launch, source)
-    "ts_b200_feature_bwd": (189.9e6 + 27.0e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_feature_bwd": (258.8e6 + 34.4e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_scan_bwd": (1254.9e6 + 521.1e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_scan_fwd": (476.3e6 + 351.2e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
 }
 
 
@@ -390,6 +414,7 @@ def run_b200(args, cfg):
     if world > 1:
         dist.barrier()
     timer.calls = {n: 0 for n in timer.calls}
+    timer.scan_launches = 0
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(local) as clocks:

@@ -79,7 +79,8 @@ CASES = [
     # payloads wider than a tile (the GN streams [g | 1] and [lambda | 1])
     (1, 2, 300, 128, 129, 1, True),
     (1, 1, 200, 64, 160, 1, False),
-    # long sequences: the two-level tile prefix (more than 32 tiles)
+    # long sequences: the two-level tile prefix (32 tiles and more)
+    (1, 2, 4096, 128, 66, 1, True),
     (1, 2, 4200, 64, 65, 2, True),
     (1, 1, 8300, 32, 16, 1, True),
 ]

@@ -165,11 +165,11 @@ __host__ __device__ inline dim3 prefix_grid(int DkM, int DvP, int R, int BH) {
 constexpr int kPrefixBatch = 8;   // tiles whose states are loaded together
 constexpr int kSegTiles = 16;     // tiles per segment of the two-level prefix
 
-// Segments of the backward's two-level prefix: used for sequences of more
-// than two segments without stale slots (whose paired lanes run the serial
+// Segments of the backward's two-level prefix: used for sequences of two or
+// more segments without stale slots (whose paired lanes run the serial
 // chain).
 __host__ __device__ inline int prefix_segments(int NT, bool any_stale) {
-  return (!any_stale && NT > 2 * kSegTiles) ? (NT + kSegTiles - 1) / kSegTiles : 0;
+  return (!any_stale && NT >= 2 * kSegTiles) ? (NT + kSegTiles - 1) / kSegTiles : 0;
 }
 
 // Lane of a two-level prefix kernel: as prefix_lane, with the segment in
