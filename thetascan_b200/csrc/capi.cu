@@ -230,7 +230,7 @@ int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts
   g.all_tiles = (g.dfinal != nullptr || g.dinit != nullptr || p.init != nullptr || grad->stage != 0) ? 1 : 0;
   g.gstates = static_cast<float*>(grad->workspace);
   g.gimages = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p));
-  g.pstates = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p) + images_bytes(p));
+  g.pstates = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(grad->workspace) + states_bytes(p) + images_bytes(p));
   g.gsegs = reinterpret_cast<float*>(static_cast<uint8_t*>(grad->workspace) + 2 * states_bytes(p) + images_bytes(p));
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (grad->stage == 1) {

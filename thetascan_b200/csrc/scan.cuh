@@ -71,8 +71,9 @@ struct ScanGradParams {
   int dv_strided;
   int grad_bf16;
   float* dla[kMaxSlots];     // an auxiliary slot shares its stale slot's
-  float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS, then G in place
-  float* pstates;            // [B,H,NT,R,DkM,DvP] f32: key-weight derivative of each tile's state
+  float* gstates;            // [B,H,NT,R,DkM,DvP] f32: local dS of every tile
+  __nv_bfloat16* pstates;    // [B,H,NT,R,DkM,DvP] bf16: key-weight derivative of each tile's state
+                             // (only ever dotted into the log-retention gradient)
   __nv_bfloat16* gimages;    // [B,H,NT,R] images of G (DvP rows x DkP cols)
   const float* dfinal;       // gradient of the final state (G of the last tile), or null
   float* dinit;              // gradient of the initial state (written), or null

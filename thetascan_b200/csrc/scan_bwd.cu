@@ -18,7 +18,7 @@
 // with g = dout . v^T.  Every term is a natural sum of positive-weight
 // contractions (no two large terms cancel), evaluated in f32.  Kernels:
 //   scan_bwd_state_kernel  local dS per tile                     (tcgen05)
-//   scan_bwd_prefix_kernel reverse scan -> G per tile (f32 + bf16 image)
+//   scan_bwd_prefix_kernel reverse scan -> G per tile (bf16 image; f32 along the chain)
 //   scan_bwd_dqk_kernel    ds (summed over retentions), then dq or dk (tcgen05)
 //   scan_bwd_dv_kernel     P_r, dv, f-term                       (tcgen05)
 // A stale slot X and its auxiliary slot a (scan.cuh) enter the same sums with
@@ -204,14 +204,14 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
           for (int mb = 0; mb < mblocks; ++mb)
             gemm_issue(t_x + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
         });
-        float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+        __nv_bfloat16* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
         for (int mb = 0; mb < mblocks; ++mb) {
-          float* col = dst + mb * kTile + row;
+          __nv_bfloat16* col = dst + mb * kTile + row;
           for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
             float v[16];
             tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = v[e];
+            for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = __float2bfloat16_rn(v[e]);
           }
         }
       }
@@ -230,14 +230,14 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
         for (int mb = 0; mb < mblocks; ++mb)
           gemm_issue(t_x + mb * p.DvP, mnmajor(tk, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
       });
-      float* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+      __nv_bfloat16* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
       for (int mb = 0; mb < mblocks; ++mb) {
-        float* col = dst + mb * kTile + row;
+        __nv_bfloat16* col = dst + mb * kTile + row;
         for (int c = 16 * part; c < p.DvP; c += kChunkStep) {
           float v[16];
           tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c), v);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = v[e];
+          for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c + e) * p.DkM] = __float2bfloat16_rn(v[e]);
         }
       }
     }
@@ -294,9 +294,6 @@ __device__ __forceinline__ void stale_reverse_prefix(const ScanParams& p, const 
   float acc = 0.f;
   auto store8 = [&](int slot, int n, const float* G) {
     const size_t si = state_index(p, l.b, l.h, n, slot);
-    float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
-    gp[0] = make_float4(G[0], G[1], G[2], G[3]);
-    gp[1] = make_float4(G[4], G[5], G[6], G[7]);
     if (in_image) {
       uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
       *reinterpret_cast<uint4*>(img) = pack8(G);
@@ -308,16 +305,19 @@ __device__ __forceinline__ void stale_reverse_prefix(const ScanParams& p, const 
     out[0] = x0.x; out[1] = x0.y; out[2] = x0.z; out[3] = x0.w;
     out[4] = x1.x; out[5] = x1.y; out[6] = x1.z; out[7] = x1.w;
   };
+  auto load8h = [&](const __nv_bfloat16* base, int slot, int n, float* out) {
+    unpack8(*reinterpret_cast<const uint4*>(base + state_index(p, l.b, l.h, n, slot) * p.DkM * p.DvP + elem), out);
+  };
   for (int n = p.NT - 1; n >= 0 && l.active; --n) {
     float lx[8] = {}, lA[8] = {}, lD[8] = {}, pa[8] = {}, sa[8] = {};
     if (n >= 1) {
       load8(g.gstates, r, n, lx);
       load8(g.gstates, a, n, lA);
-      if (want) load8(g.pstates, r, n, lD);
+      if (want) load8h(g.pstates, r, n, lD);
     }
     const bool terms = want && n + 1 < p.NT;
     if (terms) {
-      load8(g.pstates, a, n, pa);
+      load8h(g.pstates, a, n, pa);
       load8(p.states, a, n, sa);
     }
     store8(r, n, GX);
@@ -337,8 +337,10 @@ __device__ __forceinline__ void stale_reverse_prefix(const ScanParams& p, const 
   if (want) add_block_dla(acc, g.dla[r], l.h);
 }
 
-// G(n) = e^{128 la} G(n+1) + dSloc(n+1), G(NT-1) = 0, per state element; and
-// the key-weight and closing terms of the log-retention gradient.
+// G(n) = e^{128 la} G(n+1) + dSloc(n+1), G(NT-1) = 0, per state element, kept
+// in f32 registers along the chain and stored as the bf16 images that the dk
+// and dv kernels read (nothing reads an f32 copy); and the key-weight and
+// closing terms of the log-retention gradient.
 __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, ScanGradParams g) {
   const PrefixLane l = prefix_lane(p);
   const int r = l.r;
@@ -403,11 +405,12 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
         // pstates + C'_n S_in: the weight of G(n) in d la (C' = d C / d la).
         const float kc = n + 1 < p.NT ? static_cast<float>(kTile) * closing
                                       : static_cast<float>(len_last) * closing_last;
-        const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
+        float pf[8];
+        unpack8(*reinterpret_cast<const uint4*>(g.pstates + base), pf);
         const float4* sp = reinterpret_cast<const float4*>(p.states + base);
-        const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1 = sp[1];
-        pw[k][0] = make_float4(p0.x + kc * s0.x, p0.y + kc * s0.y, p0.z + kc * s0.z, p0.w + kc * s0.w);
-        pw[k][1] = make_float4(p1.x + kc * s1.x, p1.y + kc * s1.y, p1.z + kc * s1.z, p1.w + kc * s1.w);
+        const float4 s0 = sp[0], s1 = sp[1];
+        pw[k][0] = make_float4(pf[0] + kc * s0.x, pf[1] + kc * s0.y, pf[2] + kc * s0.z, pf[3] + kc * s0.w);
+        pw[k][1] = make_float4(pf[4] + kc * s1.x, pf[5] + kc * s1.y, pf[6] + kc * s1.z, pf[7] + kc * s1.w);
       }
     }
 #pragma unroll
@@ -416,9 +419,6 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_kernel(ScanParams p, Scan
       if (n < 0) break;
       const size_t si = state_index(p, l.b, l.h, n, r);
       if (g.store) {
-        float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
-        gp[0] = make_float4(G[0], G[1], G[2], G[3]);
-        gp[1] = make_float4(G[4], G[5], G[6], G[7]);
         if (in_image) {
           uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
           *reinterpret_cast<uint4*>(img) = pack8(G);
@@ -575,11 +575,12 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_apply_kernel(ScanParams p
       if (want && n < last_dla) {
         const float kc = n + 1 < p.NT ? static_cast<float>(kTile) * closing
                                       : static_cast<float>(len_last) * closing_last;
-        const float4* pp = reinterpret_cast<const float4*>(g.pstates + base);
+        float pf[8];
+        unpack8(*reinterpret_cast<const uint4*>(g.pstates + base), pf);
         const float4* sp = reinterpret_cast<const float4*>(p.states + base);
-        const float4 p0 = pp[0], p1 = pp[1], s0 = sp[0], s1v = sp[1];
-        pw[k][0] = make_float4(p0.x + kc * s0.x, p0.y + kc * s0.y, p0.z + kc * s0.z, p0.w + kc * s0.w);
-        pw[k][1] = make_float4(p1.x + kc * s1v.x, p1.y + kc * s1v.y, p1.z + kc * s1v.z, p1.w + kc * s1v.w);
+        const float4 s0 = sp[0], s1v = sp[1];
+        pw[k][0] = make_float4(pf[0] + kc * s0.x, pf[1] + kc * s0.y, pf[2] + kc * s0.z, pf[3] + kc * s0.w);
+        pw[k][1] = make_float4(pf[4] + kc * s1v.x, pf[5] + kc * s1v.y, pf[6] + kc * s1v.z, pf[7] + kc * s1v.w);
       }
     }
 #pragma unroll
@@ -588,9 +589,6 @@ __global__ void __launch_bounds__(256) scan_bwd_prefix_apply_kernel(ScanParams p
       if (n < n0) break;
       const size_t si = state_index(p, l.b, l.h, n, r);
       if (g.store) {
-        float4* gp = reinterpret_cast<float4*>(g.gstates + si * p.DkM * p.DvP + elem);
-        gp[0] = make_float4(G[0], G[1], G[2], G[3]);
-        gp[1] = make_float4(G[4], G[5], G[6], G[7]);
         if (in_image) {
           uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p)) + img_off;
           *reinterpret_cast<uint4*>(img) = pack8(G);
