@@ -74,7 +74,8 @@ int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, i
  * w = 1 (plain sum), alpha_h^(t-i) (static per-head log-retention) or
  * 1 - alpha_h^(t-i) (the stale view, `stale` below).  The
  * score tile q.k^T is formed once and shared by all retentions; the carried
- * state is f32.  Streams are bf16; their innermost dimension is contiguous.
+ * state is f32.  Streams are bf16 (f32 with f32_streams below); their
+ * innermost dimension is contiguous.
  */
 typedef struct ts_scan_args {
   int batch, heads, tokens;
@@ -122,6 +123,17 @@ typedef struct ts_scan_args {
    * log_alpha[r]; takes no boundary states (init/final NULL, stage 0).  Each
    * stale retention carries one extra decayed state in the workspace. */
   int stale[TS_MAX_RETENTIONS];
+  /* Nonzero: q, k, v are f32 streams, out is f32 (out_dtype TS_DTYPE_F32),
+   * and the backward's dout, dq, dk and dv are f32 (grad_dtype TS_DTYPE_F32,
+   * dv contiguous).  Float32 streams are scanned with f32 FMAs on the CUDA
+   * cores -- bf16 or tf32 tensor-core operands cannot meet the reference's
+   * float32 tolerance (rel-err 1e-5) -- for dk, dv <= 256 within the shared
+   * memory of one CTA (dk 128 with dv up to 248, dk 256 with dv up to 123), without
+   * stale retentions, boundary states or stages (TS_ERR_NOT_IMPLEMENTED
+   * otherwise; a stale view of f32 streams is the difference of the plain and
+   * recency reads, which the host forms as the reference does).  Zero: bf16
+   * streams on the tensor cores. */
+  int f32_streams;
 } ts_scan_args;
 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args);
@@ -131,7 +143,8 @@ int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream);
 
 /* Gradients of the multi-view scan (the autograd of scan_chunk.py:246-339,
  * pinned by tests/test_scan_chunk.py:271-340 of the reference).
- * dout[r]: bf16 [B,H,T,dv] contiguous.  dq/dk f32 or bf16 [B,H,T,dk], dv
+ * dout[r]: bf16 [B,H,T,dv] contiguous (f32 for f32 streams).  dq/dk f32 or
+ * bf16 [B,H,T,dk], dv
  * [B,H,T,dv] contiguous in grad_dtype (dv excludes nothing: with
  * v_append_unit the unit column's gradient is computed and discarded).
  * dlog_alpha[r]: device f32 [heads], ACCUMULATED into (zero it first); may be

@@ -1,0 +1,269 @@
+"""GPU parity of the float32 path: the f32 scan kernels and the float32 mixer.
+
+The reference's fp32 configuration (config 1: softmax-partition features,
+B=2, T=512, d_model=256, H=4, d_k=d_v=64, m=64, recency bank 0.95) sets the
+float32 bound: ``max|got - ref| / max|ref| <= 1e-5`` on outputs and every
+gradient, against the float64 oracle evaluated at the same float32 inputs.
+The scan kernels are checked on their own (forward, q/k/v and log-retention
+gradients, ragged and single-tile lengths, 32- and 64-token tiles, stale
+views formed as the reference forms them), then the whole float32 mixer, and
+the float32 mixer against the reference's own golden fixtures.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import pytest
+import torch
+
+from oracle import mixer as omixer
+from oracle import scan as oscan
+
+pytestmark = pytest.mark.gpu
+F32_TOL = 1e-5
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+sys.path.insert(0, os.path.dirname(__file__))
+
+
+def rel_err(got, want):
+    got = got.detach().to("cpu", torch.float64)
+    want = want.detach().to("cpu", torch.float64)
+    return float((got - want).abs().max() / want.abs().max().clamp_min(1e-30))
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda")
+
+
+def _streams(B, H, T, Dk, Dv, seed=0, positive=False):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, T, Dk, generator=g) / Dk ** 0.5
+    k = torch.randn(B, H, T, Dk, generator=g) / Dk ** 0.5
+    if positive:
+        q, k = q.abs(), k.abs()
+    return q, k, torch.randn(B, H, T, Dv, generator=g)
+
+
+def _retentions(H, n_decayed, with_sum):
+    rets = [None] if with_sum else []
+    for j in range(n_decayed):
+        g = torch.Generator().manual_seed(j)
+        rets.append(torch.log(0.85 + 0.04 * j + (0.999 - 0.85 - 0.04 * j) * torch.rand(H, generator=g)))
+    return rets
+
+
+F32_CASES = [
+    # B, H, T,  Dk,  Dv, n_decayed, with_sum, append_unit
+    (2, 3, 37, 5, 4, 1, True, False),         # one ragged tile
+    (1, 2, 64, 16, 8, 1, True, False),        # exactly one tile
+    (2, 4, 512, 64, 64, 1, True, True),       # config 1: m=64 keys, [v | 1] payload
+    (1, 2, 300, 64, 65, 2, True, False),
+    (1, 1, 1030, 32, 16, 2, False, False),
+    (1, 2, 200, 128, 136, 1, True, False),    # 32-token tiles (shared-memory budget)
+    (1, 2, 150, 256, 65, 1, True, True),      # config-2 key width, 32-token tiles
+    (1, 2, 97, 1, 64, 1, True, False),        # unit queries and keys: the feature-mass prefix
+]
+
+
+@pytest.mark.parametrize("case", F32_CASES)
+def test_f32_scan_forward_matches_oracle(dev, case):
+    from thetascan_b200 import _lib, scan
+    B, H, T, Dk, Dv, nd, with_sum, unit = case
+    q, k, v = _streams(B, H, T, Dk, Dv)
+    rets = _retentions(H, nd, with_sum)
+    got = scan.linattn_views(q.to(dev), k.to(dev), v.to(dev), tuple(None if r is None else r.to(dev) for r in rets),
+                             append_unit=unit)
+    vv = torch.cat([v, torch.ones(B, H, T, 1)], -1) if unit else v
+    want = oscan.linattn_chunk_views(q.double(), k.double(), vv.double(),
+                                     tuple(None if r is None else r.double() for r in rets), chunk=64)
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for g_, w_ in zip(got, want):
+        assert g_.dtype == torch.float32 and g_.shape == w_.shape
+        assert rel_err(g_, w_) < F32_TOL
+
+
+@pytest.mark.parametrize("positive", [False, True])
+@pytest.mark.parametrize("index", range(len(F32_CASES)))
+def test_f32_scan_backward_matches_oracle(dev, index, positive):
+    from thetascan_b200 import _lib, scan
+    B, H, T, Dk, Dv, nd, with_sum, unit = F32_CASES[index]
+    q, k, v = _streams(B, H, T, Dk, Dv, seed=1, positive=positive)
+    rets = _retentions(H, nd, with_sum)
+    g = torch.Generator().manual_seed(7)
+    width = Dv + (1 if unit else 0)
+    weights = [torch.randn(B, H, T, width, generator=g, dtype=torch.float64) for _ in rets]
+
+    def loss(outs):
+        return sum((o.double() * w.to(o.device)).sum() for o, w in zip(outs, weights))
+
+    leaves = [x.to(dev).requires_grad_(True) for x in (q, k, v)]
+    rleaves = [None if r is None else r.to(dev).requires_grad_(True) for r in rets]
+    loss(scan.linattn_views(*leaves, tuple(rleaves), append_unit=unit)).backward()
+    oleaves = [x.double().requires_grad_(True) for x in (q, k, v)]
+    orets = [None if r is None else r.double().requires_grad_(True) for r in rets]
+    ov = torch.cat([oleaves[2], torch.ones(B, H, T, 1, dtype=torch.float64)], -1) if unit else oleaves[2]
+    loss(oscan.linattn_chunk_views(oleaves[0], oleaves[1], ov, tuple(orets), chunk=64)).backward()
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for name, got, want in zip("qkv", leaves, oleaves):
+        assert got.grad.dtype == torch.float32
+        assert rel_err(got.grad, want.grad) < F32_TOL, name
+    for got, want in zip(rleaves, orets):
+        if got is not None:
+            assert rel_err(got.grad, want.grad) < F32_TOL
+
+
+def test_f32_stale_views_are_sum_minus_recency(dev):
+    """A stale view of float32 streams is the reference's FadeStale
+    difference S_sum - S_fast (interface.py:268-273)."""
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv = 1, 2, 300, 32, 17
+    q, k, v = _streams(B, H, T, Dk, Dv, seed=3, positive=True)
+    rets = _retentions(H, 2, True)
+    leaves = [x.to(dev).requires_grad_(True) for x in (q, k, v)]
+    rl = [None if r is None else r.to(dev).requires_grad_(True) for r in rets]
+    got = scan.linattn_views(*leaves, tuple(rl), stale=(False, True, True))
+    sum((o.double() * (i + 1)).sum() for i, o in enumerate(got)).backward()
+    ol = [x.double().requires_grad_(True) for x in (q, k, v)]
+    orl = [None if r is None else r.double().requires_grad_(True) for r in rets]
+    plain = oscan.linattn_chunk_views(*ol, tuple(orl), chunk=64)
+    want = [plain[0], plain[0] - plain[1], plain[0] - plain[2]]
+    sum((o * (i + 1)).sum() for i, o in enumerate(want)).backward()
+    for g_, w_ in zip(got, want):
+        assert rel_err(g_, w_) < F32_TOL
+    for a, b in zip(leaves + rl[1:], ol + orl[1:]):
+        assert rel_err(a.grad, b.grad) < F32_TOL
+
+
+def test_f32_scan_errors(dev):
+    import ctypes
+    from thetascan_b200 import _lib, scan
+    q, k, v = (x.to(dev) for x in _streams(1, 2, 16, 8, 8))
+    with pytest.raises(NotImplementedError):
+        scan.linattn(q, k.bfloat16(), v)              # mixed stream dtypes
+    with pytest.raises(NotImplementedError):
+        scan.linattn_views_stream(q, k, v, (None,))   # boundary states: bf16 streams only
+    # the C ABI refuses boundary states, stages and stale slots of f32 streams
+    lib = _lib.load()
+    out = torch.empty(1, 2, 16, 8, device=dev)
+    args = scan._build_args(q, k, v, [None], [out], False)
+    args.stage = 1
+    assert lib.ts_b200_scan_workspace_bytes(ctypes.byref(args)) == 0
+    args.stage, args.stale[0] = 0, 1
+    assert lib.ts_b200_scan_workspace_bytes(ctypes.byref(args)) == 0
+    args.stale[0] = 0
+    args.out_dtype = _lib.TS_DTYPE_BF16
+    assert lib.ts_b200_scan_workspace_bytes(ctypes.byref(args)) == 0
+    # static entry point: no f32 streams
+    args.out_dtype = _lib.TS_DTYPE_F32
+    with pytest.raises(NotImplementedError):
+        _lib.check(lib.ts_b200_scan_fwd_static(ctypes.byref(args), scan._stream()))
+
+
+# ------------------------------------------------------------------- mixer
+
+def _config1():
+    from thetascan_b200.config import KernelConfig, TemporalConfig, ThetaScanConfig
+    return ThetaScanConfig(d_model=256, n_heads=4, memory_multiplier=1, feature_expansion=1, family="kernel",
+                           kernel=KernelConfig(feature_map="softmax_partition"),
+                           temporal=TemporalConfig(mode="bank", retention_init=0.95))
+
+
+def _oracle_grads(module, core_cfg, x, w):
+    params = {n: t.detach().cpu().double().requires_grad_(True) for n, t in module._core.named_parameters()}
+    for n, t in module._core.named_buffers():
+        if n.startswith("_expand_"):
+            params[n] = t.detach().cpu().double()
+    xo = x.detach().cpu().double().requires_grad_(True)
+    yo = omixer.mixer_forward(params, core_cfg, xo)
+    (yo * w).sum().backward()
+    return yo, xo.grad, params
+
+
+def test_config1_f32_mixer_matches_oracle(dev):
+    """Config 1 end to end in float32: output, input gradient and every
+    parameter gradient within 1e-5 of the float64 oracle (default-initialised
+    weights from seed 0 with a nonzero slow decode W2 and blend, x ~ N(0,1))."""
+    from thetascan_b200.mixer import ThetaScan
+    cfg = _config1()
+    torch.manual_seed(0)
+    module = ThetaScan(cfg)
+    with torch.no_grad():
+        g = torch.Generator().manual_seed(3)
+        module._core.W2[0].copy_(torch.randn(module._core.W2[0].shape, generator=g) * 0.2)
+        module._core.fade_eta.copy_(torch.randn(4, generator=g) * 0.5)
+    module = module.to(dev)
+    B, T = 2, 512
+    x = torch.randn(B, T, 256, generator=torch.Generator().manual_seed(4))
+    w = torch.randn(B, T, 256, generator=torch.Generator().manual_seed(5), dtype=torch.float64)
+    xg = x.to(dev).requires_grad_(True)
+    y = module(xg)
+    assert y.dtype == torch.float32
+    (y.double() * w.to(dev)).sum().backward()
+    core_cfg = {"n_heads": 4, "head_dim": 64, "feature_expansion": 1, "kernel_kind": "softmax_partition",
+                "softmax_gain": float(cfg.kernel.kernel_sharpness), "rope": cfg.rope.mode,
+                "rope_frac": cfg.rope.fraction, "rope_base": float(cfg.rope.base), "read_fade": True,
+                "read_fade_mode": "fast", "read_norm": "key_mass", "eps": 1e-6, "scan_chunk": 128}
+    yo, xgo, params = _oracle_grads(module, core_cfg, x, w)
+    assert rel_err(y, yo) < F32_TOL
+    assert rel_err(xg.grad, xgo) < F32_TOL
+    for name, p in module._core.named_parameters():
+        if p.grad is not None:
+            assert rel_err(p.grad, params[name].grad) < F32_TOL, name
+
+
+GOLDEN_CASES = ["relu2_d64_ragged", "bspline_stale", "softmax_bank_fast", "relu2_expanded_rope",
+                "softmax_sum_feature_mass"]
+
+
+def _oracle_on_fixture(case, dtype):
+    """The oracle mixer on the fixture's float32-rounded inputs, computed in
+    ``dtype``: float64 is the exact answer; float32 runs the reference's own
+    float32 arithmetic (the oracle restates its operations one for one)."""
+    from test_oracle_golden import _core_cfg
+    params = {n: t.detach().float().to(dtype).clone() for n, t in case["params"].items()}
+    for n in params:
+        if not n.startswith("_"):
+            params[n].requires_grad_(True)
+    x = case["x"].detach().float().to(dtype).clone().requires_grad_(True)
+    y = omixer.mixer_forward(params, _core_cfg(case), x)
+    (y * case["out_weight"].to(dtype)).sum().backward()
+    return y.detach(), x.grad, {n: t.grad for n, t in params.items() if t.grad is not None}
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_f32_mixer_matches_reference_golden_fixture(dev, name):
+    """The float32 mixer on the reference's own fixtures: output against the
+    fixture, output and every gradient against the float64 oracle at the same
+    float32 inputs, within 1e-5 -- or, where the reference's own float32
+    arithmetic misses the float64 answer by more than that, within twice the
+    reference's own float32 error.  That is the stale B-spline fixture: its
+    stale view is the reference's difference S_sum - S_fast, which cancels on
+    early tokens, and the reference in float32 misses the float64 input
+    gradient by 3.7e-3 of its largest entry (the float32 path here by ~1e-3)."""
+    from thetascan_b200.config import ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+
+    case = torch.load(os.path.join(GOLDEN, "mixer_cases.pt"), weights_only=False)[name]
+    module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    xg = case["x"].detach().float().to(dev).requires_grad_(True)
+    y = module(xg)
+    assert y.dtype == torch.float32
+    (y.double() * case["out_weight"].to(dev, torch.float64)).sum().backward()
+    y64, xg64, g64 = _oracle_on_fixture(case, torch.float64)
+    y32, xg32, g32 = _oracle_on_fixture(case, torch.float32)
+
+    def bound(ref32, ref64):
+        return max(F32_TOL, 2.0 * rel_err(ref32, ref64))
+
+    assert rel_err(y, case["y"]) < F32_TOL
+    assert rel_err(y, y64) < F32_TOL
+    assert rel_err(xg.grad, xg64) < bound(xg32, xg64)
+    for n, p in module._core.named_parameters():
+        if p.grad is not None:
+            assert rel_err(p.grad, g64[n]) < bound(g32[n], g64[n]), n

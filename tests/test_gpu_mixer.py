@@ -7,7 +7,8 @@
    feature-mass read): output, input gradient and every parameter gradient.
 2. Against the float64 oracle mixer on a config-2-shaped module (relu2 ridge
    with 2x random feature expansion, m=256, partial RoPE, fast bank).
-Tolerance: ``max|got - ref| / max|ref| <= 2e-2`` (bf16 streams).
+Inputs are bf16 (the tensor-core path).  Tolerance:
+``max|got - ref| / max|ref| <= 2e-2`` (bf16 streams).
 """
 from __future__ import annotations
 
@@ -104,8 +105,11 @@ def test_mixer_matches_reference_golden_fixture(dev, name):
     module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
     state = {"_core." + n: t.float() for n, t in case["params"].items() if not n.startswith("_expand_")}
     module.load_state_dict(state)
-    x = case["x"].float().to(dev).requires_grad_(True)
+    # a bf16 input runs the tensor-core path (a float32 one the float32 path,
+    # tests/test_gpu_f32.py)
+    x = case["x"].to(dev).bfloat16().requires_grad_(True)
     y = module(x)
+    assert y.dtype == torch.bfloat16
     assert rel_err(y, case["y"]) < BF16_TOL
     (y.double() * case["out_weight"].to(dev)).sum().backward()
     y_o, xg_o, grads_o = _oracle_at_bf16_inputs(case)
@@ -140,6 +144,7 @@ def test_config2_shaped_mixer_matches_oracle(dev):
     module = module.to(dev)
     B, T = 2, 600
     x = torch.randn(B, T, 256, generator=torch.Generator().manual_seed(4))
+    x = x.bfloat16()
     xg = x.to(dev).requires_grad_(True)
     y = module(xg)
     w = torch.randn(B, T, 256, generator=torch.Generator().manual_seed(5), dtype=torch.float64)

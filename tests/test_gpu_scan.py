@@ -212,7 +212,7 @@ def test_scan_errors_follow_the_reference_contract(lib):
     with pytest.raises(NotImplementedError):
         scan.linattn(q, k, v, -torch.rand(1, 2, 16, 8, device="cuda"))
     with pytest.raises(NotImplementedError):
-        scan.linattn(q.float(), k.float(), v.float())
+        scan.linattn(q.float(), k, v)   # mixed stream dtypes
     with pytest.raises(RuntimeError):
         scan.linattn(q.cpu(), k.cpu(), v.cpu())
 

@@ -60,7 +60,7 @@ def test_sharded_mixer_matches_unsharded(dev, kind, P, T):
     from thetascan_b200.seqpar import SequentialShards
     module = _module(kind, dev)
     g = torch.Generator(device="cpu").manual_seed(5)
-    x = torch.randn(2, T, 256, generator=g).to(dev)
+    x = torch.randn(2, T, 256, generator=g).to(dev).bfloat16()
     w = torch.randn(2, T, 256, generator=g).to(dev)
 
     xf = x.clone().requires_grad_(True)

@@ -35,6 +35,7 @@ class ScanArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("init_state", ctypes.c_void_p), ("final_state", ctypes.c_void_p), ("stage", ctypes.c_int),
         ("stale", ctypes.c_int * MAX_RETENTIONS),
+        ("f32_streams", ctypes.c_int),
     ]
 
 

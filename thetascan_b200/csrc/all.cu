@@ -4,6 +4,7 @@
 #include "selftest.cu"
 #include "scan_fwd.cu"
 #include "scan_bwd.cu"
+#include "scan_f32.cu"
 #include "feature.cu"
 #include "kread.cu"
 #include "mass.cu"

@@ -5,6 +5,7 @@
 
 #include "capi_internal.h"
 #include "scan.cuh"
+#include "scan_f32.cuh"
 
 namespace ts {
 
@@ -128,6 +129,105 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
   return TS_OK;
 }
 
+// ------------------------------------------------------------ f32 streams
+
+static size_t f32_states_bytes(const ScanF32Params& p) {
+  return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * p.Dk * p.Dv * sizeof(float));
+}
+
+// Validate `a` (f32_streams set) and fill `p` (workspace pointers left null).
+static int build_scan_f32_params(const ts_scan_args* a, ScanF32Params* p) {
+  if (a->batch < 1 || a->heads < 1 || a->tokens < 1)
+    return set_error(TS_ERR_VALUE, "scan: batch, heads and tokens must be >= 1");
+  if (a->dk < 1 || a->dk > kF32MaxDk)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan (f32 streams): key width %d outside 1..%d", a->dk, kF32MaxDk);
+  if (a->v_append_unit < 0 || a->v_append_unit > 2)
+    return set_error(TS_ERR_VALUE, "scan: v_append_unit must be 0, 1 or 2");
+  if (a->dv < 1 + a->v_append_unit || a->dv > kF32MaxDv)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan (f32 streams): payload width %d outside 1..%d", a->dv,
+                     kF32MaxDv);
+  if (a->n_retentions < 1 || a->n_retentions > TS_MAX_RETENTIONS)
+    return set_error(TS_ERR_VALUE, "scan: n_retentions must be in 1..%d", TS_MAX_RETENTIONS);
+  if (!a->q || !a->k || !a->v) return set_error(TS_ERR_VALUE, "scan: null stream pointer");
+  if (a->out_dtype != TS_DTYPE_F32)
+    return set_error(TS_ERR_VALUE, "scan: f32 streams give f32 outputs (out_dtype TS_DTYPE_F32)");
+  if (a->init_state || a->final_state || a->stage != 0)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan: f32 streams take no boundary states or stages");
+  std::memset(p, 0, sizeof(*p));
+  p->B = a->batch;
+  p->H = a->heads;
+  p->T = a->tokens;
+  p->Dk = a->dk;
+  p->Dv = a->dv;
+  // 64-token tiles where the backward's tiles and one staged state fit, else 32
+  p->TL = scan_f32_smem(64, a->dk, a->dv, true) <= kMaxSmem ? 64 : 32;
+  if (scan_f32_smem(p->TL, a->dk, a->dv, true) > kMaxSmem)
+    return set_error(TS_ERR_NOT_IMPLEMENTED,
+                     "scan (f32 streams): key width %d with payload width %d exceeds the shared-memory budget of one CTA",
+                     a->dk, a->dv);
+  p->NT = ceil_div(a->tokens, p->TL);
+  p->R = a->n_retentions;
+  p->v_unit = a->v_append_unit;
+  if (static_cast<long long>(p->B) * p->H * p->R > 65535)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan (f32 streams): batch x heads x retentions above 65535");
+  p->q = static_cast<const float*>(a->q);
+  p->k = static_cast<const float*>(a->k);
+  p->v = static_cast<const float*>(a->v);
+  for (int i = 0; i < 3; ++i) {
+    p->qs[i] = a->q_strides[i];
+    p->ks[i] = a->k_strides[i];
+    p->vs[i] = a->v_strides[i];
+  }
+  for (int r = 0; r < p->R; ++r) {
+    if (a->stale[r])
+      return set_error(TS_ERR_NOT_IMPLEMENTED,
+                       "scan: stale retentions of f32 streams are formed by the host (plain read minus recency read)");
+    if (!a->out[r]) return set_error(TS_ERR_VALUE, "scan: null output pointer for retention %d", r);
+    p->la[r] = a->log_alpha[r];
+    p->out[r] = static_cast<float*>(a->out[r]);
+  }
+  return TS_OK;
+}
+
+static int scan_f32_fwd(const ts_scan_args* a, cudaStream_t s) {
+  ScanF32Params p;
+  if (int e = build_scan_f32_params(a, &p)) return e;
+  const size_t need = f32_states_bytes(p);
+  if (!a->workspace || a->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_fwd: workspace of %zu bytes needed", need);
+  p.states = static_cast<float*>(a->workspace);
+  return launch_scan_f32_fwd(p, s);
+}
+
+static int scan_f32_bwd(const ts_scan_args* a, const ts_scan_grad_args* g, cudaStream_t s) {
+  ScanF32Params p;
+  if (int e = build_scan_f32_params(a, &p)) return e;
+  if (!g) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient arguments");
+  const size_t need = f32_states_bytes(p);
+  if (!a->workspace || a->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_bwd: the forward workspace (%zu bytes) is required", need);
+  if (!g->workspace || g->workspace_bytes < need)
+    return set_error(TS_ERR_VALUE, "scan_bwd: backward workspace of %zu bytes needed", need);
+  if (g->grad_dtype != TS_DTYPE_F32)
+    return set_error(TS_ERR_VALUE, "scan_bwd: f32 streams give f32 gradients (grad_dtype TS_DTYPE_F32)");
+  if (g->dv_strides[0] | g->dv_strides[1] | g->dv_strides[2])
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan_bwd: f32 streams write a contiguous dv");
+  if (g->dfinal_state || g->dinit_state || g->stage != 0)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan_bwd: f32 streams take no boundary states or stages");
+  if (!g->dq || !g->dk || !g->dv) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
+  for (int r = 0; r < p.R; ++r) {
+    p.dout[r] = static_cast<const float*>(g->dout[r]);
+    if (!p.dout[r]) return set_error(TS_ERR_VALUE, "scan_bwd: null dout for retention %d", r);
+    p.dla[r] = g->dlog_alpha[r];
+  }
+  p.dq = static_cast<float*>(g->dq);
+  p.dk = static_cast<float*>(g->dk);
+  p.dv = static_cast<float*>(g->dv);
+  p.states = static_cast<float*>(a->workspace);
+  p.gstates = static_cast<float*>(g->workspace);
+  return launch_scan_f32_bwd(p, s);
+}
+
 }  // namespace ts
 
 using namespace ts;
@@ -162,18 +262,27 @@ int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, i
 }
 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
+  if (args && args->f32_streams) {
+    ScanF32Params p;
+    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) : 0;
+  }
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;
   return states_bytes(p) + images_bytes(p);
 }
 
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* args) {
+  if (args && args->f32_streams) {
+    ScanF32Params p;
+    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) : 0;
+  }
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;
   return 2 * states_bytes(p) + images_bytes(p) + segs_bytes(p);
 }
 
 int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
+  if (args && args->f32_streams) return scan_f32_fwd(args, reinterpret_cast<cudaStream_t>(stream));
   ScanParams p;
   if (int e = build_scan_params(args, &p)) return e;
   const size_t need = states_bytes(p) + images_bytes(p);
@@ -194,6 +303,7 @@ int ts_b200_scan_fwd(const ts_scan_args* args, ts_stream_t stream) {
 }
 
 int ts_b200_scan_bwd(const ts_scan_args* args, const ts_scan_grad_args* grad, ts_stream_t stream) {
+  if (args && args->f32_streams) return scan_f32_bwd(args, grad, reinterpret_cast<cudaStream_t>(stream));
   ScanParams p;
   if (int e = build_scan_params(args, &p)) return e;
   if (!grad) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient arguments");

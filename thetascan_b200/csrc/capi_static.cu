@@ -47,6 +47,8 @@ int scratch_address(void** out) {
 
 extern "C" int ts_b200_scan_fwd_static(const ts_scan_args* args, ts_stream_t stream) {
   using namespace ts;
+  if (args && args->f32_streams)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "scan_fwd_static: f32 streams need ts_b200_scan_fwd with a workspace");
   ScanParams p;
   if (int e = build_scan_params(args, &p)) return e;
   if (args->stage != 0) return set_error(TS_ERR_VALUE, "scan_fwd_static: only the whole forward (stage 0)");

@@ -12,8 +12,12 @@ cuBLAS GEMMs and the hot path (feature maps, multi-view scan, normalized read
 and bank blend) as the sm_100a kernels of :mod:`thetascan_b200.kernel`.  With
 the fused q/k/v projection, RoPE and the L2 norm of q and k run inside the
 feature kernels (and their backward inside the feature backward); the other
-projection layouts apply them as PyTorch f32 elementwise ops.  Streams are bf16; a float32
-input is computed with bf16 streams and returned in float32.
+projection layouts apply them as PyTorch f32 elementwise ops.  A bf16 input
+runs bf16 streams on the tensor cores.  A float32 input runs float32
+throughout, as the reference computes its fp32 configuration: the per-token
+math in float32 PyTorch and every sequence read on the float32 scan kernels
+(:mod:`thetascan_b200.precise`); the GN family keeps its float32 per-token
+math with bf16 scan streams for either input.
 """
 from __future__ import annotations
 
@@ -284,6 +288,28 @@ class ThetaScanCore(nn.Module):
         y = per_token(out, y, xf, self.proj_out.weight, *gate)
         return y.to(x.dtype)
 
+    def _forward_f32(self, x, shard):
+        """Kernel family on a float32 input: float32 throughout, the sequence
+        reads on the float32 scan kernels (:mod:`thetascan_b200.precise`)."""
+        from .precise import kernel_core_f32
+        if shard is not None:
+            raise NotImplementedError("thetascan_b200: sequence shards run bf16 streams; pass a bf16 input")
+        B, T, _ = x.shape
+        H, d = self.n_heads, self.head_dim
+        rot, base = self._rot, self.cfg.rope.base
+        q, k, v = self.project(x)
+        q, k = _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base))
+        if self.vmlp_in is not None:
+            v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
+        W1, W2 = self.effective_weights()
+        log_alphas, etas = self.fade()
+        y = kernel_core_f32(q, k, v.contiguous(), W1, W2, self.spec, log_alphas=log_alphas, etas=etas,
+                            **self.kernel_controls()).transpose(1, 2)
+        if self.ogate is not None:
+            lin = self.ogate.g.lin
+            y = y * F.silu(F.linear(x, lin.weight, lin.bias).view(B, T, H, d))
+        return F.linear(y.reshape(B, T, H * d), self.proj_out.weight)
+
     def effective_weights(self):
         """``U W1`` and ``W2 D`` (block.py:546-567)."""
         W1, W2 = self.W1[0], self.W2[0]
@@ -346,6 +372,8 @@ class ThetaScanCore(nn.Module):
             raise RuntimeError("thetascan_b200 requires a CUDA input")
         if self.cfg.family == "gn":
             return self._forward_gn(x, shard)
+        if x.dtype == torch.float32:
+            return self._forward_f32(x, shard)
         B, T, _ = x.shape
         H, d = self.n_heads, self.head_dim
         out_dtype = x.dtype

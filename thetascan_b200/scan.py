@@ -7,10 +7,13 @@ dtype and errors, computed by the sm_100a kernels behind the C ABI
 reference's but does not change the result: the kernels tile the sequence in
 128-token tiles internally, and the chunked algebra is exact for any tile.
 
-Supported: bf16 streams on a CUDA device, the plain causal sum (``None``) and
-static per-head log-retentions (``[H]``), up to four retentions per call,
-``Dk <= 256`` and ``Dv <= 128``.  Per-token retention streams (``[B,H,T,1]``)
-and float32 streams raise ``NotImplementedError``; a non-CUDA tensor raises
+Supported: bf16 streams on the tensor cores and float32 streams on the CUDA
+cores (f32 FMAs: the float32 tolerance of the reference is out of reach of
+bf16 or tf32 operands), on a CUDA device, with the plain causal sum
+(``None``) and static per-head log-retentions (``[H]``), up to four
+retentions per call, ``Dk`` and ``Dv`` up to 256 within the CTA budgets
+(float32: ``Dk = 128`` with ``Dv <= 248``, ``Dk = 256`` with ``Dv <= 123``).  Per-token retention streams (``[B,H,T,1]``) and mixed stream
+dtypes raise ``NotImplementedError``; a non-CUDA tensor raises
 ``RuntimeError``.  Nothing falls back to a CPU implementation.
 """
 from __future__ import annotations
@@ -55,6 +58,7 @@ def _build_args(q, k, v, las, outs, append_unit, workspace=None, stale=None):
         if outs is not None:
             a.out[i] = outs[i].data_ptr()
     a.out_dtype = _lib.TS_DTYPE_BF16 if (outs is not None and outs[0].dtype == torch.bfloat16) else _lib.TS_DTYPE_F32
+    a.f32_streams = 1 if q.dtype == torch.float32 else 0
     if workspace is not None:
         a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     return a
@@ -103,8 +107,10 @@ class _ScanViews(torch.autograd.Function):
         las = [la if present else None for la, present in zip(saved[4 + n:4 + 2 * n], ctx.ret_present)]
         B, H, T, Dk = q.shape
         dv_width = outs[0].shape[-1]
-        dgrads = [torch.zeros(B, H, T, dv_width, dtype=torch.bfloat16, device=q.device) if d is None
-                  else d.to(torch.bfloat16).contiguous() for d in douts]
+        # bf16 streams take bf16 read gradients; f32 streams keep them f32
+        gdt = torch.float32 if q.dtype == torch.float32 else torch.bfloat16
+        dgrads = [torch.zeros(B, H, T, dv_width, dtype=gdt, device=q.device) if d is None
+                  else d.to(gdt).contiguous() for d in douts]
         args = _build_args(q, k, v, las, outs, ctx.append_unit, ws, stale=ctx.stale)
         g = _lib.ScanGradArgs()
         dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
@@ -133,9 +139,10 @@ def _check_inputs(q, k, v, retentions, chunk):
     for x in (q, k, v):
         if not x.is_cuda:
             raise RuntimeError("b200 backend requires CUDA tensors")
-    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.bfloat16, torch.float32):
         raise NotImplementedError(
-            "b200 backend: bf16 streams only (float32 needs the split-precision tensor-core path)")
+            "b200 backend: q, k and v must all be bf16 (tensor cores) or all float32 (CUDA cores), "
+            f"got {q.dtype}, {k.dtype}, {v.dtype}")
     H = q.shape[1]
     for r in retentions:
         if r is None:
@@ -169,6 +176,12 @@ def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_uni
     for r, st in zip(retentions, stale):
         if st and r is None:
             raise ValueError("b200 scan: a stale view needs a retention")
+    if any(stale) and q.dtype == torch.float32:
+        # float32: the stale view as the reference forms it, S_sum - S_fast
+        # (FadeStale.scan_terms, interface.py:268-273); the difference loses
+        # nothing the float32 tolerance would see
+        reads = linattn_views(q, k, v, tuple(retentions) + (None,), chunk, append_unit=append_unit)
+        return tuple(reads[-1] - o if st else o for o, st in zip(reads[:-1], stale))
     outs = []
     # The kernels take at most four retentions per call; longer tuples are split.
     for start in range(0, len(retentions), _lib.MAX_RETENTIONS):
@@ -198,6 +211,8 @@ def linattn_views_stream(q, k, v, retentions, state=None, *, append_unit: bool =
     if not retentions:
         return (), state
     _check_inputs(q, k, v, retentions, DEFAULT_CHUNK)
+    if q.dtype == torch.float32:
+        raise NotImplementedError("b200 streaming scan: bf16 streams only")
     if len(retentions) > _lib.MAX_RETENTIONS:
         raise NotImplementedError(f"b200 streaming scan: at most {_lib.MAX_RETENTIONS} retentions per call")
     lib = _lib.load()
