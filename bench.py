@@ -41,6 +41,10 @@ METRIC = "mixer fwd+bwd tokens/s at T=4K/32K, 1/2/4/8 B200, % of tensor roofline
 CONFIGS = {
     # name: (B, T, d_model, H, memory_multiplier, expansion, feature_map, rope, J)
     "c2": dict(B=8, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
+    # config 1: the reference's float32 case (softmax partition, m = d = 64, recency
+    # bank initialised at 0.95), float32 end to end on the f32 scan kernels
+    "c1": dict(B=2, T=512, D=256, H=4, mult=1, expansion=1, fmap="softmax_partition", rope="none", J=1,
+               dtype="f32", retention_spread=False),
     "small": dict(B=2, T=1024, D=512, H=8, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
     # config-2 shapes at batch 2: inputs still larger than L2, for profiler captures
     "c2b2": dict(B=2, T=4096, D=1024, H=16, mult=4, expansion=2, fmap="relu2_ridge", rope="partial", J=1),
@@ -59,6 +63,8 @@ CONFIGS = {
 }
 
 WORKLOADS = {
+    "c1": "config 1: ThetaScan-Kernel softmax partition m=64, fast bank 0.95, output gate, float32 end to end "
+          "(float32 scan kernels on the CUDA cores); fwd+bwd, loss=mean(y^2)",
     "c2": "config 2: ThetaScan-Kernel relu2 ridge m=256 (2x expansion), partial RoPE, 1-branch fast bank, "
           "output gate; fwd+bwd, loss=mean(y^2)",
     "c3": "config 3: ThetaScan-GN relu2, head_dim 128, m=128, two-stage feature-mass read "
@@ -94,7 +100,7 @@ def build_module(cfg, device):
         family="kernel", kernel=kernel, rope=RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=temporal)
     torch.manual_seed(0)
     module = ThetaScan(config)
-    if cfg["J"] == 1:
+    if cfg["J"] == 1 and cfg.get("retention_spread", True):
         # per-head retentions alpha_h ~ U(0.9, 0.999), as the config-2 statement has them
         with torch.no_grad():
             alphas = 0.9 + 0.099 * torch.rand(cfg["H"], generator=torch.Generator().manual_seed(0))
@@ -198,6 +204,9 @@ class PhaseTimer:
         """Kernels one scan call launches (the launch logic of the C ABI:
         csrc/scan_fwd.cu launch_scan_fwd, csrc/scan_bwd.cu launch_scan_bwd)."""
         a = args[0]._obj
+        if a.f32_streams:
+            # csrc/scan_f32.cu: local states (more than one tile), prefix, tile kernel
+            return (1 if a.tokens > 64 else 0) + 2
         nt = -(-a.tokens // 128)
         stale = any(a.stale[i] for i in range(a.n_retentions))
         if name == "ts_b200_scan_fwd":
@@ -384,7 +393,8 @@ def run_b200(args, cfg):
         T = L
     else:
         gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
-        x_host = torch.randn(B, T, cfg["D"], generator=gen).to(torch.bfloat16).pin_memory()
+        xdt = torch.float32 if cfg.get("dtype") == "f32" else torch.bfloat16
+        x_host = torch.randn(B, T, cfg["D"], generator=gen).to(xdt).pin_memory()
     x = x_host.to(device)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
@@ -533,7 +543,15 @@ def run_b200(args, cfg):
     if dominant in MEASURED_TRAFFIC and args.config in ("c2", "c2b2"):
         tb, ttok, _ = MEASURED_TRAFFIC[dominant]
         traffic = tb * (B * T) / ttok
-    if flops_launch / max(bytes_launch, 1) < ridge:
+    if cfg.get("dtype") == "f32":
+        # float32 scan kernels: f32 FMAs on the CUDA cores (no tensor cores)
+        fma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        achieved = flops_launch / launch_s / 1e12
+        roofline = {"bound": "fp32 cuda cores", "kernel": dominant, "achieved": achieved, "peak": fma_peak,
+                    "unit": "TFLOP/s", "frac": achieved / fma_peak, "traffic": None,
+                    "flops_per_launch": flops_launch,
+                    "peak_source": "nominal: 148 SMs x 128 f32 lanes x 2 x 1.965 GHz"}
+    elif flops_launch / max(bytes_launch, 1) < ridge:
         achieved = bytes_launch / launch_s / 1e9
         roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
                     "frac": achieved / peak_hbm, "traffic": traffic, "bytes_per_launch": bytes_launch,
@@ -550,7 +568,8 @@ def run_b200(args, cfg):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True,
         "scaling": "strong" if seqpar else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic x ~ N(0,1), seeded random-init weights",
+        "vs_baseline": None, "dtype": "f32" if cfg.get("dtype") == "f32" else "bf16",
+        "data": "synthetic x ~ N(0,1), seeded random-init weights",
         "config": {"workload": WORKLOADS.get(args.config, f"{args.config}: {cfg}"),
                    "model": "ThetaScan-Kernel mixer", "global_batch": B if seqpar else B * world,
                    "seq_len": T * world if seqpar else T,
@@ -573,6 +592,13 @@ def run_b200(args, cfg):
         "wall_s": wall,
         "device_status": status,
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c1":
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        secs = statistics.median(cpu_reference_step(cfg, T, "bank") for _ in range(3))
+        line["cpu_baseline"] = {"value": T / secs, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"config 1, B=1, T={T}, full bank, chunk form of the reference "
+                                          f"(float32 oracle restatement), forward+backward, median of 3"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c2":
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
