@@ -172,10 +172,14 @@ __device__ __forceinline__ void project(const FeatParams& p, MmaCtx& ctx, const 
 
 // Row statistics of the feature map for this thread's row.
 struct RowState {
-  float inv;   // 1 / rms(a)
-  float mass;  // relu2: sum of squared ReLU; softmax: sum of exp
-  float mx;    // softmax: max logit
-  float dphi;  // with a gradient: sum_j g_j phi_j (relu2 / softmax)
+  float inv;    // 1 / rms(a)
+  float mass;   // relu2: sum of squared ReLU; softmax: sum of exp
+  float mx;     // softmax: max logit
+  float dphi;   // with a gradient: sum_j g_j phi_j (relu2 / softmax)
+  // With a gradient, row totals of the RMSNorm backward and the per-head
+  // controls: dot_a = sum_j dpre_j a_j, dthr = -sum_j dpre_j (relu2),
+  // dgain = sum_j dpre_j sc_j / gain_j (softmax, one gain per head).
+  float dot_a, dthr, dgain;
 };
 
 struct NoGrad {
@@ -188,11 +192,18 @@ struct NoGrad {
 // pass, then one online pass for the max, the partition sum E and sum g e
 // (each part rescales its running sums when its max grows; the parts are
 // combined at the common max).  With kWithGrad, `grad16(c, g)` supplies the
-// feature gradient of columns [c, c+16) and dphi = sum_j g_j phi_j.
+// feature gradient of columns [c, c+16) and dphi = sum_j g_j phi_j, and the
+// same pass forms the row totals that need dpre_j only through sums:
+//   relu2   dpre_j = (g_j - dphi) 2 u_j / mass, so
+//           dot_a = 2/mass (sum g u a - dphi sum u a), dthr = -2/mass (sum g u - dphi sum u);
+//   softmax dpre_j = gain_j phi_j (g_j - dphi), phi_j = e_j / E, so
+//           dot_a = (sum gain e g a - dphi sum gain e a) / E,
+//           dgain = (sum e g sc - dphi sum e sc) / E
+// (the softmax sums rescaled with E when the running max grows).
 template <int KIND, bool kWithGrad, class Grad>
 __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
   const int part = my_part();
-  RowState s{0.f, 0.f, -INFINITY, 0.f};
+  RowState s{0.f, 0.f, -INFINITY, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
   for (int c = 16 * part; c < p.PP; c += kChunkStep) {
     float a[16];
@@ -204,7 +215,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
   if constexpr (KIND == kRelu2) {
     const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
-    float M = 0.f, Sg = 0.f;
+    float M = 0.f, Sg = 0.f, Sgua = 0.f, Sua = 0.f, Sgu = 0.f, Su = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], g[16];
       tmem_ld16(ta_row + c, a);
@@ -215,17 +226,33 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
         if (i < p.P) {
           const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i) - thr, 0.f);
           M += u * u;
-          if (kWithGrad) Sg += g[e] * u * u;
+          if (kWithGrad) {
+            const float gu = g[e] * u;
+            Sg += gu * u;
+            Sgua += gu * a[e];
+            Sua += u * a[e];
+            Sgu += gu;
+            Su += u;
+          }
         }
       }
     }
     s.mass = row_pair_sum(M, pair);
     if (kWithGrad) {
       Sg = row_pair_sum(Sg, pair);
-      s.dphi = s.mass > p.eps ? Sg / s.mass : 0.f;
+      Sgua = row_pair_sum(Sgua, pair);
+      Sua = row_pair_sum(Sua, pair);
+      Sgu = row_pair_sum(Sgu, pair);
+      Su = row_pair_sum(Su, pair);
+      if (s.mass > p.eps) {
+        s.dphi = Sg / s.mass;
+        const float k2 = 2.f / s.mass;
+        s.dot_a = k2 * (Sgua - s.dphi * Sua);
+        s.dthr = -k2 * (Sgu - s.dphi * Su);
+      }
     }
   } else if constexpr (KIND == kSoftmax) {
-    float m = -INFINITY, E = 0.f, Sg = 0.f;
+    float m = -INFINITY, E = 0.f, Sg = 0.f, T1 = 0.f, T2 = 0.f, T3 = 0.f, T4 = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], g[16], l[16];
       tmem_ld16(ta_row + c, a);
@@ -240,22 +267,47 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
       if (cm > m) {
         const float r = __expf(m - cm);
         E *= r;
-        Sg *= r;
+        if (kWithGrad) {
+          Sg *= r;
+          T1 *= r;
+          T2 *= r;
+          T3 *= r;
+          T4 *= r;
+        }
         m = cm;
       }
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        if (c + e < p.P) {
+        const int i = c + e;
+        if (i < p.P) {
           const float w = __expf(l[e] - m);
           E += w;
-          if (kWithGrad) Sg += g[e] * w;
+          if (kWithGrad) {
+            const float gain = ctl_gain(p, h, i);
+            const float sc = a[e] * s.inv + ctl_bias(p, h, i);
+            const float gw = g[e] * w;
+            Sg += gw;
+            T1 += gain * gw * a[e];
+            T2 += gain * w * a[e];
+            T3 += gw * sc;
+            T4 += w * sc;
+          }
         }
       }
     }
     s.mx = row_pair_max(m, pair);
     const float r = __expf(m - s.mx);  // 0 for a part without columns (m = -inf)
     s.mass = row_pair_sum(E * r, pair);
-    if (kWithGrad) s.dphi = row_pair_sum(Sg * r, pair) / s.mass;
+    if (kWithGrad) {
+      const float inv_E = 1.f / s.mass;
+      s.dphi = row_pair_sum(Sg * r, pair) * inv_E;
+      T1 = row_pair_sum(T1 * r, pair);
+      T2 = row_pair_sum(T2 * r, pair);
+      T3 = row_pair_sum(T3 * r, pair);
+      T4 = row_pair_sum(T4 * r, pair);
+      s.dot_a = (T1 - s.dphi * T2) * inv_E;
+      s.dgain = (T3 - s.dphi * T4) * inv_E;
+    }
   }
   return s;
 }
@@ -847,34 +899,19 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
                    : "memory");
     }
   } else {
-    // Sweep 1: sum_j dpre_j a_j (RMSNorm backward) and the control gradients.
-    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-      float a[16], dp[16];
-      tmem_ld16(ta_row + c, a);
-      dpre_chunk(c, a, dp);
-  #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        dot_a += dp[e] * a[e];
-        if (KIND == kRelu2) dthr -= dp[e];
-        if (KIND == kSoftmax && c + e < p.P) {
-          const float gain = ctl_gain(p, h, c + e);
-          const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
-          if (p.gain_mode == 1) dgain_head += dp[e] * sc / gain;
-          if (p.gain_mode == 2 && valid) atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / gain);
-        }
-        if (spline && c + e < p.P) dscale += dp[e] * a[e] * st.inv / ctl_scale(p, h);
-        if (p.bias != nullptr && p.dbias != nullptr && valid && c + e < p.P)
-          atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
-      }
+    // The statistics pass formed dot_a = sum_j dpre_j a_j (RMSNorm backward)
+    // and the per-head control gradients as row totals (counted once per row).
+    dot_a = valid ? st.dot_a : 0.f;
+    if (valid && part == 0) {
+      dthr = st.dthr;
+      dgain_head = st.dgain;
     }
-    dot_a = row_pair_sum(dot_a, pair);
-    if (!valid) {
-      dot_a = 0.f;
-      dthr = dscale = dgain_head = 0.f;
-    }
-    // Sweep 2: (phi -> tile for dW2 unless stored) and dA = inv * dpre - a * inv^3 * dot_a / P.
+    // One sweep: (phi -> tile for dW2 unless stored), dA = inv * dpre - a *
+    // inv^3 * dot_a / P, and the per-feature control gradients.
     if (decode && !phi_stored) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
+    const bool dbias = p.bias != nullptr && p.dbias != nullptr && valid;
+    const bool dgain_feat = KIND == kSoftmax && p.gain_mode == 2 && valid;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], dp[16], da[16];
       tmem_ld16(ta_row + c, a);
@@ -883,6 +920,15 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       for (int e = 0; e < 16; ++e) da[e] = valid ? st.inv * dp[e] - a[e] * inv3 * dot_a : 0.f;
       tile_st16(tl.da, row, c / 8, pack8(da));
       tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
+      if (dbias || dgain_feat) {
+        for (int e = 0; e < 16 && c + e < p.P; ++e) {
+          if (dbias) atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
+          if (dgain_feat) {
+            const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
+            atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / ctl_gain(p, h, c + e));
+          }
+        }
+      }
     }
   }
   {
