@@ -218,7 +218,11 @@ class PhaseTimer:
         all_tiles = bool(g.dfinal_state or g.dinit_state or a.init_state or g.stage != 0)
         state = 1 if (g.stage != 2 and (nt > 1 or all_tiles)) else 0
         prefix = 2 if two_level else 1
-        return state + prefix + (0 if g.stage == 1 else 3)
+        # dq and dk in one kernel where v, k, q, ds and the dout tiles fit
+        # (scan_bwd.cu dqk2_fits), else two
+        dvp, dkp = -(-a.dv // 16) * 16, -(-a.dk // 16) * 16
+        merged = dvp <= 128 and 2 * dkp <= 512 and 128 * (dvp + 2 * dkp + 128 + a.n_retentions * dvp) * 2 <= 228352
+        return state + prefix + (0 if g.stage == 1 else (2 if merged else 3))
 
     def __init__(self, lib):
         self.lib = lib

@@ -739,6 +739,117 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dqk_kernel(ScanParams p, Sc
   if (warp == 0) tmem_dealloc(tmem_base, 512);
 }
 
+// dq and dk of a tile in one CTA (when the tiles fit, see dqk2_fits): ds is
+// formed once and feeds both products, v and the dout tiles are loaded once.
+// Shared memory: v, k, q, ds and every retention's dout tile.  Tensor
+// memory: g_r in columns [0, 128) while ds forms, then dq in [0, DkP) and dk
+// in [DkP, 2 DkP).  After the two ds products the k and q regions hold the
+// state images (S_in,r for dq in the k region, G_r for dk in the q region),
+// loaded one retention ahead, and the ds region holds u_r o v.
+//   dq = ds . k    + sum_r (c_r o dout_r) S_in,r^T   (tiles n >= 1 carry a state)
+//   dk = ds^T . q  + sum_r (u_r o v) G_r^T           (tiles n <= NT-2 feed one)
+__global__ void __launch_bounds__(kThreads) scan_bwd_dqk2_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float decay[4 * kTile];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int row = my_row(), part = my_part();
+  const int warp = threadIdx.x >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tv{base, kTile, p.DvP};
+  Tile tk{tv.saddr + kTile * p.DvP * 2, kTile, p.DkP};
+  Tile tq{tk.saddr + kTile * p.DkP * 2, kTile, p.DkP};
+  Tile tds{tq.saddr + kTile * p.DkP * 2, kTile, kTile};
+  Tile td[4];
+  for (int i = 0; i < 4; ++i) td[i] = Tile{tds.saddr + kTile * kTile * 2 + i * kTile * p.DvP * 2, kTile, p.DvP};
+  const Tile img_s{tk.saddr, p.DvP, p.DkP};   // S_in images (dq), after ds . k
+  const Tile img_g{tq.saddr, p.DvP, p.DkP};   // G images (dk), after ds^T . q
+  const Tile tuv{tds.saddr, kTile, p.DvP};     // u_r o v, after the ds products
+  const bool cross_q = n > 0 || p.init != nullptr;
+  const bool cross_k = n + 1 < p.NT || g.dfinal != nullptr;
+  auto image_of = [&](const __nv_bfloat16* images, int r) {
+    return reinterpret_cast<const uint8_t*>(images) + state_index(p, b, h, n, r) * static_cast<size_t>(image_bytes(p));
+  };
+  fill_decay(p, h, decay);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  load_payload(p, tv, p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2], rows);
+  load_tile(tk, p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2], p.ks[2], rows, p.Dk);
+  load_tile(tq, p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2], p.qs[2], rows, p.Dk);
+  for (int r = 0; r < p.RU; ++r) load_tile(td[r], dout_rows(p, g, r, b, h, t0), p.Dv, rows, p.Dv);
+  tiles_ready();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_g = ctx.tmem, t_dq = ctx.tmem, t_dk = ctx.tmem + p.DkP;
+
+  accumulate_ds(p, g, ctx, td, true, tv, t_g, tds, b, h, t0, rows, decay);
+  ctx.run([&] {
+    gemm_issue(t_dq, kmajor(tds), mnmajor(tk), p.DkP, kTile, false);
+    gemm_issue(t_dk, mnmajor(tds), mnmajor(tq), p.DkP, kTile, false);
+  });
+  // k, q and ds are consumed: the first images go in (one group each).
+  if (cross_q) load_image(img_s, image_of(p.images, 0), image_bytes(p));
+  cp_async_commit();
+  if (cross_k) load_image(img_g, image_of(g.gimages, 0), image_bytes(p));
+  cp_async_commit();
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    const int kind = p.kind[r];
+    if (cross_q) {
+      // rows of c o dout: c(i) = e^{la (i+1)} (decayed), 1 (stale), 1 - e^{la (i+1)}
+      // (auxiliary, on its stale partner's tile, which the partner left unscaled)
+      const Tile& ta = td[kind == kSlotAux ? p.partner[r] : r];
+      const float x = la * static_cast<float>(row + 1);
+      const float c = kind == kSlotAux ? one_minus_exp(x) : (decayed && kind != kSlotStale) ? __expf(x) : 1.f;
+      if (c != 1.f || kind == kSlotAux) {
+        for (int j = part; j < p.DvP / 8; j += kParts) {
+          float f[8];
+          unpack8(tile_ld16(ta, row, j), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= c;
+          tile_st16(ta, row, j, pack8(f));
+        }
+      }
+      // pending groups: this S_in image and the G image after it
+      ctx.run_keep_newest([&] { gemm_issue(t_dq, kmajor(ta), mnmajor(img_s), p.DkP, p.DvP, true); });
+      if (r + 1 < p.R) load_image(img_s, image_of(p.images, r + 1), image_bytes(p));
+    }
+    cp_async_commit();
+    if (cross_k) {
+      // rows of u_r o v
+      const float u = slot_key_weight(p, r, la, rows, row);
+      for (int j = part; j < p.DvP / 8; j += kParts) {
+        float f[8];
+        unpack8(tile_ld16(tv, row, j), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= u;
+        tile_st16(tuv, row, j, pack8(f));
+      }
+      // pending groups: this G image and the next S_in image
+      ctx.run_keep_newest([&] { gemm_issue(t_dk, kmajor(tuv), mnmajor(img_g), p.DkP, p.DvP, true); });
+      if (r + 1 < p.R) load_image(img_g, image_of(g.gimages, r + 1), image_bytes(p));
+    }
+    cp_async_commit();
+  }
+  cp_async_wait_all();
+  const size_t row0 = ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.Dk;
+  float* stage = reinterpret_cast<float*>(smem + (tds.saddr - base));
+  __syncthreads();
+  store_rows(t_dq, 0, p.DkP, p.Dk, rows, grad_ptr(g.dq, g.grad_bf16, row0), p.Dk, g.grad_bf16 != 0, stage,
+             Identity{});
+  store_rows(t_dk, 0, p.DkP, p.Dk, rows, grad_ptr(g.dk, g.grad_bf16, row0), p.Dk, g.grad_bf16 != 0, stage,
+             Identity{});
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, 512);
+}
+
 // ------------------------------------------------------------------ dv
 
 // dv = sum_r [ P_r^T dout_r + (u_r o k) G_r ], accumulated in one TMEM region,
@@ -910,6 +1021,14 @@ static size_t dqk_smem(const ScanParams& p, int nbuf) {
 // the kernels' static shared memory.
 constexpr size_t kDynSmemBudget = 232448 - 4096;
 static int dqk_buffers(const ScanParams& p) { return dqk_smem(p, p.RU) <= kDynSmemBudget ? p.RU : 1; }
+// The merged dq/dk kernel: v, k, q, ds and every dout tile, and the state
+// images in the k and q regions (payloads up to a tile wide).
+static size_t dqk2_smem(const ScanParams& p) {
+  return static_cast<size_t>(kTile) * (p.DvP + 2 * p.DkP + kTile + p.RU * p.DvP) * 2;
+}
+static bool dqk2_fits(const ScanParams& p) {
+  return p.DvP <= kTile && 2 * p.DkP <= 512 && dqk2_smem(p) <= kDynSmemBudget;
+}
 static size_t dv_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + 2 * p.DvP) * 2 +
          (p.DvP > kTile ? static_cast<size_t>(p.DvP) * p.DkP * 2 : 0);
@@ -949,10 +1068,17 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
   }
   if (!grads) return 0;
   const dim3 grid(p.NT, p.H, p.B);
-  scan_bwd_dqk_kernel<true><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
-  if (int e = check_launch("scan_bwd_dq_kernel")) return e;
-  scan_bwd_dqk_kernel<false><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
-  if (int e = check_launch("scan_bwd_dk_kernel")) return e;
+  if (dqk2_fits(p)) {
+    const size_t s_dqk2 = dqk2_smem(p);
+    cudaFuncSetAttribute(scan_bwd_dqk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk2));
+    scan_bwd_dqk2_kernel<<<grid, kThreads, s_dqk2, s>>>(p, g);
+    if (int e = check_launch("scan_bwd_dqk2_kernel")) return e;
+  } else {
+    scan_bwd_dqk_kernel<true><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
+    if (int e = check_launch("scan_bwd_dq_kernel")) return e;
+    scan_bwd_dqk_kernel<false><<<grid, kThreads, s_dqk, s>>>(p, g, nbuf);
+    if (int e = check_launch("scan_bwd_dk_kernel")) return e;
+  }
   scan_bwd_dv_kernel<<<grid, kThreads, s_dv, s>>>(p, g);
   return check_launch("scan_bwd_dv_kernel");
 }
