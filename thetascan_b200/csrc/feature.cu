@@ -205,11 +205,21 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   const int part = my_part();
   RowState s{0.f, 0.f, -INFINITY, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
-  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
-    float a[16];
-    tmem_ld16(ta_row + c, a);
+  if (p.PP == 4 * kChunkStep) {
+    // the common width (256 features): all four chunks behind one wait
+    float a4[4][16];
+    tmem_ld16x4(ta_row + 16 * part, kChunkStep, a4);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) ss += a[e] * a[e];
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ss += a4[k][e] * a4[k][e];
+  } else {
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ss += a[e] * a[e];
+    }
   }
   ss = row_pair_sum(ss, pair);
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
