@@ -76,36 +76,69 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 }  // namespace
 
+// Columns [c, c + V) of a row as floats (V = 2: one 8-byte load).
+template <int V>
+__device__ __forceinline__ void ld_cols(const float* __restrict__ src, float (&x)[V]) {
+  if constexpr (V == 2) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(src));
+    x[0] = v.x;
+    x[1] = v.y;
+  } else {
+    x[0] = __ldg(src);
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void st_bf16_cols(__nv_bfloat16* dst, const float (&x)[V]) {
+  if constexpr (V == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(x[0], x[1]);
+  } else {
+    dst[0] = __float2bfloat16_rn(x[0]);
+  }
+}
+
+// The slot count N = 1 + J is a template parameter so that the per-slot
+// arrays stay in registers; each lane takes V adjacent value columns at a
+// time (V = 2 when the row widths allow 8-byte loads).
+template <int N, int V>
 __global__ void __launch_bounds__(kReadWarps * 32) kread_fwd_kernel(ReadParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   float coef[5];
   slot_coefs(p, h, coef);
-  const int n = 1 + p.J;
+  const int width = p.d + p.mass_cols;
   const size_t bh = static_cast<size_t>(b) * p.H + h;
 #pragma unroll 4
   for (int i = 0; i < kRowsPerWarp; ++i) {
     const int t = blockIdx.x * kReadRows + warp * kRowsPerWarp + i;
     if (t >= p.T) break;
     const size_t row = bh * p.T + t;  // [B, H, T] row index
-    float scale[5];
-    for (int s = 0; s < n; ++s) scale[s] = p.mass_cols ? coef[s] / (slot_val(p, s, row, p.d) + p.eps) : coef[s];
+    float scale[N];
+#pragma unroll
+    for (int s = 0; s < N; ++s)
+      scale[s] = p.mass_cols ? coef[s] / (__ldg(p.out[s] + row * width + p.d) + p.eps) : coef[s];
     __nv_bfloat16* yrow = p.y + ((static_cast<size_t>(b) * p.T + t) * p.H + h) * p.d;
-    for (int c = lane; c < p.d; c += 32) {
-      float acc = __ldg(p.y0 + row * p.d + c);
-      for (int s = 0; s < n; ++s) acc += scale[s] * slot_val(p, s, row, c);
-      yrow[c] = __float2bfloat16_rn(acc);
+    for (int c = V * lane; c < p.d; c += 32 * V) {
+      float acc[V], x[V];
+      ld_cols<V>(p.y0 + row * p.d + c, acc);
+#pragma unroll
+      for (int s = 0; s < N; ++s) {
+        ld_cols<V>(p.out[s] + row * width + c, x);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] += scale[s] * x[e];
+      }
+      st_bf16_cols<V>(yrow + c, acc);
     }
   }
 }
 
+template <int N, int V>
 __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p) {
   __shared__ float red[kReadWarps][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   float coef[5];
   slot_coefs(p, h, coef);
-  const int n = 1 + p.J;
   const int width = p.d + p.mass_cols;
   const size_t bh = static_cast<size_t>(b) * p.H + h;
   float deta[4] = {0.f, 0.f, 0.f, 0.f};  // this warp's rows (every lane holds the sums)
@@ -115,45 +148,68 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p
     if (t >= p.T) break;
     const size_t row = bh * p.T + t;
     const size_t yidx = ((static_cast<size_t>(b) * p.T + t) * p.H + h) * p.d;
-    auto dy_at = [&](int c) {
-      return p.dy_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.dy)[yidx + c])
-                       : reinterpret_cast<const float*>(p.dy)[yidx + c];
-    };
-    float dymem[5];
-    for (int s = 0; s < n; ++s) {
-      if (p.mass_cols == 0) {
-        // unnormalized read: mem_s = N_s
-        float dot = 0.f;
-        for (int c = lane; c < p.d; c += 32) {
-          const float dyc = dy_at(c);
-          p.dout[s][row * width + c] = __float2bfloat16_rn(coef[s] * dyc);
-          dot += dyc * slot_val(p, s, row, c);
+    auto dy_at = [&](int c, float (&x)[V]) {
+      if (p.dy_bf16) {
+        const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(p.dy) + yidx + c;
+        if constexpr (V == 2) {
+          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(d));
+          x[0] = v.x;
+          x[1] = v.y;
+        } else {
+          x[0] = __bfloat162float(d[0]);
         }
-        dymem[s] = warp_sum(dot);
-        continue;
+      } else {
+        ld_cols<V>(reinterpret_cast<const float*>(p.dy) + yidx + c, x);
       }
-      const float inv = 1.f / (slot_val(p, s, row, p.d) + p.eps);
-      float exact = 0.f, consistent = 0.f;
-      for (int c = lane; c < p.d; c += 32) {
-        const float dyc = dy_at(c);
-        const float mem = slot_val(p, s, row, c) * inv;
-        const __nv_bfloat16 dn = __float2bfloat16_rn(coef[s] * dyc * inv);
-        p.dout[s][row * width + c] = dn;
-        exact += dyc * mem;
-        consistent += __bfloat162float(dn) * mem;
+    };
+    float inv[N], exact[N], consistent[N];
+#pragma unroll
+    for (int s = 0; s < N; ++s) {
+      inv[s] = p.mass_cols ? 1.f / (__ldg(p.out[s] + row * width + p.d) + p.eps) : 1.f;
+      exact[s] = consistent[s] = 0.f;
+    }
+    for (int c = V * lane; c < p.d; c += 32 * V) {
+      float dyc[V];
+      dy_at(c, dyc);
+      if (p.dy0 != nullptr) {
+        if constexpr (V == 2) {
+          *reinterpret_cast<float2*>(p.dy0 + row * p.d + c) = make_float2(dyc[0], dyc[1]);
+        } else {
+          p.dy0[row * p.d + c] = dyc[0];
+        }
       }
-      dymem[s] = warp_sum(exact);           // dy . mem_s
-      const float dD = -warp_sum(consistent);
-      if (lane == 0) {
-        const __nv_bfloat16 hi = __float2bfloat16_rn(dD);
-        p.dout[s][row * width + p.d] = hi;
-        if (p.mass_cols == 2) p.dout[s][row * width + p.d + 1] = __float2bfloat16_rn(dD - __bfloat162float(hi));
+#pragma unroll
+      for (int s = 0; s < N; ++s) {
+        float x[V], dn[V];
+        ld_cols<V>(p.out[s] + row * width + c, x);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          // mass_cols == 0 (unnormalized read): mem_s = N_s and dN_s = c_s dy
+          const float mem = x[e] * inv[s];
+          dn[e] = p.mass_cols ? coef[s] * dyc[e] * inv[s] : coef[s] * dyc[e];
+          exact[s] += dyc[e] * mem;
+          // dN is rounded first; the mass gradient uses the rounded values
+          consistent[s] += __bfloat162float(__float2bfloat16_rn(dn[e])) * mem;
+        }
+        st_bf16_cols<V>(p.dout[s] + row * width + c, dn);
       }
     }
-    if (p.dy0 != nullptr)
-      for (int c = lane; c < p.d; c += 32) p.dy0[row * p.d + c] = dy_at(c);
+    float dymem[N];
+#pragma unroll
+    for (int s = 0; s < N; ++s) {
+      dymem[s] = warp_sum(exact[s]);  // dy . mem_s
+      if (p.mass_cols) {
+        const float dD = -warp_sum(consistent[s]);
+        if (lane == 0) {
+          const __nv_bfloat16 hi = __float2bfloat16_rn(dD);
+          p.dout[s][row * width + p.d] = hi;
+          if (p.mass_cols == 2) p.dout[s][row * width + p.d + 1] = __float2bfloat16_rn(dD - __bfloat162float(hi));
+        }
+      }
+    }
     // fast: d eta_j = dy.mem(1+j) - dy.mem(0); stale: d eta_j = -dy.mem(1+j)
-    for (int j = 0; j < p.J; ++j) deta[j] += (p.mode == 1) ? dymem[1 + j] - dymem[0] : -dymem[1 + j];
+#pragma unroll
+    for (int j = 0; j < N - 1; ++j) deta[j] += (p.mode == 1) ? dymem[1 + j] - dymem[0] : -dymem[1 + j];
   }
   if (p.deta == nullptr || p.J == 0) return;  // uniform across the block
   if (lane == 0)
@@ -166,14 +222,33 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p
   }
 }
 
-int launch_kread_fwd(const ReadParams& p, cudaStream_t s) {
-  kread_fwd_kernel<<<dim3(ceil_div(p.T, kReadRows), p.H, p.B), kReadWarps * 32, 0, s>>>(p);
+template <int N>
+static int launch_kread_n(const ReadParams& p, cudaStream_t s, bool backward) {
+  const dim3 grid(ceil_div(p.T, kReadRows), p.H, p.B);
+  // 8-byte column pairs where every row start stays 8-byte aligned
+  const bool pairs = (p.d % 2) == 0 && ((p.d + p.mass_cols) % 2) == 0;
+  if (backward) {
+    if (pairs) kread_bwd_kernel<N, 2><<<grid, kReadWarps * 32, 0, s>>>(p);
+    else kread_bwd_kernel<N, 1><<<grid, kReadWarps * 32, 0, s>>>(p);
+    return check_launch("kread_bwd_kernel");
+  }
+  if (pairs) kread_fwd_kernel<N, 2><<<grid, kReadWarps * 32, 0, s>>>(p);
+  else kread_fwd_kernel<N, 1><<<grid, kReadWarps * 32, 0, s>>>(p);
   return check_launch("kread_fwd_kernel");
 }
 
-int launch_kread_bwd(const ReadParams& p, cudaStream_t s) {
-  kread_bwd_kernel<<<dim3(ceil_div(p.T, kReadRows), p.H, p.B), kReadWarps * 32, 0, s>>>(p);
-  return check_launch("kread_bwd_kernel");
+static int launch_kread(const ReadParams& p, cudaStream_t s, bool backward) {
+  switch (1 + p.J) {
+    case 1: return launch_kread_n<1>(p, s, backward);
+    case 2: return launch_kread_n<2>(p, s, backward);
+    case 3: return launch_kread_n<3>(p, s, backward);
+    case 4: return launch_kread_n<4>(p, s, backward);
+    default: return launch_kread_n<5>(p, s, backward);
+  }
 }
+
+int launch_kread_fwd(const ReadParams& p, cudaStream_t s) { return launch_kread(p, s, false); }
+
+int launch_kread_bwd(const ReadParams& p, cudaStream_t s) { return launch_kread(p, s, true); }
 
 }  // namespace ts
