@@ -418,7 +418,9 @@ __device__ __forceinline__ void store_tile(const Tile& t, __nv_bfloat16* __restr
     } else {
       float f[8];
       unpack8(v, f);
-      for (int e = 0; e < 8 && c0 + e < cols_valid; ++e) dst[r * ld + c0 + e] = __float2bfloat16_rn(f[e]);
+      #pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (c0 + e < cols_valid) dst[r * ld + c0 + e] = __float2bfloat16_rn(f[e]);
     }
   }
 }
@@ -485,7 +487,9 @@ __device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, 
           if (whole && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
             *reinterpret_cast<uint4*>(d) = pack8(x);
           } else {
-            for (int q = 0; q < 8 && e0 + q < cols; ++q) d[q] = __float2bfloat16_rn(x[q]);
+            #pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (e0 + q < cols) d[q] = __float2bfloat16_rn(x[q]);
           }
         } else {
           float* d = reinterpret_cast<float*>(dst) + off;
@@ -493,7 +497,9 @@ __device__ __forceinline__ void store_rows(uint32_t tbase, int tcol, int ncols, 
             reinterpret_cast<float4*>(d)[0] = make_float4(x[0], x[1], x[2], x[3]);
             reinterpret_cast<float4*>(d)[1] = make_float4(x[4], x[5], x[6], x[7]);
           } else {
-            for (int q = 0; q < 8 && e0 + q < cols; ++q) d[q] = x[q];
+            #pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (e0 + q < cols) d[q] = x[q];
           }
         }
       }

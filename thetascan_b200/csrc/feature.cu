@@ -542,11 +542,15 @@ __device__ void store_row_grads(const FeatParams& p, uint32_t t_dx, int sel, int
         *reinterpret_cast<uint4*>(dst + c) = pack8(g[k]);
         *reinterpret_cast<uint4*>(dst + c + 8) = pack8(g[k] + 8);
       } else {
-        for (int e = 0; e < 16 && c + e < p.d; ++e) dst[c + e] = __float2bfloat16_rn(g[k][e]);
+        #pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (c + e < p.d) dst[c + e] = __float2bfloat16_rn(g[k][e]);
       }
     } else {
       float* dst = p.dx[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + tok) * p.d;
-      for (int e = 0; e < 16 && c + e < p.d; ++e) dst[c + e] = g[k][e];
+      #pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c + e < p.d) dst[c + e] = g[k][e];
     }
   }
 }
@@ -617,7 +621,9 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
       tile_st16(tphi, row, c / 8, pack8(f));
       tile_st16(tphi, row, c / 8 + 1, pack8(f + 8));
       if (row32 != nullptr && !zero_row) {
-        for (int e = 0; e < 16 && c + e < p.m; ++e) row32[c + e] = f[e];
+        #pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (c + e < p.m) row32[c + e] = f[e];
       }
     }
   }
@@ -931,7 +937,9 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       tile_st16(tl.da, row, c / 8, pack8(da));
       tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
       if (dbias || dgain_feat) {
-        for (int e = 0; e < 16 && c + e < p.P; ++e) {
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          if (c + e >= p.P) break;
           if (dbias) atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
           if (dgain_feat) {
             const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
@@ -971,11 +979,15 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       tmem_ld16(tmem_addr(t_a + mb * p.dP, quad * 32, c), v);
       if (prj < p.P && p.dW1) {
         float* wrow = p.dW1 + (static_cast<size_t>(h) * p.P + prj) * p.d;
-        for (int e = 0; e < 16 && c + e < p.d; e += 4) {
+        #pragma unroll
+        for (int e = 0; e < 16; e += 4) {
+          if (c + e >= p.d) break;
           if (c + e + 4 <= p.d && (p.d & 3) == 0) {
             atomicAdd(reinterpret_cast<float4*>(wrow + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
           } else {
-            for (int q = 0; q < 4 && c + e + q < p.d; ++q) atomicAdd(wrow + c + e + q, v[e + q]);
+            #pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (c + e + q < p.d) atomicAdd(wrow + c + e + q, v[e + q]);
           }
         }
       }
@@ -991,13 +1003,19 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
           if (p.dW2_t && (p.d & 3) == 0) {
             // [H, m, d]: this row's d values are contiguous
             float* wrow = p.dW2 + (static_cast<size_t>(h) * p.m + fi) * p.d;
-            for (int e = 0; e < 16 && c + e < p.d; e += 4)
+            #pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              if (c + e < p.d)
               atomicAdd(reinterpret_cast<float4*>(wrow + c + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
           } else if (p.dW2_t) {
-            for (int e = 0; e < 16 && c + e < p.d; ++e)
+            #pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < p.d)
               atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.m + fi) * p.d + c + e, v[e]);
           } else {
-            for (int e = 0; e < 16 && c + e < p.d; ++e)
+            #pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < p.d)
               atomicAdd(p.dW2 + (static_cast<size_t>(h) * p.d + c + e) * p.m + fi, v[e]);
           }
         }
