@@ -304,9 +304,9 @@ def bytes_per_token(cfg):
 # timed config by its number of token rows (traffic grows with B * T).
 MEASURED_TRAFFIC = {
     # entry point: (bytes per launch at the profiled size, tokens of that launch, source)
-    "ts_b200_feature_bwd": (258.8e6 + 34.4e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
-    "ts_b200_scan_bwd": (1254.9e6 + 521.1e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
-    "ts_b200_scan_fwd": (476.3e6 + 351.2e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_feature_bwd": (258.1e6 + 29.9e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_scan_bwd": (1330.6e6 + 363.6e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
+    "ts_b200_scan_fwd": (476.2e6 + 344.9e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
 }
 
 
