@@ -70,11 +70,27 @@ struct FeatParams {
   long long dxs[2][3];
 };
 
+// Kernels are instantiated per feature kind KF & kKindMask; with kPlainBit
+// set the map has no score bias, no relu2 threshold, one fixed softmax gain
+// and no column tail (P == PP), so the per-element controls and bounds
+// checks compile away.
+constexpr int kKindMask = 7;
+constexpr int kPlainBit = 8;
+
+template <bool kPlain = false>
 __device__ __forceinline__ float ctl_bias(const FeatParams& p, int h, int i) {
+  if constexpr (kPlain) return 0.f;
   return p.bias ? __ldg(p.bias + h * p.m + i) : 0.f;
 }
+template <bool kPlain = false>
 __device__ __forceinline__ float ctl_gain(const FeatParams& p, int h, int i) {
+  if constexpr (kPlain) return p.gain_scalar;
   return p.gain_mode == 0 ? p.gain_scalar : p.gain_mode == 1 ? __ldg(p.gain + h) : __ldg(p.gain + h * p.m + i);
+}
+template <bool kPlain = false>
+__device__ __forceinline__ float ctl_thr(const FeatParams& p, int h) {
+  if constexpr (kPlain) return 0.f;
+  return p.thr ? __ldg(p.thr + h) : 0.f;
 }
 __device__ __forceinline__ float ctl_scale(const FeatParams& p, int h) {
   return p.scale ? __ldg(p.scale + h) : p.scale_scalar;
@@ -200,8 +216,10 @@ struct NoGrad {
 //           dot_a = (sum gain e g a - dphi sum gain e a) / E,
 //           dgain = (sum e g sc - dphi sum e sc) / E
 // (the softmax sums rescaled with E when the running max grows).
-template <int KIND, bool kWithGrad, class Grad>
+template <int KF, bool kWithGrad, class Grad>
 __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
+  constexpr int KIND = KF & kKindMask;
+  constexpr bool kPlain = (KF & kPlainBit) != 0;
   const int part = my_part();
   RowState s{0.f, 0.f, -INFINITY, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
@@ -224,7 +242,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   ss = row_pair_sum(ss, pair);
   s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
   if constexpr (KIND == kRelu2) {
-    const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+    const float thr = ctl_thr<kPlain>(p, h);
     float M = 0.f, Sg = 0.f, Sgua = 0.f, Sua = 0.f, Sgu = 0.f, Su = 0.f;
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], g[16];
@@ -233,8 +251,8 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        if (i < p.P) {
-          const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i) - thr, 0.f);
+        if (kPlain || i < p.P) {
+          const float u = fmaxf(a[e] * s.inv + ctl_bias<kPlain>(p, h, i) - thr, 0.f);
           M += u * u;
           if (kWithGrad) {
             const float gu = g[e] * u;
@@ -271,7 +289,7 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        l[e] = i < p.P ? ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) : -INFINITY;
+        l[e] = (kPlain || i < p.P) ? ctl_gain<kPlain>(p, h, i) * (a[e] * s.inv + ctl_bias<kPlain>(p, h, i)) : -INFINITY;
         cm = fmaxf(cm, l[e]);
       }
       if (cm > m) {
@@ -289,12 +307,12 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
-        if (i < p.P) {
+        if (kPlain || i < p.P) {
           const float w = __expf(l[e] - m);
           E += w;
           if (kWithGrad) {
-            const float gain = ctl_gain(p, h, i);
-            const float sc = a[e] * s.inv + ctl_bias(p, h, i);
+            const float gain = ctl_gain<kPlain>(p, h, i);
+            const float sc = a[e] * s.inv + ctl_bias<kPlain>(p, h, i);
             const float gw = g[e] * w;
             Sg += gw;
             T1 += gain * gw * a[e];
@@ -323,25 +341,28 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
 }
 
 // phi values for columns [c, c+16) of the (relu2 / softmax) feature row.
-template <int KIND>
+template <int KF>
 __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s, const float* a, int c, int h,
                                           float* out) {
+  constexpr int KIND = KF & kKindMask;
+  constexpr bool kPlain = (KF & kPlainBit) != 0;
+  (void)kPlain;
   if constexpr (KIND == kRelu2) {
-    const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+    const float thr = ctl_thr<kPlain>(p, h);
     const bool live = s.mass > p.eps;
     const float inv_mass = 1.f / fmaxf(s.mass, p.eps);
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int i = c + e;
-      const float u = fmaxf(a[e] * s.inv + ctl_bias(p, h, i < p.P ? i : 0) - thr, 0.f);
-      out[e] = i < p.P ? (live ? u * u * inv_mass : 1.f / static_cast<float>(p.m)) : 0.f;
+      const float u = fmaxf(a[e] * s.inv + ctl_bias<kPlain>(p, h, (kPlain || i < p.P) ? i : 0) - thr, 0.f);
+      out[e] = (kPlain || i < p.P) ? (live ? u * u * inv_mass : 1.f / static_cast<float>(p.m)) : 0.f;
     }
   } else {
     const float inv_E = 1.f / s.mass;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int i = c + e;
-      out[e] = i < p.P ? __expf(ctl_gain(p, h, i) * (a[e] * s.inv + ctl_bias(p, h, i)) - s.mx) * inv_E : 0.f;
+      out[e] = (kPlain || i < p.P) ? __expf(ctl_gain<kPlain>(p, h, i) * (a[e] * s.inv + ctl_bias<kPlain>(p, h, i)) - s.mx) * inv_E : 0.f;
     }
   }
 }
@@ -564,9 +585,12 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
 }
 
 // phi of this thread's row and column chunks into the phi tile (bf16).
-template <int KIND>
+template <int KF>
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
                                                 const Tile& tphi, bool zero_row, float* row32 = nullptr) {
+  constexpr int KIND = KF & kKindMask;
+  constexpr bool kPlain = (KF & kPlainBit) != 0;
+  (void)kPlain;
   const int row = my_row(), part = my_part();
   if constexpr (KIND == kBspline) {
     const float sc = ctl_scale(p, h);
@@ -613,7 +637,7 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], f[16];
       tmem_ld16(ta_row + c, a);
-      phi_chunk<KIND>(p, st, a, c, h, f);
+      phi_chunk<KF>(p, st, a, c, h, f);
       if (zero_row) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) f[e] = 0.f;
@@ -640,7 +664,7 @@ __device__ __forceinline__ void feature_tile_coords(const FeatParams& p, int i, 
   b = rest / p.nsel;
 }
 
-template <int KIND>
+template <int KF>
 __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
@@ -701,12 +725,12 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
     if (p.rot > 0 || p.l2norm) prepare_rows(p, tl.x, t0, rows, row_norm, pair);
     ctx.run_keep_newest([&] { gemm_issue(t_a, kmajor(tl.x), kmajor(tl.w1), p.PP, p.dP, false); });
 
-    const RowState st = row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{});
+    const RowState st = row_stats<KF, false>(p, ta_row, h, pair, NoGrad{});
     // Rows past the sequence end get zero features, so the decode below and
     // the stored tile are exact zeros there.
     float* row32 = (sel == 1 && p.phi_q32 != nullptr && row < rows)
                       ? p.phi_q32 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + row) * p.m : nullptr;
-    phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, row >= rows, row32);
+    phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, row >= rows, row32);
     __syncthreads();
     __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
     store_tile(tl.phi, out, p.m, rows, p.m);
@@ -731,8 +755,10 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
 
 // ------------------------------------------------------------------ backward
 
-template <int KIND>
+template <int KF>
 __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) {
+  constexpr int KIND = KF & kKindMask;
+  constexpr bool kPlain = (KF & kPlainBit) != 0;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
@@ -815,23 +841,23 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
   };
 
-  const RowState st = spline ? row_stats<KIND, false>(p, ta_row, h, pair, NoGrad{})
-                             : row_stats<KIND, true>(p, ta_row, h, pair, grad16);
+  const RowState st = spline ? row_stats<KF, false>(p, ta_row, h, pair, NoGrad{})
+                             : row_stats<KF, true>(p, ta_row, h, pair, grad16);
   const float dot_phi = st.dphi;  // sum_j g_j phi_j (relu2 / softmax Jacobians)
   // dpre for columns [c, c+16) (projection index for B-splines).
   auto dpre_chunk = [&](int c, const float* a, float* dp) {
     if constexpr (KIND == kRelu2) {
       float g[16];
       grad16(c, g);
-      const float thr = p.thr ? __ldg(p.thr + h) : 0.f;
+      const float thr = ctl_thr<kPlain>(p, h);
       const bool live = st.mass > p.eps;
       const float inv_mass = 1.f / fmaxf(st.mass, p.eps);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
         float d = 0.f;
-        if (i < p.P && live) {
-          const float u = fmaxf(a[e] * st.inv + ctl_bias(p, h, i) - thr, 0.f);
+        if ((kPlain || i < p.P) && live) {
+          const float u = fmaxf(a[e] * st.inv + ctl_bias<kPlain>(p, h, i) - thr, 0.f);
           d = (g[e] - dot_phi) * inv_mass * 2.f * u;
         }
         dp[e] = d;
@@ -844,9 +870,9 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       for (int e = 0; e < 16; ++e) {
         const int i = c + e;
         float d = 0.f;
-        if (i < p.P) {
-          const float gain = ctl_gain(p, h, i);
-          const float sc = a[e] * st.inv + ctl_bias(p, h, i);
+        if (kPlain || i < p.P) {
+          const float gain = ctl_gain<kPlain>(p, h, i);
+          const float sc = a[e] * st.inv + ctl_bias<kPlain>(p, h, i);
           const float ph = __expf(gain * sc - st.mx) * inv_E;
           d = gain * ph * (g[e] - dot_phi);
         }
@@ -902,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
     dot_a = row_pair_sum(dot_a, pair);
     if (!valid) dot_a = dscale = 0.f;
-    if (decode && !phi_stored) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
 #pragma unroll
     for (int i = 0; i < kMaxSplineOwn; ++i) {
@@ -924,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
     // One sweep: (phi -> tile for dW2 unless stored), dA = inv * dpre - a *
     // inv^3 * dot_a / P, and the per-feature control gradients.
-    if (decode && !phi_stored) phi_row_to_tile<KIND>(p, st, ta_row, h, tl.phi, !valid);
+    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
     const bool dbias = p.bias != nullptr && p.dbias != nullptr && valid;
     const bool dgain_feat = KIND == kSoftmax && p.gain_mode == 2 && valid;
@@ -942,8 +968,8 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
           if (c + e >= p.P) break;
           if (dbias) atomicAdd(p.dbias + h * p.m + c + e, dp[e]);
           if (dgain_feat) {
-            const float sc = a[e] * st.inv + ctl_bias(p, h, c + e);
-            atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / ctl_gain(p, h, c + e));
+            const float sc = a[e] * st.inv + ctl_bias<kPlain>(p, h, c + e);
+            atomicAdd(p.dgain + h * p.m + c + e, dp[e] * sc / ctl_gain<kPlain>(p, h, c + e));
           }
         }
       }
@@ -1053,37 +1079,47 @@ size_t feature_bwd_smem(const FeatParams& p) {
 
 // One instantiation per feature kind: the kind decides the per-element code
 // of every sweep, and specialising keeps each kind's locals in registers.
-template <int KIND>
+template <int KF>
 static int launch_feature_fwd_kind(const FeatParams& p, cudaStream_t s) {
   const size_t sm = feature_fwd_smem(p);
-  cudaFuncSetAttribute(feature_fwd_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  cudaFuncSetAttribute(feature_fwd_kernel<KF>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   const int NT = ceil_div(p.T, kTile);
   const int G = persistent_ctas_per_head(p, p.B * p.nsel * NT);
-  feature_fwd_kernel<KIND><<<dim3(G, p.H), kThreads, sm, s>>>(p);
+  feature_fwd_kernel<KF><<<dim3(G, p.H), kThreads, sm, s>>>(p);
   return check_launch("feature_fwd_kernel");
 }
 
-template <int KIND>
+template <int KF>
 static int launch_feature_bwd_kind(const FeatParams& p, cudaStream_t s) {
   const size_t sm = feature_bwd_smem(p);
-  cudaFuncSetAttribute(feature_bwd_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  cudaFuncSetAttribute(feature_bwd_kernel<KF>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   const int NT = ceil_div(p.T, kTile);
-  feature_bwd_kernel<KIND><<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
+  feature_bwd_kernel<KF><<<dim3(NT, p.H, p.B * p.nsel), kThreads, sm, s>>>(p);
   return check_launch("feature_bwd_kernel");
 }
 
+// A relu2 / softmax map without per-feature or per-head controls over whole
+// column chunks runs the plain instantiation.
+static bool plain_map(const FeatParams& p) {
+  return p.kind != kBspline && p.bias == nullptr && p.thr == nullptr && p.gain_mode == 0 && p.P == p.PP;
+}
+
 int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
+  const bool plain = plain_map(p);
   switch (p.kind) {
-    case kRelu2: return launch_feature_fwd_kind<kRelu2>(p, s);
-    case kSoftmax: return launch_feature_fwd_kind<kSoftmax>(p, s);
+    case kRelu2: return plain ? launch_feature_fwd_kind<kRelu2 | kPlainBit>(p, s) : launch_feature_fwd_kind<kRelu2>(p, s);
+    case kSoftmax:
+      return plain ? launch_feature_fwd_kind<kSoftmax | kPlainBit>(p, s) : launch_feature_fwd_kind<kSoftmax>(p, s);
     default: return launch_feature_fwd_kind<kBspline>(p, s);
   }
 }
 
 int launch_feature_bwd(const FeatParams& p, cudaStream_t s) {
+  const bool plain = plain_map(p);
   switch (p.kind) {
-    case kRelu2: return launch_feature_bwd_kind<kRelu2>(p, s);
-    case kSoftmax: return launch_feature_bwd_kind<kSoftmax>(p, s);
+    case kRelu2: return plain ? launch_feature_bwd_kind<kRelu2 | kPlainBit>(p, s) : launch_feature_bwd_kind<kRelu2>(p, s);
+    case kSoftmax:
+      return plain ? launch_feature_bwd_kind<kSoftmax | kPlainBit>(p, s) : launch_feature_bwd_kind<kSoftmax>(p, s);
     default: return launch_feature_bwd_kind<kBspline>(p, s);
   }
 }
