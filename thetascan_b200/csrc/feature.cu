@@ -109,34 +109,58 @@ __device__ __forceinline__ float ctl_scale(const FeatParams& p, int h) {
 __device__ __forceinline__ float bspline_knot(int i, int nb, float bound, float step) {
   return i <= 3 ? -bound : (i >= nb ? bound : -bound + static_cast<float>(i - 3) * step);
 }
-__device__ __forceinline__ void bspline_local(float c, int nb, float bound, float* val, float* der, int& first,
-                                              bool& inside) {
+
+// The knots (nb + 4 of them, nb <= 16) and the reciprocals of the knot
+// differences the recursion divides by, rd[o-1][i] = 1 / (knot[i+o] - knot[i])
+// (0 where the difference is zero: the reference drops those terms), built
+// once per CTA so that the recursion multiplies instead of dividing.
+constexpr int kMaxKnots = 20;
+struct SplineTable {
+  float knot[kMaxKnots];
+  float rd[3][kMaxKnots];
+  float inv_step;
+};
+
+__device__ void build_spline_table(SplineTable& t, int nb, float bound) {
+  const float step = 2.f * bound / static_cast<float>(nb - 3);
+  const int nk = nb + 4;
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) t.knot[i] = bspline_knot(i, nb, bound, step);
+  __syncthreads();
+  for (int e = threadIdx.x; e < 3 * nk; e += blockDim.x) {
+    const int o = 1 + e / nk, i = e % nk;
+    float r = 0.f;
+    if (i + o < nk) {
+      const float dl = t.knot[i + o] - t.knot[i];
+      r = dl > 0.f ? 1.f / dl : 0.f;
+    }
+    t.rd[o - 1][i] = r;
+  }
+  if (threadIdx.x == 0) t.inv_step = 1.f / step;
+  __syncthreads();
+}
+
+__device__ __forceinline__ void bspline_local(float c, int nb, float bound, const SplineTable& t, float* val,
+                                              float* der, int& first, bool& inside) {
   const float hi = nextafterf(bound, -bound);
   inside = (c >= -bound) && (c <= bound);
   float x = fminf(fmaxf(c, -bound), bound);
   if (x > hi) x = hi;
-  const float step = 2.f * bound / static_cast<float>(nb - 3);
-  int j = 3 + static_cast<int>(floorf((x + bound) / step));
+  int j = 3 + static_cast<int>(floorf((x + bound) * t.inv_step));
   j = min(max(j, 3), nb - 1);
-  while (j > 3 && x < bspline_knot(j, nb, bound, step)) --j;
-  while (j < nb - 1 && x >= bspline_knot(j + 1, nb, bound, step)) ++j;
+  while (j > 3 && x < t.knot[j]) --j;
+  while (j < nb - 1 && x >= t.knot[j + 1]) ++j;
   float B[4] = {0.f, 0.f, 0.f, 1.f}, D[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int o = 1; o <= 3; ++o) {
 #pragma unroll
     for (int s = 3 - o; s < 4; ++s) {
       const int i = j - 3 + s;
-      const float ki = bspline_knot(i, nb, bound, step), ki1 = bspline_knot(i + 1, nb, bound, step);
-      const float kio = bspline_knot(i + o, nb, bound, step), kio1 = bspline_knot(i + o + 1, nb, bound, step);
-      const float dl = kio - ki;
-      const float dr = kio1 - ki1;
-      const float L = dl > 0.f ? (x - ki) / dl : 0.f;
-      const float R = dr > 0.f ? (kio1 - x) / dr : 0.f;
-      const float dL = dl > 0.f ? 1.f / dl : 0.f;
-      const float dR = dr > 0.f ? -1.f / dr : 0.f;
+      const float rl = t.rd[o - 1][i], rr = t.rd[o - 1][i + 1];
+      const float L = (x - t.knot[i]) * rl;
+      const float R = (t.knot[i + o + 1] - x) * rr;
       const float b1 = s < 3 ? B[s + 1] : 0.f, d1 = s < 3 ? D[s + 1] : 0.f;
       const float nb_ = L * B[s] + R * b1;
-      const float nd_ = dL * B[s] + L * D[s] + dR * b1 + R * d1;
+      const float nd_ = rl * B[s] + L * D[s] - rr * b1 + R * d1;
       B[s] = nb_;
       D[s] = nd_;
     }
@@ -151,11 +175,11 @@ __device__ __forceinline__ void bspline_local(float c, int nb, float bound, floa
     S += B[s];
     dS += D[s];
   }
-  S = fmaxf(S, 1.17549435e-38f);
+  const float invS = 1.f / fmaxf(S, 1.17549435e-38f);
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
-    val[s] = B[s] / S;
-    der[s] = (D[s] * S - B[s] * dS) / (S * S);
+    val[s] = B[s] * invS;
+    der[s] = (D[s] - B[s] * dS * invS) * invS;
   }
   first = j - 3;
 }
@@ -587,7 +611,8 @@ __device__ __forceinline__ float tile_elem(const Tile& t, int r, int c) {
 // phi of this thread's row and column chunks into the phi tile (bf16).
 template <int KF>
 __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowState& st, uint32_t ta_row, int h,
-                                                const Tile& tphi, bool zero_row, float* row32 = nullptr) {
+                                                const Tile& tphi, bool zero_row, const SplineTable* spl,
+                                                float* row32 = nullptr) {
   constexpr int KIND = KF & kKindMask;
   constexpr bool kPlain = (KF & kPlainBit) != 0;
   (void)kPlain;
@@ -617,7 +642,7 @@ __device__ __forceinline__ void phi_row_to_tile(const FeatParams& p, const RowSt
       float val[4], der[4];
       int first;
       bool inside;
-      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
+      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, *spl, val, der, first, inside);
       for (int ii = 0; ii < p.nb; ii += 8) {
         float f[8];
 #pragma unroll
@@ -669,6 +694,8 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
+  __shared__ SplineTable spl_table;
+  if constexpr ((KF & kKindMask) == kBspline) build_spline_table(spl_table, p.nb, p.bound);
   __shared__ float pair[kThreads];
   __shared__ float row_norm[kTile];
   const int h = blockIdx.y;
@@ -730,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_fwd_kernel(FeatParams p) 
     // the stored tile are exact zeros there.
     float* row32 = (sel == 1 && p.phi_q32 != nullptr && row < rows)
                       ? p.phi_q32 + ((static_cast<size_t>(b) * p.H + h) * p.T + t0 + row) * p.m : nullptr;
-    phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, row >= rows, row32);
+    phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, row >= rows, &spl_table, row32);
     __syncthreads();
     __nv_bfloat16* out = p.phi[sel] + ((static_cast<size_t>(b) * p.H + h) * p.T + t0) * p.m;
     store_tile(tl.phi, out, p.m, rows, p.m);
@@ -762,6 +789,8 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_base;
+  __shared__ SplineTable spl_table;
+  if constexpr (KIND == kBspline) build_spline_table(spl_table, p.nb, p.bound);
   __shared__ float red[32];
   __shared__ float pair[kThreads];
   __shared__ float row_norm[kTile];
@@ -912,7 +941,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
       float val[4], der[4];
       int first;
       bool inside;
-      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, val, der, first, inside);
+      bspline_local(a_own[i] * st.inv * sc, p.nb, p.bound, spl_table, val, der, first, inside);
       float g[16];
       grad16(pj * p.nb, g);   // basis functions 0..15 of projection pj (nb <= 16)
       float dc = 0.f;
@@ -928,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
     dot_a = row_pair_sum(dot_a, pair);
     if (!valid) dot_a = dscale = 0.f;
-    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid);
+    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid, &spl_table);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
 #pragma unroll
     for (int i = 0; i < kMaxSplineOwn; ++i) {
@@ -950,7 +979,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
     // One sweep: (phi -> tile for dW2 unless stored), dA = inv * dpre - a *
     // inv^3 * dot_a / P, and the per-feature control gradients.
-    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid);
+    if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid, &spl_table);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
     const bool dbias = p.bias != nullptr && p.dbias != nullptr && valid;
     const bool dgain_feat = KIND == kSoftmax && p.gain_mode == 2 && valid;
