@@ -247,6 +247,164 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_state_kernel(ScanParams p, 
   if (warp == 0) tmem_dealloc(tmem_base, ncols);
 }
 
+// The same per-tile terms where two more payload tiles fit (bstate2_fits):
+// every slot's rows come from a raw dout tile that was copied in while the
+// previous slot computed, and the two row operands of a slot (c o dout for
+// dSloc, and the la-derivative weights o dout for the carry term, or
+// e^{la(i+1)} o dout for a stale slot's dSloc_delta) are formed together so
+// that both products run in one tensor-core round.
+__global__ void __launch_bounds__(kThreads) scan_bwd_state2_kernel(ScanParams p, ScanGradParams g) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float red[32];
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int row = my_row(), part = my_part(), quad = my_quad();
+  const int warp = threadIdx.x >> 5;
+  const int t0 = n * kTile;
+  const int rows = min(kTile, p.T - t0);
+  const uint32_t base = smem_u32(smem);
+  Tile tq{base, kTile, p.DkM};
+  Tile tw{tq.saddr + kTile * p.DkM * 2, kTile, p.DvP};    // c o dout, or the B' rows
+  Tile tk{tw.saddr + kTile * p.DvP * 2, kTile, p.DkM};
+  Tile tv{tk.saddr + kTile * p.DkM * 2, kTile, p.DvP};
+  Tile tx{tv.saddr + kTile * p.DvP * 2, kTile, p.DvP};    // the second row operand
+  Tile traw{tx.saddr + kTile * p.DvP * 2, kTile, p.DvP};  // raw dout of the slot in hand
+  const int mblocks = p.DkM / kTile;
+  const int region = mblocks * p.DvP;
+  const uint32_t ncols = tmem_cols_for(2 * region);
+  bool any_dla = false;
+  for (int r = 0; r < p.R; ++r) any_dla |= (p.la[r] != nullptr && g.dla[r] != nullptr);
+  const bool local = n >= 1 || g.all_tiles;
+  // an auxiliary slot is read through its stale slot's dout
+  auto src_of = [&](int r) { return dout_rows(p, g, p.kind[r] == kSlotAux ? p.partner[r] : r, b, h, t0); };
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, ncols);
+  load_tile(tq, p.q + b * p.qs[0] + h * p.qs[1] + static_cast<long long>(t0) * p.qs[2], p.qs[2], rows, p.Dk);
+  if (any_dla && (n + 1 < p.NT || g.all_tiles)) {
+    load_tile(tk, p.k + b * p.ks[0] + h * p.ks[1] + static_cast<long long>(t0) * p.ks[2], p.ks[2], rows, p.Dk);
+    load_payload(p, tv, p.v + b * p.vs[0] + h * p.vs[1] + static_cast<long long>(t0) * p.vs[2], rows);
+  }
+  if (local) load_tile(traw, src_of(0), p.Dv, rows, p.Dv);
+  tiles_ready();
+  MmaCtx ctx{&bar, tmem_base, 0u, true};
+  const uint32_t t_d = ctx.tmem, t_x = ctx.tmem + static_cast<uint32_t>(region);
+
+  for (int r = 0; r < p.R; ++r) {
+    const float la = head_la(p, r, h);
+    const bool decayed = p.la[r] != nullptr;
+    const int kind = p.kind[r];
+    const bool want = decayed && g.dla[r] != nullptr;
+    // the stale slot's own carry is 1: only its key weights depend on la
+    const bool want_carry = want && kind != kSlotStale;
+    const bool want_delta = want && kind == kSlotStale;
+    const bool use_x = want_carry || want_delta;   // block-uniform
+    if (local) {
+      cp_async_wait_all();
+      __syncthreads();
+      // this row's weights: c(i) for dSloc; for the second operand the
+      // la-derivative of the carry, d/dla c(i) = (i+1) c(i) (decayed) or
+      // -(i+1) e^{la (i+1)} (auxiliary, c = 1 - e^{la (i+1)}), or for a stale
+      // slot the decayed carry e^{la (i+1)} of dSloc_delta
+      const float x = la * static_cast<float>(row + 1);
+      const float ex = decayed ? __expf(x) : 1.f;
+      const float c = kind == kSlotAux ? one_minus_exp(x) : (decayed && kind != kSlotStale) ? ex : 1.f;
+      // A decayed slot's carry operand is (i+1) times the ROUNDED c o dout
+      // row, so that its terms cancel against dSloc's exactly as the
+      // log-retention gradient's other terms expect; the auxiliary and stale
+      // operands are formed from the raw rows.
+      const bool from_rounded = want_carry && kind != kSlotAux;
+      const float cx = from_rounded ? static_cast<float>(row + 1)
+                                    : want_delta ? ex : -static_cast<float>(row + 1) * ex;
+      for (int j = part; j < p.DvP / 8; j += kParts) {
+        float f[8], y[8];
+        unpack8(tile_ld16(traw, row, j), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float fc = f[e] * c;
+          y[e] = (from_rounded ? __bfloat162float(__float2bfloat16_rn(fc)) : f[e]) * cx;
+          f[e] = fc;
+        }
+        tile_st16(tw, row, j, pack8(f));
+        if (use_x) tile_st16(tx, row, j, pack8(y));
+      }
+      // the raw tile is consumed: the next slot's rows stream in meanwhile
+      __syncthreads();
+      if (r + 1 < p.R) load_tile(traw, src_of(r + 1), p.Dv, rows, p.Dv);
+      cp_async_commit();
+      ctx.run_keep_newest([&] {
+        for (int mb = 0; mb < mblocks; ++mb)
+          gemm_issue(t_d + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+        if (use_x)
+          for (int mb = 0; mb < mblocks; ++mb)
+            gemm_issue(t_x + mb * p.DvP, mnmajor(tq, 0, mb * kTile), mnmajor(tx), p.DvP, kTile, false);
+      });
+      float carry_dot = 0.f;
+      const size_t si = state_index(p, b, h, n, r) * p.DkM * p.DvP;
+      __nv_bfloat16* pdst = g.pstates + si;
+      for (int mb = 0; mb < mblocks; ++mb) {
+        const size_t f = static_cast<size_t>(mb * kTile + row);  // value-major [DvP][DkM]
+        for (int c0 = 16 * part; c0 < p.DvP; c0 += kChunkStep) {
+          float v[16];
+          tmem_ld16(tmem_addr(t_d, quad * 32, mb * p.DvP + c0), v);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) g.gstates[si + static_cast<size_t>(c0 + e) * p.DkM + f] = v[e];
+          if (use_x) {
+            float xv[16];
+            tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c0), xv);
+            if (want_carry) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) carry_dot += xv[e] * p.states[si + static_cast<size_t>(c0 + e) * p.DkM + f];
+            } else {
+              // dSloc_delta(n) = sum_t e^{la (i+1)} q_t^T dout_X[t]: the local
+              // term of G_delta = G_X - G_a, carried by the reverse prefix on
+              // its own, kept in this tile's pstates
+#pragma unroll
+              for (int e = 0; e < 16; ++e) pdst[static_cast<size_t>(c0 + e) * p.DkM + f] = __float2bfloat16_rn(xv[e]);
+            }
+          }
+        }
+      }
+      if (want_carry) {
+        const float sum = block_sum(carry_dot, red);
+        if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
+      }
+    }
+    if (want && kind != kSlotStale && (n + 1 < p.NT || g.all_tiles)) {
+      // B'(n): key-weight derivative of the state this tile leaves behind.
+      const float wgt = slot_key_weight_dla(p, r, la, rows, row);
+      for (int j = part; j < p.DvP / 8; j += kParts) {
+        float f[8];
+        unpack8(tile_ld16(tv, row, j), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= wgt;
+        tile_st16(tw, row, j, pack8(f));
+      }
+      ctx.run_keep_newest([&] {
+        for (int mb = 0; mb < mblocks; ++mb)
+          gemm_issue(t_x + mb * p.DvP, mnmajor(tk, 0, mb * kTile), mnmajor(tw), p.DvP, kTile, false);
+      });
+      __nv_bfloat16* dst = g.pstates + state_index(p, b, h, n, r) * p.DkM * p.DvP;
+      for (int mb = 0; mb < mblocks; ++mb) {
+        __nv_bfloat16* col = dst + mb * kTile + row;
+        for (int c0 = 16 * part; c0 < p.DvP; c0 += kChunkStep) {
+          float v[16];
+          tmem_ld16(tmem_addr(t_x, quad * 32, mb * p.DvP + c0), v);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) col[static_cast<size_t>(c0 + e) * p.DkM] = __float2bfloat16_rn(v[e]);
+        }
+      }
+    }
+  }
+  cp_async_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_base, ncols);
+}
+
 // ------------------------------------------------------------------ reverse prefix
 
 // Sum over the block's threads of `acc`, added to dla[h] by thread 0.
@@ -1034,6 +1192,9 @@ static size_t dv_smem(const ScanParams& p) {
          (p.DvP > kTile ? static_cast<size_t>(p.DvP) * p.DkP * 2 : 0);
 }
 static size_t bstate_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (2 * p.DkM + 2 * p.DvP) * 2; }
+// The state kernel with the raw dout tile and the second row operand.
+static size_t bstate2_smem(const ScanParams& p) { return static_cast<size_t>(kTile) * (2 * p.DkM + 4 * p.DvP) * 2; }
+static bool bstate2_fits(const ScanParams& p) { return bstate2_smem(p) <= kDynSmemBudget; }
 
 size_t scan_bwd_max_smem(const ScanParams& p) {
   size_t m = dqk_smem(p, dqk_buffers(p));
@@ -1053,8 +1214,16 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
   cudaFuncSetAttribute(scan_bwd_dqk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
   if (tile_terms && (p.NT > 1 || g.all_tiles)) {
-    scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
-    if (int e = check_launch("scan_bwd_state_kernel")) return e;
+    if (bstate2_fits(p)) {
+      const size_t s_state2 = bstate2_smem(p);
+      cudaFuncSetAttribute(scan_bwd_state2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(s_state2));
+      scan_bwd_state2_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state2, s>>>(p, g);
+      if (int e = check_launch("scan_bwd_state2_kernel")) return e;
+    } else {
+      scan_bwd_state_kernel<<<dim3(p.NT, p.H, p.B), kThreads, s_state, s>>>(p, g);
+      if (int e = check_launch("scan_bwd_state_kernel")) return e;
+    }
   }
   if (p.NS > 0) {
     const dim3 grid = seg_grid(p.DkM, p.DvP, p.R, p.B * p.H, p.NS);
