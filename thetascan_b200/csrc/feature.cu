@@ -92,6 +92,14 @@ __device__ __forceinline__ float ctl_thr(const FeatParams& p, int h) {
   if constexpr (kPlain) return 0.f;
   return p.thr ? __ldg(p.thr + h) : 0.f;
 }
+
+// Packed f32x2 arithmetic (two lanes per instruction; each lane rounds as
+// the scalar operation does) for the plain relu2 loops.
+__device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y); }
+__device__ __forceinline__ float2 relu2_u(float2 a, float2 inv) {
+  const float2 t = __fmul2_rn(a, inv);
+  return f2(fmaxf(t.x, 0.f), fmaxf(t.y, 0.f));
+}
 __device__ __forceinline__ float ctl_scale(const FeatParams& p, int h) {
   return p.scale ? __ldg(p.scale + h) : p.scale_scalar;
 }
@@ -268,6 +276,36 @@ __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_r
   if constexpr (KIND == kRelu2) {
     const float thr = ctl_thr<kPlain>(p, h);
     float M = 0.f, Sg = 0.f, Sgua = 0.f, Sua = 0.f, Sgu = 0.f, Su = 0.f;
+    if constexpr (kPlain) {
+      // u = relu(a * inv) over whole chunks, two columns per instruction
+      const float2 inv2 = f2(s.inv, s.inv);
+      float2 M2 = f2(0.f, 0.f), Sg2 = M2, Sgua2 = M2, Sua2 = M2, Sgu2 = M2, Su2 = M2;
+      for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+        float a[16], g[16];
+        tmem_ld16(ta_row + c, a);
+        if (kWithGrad) grad16(c, g);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const float2 a2 = f2(a[e], a[e + 1]);
+          const float2 u2 = relu2_u(a2, inv2);
+          M2 = __ffma2_rn(u2, u2, M2);
+          if (kWithGrad) {
+            const float2 gu2 = __fmul2_rn(f2(g[e], g[e + 1]), u2);
+            Sg2 = __ffma2_rn(gu2, u2, Sg2);
+            Sgua2 = __ffma2_rn(gu2, a2, Sgua2);
+            Sua2 = __ffma2_rn(u2, a2, Sua2);
+            Sgu2 = __fadd2_rn(Sgu2, gu2);
+            Su2 = __fadd2_rn(Su2, u2);
+          }
+        }
+      }
+      M = M2.x + M2.y;
+      Sg = Sg2.x + Sg2.y;
+      Sgua = Sgua2.x + Sgua2.y;
+      Sua = Sua2.x + Sua2.y;
+      Sgu = Sgu2.x + Sgu2.y;
+      Su = Su2.x + Su2.y;
+    } else
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], g[16];
       tmem_ld16(ta_row + c, a);
@@ -371,7 +409,19 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
   constexpr int KIND = KF & kKindMask;
   constexpr bool kPlain = (KF & kPlainBit) != 0;
   (void)kPlain;
-  if constexpr (KIND == kRelu2) {
+  if constexpr (KIND == kRelu2 && kPlain) {
+    const bool live = s.mass > p.eps;
+    const float inv_mass = 1.f / fmaxf(s.mass, p.eps);
+    const float2 inv2 = f2(s.inv, s.inv), im2 = f2(inv_mass, inv_mass);
+    const float uniform = 1.f / static_cast<float>(p.m);
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const float2 u2 = relu2_u(f2(a[e], a[e + 1]), inv2);
+      const float2 v2 = __fmul2_rn(__fmul2_rn(u2, u2), im2);
+      out[e] = live ? v2.x : uniform;
+      out[e + 1] = live ? v2.y : uniform;
+    }
+  } else if constexpr (KIND == kRelu2) {
     const float thr = ctl_thr<kPlain>(p, h);
     const bool live = s.mass > p.eps;
     const float inv_mass = 1.f / fmaxf(s.mass, p.eps);
@@ -983,6 +1033,30 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
     const bool dbias = p.bias != nullptr && p.dbias != nullptr && valid;
     const bool dgain_feat = KIND == kSoftmax && p.gain_mode == 2 && valid;
+    if constexpr (KIND == kRelu2 && kPlain) {
+      // dpre = (g - dphi) (2 / mass) u (live rows), two columns per instruction
+      const bool live = st.mass > p.eps && valid;
+      const float k2 = 2.f / fmaxf(st.mass, p.eps);
+      const float2 inv2 = f2(st.inv, st.inv), k22 = f2(k2, k2), mdphi = f2(-dot_phi, -dot_phi);
+      const float2 c3 = f2(inv3 * dot_a, inv3 * dot_a);
+      for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+        float a[16], g[16], da[16];
+        tmem_ld16(ta_row + c, a);
+        grad16(c, g);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const float2 a2 = f2(a[e], a[e + 1]);
+          const float2 u2 = relu2_u(a2, inv2);
+          const float2 dp2 = __fmul2_rn(__fmul2_rn(__fadd2_rn(f2(g[e], g[e + 1]), mdphi), k22), u2);
+          const float2 x2 = __fmul2_rn(a2, c3);
+          const float2 da2 = __ffma2_rn(inv2, live ? dp2 : f2(0.f, 0.f), f2(-x2.x, -x2.y));
+          da[e] = valid ? da2.x : 0.f;
+          da[e + 1] = valid ? da2.y : 0.f;
+        }
+        tile_st16(tl.da, row, c / 8, pack8(da));
+        tile_st16(tl.da, row, c / 8 + 1, pack8(da + 8));
+      }
+    } else
     for (int c = 16 * part; c < p.PP; c += kChunkStep) {
       float a[16], dp[16], da[16];
       tmem_ld16(ta_row + c, a);
