@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(kReadWarps * 32) kread_bwd_kernel(ReadParams p
     for (int j = 0; j < N - 1; ++j) deta[j] += (p.mode == 1) ? dymem[1 + j] - dymem[0] : -dymem[1 + j];
   };
   if constexpr (G > 0) {
-    constexpr int kB = ReadBatch<N, V, G>::kRows;
+    // the backward keeps more per row (dN, the partial sums): a smaller batch
+    // for three and more slots keeps its registers within two blocks per SM
+    constexpr int kB = N >= 3 ? (ReadBatch<N, V, G>::kRows > 2 ? 2 : ReadBatch<N, V, G>::kRows) : ReadBatch<N, V, G>::kRows;
     for (int i0 = 0; i0 < kRowsPerWarp; i0 += kB) {
       float mass[kB][N], dy[kB][G][V], x[kB][G][N][V];
 #pragma unroll
