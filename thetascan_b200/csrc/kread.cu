@@ -22,8 +22,9 @@
 // rounded numbers (whose residual grows like 1/D for small masses).  With two
 // mass columns dD travels as bf16 hi + lo, exact to ~2^-17.
 // A block owns kReadRows consecutive tokens of one (batch, head); each warp
-// takes kRowsPerWarp of them, lanes striding the value columns, with
-// read-only loads the compiler may batch across rows.
+// takes kRowsPerWarp of them, lanes striding the value columns in 8-byte
+// pairs; rows of 64 or 128 columns are loaded a batch of rows at a time
+// before any arithmetic (several rows' loads in flight per warp).
 #include "capi_internal.h"
 #include "common.cuh"
 
