@@ -39,4 +39,52 @@ def run(device: torch.device) -> None:
     errors += [_rel(a.grad, b.grad) for a, b in zip(leaves, ol)]
     if max(errors) > 2e-2:
         raise RuntimeError(f"smoke: CUDA path differs from the oracle (rel errors {errors})")
-    print(f"smoke ok: max rel err {max(errors):.2e}")
+
+    # the float32 scan kernels on the same streams, within the float32 bound
+    l32 = [x.float().to(device).requires_grad_(True) for x in (q, k, v)]
+    outs32 = scan.linattn_views(*l32, (None, la.to(device)), append_unit=True)
+    sum(o.sum() for o in outs32).backward()
+    errors32 = [_rel(a, b) for a, b in zip(outs32, want)] + [_rel(a.grad, b.grad) for a, b in zip(l32, ol)]
+    if max(errors32) > 1e-5:
+        raise RuntimeError(f"smoke: float32 scan differs from the oracle (rel errors {errors32})")
+
+    # the whole mixer (projections, feature kernels, scans, read) forward+backward
+    _mixer(device)
+    print(f"smoke ok: bf16 scan max rel err {max(errors):.2e}, float32 scan {max(errors32):.2e}")
+
+
+def _mixer(device: torch.device) -> None:
+    from oracle import mixer as omixer
+    from .config import KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
+    from .mixer import ThetaScan
+
+    cfg = ThetaScanConfig(d_model=128, n_heads=2, memory_multiplier=2, feature_expansion=2, family="kernel",
+                          kernel=KernelConfig(feature_map="relu2_ridge"), rope=RoPEConfig(mode="partial"),
+                          temporal=TemporalConfig(mode="bank", retention_init=0.95))
+    torch.manual_seed(0)
+    module = ThetaScan(cfg)
+    with torch.no_grad():
+        module._core.W2[0].copy_(torch.randn(module._core.W2[0].shape, generator=torch.Generator().manual_seed(1)) * 0.2)
+    module = module.to(device)
+    x = torch.randn(1, 160, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    xg = x.to(device).requires_grad_(True)
+    y = module(xg)
+    y.float().square().mean().backward()
+    if _lib_status(device) != 0:
+        raise RuntimeError("smoke: a kernel reported a device-side timeout")
+    if not all(torch.isfinite(p.grad).all() for p in module.parameters() if p.grad is not None):
+        raise RuntimeError("smoke: non-finite mixer gradient")
+    core = {"n_heads": 2, "head_dim": 64, "feature_expansion": 2, "kernel_kind": "relu2_ridge", "rope": "partial",
+            "rope_frac": 0.5, "rope_base": 10000.0, "read_fade": True, "read_fade_mode": "fast",
+            "read_norm": "key_mass", "eps": 1e-6, "scan_chunk": 64}
+    params = {n: t.detach().cpu().double() for n, t in module._core.named_parameters()}
+    params.update({n: t.detach().cpu().double() for n, t in module._core.named_buffers() if n.startswith("_expand_")})
+    want = omixer.mixer_forward(params, core, x.double())
+    err = _rel(y, want)
+    if err > 2e-2:
+        raise RuntimeError(f"smoke: mixer output differs from the oracle (rel error {err:.2e})")
+
+
+def _lib_status(device) -> int:
+    from . import _lib
+    return _lib.device_status(torch.cuda.current_stream(device).cuda_stream)
