@@ -83,6 +83,43 @@ def per_token_f32(fn, *tensors):
     return fn(*tensors)
 
 
+class _HeadMap(torch.autograd.Function):
+    """``y[b,h,t] = W[h] x[b,h,t]`` for ``W [H,o,i]``, ``x [B,H,T,i]``, f32.
+
+    The weight gradient sums over all B*T tokens of a head; as one GEMM per
+    head (what an einsum's backward does) that is a handful of output tiles
+    with a 10^5-long reduction, so few SMs work.  Here the token axis is cut
+    into chunks that become batch entries (a view of the contiguous input),
+    the per-chunk products run in parallel, and their sum is taken after."""
+
+    @staticmethod
+    def forward(ctx, W, x):
+        ctx.save_for_backward(W, x)
+        return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+
+    @staticmethod
+    def backward(ctx, gy):
+        W, x = ctx.saved_tensors
+        gW = gx = None
+        if ctx.needs_input_grad[1]:
+            gx = torch.matmul(gy, W.unsqueeze(0))
+        if ctx.needs_input_grad[0]:
+            B, H, T, i = x.shape
+            o = gy.shape[-1]
+            xc, gc = x.contiguous(), gy.contiguous()
+            S = 1
+            while T % (2 * S) == 0 and T // (2 * S) >= 512 and B * H * S < 512:
+                S *= 2
+            part = torch.bmm(gc.view(B * H * S, T // S, o).transpose(1, 2), xc.view(B * H * S, T // S, i))
+            gW = part.view(B, H, S, o, i).sum(dim=(0, 2))
+        return gW, gx
+
+
+def head_map(W, x):
+    """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (see _HeadMap)."""
+    return _HeadMap.apply(W, x)
+
+
 def _activation(nonlin, pre):
     if nonlin == "relu2":
         r = F.relu(pre)
@@ -151,18 +188,18 @@ def _scan(query, keys, payload, append_unit, retentions, stale=None):
 
 def gn_write(k, v, W1, W2, tau, nonlin, eps):
     """(h, g, lambda) of every token, f32 (reference engine.py:161-340, depth 1)."""
-    a = torch.einsum("hmd,bhtd->bhtm", W1, k)
+    a = head_map(W1, k)
     pre, inv = _rmsnorm(a, eps)
     pre = _thresholded(pre, tau)
     h = _activation(nonlin, pre)
-    o = k + torch.einsum("hdm,bhtm->bhtd", W2, h)
+    o = k + head_map(W2, h)
     r = v - o
     dsig = _activation_grad(nonlin, pre)
     s = dsig * inv
-    rowsq = torch.einsum("hdm,bhtm->bhtd", W2 * W2, s * s)
+    rowsq = head_map(W2 * W2, s * s)
     diag = h.square().sum(-1, keepdim=True) + k.square().sum(-1, keepdim=True) * rowsq
     lam = r / (diag + eps)
-    g = dsig * torch.einsum("hdm,bhtd->bhtm", W2, lam) * inv
+    g = dsig * head_map(W2.transpose(1, 2), lam) * inv
     return h, g, lam
 
 
@@ -193,7 +230,7 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
     flags = stale if any(stale) else None
 
     def query_pre(qq, w1, *t):
-        a = torch.einsum("hmd,bhtd->bhtm", w1, qq)
+        a = head_map(w1, qq)
         return a, _activation("relu2", _thresholded(_rmsnorm(a, eps)[0], t[0] if t else None))
 
     a_q, h0 = per_token_f32(query_pre, qf, W1f, *extra)
@@ -207,7 +244,7 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
 
     def features(pre, w2, *t):
         hq = _activation(nonlin, _thresholded(_rmsnorm(pre, eps)[0], t[0] if t else None))
-        return hq, torch.einsum("hdm,bhtm->bhtd", w2, hq)
+        return hq, head_map(w2, hq)
 
     # stage 2, one query per view
     outs = []
