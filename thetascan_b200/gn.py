@@ -60,13 +60,16 @@ class _PerToken(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         inputs = [t.detach().requires_grad_(t.requires_grad) for t in ctx.saved_tensors]
-        with _tf32(), torch.enable_grad():
-            out = ctx.fn(*inputs)
-        outs = [out] if ctx.single else list(out)
-        pairs = [(o, g) for o, g in zip(outs, grads) if g is not None and o.requires_grad]
-        wanted = [t for t in inputs if t.requires_grad]
-        got = torch.autograd.grad([o for o, _ in pairs], wanted, [g for _, g in pairs], allow_unused=True) \
-            if pairs and wanted else [None] * len(wanted)
+        with _tf32():
+            with torch.enable_grad():
+                out = ctx.fn(*inputs)
+            outs = [out] if ctx.single else list(out)
+            pairs = [(o, g) for o, g in zip(outs, grads) if g is not None and o.requires_grad]
+            wanted = [t for t in inputs if t.requires_grad]
+            # the gradient GEMMs (the projections' weight gradients above all)
+            # run inside the TF32 setting too
+            got = torch.autograd.grad([o for o, _ in pairs], wanted, [g for _, g in pairs], allow_unused=True) \
+                if pairs and wanted else [None] * len(wanted)
         it = iter(got)
         return (None, *[next(it) if t.requires_grad else None for t in inputs])
 
