@@ -28,7 +28,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .scan import _ScanViews
+from .scan import _ScanViewsFromF32
 
 
 class _tf32:
@@ -170,21 +170,19 @@ def _piece_width(n_retentions, Dk):
 
 
 def _scan(query, keys, payload, append_unit, retentions, stale=None):
-    """f32 reads of the multi-view scan kernels (bf16 streams).  The scan is
-    linear in the payload, so a payload wider than one call takes is read in
-    column pieces (the mass column rides on the last)."""
-    bf = torch.bfloat16
-    q, k = query.to(bf).contiguous(), keys.to(bf).contiguous()
+    """f32 reads of the multi-view scan kernels (bf16 streams, f32 gradients
+    back).  The scan is linear in the payload, so a payload wider than one
+    call takes is read in column pieces (the mass column rides on the last)."""
     width = payload.shape[-1]
-    step = _piece_width(len(retentions), q.shape[-1]) - 1
+    step = _piece_width(len(retentions), query.shape[-1]) - 1
     if width + (1 if append_unit else 0) <= step + 1:
-        return _ScanViews.apply(q, k, payload.to(bf).contiguous(), append_unit, torch.float32, stale, *retentions)
+        return _ScanViewsFromF32.apply(query, keys, payload, append_unit, stale, *retentions)
     parts = [[] for _ in retentions]
     for start in range(0, width, step):
-        piece = payload[..., start:start + step].to(bf).contiguous()
+        piece = payload[..., start:start + step]
         last = start + step >= width
-        for i, read in enumerate(_ScanViews.apply(q, k, piece, append_unit and last, torch.float32, stale,
-                                                  *retentions)):
+        for i, read in enumerate(_ScanViewsFromF32.apply(query, keys, piece, append_unit and last, stale,
+                                                         *retentions)):
             parts[i].append(read)
     return tuple(torch.cat(p, dim=-1) for p in parts)
 

@@ -89,6 +89,7 @@ class _ScanViews(torch.autograd.Function):
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
         ctx.append_unit = append_unit
         ctx.stale = stale
+        ctx.grad_dtypes = (q.dtype, k.dtype, v.dtype)
         ctx.n_ret = len(las)
         ctx.ret_present = [r is not None for r in retentions]
         ctx.ret_dtypes = [None if r is None else r.dtype for r in retentions]
@@ -130,7 +131,30 @@ class _ScanViews(torch.autograd.Function):
         ret_grads = []
         for dla, dtype, shape in zip(dlas, ctx.ret_dtypes, ctx.ret_shapes):
             ret_grads.append(None if dla is None else dla.to(dtype).reshape(shape))
-        return (dq.to(q.dtype), dk.to(k.dtype), dvv.to(v.dtype), None, None, None, *ret_grads)
+        qd, kd, vd = ctx.grad_dtypes
+        return (dq.to(qd), dk.to(kd), dvv.to(vd), None, None, None, *ret_grads)
+
+
+class _ScanViewsFromF32(torch.autograd.Function):
+    """The multi-view scan of float32 q, k, v on bf16 streams: the inputs are
+    rounded to bf16 here (what the tensor-core kernels read), the reads are
+    f32, and the gradients return in float32 as the kernels write them, with
+    no bf16 round trip on the way back.  Used by callers whose per-token math
+    around the scan is float32 (the GN family)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, append_unit, stale, *retentions):
+        bf = torch.bfloat16
+        outs = _ScanViews.forward(ctx, q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(),
+                                  append_unit, torch.float32, stale, *retentions)
+        ctx.grad_dtypes = (q.dtype, k.dtype, v.dtype)
+        return outs
+
+    @staticmethod
+    def backward(ctx, *douts):
+        grads = _ScanViews.backward(ctx, *douts)
+        # drop the out_dtype slot of _ScanViews' signature
+        return grads[:4] + grads[5:]
 
 
 def _check_inputs(q, k, v, retentions, chunk):
