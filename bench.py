@@ -349,13 +349,14 @@ def run_reference(args, cfg):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     T = args.ref_tokens
-    cpu_reference_step(cfg, 128, "bank")  # warm-up of the allocator and kernels
+    for _ in range(args.warmup):              # untimed warm-up steps of the same sample
+        cpu_reference_step(cfg, T, "bank")
     times = [cpu_reference_step(cfg, T, "bank") for _ in range(max(1, args.steps))]
     per_step = statistics.median(times)
     value = T / per_step
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": len(times), "warmup": 1, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config 2 per-token shape, bounded CPU sample B=1 T={T}", "model": "ThetaScan-Kernel",
                    "global_batch": 1, "seq_len": T, "parallelism": "cpu"},
