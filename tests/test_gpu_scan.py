@@ -2,7 +2,7 @@
 
 The CUDA path is checked against the float64 CPU oracle (``oracle.scan``),
 which is itself pinned to the reference by tests/test_oracle_golden.py.
-Tolerance (SURVEY parity gate, bf16 streams with f32 state):
+Tolerance (the bf16 parity bound, bf16 streams with f32 state):
 ``max|got - ref| / max|ref| <= 2e-2`` on outputs and gradients.
 """
 from __future__ import annotations
