@@ -264,9 +264,12 @@ class ThetaScanCore(nn.Module):
             finally:
                 for n in names:
                     _set_param(self, n, saved[n])
-            return _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base)), v.contiguous()
+            return q.contiguous(), k.contiguous(), v.contiguous()
 
+        # the projection GEMMs under TF32 (recomputed in the backward); RoPE
+        # and the L2 norm have no GEMM, so they run once under plain autograd
         q, k, v = per_token(qkv, xf, *[params[n] for n in names])
+        q, k = _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base))
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         W1, W2 = self.effective_weights()
