@@ -352,7 +352,7 @@ int ts_b200_kread_bwd(const ts_kread_args* args, const ts_kread_grad_args* grad,
  * (view.mass_cum: causal_prefix_sum, ema_cumsum or their stale difference,
  * src/thetascan/_core/ops/interface.py:58-107, 216-230, 278-279, 306-307)
  * before an unnormalized scan of that view:
- *   q_scaled = phi_q / (mass + eps)   (bf16)
+ *   q_scaled = phi_q / (mass + eps)   (bf16, or f32 with q_scaled_f32)
  * w = 1 (log_alpha NULL), alpha_h^(t-i), or 1 - alpha_h^(t-i) (stale != 0).
  */
 typedef struct ts_mass_args {
@@ -365,6 +365,8 @@ typedef struct ts_mass_args {
   void* q_scaled;           /* bf16 [B,H,T,m] out (forward) */
   const float* phi_q_f32;   /* f32 [B,H,T,m] phi(q), read instead of phi_q when set
                              * (ts_feature_args.phi_q_f32: one rounding, of the quotient) */
+  int q_scaled_f32;         /* nonzero: q_scaled is f32 (8-byte aligned), unrounded, for a
+                             * float32 scan; the backward's d mass then uses that quotient */
 } ts_mass_args;
 
 int ts_b200_mass_query_fwd(const ts_mass_args* args, ts_stream_t stream);

@@ -123,7 +123,7 @@ class MassArgs(ctypes.Structure):
         ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("width", ctypes.c_int),
         ("phi_k", ctypes.c_void_p), ("phi_q", ctypes.c_void_p), ("log_alpha", ctypes.c_void_p),
         ("stale", ctypes.c_int), ("eps", ctypes.c_float), ("q_scaled", ctypes.c_void_p),
-        ("phi_q_f32", ctypes.c_void_p),
+        ("phi_q_f32", ctypes.c_void_p), ("q_scaled_f32", ctypes.c_int),
     ]
 
 

@@ -144,7 +144,10 @@ int build_mass_params(const ts_mass_args* a, MassParams* p) {
   p->la = a->log_alpha;
   p->stale = a->stale ? 1 : 0;
   p->eps = a->eps;
-  p->qs = static_cast<__nv_bfloat16*>(a->q_scaled);
+  p->qs = a->q_scaled;
+  p->qs_f32 = a->q_scaled_f32 ? 1 : 0;
+  if (p->qs_f32 && (reinterpret_cast<uintptr_t>(a->q_scaled) & 7))
+    return set_error(TS_ERR_VALUE, "mass: an f32 q_scaled must be 8-byte aligned");
   return TS_OK;
 }
 }  // namespace

@@ -8,11 +8,12 @@
 // all nonnegative:
 //   D_t = alpha D_{t-1} + x_t                      (recency mass)
 //   X_t = X_{t-1} + (1 - alpha) D_{t-1}            (stale mass, no cancellation)
-// Forward output: q_scaled_t = phi_q_t / (mass_t + eps), bf16.
+// Forward output: q_scaled_t = phi_q_t / (mass_t + eps), bf16 (or f32 for a
+// float32 scan).
 //
 // Backward, with g = d q_scaled:
 //   d phi_q_t  += g_t / (mass_t + eps)
-//   d mass_t    = -g_t q_scaled_t / (mass_t + eps)      (q_scaled as rounded to bf16)
+//   d mass_t    = -g_t q_scaled_t / (mass_t + eps)      (q_scaled as the scan read it)
 //   d phi_k_j  += sum_{t>=j} w(t-j) d mass_t        (reverse recursions)
 //   d la       += sum_t d mass_t dmass_t/dla,  dD_t/dla = F_t = alpha (F_{t-1} + D_{t-1}),
 //                 dX_t/dla = -F_t
@@ -33,7 +34,8 @@ struct MassParams {
   const float* la;             // [H] or null (plain prefix sum)
   int stale;
   float eps;
-  __nv_bfloat16* qs;           // [B,H,T,m] out
+  void* qs;                    // [B,H,T,m] out, bf16 or (qs_f32) f32
+  int qs_f32;
   // backward
   const void* dqs;
   int dqs_bf16;
@@ -97,8 +99,12 @@ __global__ void __launch_bounds__(256) mass_fwd_kernel(MassParams p) {
       if (t0 + i >= p.T) break;
       const float m0 = s0.step(xk[i].x, alpha, open, decayed, p.stale, false);
       const float m1 = s1.step(xk[i].y, alpha, open, decayed, p.stale, false);
-      *reinterpret_cast<__nv_bfloat162*>(p.qs + base + static_cast<size_t>(t0 + i) * p.m) =
-          __floats2bfloat162_rn(xq[i].x / (m0 + p.eps), xq[i].y / (m1 + p.eps));
+      const size_t o = base + static_cast<size_t>(t0 + i) * p.m;
+      const float2 qv = make_float2(xq[i].x / (m0 + p.eps), xq[i].y / (m1 + p.eps));
+      if (p.qs_f32)
+        *reinterpret_cast<float2*>(static_cast<float*>(p.qs) + o) = qv;
+      else
+        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.qs) + o) = __float22bfloat162_rn(qv);
     }
   }
 }
@@ -142,10 +148,12 @@ __global__ void __launch_bounds__(256) mass_bwd_kernel(MassParams p) {
         cur.x += g[i].x * i0;
         cur.y += g[i].y * i1;
         *dq = cur;
-        // d mass from the bf16 quotient the scan read (the forward's value):
-        // its gradient then cancels against the scan's d phi_k as the
-        // quotient rule does, instead of leaving a 2^-9 residual of each term
-        const float2 qs = __bfloat1622float2(__floats2bfloat162_rn(xq[i].x / (m0 + p.eps), xq[i].y / (m1 + p.eps)));
+        // d mass from the quotient the scan read (the forward's value, bf16-
+        // rounded for a bf16 scan): its gradient then cancels against the
+        // scan's d phi_k as the quotient rule does, instead of leaving a 2^-9
+        // residual of each term
+        float2 qs = make_float2(xq[i].x / (m0 + p.eps), xq[i].y / (m1 + p.eps));
+        if (!p.qs_f32) qs = __bfloat1622float2(__float22bfloat162_rn(qs));
         const float dm0 = -g[i].x * qs.x * i0, dm1 = -g[i].y * qs.y * i1;
         *reinterpret_cast<float2*>(p.dmass + o) = make_float2(dm0, dm1);
         if (want) {

@@ -474,8 +474,9 @@ class _MassQuery(torch.autograd.Function):
     query of that view's unnormalized scan in the feature-mass read."""
 
     @staticmethod
-    def _args(phi_k, phi_q, la, stale, eps, out):
-        """``phi_q`` bf16, or f32 (read instead, one rounding less)."""
+    def _args(phi_k, phi_q, la, stale, eps, out, f32_quotient=False):
+        """``phi_q`` bf16, or f32 (read instead, one rounding less); the
+        quotient bf16, or unrounded f32 for a float32 scan."""
         B, H, T, m = phi_k.shape
         a = _lib.MassArgs()
         a.batch, a.heads, a.tokens, a.width = B, H, T, m
@@ -487,13 +488,14 @@ class _MassQuery(torch.autograd.Function):
         a.log_alpha = _ptr(la)
         a.stale, a.eps = 1 if stale else 0, eps
         a.q_scaled = _ptr(out)
+        a.q_scaled_f32 = 1 if f32_quotient else 0
         return a
 
     @staticmethod
     def forward(ctx, phi_k, phi_q, la, stale, eps):
         lib = _lib.load()
         la32 = None if la is None else la.detach().reshape(-1).to(torch.float32).contiguous()
-        qn = torch.empty_like(phi_q)
+        qn = torch.empty(phi_q.shape, dtype=torch.bfloat16, device=phi_q.device)
         a = _MassQuery._args(phi_k, phi_q, la32, stale, eps, qn)
         _lib.check(lib.ts_b200_mass_query_fwd(ctypes.byref(a), _stream()))
         ctx.stale, ctx.eps, ctx.la32 = stale, eps, la32
@@ -522,6 +524,18 @@ class _MassQuery(torch.autograd.Function):
         if dla is not None:
             dla = dla.to(ctx.la_meta[0]).reshape(ctx.la_meta[1])
         return dphi_k, dphi_q, dla, None, None
+
+
+def _stale_f32_args(query, f32_kv, la, out, workspace=None):
+    """Scan arguments of a stale feature-mass view on float32 streams: the
+    f32 quotient against f32 copies of the bf16 keys and values, read as the
+    plain sum and the decayed view (the stale read is their difference, as
+    the reference forms it).  Returns the arguments and the decayed read to
+    subtract from ``out``; in the backward (``workspace`` given) nothing is
+    written and ``out`` only fills both output slots."""
+    k32, v32 = f32_kv
+    fast = out if workspace is not None else torch.empty_like(out)
+    return _build_args(query, k32, v32, [None, la], [out, fast], 0, workspace), fast
 
 
 class _KernelCoreViews(torch.autograd.Function):
@@ -561,17 +575,27 @@ class _KernelCoreViews(torch.autograd.Function):
         else:
             groups = []
             for i, la in enumerate(las):
-                qn = torch.empty_like(phi_q)
-                ma = _MassQuery._args(phi_k, phi_q32, la, flags[i], spec.eps, qn)
+                # a stale view's quotient stays f32 and its scan runs on f32 streams
+                qn = torch.empty(B, H, T, m, dtype=torch.float32 if flags[i] else torch.bfloat16, device=dev)
+                ma = _MassQuery._args(phi_k, phi_q32, la, flags[i], spec.eps, qn, f32_quotient=flags[i])
                 _lib.check(lib.ts_b200_mass_query_fwd(ctypes.byref(ma), _stream()))
                 groups.append((qn, [i]))
         scans = []
+        f32_kv = None
         for query, idx in groups:
-            sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0,
-                             stale=[flags[i] for i in idx])
+            if query.dtype == torch.float32:
+                if f32_kv is None:
+                    f32_kv = (phi_k.float(), v.float().contiguous())
+                sa, extra = _stale_f32_args(query, f32_kv, las[idx[0]], slots[idx[0]])
+            else:
+                sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0,
+                                 stale=[flags[i] for i in idx])
+                extra = None
             ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
             sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
             _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
+            if extra is not None:
+                slots[idx[0]].sub_(extra)
             scans.append((query, idx, ws))
         eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
         y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=dev)
@@ -580,6 +604,7 @@ class _KernelCoreViews(torch.autograd.Function):
         ctx.spec, ctx.ctl, ctx.W, ctx.las, ctx.flags = spec, ctl, (W1b, W2b), las, flags
         ctx.scans, ctx.slots, ctx.eta, ctx.y0 = scans, slots, eta, y0
         ctx.phi = (phi_q, phi_k, phi_q32)
+        ctx.f32_kv = f32_kv
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, W1.dtype, W2.dtype)
         ctx.has_eta = etas is not None
         ctx.save_for_backward(q, k, v)
@@ -618,15 +643,25 @@ class _KernelCoreViews(torch.autograd.Function):
         dv = torch.zeros(B, H, T, d, dtype=torch.float32, device=dev)
         dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
         for query, idx, ws in ctx.scans:
-            sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0, ws,
-                             stale=[flags[i] for i in idx])
             sg = _lib.ScanGradArgs()
+            if query.dtype == torch.float32:
+                # sum - fast: the fast slot's read gradient is -dslot, which
+                # also gives its log-retention gradient the stale view's sign
+                i = idx[0]
+                sa, _ = _stale_f32_args(query, ctx.f32_kv, las[i], slots[i], ws)
+                dsum = dslots[i].float()
+                dfast = -dsum
+                sg.dout[0], sg.dout[1] = dsum.data_ptr(), dfast.data_ptr()
+                sg.dlog_alpha[1] = _ptr(dlas[i])
+            else:
+                sa = _build_args(query, phi_k, v, [las[i] for i in idx], [slots[i] for i in idx], 0, ws,
+                                 stale=[flags[i] for i in idx])
+                for j, i in enumerate(idx):
+                    sg.dout[j] = dslots[i].data_ptr()
+                    sg.dlog_alpha[j] = _ptr(dlas[i])
             dq_s = torch.empty(B, H, T, m, dtype=torch.float32, device=dev)
             dk_s = torch.empty_like(dq_s)
             dv_s = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-            for j, i in enumerate(idx):
-                sg.dout[j] = dslots[i].data_ptr()
-                sg.dlog_alpha[j] = _ptr(dlas[i])
             sg.dq, sg.dk, sg.dv = dq_s.data_ptr(), dk_s.data_ptr(), dv_s.data_ptr()
             sg.grad_dtype = _lib.TS_DTYPE_F32
             gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
@@ -639,7 +674,7 @@ class _KernelCoreViews(torch.autograd.Function):
                 dphi_q += dq_s
                 continue
             i = idx[0]
-            ma = _MassQuery._args(phi_k, phi_q32, las[i], flags[i], spec.eps, None)
+            ma = _MassQuery._args(phi_k, phi_q32, las[i], flags[i], spec.eps, None, f32_quotient=flags[i])
             mg = _lib.MassGradArgs()
             mg.dq_scaled, mg.dq_dtype = dq_s.data_ptr(), _lib.TS_DTYPE_F32
             mg.dphi_q, mg.dphi_k, mg.dlog_alpha = dphi_q.data_ptr(), dphi_k.data_ptr(), _ptr(dlas[i])
