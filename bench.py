@@ -135,59 +135,119 @@ def flops_per_token(cfg):
 # --------------------------------------------------------------------------- measurement helpers
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region.
+
+    A thread reads NVML every 10 ms (read-only queries: the current and the
+    maximum SM clock and the active clock-event reasons); where NVML cannot be
+    loaded it reads ``nvidia-smi -lms 200`` instead.  ``__enter__`` returns once
+    the first sample is in, so that the record covers the start of the timed
+    region as well as its end."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index):
+    def __init__(self, index, period_s=0.01):
         self.index = index
+        self.period = period_s
         self.proc = None
-        self.lines = []
+        self.thread = None
+        self.stop = threading.Event()
+        self.samples = []  # (sm MHz, max sm MHz, set of active reasons)
+        self.source = None
 
     def __enter__(self):
+        if not self._start_nvml():
+            self._start_smi()
+        deadline = time.perf_counter() + 3.0
+        while (not self.samples and self.thread is not None and self.thread.is_alive()
+               and time.perf_counter() < deadline):
+            time.sleep(0.002)
+        return self
+
+    def _start_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            masks = [(name, getattr(pynvml, attr)) for name, attr in self.REASONS]
+
+            def sample():
+                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                return sm, max_mhz, {name for name, mask in masks if bits & mask}
+
+            first = sample()
+        except Exception:
+            return False
+
+        def run():
+            try:
+                self.samples.append(first)
+                while not self.stop.wait(self.period):
+                    self.samples.append(sample())
+            except Exception:
+                pass
+            finally:
+                try:
+                    pynvml.nvmlShutdown()
+                except Exception:
+                    pass
+
+        self.source = f"nvml every {self.period * 1e3:.0f} ms"
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        return True
+
+    def _start_smi(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
         except OSError:
             self.proc = None
-        return self
+            return
+        self.source = "nvidia-smi every 200 ms"
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
+        self.thread.start()
 
-    def _read(self):
+    def _read_smi(self):
+        names = [name for name, _ in self.REASONS]
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            self.samples.append((sm, mx, {n for n, flag in zip(names, parts[5:9])
+                                          if flag.lower().startswith("active")}))
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
+        samples = list(self.samples)
+        if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[0] for s in samples),
+                "sm_max_mhz": max(s[1] for s in samples),
+                "reasons": sorted(set().union(*(s[2] for s in samples))),
+                "samples": len(samples), "sampler": self.source}
 
 
 class PhaseTimer:
