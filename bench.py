@@ -638,7 +638,8 @@ def run_b200(args, cfg):
                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": traffic,
                     "bytes_per_launch": bytes_launch, "flops_per_launch": flops_launch,
                     "peak_source": f"{peak_kind} bf16_tflops_sustained"}
-    mixer_tflops = mixer_flops * value / 1e12
+    # Per GPU: `value` is the whole job's tokens/s, the peak one GPU's.
+    mixer_tflops = mixer_flops * value / world / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True,
@@ -652,7 +653,7 @@ def run_b200(args, cfg):
                    "parallelism": f"sp{world}" if seqpar else (f"dp{world}" if world > 1 else "single"),
                    "l2": "256 MB buffer written before every timed step"},
         "roofline": roofline,
-        "mixer_roofline": {"achieved": mixer_tflops, "peak": peak_sus, "unit": "TFLOP/s",
+        "mixer_roofline": {"achieved": mixer_tflops, "peak": peak_sus, "unit": "TFLOP/s", "per": "gpu",
                            "frac": mixer_tflops / peak_sus, "flop_per_token": mixer_flops,
                            "core_flop_per_token": core_flops},
         "phase_ms": {k.replace("ts_b200_", ""): round(v, 4) for k, v in phase_ms.items()},
