@@ -5,7 +5,7 @@
  * boundary; each entry point below names the reference interface it stands in
  * for (paths relative to the reference project root).  A Python host reaches
  * these through ctypes (thetascan_b200/_lib.py); any other host binds them the
- * same way.
+ * same way, with plain pointers, sizes and this header's structs.
  *
  * Conventions
  *  - All tensor pointers are DEVICE pointers on the current CUDA device.
@@ -192,8 +192,11 @@ int ts_b200_scan_bwd(const ts_scan_args* fwd, const ts_scan_grad_args* grad, ts_
  *    library, held by every GPU that loads it until the process exits.  A
  *    shape needing more (ts_b200_scan_workspace_bytes > the limit) is
  *    rejected with TS_ERR_VALUE before anything is launched.
- *  - The first call on each device resolves the array's device address with
- *    that device current; make that first call before any stream capture.
+ *  - Every call looks up the array's device address in the current device's
+ *    context (a host-side lookup, no stream operation), so the address stays
+ *    right after that context is destroyed and created again.  The first
+ *    lookup on a device may load the library's module there: make the first
+ *    call on each device before any stream capture.
  *  - All calls on one GPU share that GPU's copy of the array, which keeps
  *    the last call's contents: calls that overlap on the same GPU (say, on
  *    two streams) race, so serialize them.  Nothing in it needs clearing:

@@ -202,6 +202,15 @@ GN_CONFIGS = {
         temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=1, T=160, dtype="float32"),
 }
 
+# Config-3 width (head_dim 128, m = 128, relu2, two-stage feature-mass read,
+# the plain sum view) at T = 1024; written to its own file, gn_c3_cases.pt.
+GN_C3_CONFIGS = {
+    "gn_c3_d128_T1024": dict(
+        d_model=256, n_heads=2, memory_multiplier=1, family="gn",
+        gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="sum"), B=1, T=1024, dtype="float32"),
+}
+
 GN_CORE_KEYS = (
     "d_model", "n_heads", "head_dim", "mem_hidden", "feature_expansion", "expansion_key", "depth",
     "write_rule", "nonlin", "learn_thresh", "write_iters", "fast_w1", "act_norm", "qk_norm",
@@ -209,11 +218,11 @@ GN_CORE_KEYS = (
     "read_norm", "read_norm_w1", "read_norm_mode", "eps", "scan_chunk", "share_kq", "key_value_heads")
 
 
-def gn_cases():
+def gn_cases(configs=None):
     from thetascan import GNConfig, RoPEConfig, TemporalConfig, ThetaScan, ThetaScanConfig
 
     out = {}
-    for name, spec in GN_CONFIGS.items():
+    for name, spec in (GN_CONFIGS if configs is None else configs).items():
         spec = dict(spec)
         B, T = spec.pop("B"), spec.pop("T")
         dtype = getattr(torch, spec.pop("dtype", "float64"))
@@ -254,7 +263,12 @@ def gn_cases():
     return out
 
 
-GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases}
+def gn_c3_cases():
+    return gn_cases(GN_C3_CONFIGS)
+
+
+GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases,
+              "gn_c3": gn_c3_cases}
 
 
 def main():

@@ -1,6 +1,6 @@
 """``thetascan_b200.integration.install`` registers backend "b200" in an
 installed reference package (CPU checks of the routing; skipped where the
-reference package is not importable, e.g. on the GPU box)."""
+reference package is not importable, see ``tests/_refpkg.py``)."""
 from __future__ import annotations
 
 import os
@@ -9,14 +9,13 @@ import sys
 import pytest
 import torch
 
-REF_SRC = "/".join(["", "root", "reference", "src"])
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refpkg import import_reference  # noqa: E402
 
 
 @pytest.fixture(scope="module")
 def thetascan():
-    if os.path.isdir(REF_SRC) and REF_SRC not in sys.path:
-        sys.path.insert(0, REF_SRC)
-    ts = pytest.importorskip("thetascan")
+    ts = import_reference()
     from thetascan_b200 import integration
     integration.install()
     return ts

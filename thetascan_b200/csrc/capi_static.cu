@@ -7,8 +7,6 @@
 // For them this variant keeps its scratch in a fixed file-scope device array
 // of TS_STATIC_SCRATCH_BYTES that every GPU loading the library holds until
 // exit; the caller still passes inputs and outputs.
-#include <mutex>
-
 #include "capi_internal.h"
 #include "scan.cuh"
 
@@ -18,27 +16,18 @@ static __device__ __align__(256) unsigned char g_scan_scratch[TS_STATIC_SCRATCH_
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_address[kMaxDevices] = {};
-
-// Device address of g_scan_scratch on the current device.  Resolved once per
-// device, with that device current, on the first call there; the symbol name
-// itself is only a host-side handle and must never reach a kernel.
+// Device address of g_scan_scratch in the current device's context.  The
+// symbol name itself is only a host-side handle and must never reach a
+// kernel.  The address is looked up on every call (a host-side table lookup,
+// no stream operation), so it stays right when the context is torn down and
+// created again (cudaDeviceReset, a host runtime that releases the primary
+// context), which loads the module afresh and may move the array.
 int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "scan_fwd_static: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return set_error(TS_ERR_VALUE, "scan_fwd_static: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_address[dev] == nullptr) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_scan_scratch);
-    if (e != cudaSuccess || ptr == nullptr)
-      return set_error(TS_ERR_CUDA, "scan_fwd_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_scratch_address[dev] = ptr;
-  }
-  *out = g_scratch_address[dev];
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scan_scratch);
+  if (e != cudaSuccess || ptr == nullptr)
+    return set_error(TS_ERR_CUDA, "scan_fwd_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  *out = ptr;
   return TS_OK;
 }
 

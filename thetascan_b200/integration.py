@@ -121,6 +121,11 @@ def _fused_core(module):
     configuration is outside the fused path (the scan-level path then runs)."""
     cached = getattr(module, "_b200_fused", None)
     if cached is not None:
+        # Parameters are shared objects and follow module.to(); buffers are
+        # replaced by it, so hand the view the module's current ones.
+        for name, buf in module.named_buffers():
+            if name.startswith("_expand_"):
+                cached._buffers[name] = buf
         return cached
     cfg = module.cfg
     if cfg.write_rule != "kernel" or not cfg.read_norm or cfg.read_norm_mode != "key_mass":
