@@ -13,8 +13,8 @@ all-reduce the mixer's parameter gradients over NCCL, as a data-parallel
 step does.  ``--config c4`` (config 4: T = 32768, B-spline features, four
 views) instead splits the sequences into N contiguous shards, one per rank,
 that exchange their chunk states with one NCCL all-gather per step (strong
-scaling: the B x T tokens are fixed).  ``--impl reference`` times the reference's CPU implementation
-(the float32 oracle restatement of its chunk backend) on the host cores.
+scaling: the B x T tokens are fixed).  ``--impl reference`` times the reference package's own CPU
+implementation (its chunk backend, float32, from ``baseline/_ref``) on the host cores.
 
 One JSON line is printed by rank 0.
 """
@@ -151,8 +151,12 @@ class ClockSampler:
                ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
                ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index, period_s=0.01):
-        self.index = index
+    def __init__(self, bus_id, period_s=0.01):
+        # The device is named by its PCI bus id ("DDDDDDDD:BB:DD.F"), not an
+        # ordinal: NVML and nvidia-smi number GPUs physically and ignore
+        # CUDA_VISIBLE_DEVICES, so the CUDA ordinal of a leased GPU can be
+        # another GPU's NVML index.
+        self.bus_id = bus_id
         self.period = period_s
         self.proc = None
         self.thread = None
@@ -173,7 +177,9 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            by_bus = getattr(pynvml, "nvmlDeviceGetHandleByPciBusId_v2", None) or \
+                pynvml.nvmlDeviceGetHandleByPciBusId
+            handle = by_bus(self.bus_id)
             max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
             masks = [(name, getattr(pynvml, attr)) for name, attr in self.REASONS]
 
@@ -207,7 +213,7 @@ class ClockSampler:
     def _start_smi(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "-i", self.bus_id, f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -243,11 +249,17 @@ class ClockSampler:
     def summary(self):
         samples = list(self.samples)
         if not samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "bus_id": self.bus_id}
         return {"sm_mhz": statistics.median(s[0] for s in samples),
                 "sm_max_mhz": max(s[1] for s in samples),
                 "reasons": sorted(set().union(*(s[2] for s in samples))),
-                "samples": len(samples), "sampler": self.source}
+                "samples": len(samples), "sampler": self.source, "bus_id": self.bus_id}
+
+
+def device_bus_id(index):
+    """PCI bus id of CUDA device ``index`` in NVML's format."""
+    props = torch.cuda.get_device_properties(index)
+    return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
 
 
 class PhaseTimer:
@@ -372,12 +384,71 @@ MEASURED_TRAFFIC = {
 
 # --------------------------------------------------------------------------- CPU reference
 
-def cpu_reference_step(cfg, T, view_set):
-    """One forward+backward of the reference CPU algorithm (oracle restatement).
+def reference_package():
+    """The reference ``thetascan`` package itself (pure PyTorch): the
+    directory ``$THETASCAN_REFERENCE_PATH`` names, else the offline install
+    under ``baseline/_ref``; None where neither holds it."""
+    path = os.environ.get("THETASCAN_REFERENCE_PATH") or os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "thetascan")):
+        return None
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    import thetascan
+    return thetascan
 
-    ``view_set="bank"`` runs the chunk form with the full bank (the
-    reference's fastest CPU path); ``"sum"`` runs the prefix-sum (cumsum)
-    backend, which the reference restricts to the plain sum view."""
+
+def reference_module(ts, cfg, backend, view_set):
+    """The reference's own public mixer for a bench workload, float32 on the
+    CPU, with ``backend`` ("chunk", its fastest CPU path, or "cumsum", which
+    takes the plain sum view only) and the same seeded weights as the GPU
+    arm's module.  A bank of more than two recency branches (config 4) is
+    beyond the reference's configuration; its arm runs two (0.9, 0.99)."""
+    C = ts
+    runtime = C.RuntimeConfig(backend=backend)
+    if cfg.get("family") == "gn":
+        config = C.ThetaScanConfig(
+            d_model=cfg["D"], n_heads=cfg["H"], memory_multiplier=cfg["mult"], family="gn",
+            gn=C.GNConfig(nonlinearity=cfg["fmap"], jacobian_steps=1, read_normalization=cfg["gn_read"]),
+            rope=C.RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=C.TemporalConfig(mode="sum"),
+            runtime=runtime)
+    else:
+        kernel = C.KernelConfig(feature_map=cfg["fmap"], bspline_basis_count=cfg.get("basis", 8))
+        if view_set == "sum":
+            temporal = C.TemporalConfig(mode="sum")
+        elif cfg["J"] == 1:
+            temporal = C.TemporalConfig(mode="bank", retention_init=0.95)
+        else:
+            temporal = C.TemporalConfig(mode="bank", recency_branches=2, retention_inits=tuple(cfg["retentions"][:2]))
+        config = C.ThetaScanConfig(
+            d_model=cfg["D"], n_heads=cfg["H"], memory_multiplier=cfg["mult"],
+            feature_expansion=cfg["expansion"], family="kernel", kernel=kernel,
+            rope=C.RoPEConfig(mode=cfg["rope"], fraction=0.5), temporal=temporal, runtime=runtime)
+    torch.manual_seed(0)
+    module = C.ThetaScan(config).float()
+    if view_set != "sum" and cfg.get("family") != "gn" and cfg["J"] == 1 and cfg.get("retention_spread", True):
+        with torch.no_grad():
+            alphas = 0.9 + 0.099 * torch.rand(cfg["H"], generator=torch.Generator().manual_seed(0))
+            module._core.fade_alpha.copy_(torch.log(alphas / (1.0 - alphas)))
+    return module
+
+
+def cpu_reference_step(cfg, T, view_set):
+    """One forward+backward on the host CPU of the reference's own code for
+    this workload at batch 1 and ``T`` tokens; returns (seconds, kind).
+
+    ``view_set="bank"`` runs the reference's chunk backend with the
+    workload's bank (its fastest CPU path); ``"sum"`` runs its cumsum backend,
+    which the reference restricts to the plain sum view.  Where the reference
+    package is absent, the float32 restatement under ``oracle/`` runs the same
+    algorithm instead (kind "port")."""
+    ts = reference_package()
+    x = torch.randn(1, T, cfg["D"], generator=torch.Generator().manual_seed(0))
+    if ts is not None:
+        module = reference_module(ts, cfg, "cumsum" if view_set == "sum" else "chunk", view_set)
+        t0 = time.perf_counter()
+        y = module(x)
+        y.square().mean().backward()
+        return time.perf_counter() - t0, "reference"
     from oracle import mixer as omixer
     from oracle import scan as oscan
 
@@ -395,11 +466,20 @@ def cpu_reference_step(cfg, T, view_set):
         scan_fn = lambda q, k, v, rets: tuple(oscan.linattn_cumsum(q, k, v) for _ in rets)
     else:
         scan_fn = None
-    x = torch.randn(1, T, cfg["D"], generator=torch.Generator().manual_seed(0))
     t0 = time.perf_counter()
     y = omixer.mixer_forward(params, core_cfg, x, scan_fn=scan_fn)
     y.square().mean().backward()
-    return time.perf_counter() - t0
+    return time.perf_counter() - t0, "port"
+
+
+def _reference_sample(kind, view_set, T, n):
+    what = ("the reference package's chunk backend (its fastest CPU path), the workload's view bank"
+            if view_set == "bank" else
+            "the reference package's cumsum backend, plain sum view (cumsum rejects banks)")
+    if kind == "port":
+        what = "float32 restatement of the reference under oracle/ (reference package absent): " + what
+    return (f"{what}; float32, batch 1 x {T} tokens of the workload's per-token shape, forward+backward, "
+            f"median of {n}; tokens/s = {T} / median seconds (the GPU arm's batch and length are larger)")
 
 
 def run_reference(args, cfg):
@@ -411,18 +491,19 @@ def run_reference(args, cfg):
     T = args.ref_tokens
     for _ in range(args.warmup):              # untimed warm-up steps of the same sample
         cpu_reference_step(cfg, T, "bank")
-    times = [cpu_reference_step(cfg, T, "bank") for _ in range(max(1, args.steps))]
-    per_step = statistics.median(times)
+    runs = [cpu_reference_step(cfg, T, "bank") for _ in range(max(1, args.steps))]
+    per_step = statistics.median(t for t, _ in runs)
+    kind = runs[0][1]
     value = T / per_step
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": len(times), "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "steps": len(runs), "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config 2 per-token shape, bounded CPU sample B=1 T={T}", "model": "ThetaScan-Kernel",
-                   "global_batch": 1, "seq_len": T, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"B=1, T={T}, full bank, chunk form of the reference (float32 oracle restatement), "
-                                   f"forward+backward, median of {len(times)}"},
+        "config": {"workload": f"{args.config} per-token shape, bounded CPU sample B=1 T={T}",
+                   "model": "ThetaScan mixer (reference package)", "global_batch": 1, "seq_len": T,
+                   "parallelism": "cpu", "normalization": "tokens/s = B*T of the sample / seconds per step"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": _reference_sample(kind, "bank", T, len(runs))},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -492,7 +573,7 @@ def run_b200(args, cfg):
     timer.scan_launches = 0
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clocks:
+    with ClockSampler(device_bus_id(local)) as clocks:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -669,22 +750,17 @@ def run_b200(args, cfg):
         "wall_s": wall,
         "device_status": status,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c1":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in ("c1", "c2"):
+        # the reference's own CPU code on a bounded sample (c1: its chunk
+        # backend on the whole config-1 workload; c2: its cumsum backend, the
+        # baseline's CPU arm, on one 1024-token sequence)
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
-        secs = statistics.median(cpu_reference_step(cfg, T, "bank") for _ in range(3))
-        line["cpu_baseline"] = {"value": T / secs, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"config 1, B=1, T={T}, full bank, chunk form of the reference "
-                                          f"(float32 oracle restatement), forward+backward, median of 3"}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c2":
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
-        T_cpu = args.ref_tokens
-        secs = cpu_reference_step(cfg, T_cpu, "sum")
-        line["cpu_baseline"] = {"value": T_cpu / secs, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"reference cumsum backend (float32 oracle restatement), config 2 "
-                                          f"per-token shape, B=1, T={T_cpu}, plain-sum view (cumsum rejects banks), "
-                                          f"one forward+backward"}
+        view_set, T_cpu, reps = ("bank", T, 3) if args.config == "c1" else ("sum", args.ref_tokens, 1)
+        runs = [cpu_reference_step(cfg, T_cpu, view_set) for _ in range(reps)]
+        secs = statistics.median(t for t, _ in runs)
+        line["cpu_baseline"] = {"value": T_cpu / secs, "unit": "tokens/s", "cores": threads, "kind": runs[0][1],
+                                "sample": _reference_sample(runs[0][1], view_set, T_cpu, reps)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

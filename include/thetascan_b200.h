@@ -65,6 +65,14 @@ int ts_b200_device_status(ts_stream_t stream, int* status);
 int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
                          ts_stream_t stream);
 
+/* The same product with both operands loaded by TMA (64-column boxes, 128-byte
+ * swizzle) and read through swizzled descriptors.  Sources: A [128 x K]
+ * row-major, or A^T [K x 128] if a_mn; B [K x N] row-major if b_mn, else
+ * B^T [N x K].  N and K are 64 or 128.  No reference counterpart: it
+ * validates the operand layouts of the TMA-fed kernels. */
+int ts_b200_selftest_tma_mma(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                             ts_stream_t stream);
+
 /* ------------------------------------------------------------------ scan
  *
  * Multi-view inclusive causal scan, the contract of

@@ -16,6 +16,7 @@ import types
 import pytest
 
 _ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BUS = "00000000:1B:00.0"
 
 
 def _load_bench():
@@ -52,7 +53,8 @@ def _fake_nvml(clocks, reasons, fail_init=False):
 
     m.nvmlInit = init
     m.nvmlShutdown = lambda: state.__setitem__("shutdown", state["shutdown"] + 1)
-    m.nvmlDeviceGetHandleByIndex = lambda i: ("gpu", i)
+    m.nvmlDeviceGetHandleByIndex = lambda i: pytest.fail("the sampler must not open a GPU by NVML index")
+    m.nvmlDeviceGetHandleByPciBusId_v2 = lambda bus: state.__setitem__("bus", bus) or ("gpu", bus)
     m.nvmlDeviceGetMaxClockInfo = lambda h, kind: 1965
     m.nvmlDeviceGetClockInfo = clock
     m.nvmlDeviceGetCurrentClocksEventReasons = event_reasons
@@ -64,10 +66,11 @@ def test_nvml_samples_clocks_and_reasons(monkeypatch):
     bench = _load_bench()
     fake = _fake_nvml([1965, 1965, 1800, 1965], [0, 0x4, 0x4, 0])
     monkeypatch.setitem(sys.modules, "pynvml", fake)
-    with bench.ClockSampler(0, period_s=0.005) as c:
+    with bench.ClockSampler(BUS, period_s=0.005) as c:
         assert c.samples, "__enter__ returns only after the first sample"
         time.sleep(0.05)
     s = c.summary()
+    assert fake.state["bus"] == BUS and s["bus_id"] == BUS
     assert s["samples"] >= 4
     assert s["sm_max_mhz"] == 1965.0
     assert s["sm_mhz"] == 1965.0
@@ -79,7 +82,7 @@ def test_nvml_samples_clocks_and_reasons(monkeypatch):
 def test_slowdown_reasons_are_reported(monkeypatch):
     bench = _load_bench()
     monkeypatch.setitem(sys.modules, "pynvml", _fake_nvml([1200], [0x40 | 0x8 | 0x20]))
-    with bench.ClockSampler(0, period_s=0.005) as c:
+    with bench.ClockSampler(BUS, period_s=0.005) as c:
         time.sleep(0.02)
     assert c.summary()["reasons"] == ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"]
 
@@ -92,9 +95,24 @@ def test_unsampled_without_nvml_or_nvidia_smi(monkeypatch):
         raise OSError("nvidia-smi not found")
 
     monkeypatch.setattr(bench.subprocess, "Popen", no_smi)
-    with bench.ClockSampler(0) as c:
+    with bench.ClockSampler(BUS) as c:
         pass
-    assert c.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    assert c.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "bus_id": BUS}
+
+
+def test_nvidia_smi_fallback_names_the_bus_id(monkeypatch):
+    bench = _load_bench()
+    monkeypatch.setitem(sys.modules, "pynvml", _fake_nvml([1965], [0], fail_init=True))
+    seen = {}
+
+    def fake_popen(cmd, **k):
+        seen["cmd"] = cmd
+        raise OSError("stop here")
+
+    monkeypatch.setattr(bench.subprocess, "Popen", fake_popen)
+    with bench.ClockSampler(BUS):
+        pass
+    assert seen["cmd"][:3] == ["nvidia-smi", "-i", BUS]
 
 
 if __name__ == "__main__":

@@ -50,6 +50,25 @@ def test_tcgen05_tile_product_matches_matmul(lib, a_mn, b_mn, N, K):
     assert rel_err(D, want) < 1e-3
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("N,K", [(64, 64), (128, 128), (64, 128), (128, 64)])
+def test_tma_swizzled_tile_product_matches_matmul(lib, a_mn, b_mn, N, K):
+    """Operands loaded by TMA with the 128-byte swizzle and read through the
+    swizzled K-major / MN-major descriptors the TMA-fed kernels use."""
+    g = torch.Generator(device="cuda").manual_seed(N * 7 + K)
+    A = torch.randn(128, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(K, N, device="cuda", generator=g).to(torch.bfloat16)
+    a_src = (A.t() if a_mn else A).contiguous()
+    b_src = (B if b_mn else B.t()).contiguous()
+    D = torch.empty(128, N, device="cuda", dtype=torch.float32)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lib.check(lib.load().ts_b200_selftest_tma_mma(a_src.data_ptr(), b_src.data_ptr(), D.data_ptr(), N, K, a_mn,
+                                                  b_mn, s))
+    assert lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    want = A.double() @ B.double()
+    assert rel_err(D, want) < 1e-3
+
+
 # ----------------------------------------------------------------- scan forward/backward
 
 def _streams(B, H, T, Dk, Dv, seed=0, positive=False):

@@ -60,6 +60,8 @@ SIGNATURES = {
     "ts_b200_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "ts_b200_selftest_mma": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "ts_b200_selftest_tma_mma": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "ts_b200_scan_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScanArgs)]),
     "ts_b200_scan_fwd": (ctypes.c_int, [ctypes.POINTER(ScanArgs), ctypes.c_void_p]),
     "ts_b200_scan_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScanArgs)]),

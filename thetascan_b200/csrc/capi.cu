@@ -261,6 +261,11 @@ int ts_b200_selftest_mma(const void* A, const void* B, float* D, int N, int K, i
   return selftest_mma(A, B, D, N, K, a_mn, b_mn, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int ts_b200_selftest_tma_mma(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                             ts_stream_t stream) {
+  return selftest_tma_mma(A, B, D, N, K, a_mn, b_mn, reinterpret_cast<cudaStream_t>(stream));
+}
+
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
   if (args && args->f32_streams) {
     ScanF32Params p;

@@ -400,23 +400,33 @@ size_t scan_out_smem(const ScanParams& p) {
   return static_cast<size_t>(kTile) * (2 * p.DkP + kTile + p.DvP) * 2 + static_cast<size_t>(p.DvP) * p.DkP * 2;
 }
 
-// The three forward kernels; `tile_states` / `outputs` select the parts that
-// run (the stages of a sequence shard run them separately).
+int launch_scan_chain(const ScanParams& p, cudaStream_t s);
+
+// The forward kernels; `tile_states` / `outputs` select the parts that run
+// (the stages of a sequence shard run them separately).  The carried states
+// come from the TMEM-resident chain (scan_chain.cu) where it applies -- it
+// recomputes every tile's update from k and v, so a stage-2 call does not
+// need stage 1's tile updates -- else from the per-tile updates and the
+// tile prefix below.
 int launch_scan_fwd(const ScanParams& p, cudaStream_t s, bool tile_states, bool outputs) {
   const size_t sm1 = scan_state_smem(p), sm3 = scan_out_smem(p);
   cudaFuncSetAttribute(scan_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm1));
   cudaFuncSetAttribute(scan_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm3));
-  const int state_tiles = p.all_tiles ? p.NT : p.NT - 1;
-  if (tile_states && state_tiles > 0) {
-    scan_state_kernel<<<dim3(state_tiles, p.H, p.B), kThreads, sm1, s>>>(p);
-    if (int e = check_launch("scan_state_kernel")) return e;
+  const int chained = launch_scan_chain(p, s);
+  if (chained < 0) return -chained;
+  if (chained == 0) {
+    const int state_tiles = p.all_tiles ? p.NT : p.NT - 1;
+    if (tile_states && state_tiles > 0) {
+      scan_state_kernel<<<dim3(state_tiles, p.H, p.B), kThreads, sm1, s>>>(p);
+      if (int e = check_launch("scan_state_kernel")) return e;
+    }
+    // One serial chain per state element: the forward chain streams one input
+    // and two outputs per tile at about half of HBM bandwidth already (a
+    // two-level version, measured, was slower for its second read of the tile
+    // states); the backward's three inputs per tile take the two-level form.
+    scan_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p);
+    if (int e = check_launch("scan_prefix_kernel")) return e;
   }
-  // One serial chain per state element: the forward chain streams one input
-  // and two outputs per tile at about half of HBM bandwidth already (a
-  // two-level version, measured, was slower for its second read of the tile
-  // states); the backward's three inputs per tile take the two-level form.
-  scan_prefix_kernel<<<prefix_grid(p.DkM, p.DvP, p.R, p.B * p.H), 256, 0, s>>>(p);
-  if (int e = check_launch("scan_prefix_kernel")) return e;
   if (!outputs) return 0;
   scan_out_kernel<<<dim3(p.NT, p.H, p.B), kThreads, sm3, s>>>(p);
   return check_launch("scan_out_kernel");
