@@ -38,6 +38,10 @@ def activation(nonlin: str, pre: torch.Tensor) -> torch.Tensor:
         return r * r
     if nonlin == "silu":
         return F.silu(pre)
+    if nonlin == "tanh":
+        # extension (config 3 as the baseline states it): an entry of the
+        # reference's ELEMENTWISE table (nonlin.py:28-31), tanh / 1 - h^2
+        return torch.tanh(pre)
     raise ValueError(f"unsupported GN nonlinearity: {nonlin!r}")
 
 
@@ -48,6 +52,9 @@ def activation_grad(nonlin: str, pre: torch.Tensor) -> torch.Tensor:
     if nonlin == "silu":
         s = torch.sigmoid(pre)
         return s * (1 + pre * (1 - s))
+    if nonlin == "tanh":
+        h = torch.tanh(pre)
+        return 1.0 - h * h
     raise ValueError(f"unsupported GN nonlinearity: {nonlin!r}")
 
 

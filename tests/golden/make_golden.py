@@ -267,8 +267,59 @@ def gn_c3_cases():
     return gn_cases(GN_C3_CONFIGS)
 
 
+def gn_tanh_cases():
+    """Config 3 as the baseline states it -- a tanh GN net with damping 1e-2 --
+    which the reference's configuration cannot express: its GN nonlinearity
+    table (nonlin.py:28-31) has no tanh and its public config no damping.  The
+    fixture runs the reference's own engine with the table extended by
+    (tanh, 1 - h^2) and the core epsilon (_core/config.py:191: the damping of
+    the lambda solve, engine.py:255, and the L2/RMS/read epsilons) set to
+    1e-2 on the constructed module; the read is unnormalized, since the
+    feature-mass normalizations need nonnegative features
+    (_core/config.py:420-423).  Head dim 128, m = 128, the plain sum view
+    and a two-branch fast bank.  The matching b200 config is stored beside."""
+    from thetascan import GNConfig, RoPEConfig, TemporalConfig, ThetaScan, ThetaScanConfig
+    from thetascan._core.ops import nonlin
+
+    nonlin.ELEMENTWISE.setdefault("tanh", (torch.tanh, lambda pre, h: 1.0 - h * h))
+    out = {}
+    specs = {
+        "gn_tanh_d128_sum": (TemporalConfig(mode="sum"), 1, 256),
+        "gn_tanh_d128_bank2": (TemporalConfig(mode="bank", recency_branches=2, retention_inits=(0.9, 0.99)), 1, 200),
+    }
+    for name, (temporal, B, T) in specs.items():
+        cfg = ThetaScanConfig(d_model=256, n_heads=2, memory_multiplier=1, family="gn",
+                              gn=GNConfig(nonlinearity="relu2", read_normalization="none"),
+                              rope=RoPEConfig(mode="partial", fraction=0.5), temporal=temporal)
+        torch.manual_seed(0)
+        module = ThetaScan(cfg).to(torch.float64)
+        core = module._core
+        core.cfg.nonlin = "tanh"
+        core.cfg.eps = 1e-2
+        with torch.no_grad():
+            for p in core.W2:
+                p.copy_(_seeded(5, *p.shape) * 0.2)
+            if core.fade_eta is not None:
+                core.fade_eta.copy_(_seeded(6, *core.fade_eta.shape) * 0.5)
+        x = _seeded(8, B, T, cfg.d_model).requires_grad_(True)
+        y = module(x)
+        weight = _seeded(9, *y.shape)
+        (y * weight).sum().backward()
+        b200_cfg = cfg.to_dict()
+        b200_cfg["gn"] = dict(b200_cfg["gn"], nonlinearity="tanh", damping=1e-2)
+        out[name] = {
+            "public_config": cfg.to_dict(), "b200_config": b200_cfg, "B": B, "T": T,
+            "core": {k: getattr(core.cfg, k) for k in GN_CORE_KEYS},
+            "params": {n: t.detach().float() for n, t in core.state_dict(keep_vars=True).items() if t is not None},
+            "x": x.detach().float(), "y": y.detach().float(), "out_weight": weight.float(),
+            "x_grad": x.grad.detach().float(),
+            "grads": {n: p.grad.detach().float() for n, p in core.named_parameters() if p.grad is not None},
+        }
+    return out
+
+
 GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases,
-              "gn_c3": gn_c3_cases}
+              "gn_c3": gn_c3_cases, "gn_tanh": gn_tanh_cases}
 
 
 def main():

@@ -68,7 +68,9 @@ def test_nvml_samples_clocks_and_reasons(monkeypatch):
     monkeypatch.setitem(sys.modules, "pynvml", fake)
     with bench.ClockSampler(BUS, period_s=0.005) as c:
         assert c.samples, "__enter__ returns only after the first sample"
-        time.sleep(0.05)
+        deadline = time.perf_counter() + 5.0
+        while len(c.samples) < 4 and time.perf_counter() < deadline:
+            time.sleep(0.01)
     s = c.summary()
     assert fake.state["bus"] == BUS and s["bus_id"] == BUS
     assert s["samples"] >= 4

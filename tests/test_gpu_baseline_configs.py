@@ -9,7 +9,10 @@ the head counts, feature widths and sequence lengths of the baseline configs:
   the float64 oracle mixer: output, input gradient, every parameter gradient;
 * config 3 -- GN family at head_dim 128, m = 128, relu2 with the two-stage
   feature-mass read, T = 1024, against a fixture that the reference GN mixer
-  produced (``tests/golden/make_golden.py``, ``gn_c3``);
+  produced (``tests/golden/make_golden.py``, ``gn_c3``); and config 3 as the
+  baseline states it, a tanh net with damping 1e-2 and the unnormalized
+  read, against the reference engine run with tanh in its nonlinearity table
+  and core epsilon 1e-2 (``gn_tanh``);
 * config 4 -- projected B-spline features with 16 basis functions (m = 128),
   the four-view bank (sum + 0.9 / 0.99 / 0.999), d_model 1024, 16 heads,
   T = 8192, against the float64 oracle, and the same mixer run as 4 and 8
@@ -174,6 +177,32 @@ def test_config3_width_gn_matches_reference_fixture(dev):
     case = torch.load(os.path.join(GOLDEN, "gn_c3_cases.pt"), weights_only=False)["gn_c3_d128_T1024"]
     module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
     assert module._core.head_dim == 128 and module._core.W1[0].shape[1] == 128
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    x = case["x"].float().to(dev).requires_grad_(True)
+    y = module(x)
+    (y.double() * case["out_weight"].to(dev)).sum().backward()
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    assert rel_err(y, case["y"]) < BF16_TOL
+    assert rel_err(x.grad, case["x_grad"]) < BF16_TOL
+    grads = dict(module._core.named_parameters())
+    for n, want in case["grads"].items():
+        assert rel_err(grads[n].grad, want) < BF16_TOL, n
+
+
+@pytest.mark.parametrize("name", ["gn_tanh_d128_sum", "gn_tanh_d128_bank2"])
+def test_config3_tanh_gn_matches_reference_engine_fixture(dev, name):
+    """The tanh GN net with damping (``GNConfig(nonlinearity="tanh",
+    damping=1e-2)``, an extension of the public config) against the
+    reference's own engine extended by the same table entry and epsilon."""
+    from thetascan_b200 import _lib
+    from thetascan_b200.config import ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+
+    case = torch.load(os.path.join(GOLDEN, "gn_tanh_cases.pt"), weights_only=False)[name]
+    cfg = ThetaScanConfig.from_dict(case["b200_config"])
+    assert cfg.gn.nonlinearity == "tanh" and cfg.gn.damping == 1e-2
+    module = ThetaScan(cfg).to(dev)
     module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
                             if not n.startswith("_expand_")})
     x = case["x"].float().to(dev).requires_grad_(True)

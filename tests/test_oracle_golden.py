@@ -155,3 +155,26 @@ def test_gn_mixer_oracle_matches_reference_forward_and_backward(name):
     _close(x.grad, case["x_grad"].to(torch.float64), tol)
     for n, g in case["grads"].items():
         _close(params[n].grad, g.to(torch.float64), tol)
+
+
+@pytest.mark.parametrize("file,name", [("gn_c3_cases.pt", "gn_c3_d128_T1024"),
+                                       ("gn_tanh_cases.pt", "gn_tanh_d128_sum"),
+                                       ("gn_tanh_cases.pt", "gn_tanh_d128_bank2")])
+def test_gn_oracle_matches_reference_at_config3_width(file, name):
+    """The GN restatement at config 3's widths (head_dim 128, m = 128): the
+    relu2 two-stage read, and the tanh net with damping 1e-2 and the
+    unnormalized read -- config 3 as the baseline states it, which the
+    reference engine runs once its nonlinearity table holds tanh and its core
+    epsilon is 1e-2 (tests/golden/make_golden.py, gn_tanh_cases)."""
+    case = _load(file)[name]
+    params = {n: t.to(torch.float64).clone().requires_grad_(t.is_floating_point() and not n.startswith("_"))
+              for n, t in case["params"].items()}
+    x = case["x"].to(torch.float64).clone().requires_grad_(True)
+    y = mixer.mixer_forward(params, dict(case["core"]), x)
+    # float32 fixtures of float64 runs: the stored inputs are rounded
+    tol = 2e-5
+    _close(y, case["y"].to(torch.float64), tol)
+    (y * case["out_weight"].to(torch.float64)).sum().backward()
+    _close(x.grad, case["x_grad"].to(torch.float64), tol)
+    for n, g in case["grads"].items():
+        _close(params[n].grad, g.to(torch.float64), tol)

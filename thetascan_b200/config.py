@@ -48,11 +48,23 @@ class GNConfig:
     nonlinearity: str = "relu2"
     jacobian_steps: int = 1
     read_normalization: str = "none"
+    # Extension beyond the reference (whose public config exposes neither):
+    # "tanh" as a GN nonlinearity (h = tanh(pre), sigma' = 1 - h^2, the
+    # pattern of the reference's nonlinearity table, nonlin.py:28-31; signed,
+    # so only with read_normalization "none"), and `damping`, the GN family's
+    # core epsilon (the reference's cfg.eps, _core/config.py:191: the damping
+    # of the lambda solve, engine.py:255, and the epsilon of the q/k L2 norm,
+    # the RMS norms and the read normalizations).  None keeps 1e-6.
+    damping: float | None = None
 
     def validate(self) -> None:
         _strict_int("GNConfig.jacobian_steps", self.jacobian_steps)
-        if self.nonlinearity not in ("relu2", "relu2_threshold", "silu", "swiglu"):
+        if self.nonlinearity not in ("relu2", "relu2_threshold", "silu", "swiglu", "tanh"):
             raise ValueError(f"unknown GN nonlinearity: {self.nonlinearity!r}")
+        if self.damping is not None:
+            _finite("GNConfig.damping", self.damping)
+            if not self.damping > 0:
+                raise ValueError("GNConfig.damping must be positive")
         if self.jacobian_steps not in (1, 2):
             raise ValueError("GNConfig.jacobian_steps must be 1 or 2")
         if self.read_normalization not in ("none", "w2_feature_mass", "both_feature_mass"):

@@ -28,7 +28,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .scan import _ScanViewsFromF32
+from .scan import scan_views_f32
 
 
 class _tf32:
@@ -129,6 +129,8 @@ def _activation(nonlin, pre):
         return r * r
     if nonlin == "silu":
         return F.silu(pre)
+    if nonlin == "tanh":
+        return torch.tanh(pre)
     raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
 
 
@@ -138,6 +140,10 @@ def _activation_grad(nonlin, pre):
     if nonlin == "silu":
         s = torch.sigmoid(pre)
         return s * (1 + pre * (1 - s))
+    if nonlin == "tanh":
+        # sigma'(pre) = 1 - tanh(pre)^2, the table's (act, dact(pre, h)) pattern
+        h = torch.tanh(pre)
+        return 1.0 - h * h
     raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
 
 
@@ -176,13 +182,12 @@ def _scan(query, keys, payload, append_unit, retentions, stale=None):
     width = payload.shape[-1]
     step = _piece_width(len(retentions), query.shape[-1]) - 1
     if width + (1 if append_unit else 0) <= step + 1:
-        return _ScanViewsFromF32.apply(query, keys, payload, append_unit, stale, *retentions)
+        return scan_views_f32(query, keys, payload, append_unit, stale, retentions)
     parts = [[] for _ in retentions]
     for start in range(0, width, step):
         piece = payload[..., start:start + step]
         last = start + step >= width
-        for i, read in enumerate(_ScanViewsFromF32.apply(query, keys, piece, append_unit and last, stale,
-                                                         *retentions)):
+        for i, read in enumerate(scan_views_f32(query, keys, piece, append_unit and last, stale, retentions)):
             parts[i].append(read)
     return tuple(torch.cat(p, dim=-1) for p in parts)
 

@@ -147,7 +147,8 @@ def _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue):
 
     las = [None] + ([] if log_alphas is None else
                     [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
-    slots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.float32, device=dev) for _ in las]
+    slots_all = torch.empty(len(las), B, H, T, d + MASS_COLS, dtype=torch.float32, device=dev)
+    slots = list(slots_all.unbind(0))
     sa = _build_args(phi_q, phi_k, v, las, slots, MASS_COLS, stale=_stale_flags(spec, len(las)))
     ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
     sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -157,8 +158,19 @@ def _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue):
     y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=dev)
     ra = _kread_args(spec, slots, eta, y0, y)
     _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
-    state = dict(W1b=W1b, W2b=W2b, phi_q=phi_q, phi_k=phi_k, ws=ws, slots=slots, las=las, eta=eta, y0=y0)
+    state = dict(W1b=W1b, W2b=W2b, phi_q=phi_q, phi_k=phi_k, ws=ws, slots=slots, slots_all=slots_all, las=las,
+                 eta=eta, y0=y0)
     return y, state
+
+
+def _saved_state(W1, W2, log_alphas, etas, phi_q, phi_k, y0, slots_all, ws):
+    """The forward state of :func:`_core_forward` rebuilt from the tensors a
+    forward op returned (the bf16 weight copies are made again)."""
+    las = [None] + ([] if log_alphas is None else
+                    [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
+    eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
+    return dict(W1b=W1.detach().to(torch.bfloat16).contiguous(), W2b=W2.detach().to(torch.bfloat16).contiguous(),
+                phi_q=phi_q, phi_k=phi_k, ws=ws, slots=list(slots_all.unbind(0)), las=las, eta=eta, y0=y0)
 
 
 def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out):
@@ -252,60 +264,10 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     return dict(dq=dq, dk=dk, dvaug=dvaug, dW1=dW1, dW2=dW2, dla=dla, deta=deta, **grads)
 
 
-class _KernelCore(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, spec, q, k, v, W1, W2, thr, bias, gain, scale, log_alphas, etas):
-        ctl = _controls(thr, bias, gain, scale)
-        y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, None)
-        ctx.spec, ctx.st, ctx.ctl = spec, st, ctl
-        ctx.dtypes = (q.dtype, k.dtype, v.dtype, W1.dtype, W2.dtype)
-        ctx.save_for_backward(q, k, v)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        q, k, v = ctx.saved_tensors
-        g = _core_backward(ctx.spec, q, k, v, ctx.st, ctx.ctl, dy, None, None, None, None)
-        qd, kd, vd, w1d, w2d = ctx.dtypes
-        d = q.shape[-1]
-        return (None, g["dq"].to(qd), g["dk"].to(kd), g["dvaug"][..., :d].to(vd), g["dW1"].to(w1d),
-                g["dW2"].to(w2d), g["thr"], g["bias"], g["gain"], g["scale"], g["dla"], g["deta"])
-
-
 def _qkv_views(qkv, H, d):
     B, T = qkv.shape[:2]
     q, k, v = qkv.view(B, T, 3, H, d).permute(2, 0, 3, 1, 4)
     return q, k, v
-
-
-class _KernelCoreQKV(torch.autograd.Function):
-    """The hot path from the raw fused projection ``qkv [B,T,3Hd]``: RoPE and
-    L2 norm run inside the feature kernels, v is read in place, and the
-    backward writes the q, k and v gradients straight into ``d qkv``."""
-
-    @staticmethod
-    def forward(ctx, spec, prologue, H, qkv, W1, W2, thr, bias, gain, scale, log_alphas, etas):
-        d = qkv.shape[-1] // (3 * H)
-        q, k, v = _qkv_views(qkv, H, d)
-        ctl = _controls(thr, bias, gain, scale)
-        y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue)
-        ctx.spec, ctx.prologue, ctx.H, ctx.st, ctx.ctl = spec, prologue, H, st, ctl
-        ctx.dtypes = (W1.dtype, W2.dtype)
-        ctx.save_for_backward(qkv)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        (qkv,) = ctx.saved_tensors
-        H = ctx.H
-        d = qkv.shape[-1] // (3 * H)
-        q, k, v = _qkv_views(qkv, H, d)
-        dqkv = torch.empty_like(qkv)
-        dq, dk, dv = _qkv_views(dqkv, H, d)
-        g = _core_backward(ctx.spec, q, k, v, ctx.st, ctx.ctl, dy, ctx.prologue, dq, dk, dv)
-        w1d, w2d = ctx.dtypes
-        return (None, None, None, dqkv, g["dW1"].to(w1d), g["dW2"].to(w2d), g["thr"], g["bias"], g["gain"],
-                g["scale"], g["dla"], g["deta"])
 
 
 class _ShardScan:
@@ -804,8 +766,15 @@ def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None,
         raise ValueError("kernel_core_qkv: log_alphas are required exactly for a bank (mode fast/stale)")
     if spec.read != "key_mass":
         raise NotImplementedError("kernel_core_qkv: the fused projection path reads with key mass; use kernel_core")
-    return _KernelCoreQKV.apply(spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain, spline_scale,
-                                log_alphas, etas)
+    from . import ops  # noqa: F401  (registers the operators)
+    rot = prologue.rot if prologue is not None else 0
+    outs = torch.ops.thetascan_b200.kernel_mixer_qkv_fwd(
+        qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas,
+        prologue.cos if rot else None, prologue.sin if rot else None, H, rot,
+        -1.0 if prologue is None or prologue.l2norm_eps is None else float(prologue.l2norm_eps),
+        spec.kind, spec.mode, float(spec.eps), float(spec.gain), int(spec.basis), float(spec.bound),
+        float(spec.spline_scale))
+    return outs[0]
 
 
 def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias=None, gain=None,
@@ -832,4 +801,8 @@ def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias
     if spec.read != "key_mass":
         return _KernelCoreViews.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale,
                                       log_alphas, etas)
-    return _KernelCore.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas)
+    from . import ops  # noqa: F401  (registers the operators)
+    outs = torch.ops.thetascan_b200.kernel_mixer_fwd(
+        q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, spec.kind, spec.mode,
+        float(spec.eps), float(spec.gain), int(spec.basis), float(spec.bound), float(spec.spline_scale))
+    return outs[0]

@@ -269,17 +269,19 @@ class ThetaScanCore(nn.Module):
         # the projection GEMMs under TF32 (recomputed in the backward); RoPE
         # and the L2 norm have no GEMM, so they run once under plain autograd
         q, k, v = per_token(qkv, xf, *[params[n] for n in names])
-        q, k = _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base))
+        gn = self.cfg.gn
+        eps = 1e-6 if gn.damping is None else float(gn.damping)
+        q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
-        gn = self.cfg.gn
         y = gn_core(q, k, v, W1, W2, None if self.Wg is None else self.Wg[0],
                     nonlin="relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity,
                     read_norm=gn.read_normalization != "none",
                     read_norm_w1=gn.read_normalization == "both_feature_mass",
-                    log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum")
+                    log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum",
+                    eps=eps)
         y = y.transpose(1, 2)
 
         def out(yy, xx, w_out, *gate):

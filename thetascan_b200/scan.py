@@ -71,90 +71,77 @@ def _workspace(lib, fn, args, device):
     return torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
-class _ScanViews(torch.autograd.Function):
-    """Autograd wrapper of the multi-view scan kernels."""
-
-    @staticmethod
-    def forward(ctx, q, k, v, append_unit, out_dtype, stale, *retentions):
-        lib = _lib.load()
-        las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
-        B, H, T, _ = q.shape
-        dv = v.shape[-1] + (1 if append_unit else 0)
-        # The kernels write f32 reads; the backward's log-retention term uses
-        # them unrounded, and the caller gets them in the stream dtype.
-        outs = [torch.empty(B, H, T, dv, dtype=torch.float32, device=q.device) for _ in las]
-        args = _build_args(q, k, v, las, outs, append_unit, stale=stale)
-        ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
-        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
-        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
-        ctx.append_unit = append_unit
-        ctx.stale = stale
-        ctx.grad_dtypes = (q.dtype, k.dtype, v.dtype)
-        ctx.n_ret = len(las)
-        ctx.ret_present = [r is not None for r in retentions]
-        ctx.ret_dtypes = [None if r is None else r.dtype for r in retentions]
-        ctx.ret_shapes = [None if r is None else r.shape for r in retentions]
-        saved_las = [la if la is not None else torch.empty(0, device=q.device) for la in las]
-        ctx.save_for_backward(q, k, v, ws, *outs, *saved_las)
-        return tuple(o.to(out_dtype) for o in outs)
-
-    @staticmethod
-    def backward(ctx, *douts):
-        lib = _lib.load()
-        n = ctx.n_ret
-        saved = ctx.saved_tensors
-        q, k, v, ws = saved[:4]
-        outs = list(saved[4:4 + n])
-        las = [la if present else None for la, present in zip(saved[4 + n:4 + 2 * n], ctx.ret_present)]
-        B, H, T, Dk = q.shape
-        dv_width = outs[0].shape[-1]
-        # bf16 streams take bf16 read gradients; f32 streams keep them f32
-        gdt = torch.float32 if q.dtype == torch.float32 else torch.bfloat16
-        dgrads = [torch.zeros(B, H, T, dv_width, dtype=gdt, device=q.device) if d is None
-                  else d.to(gdt).contiguous() for d in douts]
-        args = _build_args(q, k, v, las, outs, ctx.append_unit, ws, stale=ctx.stale)
-        g = _lib.ScanGradArgs()
-        dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
-        dk = torch.empty_like(dq)
-        dvv = torch.empty(B, H, T, dv_width, dtype=torch.float32, device=q.device)
-        dlas = [None if la is None else torch.zeros(H, dtype=torch.float32, device=q.device) for la in las]
-        for i in range(n):
-            g.dout[i] = dgrads[i].data_ptr()
-            g.dlog_alpha[i] = None if dlas[i] is None else dlas[i].data_ptr()
-        g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dvv.data_ptr()
-        g.grad_dtype = _lib.TS_DTYPE_F32
-        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, args, q.device)
-        g.workspace, g.workspace_bytes = gws.data_ptr(), gws.numel()
-        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(args), ctypes.byref(g), _stream()))
-        if ctx.append_unit:
-            dvv = dvv[..., :-1]
-        ret_grads = []
-        for dla, dtype, shape in zip(dlas, ctx.ret_dtypes, ctx.ret_shapes):
-            ret_grads.append(None if dla is None else dla.to(dtype).reshape(shape))
-        qd, kd, vd = ctx.grad_dtypes
-        return (dq.to(qd), dk.to(kd), dvv.to(vd), None, None, None, *ret_grads)
+def _scan_fwd_impl(q, k, v, retentions, append_unit, stale, round_streams):
+    """Body of the ``thetascan_b200::scan_views_fwd`` op: f32 reads of every
+    retention, stacked ``[R,B,H,T,Dv(+unit)]``, and the workspace that holds
+    the carried chunk states for the backward."""
+    lib = _lib.load()
+    if round_streams:
+        q, k, v = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    B, H, T, _ = q.shape
+    dv = v.shape[-1] + append_unit
+    # The kernels write f32 reads; the backward's log-retention term uses
+    # them unrounded, and the caller casts them to the stream dtype.
+    outs_all = torch.empty(len(las), B, H, T, dv, dtype=torch.float32, device=q.device)
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, stale=stale if any(stale) else None)
+    ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
+    return outs_all, ws
 
 
-class _ScanViewsFromF32(torch.autograd.Function):
+def _scan_bwd_impl(douts, q, k, v, retentions, outs_all, ws, append_unit, stale, round_streams):
+    """Body of the ``thetascan_b200::scan_views_bwd`` op: f32 gradients of q,
+    k, v (without the unit columns) and ``[R,H]`` log-retention gradients."""
+    lib = _lib.load()
+    if round_streams:
+        q, k, v = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    n = len(las)
+    B, H, T, Dk = q.shape
+    dv_width = outs_all.shape[-1]
+    # bf16 streams take bf16 read gradients; f32 streams keep them f32
+    gdt = torch.float32 if q.dtype == torch.float32 else torch.bfloat16
+    dgrads = [douts[i].to(gdt).contiguous() for i in range(n)]
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, ws, stale=stale if any(stale) else None)
+    g = _lib.ScanGradArgs()
+    dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
+    dk = torch.empty_like(dq)
+    dvv = torch.empty(B, H, T, dv_width, dtype=torch.float32, device=q.device)
+    dla = torch.zeros(n, H, dtype=torch.float32, device=q.device)
+    for i in range(n):
+        g.dout[i] = dgrads[i].data_ptr()
+        g.dlog_alpha[i] = None if las[i] is None else dla[i].data_ptr()
+    g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dvv.data_ptr()
+    g.grad_dtype = _lib.TS_DTYPE_F32
+    gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, args, q.device)
+    g.workspace, g.workspace_bytes = gws.data_ptr(), gws.numel()
+    _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(args), ctypes.byref(g), _stream()))
+    if append_unit:
+        dvv = dvv[..., :v.shape[-1]].contiguous()
+    return dq, dk, dvv, dla
+
+
+def _scan_views_op(q, k, v, retentions, append_unit, stale, round_streams):
+    """The multi-view scan as the ``thetascan_b200::scan_views_fwd`` custom op
+    (autograd and fake implementation registered in :mod:`thetascan_b200.ops`);
+    returns the f32 reads of every retention."""
+    from . import ops  # noqa: F401  (registers the operators)
+    outs_all, _ = torch.ops.thetascan_b200.scan_views_fwd(
+        q, k, v, [r for r in retentions if r is not None], [r is not None for r in retentions], int(append_unit),
+        [bool(x) for x in stale], bool(round_streams))
+    return outs_all.unbind(0)
+
+
+def scan_views_f32(q, k, v, append_unit, stale, retentions):
     """The multi-view scan of float32 q, k, v on bf16 streams: the inputs are
-    rounded to bf16 here (what the tensor-core kernels read), the reads are
+    rounded to bf16 inside (what the tensor-core kernels read), the reads are
     f32, and the gradients return in float32 as the kernels write them, with
     no bf16 round trip on the way back.  Used by callers whose per-token math
     around the scan is float32 (the GN family)."""
-
-    @staticmethod
-    def forward(ctx, q, k, v, append_unit, stale, *retentions):
-        bf = torch.bfloat16
-        outs = _ScanViews.forward(ctx, q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(),
-                                  append_unit, torch.float32, stale, *retentions)
-        ctx.grad_dtypes = (q.dtype, k.dtype, v.dtype)
-        return outs
-
-    @staticmethod
-    def backward(ctx, *douts):
-        grads = _ScanViews.backward(ctx, *douts)
-        # drop the out_dtype slot of _ScanViews' signature
-        return grads[:4] + grads[5:]
+    flags = [bool(x) for x in stale] if stale is not None else [False] * len(retentions)
+    return tuple(_scan_views_op(q, k, v, retentions, append_unit, flags, True))
 
 
 def _check_inputs(q, k, v, retentions, chunk):
@@ -211,7 +198,7 @@ def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_uni
     for start in range(0, len(retentions), _lib.MAX_RETENTIONS):
         group = tuple(retentions[start:start + _lib.MAX_RETENTIONS])
         flags = stale[start:start + _lib.MAX_RETENTIONS]
-        outs.extend(_ScanViews.apply(q, k, v, append_unit, q.dtype, flags if any(flags) else None, *group))
+        outs.extend(o.to(q.dtype) for o in _scan_views_op(q, k, v, group, int(append_unit), flags, False))
     return tuple(outs)
 
 
