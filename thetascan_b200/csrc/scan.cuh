@@ -81,6 +81,10 @@ struct ScanGradParams {
   int store;                 // the reverse prefix writes G, images and its log-retention terms
   int zero_start_final;      // dfinal is the gradient of the final state from a zero start
   float* gsegs;              // [B,H,R,NS,DkM,DvP] f32: segment totals of the reverse prefix (NS > 0)
+  // The reverse chain (scan_bwd_chain.cu) ran: the dv kernel adds the
+  // key-weight term of the log-retention gradient, <G_n, B'(n)>, from its
+  // per-row cross products.
+  int key_dla_in_dv;
 };
 
 __device__ __forceinline__ float head_la(const ScanParams& p, int r, int h) {

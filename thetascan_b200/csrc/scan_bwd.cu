@@ -1107,6 +1107,12 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
     });
     if (cross && fold) {
       const float u = slot_key_weight(p, r, la, rows, row);
+      // With the reverse chain, the key-weight term of the log-retention
+      // gradient, <G_n, B'(n)> = sum_j (len-1-j) u(j) (k_j G_n) . [v_j], from
+      // this row's cross product and payload row.
+      const bool key_dla = g.key_dla_in_dv && want;
+      const float wk = key_dla ? slot_key_weight_dla(p, r, la, rows, row) : 0.f;
+      float kacc = 0.f;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int c = 16 * part + kChunkStep * k;
@@ -1115,6 +1121,17 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_dv_kernel(ScanParams p, Sca
         tmem_ld16(tmem_addr(t_x, quad * 32, c), v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) xacc[k][e] = fmaf(u, v[e], xacc[k][e]);
+        if (key_dla) {
+          float pl[16];
+          unpack8(tile_ld16(tv, row, c / 8), pl);
+          unpack8(tile_ld16(tv, row, c / 8 + 1), pl + 8);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) kacc = fmaf(v[e], pl[e], kacc);
+        }
+      }
+      if (key_dla) {
+        const float sum = block_sum(wk * kacc, red);
+        if (threadIdx.x == 0) atomicAdd(g.dla[r] + h, sum);
       }
     }
     if (want) {
@@ -1206,14 +1223,29 @@ size_t scan_bwd_max_smem(const ScanParams& p) {
 // The backward kernels; `tile_terms` runs the local per-tile terms, `grads`
 // the dq / dk / dv kernels (the stages of a sequence shard run them apart;
 // the reverse prefix runs in both).
-int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s, bool tile_terms, bool grads) {
+int launch_scan_bwd_chain(const ScanParams& p, const ScanGradParams& g, cudaStream_t s);
+
+// The backward kernels; `tile_terms` / `grads` select the parts that run (the
+// stages of a sequence shard run them separately).  The state gradients come
+// from the TMEM-resident reverse chain (scan_bwd_chain.cu) where it applies,
+// else from the per-tile local terms and the reverse tile prefix below.
+int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g_in, cudaStream_t s, bool tile_terms, bool grads) {
+  ScanGradParams g = g_in;
+  g.key_dla_in_dv = 0;
+  if (tile_terms && grads) {
+    const int chained = launch_scan_bwd_chain(p, g, s);
+    if (chained < 0) return -chained;
+    g.key_dla_in_dv = chained;
+  }
   const int nbuf = dqk_buffers(p);
   const size_t s_state = bstate_smem(p), s_dqk = dqk_smem(p, nbuf), s_dv = dv_smem(p);
   cudaFuncSetAttribute(scan_bwd_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_state));
   cudaFuncSetAttribute(scan_bwd_dqk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dqk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dqk));
   cudaFuncSetAttribute(scan_bwd_dv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s_dv));
-  if (tile_terms && (p.NT > 1 || g.all_tiles)) {
+  if (g.key_dla_in_dv) {
+    // the reverse chain wrote every G image and its log-retention terms
+  } else if (tile_terms && (p.NT > 1 || g.all_tiles)) {
     if (bstate2_fits(p)) {
       const size_t s_state2 = bstate2_smem(p);
       cudaFuncSetAttribute(scan_bwd_state2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1225,7 +1257,8 @@ int launch_scan_bwd(const ScanParams& p, const ScanGradParams& g, cudaStream_t s
       if (int e = check_launch("scan_bwd_state_kernel")) return e;
     }
   }
-  if (p.NS > 0) {
+  if (g.key_dla_in_dv) {
+  } else if (p.NS > 0) {
     const dim3 grid = seg_grid(p.DkM, p.DvP, p.R, p.B * p.H, p.NS);
     scan_bwd_prefix_seg_kernel<<<grid, seg_threads(p.DkM), 0, s>>>(p, g);
     if (int e = check_launch("scan_bwd_prefix_seg_kernel")) return e;

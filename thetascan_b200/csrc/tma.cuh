@@ -55,8 +55,24 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` contiguous bytes (multiple of 16; both
+// addresses 16-byte aligned) from global memory into shared memory, counted
+// on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Byte offset of the 16-byte chunk `c8` (columns 8 c8 .. 8 c8 + 7) of row
+// `row` inside a 128-byte-swizzled box (1024-byte aligned): the chunk index
+// is XORed with the row's position in its 8-row group.
+__device__ __forceinline__ uint32_t sw128_offset(int row, int c8) {
+  return static_cast<uint32_t>(row) * kSwRow + static_cast<uint32_t>((c8 ^ (row & 7)) * 16);
 }
 
 // Shared-memory descriptor of a 128-byte-swizzled operand (layout type 2).
