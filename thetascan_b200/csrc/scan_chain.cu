@@ -1,11 +1,12 @@
 // Forward tile states of the multi-view scan as one sequential chain per
 // (batch, head): the f32 state of every retention slot stays in tensor memory
 // from the first tile to the last, so no per-tile update or carried state
-// makes a round trip through HBM.  Per tile n, with C_n = e^{la len_n}:
-//   S_in(n) (TMEM)  -> bf16 image and (decayed slots) f32 copy for the reads
-//                      and the backward, written straight from registers;
-//   S <- C_n S_in(n)                                    (TMEM, in place)
-//   S += k_n^T (u_r o [v_n | 1])                        (tcgen05, into S)
+// makes a round trip through HBM.  Per tile n and slot r, with
+// C_n = e^{la_r len_n}:
+//   S_in(n)  -> bf16 image and (decayed slots) f32 copy for the reads and the
+//               backward, written straight from registers;
+//   S <- C_n S_in(n)                                      (TMEM, in place)
+//   S += k_n^T (u_r o [v_n | 1])                          (tcgen05, into S)
 // which is the exclusive tile prefix of the reference chunk backend
 // (src/thetascan/_core/ops/scan_chunk.py:170-212: per-tile update with the
 // key weights of the leaving state, carried by the tile's closing factor),
@@ -14,13 +15,15 @@
 // applies: slots without a stale view, payload widths of whole 64-column
 // boxes plus up to two unit columns, and states that fit the 512 TMEM columns.
 //
-// Warp roles (160 threads):
-//   warp 0, lane 0  TMA loads of the key and payload tiles into a two-stage
-//                   ring (128-byte-swizzled boxes, tensor maps of this GPU's
-//                   own memory, no multicast) and the tcgen05 MMA issue;
+// The slots are interleaved: slot r's update product of tile n runs while the
+// epilogue writes out slot r + 1, and the key and payload tiles run through a
+// two-stage load ring, so loads, products and the write-out overlap.  Warp
+// roles (160 threads):
+//   warp 0, lane 0  TMA loads (128-byte-swizzled boxes, tensor maps of this
+//                   GPU's own memory, no multicast) and the tcgen05 MMA issue;
 //   warps 1-4       epilogue: one TMEM lane quadrant each (warp w reads lanes
-//                   32 (w % 4) ..), the weighted payload tiles of every slot,
-//                   the state images / copies and the closing rescale.
+//                   32 (w % 4) ..): each slot's weighted payload tile, the
+//                   state write-out and the closing rescale.
 // Every wait is bounded; a wait that gives up records a device error and the
 // CTA drains its own copies and MMAs in flight before it frees TMEM and exits.
 #include "capi_internal.h"
@@ -36,8 +39,7 @@ constexpr int kChainThreads = 160;
 struct ChainLayout {
   int kboxes, vboxes;       // 64-column boxes of a key tile (DkM / 64) and a payload tile
   uint32_t k_bytes, v_bytes;
-  uint32_t stage_bytes;     // one stage of the load ring: key tile then payload tile
-  uint32_t unit_bytes;      // unit-column tile of one slot (128 rows x 16 columns, no swizzle)
+  uint32_t stage_bytes;     // one stage of the load ring: key tile, then payload tile
   uint32_t wv_bytes;        // one slot's weighted payload: swizzled boxes, then its unit tile
   uint32_t off_wv, total;   // byte offsets from the 1024-aligned base
 };
@@ -49,8 +51,7 @@ __host__ __device__ inline ChainLayout chain_layout(int DkM, int dv_boxes, int v
   L.k_bytes = L.kboxes * kSwBox;
   L.v_bytes = L.vboxes * kSwBox;
   L.stage_bytes = L.k_bytes + L.v_bytes;
-  L.unit_bytes = v_unit ? kTile * 16 * 2 : 0;
-  L.wv_bytes = L.v_bytes + L.unit_bytes;
+  L.wv_bytes = L.v_bytes + (v_unit ? kTile * 16 * 2 : 0);
   L.off_wv = 2 * L.stage_bytes;
   L.total = L.off_wv + R * L.wv_bytes;
   return L;
@@ -61,9 +62,10 @@ __device__ __forceinline__ uint32_t chain_tmem_cols(int n) {
 }
 
 struct ChainShared {
-  uint64_t full[2];   // stage s loaded (transaction bytes)
-  uint64_t mma;       // this tile's state updates complete
-  uint64_t epi;       // the epilogue has prepared this tile (128 arrivals)
+  // Each barrier runs at most one phase ahead of every thread that waits on it.
+  uint64_t full[2];                 // stage s holds its tile's key and payload rows
+  uint64_t epi[TS_MAX_RETENTIONS];  // slot r of the tile is written out and its payload built (128 arrivals)
+  uint64_t mma[TS_MAX_RETENTIONS];  // slot r's update product of the tile is complete
   uint32_t tmem;
   int abort;
 };
@@ -78,17 +80,19 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.H, h = blockIdx.x % p.H;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const int dv_boxes = (p.Dv - p.v_unit) / 64;
-  const ChainLayout L = chain_layout(p.DkM, dv_boxes, p.v_unit, p.R);
+  const ChainLayout L = chain_layout(p.DkM, (p.Dv - p.v_unit) / 64, p.v_unit, p.R);
   const int mblocks = p.DkM / kTile;
-  const uint32_t ncols = chain_tmem_cols(p.R * mblocks * p.DvP);
+  const int region = mblocks * p.DvP;          // TMEM columns of one slot's state
+  const uint32_t ncols = chain_tmem_cols(p.R * region);
   const int NT = p.NT;
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.full[0], 1);
     mbar_init(&sh.full[1], 1);
-    mbar_init(&sh.mma, 1);
-    mbar_init(&sh.epi, 4 * 32);
+    for (int r = 0; r < TS_MAX_RETENTIONS; ++r) {
+      mbar_init(&sh.epi[r], 4 * 32);
+      mbar_init(&sh.mma[r], 1);
+    }
     sh.abort = 0;
     fence_mbar_init();
     tma_prefetch_map(&map_k);
@@ -104,34 +108,31 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     if (lane == 0) {
       // ---------------------------------------------------------------- loads + MMA
       auto issue_load = [&](int n) {
-        const int s = n & 1;
-        uint64_t* bar = &sh.full[s];
+        uint64_t* bar = &sh.full[n & 1];
+        const uint32_t dst = base + (n & 1) * L.stage_bytes;
         mbar_expect_tx(bar, L.stage_bytes);
-        const uint32_t dst = base + s * L.stage_bytes;
         for (int i = 0; i < L.kboxes; ++i) tma_load_4d(dst + i * kSwBox, &map_k, i * 64, n * kTile, h, b, bar);
         for (int i = 0; i < L.vboxes; ++i)
           tma_load_4d(dst + L.k_bytes + i * kSwBox, &map_v, i * 64, n * kTile, h, b, bar);
       };
       int last_load[2] = {-1, -1};
-      int committed = -1;
+      int commits = 0;
       bool ok = true;
-      issue_load(0);
-      last_load[0] = 0;
-      if (NT > 1) {
-        issue_load(1);
-        last_load[1] = 1;
+      for (int n = 0; n < 2 && n < NT; ++n) {
+        issue_load(n);
+        last_load[n] = n;
       }
       const uint32_t id_v = idesc_bf16(kTile, 64 * L.vboxes, true, true);
       const uint32_t id_u = idesc_bf16(kTile, 16, true, true);
       for (int n = 0; n < NT && ok; ++n) {
-        ok = mbar_wait(&sh.epi, n & 1, kErrMmaTimeout);
-        if (!ok || *(volatile int*)&sh.abort) break;
-        tc_fence_after();
         const uint32_t kaddr = base + (n & 1) * L.stage_bytes;
-        for (int r = 0; r < p.R; ++r) {
+        for (int r = 0; r < p.R && ok; ++r) {
+          ok = mbar_wait(&sh.epi[r], n & 1, kErrMmaTimeout);
+          if (!ok || *(volatile int*)&sh.abort) break;
+          tc_fence_after();
           const uint32_t wv = base + L.off_wv + r * L.wv_bytes;
           for (int mb = 0; mb < mblocks; ++mb) {
-            const uint32_t d = tmem + static_cast<uint32_t>((r * mblocks + mb) * p.DvP);
+            const uint32_t d = tmem + static_cast<uint32_t>(r * region + mb * p.DvP);
 #pragma unroll 1
             for (int ks = 0; ks < kTile / 16; ++ks) {
               // A = k^T (features x tokens): MN-major, 64-feature boxes LBO apart
@@ -144,28 +145,35 @@ __global__ void __launch_bounds__(kChainThreads, 1)
               }
             }
           }
+          mma_commit(&sh.mma[r]);
+          ++commits;
         }
-        mma_commit(&sh.mma);
-        committed = n;
+        if (!ok || *(volatile int*)&sh.abort) break;
         if (n + 2 < NT) {
-          // stage n & 1 is free once this tile's products have read it
-          ok = mbar_wait(&sh.mma, n & 1, kErrMmaTimeout);
+          // stage n & 1 is free once the tile's last product has read the key
+          // tile (commits complete in issue order; the epilogue consumed the
+          // payload tile before it handed over)
+          ok = mbar_wait(&sh.mma[p.R - 1], n & 1, kErrMmaTimeout);
           if (!ok) break;
           issue_load(n + 2);
           last_load[n & 1] = n + 2;
         }
       }
       if (!ok) *(volatile int*)&sh.abort = 1;
-      // Drain: every issued load has landed and the last products are done
-      // before the CTA frees its tensor memory and exits.
-      for (int s = 0; s < 2; ++s)
-        if (last_load[s] >= 0) mbar_wait(&sh.full[s], (last_load[s] >> 1) & 1, kErrCopyTimeout);
-      if (committed >= 0) mbar_wait(&sh.mma, committed & 1, kErrMmaTimeout);
+      // Drain: every issued load has landed and every product is done before
+      // the CTA frees its tensor memory and exits.
+      for (int st = 0; st < 2; ++st)
+        if (last_load[st] >= 0) mbar_wait(&sh.full[st], (last_load[st] >> 1) & 1, kErrCopyTimeout);
+      if (commits > 0) {
+        const int tiles_done = (commits + p.R - 1) / p.R;   // the last tile reached, partly or fully
+        const int last_r = (commits - 1) % p.R;
+        mbar_wait(&sh.mma[last_r], (tiles_done - 1) & 1, kErrMmaTimeout);
+      }
     }
   } else {
     // -------------------------------------------------------------------- epilogue
     const int quad = warp & 3;
-    const int lrow = 32 * quad + lane;   // TMEM lane = token row of the payload tiles = feature row of a state block
+    const int lrow = 32 * quad + lane;   // TMEM lane = token row of the payload tile = feature row of a state block
     bool ok = true;
     // S_in(0): the initial state, or zero.
     for (int r = 0; r < p.R; ++r)
@@ -177,34 +185,43 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           for (int e = 0; e < 16; ++e)
             v[e] = (p.init != nullptr && f < p.Dk && c + e < p.Dv)
                        ? __ldg(p.init + boundary_index(p, b, h, r, f, c + e)) : 0.f;
-          tmem_st16(tmem_addr(tmem, 32 * quad, (r * mblocks + mb) * p.DvP + c), v);
+          tmem_st16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
         }
       }
-    for (int n = 0; n < NT; ++n) {
-      const int s = n & 1;
+    for (int n = 0; n < NT && ok; ++n) {
       const int len = tile_len(p, n);
-      if (ok) ok = mbar_wait(&sh.full[s], (n >> 1) & 1, kErrCopyTimeout);
-      if (ok && n > 0) ok = mbar_wait(&sh.mma, (n - 1) & 1, kErrMmaTimeout);
-      if (!ok || *(volatile int*)&sh.abort) {
-        *(volatile int*)&sh.abort = 1;
-        break;
-      }
-      tc_fence_after();
-      // Weighted payloads u_r(j) [v_j | 1] of every slot (row j = lrow).  A
-      // swizzled row is one 128-byte line whatever its chunk order, so the
-      // row scaling ignores the swizzle.
-      const uint32_t vrow = base + s * L.stage_bytes + L.k_bytes + lrow * kSwRow;
-      for (int r = 0; r < p.R; ++r) {
-        const float u = slot_key_weight(p, r, head_la(p, r, h), len, lrow);
+      ok = mbar_wait(&sh.full[n & 1], (n >> 1) & 1, kErrCopyTimeout);
+      if (!ok) break;
+      const uint32_t vrow = base + (n & 1) * L.stage_bytes + L.k_bytes + lrow * kSwRow;
+      for (int r = 0; r < p.R && ok; ++r) {
+        const bool decayed = p.la[r] != nullptr;
+        const float la = head_la(p, r, h);
+        // S_in(n) of this slot is complete (and its payload buffer free) once
+        // the previous tile's product of this slot is
+        if (n > 0) ok = mbar_wait(&sh.mma[r], (n - 1) & 1, kErrMmaTimeout);
+        if (!ok || *(volatile int*)&sh.abort) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // Weighted payload u(j) [v_j | 1] (row j = lrow).  A swizzled row is
+        // one 128-byte line whatever its chunk order, so the row scaling
+        // ignores the swizzle; each lane walks its row's chunks from its own
+        // starting chunk (row % 8), so the 8 lanes of a shared-memory phase
+        // touch 8 different bank groups.
+        const float u = slot_key_weight(p, r, la, len, lrow);
         const uint32_t wv = base + L.off_wv + r * L.wv_bytes;
         for (int i = 0; i < L.vboxes; ++i) {
+          uint4 raw[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) raw[c] = ld_shared_v4(vrow + i * kSwBox + ((c ^ (lrow & 7)) * 16));
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             float f8[8];
-            unpack8(ld_shared_v4(vrow + i * kSwBox + c * 16), f8);
+            unpack8(raw[c], f8);
 #pragma unroll
             for (int e = 0; e < 8; ++e) f8[e] *= u;
-            st_shared_v4(wv + i * kSwBox + lrow * kSwRow + c * 16, pack8(f8));
+            st_shared_v4(wv + i * kSwBox + lrow * kSwRow + ((c ^ (lrow & 7)) * 16), pack8(f8));
           }
         }
         if (p.v_unit) {
@@ -214,13 +231,9 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           st_shared_v4(wv + L.v_bytes + lrow * 16, make_uint4(pack_bf16(u, w1), 0u, 0u, 0u));
           st_shared_v4(wv + L.v_bytes + kTile * 16 + lrow * 16, make_uint4(0u, 0u, 0u, 0u));
         }
-      }
-      fence_async_smem();
-      // S_in(n) out (images for the reads, f32 copies of decayed slots for
-      // the backward), then the closing rescale in place.
-      for (int r = 0; r < p.R; ++r) {
-        const bool decayed = p.la[r] != nullptr;
-        const float la = head_la(p, r, h);
+        fence_async_smem();
+        // S_in(n) out (the image for the reads, an f32 copy of a decayed slot
+        // for the backward), then the closing rescale in place.
         const float closing = decayed ? __expf(la * static_cast<float>(len)) : 1.f;
         const size_t si = state_index(p, b, h, n, r);
         float* st = p.states + si * p.DkM * p.DvP;
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           const int f = mb * kTile + lrow;
           const int f0 = f & ~7;
           for (int c = 0; c < p.DvP; c += 16) {
-            const uint32_t ta = tmem_addr(tmem, 32 * quad, (r * mblocks + mb) * p.DvP + c);
+            const uint32_t ta = tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c);
             float v[16];
             tmem_ld16(ta, v);
             if (p.store) {
@@ -255,13 +268,14 @@ __global__ void __launch_bounds__(kChainThreads, 1)
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(&sh.epi[r]);
       }
-      tc_fence_before();
-      mbar_arrive(&sh.epi);
     }
-    // The final state, after the last tile's update.
-    if (ok && !*(volatile int*)&sh.abort && p.final_state != nullptr) {
-      ok = mbar_wait(&sh.mma, (NT - 1) & 1, kErrMmaTimeout);
+    if (!ok) *(volatile int*)&sh.abort = 1;
+    // The final state, after the last tile's updates.
+    if (ok && p.final_state != nullptr) {
+      for (int r = 0; r < p.R && ok; ++r) ok = mbar_wait(&sh.mma[r], (NT - 1) & 1, kErrMmaTimeout);
       tc_fence_after();
       if (ok) {
         for (int r = 0; r < p.R; ++r)
@@ -269,7 +283,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
             const int f = mb * kTile + lrow;
             for (int c = 0; c < p.DvP; c += 16) {
               float v[16];
-              tmem_ld16(tmem_addr(tmem, 32 * quad, (r * mblocks + mb) * p.DvP + c), v);
+              tmem_ld16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
               if (f < p.Dk) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
