@@ -5,23 +5,26 @@
 //   dSloc(n) = sum_t c(i) q_t^T dout_t                    (tcgen05, into G)
 // the reverse of the forward recursion S_in(n+1) = C_n S_in(n) + dS(n)
 // (reference scan_chunk.py:170-212).  Per tile it writes the bf16 image of
-// G(n) that the dq/dk and dv kernels read, and it adds two terms of the
-// log-retention gradient of every decayed slot,
-//   carry    <S_in(n), sum_t (i+1) c(i) q_t^T dout_t>     (a second product
-//            into a scratch TMEM block, against the forward's f32 S_in(n))
+// G(n) that the dq/dk and dv kernels read, and for a decayed slot it adds two
+// terms of the log-retention gradient,
+//   carry    <S_in(n), sum_t (i+1) c(i) q_t^T dout_t>     (a second product,
+//            one 128-feature block at a time into a scratch TMEM block,
+//            against the forward's f32 S_in(n))
 //   closing  len_n C_n <G(n), S_in(n)>,
 // while the key-weight term <G(n), B'(n)> is formed by the dv kernel from its
 // per-row cross products (ScanGradParams.key_dla_in_dv).  It replaces the
 // per-tile local-term kernel and the HBM reverse prefix (f32 dSloc written,
 // re-read and rewritten per tile) where it applies: no stale slots, the whole
 // backward in one call (stage 0), payloads of whole 64-column boxes plus up
-// to two extra columns and at most 128 wide, states within tensor memory.
+// to two extra columns and at most 128 wide.
 //
-// Operands: the q tile by TMA (128-byte swizzle, this GPU's memory, no
-// multicast); every slot's raw dout rows by one untiled bulk copy; the
-// epilogue forms the weighted row operands c(i) dout (rounded to bf16) and,
-// for the carry term, (i+1) times that rounded row, in the swizzled MN-major
-// layout the tensor core reads.
+// Operands: q tiles by TMA (128-byte swizzle, this GPU's memory, no
+// multicast) through a two-stage ring; every slot's raw dout rows by one
+// untiled bulk copy per tile; the epilogue forms each slot's weighted row
+// operand c(i) dout (rounded to bf16) and, for the carry term first, (i+1)
+// times that rounded row, in the swizzled MN-major layout the tensor core
+// reads, in the slot's operand buffer.  The slots are interleaved: slot r's
+// dSloc product runs while the epilogue works on slot r + 1.
 //
 // Warp roles (160 threads): warp 0 lane 0 issues the copies and the MMAs;
 // warps 1-4 (one TMEM lane quadrant each) form operands and read G.  Every
@@ -39,10 +42,10 @@ constexpr int kBwdChainThreads = 160;
 
 struct BwdChainLayout {
   int qboxes, vboxes;
-  uint32_t q_bytes;        // q tile: DkM / 64 swizzled boxes
+  uint32_t q_bytes;        // one q tile: DkM / 64 swizzled boxes (two, a ring)
+  uint32_t op_bytes;       // one slot's row operand: swizzled boxes + 16-column unit tile
   uint32_t raw_bytes;      // one slot's raw dout rows (128 x Dv bf16, 16-byte multiple)
-  uint32_t op_bytes;       // one row operand: swizzled boxes + 16-column unit tile
-  uint32_t off_raw, off_op, off_x, total;
+  uint32_t off_op, off_raw, total;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
@@ -52,11 +55,10 @@ __host__ __device__ inline BwdChainLayout bwd_chain_layout(int DkM, int Dv, int 
   L.qboxes = DkM / 64;
   L.vboxes = (Dv - v_unit) / 64;
   L.q_bytes = L.qboxes * kSwBox;
-  L.raw_bytes = align_up(static_cast<uint32_t>(kTile * Dv * 2), 16);
   L.op_bytes = L.vboxes * kSwBox + (v_unit ? kTile * 16 * 2 : 0);
-  L.off_op = L.q_bytes;                                   // 1024-aligned
-  L.off_x = L.off_op + R * L.op_bytes;                    // 1024-aligned (op_bytes is)
-  L.off_raw = L.off_x + L.op_bytes;
+  L.raw_bytes = align_up(static_cast<uint32_t>(kTile * Dv * 2), 16);
+  L.off_op = 2 * L.q_bytes;                // 1024-aligned
+  L.off_raw = L.off_op + R * L.op_bytes;   // 1024-aligned (op_bytes is)
   L.total = L.off_raw + R * L.raw_bytes;
   return L;
 }
@@ -68,9 +70,10 @@ __device__ __forceinline__ uint32_t bwd_chain_tmem_cols(int n) {
 struct BwdChainShared {
   // Each barrier runs at most one phase ahead of every thread that waits on
   // it, so parity waits are exact:
-  uint64_t load;                      // q tile and raw dout rows of a tile landed
-  uint64_t epi_x;                     // the carry operand of a slot is ready (128 arrivals)
-  uint64_t mma_x;                     // the carry product is done
+  uint64_t load_q[2];                 // q ring stage s holds its tile
+  uint64_t load_raw;                  // the tile's raw dout rows of every slot landed
+  uint64_t epi_x;                     // a carry operand is ready / the scratch block is free (128 arrivals)
+  uint64_t mma_x;                     // a carry product is done
   uint64_t epi_g[TS_MAX_RETENTIONS];  // slot r's G pass is done and its dSloc operand ready
   uint64_t mma_g[TS_MAX_RETENTIONS];  // slot r's dSloc product is done
   uint32_t tmem;
@@ -127,6 +130,7 @@ __device__ __forceinline__ void build_row_operand(uint32_t op, uint32_t raw_row,
 
 __global__ void __launch_bounds__(kBwdChainThreads, 1)
     scan_bwd_chain_kernel(ScanParams p, ScanGradParams g, const __grid_constant__ CUtensorMap map_q) {
+  constexpr int kMaxDvP = kTile;
   extern __shared__ uint8_t smem_raw[];
   __shared__ BwdChainShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,16 +139,18 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
   const int dvv = p.Dv - p.v_unit;
   const BwdChainLayout L = bwd_chain_layout(p.DkM, p.Dv, p.v_unit, p.R);
   const int mblocks = p.DkM / kTile;
-  const int region = mblocks * p.DvP;               // TMEM columns of one slot's G
-  const uint32_t t_x = static_cast<uint32_t>(p.R * region);   // scratch block after the G blocks
-  const uint32_t ncols = bwd_chain_tmem_cols(p.R * region + region);
+  const int region = mblocks * p.DvP;                  // TMEM columns of one slot's G
+  const uint32_t t_x = static_cast<uint32_t>(p.R * region);   // scratch block (one M block) after the G blocks
+  const uint32_t ncols = bwd_chain_tmem_cols(p.R * region + p.DvP);
   const int NT = p.NT;
   const int last_dla = g.dfinal != nullptr ? NT : NT - 1;   // tiles whose leaving state carries gradient
   auto local = [&](int n) { return n >= 1 || g.all_tiles; };
   auto want = [&](int r) { return p.la[r] != nullptr && g.dla[r] != nullptr; };
 
   if (threadIdx.x == 0) {
-    mbar_init(&sh.load, 1);
+    mbar_init(&sh.load_q[0], 1);
+    mbar_init(&sh.load_q[1], 1);
+    mbar_init(&sh.load_raw, 1);
     mbar_init(&sh.epi_x, 4 * 32);
     mbar_init(&sh.mma_x, 1);
     for (int r = 0; r < TS_MAX_RETENTIONS; ++r) {
@@ -164,76 +170,100 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- copies + MMA
-      auto issue_load = [&](int n) {
-        const int len = tile_len(p, n);
-        uint32_t bytes = L.q_bytes;
-        for (int r = 0; r < p.RU; ++r) bytes += static_cast<uint32_t>(len * p.Dv * 2);
-        mbar_expect_tx(&sh.load, bytes);
-        for (int i = 0; i < L.qboxes; ++i) tma_load_4d(base + i * kSwBox, &map_q, i * 64, n * kTile, h, b, &sh.load);
-        for (int r = 0; r < p.RU; ++r) {
+      // tiles are processed in the order k = 0 .. NT-1, tile n = NT-1-k
+      auto issue_q = [&](int k) {
+        const int n = NT - 1 - k;
+        uint64_t* bar = &sh.load_q[k & 1];
+        mbar_expect_tx(bar, L.q_bytes);
+        for (int i = 0; i < L.qboxes; ++i)
+          tma_load_4d(base + (k & 1) * L.q_bytes + i * kSwBox, &map_q, i * 64, n * kTile, h, b, bar);
+      };
+      auto issue_raw = [&](int k) {
+        const int n = NT - 1 - k;
+        const uint32_t bytes = static_cast<uint32_t>(tile_len(p, n) * p.Dv * 2);
+        mbar_expect_tx(&sh.load_raw, bytes * p.R);
+        for (int r = 0; r < p.R; ++r) {
           const __nv_bfloat16* src = g.dout[r] + ((static_cast<size_t>(b) * p.H + h) * p.T + n * kTile) * p.Dv;
-          bulk_load(base + L.off_raw + r * L.raw_bytes, src, static_cast<uint32_t>(len * p.Dv * 2), &sh.load);
+          bulk_load(base + L.off_raw + r * L.raw_bytes, src, bytes, &sh.load_raw);
         }
       };
       const uint32_t id_v = idesc_bf16(kTile, 64 * L.vboxes, true, true);
       const uint32_t id_u = idesc_bf16(kTile, 16, true, true);
-      // D (+)= q^T . op for every M block: A = q^T (features x tokens), MN-major.
-      auto product = [&](uint32_t d, uint32_t op, bool accumulate) {
-        for (int mb = 0; mb < mblocks; ++mb) {
+      // D (+)= q[:, block mb]^T . op: A = q^T (features x tokens), MN-major.
+      auto product = [&](uint32_t qaddr, uint32_t d, int mb, uint32_t op, bool accumulate) {
 #pragma unroll 1
-          for (int ks = 0; ks < kTile / 16; ++ks) {
-            const uint64_t ad = smem_desc_sw128(base + 2 * mb * kSwBox + ks * 16 * kSwRow, kSwBox, kSwGroup);
-            const uint64_t bd = smem_desc_sw128(op + ks * 16 * kSwRow, kSwBox, kSwGroup);
-            const uint32_t acc = (accumulate || ks > 0) ? 1u : 0u;
-            mma_bf16(d + mb * p.DvP, ad, bd, id_v, acc);
-            if (p.v_unit) {
-              const uint64_t ud = smem_desc(op + L.vboxes * kSwBox + ks * 256, 128, kTile * 16);
-              mma_bf16(d + mb * p.DvP + 64 * L.vboxes, ad, ud, id_u, acc);
-            }
+        for (int ks = 0; ks < kTile / 16; ++ks) {
+          const uint64_t ad = smem_desc_sw128(qaddr + 2 * mb * kSwBox + ks * 16 * kSwRow, kSwBox, kSwGroup);
+          const uint64_t bd = smem_desc_sw128(op + ks * 16 * kSwRow, kSwBox, kSwGroup);
+          const uint32_t acc = (accumulate || ks > 0) ? 1u : 0u;
+          mma_bf16(d, ad, bd, id_v, acc);
+          if (p.v_unit) {
+            const uint64_t ud = smem_desc(op + L.vboxes * kSwBox + ks * 256, 128, kTile * 16);
+            mma_bf16(d + 64 * L.vboxes, ad, ud, id_u, acc);
           }
         }
       };
       bool ok = true;
-      int loads = 0, nx = 0;
-      int ng[TS_MAX_RETENTIONS] = {0, 0, 0, 0};   // epi_g phases consumed = dSloc tiles seen, per slot
-      int cg[TS_MAX_RETENTIONS] = {0, 0, 0, 0};   // dSloc commits, per slot
-      issue_load(NT - 1);
-      ++loads;
-      for (int n = NT - 1; n >= 0 && ok; --n) {
+      int last_q[2] = {-1, -1}, raws = 0, nex = 0, nx = 0;
+      int ng[TS_MAX_RETENTIONS] = {0, 0, 0, 0};
+      issue_q(0);
+      last_q[0] = 0;
+      issue_raw(0);
+      ++raws;
+      if (NT > 1) {
+        issue_q(1);
+        last_q[1] = 1;
+      }
+      for (int k = 0; k < NT && ok; ++k) {
+        const int n = NT - 1 - k;
+        const uint32_t qaddr = base + (k & 1) * L.q_bytes;
+        ok = mbar_wait(&sh.load_q[k & 1], (k >> 1) & 1, kErrCopyTimeout);   // the tile's q landed
+        if (!ok) break;
         for (int r = 0; r < p.R && ok; ++r) {
+          const uint32_t op = base + L.off_op + r * L.op_bytes;
           if (want(r) && local(n)) {
-            ok = mbar_wait(&sh.epi_x, nx & 1, kErrMmaTimeout);
-            ++nx;
+            for (int mb = 0; mb < mblocks && ok; ++mb) {
+              ok = mbar_wait(&sh.epi_x, nex & 1, kErrMmaTimeout);
+              ++nex;
+              if (!ok || *(volatile int*)&sh.abort) break;
+              tc_fence_after();
+              product(qaddr, tmem + t_x, mb, op, false);
+              mma_commit(&sh.mma_x);
+              ++nx;
+            }
             if (!ok || *(volatile int*)&sh.abort) break;
-            tc_fence_after();
-            product(tmem + t_x, base + L.off_x, false);
-            mma_commit(&sh.mma_x);
           }
-          ok = mbar_wait(&sh.epi_g[r], ng[r] & 1, kErrMmaTimeout);
-          ++ng[r];
+          ok = mbar_wait(&sh.epi_g[r], k & 1, kErrMmaTimeout);
           if (!ok || *(volatile int*)&sh.abort) break;
           tc_fence_after();
           if (local(n)) {
-            product(tmem + static_cast<uint32_t>(r * region), base + L.off_op + r * L.op_bytes, true);
+            for (int mb = 0; mb < mblocks; ++mb)
+              product(qaddr, tmem + static_cast<uint32_t>(r * region + mb * p.DvP), mb, op, true);
             mma_commit(&sh.mma_g[r]);
-            ++cg[r];
+            ++ng[r];
+          }
+          // every slot's raw rows are consumed once the last slot handed over
+          if (r == p.R - 1 && k + 1 < NT) {
+            issue_raw(k + 1);
+            ++raws;
           }
         }
-        if (!ok) break;
-        if (n > 0) {
-          // the tile's q and raw rows are consumed once its last product is
-          // done (commits complete in issue order)
-          ok = mbar_wait(&sh.mma_g[p.R - 1], (cg[p.R - 1] - 1) & 1, kErrMmaTimeout);
+        if (!ok || *(volatile int*)&sh.abort) break;
+        if (k + 2 < NT) {
+          // this q stage is free once the tile's last product has read it
+          ok = mbar_wait(&sh.mma_g[p.R - 1], (ng[p.R - 1] - 1) & 1, kErrMmaTimeout);
           if (!ok) break;
-          issue_load(n - 1);
-          ++loads;
+          issue_q(k + 2);
+          last_q[k & 1] = k + 2;
         }
       }
       if (!ok) *(volatile int*)&sh.abort = 1;
-      // drain: the last load and every slot's last product
-      mbar_wait(&sh.load, (loads - 1) & 1, kErrCopyTimeout);
+      // drain: every copy has landed and every product is done
+      for (int st = 0; st < 2; ++st)
+        if (last_q[st] >= 0) mbar_wait(&sh.load_q[st], (last_q[st] >> 1) & 1, kErrCopyTimeout);
+      mbar_wait(&sh.load_raw, (raws - 1) & 1, kErrCopyTimeout);
       for (int r = 0; r < p.R; ++r)
-        if (cg[r] > 0) mbar_wait(&sh.mma_g[r], (cg[r] - 1) & 1, kErrMmaTimeout);
+        if (ng[r] > 0) mbar_wait(&sh.mma_g[r], (ng[r] - 1) & 1, kErrMmaTimeout);
       if (nx > 0) mbar_wait(&sh.mma_x, (nx - 1) & 1, kErrMmaTimeout);
     }
   } else {
@@ -241,8 +271,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
     const int quad = warp & 3;
     const int lrow = 32 * quad + lane;   // token row of the operands, feature row of a G block
     bool ok = true;
-    int loads = 0, nx = 0;
-    int cg[TS_MAX_RETENTIONS] = {0, 0, 0, 0};   // dSloc commits waited for, per slot
+    int nx = 0;
     float acc[TS_MAX_RETENTIONS] = {0.f, 0.f, 0.f, 0.f};
     // G(NT-1): the gradient of the final state, or zero.
     for (int r = 0; r < p.R; ++r)
@@ -257,66 +286,78 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           tmem_st16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
         }
       }
-    for (int n = NT - 1; n >= 0 && ok; --n) {
+    for (int k = 0; k < NT && ok; ++k) {
+      const int n = NT - 1 - k;
       const int len = tile_len(p, n);
-      ok = mbar_wait(&sh.load, loads & 1, kErrCopyTimeout);
-      ++loads;
+      ok = mbar_wait(&sh.load_raw, k & 1, kErrCopyTimeout);
       if (!ok) break;
       for (int r = 0; r < p.R && ok; ++r) {
         const bool decayed = p.la[r] != nullptr;
         const float la = head_la(p, r, h);
         const float c_row = decayed ? __expf(la * static_cast<float>(lrow + 1)) : 1.f;   // carry c(i), row i = lrow
         const uint32_t raw_row = base + L.off_raw + r * L.raw_bytes + lrow * p.Dv * 2;
-        const bool carry = want(r) && local(n);
-        if (carry) {
-          // (i+1) c(i) dout, from the bf16-rounded c(i) dout of dSloc's operand
-          build_row_operand(base + L.off_x, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len,
-                            c_row, static_cast<float>(lrow + 1));
-          fence_async_smem();
-          mbar_arrive(&sh.epi_x);
-          ok = mbar_wait(&sh.mma_x, nx & 1, kErrMmaTimeout);
-          ++nx;
-          if (!ok) break;
-        }
-        if (cg[r] < NT - 1 - n) {
-          // G(n) of this slot: the previous tile's dSloc product is done
-          ok = mbar_wait(&sh.mma_g[r], cg[r] & 1, kErrMmaTimeout);
-          ++cg[r];
-          if (!ok) break;
+        const uint32_t op = base + L.off_op + r * L.op_bytes;
+        // G(n) of this slot is complete (and its operand buffer free) once the
+        // previous tile's dSloc product of this slot is
+        if (k > 0) ok = mbar_wait(&sh.mma_g[r], (k - 1) & 1, kErrMmaTimeout);
+        if (!ok || *(volatile int*)&sh.abort) {
+          ok = false;
+          break;
         }
         tc_fence_after();
-        // G(n): image out, log-retention terms, closing rescale.
+        const bool carry = want(r) && local(n);
         const bool closing_term = want(r) && n < last_dla;
+        if (carry) {
+          // (i+1) c(i) dout, from the bf16-rounded c(i) dout of dSloc's operand
+          build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row,
+                            static_cast<float>(lrow + 1));
+          fence_async_smem();
+          tc_fence_before();
+          mbar_arrive(&sh.epi_x);
+        }
+        // G(n): image out, log-retention terms, closing rescale; one
+        // 128-feature block at a time (the carry product of a block in the
+        // scratch block).
         const float closing = decayed ? __expf(la * static_cast<float>(len)) : 1.f;
         const float kc = static_cast<float>(len) * closing;
         const size_t si = state_index(p, b, h, n, r);
         const float* s_in = p.states + si * p.DkM * p.DvP;
         uint8_t* img = reinterpret_cast<uint8_t*>(g.gimages) + si * static_cast<size_t>(image_bytes(p));
-        for (int mb = 0; mb < mblocks; ++mb) {
+        for (int mb = 0; mb < mblocks && ok; ++mb) {
           const int f = mb * kTile + lrow;
           const int f0 = f & ~7;
-          for (int c = 0; c < p.DvP; c += 16) {
+          float sv[kMaxDvP];
+          if (carry || closing_term) {
+            // every column of this feature row in flight at once
+#pragma unroll
+            for (int c = 0; c < kMaxDvP; ++c)
+              if (c < p.DvP) sv[c] = s_in[static_cast<size_t>(c) * p.DkM + f];
+          }
+          if (carry) {
+            ok = mbar_wait(&sh.mma_x, nx & 1, kErrMmaTimeout);
+            ++nx;
+            if (!ok) break;
+            tc_fence_after();
+          }
+          float part = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < kMaxDvP / 16; ++kk) {
+            const int c = 16 * kk;
+            if (c >= p.DvP) break;
             const uint32_t ta = tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c);
             float v[16];
             tmem_ld16(ta, v);
-            if (carry || closing_term) {
-              float s[16];
+            if (carry) {
+              float x[16];
+              tmem_ld16(tmem_addr(tmem, 32 * quad, t_x + c), x);
 #pragma unroll
-              for (int e = 0; e < 16; ++e) s[e] = s_in[static_cast<size_t>(c + e) * p.DkM + f];
-              float part = 0.f;
-              if (carry) {
-                float x[16];
-                tmem_ld16(tmem_addr(tmem, 32 * quad, t_x + mb * p.DvP + c), x);
+              for (int e = 0; e < 16; ++e) part = fmaf(sv[c + e], x[e], part);
+            }
+            if (closing_term) {
+              float cg = 0.f;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) part = fmaf(s[e], x[e], part);
-              }
-              if (closing_term) {
-                float cg = 0.f;
-#pragma unroll
-                for (int e = 0; e < 16; ++e) cg = fmaf(s[e], v[e], cg);
-                part = fmaf(kc, cg, part);
-              }
-              acc[r] += part;
+              for (int e = 0; e < 16; ++e) cg = fmaf(sv[c + e], v[e], cg);
+              part = fmaf(kc, cg, part);
             }
             if (g.store) {
 #pragma unroll
@@ -336,11 +377,17 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
               tmem_st16(ta, v);
             }
           }
+          acc[r] += part;
+          if (carry && mb + 1 < mblocks) {
+            // the scratch block is free for the next block's carry product
+            tc_fence_before();
+            mbar_arrive(&sh.epi_x);
+          }
         }
-        // dSloc(n)'s row operand c(i) dout
+        if (!ok) break;
+        // dSloc(n)'s row operand c(i) dout (the carry products are done)
         if (local(n))
-          build_row_operand(base + L.off_op + r * L.op_bytes, raw_row, dvv, p.v_unit, L.vboxes,
-                            L.vboxes * kSwBox, lrow, lrow < len, c_row, 1.f);
+          build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row, 1.f);
         fence_async_smem();
         tc_fence_before();
         mbar_arrive(&sh.epi_g[r]);
@@ -349,8 +396,8 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
     if (!ok) *(volatile int*)&sh.abort = 1;
     // G(-1): the gradient of the initial state, after tile 0's dSloc products.
     if (ok && g.dinit != nullptr) {
-      for (int r = 0; r < p.R && ok; ++r)
-        if (cg[r] < NT) ok = mbar_wait(&sh.mma_g[r], cg[r] & 1, kErrMmaTimeout);
+      if (local(0))
+        for (int r = 0; r < p.R && ok; ++r) ok = mbar_wait(&sh.mma_g[r], (NT - 1) & 1, kErrMmaTimeout);
       tc_fence_after();
       if (ok) {
         for (int r = 0; r < p.R; ++r)
@@ -394,7 +441,7 @@ int launch_scan_bwd_chain(const ScanParams& p, const ScanGradParams& g, cudaStre
   const int dvv = p.Dv - p.v_unit;
   if (p.any_stale || p.R != p.RU || g.zero_start_final || !g.store) return 0;
   if (dvv % 64 != 0 || p.DvP != dvv + (p.v_unit ? 16 : 0) || p.DvP > kTile || p.Dv % 2 != 0) return 0;
-  if ((p.R + 1) * (p.DkM / kTile) * p.DvP > 512) return 0;
+  if (p.R * (p.DkM / kTile) * p.DvP + p.DvP > 512) return 0;
   // raw dout rows by untiled bulk copies: 16-byte aligned starts and lengths
   const long long len_last = p.T - static_cast<long long>(p.NT - 1) * kTile;
   if ((static_cast<long long>(p.T) * p.Dv * 2) % 16 != 0 || (len_last * p.Dv * 2) % 16 != 0) return 0;
