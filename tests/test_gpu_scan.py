@@ -268,6 +268,63 @@ def test_streamed_segments_equal_one_call(lib, segments):
         assert rel_err(state[:, :, r], want) < BF16_TOL, r
 
 
+@pytest.mark.parametrize("segments", [(100, 300), (1000, 1200, 256)])
+def test_streamed_segments_backward_equals_one_call(lib, segments):
+    """The backward through a chain of streamed segments -- the state's
+    gradient handed from each segment to the one before it -- gives the
+    gradients of one call over the whole sequence: q, k, v and every
+    log-retention; a loss on the final state reaches every segment too."""
+    from thetascan_b200.scan import linattn_views, linattn_views_stream
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(23)
+    B, H, T, Dk, Dv = 1, 2, sum(segments), 64, 64
+    q0 = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
+    k0 = (torch.rand(B, H, T, Dk, generator=g) / 8).to(torch.bfloat16).to(dev)
+    v0 = torch.randn(B, H, T, Dv, generator=g).to(torch.bfloat16).to(dev)
+    la0 = [torch.log(0.9 + 0.09 * torch.rand(H, generator=g)).to(dev) for _ in range(2)]
+    w = [torch.randn(B, H, T, Dv + 1, generator=g).to(dev) for _ in range(3)]
+    ws = torch.randn(B, H, 3, Dk, Dv + 1, generator=g).to(dev)
+
+    def leaves():
+        return ([t.clone().requires_grad_(True) for t in (q0, k0, v0)],
+                [a.clone().requires_grad_(True) for a in la0])
+
+    (q, k, v), la = leaves()
+    full = linattn_views(q, k, v, (None, *la), append_unit=True)
+    loss = sum((o.float() * wi).sum() for o, wi in zip(full, w))
+    loss.backward()
+    want = [t.grad for t in (q, k, v, *la)]
+
+    (q, k, v), la = leaves()
+    state, pieces, t0 = None, [], 0
+    for seg in segments:
+        sl = slice(t0, t0 + seg)
+        outs, state = linattn_views_stream(q[:, :, sl], k[:, :, sl], v[:, :, sl], (None, *la), state, append_unit=True)
+        pieces.append(outs)
+        t0 += seg
+    loss = sum((torch.cat([p[r] for p in pieces], dim=2).float() * w[r]).sum() for r in range(3))
+    loss.backward()
+    for got, ref in zip((q.grad, k.grad, v.grad, *(a.grad for a in la)), want):
+        assert rel_err(got, ref) < BF16_TOL
+
+    # a loss on the final state alone: its gradient reaches the first segment
+    (q, k, v), la = leaves()
+    state = None
+    for i, seg in enumerate(segments):
+        sl = slice(sum(segments[:i]), sum(segments[:i + 1]))
+        _, state = linattn_views_stream(q[:, :, sl], k[:, :, sl], v[:, :, sl], (None, *la), state, append_unit=True)
+    (state * ws).sum().backward()
+    kk = k0.double().cpu().requires_grad_(True)
+    vv = torch.cat((v0.double(), torch.ones(B, H, T, 1, dtype=torch.float64, device=dev)), -1).cpu()
+    back = (T - 1 - torch.arange(T, dtype=torch.float64))
+    total = 0
+    for r, a in enumerate([None, *la0]):
+        wt = torch.ones(H, T, dtype=torch.float64) if a is None else torch.exp(a.double().cpu()[:, None] * back)
+        total = total + (torch.einsum("bhtf,ht,bhtc->bhfc", kk, wt, vv) * ws[:, :, r].double().cpu()).sum()
+    total.backward()
+    assert rel_err(k.grad, kk.grad) < BF16_TOL
+
+
 # ----------------------------------------------------------------- stale retentions
 
 # B, H, T, Dk, Dv, retention layout: "s" plain sum, "d" decayed, "x" stale

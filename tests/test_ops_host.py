@@ -10,7 +10,7 @@ import torch
 from thetascan_b200 import ops
 
 NAMES = ["scan_views_fwd", "scan_views_bwd", "kernel_mixer_fwd", "kernel_mixer_bwd", "kernel_mixer_qkv_fwd",
-         "kernel_mixer_qkv_bwd"]
+         "kernel_mixer_qkv_bwd", "scan_views_stream_fwd", "scan_views_stream_bwd"]
 
 
 @pytest.mark.parametrize("name", NAMES)

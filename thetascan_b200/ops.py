@@ -340,3 +340,77 @@ def _qkv_backward_op(ctx, dy, *unused):
 
 
 torch.library.register_autograd(f"{LIB}::kernel_mixer_qkv_fwd", _qkv_backward_op, setup_context=_qkv_setup)
+
+
+# --------------------------------------------------------------------------- streaming scan
+
+@torch.library.custom_op(f"{LIB}::scan_views_stream_fwd", mutates_args=())
+def scan_views_stream_fwd(q: Tensor, k: Tensor, v: Tensor, log_alphas: list[Tensor], present: list[bool],
+                          append_unit: int, state: Optional[Tensor]) -> tuple[Tensor, Tensor, Tensor]:
+    """One segment of a streamed scan: f32 reads ``[R,B,H,T,Dv(+unit)]``
+    continuing from ``state`` (f32 ``[B,H,R,Dk,Dv]``, None = zero), the state
+    after the segment, and the forward workspace."""
+    from .scan import _stream_fwd_impl
+    _require_cuda(q, k, v, state, *log_alphas)
+    return _stream_fwd_impl(q, k, v, _retentions(log_alphas, present), append_unit, state)
+
+
+@scan_views_stream_fwd.register_fake
+def _(q, k, v, log_alphas, present, append_unit, state):
+    B, H, T, dk = (int(s) for s in q.shape)
+    dvp = int(v.shape[-1])
+    R = len(present)
+    outs = q.new_empty(R, B, H, T, dvp + append_unit, dtype=torch.float32)
+    new_state = q.new_empty(B, H, R, dk, dvp + append_unit, dtype=torch.float32)
+    nbytes = _scan_workspace_nbytes(B, H, T, dk, dvp, append_unit, list(present), [False] * R, False)
+    return outs, new_state, q.new_empty(nbytes, dtype=torch.uint8)
+
+
+@torch.library.custom_op(f"{LIB}::scan_views_stream_bwd", mutates_args=())
+def scan_views_stream_bwd(douts: Tensor, dstate: Tensor, q: Tensor, k: Tensor, v: Tensor, log_alphas: list[Tensor],
+                          present: list[bool], outs: Tensor, ws: Tensor, append_unit: int,
+                          state: Optional[Tensor]) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Gradients of q, k, v, every retention (``[R,H]``) and of the entering
+    state (empty when there was none) from those of the reads and the
+    leaving state."""
+    from .scan import _stream_bwd_impl
+    _require_cuda(douts, dstate, q, k, v, outs, ws, state, *log_alphas)
+    return _stream_bwd_impl(douts, dstate, q, k, v, _retentions(log_alphas, present), outs, ws, append_unit, state)
+
+
+@scan_views_stream_bwd.register_fake
+def _(douts, dstate, q, k, v, log_alphas, present, outs, ws, append_unit, state):
+    f = torch.float32
+    return (q.new_empty(q.shape, dtype=f), k.new_empty(k.shape, dtype=f), v.new_empty(v.shape, dtype=f),
+            q.new_empty(len(present), q.shape[1], dtype=f),
+            q.new_empty(0) if state is None else torch.empty_like(state))
+
+
+def _stream_setup(ctx, inputs, output):
+    q, k, v, log_alphas, present, append_unit, state = inputs
+    outs, new_state, ws = output
+    ctx.present = list(present)
+    ctx.ret_meta = [(r.dtype, r.shape) for r in log_alphas]
+    ctx.append_unit = append_unit
+    ctx.has_state = state is not None
+    ctx.dtypes = (q.dtype, k.dtype, v.dtype)
+    ctx.mark_non_differentiable(ws)
+    ctx.set_materialize_grads(False)
+    ctx.save_for_backward(q, k, v, outs, new_state, ws, state, *log_alphas)
+
+
+def _stream_backward(ctx, douts, dstate, dws):
+    q, k, v, outs, new_state, ws, state, *log_alphas = ctx.saved_tensors
+    if douts is None:
+        douts = torch.zeros_like(outs)
+    if dstate is None:
+        dstate = torch.zeros_like(new_state)
+    dq, dk, dv, dla, dinit = scan_views_stream_bwd(douts, dstate, q, k, v, log_alphas, ctx.present, outs, ws,
+                                                   ctx.append_unit, state)
+    qd, kd, vd = ctx.dtypes
+    rows = [i for i, p in enumerate(ctx.present) if p]
+    dret = [dla[i].to(meta[0]).reshape(meta[1]) for i, meta in zip(rows, ctx.ret_meta)]
+    return (dq.to(qd), dk.to(kd), dv.to(vd), dret, None, None, dinit if ctx.has_state else None)
+
+
+torch.library.register_autograd(f"{LIB}::scan_views_stream_fwd", _stream_backward, setup_context=_stream_setup)

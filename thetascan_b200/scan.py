@@ -208,17 +208,79 @@ def linattn(q, k, v, decay=None, chunk: int = DEFAULT_CHUNK, log_alpha=None):
     return linattn_views(q, k, v, (retention,), chunk)[0]
 
 
+def _stream_fwd_impl(q, k, v, retentions, append_unit, state):
+    """Body of ``thetascan_b200::scan_views_stream_fwd``: the forward scan of
+    one segment with boundary states (``ts_scan_args.init_state`` /
+    ``final_state``)."""
+    lib = _lib.load()
+    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    B, H, T, Dk = q.shape
+    dv = v.shape[-1] + append_unit
+    if state is not None:
+        if tuple(state.shape) != (B, H, len(las), Dk, dv) or state.dtype != torch.float32:
+            raise ValueError(f"b200 streaming scan: state must be f32 [{B},{H},{len(las)},{Dk},{dv}]")
+        state = state.contiguous()
+    outs_all = torch.empty(len(las), B, H, T, dv, dtype=torch.float32, device=q.device)
+    new_state = torch.empty(B, H, len(las), Dk, dv, dtype=torch.float32, device=q.device)
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit)
+    ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    args.init_state = None if state is None else state.data_ptr()
+    args.final_state = new_state.data_ptr()
+    _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
+    return outs_all, new_state, ws
+
+
+def _stream_bwd_impl(douts, dstate, q, k, v, retentions, outs_all, ws, append_unit, state):
+    """Body of ``thetascan_b200::scan_views_stream_bwd``: the backward of one
+    segment from the gradients of its reads and of its leaving state
+    (``ts_scan_grad_args.dfinal_state``), with the gradient of the entering
+    state (``dinit_state``)."""
+    lib = _lib.load()
+    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    n = len(las)
+    B, H, T, Dk = q.shape
+    dv_width = outs_all.shape[-1]
+    dgrads = [douts[i].to(torch.bfloat16).contiguous() for i in range(n)]
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, ws)
+    if state is not None:
+        state = state.contiguous()
+        args.init_state = state.data_ptr()
+    g = _lib.ScanGradArgs()
+    dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
+    dk = torch.empty_like(dq)
+    dvv = torch.empty(B, H, T, dv_width, dtype=torch.float32, device=q.device)
+    dla = torch.zeros(n, H, dtype=torch.float32, device=q.device)
+    dstate = dstate.to(torch.float32).contiguous()
+    dinit = torch.empty_like(state) if state is not None else None
+    for i in range(n):
+        g.dout[i] = dgrads[i].data_ptr()
+        g.dlog_alpha[i] = None if las[i] is None else dla[i].data_ptr()
+    g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dvv.data_ptr()
+    g.grad_dtype = _lib.TS_DTYPE_F32
+    g.dfinal_state = dstate.data_ptr()
+    g.dinit_state = None if dinit is None else dinit.data_ptr()
+    gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, args, q.device)
+    g.workspace, g.workspace_bytes = gws.data_ptr(), gws.numel()
+    _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(args), ctypes.byref(g), _stream()))
+    if append_unit:
+        dvv = dvv[..., :v.shape[-1]].contiguous()
+    return dq, dk, dvv, dla, (q.new_empty(0, dtype=torch.float32) if dinit is None else dinit)
+
+
 def linattn_views_stream(q, k, v, retentions, state=None, *, append_unit: bool = False):
-    """Streaming form of :func:`linattn_views` (forward only): scan this
-    segment of the sequence continuing from ``state`` and return
-    ``(outputs, new_state)``.
+    """Streaming form of :func:`linattn_views`: scan this segment of the
+    sequence continuing from ``state`` and return ``(outputs, new_state)``,
+    differentiable in the streams, the retentions and ``state``.
 
     ``state`` is what the previous segment returned (``None`` for the start
     of the sequence): f32 ``[B,H,R,Dk,Dv]`` with ``R = len(retentions)`` and
     ``Dv`` the payload width (``+1`` with ``append_unit``), the carried chunk
     state of every retention -- the persistent fast state of a decoder.
     Scanning a sequence segment by segment gives the outputs of one call over
-    the whole sequence (to rounding), for segments of any lengths."""
+    the whole sequence (to rounding), for segments of any lengths, and the
+    backward through the chain of segments gives the one call's gradients
+    (the state's gradient flows from each segment into the one before)."""
     if not retentions:
         return (), state
     _check_inputs(q, k, v, retentions, DEFAULT_CHUNK)
@@ -226,20 +288,8 @@ def linattn_views_stream(q, k, v, retentions, state=None, *, append_unit: bool =
         raise NotImplementedError("b200 streaming scan: bf16 streams only")
     if len(retentions) > _lib.MAX_RETENTIONS:
         raise NotImplementedError(f"b200 streaming scan: at most {_lib.MAX_RETENTIONS} retentions per call")
-    lib = _lib.load()
-    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
-    B, H, T, Dk = q.shape
-    dv = v.shape[-1] + (1 if append_unit else 0)
-    if state is not None:
-        if tuple(state.shape) != (B, H, len(las), Dk, dv) or state.dtype != torch.float32:
-            raise ValueError(f"b200 streaming scan: state must be f32 [{B},{H},{len(las)},{Dk},{dv}]")
-        state = state.contiguous()
-    outs = [torch.empty(B, H, T, dv, dtype=torch.float32, device=q.device) for _ in las]
-    new_state = torch.empty(B, H, len(las), Dk, dv, dtype=torch.float32, device=q.device)
-    args = _build_args(q, k, v, las, outs, append_unit)
-    ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
-    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
-    args.init_state = None if state is None else state.data_ptr()
-    args.final_state = new_state.data_ptr()
-    _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
-    return tuple(o.to(q.dtype) for o in outs), new_state
+    from . import ops  # noqa: F401  (registers the operators)
+    outs_all, new_state, _ = torch.ops.thetascan_b200.scan_views_stream_fwd(
+        q, k, v, [r for r in retentions if r is not None], [r is not None for r in retentions], int(append_unit),
+        state)
+    return tuple(o.to(q.dtype) for o in outs_all.unbind(0)), new_state
