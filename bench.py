@@ -58,6 +58,12 @@ CONFIGS = {
                rope="partial", J=3, retentions=(0.9, 0.99, 0.999), seqpar=True),
     # config 3: Gauss-Newton fast weights, head_dim 128, m = 128, relu2, two-stage
     # feature-mass read (both_feature_mass), one Jacobian step, the plain sum view.
+    # config 5: a ~17M-parameter hybrid LM training step (nine blocks, d_model
+    # 512, 8 heads, vocab 1024, tied embeddings, MLP ratio 2; the two middle
+    # blocks ThetaScan-GN with 2x expansion, the rest causal attention),
+    # global batch 64 x 1024 uniform token ids, AdamW, bf16 autocast; the
+    # global batch is split over the GPUs (strong scaling).
+    "c5": dict(B=64, T=1024, D=512, H=8, vocab=1024, layers=9, family="lm"),
     "c3": dict(B=8, T=8192, D=1024, H=8, mult=1, expansion=1, family="gn", fmap="relu2",
                gn_read="both_feature_mass", rope="partial", J=0),
 }
@@ -69,6 +75,10 @@ WORKLOADS = {
           "output gate; fwd+bwd, loss=mean(y^2)",
     "c3": "config 3: ThetaScan-GN relu2, head_dim 128, m=128, two-stage feature-mass read "
           "(both_feature_mass), 1 Jacobian step, sum view, output gate; fwd+bwd, loss=mean(y^2)",
+    "c5": "config 5: hybrid LM training step, 9 blocks (d_model 512, 8 heads, MLP ratio 2, vocab 1024, tied "
+          "embeddings), blocks 4-5 ThetaScan-GN (relu2 threshold, 2x expansion, m=256, two-stage feature-mass "
+          "read, fast bank), the rest causal attention; global batch 64 x 1024 uniform tokens, AdamW, bf16 "
+          "autocast",
     "c4": "config 4: ThetaScan-Kernel projected B-spline (16 basis, m=128), partial RoPE, fast bank "
           "0.9/0.99/0.999 + sum (4 views), output gate, T=32768; sequence-sharded over the GPUs; "
           "fwd+bwd, loss=mean(y^2)",
@@ -482,6 +492,32 @@ def _reference_sample(kind, view_set, T, n):
             f"median of {n}; tokens/s = {T} / median seconds (the GPU arm's batch and length are larger)")
 
 
+def reference_lm_step(cfg, T):
+    """One training step (forward, backward, AdamW) of the config-5 hybrid LM
+    on the host CPU with the reference package's own GN mixer (float32,
+    chunk backend), batch 1 x T tokens; returns (seconds, kind)."""
+    from thetascan_b200.lm import HybridLM, gn_mixer_config
+    ts = reference_package()
+    if ts is None:
+        raise SystemExit("config 5's reference arm needs the reference package (baseline/_ref)")
+
+    def reference_mixer(c):
+        d = c.to_dict()
+        d["gn"] = {k: v for k, v in d["gn"].items() if k != "damping"}
+        d["runtime"] = {"backend": "chunk", "scan_chunk": 512}
+        return ts.ThetaScan(ts.ThetaScanConfig.from_dict(d))
+
+    torch.manual_seed(2)
+    model = HybridLM(vocab=cfg["vocab"], d_model=cfg["D"], n_layers=cfg["layers"], n_heads=cfg["H"],
+                     mixer_config=gn_mixer_config(cfg["D"], cfg["H"]), mixer_factory=reference_mixer)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.0)
+    tokens = torch.randint(0, cfg["vocab"], (1, T + 1), generator=torch.Generator().manual_seed(2))
+    t0 = time.perf_counter()
+    model.loss(tokens).backward()
+    opt.step()
+    return time.perf_counter() - t0, "reference"
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -489,6 +525,27 @@ def run_reference(args, cfg):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     T = args.ref_tokens
+    if cfg.get("family") == "lm":
+        for _ in range(args.warmup):
+            reference_lm_step(cfg, T)
+        runs = [reference_lm_step(cfg, T) for _ in range(max(1, args.steps))]
+        per_step = statistics.median(t for t, _ in runs)
+        value = T / per_step
+        sample = (f"the config-5 hybrid LM on the host CPU with the reference package's own GN mixer (chunk "
+                  f"backend), float32, batch 1 x {T} tokens, forward+backward+AdamW, median of {len(runs)}; "
+                  f"tokens/s = {T} / median seconds")
+        print(json.dumps({
+            "impl": "reference", "metric": "hybrid LM training step tokens/s (config 5)", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(runs), "warmup": args.warmup,
+            "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"c5 bounded CPU sample B=1 T={T}", "model": "hybrid LM (reference mixer)",
+                       "global_batch": 1, "seq_len": T, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     for _ in range(args.warmup):              # untimed warm-up steps of the same sample
         cpu_reference_step(cfg, T, "bank")
     runs = [cpu_reference_step(cfg, T, "bank") for _ in range(max(1, args.steps))]
@@ -768,6 +825,121 @@ def run_b200(args, cfg):
         dist.destroy_process_group()
 
 
+def run_lm(args, cfg):
+    """Config 5: whole training steps (forward, backward, gradient all-reduce
+    across ranks, AdamW) of the hybrid LM on uniform random tokens."""
+    from thetascan_b200.lm import HybridLM
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    if cfg["B"] % world:
+        raise SystemExit(f"global batch {cfg['B']} does not split over {world} GPUs")
+    B, T = cfg["B"] // world, cfg["T"]
+    torch.manual_seed(2)
+    model = HybridLM(vocab=cfg["vocab"], d_model=cfg["D"], n_layers=cfg["layers"], n_heads=cfg["H"]).to(device)
+    params = [p for p in model.parameters() if p.requires_grad]
+    n_params = sum(p.numel() for p in params)
+    opt = torch.optim.AdamW(params, lr=3e-4, weight_decay=0.0, fused=True)
+    gen = torch.Generator().manual_seed(2)
+    tokens_all = torch.randint(0, cfg["vocab"], (cfg["B"], T + 1), generator=gen)
+    tok_host = tokens_all[rank * B:(rank + 1) * B].contiguous().pin_memory()
+    tok = tok_host.to(device)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step(inp):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model.loss(inp)
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1) for p in params])
+            dist.all_reduce(flat)
+            flat.div_(world)
+            offset = 0
+            for p in params:
+                n = p.numel()
+                p.grad.copy_(flat[offset:offset + n].view_as(p.grad))
+                offset += n
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(args.warmup):
+        step(tok)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(device_bus_id(local)) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            loss = step(tok)
+        r1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    mean_ms = r0.elapsed_time(r1) / args.steps
+    # end to end: each step's tokens copied from pinned host memory, the loss read back
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    buf = torch.empty_like(tok)
+    e0.record()
+    for _ in range(args.steps):
+        buf.copy_(tok_host, non_blocking=True)
+        loss = step(buf)
+        loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([mean_ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mean_ms, e2e_ms = float(t[0]), float(t[1])
+    tokens = cfg["B"] * T
+    value = tokens / (mean_ms / 1e3)
+    # model FLOPs per token: 6 N for the dense weights plus the causal
+    # attention score/value products of the attention blocks (3 x 2 x 2 x T/2 x d)
+    n_attn = cfg["layers"] - 2
+    flop_per_token = 6 * n_params + n_attn * 3 * 2 * 2 * (T / 2) * cfg["D"]
+    peak_sus, _, _, peak_kind = load_peaks()
+    achieved = flop_per_token * value / world / 1e12
+    line = {
+        "metric": "hybrid LM training step tokens/s (config 5)", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic uniform token ids (seed 2), seeded random-init weights",
+        "config": {"workload": WORKLOADS["c5"], "model": f"hybrid LM, {n_params / 1e6:.2f} M parameters",
+                   "global_batch": cfg["B"], "seq_len": T, "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "256 MB buffer written before every timed step"},
+        "roofline": {"bound": "tensor", "kernel": "whole step", "achieved": achieved, "peak": peak_sus,
+                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": None,
+                     "flop_per_token": flop_per_token, "peak_source": f"{peak_kind} bf16_tflops_sustained"},
+        "loss": float(loss.detach()),
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": tok_host.numel() * tok_host.element_size() * world, "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms},
+        "clocks": clocks.summary(),
+        "device_status": _device_status(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _device_status():
+    from thetascan_b200 import _lib
+    return _lib.device_status(torch.cuda.current_stream().cuda_stream)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -783,6 +955,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif cfg.get("family") == "lm":
+        run_lm(args, cfg)
     else:
         run_b200(args, cfg)
 

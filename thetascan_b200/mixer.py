@@ -375,6 +375,15 @@ class ThetaScanCore(nn.Module):
         chunk states of the earlier slices arrive through one exchange."""
         if not x.is_cuda:
             raise RuntimeError("thetascan_b200 requires a CUDA input")
+        if torch.is_autocast_enabled("cuda"):
+            # The mixer picks its own precisions (bf16 streams on the tensor
+            # cores with f32 states; the GN family's per-token math in f32),
+            # so autocast is off inside; under a bf16 autocast a float32 input
+            # of the kernel family takes the bf16 path.
+            to_bf16 = (self.cfg.family != "gn" and x.dtype == torch.float32
+                       and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+            with torch.autocast("cuda", enabled=False):
+                return self.forward(x.to(torch.bfloat16) if to_bf16 else x, shard)
         if self.cfg.family == "gn":
             return self._forward_gn(x, shard)
         if x.dtype == torch.float32:
