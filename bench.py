@@ -273,56 +273,24 @@ def device_bus_id(index):
 
 
 class PhaseTimer:
-    """Time each C-ABI entry point with CUDA events on the launching stream.
+    """Time each C-ABI entry point with CUDA events on the launching stream
+    (wraps the bound ctypes functions of the library)."""
 
-    Wraps the bound ctypes functions of the library; counts our kernel
-    launches per entry point."""
-
-    KERNELS = {"ts_b200_feature_fwd": 1, "ts_b200_scan_fwd": 3, "ts_b200_kread_fwd": 1,
-               "ts_b200_kread_bwd": 1, "ts_b200_scan_bwd": 5, "ts_b200_feature_bwd": 1}
-
-    @staticmethod
-    def scan_kernels(name, args):
-        """Kernels one scan call launches (the launch logic of the C ABI:
-        csrc/scan_fwd.cu launch_scan_fwd, csrc/scan_bwd.cu launch_scan_bwd)."""
-        a = args[0]._obj
-        if a.f32_streams:
-            # csrc/scan_f32.cu: local states (more than one tile), prefix, tile kernel
-            return (1 if a.tokens > 64 else 0) + 2
-        nt = -(-a.tokens // 128)
-        stale = any(a.stale[i] for i in range(a.n_retentions))
-        if name == "ts_b200_scan_fwd":
-            stage = a.stage
-            state = 1 if (stage != 2 and (nt > 1 or a.final_state or stage == 1)) else 0
-            return state + 1 + (0 if stage == 1 else 1)
-        g = args[1]._obj
-        two_level = (not stale) and nt >= 32
-        all_tiles = bool(g.dfinal_state or g.dinit_state or a.init_state or g.stage != 0)
-        state = 1 if (g.stage != 2 and (nt > 1 or all_tiles)) else 0
-        prefix = 2 if two_level else 1
-        # dq and dk in one kernel where v, k, q, ds and the dout tiles fit
-        # (scan_bwd.cu dqk2_fits), else two
-        dvp, dkp = -(-a.dv // 16) * 16, -(-a.dk // 16) * 16
-        merged = dvp <= 128 and 2 * dkp <= 512 and 128 * (dvp + 2 * dkp + 128 + a.n_retentions * dvp) * 2 <= 228352
-        return state + prefix + (0 if g.stage == 1 else (2 if merged else 3))
+    ENTRY_POINTS = ("ts_b200_feature_fwd", "ts_b200_scan_fwd", "ts_b200_kread_fwd", "ts_b200_kread_bwd",
+                    "ts_b200_scan_bwd", "ts_b200_feature_bwd")
 
     def __init__(self, lib):
         self.lib = lib
         self.saved = {}
-        self.events = {name: [] for name in self.KERNELS}
-        self.calls = {name: 0 for name in self.KERNELS}
-        self.scan_launches = 0
+        self.events = {name: [] for name in self.ENTRY_POINTS}
         self.timing = False
 
     def install(self):
-        for name in self.KERNELS:
+        for name in self.ENTRY_POINTS:
             fn = getattr(self.lib, name)
             self.saved[name] = fn
 
             def wrapper(*a, _fn=fn, _name=name):
-                self.calls[_name] += 1
-                if _name in ("ts_b200_scan_fwd", "ts_b200_scan_bwd"):
-                    self.scan_launches += self.scan_kernels(_name, a)
                 if not self.timing:
                     return _fn(*a)
                 start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -336,10 +304,6 @@ class PhaseTimer:
     def uninstall(self):
         for name, fn in self.saved.items():
             setattr(self.lib, name, fn)
-
-    def launches(self):
-        return self.scan_launches + sum(self.calls[n] * k for n, k in self.KERNELS.items()
-                                        if n not in ("ts_b200_scan_fwd", "ts_b200_scan_bwd"))
 
     def total_ms(self):
         """Device time of each entry point summed over the timed calls (a
@@ -381,15 +345,44 @@ def bytes_per_token(cfg):
     }
 
 
-# DRAM bytes (read + write) of one launch measured by ncu, from the summaries
-# under profiles/ (config-2 shapes at batch 2), scaled to a launch of the
-# timed config by its number of token rows (traffic grows with B * T).
-MEASURED_TRAFFIC = {
-    # entry point: (bytes per launch at the profiled size, tokens of that launch, source)
-    "ts_b200_feature_bwd": (258.1e6 + 29.9e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
-    "ts_b200_scan_bwd": (1330.6e6 + 363.6e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
-    "ts_b200_scan_fwd": (476.2e6 + 344.9e6, 2 * 4096, "profiles/tile_kernels_c2b2.md"),
-}
+def source_hash():
+    """First 16 hex digits of a SHA-256 over the library's sources (the CUDA
+    files and the C-ABI header), naming the build a profile was taken on."""
+    import hashlib
+    h = hashlib.sha256()
+    names = sorted(os.listdir(os.path.join(ROOT, "thetascan_b200", "csrc")))
+    for name in names:
+        with open(os.path.join(ROOT, "thetascan_b200", "csrc", name), "rb") as f:
+            h.update(name.encode() + b"\0" + f.read())
+    with open(os.path.join(ROOT, "include", "thetascan_b200.h"), "rb") as f:
+        h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def measured_traffic(entry, tokens):
+    """DRAM bytes (read + write) of one launch of a C-ABI entry point, from
+    the ncu summary ``profiles/traffic_c2.md``: its kernels' bytes at the
+    profiled size, scaled by tokens to this launch (traffic grows with
+    B * T), and only when the summary names this build's source hash
+    (``None`` otherwise, so a stale profile never reports)."""
+    path = os.path.join(ROOT, "profiles", "traffic_c2.md")
+    if not os.path.exists(path):
+        return None, "no traffic profile"
+    rows, build, tokens_at = {}, None, None
+    with open(path) as f:
+        for line in f:
+            if line.startswith("source hash:"):
+                build = line.split(":", 1)[1].strip().strip("`")
+            elif line.startswith("tokens per launch:"):
+                tokens_at = int(line.split(":", 1)[1])
+            elif line.startswith("| `ts_b200_"):
+                cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
+                rows[cells[0]] = float(cells[1]) * 1e6
+    if build != source_hash():
+        return None, f"profile of build {build}, this build is {source_hash()}"
+    if entry not in rows or not tokens_at:
+        return None, "entry point not profiled"
+    return rows[entry] * tokens / tokens_at, f"profiles/traffic_c2.md (build {build})"
 
 
 # --------------------------------------------------------------------------- CPU reference
@@ -626,8 +619,7 @@ def run_b200(args, cfg):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    timer.calls = {n: 0 for n in timer.calls}
-    timer.scan_launches = 0
+    launches0 = lib.ts_b200_launch_count()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(device_bus_id(local)) as clocks:
@@ -653,7 +645,8 @@ def run_b200(args, cfg):
             dist.barrier()
         wall = time.perf_counter() - wall0
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    launches = timer.launches() // max(1, args.steps)
+    # the library's own count of the kernels it launched in the timed region
+    launches = lib.ts_b200_launch_count() - launches0
     mean_ms = region0.elapsed_time(region1) / args.steps
     if world > 1:
         t = torch.tensor([mean_ms], device=device)
@@ -752,10 +745,7 @@ def run_b200(args, cfg):
     flops_launch = per_token[dominant] * B * T
     bytes_launch = bytes_per_token(cfg)[dominant] * B * T
     ridge = peak_sus * 1e12 / (peak_hbm * 1e9)
-    traffic = None
-    if dominant in MEASURED_TRAFFIC and args.config in ("c2", "c2b2"):
-        tb, ttok, _ = MEASURED_TRAFFIC[dominant]
-        traffic = tb * (B * T) / ttok
+    traffic, traffic_source = measured_traffic(dominant, B * T) if args.config in ("c2", "c2b2") else (None, None)
     if cfg.get("dtype") == "f32":
         # float32 scan kernels: f32 FMAs on the CUDA cores (no tensor cores)
         fma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
@@ -767,13 +757,15 @@ def run_b200(args, cfg):
     elif flops_launch / max(bytes_launch, 1) < ridge:
         achieved = bytes_launch / launch_s / 1e9
         roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
-                    "frac": achieved / peak_hbm, "traffic": traffic, "bytes_per_launch": bytes_launch,
+                    "frac": achieved / peak_hbm, "traffic": traffic, "traffic_source": traffic_source,
+                    "bytes_per_launch": bytes_launch,
                     "flops_per_launch": flops_launch, "tflops": flops_launch / launch_s / 1e12,
                     "peak_source": f"{peak_kind} hbm_gbs"}
     else:
         achieved = flops_launch / launch_s / 1e12
         roofline = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_sus,
                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": traffic,
+                    "traffic_source": traffic_source,
                     "bytes_per_launch": bytes_launch, "flops_per_launch": flops_launch,
                     "peak_source": f"{peak_kind} bf16_tflops_sustained"}
     # Per GPU: `value` is the whole job's tokens/s, the peak one GPU's.
@@ -800,7 +792,7 @@ def run_b200(args, cfg):
                 "ms_per_step": e2e, "mode": "pipelined input copies (copy stream, double buffer)",
                 "repetitions_ms_per_step": e2e_runs,
                 "serial_value": tokens / (serial_ms / 1e3), "serial_ms_per_step": serial_ms},
-        "gpu_launches": launches * args.steps,
+        "gpu_launches": launches,
         "host_enqueue_ms_per_step": host_ms,
         "step_ms_spread": [min(step_ms), max(step_ms)],
         "clocks": clocks.summary(),

@@ -50,6 +50,11 @@ enum { TS_DTYPE_F32 = 0, TS_DTYPE_BF16 = 1 };
 /* Library version string. */
 const char* ts_b200_version(void);
 
+/* Kernels this library has launched in the process so far (every entry
+ * point counts each of its launches).  No reference counterpart: a host
+ * reads it before and after a region to count the region's launches. */
+long long ts_b200_launch_count(void);
+
 /* Copy the message of the last failed call on this thread into buf (always
  * NUL-terminated); returns that call's error code. */
 int ts_b200_last_error(char* buf, size_t len);

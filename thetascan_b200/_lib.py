@@ -56,6 +56,7 @@ class ScanGradArgs(ctypes.Structure):
 # against the header.
 SIGNATURES = {
     "ts_b200_version": (ctypes.c_char_p, []),
+    "ts_b200_launch_count": (ctypes.c_longlong, []),
     "ts_b200_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
     "ts_b200_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "ts_b200_selftest_mma": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,

@@ -1,4 +1,5 @@
 // C-ABI entry points: argument validation, workspace sizing and launches.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -24,7 +25,12 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+namespace {
+std::atomic<long long> g_launches{0};
+}  // namespace
+
 int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return TS_OK;
@@ -235,6 +241,8 @@ using namespace ts;
 extern "C" {
 
 const char* ts_b200_version(void) { return "thetascan_b200 0.1.0 (sm_100a)"; }
+
+long long ts_b200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int ts_b200_last_error(char* buf, size_t len) {
   if (buf && len) {
