@@ -147,6 +147,15 @@ typedef struct ts_scan_args {
    * recency reads, which the host forms as the reference does).  Zero: bf16
    * streams on the tensor cores. */
   int f32_streams;
+  /* Per-token retention streams, the [B,H,T,1] decay of the reference's
+   * chunk scan (scan_chunk.py:122-155, 208-212; the data-dependent EMA views
+   * of interface.py:216-230): where log_alpha_stream[r] is non-NULL it is a
+   * contiguous f32 [B,H,T] log-retention stream (<= 0) and retention r reads
+   * with w(t,i) = exp(sum_{i<s<=t} log_alpha_stream[s]) in place of
+   * log_alpha[r] (which must then be NULL).  f32 streams only
+   * (TS_ERR_NOT_IMPLEMENTED otherwise); the backward writes
+   * ts_scan_grad_args.dlog_alpha_stream[r]. */
+  const float* log_alpha_stream[TS_MAX_RETENTIONS];
 } ts_scan_args;
 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args);
@@ -190,6 +199,9 @@ typedef struct ts_scan_grad_args {
   const float* dfinal_state;
   float* dinit_state;
   int stage;
+  /* Gradients of the per-token retention streams, f32 [B,H,T] (written, not
+   * accumulated), or NULL (not wanted). */
+  float* dlog_alpha_stream[TS_MAX_RETENTIONS];
 } ts_scan_grad_args;
 
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* fwd);

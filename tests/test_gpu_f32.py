@@ -163,6 +163,131 @@ def test_f32_scan_errors(dev):
         _lib.check(lib.ts_b200_scan_fwd_static(ctypes.byref(args), scan._stream()))
 
 
+# ------------------------------------------------------------------- per-token retention streams
+
+def _log_retention_stream(B, H, T, seed, slow=False):
+    """A gated ``[B,H,T,1]`` log-retention stream (log-sigmoid gates, <= 0);
+    ``slow`` puts it near zero, long memory across many tiles."""
+    g = torch.Generator().manual_seed(100 + seed)
+    x = torch.randn(B, H, T, 1, generator=g) + (6.0 if slow else 2.0)
+    return torch.nn.functional.logsigmoid(x)
+
+
+STREAM_CASES = [
+    # B, H, T,  Dk,  Dv, retention kinds (s = stream, a = static, n = sum), append_unit
+    (2, 3, 37, 5, 4, "s", False),              # one ragged tile
+    (1, 2, 64, 16, 8, "ns", False),            # exactly one tile
+    (2, 2, 515, 64, 64, "nsa", True),          # ragged last tile, [v | 1] payload
+    (1, 2, 1100, 32, 16, "ss", False),         # two streams, long memory
+    (1, 2, 200, 128, 136, "sn", False),        # 32-token tiles
+    (1, 1, 130, 256, 65, "s", True),           # widest keys
+]
+
+
+def _kind_retentions(B, H, T, kinds):
+    rets = []
+    for j, c in enumerate(kinds):
+        if c == "n":
+            rets.append(None)
+        elif c == "a":
+            rets.append(_retentions(H, 1, False)[0])
+        else:
+            rets.append(_log_retention_stream(B, H, T, seed=j, slow=j % 2 == 1))
+    return rets
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("index", range(len(STREAM_CASES)))
+def test_stream_retention_scan_matches_oracle(dev, index, dtype):
+    """Per-token retention streams (scan_chunk.py:141-155, 326-336): the
+    float32 CUDA-core kernels, forward and every gradient (q, k, v and the
+    per-token log-retention stream), against the float64 oracle at the same
+    inputs.  bf16 streams are widened exactly and the reads rounded to bf16
+    on the way out."""
+    from thetascan_b200 import _lib, scan
+    B, H, T, Dk, Dv, kinds, unit = STREAM_CASES[index]
+    q, k, v = (x.to(dtype) for x in _streams(B, H, T, Dk, Dv, seed=5, positive=True))
+    rets = _kind_retentions(B, H, T, kinds)
+    g = torch.Generator().manual_seed(9)
+    width = Dv + (1 if unit else 0)
+    weights = [torch.randn(B, H, T, width, generator=g, dtype=torch.float64) for _ in rets]
+    if dtype == torch.bfloat16:   # the gradient the kernels take is the bf16 one
+        weights = [w.bfloat16().double() for w in weights]
+
+    def loss(outs):
+        return sum((o.double() * w.to(o.device)).sum() for o, w in zip(outs, weights))
+
+    leaves = [x.to(dev).requires_grad_(True) for x in (q, k, v)]
+    rleaves = [None if r is None else r.to(dev).requires_grad_(True) for r in rets]
+    got = scan.linattn_views(*leaves, tuple(rleaves), append_unit=unit)
+    loss(got).backward()
+    oleaves = [x.double().requires_grad_(True) for x in (q, k, v)]
+    orets = [None if r is None else r.double().requires_grad_(True) for r in rets]
+    ov = torch.cat([oleaves[2], torch.ones(B, H, T, 1, dtype=torch.float64)], -1) if unit else oleaves[2]
+    want = oscan.linattn_chunk_views(oleaves[0], oleaves[1], ov, tuple(orets), chunk=64)
+    loss(want).backward()
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    out_tol = F32_TOL if dtype == torch.float32 else 8e-3   # bf16 rounding of the reads
+    for g_, w_ in zip(got, want):
+        assert g_.dtype == dtype and g_.shape == w_.shape
+        assert rel_err(g_, w_) < out_tol
+    for name, a, b in zip("qkv", leaves, oleaves):
+        assert a.grad.dtype == dtype
+        assert rel_err(a.grad, b.grad) < (F32_TOL if dtype == torch.float32 else 8e-3), name
+    for a, b in zip(rleaves, orets):
+        if a is not None:
+            assert a.grad.shape == b.grad.shape
+            assert rel_err(a.grad, b.grad) < (F32_TOL if dtype == torch.float32 else 8e-3)
+
+
+def test_stream_retention_matches_reference_golden_case(dev):
+    """The reference's own stream case (tests/golden/scan_cases.pt, recorded
+    from scan_chunk.linattn at chunk 8): output and the gradients of
+    ``out.square().sum()`` with respect to q, k, v and the stream."""
+    from thetascan_b200 import scan
+    case = torch.load(os.path.join(GOLDEN, "scan_cases.pt"), weights_only=False)["cases"][2]
+    assert case["name"] == "stream"
+    leaves = [case[n].float().to(dev).requires_grad_(True) for n in ("q", "k", "v", "retention")]
+    out = scan.linattn(*leaves[:3], leaves[3], chunk=case["chunk"])
+    assert rel_err(out, case["out"]) < F32_TOL
+    out.double().square().sum().backward()
+    for a, want in zip(leaves, case["grads"]):
+        assert rel_err(a.grad, want) < F32_TOL
+
+
+def test_stream_retention_equals_static_when_constant(dev):
+    """A stream that repeats a head's static log-retention at every token
+    gives the static retention's reads, and its per-token gradient sums to
+    the static gradient (the reference's _retention_stream widening,
+    interface.py:110-117)."""
+    from thetascan_b200 import scan
+    B, H, T, Dk, Dv = 2, 3, 333, 32, 24
+    q, k, v = (x.to(dev) for x in _streams(B, H, T, Dk, Dv, seed=11, positive=True))
+    la = _retentions(H, 1, False)[0].to(dev)
+    stream = la.view(1, H, 1, 1).expand(B, H, T, 1).contiguous()
+    a = la.clone().requires_grad_(True)
+    b = stream.clone().requires_grad_(True)
+    ya = scan.linattn(q, k, v, log_alpha=a)
+    yb = scan.linattn(q, k, v, log_alpha=b)
+    assert rel_err(yb, ya) < F32_TOL
+    w = torch.randn(B, H, T, Dv, device=dev)
+    (ya * w).sum().backward()
+    (yb * w).sum().backward()
+    assert rel_err(b.grad.sum(dim=(0, 2, 3)), a.grad) < F32_TOL
+
+
+def test_stream_retention_errors(dev):
+    from thetascan_b200 import scan
+    q, k, v = (x.to(dev) for x in _streams(1, 2, 16, 8, 8))
+    with pytest.raises(ValueError):
+        scan.linattn(q, k, v, log_alpha=torch.zeros(1, 2, 15, 1, device=dev))   # wrong length
+    with pytest.raises(NotImplementedError):
+        scan.linattn(q, k, v, log_alpha=torch.zeros(1, 2, 16, 2, device=dev))   # per-channel decay
+    with pytest.raises(NotImplementedError):
+        scan.linattn_views_stream(q.bfloat16(), k.bfloat16(), v.bfloat16(),
+                                  (torch.zeros(1, 2, 16, 1, device=dev),))
+
+
 # ------------------------------------------------------------------- mixer
 
 def _config1():

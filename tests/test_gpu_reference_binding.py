@@ -110,3 +110,26 @@ def test_reference_gn_mixer_scans_on_b200_match_reference_chunk(ref):
     assert integration._fused_core(module._core) is None   # reference forward, b200 scans
     x = torch.randn(2, 300, 128, generator=torch.Generator().manual_seed(8))
     _compare(module, reference, x, torch.float32, torch.device("cuda"), 1e-4)
+
+
+def test_reference_scan_plugin_point_takes_retention_streams(ref):
+    """The reference's scan plugin point (``interface._fn``) with a per-token
+    ``[B,H,T,1]`` log-retention stream: ``backend="b200"`` on float32 CUDA
+    tensors against the reference's own chunk scan in float64."""
+    from thetascan._core.ops import interface, scan_chunk
+    g = torch.Generator().manual_seed(21)
+    B, H, T, Dk, Dv = 2, 3, 700, 48, 40
+    q, k = (torch.randn(B, H, T, Dk, generator=g).abs() / Dk ** 0.5 for _ in range(2))
+    v = torch.randn(B, H, T, Dv, generator=g)
+    decay = torch.nn.functional.logsigmoid(torch.randn(B, H, T, 1, generator=g) + 4.0)
+    w = torch.randn(B, H, T, Dv, generator=g, dtype=torch.float64)
+    leaves = [x.cuda().requires_grad_(True) for x in (q, k, v, decay)]
+    y = interface._fn("b200", 128)(*leaves)
+    (y.double() * w.cuda()).sum().backward()
+    rleaves = [x.double().requires_grad_(True) for x in (q, k, v, decay)]
+    yr = scan_chunk.linattn(*rleaves, chunk=128)
+    (yr * w).sum().backward()
+    assert y.dtype == torch.float32
+    assert rel_err(y, yr) < 1e-5
+    for a, b in zip(leaves, rleaves):
+        assert rel_err(a.grad, b.grad) < 1e-5

@@ -36,6 +36,7 @@ class ScanArgs(ctypes.Structure):
         ("init_state", ctypes.c_void_p), ("final_state", ctypes.c_void_p), ("stage", ctypes.c_int),
         ("stale", ctypes.c_int * MAX_RETENTIONS),
         ("f32_streams", ctypes.c_int),
+        ("log_alpha_stream", c_ptr4),
     ]
 
 
@@ -48,6 +49,7 @@ class ScanGradArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("dv_strides", c_int64_3),
         ("dfinal_state", ctypes.c_void_p), ("dinit_state", ctypes.c_void_p), ("stage", ctypes.c_int),
+        ("dlog_alpha_stream", c_ptr4),
     ]
 
 

@@ -69,6 +69,10 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
   if (a->n_retentions < 1 || a->n_retentions > TS_MAX_RETENTIONS)
     return set_error(TS_ERR_VALUE, "scan: n_retentions must be in 1..%d", TS_MAX_RETENTIONS);
   if (!a->q || !a->k || !a->v) return set_error(TS_ERR_VALUE, "scan: null stream pointer");
+  for (int r = 0; r < TS_MAX_RETENTIONS && r < a->n_retentions; ++r)
+    if (a->log_alpha_stream[r])
+      return set_error(TS_ERR_NOT_IMPLEMENTED,
+                       "scan: per-token retention streams take f32 streams (f32_streams), on the CUDA cores");
   if (a->out_dtype != TS_DTYPE_F32 && a->out_dtype != TS_DTYPE_BF16)
     return set_error(TS_ERR_VALUE, "scan: out_dtype must be TS_DTYPE_F32 or TS_DTYPE_BF16");
   std::memset(p, 0, sizeof(*p));
@@ -140,6 +144,11 @@ static int build_scan_params(const ts_scan_args* a, ScanParams* p) {
 static size_t f32_states_bytes(const ScanF32Params& p) {
   return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * p.Dk * p.Dv * sizeof(float));
 }
+// Per-tile scalars of per-token retention streams (closings in the forward
+// workspace, closing terms in the backward's), after the states.
+static size_t f32_tile_bytes(const ScanF32Params& p) {
+  return align256(static_cast<size_t>(p.B) * p.H * p.NT * p.R * sizeof(float));
+}
 
 // Validate `a` (f32_streams set) and fill `p` (workspace pointers left null).
 static int build_scan_f32_params(const ts_scan_args* a, ScanF32Params* p) {
@@ -189,7 +198,10 @@ static int build_scan_f32_params(const ts_scan_args* a, ScanF32Params* p) {
       return set_error(TS_ERR_NOT_IMPLEMENTED,
                        "scan: stale retentions of f32 streams are formed by the host (plain read minus recency read)");
     if (!a->out[r]) return set_error(TS_ERR_VALUE, "scan: null output pointer for retention %d", r);
+    if (a->log_alpha_stream[r] && a->log_alpha[r])
+      return set_error(TS_ERR_VALUE, "scan: retention %d has both a static and a per-token log-retention", r);
     p->la[r] = a->log_alpha[r];
+    p->las[r] = a->log_alpha_stream[r];
     p->out[r] = static_cast<float*>(a->out[r]);
   }
   return TS_OK;
@@ -198,10 +210,11 @@ static int build_scan_f32_params(const ts_scan_args* a, ScanF32Params* p) {
 static int scan_f32_fwd(const ts_scan_args* a, cudaStream_t s) {
   ScanF32Params p;
   if (int e = build_scan_f32_params(a, &p)) return e;
-  const size_t need = f32_states_bytes(p);
+  const size_t need = f32_states_bytes(p) + f32_tile_bytes(p);
   if (!a->workspace || a->workspace_bytes < need)
     return set_error(TS_ERR_VALUE, "scan_fwd: workspace of %zu bytes needed", need);
   p.states = static_cast<float*>(a->workspace);
+  p.closing = reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) + f32_states_bytes(p));
   return launch_scan_f32_fwd(p, s);
 }
 
@@ -209,7 +222,7 @@ static int scan_f32_bwd(const ts_scan_args* a, const ts_scan_grad_args* g, cudaS
   ScanF32Params p;
   if (int e = build_scan_f32_params(a, &p)) return e;
   if (!g) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient arguments");
-  const size_t need = f32_states_bytes(p);
+  const size_t need = f32_states_bytes(p) + f32_tile_bytes(p);
   if (!a->workspace || a->workspace_bytes < need)
     return set_error(TS_ERR_VALUE, "scan_bwd: the forward workspace (%zu bytes) is required", need);
   if (!g->workspace || g->workspace_bytes < need)
@@ -221,16 +234,22 @@ static int scan_f32_bwd(const ts_scan_args* a, const ts_scan_grad_args* g, cudaS
   if (g->dfinal_state || g->dinit_state || g->stage != 0)
     return set_error(TS_ERR_NOT_IMPLEMENTED, "scan_bwd: f32 streams take no boundary states or stages");
   if (!g->dq || !g->dk || !g->dv) return set_error(TS_ERR_VALUE, "scan_bwd: null gradient output");
+  bool any_stream = false;
   for (int r = 0; r < p.R; ++r) {
     p.dout[r] = static_cast<const float*>(g->dout[r]);
     if (!p.dout[r]) return set_error(TS_ERR_VALUE, "scan_bwd: null dout for retention %d", r);
     p.dla[r] = g->dlog_alpha[r];
+    p.dlas[r] = p.las[r] ? g->dlog_alpha_stream[r] : nullptr;
+    any_stream |= p.dlas[r] != nullptr;
   }
   p.dq = static_cast<float*>(g->dq);
   p.dk = static_cast<float*>(g->dk);
   p.dv = static_cast<float*>(g->dv);
   p.states = static_cast<float*>(a->workspace);
+  p.closing = reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) + f32_states_bytes(p));
   p.gstates = static_cast<float*>(g->workspace);
+  p.zterm = any_stream ? reinterpret_cast<float*>(static_cast<uint8_t*>(g->workspace) + f32_states_bytes(p))
+                       : nullptr;
   return launch_scan_f32_bwd(p, s);
 }
 
@@ -277,7 +296,7 @@ int ts_b200_selftest_tma_mma(const void* A, const void* B, float* D, int N, int 
 size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
   if (args && args->f32_streams) {
     ScanF32Params p;
-    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) : 0;
+    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) + f32_tile_bytes(p) : 0;
   }
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;
@@ -287,7 +306,7 @@ size_t ts_b200_scan_workspace_bytes(const ts_scan_args* args) {
 size_t ts_b200_scan_bwd_workspace_bytes(const ts_scan_args* args) {
   if (args && args->f32_streams) {
     ScanF32Params p;
-    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) : 0;
+    return build_scan_f32_params(args, &p) == TS_OK ? f32_states_bytes(p) + f32_tile_bytes(p) : 0;
   }
   ScanParams p;
   if (build_scan_params(args, &p) != TS_OK) return 0;

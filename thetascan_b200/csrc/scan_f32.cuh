@@ -18,6 +18,8 @@ struct ScanF32Params {
   const float* v;
   long long qs[3], ks[3], vs[3];
   const float* la[TS_MAX_RETENTIONS];  // [H] or null (plain sum)
+  const float* las[TS_MAX_RETENTIONS]; // [B,H,T] per-token log-retention stream, or null
+  float* closing;                      // [B*H][NT][R] exp(sum of a tile's stream), stream retentions
   float* out[TS_MAX_RETENTIONS];       // [B,H,T,Dv]
   // [B*H][NT][R][Dk][Dv]: each tile's local update, then (after the tile
   // prefix) the state entering each tile
@@ -28,6 +30,8 @@ struct ScanF32Params {
   float* dk;
   float* dv;                             // [B,H,T,Dv]
   float* dla[TS_MAX_RETENTIONS];         // [H], accumulated; null = not wanted
+  float* dlas[TS_MAX_RETENTIONS];        // [B,H,T] gradient of a stream (written); null = not wanted
+  float* zterm;                          // [B*H][NT][R] C_n <G(n), S_in(n)> of stream retentions (zeroed)
   // [B*H][NT][R][Dk][Dv]: each tile's local read gradient, then the gradient
   // of the state leaving each tile
   float* gstates;

@@ -45,7 +45,8 @@ def _require_cuda(*tensors):
 
 # --------------------------------------------------------------------------- workspace sizes
 
-def _scan_workspace_nbytes(B, H, T, dk, dv_payload, n_unit, present, stale, f32_streams, backward=False):
+def _scan_workspace_nbytes(B, H, T, dk, dv_payload, n_unit, present, stale, f32_streams, backward=False,
+                           streams=None):
     """Workspace bytes of a scan call of this shape (the C ABI's size query,
     answered from shapes alone with placeholder pointers; nothing is read)."""
     lib = _lib.load()
@@ -58,7 +59,9 @@ def _scan_workspace_nbytes(B, H, T, dk, dv_payload, n_unit, present, stale, f32_
     a.v_append_unit = n_unit
     a.n_retentions = len(present)
     for i, p in enumerate(present):
-        a.log_alpha[i] = 256 if p else None
+        stream = bool(streams and streams[i])
+        a.log_alpha[i] = 256 if (p and not stream) else None
+        a.log_alpha_stream[i] = 256 if (p and stream) else None
         a.stale[i] = 1 if (stale and stale[i]) else 0
         a.out[i] = 256
     a.out_dtype = _lib.TS_DTYPE_F32
@@ -77,7 +80,8 @@ def scan_views_fwd(q: Tensor, k: Tensor, v: Tensor, log_alphas: list[Tensor], pr
                    append_unit: int, stale: list[bool], round_streams: bool) -> tuple[Tensor, Tensor]:
     """Reads f32 ``[R,B,H,T,Dv(+unit)]`` of every retention and the forward
     workspace.  Retention r is the plain sum where ``present[r]`` is False,
-    else the next tensor of ``log_alphas`` (static, ``[H]``).
+    else the next tensor of ``log_alphas`` (static ``[H]``, or a per-token
+    stream ``[B,H,T,1]``, which runs the float32 CUDA-core kernels).
     ``round_streams``: float32 q/k/v are rounded to bf16 and run on the
     tensor cores (the GN family's per-token math is float32)."""
     from .scan import _scan_fwd_impl
@@ -90,22 +94,28 @@ def _retentions(log_alphas, present):
     return [next(it) if p else None for p in present]
 
 
+def _stream_flags(log_alphas, present):
+    return [r is not None and r.ndim == 4 for r in _retentions(log_alphas, present)]
+
+
 @scan_views_fwd.register_fake
 def _(q, k, v, log_alphas, present, append_unit, stale, round_streams):
     B, H, T, dk = (int(s) for s in q.shape)
     dvp = int(v.shape[-1])
-    f32 = q.dtype == torch.float32 and not round_streams
+    streams = _stream_flags(log_alphas, present)
+    f32 = any(streams) or (q.dtype == torch.float32 and not round_streams)
     outs = q.new_empty(len(present), B, H, T, dvp + append_unit, dtype=torch.float32)
-    nbytes = _scan_workspace_nbytes(B, H, T, dk, dvp, append_unit, list(present), stale, f32)
+    nbytes = _scan_workspace_nbytes(B, H, T, dk, dvp, append_unit, list(present), stale, f32, streams=streams)
     return outs, q.new_empty(nbytes, dtype=torch.uint8)
 
 
 @torch.library.custom_op(f"{LIB}::scan_views_bwd", mutates_args=())
 def scan_views_bwd(douts: Tensor, q: Tensor, k: Tensor, v: Tensor, log_alphas: list[Tensor], present: list[bool],
                    outs: Tensor, ws: Tensor, append_unit: int, stale: list[bool],
-                   round_streams: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Gradients of q, k, v (f32, v without the unit columns) and of every
-    retention (f32 ``[R,H]``, zero rows for the plain sum)."""
+                   round_streams: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Gradients of q, k, v (f32, v without the unit columns), of every static
+    retention (f32 ``[R,H]``, zero rows for the plain sum and for streams) and
+    of the S per-token retention streams (f32 ``[S,B,H,T]``, in order)."""
     from .scan import _scan_bwd_impl
     _require_cuda(douts, q, k, v, outs, ws, *log_alphas)
     return _scan_bwd_impl(douts, q, k, v, _retentions(log_alphas, present), outs, ws, append_unit, stale,
@@ -115,8 +125,9 @@ def scan_views_bwd(douts: Tensor, q: Tensor, k: Tensor, v: Tensor, log_alphas: l
 @scan_views_bwd.register_fake
 def _(douts, q, k, v, log_alphas, present, outs, ws, append_unit, stale, round_streams):
     f = torch.float32
+    n_streams = sum(_stream_flags(log_alphas, present))
     return (q.new_empty(q.shape, dtype=f), k.new_empty(k.shape, dtype=f), v.new_empty(v.shape, dtype=f),
-            q.new_empty(len(present), q.shape[1], dtype=f))
+            q.new_empty(len(present), q.shape[1], dtype=f), q.new_empty(n_streams, *q.shape[:3], dtype=f))
 
 
 def _scan_setup(ctx, inputs, output):
@@ -136,11 +147,17 @@ def _scan_backward(ctx, douts, dws):
     append_unit, stale, round_streams = ctx.args
     if douts is None:
         douts = torch.zeros_like(outs)
-    dq, dk, dv, dla = scan_views_bwd(douts, q, k, v, log_alphas, ctx.present, outs, ws, append_unit, stale,
-                                     round_streams)
+    dq, dk, dv, dla, dstream = scan_views_bwd(douts, q, k, v, log_alphas, ctx.present, outs, ws, append_unit,
+                                              stale, round_streams)
     qd, kd, vd = ctx.dtypes
     rows = [i for i, p in enumerate(ctx.present) if p]
-    dret = [dla[i].to(meta[0]).reshape(meta[1]) for i, meta in zip(rows, ctx.ret_meta)]
+    dret, s_index = [], 0
+    for i, (dtype, shape) in zip(rows, ctx.ret_meta):
+        if len(shape) == 4:
+            dret.append(dstream[s_index].to(dtype).reshape(shape))
+            s_index += 1
+        else:
+            dret.append(dla[i].to(dtype).reshape(shape))
     return dq.to(qd), dk.to(kd), dv.to(vd), dret, None, None, None, None
 
 

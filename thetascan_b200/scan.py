@@ -10,11 +10,19 @@ reference's but does not change the result: the kernels tile the sequence in
 Supported: bf16 streams on the tensor cores and float32 streams on the CUDA
 cores (f32 FMAs: the float32 tolerance of the reference is out of reach of
 bf16 or tf32 operands), on a CUDA device, with the plain causal sum
-(``None``) and static per-head log-retentions (``[H]``), up to four
-retentions per call, ``Dk`` and ``Dv`` up to 256 within the CTA budgets
-(float32: ``Dk = 128`` with ``Dv <= 248``, ``Dk = 256`` with ``Dv <= 123``).  Per-token retention streams (``[B,H,T,1]``) and mixed stream
-dtypes raise ``NotImplementedError``; a non-CUDA tensor raises
-``RuntimeError``.  Nothing falls back to a CPU implementation.
+(``None``), static per-head log-retentions (``[H]``) and per-token
+log-retention streams (``[B,H,T,1]``, on the float32 CUDA-core kernels for
+either stream dtype: per-tile cumulative log phases, one closing factor per
+tile), up to four retentions per call, ``Dk`` and ``Dv`` up to 256 within
+the CTA budgets (float32: ``Dk = 128`` with ``Dv <= 248``, ``Dk = 256`` with
+``Dv <= 123``).  Mixed stream dtypes raise ``NotImplementedError``; a
+non-CUDA tensor raises ``RuntimeError``.  Nothing falls back to a CPU
+implementation.
+
+A stream's weights are the exact products ``exp(L_t - L_i)`` of its
+cumulative log-retention.  The reference clamps the intra-chunk exponent at
+zero (scan_chunk.py:150-153), which only acts on positive entries (growth)
+and then depends on its chunk width; for entries <= 0 the two agree.
 """
 from __future__ import annotations
 
@@ -42,7 +50,17 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def _build_args(q, k, v, las, outs, append_unit, workspace=None, stale=None):
+def _is_stream(r):
+    return r is not None and r.ndim == 4
+
+
+def _flat_retentions(retentions):
+    """Static ``[H]`` and stream ``[B,H,T,1]`` retentions as contiguous f32
+    (a stream flattens to the kernels' ``[B,H,T]`` layout)."""
+    return [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+
+
+def _build_args(q, k, v, las, outs, append_unit, workspace=None, stale=None, streams=None):
     B, H, T, Dk = q.shape
     a = _lib.ScanArgs()
     a.batch, a.heads, a.tokens, a.dk = B, H, T, Dk
@@ -53,7 +71,9 @@ def _build_args(q, k, v, las, outs, append_unit, workspace=None, stale=None):
     a.v_append_unit = n_unit
     a.n_retentions = len(las)
     for i, la in enumerate(las):
-        a.log_alpha[i] = None if la is None else la.data_ptr()
+        stream = bool(streams and streams[i])
+        a.log_alpha[i] = None if (la is None or stream) else la.data_ptr()
+        a.log_alpha_stream[i] = la.data_ptr() if (la is not None and stream) else None
         a.stale[i] = 1 if (stale and stale[i]) else 0
         if outs is not None:
             a.out[i] = outs[i].data_ptr()
@@ -76,43 +96,63 @@ def _scan_fwd_impl(q, k, v, retentions, append_unit, stale, round_streams):
     retention, stacked ``[R,B,H,T,Dv(+unit)]``, and the workspace that holds
     the carried chunk states for the backward."""
     lib = _lib.load()
-    if round_streams:
-        q, k, v = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    q, k, v = _operand_streams(q, k, v, retentions, round_streams)
+    las = _flat_retentions(retentions)
+    streams = [_is_stream(r) for r in retentions]
     B, H, T, _ = q.shape
     dv = v.shape[-1] + append_unit
     # The kernels write f32 reads; the backward's log-retention term uses
     # them unrounded, and the caller casts them to the stream dtype.
     outs_all = torch.empty(len(las), B, H, T, dv, dtype=torch.float32, device=q.device)
-    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, stale=stale if any(stale) else None)
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, stale=stale if any(stale) else None,
+                       streams=streams)
     ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, args, q.device)
     args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(args), _stream()))
     return outs_all, ws
 
 
+def _operand_streams(q, k, v, retentions, round_streams):
+    """The q, k, v the kernels read: per-token retention streams run on the
+    float32 CUDA-core kernels (bf16 streams are widened, exactly), otherwise
+    ``round_streams`` rounds float32 streams to bf16 for the tensor cores."""
+    if any(_is_stream(r) for r in retentions):
+        return tuple(x.to(torch.float32) for x in (q, k, v))
+    if round_streams:
+        return tuple(x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+    return q, k, v
+
+
 def _scan_bwd_impl(douts, q, k, v, retentions, outs_all, ws, append_unit, stale, round_streams):
     """Body of the ``thetascan_b200::scan_views_bwd`` op: f32 gradients of q,
-    k, v (without the unit columns) and ``[R,H]`` log-retention gradients."""
+    k, v (without the unit columns), ``[R,H]`` static log-retention gradients
+    and ``[S,B,H,T]`` gradients of the S per-token retention streams."""
     lib = _lib.load()
-    if round_streams:
-        q, k, v = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-    las = [None if r is None else r.detach().reshape(-1).to(torch.float32).contiguous() for r in retentions]
+    q, k, v = _operand_streams(q, k, v, retentions, round_streams)
+    las = _flat_retentions(retentions)
+    streams = [_is_stream(r) for r in retentions]
     n = len(las)
     B, H, T, Dk = q.shape
     dv_width = outs_all.shape[-1]
     # bf16 streams take bf16 read gradients; f32 streams keep them f32
     gdt = torch.float32 if q.dtype == torch.float32 else torch.bfloat16
     dgrads = [douts[i].to(gdt).contiguous() for i in range(n)]
-    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, ws, stale=stale if any(stale) else None)
+    args = _build_args(q, k, v, las, list(outs_all.unbind(0)), append_unit, ws, stale=stale if any(stale) else None,
+                       streams=streams)
     g = _lib.ScanGradArgs()
     dq = torch.empty(B, H, T, Dk, dtype=torch.float32, device=q.device)
     dk = torch.empty_like(dq)
     dvv = torch.empty(B, H, T, dv_width, dtype=torch.float32, device=q.device)
     dla = torch.zeros(n, H, dtype=torch.float32, device=q.device)
+    dstream = torch.empty(sum(streams), B, H, T, dtype=torch.float32, device=q.device)
+    s_index = 0
     for i in range(n):
         g.dout[i] = dgrads[i].data_ptr()
-        g.dlog_alpha[i] = None if las[i] is None else dla[i].data_ptr()
+        if streams[i]:
+            g.dlog_alpha_stream[i] = dstream[s_index].data_ptr()
+            s_index += 1
+        else:
+            g.dlog_alpha[i] = None if las[i] is None else dla[i].data_ptr()
     g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dvv.data_ptr()
     g.grad_dtype = _lib.TS_DTYPE_F32
     gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, args, q.device)
@@ -120,7 +160,7 @@ def _scan_bwd_impl(douts, q, k, v, retentions, outs_all, ws, append_unit, stale,
     _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(args), ctypes.byref(g), _stream()))
     if append_unit:
         dvv = dvv[..., :v.shape[-1]].contiguous()
-    return dq, dk, dvv, dla
+    return dq, dk, dvv, dla, dstream
 
 
 def _scan_views_op(q, k, v, retentions, append_unit, stale, round_streams):
@@ -154,14 +194,19 @@ def _check_inputs(q, k, v, retentions, chunk):
         raise NotImplementedError(
             "b200 backend: q, k and v must all be bf16 (tensor cores) or all float32 (CUDA cores), "
             f"got {q.dtype}, {k.dtype}, {v.dtype}")
-    H = q.shape[1]
+    B, H, T = q.shape[:3]
     for r in retentions:
         if r is None:
             continue
         if r.ndim == 4:
             if r.shape[-1] != 1:
                 raise NotImplementedError("chunk backend: scalar decay only (v1)")
-            raise NotImplementedError("b200 backend: per-token retention streams are not supported yet")
+            if tuple(r.shape[:3]) != (B, H, T):
+                raise ValueError(
+                    f"b200 scan: a retention stream must be [B,H,T,1], got {tuple(r.shape)} for q {tuple(q.shape)}")
+            if not r.is_cuda:
+                raise RuntimeError("b200 backend requires CUDA tensors")
+            continue
         if r.numel() != H:
             raise ValueError(
                 "chunk backend: a static retention needs one entry per head, "
@@ -187,12 +232,14 @@ def linattn_views(q, k, v, retentions, chunk: int = DEFAULT_CHUNK, *, append_uni
     for r, st in zip(retentions, stale):
         if st and r is None:
             raise ValueError("b200 scan: a stale view needs a retention")
-    if any(stale) and q.dtype == torch.float32:
-        # float32: the stale view as the reference forms it, S_sum - S_fast
-        # (FadeStale.scan_terms, interface.py:268-273); the difference loses
-        # nothing the float32 tolerance would see
-        reads = linattn_views(q, k, v, tuple(retentions) + (None,), chunk, append_unit=append_unit)
-        return tuple(reads[-1] - o if st else o for o, st in zip(reads[:-1], stale))
+    streams = any(_is_stream(r) for r in retentions)
+    if any(stale) and (q.dtype == torch.float32 or streams):
+        # float32 kernels: the stale view as the reference forms it, S_sum -
+        # S_fast (FadeStale.scan_terms, interface.py:268-273); the difference
+        # loses nothing the float32 tolerance would see
+        wide = tuple(x.to(torch.float32) for x in (q, k, v))
+        reads = linattn_views(*wide, tuple(retentions) + (None,), chunk, append_unit=append_unit)
+        return tuple((reads[-1] - o if st else o).to(q.dtype) for o, st in zip(reads[:-1], stale))
     outs = []
     # The kernels take at most four retentions per call; longer tuples are split.
     for start in range(0, len(retentions), _lib.MAX_RETENTIONS):
@@ -286,6 +333,8 @@ def linattn_views_stream(q, k, v, retentions, state=None, *, append_unit: bool =
     _check_inputs(q, k, v, retentions, DEFAULT_CHUNK)
     if q.dtype == torch.float32:
         raise NotImplementedError("b200 streaming scan: bf16 streams only")
+    if any(_is_stream(r) for r in retentions):
+        raise NotImplementedError("b200 streaming scan: static retentions only (per-token streams take linattn_views)")
     if len(retentions) > _lib.MAX_RETENTIONS:
         raise NotImplementedError(f"b200 streaming scan: at most {_lib.MAX_RETENTIONS} retentions per call")
     from . import ops  # noqa: F401  (registers the operators)
