@@ -58,6 +58,10 @@ CONFIGS = {
                rope="partial", J=3, retentions=(0.9, 0.99, 0.999), seqpar=True),
     # config 3: Gauss-Newton fast weights, head_dim 128, m = 128, relu2, two-stage
     # feature-mass read (both_feature_mass), one Jacobian step, the plain sum view.
+    # The reference rejects a feature-mass read normalisation for any net but
+    # relu2 / relu2_threshold (config.py:85-90), so config 3's "tanh with read
+    # normalisation on" runs as relu2 here; the tanh net (with damping) is
+    # checked for parity with the read normalisation off.
     # config 5: a ~17M-parameter hybrid LM training step (nine blocks, d_model
     # 512, 8 heads, vocab 1024, tied embeddings, MLP ratio 2; the two middle
     # blocks ThetaScan-GN with 2x expansion, the rest causal attention),

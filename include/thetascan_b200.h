@@ -412,6 +412,81 @@ typedef struct ts_mass_grad_args {
 size_t ts_b200_mass_query_bwd_workspace_bytes(const ts_mass_args* args);
 int ts_b200_mass_query_bwd(const ts_mass_args* args, const ts_mass_grad_args* grad, ts_stream_t stream);
 
+/* ------------------------------------------------------------------ GN rows
+ *
+ * Per-token row maps of the Gauss--Newton fast-weight family, forward and
+ * backward: the write of engine._forward_theta0 / write_streams (one
+ * Jacobian step, depth 1; src/thetascan/_core/ops/engine.py:161-340) and the
+ * two read stages of engine.dual_read_views with the GN read normalisations
+ * (engine.py:455-528).  The per-head linear maps between the stages
+ * (W1 [H,m,d], W2 [H,d,m]: a = W1 k, O = W2 h, RS = (W2 o W2) s^2,
+ * U = W2^T lam, ...) are plain GEMMs over all tokens of a head and run
+ * outside these calls.  Every row tensor is f32 [B,H,T,width] contiguous
+ * (width d, m, d+1, m+1 as given, or 1 for per-row scalars); d, m <= 256.
+ *
+ *   stage                in[]                                   out[]
+ *   TS_GN_WRITE_PRE      a=W1 k [m], k [d]                      h [m], s2 [m], hh [1], kk [1]
+ *        inv = (mean a^2 + eps)^-1/2, p = a inv - tau, h = sigma(p),
+ *        s2 = (sigma'(p) inv)^2, hh = |h|^2, kk = |k|^2
+ *   TS_GN_WRITE_LAM      v, k, O=W2 h, RS [d], hh, kk           lam [d]
+ *        lam = (v - k - O) / (hh + kk RS + eps)
+ *   TS_GN_WRITE_G        a [m], U=W2^T lam [m]                  g [m] = sigma'(p) U inv
+ *   TS_GN_QUERY_PRE      a_q=W1 q [m]                           h0 [m] = relu2(a_q inv - tau)
+ *   TS_GN_FEATURES       a_q [m], R [m(+1)] or NULL             hq [m] = sigma(pre inv - tau)
+ *        pre = a_q + R[:m] / (R[m] + eps) (flags bit 0: R normalised by its
+ *        mass column), a_q + R (bit 0 clear), a_q (R NULL)
+ *   TS_GN_OUT            q, base=W2 hq [d], C [d(+1)]           y = q + base + C[:d] / (C[d] + eps)
+ *        (flags bit 0; clear: y = q + base + C)
+ *   TS_GN_OUT_BWD        dy [d], C [d+1]                        dC [d+1]
+ *   TS_GN_FEATURES_BWD   a_q, R (as forward), dhq [m]           da_q [m], dR [m(+1)]
+ *   TS_GN_QUERY_PRE_BWD  dh0 [m], a_q [m]                       da_q [m]
+ *   TS_GN_WRITE_G_BWD    dg [m], a [m]                          du [m] = dg sigma'(p) inv
+ *   TS_GN_WRITE_LAM_BWD  dlam, dlamW=W2 du, v, k, O, RS [d],    dv [d], drowsq [d], dk [d], dhh [1]
+ *                        hh, kk
+ *        dk holds the k terms outside a = W1 k (-dv + 2 k dkk)
+ *   TS_GN_WRITE_PRE_BWD  dh [m], dhO=W2^T dv [m], ds2 [m],      da [m]
+ *                        dhh [1], dg [m], U [m], a [m]
+ * Backward stages add the threshold's gradient into dtau when both tau and
+ * dtau are set; flags bit 1 makes FEATURES_BWD and QUERY_PRE_BWD add into
+ * da_q instead of overwriting it.  tau is the relu2_threshold parameter
+ * (its [H,m,1] tensor), subtracted after the normalisation.
+ */
+enum {
+  TS_GN_RELU2 = 0,
+  TS_GN_SILU = 1,
+  TS_GN_TANH = 2
+};
+
+enum {
+  TS_GN_WRITE_PRE = 1,
+  TS_GN_WRITE_LAM = 2,
+  TS_GN_WRITE_G = 3,
+  TS_GN_QUERY_PRE = 4,
+  TS_GN_FEATURES = 5,
+  TS_GN_OUT = 6,
+  TS_GN_OUT_BWD = 7,
+  TS_GN_FEATURES_BWD = 8,
+  TS_GN_QUERY_PRE_BWD = 9,
+  TS_GN_WRITE_G_BWD = 10,
+  TS_GN_WRITE_LAM_BWD = 11,
+  TS_GN_WRITE_PRE_BWD = 12
+};
+
+typedef struct ts_gn_rows_args {
+  int batch, heads, tokens;
+  int d, m;                 /* head width, fast-net hidden width: 1..256 */
+  int nonlinearity;         /* TS_GN_RELU2 / TS_GN_SILU / TS_GN_TANH (sigma of the net) */
+  float eps;                /* the net's epsilon: normalisation, damping and read masses */
+  const float* tau;         /* f32 [H,m] threshold, or NULL */
+  float* dtau;              /* f32 [H,m], ACCUMULATED (backward stages), or NULL */
+  int stage;                /* TS_GN_* */
+  int flags;                /* bit 0: normalised read; bit 1: accumulate da_q */
+  const float* in[8];       /* per stage, in the order of the table; 16-byte aligned not required */
+  float* out[4];
+} ts_gn_rows_args;
+
+int ts_b200_gn_rows(const ts_gn_rows_args* args, ts_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -140,6 +140,19 @@ class MassGradArgs(ctypes.Structure):
     ]
 
 
+class GnRowsArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int),
+        ("d", ctypes.c_int), ("m", ctypes.c_int), ("nonlinearity", ctypes.c_int), ("eps", ctypes.c_float),
+        ("tau", ctypes.c_void_p), ("dtau", ctypes.c_void_p), ("stage", ctypes.c_int), ("flags", ctypes.c_int),
+        ("inputs", ctypes.c_void_p * 8), ("outputs", ctypes.c_void_p * 4),
+    ]
+
+
+TS_GN_RELU2, TS_GN_SILU, TS_GN_TANH = 0, 1, 2
+(TS_GN_WRITE_PRE, TS_GN_WRITE_LAM, TS_GN_WRITE_G, TS_GN_QUERY_PRE, TS_GN_FEATURES, TS_GN_OUT, TS_GN_OUT_BWD,
+ TS_GN_FEATURES_BWD, TS_GN_QUERY_PRE_BWD, TS_GN_WRITE_G_BWD, TS_GN_WRITE_LAM_BWD, TS_GN_WRITE_PRE_BWD) = range(1, 13)
+
 TS_FEATURE_RELU2, TS_FEATURE_SOFTMAX, TS_FEATURE_BSPLINE = 0, 1, 2
 TS_VIEWS_SUM, TS_VIEWS_FAST, TS_VIEWS_STALE = 0, 1, 2
 
@@ -154,6 +167,7 @@ SIGNATURES.update({
     "ts_b200_mass_query_bwd_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MassArgs)]),
     "ts_b200_mass_query_bwd": (ctypes.c_int, [ctypes.POINTER(MassArgs), ctypes.POINTER(MassGradArgs),
                                               ctypes.c_void_p]),
+    "ts_b200_gn_rows": (ctypes.c_int, [ctypes.POINTER(GnRowsArgs), ctypes.c_void_p]),
 })
 
 _lock = threading.Lock()

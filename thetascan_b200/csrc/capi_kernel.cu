@@ -257,3 +257,45 @@ int ts_b200_mass_query_bwd(const ts_mass_args* args, const ts_mass_grad_args* gr
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- GN rows
+
+int ts_b200_gn_rows(const ts_gn_rows_args* a, ts_stream_t stream) {
+  using namespace ts;
+  if (!a) return set_error(TS_ERR_VALUE, "gn_rows: null arguments");
+  if (a->batch < 0 || a->heads < 0 || a->tokens < 0)
+    return set_error(TS_ERR_VALUE, "gn_rows: negative shape");
+  if (a->d < 1 || a->m < 1 || a->d > kGnMaxWidth || a->m > kGnMaxWidth)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "gn_rows: widths d=%d, m=%d outside 1..%d", a->d, a->m, kGnMaxWidth);
+  if (a->nonlinearity < TS_GN_RELU2 || a->nonlinearity > TS_GN_TANH)
+    return set_error(TS_ERR_NOT_IMPLEMENTED, "gn_rows: unknown nonlinearity %d", a->nonlinearity);
+  // inputs and outputs each stage needs (1 = required, 2 = optional)
+  static const char kIn[13][9] = {
+      "", "11", "111111", "11", "1", "12", "111", "11", "121", "11", "11", "11111111", "1111111"};
+  static const char kOut[13][5] = {"", "1111", "1", "1", "1", "1", "1", "1", "12", "1", "1", "1111", "1"};
+  if (a->stage < TS_GN_WRITE_PRE || a->stage > TS_GN_WRITE_PRE_BWD)
+    return set_error(TS_ERR_VALUE, "gn_rows: unknown stage %d", a->stage);
+  for (int i = 0; kIn[a->stage][i]; ++i)
+    if (kIn[a->stage][i] == '1' && !a->in[i]) return set_error(TS_ERR_VALUE, "gn_rows: stage %d needs in[%d]", a->stage, i);
+  for (int i = 0; kOut[a->stage][i]; ++i)
+    if (kOut[a->stage][i] == '1' && !a->out[i])
+      return set_error(TS_ERR_VALUE, "gn_rows: stage %d needs out[%d]", a->stage, i);
+  if (a->stage == TS_GN_FEATURES_BWD && a->in[1] && !a->out[1])
+    return set_error(TS_ERR_VALUE, "gn_rows: a read's gradient needs out[1]");
+  if (a->stage == TS_GN_OUT_BWD && !(a->flags & 1))
+    return set_error(TS_ERR_VALUE, "gn_rows: OUT_BWD is the normalised read's (flags bit 0)");
+  GnRowParams p{};
+  p.B = a->batch;
+  p.H = a->heads;
+  p.T = a->tokens;
+  p.d = a->d;
+  p.m = a->m;
+  p.nonlin = a->nonlinearity;
+  p.flags = a->flags;
+  p.eps = a->eps;
+  p.tau = a->tau;
+  p.dtau = a->tau ? a->dtau : nullptr;
+  for (int i = 0; i < 8; ++i) p.in[i] = a->in[i];
+  for (int i = 0; i < 4; ++i) p.out[i] = a->out[i];
+  return launch_gn_rows(p, a->stage, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,8 +1,7 @@
 """Gauss--Newton (GN) fast-weight family on the B200 path.
 
 One memory block (depth 1) with one Jacobian step, as the reference runs
-``family="gn"`` (src/thetascan/config.py:745-756).  Per token, in f32 with
-autograd:
+``family="gn"`` (src/thetascan/config.py:745-756).  Per token and head:
 
   write (engine.py:161-340)  a = W1 k, pre = rmsnorm(a) [- tau], h = sigma(pre),
                              o = k + W2 h, r = v - o,
@@ -13,22 +12,30 @@ autograd:
                              stage 2: h_v = sigma(rmsnorm(pre_v) [- tau]),
                              y_v = q + W2 h_v + [lambda-stream read of the view].
 
-Every read over the sequence -- the T-long part -- runs on the sm_100a
-multi-view scan kernels (``ts_b200_scan_fwd/bwd``) with bf16 streams, f32
-states and f32 reads: stage 1 once for all views (one score tile per view
-set), stage 2 once per view because each view's query differs
-(engine.py:355-361).  The read normalizations follow the reference:
-``both_feature_mass`` reads [g | 1] with the positive slow features
-h0 = relu2(rmsnorm(W1 q) [- tau]) against keys h and normalizes both stages
-by their mass column; ``w2_feature_mass`` reads g with q against k
-unnormalized and normalizes stage 2; ``none`` normalizes neither.
+The core is one custom op (``thetascan_b200::gn_core_fwd`` with its
+backward ``gn_core_bwd``): the nonlinear row maps run on the GN row kernels
+(``ts_b200_gn_rows``: normalisation, activation and its derivatives, the
+damped solve, the read normalisations, forward and backward, one HBM pass
+each), the per-head linear maps (W1, W2, W2^T, W2 o W2 over all tokens of a
+head) are float32 cuBLAS GEMMs, and every read over the sequence runs on
+the sm_100a multi-view scan kernels with bf16 streams, f32 states and f32
+reads: stage 1 once for all views (one score tile per view set), stage 2
+once per view because each view's query differs (engine.py:355-361).  The
+read normalizations follow the reference: ``both_feature_mass`` reads
+[g | 1] with the positive slow features h0 = relu2(rmsnorm(W1 q) [- tau])
+against keys h and normalizes both stages by their mass column;
+``w2_feature_mass`` reads g with q against k unnormalized and normalizes
+stage 2; ``none`` normalizes neither.  The backward is written out by hand
+(no recomputation under autograd).
 """
 from __future__ import annotations
 
-import torch
-import torch.nn.functional as F
+import ctypes
 
-from .scan import scan_views_f32
+import torch
+
+from . import _lib
+from .scan import _scan_bwd_impl, _scan_fwd_impl, _stream
 
 
 class _tf32:
@@ -79,84 +86,6 @@ def per_token(fn, *tensors):
     return _PerToken.apply(fn, *tensors)
 
 
-def per_token_f32(fn, *tensors):
-    """The same block in full f32: the write's solve and the features, whose
-    gradients (the log-retention one above all, a long sum over tokens) move
-    by ~2% when their operands are rounded to TF32."""
-    return fn(*tensors)
-
-
-class _HeadMap(torch.autograd.Function):
-    """``y[b,h,t] = W[h] x[b,h,t]`` for ``W [H,o,i]``, ``x [B,H,T,i]``, f32.
-
-    The weight gradient sums over all B*T tokens of a head; as one GEMM per
-    head (what an einsum's backward does) that is a handful of output tiles
-    with a 10^5-long reduction, so few SMs work.  Here the token axis is cut
-    into chunks that become batch entries (a view of the contiguous input),
-    the per-chunk products run in parallel, and their sum is taken after."""
-
-    @staticmethod
-    def forward(ctx, W, x):
-        ctx.save_for_backward(W, x)
-        return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
-
-    @staticmethod
-    def backward(ctx, gy):
-        W, x = ctx.saved_tensors
-        gW = gx = None
-        if ctx.needs_input_grad[1]:
-            gx = torch.matmul(gy, W.unsqueeze(0))
-        if ctx.needs_input_grad[0]:
-            B, H, T, i = x.shape
-            o = gy.shape[-1]
-            xc, gc = x.contiguous(), gy.contiguous()
-            S = 1
-            while T % (2 * S) == 0 and T // (2 * S) >= 512 and B * H * S < 512:
-                S *= 2
-            part = torch.bmm(gc.view(B * H * S, T // S, o).transpose(1, 2), xc.view(B * H * S, T // S, i))
-            gW = part.view(B, H, S, o, i).sum(dim=(0, 2))
-        return gW, gx
-
-
-def head_map(W, x):
-    """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (see _HeadMap)."""
-    return _HeadMap.apply(W, x)
-
-
-def _activation(nonlin, pre):
-    if nonlin == "relu2":
-        r = F.relu(pre)
-        return r * r
-    if nonlin == "silu":
-        return F.silu(pre)
-    if nonlin == "tanh":
-        return torch.tanh(pre)
-    raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
-
-
-def _activation_grad(nonlin, pre):
-    if nonlin == "relu2":
-        return 2.0 * F.relu(pre)
-    if nonlin == "silu":
-        s = torch.sigmoid(pre)
-        return s * (1 + pre * (1 - s))
-    if nonlin == "tanh":
-        # sigma'(pre) = 1 - tanh(pre)^2, the table's (act, dact(pre, h)) pattern
-        h = torch.tanh(pre)
-        return 1.0 - h * h
-    raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
-
-
-def _rmsnorm(a, eps):
-    """``a * rsqrt(mean(a^2) + eps)`` and the factor (reference norms.py:5-8)."""
-    inv = torch.rsqrt(a.square().mean(-1, keepdim=True) + eps)
-    return a * inv, inv
-
-
-def _thresholded(pre, tau):
-    return pre if tau is None else pre - tau[..., 0].unsqueeze(0).unsqueeze(2).to(pre.dtype)
-
-
 def _views(mode, J):
     """Retention slots of each view: slot 0 the plain sum, 1+j branch j (its
     decayed scan for a fast bank, its stale scan for a stale bank)."""
@@ -175,98 +104,319 @@ def _piece_width(n_retentions, Dk):
     return 144
 
 
-def _scan(query, keys, payload, append_unit, retentions, stale=None):
-    """f32 reads of the multi-view scan kernels (bf16 streams, f32 gradients
-    back).  The scan is linear in the payload, so a payload wider than one
-    call takes is read in column pieces (the mass column rides on the last)."""
-    width = payload.shape[-1]
-    step = _piece_width(len(retentions), query.shape[-1]) - 1
-    if width + (1 if append_unit else 0) <= step + 1:
-        return scan_views_f32(query, keys, payload, append_unit, stale, retentions)
-    parts = [[] for _ in retentions]
-    for start in range(0, width, step):
-        piece = payload[..., start:start + step]
-        last = start + step >= width
-        for i, read in enumerate(scan_views_f32(query, keys, piece, append_unit and last, stale, retentions)):
-            parts[i].append(read)
-    return tuple(torch.cat(p, dim=-1) for p in parts)
+# --------------------------------------------------------------------------- GN core on the row kernels
+
+_NONLIN = {"relu2": _lib.TS_GN_RELU2, "silu": _lib.TS_GN_SILU, "tanh": _lib.TS_GN_TANH}
 
 
-def gn_write(k, v, W1, W2, tau, nonlin, eps):
-    """(h, g, lambda) of every token, f32 (reference engine.py:161-340, depth 1)."""
-    a = head_map(W1, k)
-    pre, inv = _rmsnorm(a, eps)
-    pre = _thresholded(pre, tau)
-    h = _activation(nonlin, pre)
-    o = k + head_map(W2, h)
-    r = v - o
-    dsig = _activation_grad(nonlin, pre)
-    s = dsig * inv
-    rowsq = head_map(W2 * W2, s * s)
-    diag = h.square().sum(-1, keepdim=True) + k.square().sum(-1, keepdim=True) * rowsq
-    lam = r / (diag + eps)
-    g = dsig * head_map(W2.transpose(1, 2), lam) * inv
-    return h, g, lam
+class _Run:
+    """One GN core evaluation: its shape, the row-kernel launcher and the
+    allocator.  With ``fake`` set (the custom op's fake implementation)
+    nothing is launched and only the shapes of the results are formed, so
+    that the real and fake outputs come from one code path."""
+
+    def __init__(self, q, m, tau, nonlin, eps, fake):
+        if nonlin not in _NONLIN:
+            raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
+        self.B, self.H, self.T, self.d = (int(x) for x in q.shape)
+        self.m, self.nl, self.eps, self.fake = int(m), _NONLIN[nonlin], float(eps), fake
+        self.like = q
+        self.tau = None if tau is None else tau[..., 0].float().contiguous()   # [H, m]
+
+    def new(self, width, zero=False):
+        shape = (self.B, self.H, self.T) + ((width,) if width else ())
+        f = torch.zeros if zero else torch.empty
+        return f(shape, dtype=torch.float32, device=self.like.device)
+
+    def rows(self, stage, ins, outs, flags=0, dtau=None):
+        if self.fake:
+            return
+        a = _lib.GnRowsArgs()
+        a.batch, a.heads, a.tokens, a.d, a.m = self.B, self.H, self.T, self.d, self.m
+        a.nonlinearity, a.eps, a.stage, a.flags = self.nl, self.eps, stage, flags
+        a.tau = None if self.tau is None else self.tau.data_ptr()
+        a.dtau = None if dtau is None else dtau.data_ptr()
+        for i, x in enumerate(ins):
+            a.inputs[i] = None if x is None else x.data_ptr()
+        for i, x in enumerate(outs):
+            a.outputs[i] = None if x is None else x.data_ptr()
+        _lib.check(_lib.load().ts_b200_gn_rows(ctypes.byref(a), _stream()))
+
+    # ----------------------------------------------------------- scans
+
+    def scan_fwd(self, query, keys, payload, unit, rets, stale):
+        """Reads of every retention (f32, ``[B,H,T,W(+1)]``) and the state the
+        backward needs: one scan call per payload piece (see _piece_width)."""
+        pieces, reads = [], [[] for _ in rets]
+        for start, stop, u in _scan_pieces(payload.shape[-1], unit, len(rets), query.shape[-1]):
+            piece = payload[..., start:stop]
+            if self.fake:
+                from .ops import _scan_workspace_nbytes
+                outs = self.like.new_empty(len(rets), self.B, self.H, self.T, stop - start + int(u),
+                                           dtype=torch.float32)
+                nbytes = _scan_workspace_nbytes(self.B, self.H, self.T, int(query.shape[-1]), stop - start, int(u),
+                                                [r is not None for r in rets], stale, False)
+                ws = self.like.new_empty(nbytes, dtype=torch.uint8)
+            else:
+                outs, ws = _scan_fwd_impl(query, keys, piece.contiguous(), rets, int(u), list(stale), True)
+            pieces.append((start, stop, u, outs, ws))
+            for i in range(len(rets)):
+                reads[i].append(outs[i])
+        return [r[0] if len(r) == 1 else torch.cat(r, dim=-1) for r in reads], pieces
+
+    def scan_bwd(self, douts, query, keys, payload, pieces, rets, stale):
+        """Gradients of query, keys, payload and the ``[R,H]`` log-retentions
+        from the reads' gradients ``douts`` (one per retention)."""
+        dq = dk = None
+        dla = torch.zeros(len(rets), self.H, dtype=torch.float32, device=self.like.device)
+        dp = []
+        for start, stop, u, outs, ws in pieces:
+            w = stop - start + int(u)
+            g = [d_[..., start:start + w] for d_ in douts]
+            if self.fake:
+                pq, pk = torch.empty_like(query, dtype=torch.float32), torch.empty_like(keys, dtype=torch.float32)
+                pv = self.new(stop - start)
+            else:
+                pq, pk, pv, pla, _ = _scan_bwd_impl(g, query, keys, payload[..., start:stop].contiguous(), rets,
+                                                    outs, ws, int(u), list(stale), True)
+                dla += pla
+            dq = pq if dq is None else dq + pq
+            dk = pk if dk is None else dk + pk
+            dp.append(pv)
+        return dq, dk, dp[0] if len(dp) == 1 else torch.cat(dp, dim=-1), dla
+
+
+def _hm(W, x):
+    """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (batched GEMM)."""
+    return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+
+
+def _hm_wgrad(gy, x):
+    """``sum_{b,t} gy[b,h,t] x[b,h,t]^T`` per head, ``[H,o,i]``: the token axis
+    cut into chunks that run as parallel batched products, summed after."""
+    B, H, T, i = x.shape
+    o = gy.shape[-1]
+    S = 1
+    while T % (2 * S) == 0 and T // (2 * S) >= 512 and B * H * S < 512:
+        S *= 2
+    part = torch.bmm(gy.contiguous().view(B * H * S, T // S, o).transpose(1, 2),
+                     x.contiguous().view(B * H * S, T // S, i))
+    return part.view(B, H, S, o, i).sum(dim=(0, 2))
+
+
+def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, fake):
+    """The GN core: ``y`` and the tensors its backward reads (a flat list, in
+    the order _gn_backward takes them)."""
+    B, H, T, d = q.shape
+    m = W1.shape[1]
+    run = _Run(q, m, tau, nonlin, eps, fake)
+    W1, W2 = W1.float().contiguous(), W2.float().contiguous()
+    J = 0 if log_alphas is None else int(log_alphas.shape[0])
+    las = [None] + [log_alphas[j].float() for j in range(J)]
+    stale = [False] + [mode == "stale"] * J
+    a_k, h_k, s2, hh, kk, O, RS, lam, U, g = _write_forward(run, k, v, W1, W2)
+    # stage 1, shared by all views (engine.py:475-500)
+    a_q = _hm(W1, q)
+    if read_norm_w1:
+        h0 = run.new(m)
+        run.rows(_lib.TS_GN_QUERY_PRE, [a_q], [h0])
+        R1, st1 = run.scan_fwd(h0, h_k, g, True, las, stale)
+    else:
+        h0 = q.new_empty(0)
+        R1, st1 = run.scan_fwd(q, k, g, False, las, stale)
+    saved = [a_k, h_k, s2, hh, kk, O, RS, lam, U, g, a_q, h0]
+    saved += [x for piece in st1 for x in piece[3:]]
+    ys = []
+    # stage 2, one query per view (engine.py:500-528)
+    for s in range(J + 1):
+        hq = run.new(m)
+        run.rows(_lib.TS_GN_FEATURES, [a_q, R1[s]], [hq], flags=int(read_norm_w1))
+        base = _hm(W2, hq)
+        (C,), st2 = run.scan_fwd(hq, h_k, lam, bool(read_norm), [las[s]], [stale[s]])
+        y = run.new(d)
+        run.rows(_lib.TS_GN_OUT, [q, base, C], [y], flags=int(bool(read_norm)))
+        ys.append(y)
+        saved += [hq] + [x for piece in st2 for x in piece[3:]]
+    y = ys[0]
+    if J and mode == "stale":
+        # y - sum_j eta_j (y_stale_j - y_base), y_base the zero-memory read
+        # (pre = W1 q, no memory term; block.py:697-718)
+        hb = run.new(m)
+        run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
+        y_base = q + _hm(W2, hb)
+        for j in range(J):
+            y = y - etas[j].float().view(1, -1, 1, 1) * (ys[1 + j] - y_base)
+        saved += ys + [y_base]
+    elif J:
+        for j in range(J):
+            y = y + etas[j].float().view(1, -1, 1, 1) * (ys[1 + j] - ys[0])
+        saved += ys
+    return y, saved
+
+
+def _take(saved, n):
+    out, rest = saved[:n], saved[n:]
+    return out, rest
+
+
+def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read_norm, read_norm_w1, mode, eps,
+                 fake):
+    """Gradients of the GN core: q, k, v, W1, W2, tau, log_alphas, etas."""
+    B, H, T, d = q.shape
+    m = W1.shape[1]
+    run = _Run(q, m, tau, nonlin, eps, fake)
+    W1, W2 = W1.float().contiguous(), W2.float().contiguous()
+    W2t = W2.transpose(1, 2)
+    J = 0 if log_alphas is None else int(log_alphas.shape[0])
+    las = [None] + [log_alphas[j].float() for j in range(J)]
+    stale = [False] + [mode == "stale"] * J
+    (a_k, h_k, s2, hh, kk, O, RS, lam, U, g, a_q, h0), rest = _take(saved, 12)
+    q1 = h0 if read_norm_w1 else q
+    k1 = h_k if read_norm_w1 else k
+    n1 = len(_scan_pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1]))
+    flat1, rest = _take(rest, 2 * n1)
+    st1 = _pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1], flat1)
+    views = []
+    for s in range(J + 1):
+        (hq,), rest = _take(rest, 1)
+        n2 = len(_scan_pieces(d, bool(read_norm), 1, m))
+        flat2, rest = _take(rest, 2 * n2)
+        views.append((hq, _pieces(d, bool(read_norm), 1, m, flat2)))
+    dy = dy.float().contiguous()
+    # the view combination
+    tau_grad = None if tau is None else torch.zeros(H, m, dtype=torch.float32, device=q.device)
+    dla = torch.zeros(J + 1, H, dtype=torch.float32, device=q.device)
+    deta = None if J == 0 else torch.zeros(J, H, dtype=torch.float32, device=q.device)
+    # q enters every view and the zero-memory base with coefficients that sum to one
+    dq = dy.clone()
+    dys = [dy]
+    dy_base = None
+    if J:
+        ys, rest = _take(rest, J + 1)
+        e = etas.float()
+        if mode == "stale":
+            (y_base,), rest = _take(rest, 1)
+            dys = [dy] + [-e[j].view(1, -1, 1, 1) * dy for j in range(J)]
+            dy_base = e.sum(0).view(1, -1, 1, 1) * dy
+            for j in range(J):
+                deta[j] = -(dy * (ys[1 + j] - y_base)).sum(dim=(0, 2, 3))
+        else:
+            dys = [(1.0 - e.sum(0)).view(1, -1, 1, 1) * dy] + [e[j].view(1, -1, 1, 1) * dy for j in range(J)]
+            for j in range(J):
+                deta[j] = (dy * (ys[1 + j] - ys[0])).sum(dim=(0, 2, 3))
+    dW2 = torch.zeros_like(W2)
+    dh_k = run.new(m, zero=True)
+    dlam = run.new(d, zero=True)
+    da_q = run.new(m)
+    R1 = [torch.cat([p[3][i] for p in st1], dim=-1) if len(st1) > 1 else st1[0][3][i] for i in range(J + 1)]
+    dR1 = [run.new(R1[0].shape[-1]) for _ in range(J + 1)]
+    for s, (hq, st2) in enumerate(views):
+        C = st2[0][3][0] if len(st2) == 1 else torch.cat([p[3][0] for p in st2], dim=-1)
+        if read_norm:
+            dC = run.new(d + 1)
+            run.rows(_lib.TS_GN_OUT_BWD, [dys[s], C], [dC], flags=1)
+        else:
+            dC = dys[s]
+        dhq, dhk_s, dlam_s, dla_s = run.scan_bwd([dC], hq, h_k, lam, st2, [las[s]], [stale[s]])
+        dh_k += dhk_s
+        dlam += dlam_s
+        dla[s] += dla_s[0]
+        dhq = dhq + _hm(W2t, dys[s])
+        dW2 += _hm_wgrad(dys[s], hq)
+        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, R1[s], dhq], [da_q, dR1[s]],
+                 flags=int(read_norm_w1) | (2 if s else 0), dtau=tau_grad)
+    if dy_base is not None:
+        hb = run.new(m)
+        run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
+        dW2 += _hm_wgrad(dy_base, hb)
+        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base)], [da_q, None], flags=2, dtau=tau_grad)
+    # stage 1
+    dq1, dk1, dg, dla1 = run.scan_bwd(dR1, q1, k1, g, st1, las, stale)
+    dla += dla1
+    dk = None
+    if read_norm_w1:
+        dh_k += dk1
+        run.rows(_lib.TS_GN_QUERY_PRE_BWD, [dq1, a_q], [da_q], flags=2, dtau=tau_grad)
+    else:
+        dq += dq1
+        dk = dk1
+    dq += _hm(W1.transpose(1, 2), da_q)
+    dW1 = _hm_wgrad(da_q, q)
+    dk_w, dv, dW1_w, dW2_w = _write_backward(run, k, v, W1, W2, (a_k, h_k, s2, hh, kk, O, RS, lam, U),
+                                             dh_k, dg, dlam, tau_grad)
+    dk = dk_w if dk is None else dk_w + dk
+    return dq, dk, dv, dW1 + dW1_w, dW2 + dW2_w, tau_grad, dla[1:], deta
+
+
+def _write_forward(run, k, v, W1, W2):
+    """The GN write (engine.py:161-340): ``a = W1 k`` and the row streams
+    ``h, s2, hh, kk, O, RS, lam, U, g`` (h the keys, g and lam the payloads of
+    the two read stages; the rest kept for the backward)."""
+    m, d = run.m, run.d
+    a_k = _hm(W1, k)
+    h_k, s2, hh, kk = run.new(m), run.new(m), run.new(0), run.new(0)
+    run.rows(_lib.TS_GN_WRITE_PRE, [a_k, k], [h_k, s2, hh, kk])
+    O, RS = _hm(W2, h_k), _hm(W2 * W2, s2)
+    lam = run.new(d)
+    run.rows(_lib.TS_GN_WRITE_LAM, [v, k, O, RS, hh, kk], [lam])
+    U = _hm(W2.transpose(1, 2), lam)
+    g = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [g])
+    return a_k, h_k, s2, hh, kk, O, RS, lam, U, g
+
+
+def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau):
+    """Gradients of k, v, W1, W2 (and tau into ``dtau``) of the write from
+    those of its outputs h, g, lam."""
+    a_k, h_k, s2, hh, kk, O, RS, lam, U = streams
+    m, d = run.m, run.d
+    W2t = W2.transpose(1, 2)
+    du = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_G_BWD, [dg, a_k], [du])
+    dlamW = _hm(W2, du)
+    dv, drowsq, dk_w, dhh = run.new(d), run.new(d), run.new(d), run.new(0)
+    run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam, dlamW, v, k, O, RS, hh, kk], [dv, drowsq, dk_w, dhh])
+    dW2 = _hm_wgrad(lam, du) - _hm_wgrad(dv, h_k) + 2.0 * W2 * _hm_wgrad(drowsq, s2)
+    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq)
+    dhO = _hm(W2t, dv)
+    da_k = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh, dhO, ds2, dhh, dg, U, a_k], [da_k], dtau=dtau)
+    dk = dk_w + _hm(W1.transpose(1, 2), da_k)
+    return dk, dv, _hm_wgrad(da_k, k), dW2
+
+
+def _scan_pieces(width, unit, n_retentions, dk):
+    step = _piece_width(n_retentions, dk) - 1
+    if width + int(unit) <= step + 1:
+        return [(0, width, unit)]
+    return [(s, min(width, s + step), unit and min(width, s + step) >= width) for s in range(0, width, step)]
+
+
+def _pieces(width, unit, n_retentions, dk, flat):
+    """The scan state of the payload pieces from the flat saved list."""
+    return [(a, b, u, flat[2 * i], flat[2 * i + 1]) for i, (a, b, u) in enumerate(_scan_pieces(width, unit,
+                                                                                                 n_retentions, dk))]
 
 
 def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_norm_w1=True, log_alphas=None,
             etas=None, mode="fast", eps=1e-6):
-    """GN mixer core ``[B,H,T,d]`` f32 from bf16 ``q, k, v`` after RoPE / L2 norm.
+    """GN mixer core ``[B,H,T,d]`` f32 from ``q, k, v`` after RoPE / L2 norm.
 
     ``W1 [H,m,d]``, ``W2 [H,d,m]`` effective weights, ``tau [H,m,1]`` the learned
     threshold of ``relu2_threshold`` (or None), ``log_alphas``/``etas``
-    ``[J,H]`` for a fast bank."""
+    ``[J,H]`` for a bank.  Runs as the ``thetascan_b200::gn_core`` custom op
+    (the row kernels of ``ts_b200_gn_rows``, cuBLAS for the per-head maps,
+    the multi-view scan kernels for the reads)."""
     for x in (q, k, v):
         if not x.is_cuda:
             raise RuntimeError("b200 backend requires CUDA tensors")
-    m, d = W1.shape[1], q.shape[-1]
-    qf, kf, vf = q.float(), k.float(), v.float()
-    W1f, W2f = W1.float(), W2.float()
-    tauf = None if tau is None else tau.float()
-    extra = () if tauf is None else (tauf,)
-
-    def write(kk, vv, w1, w2, *t):
-        return gn_write(kk, vv, w1, w2, t[0] if t else None, nonlin, eps)
-
-    h_k, g, lam = per_token_f32(write, kf, vf, W1f, W2f, *extra)
+    if nonlin not in _NONLIN:
+        raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
     J = 0 if log_alphas is None else log_alphas.shape[0]
-    las = [None] + [log_alphas[j].float() for j in range(J)]
-    slots = _views(mode, J)
-    stale = [False] + [mode == "stale"] * J
-    flags = stale if any(stale) else None
-
-    def query_pre(qq, w1, *t):
-        a = head_map(w1, qq)
-        return a, _activation("relu2", _thresholded(_rmsnorm(a, eps)[0], t[0] if t else None))
-
-    a_q, h0 = per_token_f32(query_pre, qf, W1f, *extra)
-    # stage 1, shared by all views: the correction of the hidden preactivation
-    if read_norm_w1:
-        reads = _scan(h0, h_k, g, True, las, flags)
-        pres = [a_q + reads[s][..., :m] / (reads[s][..., m:] + eps) for s in slots]
-    else:
-        reads = _scan(q, k, g, False, las, flags)
-        pres = [a_q + reads[s] for s in slots]
-
-    def features(pre, w2, *t):
-        hq = _activation(nonlin, _thresholded(_rmsnorm(pre, eps)[0], t[0] if t else None))
-        return hq, head_map(w2, hq)
-
-    # stage 2, one query per view
-    outs = []
-    for s, pre in zip(slots, pres):
-        hq, base = per_token_f32(features, pre, W2f, *extra)
-        c = _scan(hq, h_k, lam, bool(read_norm), [las[s]], [True] if stale[s] else None)[0]
-        mem = c[..., :d] / (c[..., d:] + eps) if read_norm else c
-        outs.append(qf + base + mem)
-    y = outs[0]
-    if J and mode == "stale":
-        # y - sum_j eta_j (y_stale_j - y_base), y_base the zero-memory read
-        # (pre = W1 q, no memory term; block.py:697-718)
-        y_base = qf + per_token_f32(features, a_q, W2f, *extra)[1]
-        for j in range(J):
-            y = y - etas[j].float().view(1, -1, 1, 1) * (outs[1 + j] - y_base)
-        return y
-    for j in range(J):
-        y = y + etas[j].float().view(1, -1, 1, 1) * (outs[1 + j] - outs[0])
+    if J:
+        _views(mode, J)
+    from . import ops  # noqa: F401  (registers the operators)
+    y, _ = torch.ops.thetascan_b200.gn_core_fwd(
+        q.float().contiguous(), k.float().contiguous(), v.float().contiguous(), W1, W2, tau,
+        log_alphas, etas, nonlin, bool(read_norm), bool(read_norm_w1), mode if J else "sum", float(eps))
     return y

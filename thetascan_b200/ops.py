@@ -16,7 +16,10 @@ mode: tests/test_scan_chunk.py:663-738 of the reference project):
 * ``thetascan_b200::kernel_mixer_qkv_fwd`` / ``kernel_mixer_qkv_bwd`` -- the
   same from the raw fused projection ``qkv [B,T,3Hd]``, with RoPE and the L2
   norm inside the feature kernels and the q/k/v gradients written into one
-  ``d qkv``.
+  ``d qkv``;
+* ``thetascan_b200::gn_core_fwd`` / ``gn_core_bwd`` -- the Gauss--Newton
+  family's core (write, two-stage read, bank combination; engine.py:161-340,
+  455-528) on the GN row kernels, cuBLAS per-head maps and the scan kernels.
 
 The forward ops return the intermediates their backward needs as extra
 outputs (no state lives outside the graph).  Optional tensor inputs are
@@ -431,3 +434,78 @@ def _stream_backward(ctx, douts, dstate, dws):
 
 
 torch.library.register_autograd(f"{LIB}::scan_views_stream_fwd", _stream_backward, setup_context=_stream_setup)
+
+
+# --------------------------------------------------------------------------- GN core
+
+@torch.library.custom_op(f"{LIB}::gn_core_fwd", mutates_args=())
+def gn_core_fwd(q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor, tau: Optional[Tensor],
+                log_alphas: Optional[Tensor], etas: Optional[Tensor], nonlin: str, read_norm: bool,
+                read_norm_w1: bool, mode: str, eps: float) -> tuple[Tensor, list[Tensor]]:
+    """GN core ``y [B,H,T,d]`` f32 from f32 post-RoPE/L2 ``q, k, v`` plus the
+    intermediates of its backward (write streams, stage reads, scan states)."""
+    from .gn import _gn_forward
+    _require_cuda(q, k, v, W1, W2, tau, log_alphas, etas)
+    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, False)
+
+
+@gn_core_fwd.register_fake
+def _(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps):
+    from .gn import _gn_forward
+    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, True)
+
+
+@torch.library.custom_op(f"{LIB}::gn_core_bwd", mutates_args=())
+def gn_core_bwd(dy: Tensor, q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor, tau: Optional[Tensor],
+                log_alphas: Optional[Tensor], etas: Optional[Tensor], saved: list[Tensor], nonlin: str,
+                read_norm: bool, read_norm_w1: bool, mode: str,
+                eps: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Gradients of q, k, v, W1, W2 (f32) and of tau ``[H,m]``, the bank's
+    log-retentions and etas ``[J,H]`` (empty where the input is absent)."""
+    from .gn import _gn_backward
+    _require_cuda(dy, q, k, v, W1, W2, tau, log_alphas, etas)
+    return _gn_outputs(_gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, list(saved), nonlin, read_norm,
+                                    read_norm_w1, mode, eps, False), q)
+
+
+def _gn_outputs(grads, q):
+    return tuple(q.new_empty(0) if g_ is None else g_.contiguous() for g_ in grads)
+
+
+@gn_core_bwd.register_fake
+def _(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read_norm, read_norm_w1, mode, eps):
+    from .gn import _gn_backward
+    return _gn_outputs(_gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, list(saved), nonlin, read_norm,
+                                    read_norm_w1, mode, eps, True), q)
+
+
+def _gn_setup(ctx, inputs, output):
+    q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps = inputs
+    y, saved = output
+    ctx.args = (nonlin, read_norm, read_norm_w1, mode, eps)
+    ctx.present = (tau is not None, log_alphas is not None, etas is not None)
+    ctx.meta = [(t.dtype, t.shape) if t is not None else None for t in (q, k, v, W1, W2, tau, log_alphas, etas)]
+    ctx.n_saved = len(saved)
+    ctx.mark_non_differentiable(*saved)
+    ctx.set_materialize_grads(False)
+    ctx.save_for_backward(q, k, v, W1, W2, *[t for t in (tau, log_alphas, etas) if t is not None], *saved)
+
+
+def _gn_backward_fn(ctx, dy, dsaved):
+    t = list(ctx.saved_tensors)
+    q, k, v, W1, W2 = t[:5]
+    rest = t[5:]
+    opt = []
+    for p in ctx.present:
+        opt.append(rest.pop(0) if p else None)
+    tau, log_alphas, etas = opt
+    if dy is None:
+        dy = torch.zeros_like(q, dtype=torch.float32)
+    grads = gn_core_bwd(dy, q, k, v, W1, W2, tau, log_alphas, etas, rest, *ctx.args)
+    out = []
+    for g_, meta in zip(grads, ctx.meta):
+        out.append(None if meta is None else g_.to(meta[0]).reshape(meta[1]))
+    return (*out, None, None, None, None, None)
+
+
+torch.library.register_autograd(f"{LIB}::gn_core_fwd", _gn_backward_fn, setup_context=_gn_setup)
