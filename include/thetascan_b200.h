@@ -487,6 +487,31 @@ typedef struct ts_gn_rows_args {
 
 int ts_b200_gn_rows(const ts_gn_rows_args* args, ts_stream_t stream);
 
+/* The GN mixer's q, k, v from its fused projection (block.py:577-599 of the
+ * reference: the proj_qkv split, RoPE on q and k, then the L2 norm
+ * x / max(|x|, eps)), and the backward of that map.  qkv is the projection
+ * output f32 [B,T,3,H,d] contiguous; q, k, v f32 [B,H,T,d] contiguous.  RoPE
+ * rotates adjacent channel pairs (2j, 2j+1) of the first `rot` channels
+ * (even, 0 = none) by the phase tables cos/sin f32 [T, rot/2]. */
+typedef struct ts_gn_prep_args {
+  int batch, heads, tokens, d;   /* d <= 256 */
+  int rot;
+  const float* cos;
+  const float* sin;
+  float eps;
+  const float* qkv;
+  float* q;                      /* forward outputs */
+  float* k;
+  float* v;
+  const float* dq;               /* backward inputs */
+  const float* dk;
+  const float* dv;
+  float* dqkv;                   /* backward output, f32 [B,T,3,H,d] (written) */
+} ts_gn_prep_args;
+
+int ts_b200_gn_prep_fwd(const ts_gn_prep_args* args, ts_stream_t stream);
+int ts_b200_gn_prep_bwd(const ts_gn_prep_args* args, ts_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

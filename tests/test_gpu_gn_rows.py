@@ -234,3 +234,41 @@ def test_gn_rows_errors(dev):
     assert lib.ts_b200_gn_rows(ctypes.byref(a), None) == _lib.TS_ERR_VALUE
     a.stage, a.nonlinearity = _lib.TS_GN_WRITE_PRE, 7
     assert lib.ts_b200_gn_rows(ctypes.byref(a), None) == _lib.TS_ERR_NOT_IMPLEMENTED
+
+
+@pytest.mark.parametrize("d,rot", [(128, 64), (64, 64), (96, 0), (256, 128)])
+def test_gn_prep_matches_float64(dev, d, rot):
+    """q, k, v of the GN mixer from its fused projection: the split, RoPE on
+    the first ``rot`` channels and x / max(|x|, eps) of q and k (block.py:
+    577-599), forward and backward, against float64 on the same values."""
+    import thetascan_b200.ops  # noqa: F401
+    from thetascan_b200.mixer import _rope_tables
+    B, T, H = 2, 150, 3
+    eps = 1e-2
+    gen = torch.Generator().manual_seed(d + rot)
+    qkv = torch.randn(B, T, 3 * H * d, generator=gen).to(dev)
+    qkv[0, 3, :H * d] *= 1e-4                       # one q row below the norm floor
+    if rot:
+        cos, sin = _rope_tables(T, rot, 10000.0, str(dev))
+    else:
+        cos = sin = qkv.new_empty(0)
+    leaf = qkv.clone().requires_grad_(True)
+    q, k, v = torch.ops.thetascan_b200.gn_prep_fwd(leaf, cos, sin, rot, H, eps)
+    grads = [torch.randn(B, H, T, d, generator=gen).to(dev) for _ in range(3)]
+    sum((o * g_).sum() for o, g_ in zip((q, k, v), grads)).backward()
+
+    ref = qkv.double().requires_grad_(True)
+    rq, rk, rv = ref.view(B, T, 3, H, d).permute(2, 0, 3, 1, 4)
+
+    def rope_l2(x):
+        if rot:
+            c, s = cos.double(), sin.double()
+            e, o = x[..., 0:rot:2], x[..., 1:rot:2]
+            x = torch.cat((torch.stack((e * c - o * s, e * s + o * c), -1).flatten(-2), x[..., rot:]), -1)
+        return x / x.norm(dim=-1, keepdim=True).clamp_min(eps)
+
+    want = (rope_l2(rq), rope_l2(rk), rv)
+    sum((o * g_.double()).sum() for o, g_ in zip(want, grads)).backward()
+    for got, w in zip((q, k, v), want):
+        assert got.is_contiguous() and rel_err(got, w) < TOL
+    assert rel_err(leaf.grad, ref.grad) < TOL

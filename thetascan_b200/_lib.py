@@ -149,6 +149,15 @@ class GnRowsArgs(ctypes.Structure):
     ]
 
 
+class GnPrepArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int), ("d", ctypes.c_int),
+        ("rot", ctypes.c_int), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("eps", ctypes.c_float),
+        ("qkv", ctypes.c_void_p), ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p), ("dqkv", ctypes.c_void_p),
+    ]
+
+
 TS_GN_RELU2, TS_GN_SILU, TS_GN_TANH = 0, 1, 2
 (TS_GN_WRITE_PRE, TS_GN_WRITE_LAM, TS_GN_WRITE_G, TS_GN_QUERY_PRE, TS_GN_FEATURES, TS_GN_OUT, TS_GN_OUT_BWD,
  TS_GN_FEATURES_BWD, TS_GN_QUERY_PRE_BWD, TS_GN_WRITE_G_BWD, TS_GN_WRITE_LAM_BWD, TS_GN_WRITE_PRE_BWD) = range(1, 13)
@@ -168,6 +177,8 @@ SIGNATURES.update({
     "ts_b200_mass_query_bwd": (ctypes.c_int, [ctypes.POINTER(MassArgs), ctypes.POINTER(MassGradArgs),
                                               ctypes.c_void_p]),
     "ts_b200_gn_rows": (ctypes.c_int, [ctypes.POINTER(GnRowsArgs), ctypes.c_void_p]),
+    "ts_b200_gn_prep_fwd": (ctypes.c_int, [ctypes.POINTER(GnPrepArgs), ctypes.c_void_p]),
+    "ts_b200_gn_prep_bwd": (ctypes.c_int, [ctypes.POINTER(GnPrepArgs), ctypes.c_void_p]),
 })
 
 _lock = threading.Lock()

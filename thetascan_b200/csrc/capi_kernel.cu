@@ -299,3 +299,31 @@ int ts_b200_gn_rows(const ts_gn_rows_args* a, ts_stream_t stream) {
   for (int i = 0; i < 4; ++i) p.out[i] = a->out[i];
   return launch_gn_rows(p, a->stage, reinterpret_cast<cudaStream_t>(stream));
 }
+
+static int build_gn_prep(const ts_gn_prep_args* a, ts::GnPrepParams* p, bool backward) {
+  using namespace ts;
+  if (!a) return set_error(TS_ERR_VALUE, "gn_prep: null arguments");
+  if (a->batch < 0 || a->heads < 0 || a->tokens < 0) return set_error(TS_ERR_VALUE, "gn_prep: negative shape");
+  if (a->d < 1 || a->d > kGnMaxWidth) return set_error(TS_ERR_NOT_IMPLEMENTED, "gn_prep: d=%d outside 1..256", a->d);
+  if (a->rot < 0 || a->rot > a->d || (a->rot & 1))
+    return set_error(TS_ERR_VALUE, "gn_prep: rot=%d must be even and <= d", a->rot);
+  if (a->rot && (!a->cos || !a->sin)) return set_error(TS_ERR_VALUE, "gn_prep: null phase tables");
+  if (!a->qkv) return set_error(TS_ERR_VALUE, "gn_prep: null qkv");
+  if (backward ? (!a->dq || !a->dk || !a->dv || !a->dqkv) : (!a->q || !a->k || !a->v))
+    return set_error(TS_ERR_VALUE, "gn_prep: null stream pointer");
+  *p = GnPrepParams{a->batch, a->heads, a->tokens, a->d, a->rot, a->eps, a->qkv, a->cos, a->sin,
+                    a->q, a->k, a->v, a->dq, a->dk, a->dv, a->dqkv};
+  return TS_OK;
+}
+
+int ts_b200_gn_prep_fwd(const ts_gn_prep_args* a, ts_stream_t stream) {
+  ts::GnPrepParams p;
+  if (int e = build_gn_prep(a, &p, false)) return e;
+  return ts::launch_gn_prep(p, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ts_b200_gn_prep_bwd(const ts_gn_prep_args* a, ts_stream_t stream) {
+  ts::GnPrepParams p;
+  if (int e = build_gn_prep(a, &p, true)) return e;
+  return ts::launch_gn_prep(p, true, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -537,6 +537,116 @@ __global__ void __launch_bounds__(kGnThreads) gn_write_pre_bwd_kernel(GnRowParam
   if (p.dtau) gn_flush_dtau<W>(p, dtau, rs.h);
 }
 
+// ---------------------------------------------------------------- q/k/v preparation
+
+// The GN mixer's streams from its fused projection (block.py:577-599 of the
+// reference): q and k rotated on their first `rot` channels (adjacent pairs,
+// phases cos/sin [T][rot/2]) and L2-normalised, x / max(|x|, eps); v copied.
+// src is the projection [B,T,3,H,d]; q, k, v are [B,H,T,d].
+struct GnPrepParams {
+  int B, H, T, d, rot;
+  float eps;
+  const float* src;
+  const float* cos;
+  const float* sin;
+  float* q;
+  float* k;
+  float* v;
+  const float* dq;
+  const float* dk;
+  const float* dv;
+  float* dsrc;
+};
+
+// the rotation (sign +1) or its transpose (sign -1) of the lane's slots
+template <int W>
+__device__ __forceinline__ void gn_rotate(float (&x)[W], const GnPrepParams& p, int t, float sign) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const int c = lane + 32 * i;
+    const float other = __shfl_xor_sync(0xffffffffu, x[i], 1);
+    if (c < p.rot) {
+      const int j = c >> 1;
+      const float cs = __ldg(p.cos + static_cast<size_t>(t) * (p.rot >> 1) + j);
+      const float sn = sign * __ldg(p.sin + static_cast<size_t>(t) * (p.rot >> 1) + j);
+      x[i] = (c & 1) ? fmaf(other, sn, x[i] * cs) : fmaf(-other, sn, x[i] * cs);
+    }
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kGnThreads) gn_prep_fwd_kernel(GnPrepParams p) {
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int t0 = blockIdx.x * kGnRowsPerCta, t1 = min(p.T, t0 + kGnRowsPerCta);
+  for (int t = t0 + (threadIdx.x >> 5); t < t1; t += kGnThreads / 32) {
+    const float* row = p.src + ((static_cast<size_t>(b) * p.T + t) * 3 * p.H + h) * p.d;
+    const size_t o = (static_cast<size_t>(bh) * p.T + t) * p.d;
+    for (int which = 0; which < 2; ++which) {
+      float x[W];
+      gn_load<W>(x, row + static_cast<size_t>(which) * p.H * p.d, p.d);
+      gn_rotate<W>(x, p, t, 1.f);
+      float n = 0.f;
+#pragma unroll
+      for (int i = 0; i < W; ++i) n = fmaf(x[i], x[i], n);
+      const float inv = 1.f / fmaxf(sqrtf(gn_warp_sum(n)), p.eps);
+#pragma unroll
+      for (int i = 0; i < W; ++i) x[i] *= inv;
+      gn_store<W>((which ? p.k : p.q) + o, x, p.d);
+    }
+    float x[W];
+    gn_load<W>(x, row + static_cast<size_t>(2) * p.H * p.d, p.d);
+    gn_store<W>(p.v + o, x, p.d);
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kGnThreads) gn_prep_bwd_kernel(GnPrepParams p) {
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int t0 = blockIdx.x * kGnRowsPerCta, t1 = min(p.T, t0 + kGnRowsPerCta);
+  for (int t = t0 + (threadIdx.x >> 5); t < t1; t += kGnThreads / 32) {
+    const size_t srow = ((static_cast<size_t>(b) * p.T + t) * 3 * p.H + h) * p.d;
+    const size_t o = (static_cast<size_t>(bh) * p.T + t) * p.d;
+    for (int which = 0; which < 2; ++which) {
+      float x[W], g[W];
+      gn_load<W>(x, p.src + srow + static_cast<size_t>(which) * p.H * p.d, p.d);
+      gn_load<W>(g, (which ? p.dk : p.dq) + o, p.d);
+      gn_rotate<W>(x, p, t, 1.f);
+      float n = 0.f, dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < W; ++i) {
+        n = fmaf(x[i], x[i], n);
+        dot = fmaf(x[i], g[i], dot);
+      }
+      n = sqrtf(gn_warp_sum(n));
+      dot = gn_warp_sum(dot);
+      // out = x / max(|x|, eps): below the floor the divisor is a constant
+      const float inv = 1.f / fmaxf(n, p.eps);
+      const float c = n > p.eps ? dot * inv * inv * inv : 0.f;
+#pragma unroll
+      for (int i = 0; i < W; ++i) g[i] = fmaf(g[i], inv, -c * x[i]);
+      gn_rotate<W>(g, p, t, -1.f);
+      gn_store<W>(p.dsrc + srow + static_cast<size_t>(which) * p.H * p.d, g, p.d);
+    }
+    float g[W];
+    gn_load<W>(g, p.dv + o, p.d);
+    gn_store<W>(p.dsrc + srow + static_cast<size_t>(2) * p.H * p.d, g, p.d);
+  }
+}
+
+int launch_gn_prep(const GnPrepParams& p, bool backward, cudaStream_t s) {
+  if (p.B <= 0 || p.H <= 0 || p.T <= 0) return TS_OK;
+  const dim3 grid(ceil_div(p.T, kGnRowsPerCta), p.B * p.H);
+  if (p.d <= 128) {
+    if (backward) gn_prep_bwd_kernel<4><<<grid, kGnThreads, 0, s>>>(p);
+    else gn_prep_fwd_kernel<4><<<grid, kGnThreads, 0, s>>>(p);
+  } else {
+    if (backward) gn_prep_bwd_kernel<8><<<grid, kGnThreads, 0, s>>>(p);
+    else gn_prep_fwd_kernel<8><<<grid, kGnThreads, 0, s>>>(p);
+  }
+  return check_launch(backward ? "gn_prep_bwd_kernel" : "gn_prep_fwd_kernel");
+}
+
 // ---------------------------------------------------------------- launch
 
 template <int W>

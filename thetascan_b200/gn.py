@@ -33,6 +33,7 @@ from __future__ import annotations
 import ctypes
 
 import torch
+import torch.nn.functional as F
 
 from . import _lib
 from .scan import _scan_bwd_impl, _scan_fwd_impl, _stream
@@ -79,6 +80,33 @@ class _PerToken(torch.autograd.Function):
                 if pairs and wanted else [None] * len(wanted)
         it = iter(got)
         return (None, *[next(it) if t.requires_grad else None for t in inputs])
+
+
+class _Tf32Linear(torch.autograd.Function):
+    """``F.linear`` whose forward and backward GEMMs both run on TF32 tensor
+    cores (the autograd engine runs a backward outside the caller's TF32
+    setting); saves its input and weight, no recomputation."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = b is not None
+        with _tf32():
+            return F.linear(x, w, b)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        with _tf32():
+            dx = dy @ w if ctx.needs_input_grad[0] else None
+            dw = dy.reshape(-1, dy.shape[-1]).t() @ x.reshape(-1, x.shape[-1]) if ctx.needs_input_grad[1] else None
+        db = dy.reshape(-1, dy.shape[-1]).sum(0) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dw, db
+
+
+def tf32_linear(x, w, b=None):
+    """``F.linear(x, w, b)`` with TF32 GEMMs forward and backward."""
+    return _Tf32Linear.apply(x, w, b)
 
 
 def per_token(fn, *tensors):

@@ -236,9 +236,10 @@ class ThetaScanCore(nn.Module):
     # -------------------------------------------------------------- helpers
 
     def _forward_gn(self, x, shard):
-        """GN family: the per-token write and features in f32 PyTorch, every
-        sequence read on the scan kernels (:mod:`thetascan_b200.gn`)."""
-        from .gn import gn_core
+        """GN family: f32 projections on TF32 tensor cores, q/k preparation
+        and the GN core on the row kernels, every sequence read on the scan
+        kernels (:mod:`thetascan_b200.gn`)."""
+        from .gn import gn_core, per_token, tf32_linear
         if shard is not None:
             raise NotImplementedError("thetascan_b200: sequence shards of the GN family are not built")
         B, T, _ = x.shape
@@ -247,31 +248,38 @@ class ThetaScanCore(nn.Module):
         # rounding of its inputs (bf16 projections move the input gradient by
         # ~3%), so projections, q/k preparation and the per-token math stay
         # f32; only the scan streams are bf16.
-        from .gn import per_token
         xf = x.float()
-        names = [n for n, _ in self.named_parameters() if n.startswith("proj_") or n == "kq_bias"]
-        params = dict(self.named_parameters())
         rot, base = self._rot, self.cfg.rope.base
-
-        def qkv(xx, *ws):
-            # the module's projection with its weights passed in (so that the
-            # TF32 recomputation differentiates them)
-            saved = {n: params[n] for n in names}
-            try:
-                for n, w in zip(names, ws):
-                    _set_param(self, n, w)
-                q, k, v = self.project(xx)
-            finally:
-                for n in names:
-                    _set_param(self, n, saved[n])
-            return q.contiguous(), k.contiguous(), v.contiguous()
-
-        # the projection GEMMs under TF32 (recomputed in the backward); RoPE
-        # and the L2 norm have no GEMM, so they run once under plain autograd
-        q, k, v = per_token(qkv, xf, *[params[n] for n in names])
         gn = self.cfg.gn
         eps = 1e-6 if gn.damping is None else float(gn.damping)
-        q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
+        if self.cfg.key_value_heads is None and not self.cfg.share_key_query:
+            # fused projection, then RoPE + L2 of q and k in one row kernel
+            from . import ops  # noqa: F401  (registers the operators)
+            qkv = tf32_linear(xf, self.proj_qkv.weight)
+            if rot:
+                cos, sin = _rope_tables(T, rot, float(base), str(x.device))
+            else:
+                cos = sin = qkv.new_empty(0)
+            q, k, v = torch.ops.thetascan_b200.gn_prep_fwd(qkv, cos, sin, rot, H, eps)
+        else:
+            names = [n for n, _ in self.named_parameters() if n.startswith("proj_") or n == "kq_bias"]
+            params = dict(self.named_parameters())
+
+            def qkv_fn(xx, *ws):
+                # the module's projection with its weights passed in (so that
+                # the TF32 recomputation differentiates them)
+                saved = {n: params[n] for n in names}
+                try:
+                    for n, w in zip(names, ws):
+                        _set_param(self, n, w)
+                    q, k, v = self.project(xx)
+                finally:
+                    for n in names:
+                        _set_param(self, n, saved[n])
+                return q.contiguous(), k.contiguous(), v.contiguous()
+
+            q, k, v = per_token(qkv_fn, xf, *[params[n] for n in names])
+            q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         W1, W2 = self.effective_weights()
@@ -283,14 +291,10 @@ class ThetaScanCore(nn.Module):
                     log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum",
                     eps=eps)
         y = y.transpose(1, 2)
-
-        def out(yy, xx, w_out, *gate):
-            if gate:
-                yy = yy * F.silu(F.linear(xx, gate[0], gate[1]).view(B, T, H, d))
-            return F.linear(yy.reshape(B, T, H * d), w_out)
-
-        gate = () if self.ogate is None else (self.ogate.g.lin.weight, self.ogate.g.lin.bias)
-        y = per_token(out, y, xf, self.proj_out.weight, *gate)
+        if self.ogate is not None:
+            g = tf32_linear(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)
+            y = F.silu(g).view(B, T, H, d) * y
+        y = tf32_linear(y.reshape(B, T, H * d), self.proj_out.weight)
         return y.to(x.dtype)
 
     def _forward_f32(self, x, shard):

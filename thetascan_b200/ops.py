@@ -17,6 +17,9 @@ mode: tests/test_scan_chunk.py:663-738 of the reference project):
   same from the raw fused projection ``qkv [B,T,3Hd]``, with RoPE and the L2
   norm inside the feature kernels and the q/k/v gradients written into one
   ``d qkv``;
+* ``thetascan_b200::gn_prep_fwd`` / ``gn_prep_bwd`` -- the GN mixer's q, k, v
+  from its fused projection: RoPE and the L2 norm of q and k (block.py:
+  577-599), one row kernel each way;
 * ``thetascan_b200::gn_core_fwd`` / ``gn_core_bwd`` -- the Gauss--Newton
   family's core (write, two-stage read, bank combination; engine.py:161-340,
   455-528) on the GN row kernels, cuBLAS per-head maps and the scan kernels.
@@ -509,3 +512,78 @@ def _gn_backward_fn(ctx, dy, dsaved):
 
 
 torch.library.register_autograd(f"{LIB}::gn_core_fwd", _gn_backward_fn, setup_context=_gn_setup)
+
+
+# --------------------------------------------------------------------------- GN stream preparation
+
+def _gn_prep_call(fn, qkv, cos, sin, rot, heads, eps, outs=None, grads=None):
+    B, T, w = (int(x) for x in qkv.shape)
+    d = w // (3 * heads)
+    a = _lib.GnPrepArgs()
+    a.batch, a.heads, a.tokens, a.d, a.rot, a.eps = B, heads, T, d, rot, eps
+    a.cos, a.sin = (cos.data_ptr(), sin.data_ptr()) if rot else (None, None)
+    a.qkv = qkv.data_ptr()
+    if outs is not None:
+        a.q, a.k, a.v = (x.data_ptr() for x in outs)
+    if grads is not None:
+        (a.dq, a.dk, a.dv), a.dqkv = (x.data_ptr() for x in grads[:3]), grads[3].data_ptr()
+    _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+
+@torch.library.custom_op(f"{LIB}::gn_prep_fwd", mutates_args=())
+def gn_prep_fwd(qkv: Tensor, cos: Tensor, sin: Tensor, rot: int, heads: int,
+                eps: float) -> tuple[Tensor, Tensor, Tensor]:
+    """q, k, v f32 ``[B,H,T,d]`` from the f32 fused projection ``[B,T,3Hd]``:
+    RoPE on the first ``rot`` channels (phase tables ``[T, rot/2]``) and the
+    L2 norm of q and k."""
+    _require_cuda(qkv, cos, sin)
+    qkv = qkv.contiguous()
+    B, T, w = qkv.shape
+    d = w // (3 * heads)
+    outs = [qkv.new_empty(B, heads, T, d) for _ in range(3)]
+    _gn_prep_call(_lib.load().ts_b200_gn_prep_fwd, qkv, cos.contiguous(), sin.contiguous(), rot, heads, eps,
+                  outs=outs)
+    return tuple(outs)
+
+
+@gn_prep_fwd.register_fake
+def _(qkv, cos, sin, rot, heads, eps):
+    B, T, w = qkv.shape
+    d = w // (3 * heads)
+    return tuple(qkv.new_empty(B, heads, T, d) for _ in range(3))
+
+
+@torch.library.custom_op(f"{LIB}::gn_prep_bwd", mutates_args=())
+def gn_prep_bwd(dq: Tensor, dk: Tensor, dv: Tensor, qkv: Tensor, cos: Tensor, sin: Tensor, rot: int, heads: int,
+                eps: float) -> Tensor:
+    """Gradient of the fused projection ``[B,T,3Hd]`` (f32)."""
+    _require_cuda(dq, dk, dv, qkv, cos, sin)
+    qkv = qkv.contiguous()
+    dqkv = torch.empty_like(qkv)
+    grads = [g_.float().contiguous() for g_ in (dq, dk, dv)] + [dqkv]
+    _gn_prep_call(_lib.load().ts_b200_gn_prep_bwd, qkv, cos.contiguous(), sin.contiguous(), rot, heads, eps,
+                  grads=grads)
+    return dqkv
+
+
+@gn_prep_bwd.register_fake
+def _(dq, dk, dv, qkv, cos, sin, rot, heads, eps):
+    return torch.empty_like(qkv)
+
+
+def _gn_prep_setup(ctx, inputs, output):
+    qkv, cos, sin, rot, heads, eps = inputs
+    ctx.args = (rot, heads, eps)
+    ctx.save_for_backward(qkv, cos, sin)
+
+
+def _gn_prep_backward(ctx, dq, dk, dv):
+    qkv, cos, sin = ctx.saved_tensors
+    z = None
+    grads = [g_ if g_ is not None else torch.zeros(qkv.shape[0], ctx.args[1], qkv.shape[1],
+                                                   qkv.shape[2] // (3 * ctx.args[1]), device=qkv.device)
+             for g_ in (dq, dk, dv)]
+    return gn_prep_bwd(*grads, qkv, cos, sin, *ctx.args), z, z, None, None, None
+
+
+torch.library.register_autograd(f"{LIB}::gn_prep_fwd", _gn_prep_backward, setup_context=_gn_prep_setup)
