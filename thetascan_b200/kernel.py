@@ -322,6 +322,10 @@ class _ShardStageA(torch.autograd.Function):
         ctx.W = (W1b, W2b)
         ctx.dtypes = (W1.dtype, W2.dtype)
         ctx.save_for_backward(qkv)
+        # phi_q / phi_k reach the second half only as its scan operands (no
+        # gradient returns through them): no zero gradients are materialised
+        ctx.mark_non_differentiable(phi_q, phi_k)
+        ctx.set_materialize_grads(False)
         return phi_q, phi_k, y0, U
 
     @staticmethod
@@ -350,7 +354,9 @@ class _ShardStageA(torch.autograd.Function):
         sg.dq, sg.dk = dphi_q.data_ptr(), dphi_k.data_ptr()
         sg.grad_dtype = _lib.TS_DTYPE_BF16
         sg.workspace, sg.workspace_bytes = hold.gws.data_ptr(), hold.gws.numel()
-        dU = None if dU is None else dU.float().contiguous()
+        if dU is None:
+            dU = torch.zeros(B, H, len(hold.las), m, d + MASS_COLS, dtype=torch.float32, device=dev)
+        dU = dU.float().contiguous()
         sg.dfinal_state = _ptr(dU)
         sg.stage = 2
         _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
@@ -389,32 +395,53 @@ class _ShardStageA(torch.autograd.Function):
 
 
 class _ShardStageB(torch.autograd.Function):
-    """Second half of the scan forward of a shard: carried states from the
-    entering state S and the retention slots.  Its backward runs the first
-    half of the scan backward and returns dS, the gradient of the entering
-    state from this shard's own outputs."""
+    """Second half of the scan forward of a shard and its key-mass read:
+    carried states from the entering state S, the retention slots, then the
+    read and bank blend into token-major ``y``.  Its backward runs the read
+    backward and the first half of the scan backward (the slot gradients stay
+    bf16 inside) and returns dS, the gradient of the entering state from this
+    shard's own outputs, with d y0 and d eta."""
 
     @staticmethod
-    def forward(ctx, hold, S, phi_q, phi_k, v):
+    def forward(ctx, hold, S, v, spec, y0, etas):
         lib = _lib.load()
         hold.S = S.detach().float().contiguous()
         sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
         sa.init_state, sa.stage = hold.S.data_ptr(), 2
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
-        ctx.hold = hold
-        ctx.save_for_backward(v)
-        return tuple(hold.slots)
+        B, H, T, d = y0.shape
+        eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
+        y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=y0.device)
+        ra = _kread_args(spec, hold.slots, eta, y0.contiguous(), y)
+        _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
+        ctx.hold, ctx.spec, ctx.eta, ctx.has_eta = hold, spec, eta, etas is not None
+        ctx.save_for_backward(v, y0)
+        return y
 
     @staticmethod
-    def backward(ctx, *dslots):
+    def backward(ctx, dy):
         lib = _lib.load()
         hold = ctx.hold
-        (v,) = ctx.saved_tensors
-        B, H, T = hold.phi_q.shape[:3]
-        d = v.shape[-1]
+        v, y0 = ctx.saved_tensors
+        B, H, T, d = y0.shape
         dev = v.device
-        hold.douts = [torch.zeros(B, H, T, d + MASS_COLS, dtype=torch.bfloat16, device=dev) if g is None
-                      else g.to(torch.bfloat16).contiguous() for g in dslots]
+        dy = dy.contiguous()
+        if dy.dtype not in (torch.bfloat16, torch.float32):
+            dy = dy.float()
+        ra = _kread_args(ctx.spec, hold.slots, ctx.eta, y0.contiguous(), None)
+        ga = _lib.KReadGradArgs()
+        ga.dy = dy.data_ptr()
+        ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
+        hold.douts = [torch.empty(B, H, T, _slot_width(ctx.spec, d), dtype=torch.bfloat16, device=dev)
+                      for _ in hold.slots]
+        for i, s_ in enumerate(hold.douts):
+            ga.dslots[i] = s_.data_ptr()
+        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
+        ga.dy0 = dy0.data_ptr()
+        n = len(hold.slots)
+        deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
+        ga.deta = _ptr(deta)
+        _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
         sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
         sa.init_state, sa.stage = hold.S.data_ptr(), 2
         hold.gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
@@ -428,7 +455,7 @@ class _ShardStageB(torch.autograd.Function):
         dS = torch.empty_like(hold.S)
         sg.dinit_state, sg.stage = dS.data_ptr(), 1
         _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
-        return None, dS, None, None, None
+        return None, dS, None, None, dy0, deta if ctx.has_eta else None
 
 
 class _MassQuery(torch.autograd.Function):
@@ -667,49 +694,6 @@ class _KernelCoreViews(torch.autograd.Function):
                 grads["gain"], grads["scale"], dla, deta if ctx.has_eta else None)
 
 
-class _KRead(torch.autograd.Function):
-    """Read and bank blend as one autograd stage (key-mass normalized, or
-    unnormalized for the unnormalized and feature-mass reads): y0 and the
-    slots in, token-major y out."""
-
-    @staticmethod
-    def forward(ctx, spec, y0, etas, *slots):
-        lib = _lib.load()
-        B, H, T, d = y0.shape
-        eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
-        slots = [s.contiguous() for s in slots]
-        y = torch.empty(B, T, H, d, dtype=torch.bfloat16, device=y0.device)
-        ra = _kread_args(spec, slots, eta, y0.contiguous(), y)
-        _lib.check(lib.ts_b200_kread_fwd(ctypes.byref(ra), _stream()))
-        ctx.spec, ctx.eta, ctx.has_eta = spec, eta, etas is not None
-        ctx.save_for_backward(y0, *slots)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        lib = _lib.load()
-        y0, *slots = ctx.saved_tensors
-        B, H, T, d = y0.shape
-        dev = y0.device
-        dy = dy.contiguous()
-        if dy.dtype not in (torch.bfloat16, torch.float32):
-            dy = dy.float()
-        ra = _kread_args(ctx.spec, list(slots), ctx.eta, y0.contiguous(), None)
-        ga = _lib.KReadGradArgs()
-        ga.dy = dy.data_ptr()
-        ga.dy_dtype = _lib.TS_DTYPE_BF16 if dy.dtype == torch.bfloat16 else _lib.TS_DTYPE_F32
-        dslots = [torch.empty(B, H, T, _slot_width(ctx.spec, d), dtype=torch.bfloat16, device=dev) for _ in slots]
-        for i, s in enumerate(dslots):
-            ga.dslots[i] = s.data_ptr()
-        dy0 = torch.empty(B, H, T, d, dtype=torch.float32, device=dev)
-        ga.dy0 = dy0.data_ptr()
-        n = len(slots)
-        deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
-        ga.deta = _ptr(deta)
-        _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
-        return (None, dy0, deta if ctx.has_eta else None, *dslots)
-
-
 def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, shard, *, threshold=None,
                         score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None):
     """The hot path of :func:`kernel_core_qkv` on one contiguous shard of the
@@ -744,8 +728,7 @@ def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | N
         # collective every rank joins
         S = S + 0.0 * totals[0]
     d = qkv.shape[-1] // (3 * H)
-    slots = _ShardStageB.apply(hold, S, phi_q, phi_k, _qkv_views(qkv, H, d)[2])
-    return _KRead.apply(spec, y0, etas, *slots)
+    return _ShardStageB.apply(hold, S, _qkv_views(qkv, H, d)[2], spec, y0, etas)
 
 
 def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,
