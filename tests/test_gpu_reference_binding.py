@@ -133,3 +133,22 @@ def test_reference_scan_plugin_point_takes_retention_streams(ref):
     assert rel_err(y, yr) < 1e-5
     for a, b in zip(leaves, rleaves):
         assert rel_err(a.grad, b.grad) < 1e-5
+
+
+def test_reference_ema_mixer_scans_on_b200_match_reference_chunk(ref):
+    """The reference's data-dependent EMA mode (``TemporalConfig(mode="ema")``:
+    a decay gate makes per-token ``[B,H,T,1]`` log-retention streams for the
+    numerator scan and the key mass, interface.py:198-230) with
+    ``backend="b200"``: the reference forward runs unchanged and its stream
+    scans go through the plugin point to the float32 stream kernels."""
+    from thetascan import KernelConfig, RoPEConfig, RuntimeConfig, TemporalConfig, ThetaScanConfig
+    cfg = ThetaScanConfig(d_model=128, n_heads=2, memory_multiplier=2, family="kernel",
+                          kernel=KernelConfig(feature_map="relu2_ridge"),
+                          rope=RoPEConfig(mode="partial", fraction=0.5),
+                          temporal=TemporalConfig(mode="ema"),
+                          runtime=RuntimeConfig(backend="b200", scan_chunk=64))
+    module, reference = _pair(ref, cfg, seed=9)
+    from thetascan_b200 import integration
+    assert integration._fused_core(module._core) is None   # reference forward, b200 stream scans
+    x = torch.randn(2, 300, 128, generator=torch.Generator().manual_seed(10))
+    _compare(module, reference, x, torch.float32, torch.device("cuda"), 1e-4)
