@@ -285,7 +285,27 @@ typedef struct ts_feature_args {
   /* Optional f32 [B,H,T,m] copy of phi(q) before its bf16 rounding (16-byte
    * aligned), for the feature-mass read, which divides it by the key mass. */
   float* phi_q_f32;
+  /* Relative sparsity of the softmax partition (kernel_features.py:43-70,
+   * 95-113 of the reference): with logits l = gain (pre + bias), a feature is
+   * kept where l_j - max(l) >= log rho_h (rho clamped to [eps, 1 - eps]):
+   *   relative_soft      sparse_j = e^{l_j - max} s_j / max(sum_k e^{l_k - max} s_k, eps),
+   *                      s = sigmoid((l - max - log rho) / threshold_temperature);
+   *   relative_st        the same with the hard gate [margin >= 0] forward and
+   *                      the sigmoid's derivative backward;
+   *   relative_st_blend  phi = dense + alpha_h (sparse - dense), dense the softmax.
+   * TS_SPARSITY_NONE: the softmax partition as is. */
+  int sparsity;
+  float threshold_temperature;
+  const float* relative_threshold;  /* f32 [H]: rho in (0, 1) */
+  const float* sparse_blend;        /* f32 [H]: alpha (relative_st_blend) */
 } ts_feature_args;
+
+enum {
+  TS_SPARSITY_NONE = 0,
+  TS_SPARSITY_RELATIVE_SOFT = 1,
+  TS_SPARSITY_RELATIVE_ST = 2,
+  TS_SPARSITY_RELATIVE_ST_BLEND = 3
+};
 
 int ts_b200_feature_fwd(const ts_feature_args* args, ts_stream_t stream);
 
@@ -318,6 +338,8 @@ typedef struct ts_feature_grad_args {
    * vector atomics; 0: [H,d,m].  When ts_feature_args.phi_q is given to the
    * backward it is read as the forward's phi(q) for dw2 (else rebuilt). */
   int dw2_transposed;
+  float* drelative_threshold;  /* f32 [H], ACCUMULATED, or NULL (relative sparsity) */
+  float* dsparse_blend;        /* f32 [H], ACCUMULATED, or NULL (relative_st_blend) */
 } ts_feature_grad_args;
 
 int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args* grad, ts_stream_t stream);
@@ -483,6 +505,9 @@ typedef struct ts_gn_rows_args {
   int flags;                /* bit 0: normalised read; bit 1: accumulate da_q */
   const float* in[8];       /* per stage, in the order of the table; 16-byte aligned not required */
   float* out[4];
+  void* out_bf16;           /* forward stages: bf16 [B,H,T,width] copy of out[0] (the scans'
+                             * operand), or NULL; with it out[0] may be NULL for WRITE_G and
+                             * QUERY_PRE (g and h0 feed only the scans) */
 } ts_gn_rows_args;
 
 int ts_b200_gn_rows(const ts_gn_rows_args* args, ts_stream_t stream);

@@ -318,8 +318,77 @@ def gn_tanh_cases():
     return out
 
 
+# Relative sparsity of the softmax partition (kernel_features.py:43-113),
+# head_dim 64 and m = 128 (the kernel-tile shape), fast bank, ragged T.
+SPARSE_MIXERS = {
+    f"softmax_{mode}": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, family="kernel",
+        kernel=dict(feature_map="softmax_partition", sparsity=mode,
+                    sparse_blend_init=0.5 if mode == "relative_st_blend" else 0.0),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32")
+    for mode in ("relative_soft", "relative_st", "relative_st_blend")
+}
+
+
+def sparse_cases():
+    """Feature-level cases (the map, its gradient to the scores, the cutoff
+    and the blend) and whole mixers with each sparsity mode, from the
+    reference itself."""
+    from thetascan import KernelConfig, RoPEConfig, TemporalConfig, ThetaScan, ThetaScanConfig
+    from thetascan._core.ops import kernel_features as kf
+
+    out = {"features": {}, "mixers": {}}
+    pre = _seeded(20, 2, 3, 17, 16) * 0.5
+    bias = _seeded(21, 3, 16) * 0.1
+    gain = torch.tensor([8.0, 4.0, 12.0], dtype=torch.float64)
+    weight = _seeded(22, 2, 3, 17, 16)
+    for mode in ("relative_soft", "relative_st", "relative_st_blend"):
+        p = pre.clone().requires_grad_(True)
+        rho = torch.tensor([0.05, 0.2, 0.01], dtype=torch.float64, requires_grad=True)
+        alpha = torch.tensor([0.3, 0.7, 1.0], dtype=torch.float64, requires_grad=True)
+        phi = kf.softmax_partition_features(
+            p, gain=gain, fallback_gain=8.0, score_bias=bias, sparsity=mode, relative_threshold=rho,
+            sparse_blend_alpha=alpha if mode == "relative_st_blend" else None, threshold_temperature=0.25,
+            eps=1e-6)
+        (phi * weight).sum().backward()
+        out["features"][mode] = {
+            "pre": pre, "bias": bias, "gain": gain, "rho": rho.detach(), "alpha": alpha.detach(),
+            "weight": weight, "phi": phi.detach(), "dpre": p.grad, "drho": rho.grad,
+            "dalpha": None if alpha.grad is None else alpha.grad}
+    for name, spec in SPARSE_MIXERS.items():
+        spec = dict(spec)
+        B, T = spec.pop("B"), spec.pop("T")
+        dtype = getattr(torch, spec.pop("dtype"))
+        cfg = ThetaScanConfig(kernel=KernelConfig(**spec.pop("kernel")), rope=RoPEConfig(**spec.pop("rope")),
+                              temporal=TemporalConfig(**spec.pop("temporal")), **spec)
+        torch.manual_seed(0)
+        module = ThetaScan(cfg).to(torch.float64)
+        core = module._core
+        with torch.no_grad():
+            for p in core.W2:
+                p.copy_(_seeded(5, *p.shape) * 0.2)
+            if core.fade_eta is not None:
+                core.fade_eta.copy_(_seeded(6, *core.fade_eta.shape) * 0.5)
+            # a cutoff that removes a visible share of the features
+            core.kernel_relative_threshold_raw.copy_(torch.tensor([-2.0, -3.0], dtype=torch.float64))
+        x = _seeded(8, B, T, cfg.d_model).requires_grad_(True)
+        y = module(x)
+        w = _seeded(9, *y.shape)
+        (y * w).sum().backward()
+        out["mixers"][name] = {
+            "public_config": cfg.to_dict(), "B": B, "T": T,
+            "params": {n: t.detach().to(dtype) for n, t in core.state_dict(keep_vars=True).items()
+                       if t is not None},
+            "x": x.detach().to(dtype), "y": y.detach().to(dtype), "out_weight": w.to(dtype),
+            "x_grad": x.grad.detach().to(dtype),
+            "grads": {n: p.grad.detach().to(dtype) for n, p in core.named_parameters() if p.grad is not None},
+        }
+    return out
+
+
 GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases,
-              "gn_c3": gn_c3_cases, "gn_tanh": gn_tanh_cases}
+              "gn_c3": gn_c3_cases, "gn_tanh": gn_tanh_cases, "sparse": sparse_cases}
 
 
 def main():

@@ -26,8 +26,8 @@ def test_cpu_tensors_raise_like_the_reference_cuda_backends():
     W1, W2 = torch.zeros(2, 16, 4), torch.zeros(2, 4, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         torch.ops.thetascan_b200.kernel_mixer_fwd(q.bfloat16(), q.bfloat16(), q.bfloat16(), W1, W2, None, None,
-                                                  None, None, None, None, "relu2_ridge", "sum", 1e-6, 8.0, 8,
-                                                  3.0, 1.0)
+                                                  None, None, None, None, None, None, "relu2_ridge", "sum", 1e-6,
+                                                  8.0, 8, 3.0, 1.0, "none", 0.25)
 
 
 def test_fake_workspace_is_the_library_size_query():

@@ -178,3 +178,21 @@ def test_gn_oracle_matches_reference_at_config3_width(file, name):
     _close(x.grad, case["x_grad"].to(torch.float64), tol)
     for n, g in case["grads"].items():
         _close(params[n].grad, g.to(torch.float64), tol)
+
+
+@pytest.mark.parametrize("mode", ["relative_soft", "relative_st", "relative_st_blend"])
+def test_relative_sparsity_matches_reference(mode):
+    """The softmax partition's relative sparsity (kernel_features.py:43-113):
+    the map and its gradients to the scores, the cutoff and the blend."""
+    case = _load("sparse_cases.pt")["features"][mode]
+    pre = case["pre"].clone().requires_grad_(True)
+    rho = case["rho"].clone().requires_grad_(True)
+    alpha = case["alpha"].clone().requires_grad_(True)
+    phi = features.softmax_partition(pre, gain=case["gain"], score_bias=case["bias"], sparsity=mode, rho=rho,
+                                     blend=alpha if mode == "relative_st_blend" else None)
+    _close(phi, case["phi"])
+    (phi * case["weight"]).sum().backward()
+    _close(pre.grad, case["dpre"], 1e-8)
+    _close(rho.grad, case["drho"], 1e-8)
+    if mode == "relative_st_blend":
+        _close(alpha.grad, case["dalpha"], 1e-8)

@@ -90,6 +90,8 @@ class FeatureArgs(ctypes.Structure):
         ("rope_rot", ctypes.c_int), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
         ("rope_pos0", ctypes.c_int), ("l2norm", ctypes.c_int), ("l2norm_eps", ctypes.c_float),
         ("phi_q_f32", ctypes.c_void_p),
+        ("sparsity", ctypes.c_int), ("threshold_temperature", ctypes.c_float),
+        ("relative_threshold", ctypes.c_void_p), ("sparse_blend", ctypes.c_void_p),
     ]
 
 
@@ -104,6 +106,7 @@ class FeatureGradArgs(ctypes.Structure):
         ("dk_strides", c_int64_3), ("dq_strides", c_int64_3),
         ("dy0_bf16", ctypes.c_void_p), ("dy0_strides", c_int64_3),
         ("dw2_transposed", ctypes.c_int),
+        ("drelative_threshold", ctypes.c_void_p), ("dsparse_blend", ctypes.c_void_p),
     ]
 
 
@@ -145,7 +148,7 @@ class GnRowsArgs(ctypes.Structure):
         ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("tokens", ctypes.c_int),
         ("d", ctypes.c_int), ("m", ctypes.c_int), ("nonlinearity", ctypes.c_int), ("eps", ctypes.c_float),
         ("tau", ctypes.c_void_p), ("dtau", ctypes.c_void_p), ("stage", ctypes.c_int), ("flags", ctypes.c_int),
-        ("inputs", ctypes.c_void_p * 8), ("outputs", ctypes.c_void_p * 4),
+        ("inputs", ctypes.c_void_p * 8), ("outputs", ctypes.c_void_p * 4), ("out_bf16", ctypes.c_void_p),
     ]
 
 

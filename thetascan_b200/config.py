@@ -11,7 +11,7 @@ package executes that backend only (``"auto"`` resolves to it).
 Validation restates the reference's rules for the fields this package reads
 and raises ``NotImplementedError`` for configurations the GPU path does not
 cover yet (GN swiglu and two-step Jacobians, EMA decay gates, value anchors,
-relative sparsity, feature-space RoPE).
+feature-space RoPE).
 """
 from __future__ import annotations
 
@@ -439,6 +439,4 @@ class ThetaScanConfig:
         k = self.kernel
         if k.value_representation == "value_anchors":
             return "kernel value_anchors are not built"
-        if k.sparsity != "none":
-            return "relative kernel sparsity is not built"
         return None

@@ -90,6 +90,21 @@ int build_feature_params(const ts_feature_args* a, FeatParams* p) {
   p->pos0 = a->rope_pos0;
   p->l2norm = a->l2norm ? 1 : 0;
   p->neps = a->l2norm_eps;
+  if (a->sparsity < TS_SPARSITY_NONE || a->sparsity > TS_SPARSITY_RELATIVE_ST_BLEND)
+    return set_error(TS_ERR_VALUE, "feature: unknown sparsity %d", a->sparsity);
+  if (a->sparsity != TS_SPARSITY_NONE) {
+    if (a->kind != TS_FEATURE_SOFTMAX)
+      return set_error(TS_ERR_VALUE, "feature: relative sparsity is defined for the softmax partition only");
+    if (!a->relative_threshold) return set_error(TS_ERR_VALUE, "feature: relative sparsity needs relative_threshold");
+    if (a->sparsity == TS_SPARSITY_RELATIVE_ST_BLEND && !a->sparse_blend)
+      return set_error(TS_ERR_VALUE, "feature: relative_st_blend needs sparse_blend");
+    if (!(a->threshold_temperature > 0.f))
+      return set_error(TS_ERR_VALUE, "relative threshold temperature must be positive");
+  }
+  p->sparse_mode = a->sparsity;
+  p->temperature = a->threshold_temperature;
+  p->rho = a->relative_threshold;
+  p->alpha = a->sparse_blend;
   return TS_OK;
 }
 
@@ -198,6 +213,8 @@ int ts_b200_feature_bwd(const ts_feature_args* args, const ts_feature_grad_args*
   p.dthr = grad->dthreshold;
   p.dgain = grad->dgain;
   p.dscale = grad->dspline_scale;
+  p.drho = grad->drelative_threshold;
+  p.dalpha = grad->dsparse_blend;
   return launch_feature_bwd(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -277,9 +294,12 @@ int ts_b200_gn_rows(const ts_gn_rows_args* a, ts_stream_t stream) {
     return set_error(TS_ERR_VALUE, "gn_rows: unknown stage %d", a->stage);
   for (int i = 0; kIn[a->stage][i]; ++i)
     if (kIn[a->stage][i] == '1' && !a->in[i]) return set_error(TS_ERR_VALUE, "gn_rows: stage %d needs in[%d]", a->stage, i);
+  const bool bf16_only = (a->stage == TS_GN_WRITE_G || a->stage == TS_GN_QUERY_PRE) && a->out_bf16;
   for (int i = 0; kOut[a->stage][i]; ++i)
-    if (kOut[a->stage][i] == '1' && !a->out[i])
+    if (kOut[a->stage][i] == '1' && !a->out[i] && !(i == 0 && bf16_only))
       return set_error(TS_ERR_VALUE, "gn_rows: stage %d needs out[%d]", a->stage, i);
+  if (a->out_bf16 && a->stage > TS_GN_FEATURES)
+    return set_error(TS_ERR_VALUE, "gn_rows: out_bf16 is for the forward stages WRITE_PRE .. FEATURES");
   if (a->stage == TS_GN_FEATURES_BWD && a->in[1] && !a->out[1])
     return set_error(TS_ERR_VALUE, "gn_rows: a read's gradient needs out[1]");
   if (a->stage == TS_GN_OUT_BWD && !(a->flags & 1))
@@ -297,6 +317,7 @@ int ts_b200_gn_rows(const ts_gn_rows_args* a, ts_stream_t stream) {
   p.dtau = a->tau ? a->dtau : nullptr;
   for (int i = 0; i < 8; ++i) p.in[i] = a->in[i];
   for (int i = 0; i < 4; ++i) p.out[i] = a->out[i];
+  p.out_bf16 = static_cast<__nv_bfloat16*>(a->out_bf16);
   return launch_gn_rows(p, a->stage, reinterpret_cast<cudaStream_t>(stream));
 }
 

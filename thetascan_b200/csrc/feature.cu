@@ -3,7 +3,8 @@
 //   a   = x W1^T                       (tcgen05, TMEM, f32)
 //   pre = a * rsqrt(mean(a^2) + eps)   (RMSNorm, reference norms.py:5-8)
 //   phi = map(pre)                     (kernel_features.py:116-135 relu2 ridge,
-//                                       :73-113 softmax partition,
+//                                       :73-113 softmax partition, with
+//                                       :43-70 relative sparsity,
 //                                       :138-230 projected cubic B-spline)
 // and for q additionally y0 = q + W2 phi (the slow decode of engine.py:524 plus
 // the residual of engine.py:526).  The backward recomputes a and phi and
@@ -18,7 +19,9 @@
 
 namespace ts {
 
-enum FeatureKind { kRelu2 = 0, kSoftmax = 1, kBspline = 2 };
+// kSoftmaxSparse: the softmax partition with a relative sparsity mode
+// (FeatParams.sparse_mode); the host passes kind softmax.
+enum FeatureKind { kRelu2 = 0, kSoftmax = 1, kBspline = 2, kSoftmaxSparse = 3 };
 constexpr int kMaxBasis = 16;
 
 struct FeatParams {
@@ -68,6 +71,14 @@ struct FeatParams {
   // bf16 strided row-gradient outputs in place of the f32 dx
   __nv_bfloat16* dxb[2];
   long long dxs[2][3];
+  // relative sparsity of the softmax partition (kernel_features.py:43-70,
+  // 95-113): mode 1 relative_soft, 2 relative_st, 3 relative_st_blend
+  int sparse_mode;
+  float temperature;
+  const float* rho;         // [H] relative cutoff in (0, 1)
+  const float* alpha;       // [H] dense-to-sparse blend (mode 3)
+  float* drho;              // [H], accumulated
+  float* dalpha;            // [H], accumulated
 };
 
 // Kernels are instantiated per feature kind KF & kKindMask; with kPlainBit
@@ -228,11 +239,154 @@ struct RowState {
   // controls: dot_a = sum_j dpre_j a_j, dthr = -sum_j dpre_j (relu2),
   // dgain = sum_j dpre_j sc_j / gain_j (softmax, one gain per head).
   float dot_a, dthr, dgain;
+  // relative sparsity: sparse normaliser Z, per-column share of the max's
+  // gradient, sum g dense, sum g sparse, sum of the margin gradients,
+  // log of the clamped cutoff and the blend
+  float z, dmx, Sd, Ss, dmarg, lrho, alpha;
 };
 
 struct NoGrad {
   __device__ __forceinline__ void operator()(int, float*) const {}
 };
+
+// ---- relative sparsity (kernel_features.py:43-70): logits l_j = gain_j
+// (pre_j + b_j), shifted s_j = l_j - max l, margin m_j = s_j - log rho_h,
+// gate = sigmoid(m / temperature) (soft) or [m >= 0] with the sigmoid's
+// derivative (straight-through), sparse_j = e^{s_j} gate_j / max(sum_k
+// e^{s_k} gate_k, eps), phi = sparse, or dense + alpha (sparse - dense).
+__device__ __forceinline__ float softmax_logit(const FeatParams& p, int h, int i, float a, float inv) {
+  return ctl_gain<false>(p, h, i) * (a * inv + ctl_bias<false>(p, h, i));
+}
+
+__device__ __forceinline__ void sparse_gate(const FeatParams& p, float margin, float& gate, float& dgate) {
+  const float sg = 1.f / (1.f + __expf(-margin / p.temperature));
+  gate = p.sparse_mode == 1 ? sg : (margin >= 0.f ? 1.f : 0.f);
+  dgate = sg * (1.f - sg) / p.temperature;
+}
+
+// d loss / d l_j of one column without the share of the max's gradient
+// (dl), and its parts through the shifted logit (dshift) and the margin.
+struct SparseTerms {
+  float dl, dshift, dmargin;
+};
+__device__ __forceinline__ SparseTerms sparse_terms(const FeatParams& p, const RowState& s, float g, float l) {
+  const float ex = __expf(l - s.mx);
+  float gt, dgt;
+  sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
+  const bool blend = p.sparse_mode == 3;
+  const float cd = blend ? 1.f - s.alpha : 0.f, cs = blend ? s.alpha : 1.f;
+  const float dw = (cs * g - (s.z >= p.eps ? cs * s.Ss : 0.f)) / fmaxf(s.z, p.eps);
+  SparseTerms t;
+  t.dmargin = dw * ex * dgt;
+  t.dshift = dw * ex * gt + t.dmargin;
+  t.dl = cd * (ex / s.mass) * (g - s.Sd) + t.dshift;
+  return t;
+}
+
+// Row statistics of the sparse map: ss, then the max (and how many columns
+// hold it), then E = sum e and Z = sum e gate; with a gradient also sum g
+// dense, sum g sparse, and the row totals of dpre_j = gain_j dl_j that the
+// RMSNorm and control backward need, with the max's gradient -sum dshift
+// shared by the columns that hold the max (as torch's amax backward).
+template <int KF, bool kWithGrad, class Grad>
+__device__ RowState row_stats_sparse(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
+  const int part = my_part();
+  RowState s{0.f, 0.f, -INFINITY, 0.f, 0.f, 0.f, 0.f};
+  float ss = 0.f;
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+    float a[16];
+    tmem_ld16(ta_row + c, a);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss += a[e] * a[e];
+  }
+  ss = row_pair_sum(ss, pair);
+  s.inv = rsqrtf(ss / static_cast<float>(p.P) + p.eps);
+  s.lrho = logf(fminf(fmaxf(__ldg(p.rho + h), p.eps), 1.f - p.eps));
+  s.alpha = p.sparse_mode == 3 ? __ldg(p.alpha + h) : 1.f;
+  float m = -INFINITY;
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+    float a[16];
+    tmem_ld16(ta_row + c, a);
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (c + e < p.P) m = fmaxf(m, softmax_logit(p, h, c + e, a[e], s.inv));
+  }
+  s.mx = row_pair_max(m, pair);
+  float E = 0.f, Z = 0.f, cnt = 0.f;
+  for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+    float a[16];
+    tmem_ld16(ta_row + c, a);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if (c + e >= p.P) continue;
+      const float l = softmax_logit(p, h, c + e, a[e], s.inv);
+      const float ex = __expf(l - s.mx);
+      float gt, dgt;
+      sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
+      E += ex;
+      Z += ex * gt;
+      cnt += l == s.mx ? 1.f : 0.f;
+    }
+  }
+  s.mass = row_pair_sum(E, pair);
+  s.z = row_pair_sum(Z, pair);
+  cnt = row_pair_sum(cnt, pair);
+  if constexpr (kWithGrad) {
+    const float invE = 1.f / s.mass, invZ = 1.f / fmaxf(s.z, p.eps);
+    float Sd = 0.f, Ss = 0.f;
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16], g[16];
+      tmem_ld16(ta_row + c, a);
+      grad16(c, g);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        if (c + e >= p.P) continue;
+        const float l = softmax_logit(p, h, c + e, a[e], s.inv);
+        const float ex = __expf(l - s.mx);
+        float gt, dgt;
+        sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
+        Sd += g[e] * ex * invE;
+        Ss += g[e] * ex * gt * invZ;
+      }
+    }
+    s.Sd = row_pair_sum(Sd, pair);
+    s.Ss = row_pair_sum(Ss, pair);
+    float dsh = 0.f, dmarg = 0.f, dot = 0.f, dgn = 0.f;
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16], g[16];
+      tmem_ld16(ta_row + c, a);
+      grad16(c, g);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        if (i >= p.P) continue;
+        const float l = softmax_logit(p, h, i, a[e], s.inv);
+        const SparseTerms t = sparse_terms(p, s, g[e], l);
+        dsh += t.dshift;
+        dmarg += t.dmargin;
+        dot += ctl_gain<false>(p, h, i) * t.dl * a[e];
+        dgn += t.dl * (a[e] * s.inv + ctl_bias<false>(p, h, i));
+      }
+    }
+    dsh = row_pair_sum(dsh, pair);
+    s.dmarg = row_pair_sum(dmarg, pair);
+    s.dmx = cnt > 0.f ? -dsh / cnt : 0.f;
+    for (int c = 16 * part; c < p.PP; c += kChunkStep) {
+      float a[16];
+      tmem_ld16(ta_row + c, a);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        if (i >= p.P || softmax_logit(p, h, i, a[e], s.inv) != s.mx) continue;
+        dot += ctl_gain<false>(p, h, i) * s.dmx * a[e];
+        dgn += s.dmx * (a[e] * s.inv + ctl_bias<false>(p, h, i));
+      }
+    }
+    s.dot_a = row_pair_sum(dot, pair);
+    s.dgain = row_pair_sum(dgn, pair);
+  }
+  return s;
+}
 
 // Row statistics of the feature map; the kParts threads of a row each reduce
 // their column chunks and combine through `pair` (kThreads floats of shared
@@ -252,6 +406,7 @@ template <int KF, bool kWithGrad, class Grad>
 __device__ __forceinline__ RowState row_stats(const FeatParams& p, uint32_t ta_row, int h, float* pair, Grad grad16) {
   constexpr int KIND = KF & kKindMask;
   constexpr bool kPlain = (KF & kPlainBit) != 0;
+  if constexpr (KIND == kSoftmaxSparse) return row_stats_sparse<KF, kWithGrad>(p, ta_row, h, pair, grad16);
   const int part = my_part();
   RowState s{0.f, 0.f, -INFINITY, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
@@ -430,6 +585,22 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
       const int i = c + e;
       const float u = fmaxf(a[e] * s.inv + ctl_bias<kPlain>(p, h, (kPlain || i < p.P) ? i : 0) - thr, 0.f);
       out[e] = (kPlain || i < p.P) ? (live ? u * u * inv_mass : 1.f / static_cast<float>(p.m)) : 0.f;
+    }
+  } else if constexpr (KIND == kSoftmaxSparse) {
+    const float inv_E = 1.f / s.mass, inv_Z = 1.f / fmaxf(s.z, p.eps);
+    const bool blend = p.sparse_mode == 3;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int i = c + e;
+      float v = 0.f;
+      if (i < p.P) {
+        const float ex = __expf(softmax_logit(p, h, i, a[e], s.inv) - s.mx);
+        float gt, dgt;
+        sparse_gate(p, softmax_logit(p, h, i, a[e], s.inv) - s.mx - s.lrho, gt, dgt);
+        const float dense = ex * inv_E, sparse = ex * gt * inv_Z;
+        v = blend ? dense + s.alpha * (sparse - dense) : sparse;
+      }
+      out[e] = v;
     }
   } else {
     const float inv_E = 1.f / s.mass;
@@ -957,6 +1128,20 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
         }
         dp[e] = d;
       }
+    } else if constexpr (KIND == kSoftmaxSparse) {
+      float g[16];
+      grad16(c, g);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = c + e;
+        float d = 0.f;
+        if (i < p.P) {
+          const float l = softmax_logit(p, h, i, a[e], st.inv);
+          const float dl = sparse_terms(p, st, g[e], l).dl + (l == st.mx ? st.dmx : 0.f);
+          d = ctl_gain<false>(p, h, i) * dl;
+        }
+        dp[e] = d;
+      }
     } else {
       // B-splines run their own sweep (below).
 #pragma unroll
@@ -964,7 +1149,7 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     }
   };
 
-  float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f;
+  float dot_a = 0.f, dthr = 0.f, dscale = 0.f, dgain_head = 0.f, drho = 0.f, dalpha = 0.f;
   if constexpr (spline) {
     // B-splines: this thread's projections pj = kParts * i + part.  dpre of a
     // projection is sc * sum over the four live basis functions of
@@ -1026,13 +1211,19 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     if (valid && part == 0) {
       dthr = st.dthr;
       dgain_head = st.dgain;
+      if constexpr (KIND == kSoftmaxSparse) {
+        // margin = shifted - log clamp(rho, eps, 1 - eps)
+        const float rho = __ldg(p.rho + h);
+        drho = rho >= p.eps && rho <= 1.f - p.eps ? -st.dmarg / rho : 0.f;
+        dalpha = p.sparse_mode == 3 ? st.Ss - st.Sd : 0.f;
+      }
     }
     // One sweep: (phi -> tile for dW2 unless stored), dA = inv * dpre - a *
     // inv^3 * dot_a / P, and the per-feature control gradients.
     if (decode && !phi_stored) phi_row_to_tile<KF>(p, st, ta_row, h, tl.phi, !valid, &spl_table);
     const float inv3 = st.inv * st.inv * st.inv / static_cast<float>(p.P);
     const bool dbias = p.bias != nullptr && p.dbias != nullptr && valid;
-    const bool dgain_feat = KIND == kSoftmax && p.gain_mode == 2 && valid;
+    const bool dgain_feat = (KIND == kSoftmax || KIND == kSoftmaxSparse) && p.gain_mode == 2 && valid;
     if constexpr (KIND == kRelu2 && kPlain) {
       // dpre = (g - dphi) (2 / mass) u (live rows), two columns per instruction
       const bool live = st.mass > p.eps && valid;
@@ -1082,10 +1273,17 @@ __global__ void __launch_bounds__(kThreads, 1) feature_bwd_kernel(FeatParams p) 
     const float s1 = block_sum(dthr, red);
     const float s2 = block_sum(dscale, red);
     const float s3 = block_sum(dgain_head, red);
+    float s4 = 0.f, s5 = 0.f;
+    if constexpr (KIND == kSoftmaxSparse) {
+      s4 = block_sum(drho, red);
+      s5 = block_sum(dalpha, red);
+    }
     if (threadIdx.x == 0) {
       if (KIND == kRelu2 && p.thr && p.dthr) atomicAdd(p.dthr + h, s1);
       if (spline && p.scale && p.dscale) atomicAdd(p.dscale + h, s2);
-      if (KIND == kSoftmax && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
+      if ((KIND == kSoftmax || KIND == kSoftmaxSparse) && p.gain_mode == 1 && p.dgain) atomicAdd(p.dgain + h, s3);
+      if (KIND == kSoftmaxSparse && p.drho) atomicAdd(p.drho + h, s4);
+      if (KIND == kSoftmaxSparse && p.dalpha && p.sparse_mode == 3) atomicAdd(p.dalpha + h, s5);
     }
   }
 
@@ -1204,7 +1402,7 @@ static int launch_feature_bwd_kind(const FeatParams& p, cudaStream_t s) {
 // A relu2 / softmax map without per-feature or per-head controls over whole
 // column chunks runs the plain instantiation.
 static bool plain_map(const FeatParams& p) {
-  return p.kind != kBspline && p.bias == nullptr && p.thr == nullptr && p.gain_mode == 0 && p.P == p.PP;
+  return p.kind != kBspline && p.sparse_mode == 0 && p.bias == nullptr && p.thr == nullptr && p.gain_mode == 0 && p.P == p.PP;
 }
 
 int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
@@ -1212,6 +1410,7 @@ int launch_feature_fwd(const FeatParams& p, cudaStream_t s) {
   switch (p.kind) {
     case kRelu2: return plain ? launch_feature_fwd_kind<kRelu2 | kPlainBit>(p, s) : launch_feature_fwd_kind<kRelu2>(p, s);
     case kSoftmax:
+      if (p.sparse_mode) return launch_feature_fwd_kind<kSoftmaxSparse>(p, s);
       return plain ? launch_feature_fwd_kind<kSoftmax | kPlainBit>(p, s) : launch_feature_fwd_kind<kSoftmax>(p, s);
     default: return launch_feature_fwd_kind<kBspline>(p, s);
   }
@@ -1222,6 +1421,7 @@ int launch_feature_bwd(const FeatParams& p, cudaStream_t s) {
   switch (p.kind) {
     case kRelu2: return plain ? launch_feature_bwd_kind<kRelu2 | kPlainBit>(p, s) : launch_feature_bwd_kind<kRelu2>(p, s);
     case kSoftmax:
+      if (p.sparse_mode) return launch_feature_bwd_kind<kSoftmaxSparse>(p, s);
       return plain ? launch_feature_bwd_kind<kSoftmax | kPlainBit>(p, s) : launch_feature_bwd_kind<kSoftmax>(p, s);
     default: return launch_feature_bwd_kind<kBspline>(p, s);
   }

@@ -38,6 +38,7 @@ struct GnRowParams {
   float* dtau;
   const float* in[8];
   float* out[4];
+  __nv_bfloat16* out_bf16;  // bf16 copy of out[0] (forward stages), or null
 };
 
 // sigma, sigma', sigma'' of the fast net's nonlinearity
@@ -96,6 +97,20 @@ __device__ __forceinline__ void gn_store(float* p, const float (&r)[W], int n) {
   for (int i = 0; i < W; ++i) {
     const int c = lane + 32 * i;
     if (c < n) p[c] = r[i];
+  }
+}
+
+// out[0] of a forward stage: f32 and/or its bf16 copy (the scans' operand)
+template <int W>
+__device__ __forceinline__ void gn_store_out0(const GnRowParams& p, size_t off, const float (&r)[W], int n) {
+  if (p.out[0]) gn_store<W>(p.out[0] + off, r, n);
+  if (p.out_bf16) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      const int c = lane + 32 * i;
+      if (c < n) p.out_bf16[off + c] = __float2bfloat16_rn(r[i]);
+    }
   }
 }
 
@@ -186,7 +201,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_write_pre_kernel(GnRowParams p)
     }
     hh = gn_warp_sum(hh);
     kk = gn_warp_sum(kk);
-    gn_store<W>(p.out[0] + r * p.m, h, p.m);
+    gn_store_out0<W>(p, r * p.m, h, p.m);
     gn_store<W>(p.out[1] + r * p.m, s2, p.m);
     if ((threadIdx.x & 31) == 0) {
       p.out[2][r] = hh;
@@ -209,7 +224,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_write_lam_kernel(GnRowParams p)
     const float hh = __ldg(p.in[4] + r), kk = __ldg(p.in[5] + r);
 #pragma unroll
     for (int i = 0; i < W; ++i) lam[i] = (v[i] - k[i] - o[i]) / (fmaf(kk, q[i], hh) + p.eps);
-    gn_store<W>(p.out[0] + r * p.d, lam, p.d);
+    gn_store_out0<W>(p, r * p.d, lam, p.d);
   }
 }
 
@@ -231,7 +246,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_write_g_kernel(GnRowParams p) {
       Act<NL>::eval(fmaf(a[i], inv, -tau[i]), f, d1, d2);
       g[i] = d1 * u[i] * inv;
     }
-    gn_store<W>(p.out[0] + r * p.m, g, p.m);
+    gn_store_out0<W>(p, r * p.m, g, p.m);
   }
 }
 
@@ -251,7 +266,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_query_pre_kernel(GnRowParams p)
       const float x = fmaxf(fmaf(a[i], inv, -tau[i]), 0.f);
       h[i] = x * x;
     }
-    gn_store<W>(p.out[0] + r * p.m, h, p.m);
+    gn_store_out0<W>(p, r * p.m, h, p.m);
   }
 }
 
@@ -297,7 +312,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_features_kernel(GnRowParams p) 
       Act<NL>::eval(fmaf(pre[i], inv, -tau[i]), f, d1, d2);
       hq[i] = f;
     }
-    gn_store<W>(p.out[0] + r * p.m, hq, p.m);
+    gn_store_out0<W>(p, r * p.m, hq, p.m);
   }
 }
 

@@ -151,12 +151,18 @@ class _Run:
         self.like = q
         self.tau = None if tau is None else tau[..., 0].float().contiguous()   # [H, m]
 
-    def new(self, width, zero=False):
+    def new(self, width, zero=False, dtype=torch.float32):
         shape = (self.B, self.H, self.T) + ((width,) if width else ())
         f = torch.zeros if zero else torch.empty
-        return f(shape, dtype=torch.float32, device=self.like.device)
+        return f(shape, dtype=dtype, device=self.like.device)
 
-    def rows(self, stage, ins, outs, flags=0, dtau=None):
+    def new_bf16(self, width):
+        return self.new(width, dtype=torch.bfloat16)
+
+    def rows(self, stage, ins, outs, flags=0, dtau=None, bf16=None):
+        """One row stage; ``bf16`` receives a bf16 copy of ``outs[0]`` (the
+        scans' operand), and ``outs[0]`` may then be None for the stages
+        whose first output feeds only the scans."""
         if self.fake:
             return
         a = _lib.GnRowsArgs()
@@ -168,6 +174,7 @@ class _Run:
             a.inputs[i] = None if x is None else x.data_ptr()
         for i, x in enumerate(outs):
             a.outputs[i] = None if x is None else x.data_ptr()
+        a.out_bf16 = None if bf16 is None else bf16.data_ptr()
         _lib.check(_lib.load().ts_b200_gn_rows(ctypes.byref(a), _stream()))
 
     # ----------------------------------------------------------- scans
@@ -242,29 +249,29 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
     las = [None] + [log_alphas[j].float() for j in range(J)]
     stale = [False] + [mode == "stale"] * J
-    a_k, h_k, s2, hh, kk, O, RS, lam, U, g = _write_forward(run, k, v, W1, W2)
+    a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb = _write_forward(run, k, v, W1, W2, bf16=True)
     # stage 1, shared by all views (engine.py:475-500)
     a_q = _hm(W1, q)
     if read_norm_w1:
-        h0 = run.new(m)
-        run.rows(_lib.TS_GN_QUERY_PRE, [a_q], [h0])
-        R1, st1 = run.scan_fwd(h0, h_k, g, True, las, stale)
+        h0 = run.new_bf16(m)
+        run.rows(_lib.TS_GN_QUERY_PRE, [a_q], [None], bf16=h0)
+        R1, st1 = run.scan_fwd(h0, h_kb, g, True, las, stale)
     else:
         h0 = q.new_empty(0)
         R1, st1 = run.scan_fwd(q, k, g, False, las, stale)
-    saved = [a_k, h_k, s2, hh, kk, O, RS, lam, U, g, a_q, h0]
+    saved = [a_k, h_k, h_kb, s2, hh, kk, O, RS, lam, lamb, U, g, a_q, h0]
     saved += [x for piece in st1 for x in piece[3:]]
     ys = []
     # stage 2, one query per view (engine.py:500-528)
     for s in range(J + 1):
-        hq = run.new(m)
-        run.rows(_lib.TS_GN_FEATURES, [a_q, R1[s]], [hq], flags=int(read_norm_w1))
+        hq, hqb = run.new(m), run.new_bf16(m)
+        run.rows(_lib.TS_GN_FEATURES, [a_q, R1[s]], [hq], flags=int(read_norm_w1), bf16=hqb)
         base = _hm(W2, hq)
-        (C,), st2 = run.scan_fwd(hq, h_k, lam, bool(read_norm), [las[s]], [stale[s]])
+        (C,), st2 = run.scan_fwd(hqb, h_kb, lamb, bool(read_norm), [las[s]], [stale[s]])
         y = run.new(d)
         run.rows(_lib.TS_GN_OUT, [q, base, C], [y], flags=int(bool(read_norm)))
         ys.append(y)
-        saved += [hq] + [x for piece in st2 for x in piece[3:]]
+        saved += [hq, hqb] + [x for piece in st2 for x in piece[3:]]
     y = ys[0]
     if J and mode == "stale":
         # y - sum_j eta_j (y_stale_j - y_base), y_base the zero-memory read
@@ -298,18 +305,18 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
     las = [None] + [log_alphas[j].float() for j in range(J)]
     stale = [False] + [mode == "stale"] * J
-    (a_k, h_k, s2, hh, kk, O, RS, lam, U, g, a_q, h0), rest = _take(saved, 12)
+    (a_k, h_k, h_kb, s2, hh, kk, O, RS, lam, lamb, U, g, a_q, h0), rest = _take(saved, 14)
     q1 = h0 if read_norm_w1 else q
-    k1 = h_k if read_norm_w1 else k
+    k1 = h_kb if read_norm_w1 else k
     n1 = len(_scan_pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1]))
     flat1, rest = _take(rest, 2 * n1)
     st1 = _pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1], flat1)
     views = []
     for s in range(J + 1):
-        (hq,), rest = _take(rest, 1)
+        (hq, hqb), rest = _take(rest, 2)
         n2 = len(_scan_pieces(d, bool(read_norm), 1, m))
         flat2, rest = _take(rest, 2 * n2)
-        views.append((hq, _pieces(d, bool(read_norm), 1, m, flat2)))
+        views.append((hq, hqb, _pieces(d, bool(read_norm), 1, m, flat2)))
     dy = dy.float().contiguous()
     # the view combination
     tau_grad = None if tau is None else torch.zeros(H, m, dtype=torch.float32, device=q.device)
@@ -338,14 +345,14 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     da_q = run.new(m)
     R1 = [torch.cat([p[3][i] for p in st1], dim=-1) if len(st1) > 1 else st1[0][3][i] for i in range(J + 1)]
     dR1 = [run.new(R1[0].shape[-1]) for _ in range(J + 1)]
-    for s, (hq, st2) in enumerate(views):
+    for s, (hq, hqb, st2) in enumerate(views):
         C = st2[0][3][0] if len(st2) == 1 else torch.cat([p[3][0] for p in st2], dim=-1)
         if read_norm:
             dC = run.new(d + 1)
             run.rows(_lib.TS_GN_OUT_BWD, [dys[s], C], [dC], flags=1)
         else:
             dC = dys[s]
-        dhq, dhk_s, dlam_s, dla_s = run.scan_bwd([dC], hq, h_k, lam, st2, [las[s]], [stale[s]])
+        dhq, dhk_s, dlam_s, dla_s = run.scan_bwd([dC], hqb, h_kb, lamb, st2, [las[s]], [stale[s]])
         dh_k += dhk_s
         dlam += dlam_s
         dla[s] += dla_s[0]
@@ -376,18 +383,26 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     return dq, dk, dv, dW1 + dW1_w, dW2 + dW2_w, tau_grad, dla[1:], deta
 
 
-def _write_forward(run, k, v, W1, W2):
+def _write_forward(run, k, v, W1, W2, bf16=False):
     """The GN write (engine.py:161-340): ``a = W1 k`` and the row streams
     ``h, s2, hh, kk, O, RS, lam, U, g`` (h the keys, g and lam the payloads of
-    the two read stages; the rest kept for the backward)."""
+    the two read stages; the rest kept for the backward).  With ``bf16`` the
+    row kernels also write the scans' bf16 operands: g only in bf16, and
+    ``(h_bf16, lam_bf16)`` follow the tuple."""
     m, d = run.m, run.d
     a_k = _hm(W1, k)
     h_k, s2, hh, kk = run.new(m), run.new(m), run.new(0), run.new(0)
-    run.rows(_lib.TS_GN_WRITE_PRE, [a_k, k], [h_k, s2, hh, kk])
+    h_kb = run.new_bf16(m) if bf16 else None
+    run.rows(_lib.TS_GN_WRITE_PRE, [a_k, k], [h_k, s2, hh, kk], bf16=h_kb)
     O, RS = _hm(W2, h_k), _hm(W2 * W2, s2)
     lam = run.new(d)
-    run.rows(_lib.TS_GN_WRITE_LAM, [v, k, O, RS, hh, kk], [lam])
+    lamb = run.new_bf16(d) if bf16 else None
+    run.rows(_lib.TS_GN_WRITE_LAM, [v, k, O, RS, hh, kk], [lam], bf16=lamb)
     U = _hm(W2.transpose(1, 2), lam)
+    if bf16:
+        g = run.new_bf16(m)
+        run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [None], bf16=g)
+        return a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb
     g = run.new(m)
     run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [g])
     return a_k, h_k, s2, hh, kk, O, RS, lam, U, g

@@ -132,7 +132,7 @@ def _fused_core(module):
         return None
     if cfg.decay_gate != "off" or (cfg.read_fade and cfg.read_fade_mode != "fast") or cfg.value_centers:
         return None
-    if cfg.kernel_sparsity != "none" or (cfg.rope != "none" and cfg.rope_placement != "input"):
+    if cfg.rope != "none" and cfg.rope_placement != "input":
         return None
     from .config import KernelConfig, RoPEConfig, TemporalConfig, ThetaScanConfig
     from .mixer import ThetaScanCore
@@ -143,7 +143,10 @@ def _fused_core(module):
         bspline_bound=float(cfg.bspline_bound), bspline_scale=float(cfg.bspline_scale),
         bspline_scale_mode=cfg.bspline_scale_mode,
         value_representation="value_mlp" if cfg.value_mlp_mult > 0 else "raw",
-        value_mlp_multiplier=float(cfg.value_mlp_mult) if cfg.value_mlp_mult > 0 else 1.0)
+        value_mlp_multiplier=float(cfg.value_mlp_mult) if cfg.value_mlp_mult > 0 else 1.0,
+        sparsity=cfg.kernel_sparsity, sparse_blend_init=float(cfg.kernel_sparse_blend_init),
+        relative_threshold_init=float(cfg.kernel_relative_threshold_init),
+        threshold_temperature=float(cfg.kernel_threshold_temperature))
     temporal = TemporalConfig(mode="bank", recency_branches=cfg.fade_branches,
                               retention_inits=tuple(cfg.resolved_fade_alphas),
                               blend_mode=cfg.fade_blend_mode) if cfg.read_fade else TemporalConfig()

@@ -45,6 +45,11 @@ class KernelSpec:
     bound: float = 3.0
     spline_scale: float = 1.0   # fixed B-spline scale when no learned scale
     read: str = "key_mass"      # key_mass | feature_mass | none (engine.py:402-456)
+    sparsity: str = "none"      # none | relative_soft | relative_st | relative_st_blend (softmax partition)
+    temperature: float = 0.25   # relative-threshold gate temperature
+
+
+SPARSITY = {"none": 0, "relative_soft": 1, "relative_st": 2, "relative_st_blend": 3}
 
 
 def _ptr(t):
@@ -76,6 +81,8 @@ def _feature_args(spec, q, k, W1, W2, ctl, phi_k, phi_q, y0):
     a.spline_scale = _ptr(ctl["scale"])
     a.spline_scale_scalar = spec.spline_scale
     a.phi_k, a.phi_q, a.y0 = phi_k.data_ptr(), _ptr(phi_q), _ptr(y0)
+    a.sparsity, a.threshold_temperature = SPARSITY[spec.sparsity], spec.temperature
+    a.relative_threshold, a.sparse_blend = _ptr(ctl.get("rho")), _ptr(ctl.get("alpha"))
     return a
 
 
@@ -121,8 +128,9 @@ def _set_prologue(fa, prologue):
         fa.l2norm, fa.l2norm_eps = 1, prologue.l2norm_eps
 
 
-def _controls(thr, bias, gain, scale):
-    return {"thr": _f32(thr), "bias": _f32(bias), "gain": _f32(gain), "scale": _f32(scale)}
+def _controls(thr, bias, gain, scale, rho=None, alpha=None):
+    return {"thr": _f32(thr), "bias": _f32(bias), "gain": _f32(gain), "scale": _f32(scale), "rho": _f32(rho),
+            "alpha": _f32(alpha)}
 
 
 def _stale_flags(spec, n_slots):
@@ -254,10 +262,11 @@ def _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq_out, dk_out, dv_out)
     dW1 = torch.zeros(W1b.shape, dtype=torch.float32, device=dev)
     dW2t = torch.zeros(W2b.shape[0], W2b.shape[2], W2b.shape[1], dtype=torch.float32, device=dev)
     grads = {key: (torch.zeros_like(ctl[key]) if ctl[key] is not None else None)
-             for key in ("thr", "bias", "gain", "scale")}
+             for key in ("thr", "bias", "gain", "scale", "rho", "alpha")}
     fg.dw1, fg.dw2, fg.dw2_transposed = dW1.data_ptr(), dW2t.data_ptr(), 1
     fg.dscore_bias, fg.dthreshold = _ptr(grads["bias"]), _ptr(grads["thr"])
     fg.dgain, fg.dspline_scale = _ptr(grads["gain"]), _ptr(grads["scale"])
+    fg.drelative_threshold, fg.dsparse_blend = _ptr(grads["rho"]), _ptr(grads["alpha"])
     _lib.check(lib.ts_b200_feature_bwd(ctypes.byref(fa), ctypes.byref(fg), _stream()))
     dW2 = dW2t.transpose(1, 2)
     dla = None if n == 1 else torch.stack(dlas[1:])
@@ -695,7 +704,8 @@ class _KernelCoreViews(torch.autograd.Function):
 
 
 def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, shard, *, threshold=None,
-                        score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None):
+                        score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None,
+                        relative_threshold=None, sparse_blend=None):
     """The hot path of :func:`kernel_core_qkv` on one contiguous shard of the
     sequence (``prologue.pos0`` = its first position).  The scan runs in two
     halves around one exchange of shard totals (``shard.gather``, an
@@ -715,8 +725,8 @@ def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | N
     if spec.mode == "stale":
         raise NotImplementedError("b200 backend: sequence shards of a stale bank are not built (stale scans take "
                                   "no boundary states); fast banks and the plain sum shard")
-    if spec.read != "key_mass":
-        raise NotImplementedError("b200 backend: sequence shards read with key mass only")
+    if spec.read != "key_mass" or spec.sparsity != "none":
+        raise NotImplementedError("b200 backend: sequence shards read with key mass and no relative sparsity only")
     hold = _ShardScan()
     phi_q, phi_k, y0, U = _ShardStageA.apply(hold, spec, prologue, H, qkv, W1, W2, threshold, score_bias, gain,
                                              spline_scale, log_alphas)
@@ -732,7 +742,8 @@ def kernel_core_sharded(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | N
 
 
 def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None, *, threshold=None,
-                    score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None):
+                    score_bias=None, gain=None, spline_scale=None, log_alphas=None, etas=None,
+                    relative_threshold=None, sparse_blend=None):
     """Hot path from the raw fused projection; returns ``y`` token-major ``[B,T,H,d]``.
 
     ``qkv``: bf16 ``[B,T,3*H*d]`` output of the fused q/k/v projection
@@ -752,16 +763,16 @@ def kernel_core_qkv(qkv, H, W1, W2, spec: KernelSpec, prologue: Prologue | None,
     from . import ops  # noqa: F401  (registers the operators)
     rot = prologue.rot if prologue is not None else 0
     outs = torch.ops.thetascan_b200.kernel_mixer_qkv_fwd(
-        qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas,
+        qkv, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas, etas,
         prologue.cos if rot else None, prologue.sin if rot else None, H, rot,
         -1.0 if prologue is None or prologue.l2norm_eps is None else float(prologue.l2norm_eps),
         spec.kind, spec.mode, float(spec.eps), float(spec.gain), int(spec.basis), float(spec.bound),
-        float(spec.spline_scale))
+        float(spec.spline_scale), spec.sparsity, float(spec.temperature))
     return outs[0]
 
 
 def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias=None, gain=None,
-                spline_scale=None, log_alphas=None, etas=None):
+                spline_scale=None, log_alphas=None, etas=None, relative_threshold=None, sparse_blend=None):
     """Kernel-family hot path on the GPU; returns ``y`` token-major ``[B,T,H,d]``.
 
     ``q, k, v``: bf16 ``[B,H,T,d]`` after RoPE / L2 norm.  ``W1 [H,P,d]`` and
@@ -782,10 +793,13 @@ def kernel_core(q, k, v, W1, W2, spec: KernelSpec, *, threshold=None, score_bias
     if spec.read not in ("key_mass", "feature_mass", "none"):
         raise ValueError(f"kernel_core: unknown read normalization {spec.read!r}")
     if spec.read != "key_mass":
+        if spec.sparsity != "none":
+            raise NotImplementedError("b200 backend: relative sparsity reads with key mass only")
         return _KernelCoreViews.apply(spec, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale,
                                       log_alphas, etas)
     from . import ops  # noqa: F401  (registers the operators)
     outs = torch.ops.thetascan_b200.kernel_mixer_fwd(
-        q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, spec.kind, spec.mode,
-        float(spec.eps), float(spec.gain), int(spec.basis), float(spec.bound), float(spec.spline_scale))
+        q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas,
+        etas, spec.kind, spec.mode, float(spec.eps), float(spec.gain), int(spec.basis), float(spec.bound),
+        float(spec.spline_scale), spec.sparsity, float(spec.temperature))
     return outs[0]

@@ -163,6 +163,16 @@ class ThetaScanCore(nn.Module):
             self.kernel_relu2_threshold = nn.Parameter(torch.zeros(H))
         else:
             self.register_parameter("kernel_relu2_threshold", None)
+        if kernel and k.sparsity != "none":
+            # relative-to-maximum cutoff rho = sigmoid(raw) (block.py:167-180)
+            rho0 = float(k.relative_threshold_init)
+            self.kernel_relative_threshold_raw = nn.Parameter(torch.full((H,), math.log(rho0 / (1.0 - rho0))))
+        else:
+            self.register_parameter("kernel_relative_threshold_raw", None)
+        if kernel and k.sparsity == "relative_st_blend":
+            self.kernel_sparse_blend_raw = nn.Parameter(torch.full((H,), float(k.sparse_blend_init)))
+        else:
+            self.register_parameter("kernel_sparse_blend_raw", None)
         if kernel and k.bspline_scale_mode == "learned_per_head":
             self.bspline_scale_raw = nn.Parameter(torch.full((H,), _inverse_softplus(float(k.bspline_scale))))
         else:
@@ -230,7 +240,8 @@ class ThetaScanCore(nn.Module):
         self.spec = KernelSpec(
             kind=k.feature_map, mode=("sum" if t.mode == "sum" else t.bank_mode),
             eps=1e-6, gain=float(k.kernel_sharpness), basis=k.bspline_basis_count,
-            bound=float(k.bspline_bound), spline_scale=float(k.bspline_scale), read=k.read_normalization)
+            bound=float(k.bspline_bound), spline_scale=float(k.bspline_scale), read=k.read_normalization,
+            sparsity=k.sparsity, temperature=float(k.threshold_temperature))
         self._rot = _rope_width(d, cfg.rope.mode, cfg.rope.fraction)
 
     # -------------------------------------------------------------- helpers
@@ -343,8 +354,16 @@ class ThetaScanCore(nn.Module):
             F.softplus(self.kernel_sharpness_raw).clamp_min(torch.finfo(torch.float32).tiny)
         scale = None if self.bspline_scale_raw is None else \
             F.softplus(self.bspline_scale_raw).clamp_min(torch.finfo(torch.float32).tiny)
-        return dict(threshold=self.kernel_relu2_threshold, score_bias=self.kernel_score_bias, gain=gain,
-                    spline_scale=scale)
+        ctl = dict(threshold=self.kernel_relu2_threshold, score_bias=self.kernel_score_bias, gain=gain,
+                   spline_scale=scale)
+        if self.kernel_relative_threshold_raw is not None:
+            ctl["relative_threshold"] = torch.sigmoid(self.kernel_relative_threshold_raw)
+        if self.kernel_sparse_blend_raw is not None:
+            # forward value clamp(raw, 0, 1), gradient through sigmoid(raw) (block.py:427-438)
+            raw = self.kernel_sparse_blend_raw
+            surrogate = torch.sigmoid(raw)
+            ctl["sparse_blend"] = raw.clamp(0.0, 1.0).detach() + surrogate - surrogate.detach()
+        return ctl
 
     def project(self, x):
         """q, k, v ``[B,H,T,d]`` in the stream dtype (block.py:577-594)."""

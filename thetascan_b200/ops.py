@@ -172,10 +172,10 @@ torch.library.register_autograd(f"{LIB}::scan_views_fwd", _scan_backward, setup_
 
 # --------------------------------------------------------------------------- fused kernel-family core
 
-def _spec(kind, mode, eps, gain, basis, bound, spline_scale):
+def _spec(kind, mode, eps, gain, basis, bound, spline_scale, sparsity="none", temperature=0.25):
     from .kernel import KernelSpec
     return KernelSpec(kind=kind, mode=mode, eps=eps, gain=gain, basis=basis, bound=bound,
-                      spline_scale=spline_scale, read="key_mass")
+                      spline_scale=spline_scale, read="key_mass", sparsity=sparsity, temperature=temperature)
 
 
 def _fake_core_outputs(like, B, H, T, d, W1, kind, basis, log_alphas, mode):
@@ -195,24 +195,39 @@ def _grad_or_empty(g, like, ref):
     return ref.new_empty(0) if like is None else g.to(like.dtype)
 
 
+def _control_grads(g, controls, ref):
+    """Gradients of the six feature controls (threshold, score bias, gain,
+    spline scale, relative threshold, sparse blend), empty where absent."""
+    keys = ("thr", "bias", "gain", "scale", "rho", "alpha")
+    return [_grad_or_empty(g[key], c, ref) for key, c in zip(keys, controls)]
+
+
+# Tensor inputs of the fused core ops after the streams and weights: the six
+# feature controls (threshold, score_bias, gain, spline_scale,
+# relative_threshold, sparse_blend), then log_alphas and etas.
+_N_CORE_TENSORS = 13
+
+
 @torch.library.custom_op(f"{LIB}::kernel_mixer_fwd", mutates_args=())
 def kernel_mixer_fwd(q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor, threshold: Optional[Tensor],
                      score_bias: Optional[Tensor], gain: Optional[Tensor], spline_scale: Optional[Tensor],
+                     relative_threshold: Optional[Tensor], sparse_blend: Optional[Tensor],
                      log_alphas: Optional[Tensor], etas: Optional[Tensor], kind: str, mode: str, eps: float,
-                     gain_scalar: float, basis: int, bound: float,
-                     spline_scale_scalar: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+                     gain_scalar: float, basis: int, bound: float, spline_scale_scalar: float, sparsity: str,
+                     temperature: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     """``y [B,T,H,d]`` bf16 plus (phi_q, phi_k, y0, stacked reads, workspace)."""
     from .kernel import _controls, _core_forward
-    _require_cuda(q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas)
-    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar)
-    ctl = _controls(threshold, score_bias, gain, spline_scale)
+    _require_cuda(q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend,
+                  log_alphas, etas)
+    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity, temperature)
+    ctl = _controls(threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend)
     y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, None)
     return y, st["phi_q"], st["phi_k"], st["y0"], st["slots_all"], st["ws"]
 
 
 @kernel_mixer_fwd.register_fake
-def _(q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, kind, mode, eps, gain_scalar,
-      basis, bound, spline_scale_scalar):
+def _(q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas,
+      etas, kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity, temperature):
     B, H, T, d = (int(s) for s in q.shape)
     return _fake_core_outputs(q, B, H, T, d, W1, kind, basis, log_alphas, mode)
 
@@ -220,33 +235,35 @@ def _(q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, et
 @torch.library.custom_op(f"{LIB}::kernel_mixer_bwd", mutates_args=())
 def kernel_mixer_bwd(dy: Tensor, q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor,
                      threshold: Optional[Tensor], score_bias: Optional[Tensor], gain: Optional[Tensor],
-                     spline_scale: Optional[Tensor], log_alphas: Optional[Tensor], etas: Optional[Tensor],
+                     spline_scale: Optional[Tensor], relative_threshold: Optional[Tensor],
+                     sparse_blend: Optional[Tensor], log_alphas: Optional[Tensor], etas: Optional[Tensor],
                      phi_q: Tensor, phi_k: Tensor, y0: Tensor, slots: Tensor, ws: Tensor, kind: str, mode: str,
-                     eps: float, gain_scalar: float, basis: int, bound: float,
-                     spline_scale_scalar: float) -> list[Tensor]:
-    """Gradients of q, k, v, W1, W2, the four controls, log_alphas and etas
+                     eps: float, gain_scalar: float, basis: int, bound: float, spline_scale_scalar: float,
+                     sparsity: str, temperature: float) -> list[Tensor]:
+    """Gradients of q, k, v, W1, W2, the six controls, log_alphas and etas
     (an empty tensor where the input is None)."""
     from .kernel import _controls, _core_backward, _saved_state
     _require_cuda(dy, q, k, v, W1, W2, phi_q, phi_k, y0, slots, ws)
-    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar)
-    ctl = _controls(threshold, score_bias, gain, spline_scale)
+    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity, temperature)
+    controls = (threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend)
+    ctl = _controls(*controls)
     st = _saved_state(W1, W2, log_alphas, etas, phi_q, phi_k, y0, slots, ws)
     g = _core_backward(spec, q, k, v, st, ctl, dy, None, None, None, None)
     d = q.shape[-1]
     return [g["dq"].to(q.dtype), g["dk"].to(k.dtype), g["dvaug"][..., :d].to(v.dtype).contiguous(),
-            g["dW1"].to(W1.dtype), g["dW2"].to(W2.dtype).contiguous(), _grad_or_empty(g["thr"], threshold, q),
-            _grad_or_empty(g["bias"], score_bias, q), _grad_or_empty(g["gain"], gain, q),
-            _grad_or_empty(g["scale"], spline_scale, q), _grad_or_empty(g["dla"], log_alphas, q),
-            _grad_or_empty(g["deta"], etas, q)]
+            g["dW1"].to(W1.dtype), g["dW2"].to(W2.dtype).contiguous(), *_control_grads(g, controls, q),
+            _grad_or_empty(g["dla"], log_alphas, q), _grad_or_empty(g["deta"], etas, q)]
 
 
 @kernel_mixer_bwd.register_fake
-def _(dy, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, phi_q, phi_k, y0, slots, ws,
-      kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar):
+def _(dy, q, k, v, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas,
+      etas, phi_q, phi_k, y0, slots, ws, kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity,
+      temperature):
     def like(t, ref):
         return ref.new_empty(0) if t is None else torch.empty_like(t)
     return [torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(W1),
-            torch.empty_like(W2), like(threshold, q), like(score_bias, q), like(gain, q), like(spline_scale, q),
+            torch.empty_like(W2), *[like(c, q) for c in (threshold, score_bias, gain, spline_scale,
+                                                         relative_threshold, sparse_blend)],
             like(log_alphas, q), like(etas, q)]
 
 
@@ -255,7 +272,7 @@ def _none_if_absent(grads, inputs):
 
 
 def _core_setup(ctx, inputs, output):
-    tensors, scalars = inputs[:11], inputs[11:]
+    tensors, scalars = inputs[:_N_CORE_TENSORS], inputs[_N_CORE_TENSORS:]
     _, phi_q, phi_k, y0, slots, ws = output
     ctx.mark_non_differentiable(phi_q, phi_k, y0, slots, ws)
     # the saved intermediates take no gradient: do not fill zeros for them
@@ -274,7 +291,7 @@ def _unpack_saved(ctx, n_inputs):
 
 
 def _core_backward_op(ctx, dy, *unused):
-    inputs, (phi_q, phi_k, y0, slots, ws) = _unpack_saved(ctx, 11)
+    inputs, (phi_q, phi_k, y0, slots, ws) = _unpack_saved(ctx, _N_CORE_TENSORS)
     grads = kernel_mixer_bwd(dy, *inputs, phi_q, phi_k, y0, slots, ws, *ctx.scalars)
     return (*_none_if_absent(grads, inputs), *([None] * len(ctx.scalars)))
 
@@ -285,26 +302,30 @@ torch.library.register_autograd(f"{LIB}::kernel_mixer_fwd", _core_backward_op, s
 @torch.library.custom_op(f"{LIB}::kernel_mixer_qkv_fwd", mutates_args=())
 def kernel_mixer_qkv_fwd(qkv: Tensor, W1: Tensor, W2: Tensor, threshold: Optional[Tensor],
                          score_bias: Optional[Tensor], gain: Optional[Tensor], spline_scale: Optional[Tensor],
+                         relative_threshold: Optional[Tensor], sparse_blend: Optional[Tensor],
                          log_alphas: Optional[Tensor], etas: Optional[Tensor], rope_cos: Optional[Tensor],
                          rope_sin: Optional[Tensor], heads: int, rope_rot: int, l2norm_eps: float, kind: str,
                          mode: str, eps: float, gain_scalar: float, basis: int, bound: float,
-                         spline_scale_scalar: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+                         spline_scale_scalar: float, sparsity: str,
+                         temperature: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     """The fused core from the raw projection ``qkv [B,T,3Hd]`` (RoPE and L2
     norm inside the feature kernels)."""
     from .kernel import Prologue, _controls, _core_forward, _qkv_views
-    _require_cuda(qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, rope_cos, rope_sin)
-    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar)
+    _require_cuda(qkv, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend,
+                  log_alphas, etas, rope_cos, rope_sin)
+    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity, temperature)
     d = qkv.shape[-1] // (3 * heads)
     q, k, v = _qkv_views(qkv, heads, d)
-    ctl = _controls(threshold, score_bias, gain, spline_scale)
+    ctl = _controls(threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend)
     prologue = Prologue(rope_rot, rope_cos, rope_sin, None if l2norm_eps < 0 else l2norm_eps)
     y, st = _core_forward(spec, q, k, v, W1, W2, ctl, log_alphas, etas, prologue)
     return y, st["phi_q"], st["phi_k"], st["y0"], st["slots_all"], st["ws"]
 
 
 @kernel_mixer_qkv_fwd.register_fake
-def _(qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, rope_cos, rope_sin, heads, rope_rot,
-      l2norm_eps, kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar):
+def _(qkv, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas, etas,
+      rope_cos, rope_sin, heads, rope_rot, l2norm_eps, kind, mode, eps, gain_scalar, basis, bound,
+      spline_scale_scalar, sparsity, temperature):
     B, T, width = (int(s) for s in qkv.shape)
     d = width // (3 * heads)
     return _fake_core_outputs(qkv, B, heads, T, d, W1, kind, basis, log_alphas, mode)
@@ -313,39 +334,42 @@ def _(qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, 
 @torch.library.custom_op(f"{LIB}::kernel_mixer_qkv_bwd", mutates_args=())
 def kernel_mixer_qkv_bwd(dy: Tensor, qkv: Tensor, W1: Tensor, W2: Tensor, threshold: Optional[Tensor],
                          score_bias: Optional[Tensor], gain: Optional[Tensor], spline_scale: Optional[Tensor],
+                         relative_threshold: Optional[Tensor], sparse_blend: Optional[Tensor],
                          log_alphas: Optional[Tensor], etas: Optional[Tensor], rope_cos: Optional[Tensor],
                          rope_sin: Optional[Tensor], phi_q: Tensor, phi_k: Tensor, y0: Tensor, slots: Tensor,
                          ws: Tensor, heads: int, rope_rot: int, l2norm_eps: float, kind: str, mode: str, eps: float,
-                         gain_scalar: float, basis: int, bound: float, spline_scale_scalar: float) -> list[Tensor]:
-    """Gradients of qkv, W1, W2, the four controls, log_alphas and etas."""
+                         gain_scalar: float, basis: int, bound: float, spline_scale_scalar: float, sparsity: str,
+                         temperature: float) -> list[Tensor]:
+    """Gradients of qkv, W1, W2, the six controls, log_alphas and etas."""
     from .kernel import Prologue, _controls, _core_backward, _qkv_views, _saved_state
     _require_cuda(dy, qkv, W1, W2, phi_q, phi_k, y0, slots, ws)
-    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar)
+    spec = _spec(kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar, sparsity, temperature)
     d = qkv.shape[-1] // (3 * heads)
     q, k, v = _qkv_views(qkv, heads, d)
     dqkv = torch.empty_like(qkv)
     dq, dk, dv = _qkv_views(dqkv, heads, d)
-    ctl = _controls(threshold, score_bias, gain, spline_scale)
+    controls = (threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend)
+    ctl = _controls(*controls)
     st = _saved_state(W1, W2, log_alphas, etas, phi_q, phi_k, y0, slots, ws)
     prologue = Prologue(rope_rot, rope_cos, rope_sin, None if l2norm_eps < 0 else l2norm_eps)
     g = _core_backward(spec, q, k, v, st, ctl, dy, prologue, dq, dk, dv)
-    return [dqkv, g["dW1"].to(W1.dtype), g["dW2"].to(W2.dtype).contiguous(),
-            _grad_or_empty(g["thr"], threshold, qkv), _grad_or_empty(g["bias"], score_bias, qkv),
-            _grad_or_empty(g["gain"], gain, qkv), _grad_or_empty(g["scale"], spline_scale, qkv),
+    return [dqkv, g["dW1"].to(W1.dtype), g["dW2"].to(W2.dtype).contiguous(), *_control_grads(g, controls, qkv),
             _grad_or_empty(g["dla"], log_alphas, qkv), _grad_or_empty(g["deta"], etas, qkv)]
 
 
 @kernel_mixer_qkv_bwd.register_fake
-def _(dy, qkv, W1, W2, threshold, score_bias, gain, spline_scale, log_alphas, etas, rope_cos, rope_sin, phi_q, phi_k,
-      y0, slots, ws, heads, rope_rot, l2norm_eps, kind, mode, eps, gain_scalar, basis, bound, spline_scale_scalar):
+def _(dy, qkv, W1, W2, threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend, log_alphas, etas,
+      rope_cos, rope_sin, phi_q, phi_k, y0, slots, ws, heads, rope_rot, l2norm_eps, kind, mode, eps, gain_scalar,
+      basis, bound, spline_scale_scalar, sparsity, temperature):
     def like(t):
         return qkv.new_empty(0) if t is None else torch.empty_like(t)
-    return [torch.empty_like(qkv), torch.empty_like(W1), torch.empty_like(W2), like(threshold), like(score_bias),
-            like(gain), like(spline_scale), like(log_alphas), like(etas)]
+    return [torch.empty_like(qkv), torch.empty_like(W1), torch.empty_like(W2),
+            *[like(c) for c in (threshold, score_bias, gain, spline_scale, relative_threshold, sparse_blend)],
+            like(log_alphas), like(etas)]
 
 
 def _qkv_setup(ctx, inputs, output):
-    tensors, scalars = inputs[:11], inputs[11:]
+    tensors, scalars = inputs[:_N_CORE_TENSORS], inputs[_N_CORE_TENSORS:]
     _, phi_q, phi_k, y0, slots, ws = output
     ctx.mark_non_differentiable(phi_q, phi_k, y0, slots, ws)
     # the saved intermediates take no gradient: do not fill zeros for them
@@ -356,10 +380,10 @@ def _qkv_setup(ctx, inputs, output):
 
 
 def _qkv_backward_op(ctx, dy, *unused):
-    inputs, (phi_q, phi_k, y0, slots, ws) = _unpack_saved(ctx, 11)
+    inputs, (phi_q, phi_k, y0, slots, ws) = _unpack_saved(ctx, _N_CORE_TENSORS)
     grads = kernel_mixer_qkv_bwd(dy, *inputs, phi_q, phi_k, y0, slots, ws, *ctx.scalars)
-    # qkv, W1, W2, 4 controls, log_alphas, etas; the rope tables take no gradient
-    return (*_none_if_absent(grads, inputs[:9]), None, None, *([None] * len(ctx.scalars)))
+    # qkv, W1, W2, 6 controls, log_alphas, etas; the rope tables take no gradient
+    return (*_none_if_absent(grads, inputs[:11]), None, None, *([None] * len(ctx.scalars)))
 
 
 torch.library.register_autograd(f"{LIB}::kernel_mixer_qkv_fwd", _qkv_backward_op, setup_context=_qkv_setup)

@@ -81,7 +81,24 @@ def features(x, W1, spec, ctl) -> torch.Tensor:
         if ctl.get("score_bias") is not None:
             pre = pre + _head_control(ctl["score_bias"], pre)
         gain = ctl.get("gain")
-        return torch.softmax(pre * (spec.gain if gain is None else _head_control(gain, pre)), -1)
+        logits = pre * (spec.gain if gain is None else _head_control(gain, pre))
+        dense = torch.softmax(logits, -1)
+        if spec.sparsity == "none":
+            return dense
+        # relative sparsity (kernel_features.py:43-70, 95-113)
+        shifted = logits - logits.amax(dim=-1, keepdim=True)
+        rho = _head_control(ctl["relative_threshold"], logits).clamp(min=spec.eps, max=1.0 - spec.eps)
+        margin = shifted - rho.log()
+        soft = torch.sigmoid(margin / spec.temperature)
+        if spec.sparsity == "relative_soft":
+            gate = soft
+        else:
+            gate = (margin >= 0.0).to(soft.dtype) + soft - soft.detach()
+        weights = shifted.exp() * gate
+        sparse = weights / weights.sum(-1, keepdim=True).clamp_min(spec.eps)
+        if spec.sparsity != "relative_st_blend":
+            return sparse
+        return dense + _head_control(ctl["sparse_blend"], logits) * (sparse - dense)
     if spec.kind == "projected_bspline":
         scale = ctl.get("spline_scale")
         s = spec.spline_scale if scale is None else _head_control(scale, pre)
@@ -99,7 +116,7 @@ def _mass(phi_k, retention, stale):
 
 
 def kernel_core_f32(q, k, v, W1, W2, spec, *, threshold=None, score_bias=None, gain=None, spline_scale=None,
-                    log_alphas=None, etas=None):
+                    log_alphas=None, etas=None, relative_threshold=None, sparse_blend=None):
     """``y = q + W2 phi(q) + blended normalized memory``, float32, ``[B,H,T,d]``.
 
     Same arguments as :func:`thetascan_b200.kernel.kernel_core` with float32
@@ -111,7 +128,8 @@ def kernel_core_f32(q, k, v, W1, W2, spec, *, threshold=None, score_bias=None, g
             raise NotImplementedError("b200 float32 path: float32 streams only")
     if (log_alphas is None) != (spec.mode == "sum"):
         raise ValueError("kernel_core: log_alphas are required exactly for a bank (mode fast/stale)")
-    ctl = {"threshold": threshold, "score_bias": score_bias, "gain": gain, "spline_scale": spline_scale}
+    ctl = {"threshold": threshold, "score_bias": score_bias, "gain": gain, "spline_scale": spline_scale,
+           "relative_threshold": relative_threshold, "sparse_blend": sparse_blend}
     eps = spec.eps
     phi_k = features(k, W1, spec, ctl)
     phi_q = features(q, W1, spec, ctl)
