@@ -167,6 +167,16 @@ def feature_spec(p, cfg):
         spec["gain"] = cfg.get("softmax_gain", 8.0) if raw is None else F.softplus(raw).clamp_min(
             torch.finfo(raw.dtype).tiny)
         spec["score_bias"] = p.get("kernel_score_bias")
+        # relative sparsity (block.py:167-180, 421-438): rho = sigmoid(raw);
+        # the blend's forward value clamp(raw, 0, 1), its gradient sigmoid's
+        spec["sparsity"] = cfg.get("kernel_sparsity", "none")
+        spec["temperature"] = cfg.get("kernel_threshold_temperature", 0.25)
+        if p.get("kernel_relative_threshold_raw") is not None:
+            spec["rho"] = torch.sigmoid(p["kernel_relative_threshold_raw"])
+        raw_b = p.get("kernel_sparse_blend_raw")
+        if raw_b is not None:
+            sur = torch.sigmoid(raw_b)
+            spec["blend"] = raw_b.clamp(0.0, 1.0).detach() + sur - sur.detach()
     else:
         raw = p.get("bspline_scale_raw")
         spec["n_basis"] = cfg["bspline_basis_count"]

@@ -372,12 +372,23 @@ def sparse_cases():
                 core.fade_eta.copy_(_seeded(6, *core.fade_eta.shape) * 0.5)
             # a cutoff that removes a visible share of the features
             core.kernel_relative_threshold_raw.copy_(torch.tensor([-2.0, -3.0], dtype=torch.float64))
-        x = _seeded(8, B, T, cfg.d_model).requires_grad_(True)
+            # float32-representable inputs: the stored fixture is exact for
+            # them (a hard gate would flip under a later rounding)
+            for p in module.parameters():
+                p.copy_(p.to(dtype).to(torch.float64))
+        x = _seeded(8, B, T, cfg.d_model).to(dtype).to(torch.float64).requires_grad_(True)
         y = module(x)
         w = _seeded(9, *y.shape)
         (y * w).sum().backward()
+        core_cfg = module._core_config
         out["mixers"][name] = {
             "public_config": cfg.to_dict(), "B": B, "T": T,
+            "core": {k: getattr(core_cfg, k) for k in (
+                "d_model", "n_heads", "head_dim", "mem_hidden", "feature_expansion", "expansion_key",
+                "kernel_kind", "softmax_gain", "bspline_basis_count", "bspline_bound", "bspline_scale",
+                "rope", "rope_frac", "rope_base", "read_fade", "read_fade_mode", "fade_blend_mode",
+                "read_norm", "read_norm_mode", "eps", "scan_chunk", "share_kq", "key_value_heads",
+                "kernel_sparsity", "kernel_threshold_temperature")},
             "params": {n: t.detach().to(dtype) for n, t in core.state_dict(keep_vars=True).items()
                        if t is not None},
             "x": x.detach().to(dtype), "y": y.detach().to(dtype), "out_weight": w.to(dtype),

@@ -196,3 +196,24 @@ def test_relative_sparsity_matches_reference(mode):
     _close(rho.grad, case["drho"], 1e-8)
     if mode == "relative_st_blend":
         _close(alpha.grad, case["dalpha"], 1e-8)
+
+
+@pytest.mark.parametrize("name", ["softmax_relative_soft", "softmax_relative_st", "softmax_relative_st_blend"])
+def test_sparse_mixer_oracle_matches_reference(name):
+    """The oracle mixer with relative sparsity against the reference mixer
+    (float32 fixtures: output, input gradient, every parameter gradient)."""
+    case = _load("sparse_cases.pt")["mixers"][name]
+    params = {n: t.to(torch.float64).clone().requires_grad_(t.is_floating_point() and not n.startswith("_"))
+              for n, t in case["params"].items()}
+    x = case["x"].to(torch.float64).clone().requires_grad_(True)
+    y = mixer.mixer_forward(params, _core_cfg(case), x)
+
+    def rel(got, want):   # the fixture is stored in float32: relative to its largest entry
+        want = want.to(torch.float64)
+        return float((got.detach() - want).abs().max() / want.abs().max())
+
+    assert rel(y, case["y"]) < 1e-6
+    (y * case["out_weight"].to(torch.float64)).sum().backward()
+    assert rel(x.grad, case["x_grad"]) < 1e-6
+    for n, g in case["grads"].items():
+        assert rel(params[n].grad, g) < 1e-6, n

@@ -258,10 +258,17 @@ __device__ __forceinline__ float softmax_logit(const FeatParams& p, int h, int i
   return ctl_gain<false>(p, h, i) * (a * inv + ctl_bias<false>(p, h, i));
 }
 
+// sigmoid(z) and its derivative from w = e^{-|z|}: s(1 - s) = w / (1 + w)^2
+// keeps its relative precision where s is within a few ulp of 1 (the top
+// features, whose margin is about -log rho; 1 - s formed by subtraction loses
+// most of its digits there).
 __device__ __forceinline__ void sparse_gate(const FeatParams& p, float margin, float& gate, float& dgate) {
-  const float sg = 1.f / (1.f + __expf(-margin / p.temperature));
+  const float z = margin / p.temperature;
+  const float w = expf(-fabsf(z));
+  const float r = 1.f / (1.f + w);
+  const float sg = z >= 0.f ? r : w * r;
   gate = p.sparse_mode == 1 ? sg : (margin >= 0.f ? 1.f : 0.f);
-  dgate = sg * (1.f - sg) / p.temperature;
+  dgate = w * r * r / p.temperature;
 }
 
 // d loss / d l_j of one column without the share of the max's gradient
@@ -270,7 +277,7 @@ struct SparseTerms {
   float dl, dshift, dmargin;
 };
 __device__ __forceinline__ SparseTerms sparse_terms(const FeatParams& p, const RowState& s, float g, float l) {
-  const float ex = __expf(l - s.mx);
+  const float ex = expf(l - s.mx);
   float gt, dgt;
   sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
   const bool blend = p.sparse_mode == 3;
@@ -320,7 +327,7 @@ __device__ RowState row_stats_sparse(const FeatParams& p, uint32_t ta_row, int h
     for (int e = 0; e < 16; ++e) {
       if (c + e >= p.P) continue;
       const float l = softmax_logit(p, h, c + e, a[e], s.inv);
-      const float ex = __expf(l - s.mx);
+      const float ex = expf(l - s.mx);
       float gt, dgt;
       sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
       E += ex;
@@ -342,7 +349,7 @@ __device__ RowState row_stats_sparse(const FeatParams& p, uint32_t ta_row, int h
       for (int e = 0; e < 16; ++e) {
         if (c + e >= p.P) continue;
         const float l = softmax_logit(p, h, c + e, a[e], s.inv);
-        const float ex = __expf(l - s.mx);
+        const float ex = expf(l - s.mx);
         float gt, dgt;
         sparse_gate(p, l - s.mx - s.lrho, gt, dgt);
         Sd += g[e] * ex * invE;
@@ -594,7 +601,7 @@ __device__ __forceinline__ void phi_chunk(const FeatParams& p, const RowState& s
       const int i = c + e;
       float v = 0.f;
       if (i < p.P) {
-        const float ex = __expf(softmax_logit(p, h, i, a[e], s.inv) - s.mx);
+        const float ex = expf(softmax_logit(p, h, i, a[e], s.inv) - s.mx);
         float gt, dgt;
         sparse_gate(p, softmax_logit(p, h, i, a[e], s.inv) - s.mx - s.lrho, gt, dgt);
         const float dense = ex * inv_E, sparse = ex * gt * inv_Z;
