@@ -202,6 +202,21 @@ GN_CONFIGS = {
         temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=1, T=160, dtype="float32"),
 }
 
+# Two Jacobian steps (write_iters == 2, engine.py:323-339): unnormalized
+# reads (the reference requires it), a fast bank, head_dim 64, ragged T;
+# one relu2 and one silu net with a learned threshold alternative.
+GN_JAC2_CONFIGS = {
+    "gn_jac2_relu2_bank": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, family="gn",
+        gn=dict(nonlinearity="relu2", jacobian_steps=2, read_normalization="none"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32"),
+    "gn_jac2_threshold_sum": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="relu2_threshold", jacobian_steps=2, read_normalization="none"),
+        rope=dict(mode="partial", fraction=0.5), B=2, T=96, dtype="float32"),
+}
+
 # Config-3 width (head_dim 128, m = 128, relu2, two-stage feature-mass read,
 # the plain sum view) at T = 1024; written to its own file, gn_c3_cases.pt.
 GN_C3_CONFIGS = {
@@ -398,7 +413,12 @@ def sparse_cases():
     return out
 
 
+def gn_jac2_cases():
+    return gn_cases(GN_JAC2_CONFIGS)
+
+
 GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases,
+              "gn_jac2": gn_jac2_cases,
               "gn_c3": gn_c3_cases, "gn_tanh": gn_tanh_cases, "sparse": sparse_cases}
 
 

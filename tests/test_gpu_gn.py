@@ -54,3 +54,35 @@ def test_gn_mixer_matches_reference_fixture(dev, name):
     grads = dict(module._core.named_parameters())
     for n, want in case["grads"].items():
         assert rel_err(grads[n].grad, want) < BF16_TOL, n
+
+
+# The write of two Jacobian steps matches float64 autograd at 1e-5 on its own
+# (tests/test_gpu_gn_rows.py, two-step write); the reads scan twice the
+# streams (two g payloads, two lambda streams with their own keys), all bf16,
+# and the thresholded case's W1 gradient lands at 2.1% of its largest entry.
+JAC2_LOOSE = {("gn_jac2_threshold_sum", "W1.0"): 3e-2}
+
+
+@pytest.mark.parametrize("name", ["gn_jac2_relu2_bank", "gn_jac2_threshold_sum"])
+def test_gn_two_jacobian_steps_match_reference_fixture(dev, name):
+    """Two Jacobian steps of the write (``GNConfig(jacobian_steps=2)``, the
+    reference's ``write_iters == 2``, engine.py:323-339) with unnormalized
+    reads, against fixtures of the reference GN mixer: output, input
+    gradient, every parameter gradient."""
+    from thetascan_b200 import _lib
+    from thetascan_b200.config import ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+
+    case = torch.load(os.path.join(GOLDEN, "gn_jac2_cases.pt"), weights_only=False)[name]
+    module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    x = case["x"].float().to(dev).requires_grad_(True)
+    y = module(x)
+    (y.double() * case["out_weight"].to(dev)).sum().backward()
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    assert rel_err(y, case["y"]) < BF16_TOL
+    assert rel_err(x.grad, case["x_grad"]) < BF16_TOL
+    grads = dict(module._core.named_parameters())
+    for n, want in case["grads"].items():
+        assert rel_err(grads[n].grad, want) < JAC2_LOOSE.get((name, n), BF16_TOL), n

@@ -272,3 +272,53 @@ def test_gn_prep_matches_float64(dev, d, rot):
     for got, w in zip((q, k, v), want):
         assert got.is_contiguous() and rel_err(got, w) < TOL
     assert rel_err(leaf.grad, ref.grad) < TOL
+
+
+@pytest.mark.parametrize("threshold", [False, True])
+@pytest.mark.parametrize("nl", ["relu2", "tanh"])
+def test_gn_two_step_write_matches_float64(dev, nl, threshold):
+    """Two Jacobian steps (engine.py:117-158 with the this-token delta,
+    323-339): the second step's streams h2, g2, lam2 and the gradients of
+    both steps' six streams with respect to k, v, W1, W2 and tau, against
+    float64 autograd of the same maps."""
+    from thetascan_b200 import _lib, gn
+    B, H, T, d, m = 2, 2, 70, 64, 128
+    eps = 1e-2
+    k, v, W1, W2, tau = _inputs(dev, B, H, T, d, m, threshold, seed=7)
+    run = gn._Run(k, m, tau, nl, eps, False)
+    st = gn._write_forward(run, k, v, W1, W2, bf16=True, g32=True)
+    a_k, h_k, kk, lam, g32 = st[0], st[1], st[4], st[7], st[12]
+    two = gn._write2_forward(run, k, v, W2, a_k, h_k, kk, lam, g32)
+    g2 = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_G, [two["a2"], two["U2"]], [g2])
+
+    leaves = [x.double().requires_grad_(True) for x in (k, v, W1, W2)]
+    tl = None if tau is None else tau.double().requires_grad_(True)
+    kd, vd, W1d, W2d = leaves
+    h, g, lm = _write_ref(kd, vd, W1d, W2d, tl, nl, eps)
+    kkd = kd.square().sum(-1, keepdim=True)
+    a2 = _hm(W1d, kd) + g * kkd
+    n2, inv2 = _rms(a2, eps)
+    p2 = _thr(n2, tl)
+    h2, ds2 = _act(nl, p2), _dact(nl, p2)
+    O2 = _hm(W2d, h2) + lm * (h * h2).sum(-1, keepdim=True)
+    s2 = ds2 * inv2
+    lam2 = (vd - kd - O2) / (h2.square().sum(-1, keepdim=True) + kkd * _hm(W2d * W2d, s2 * s2) + eps)
+    g2d = ds2 * _hm(W2d.transpose(1, 2), lam2) * inv2
+    want = (h, g, lm, h2, g2d, lam2)
+    for got, w in zip((h_k, g32, lam, two["h2"], g2, two["lam2"]), want):
+        assert rel_err(got, w) < TOL
+    gen = torch.Generator().manual_seed(6)
+    cot = [torch.randn(w.shape, generator=gen, dtype=torch.float64) for w in want]
+    sum((w * c.to(dev)).sum() for w, c in zip(want, cot)).backward()
+    dh, dg, dlam, dh2, dg2, dlam2 = (c.float().to(dev) for c in cot)
+    dtau = None if tau is None else torch.zeros(H, m, device=dev)
+    dk2, dv2, dW2_2, da2, dg_f, dh_f, dlam_f = gn._write2_backward(run, k, v, W2, two, h_k, lam, g32, kk, dh2,
+                                                                   dg2, dlam2, dtau)
+    dk1, dv1, dW1, dW2_1 = gn._write_backward(run, k, v, W1, W2, st[:9], dh + dh_f, dg + dg_f, dlam + dlam_f,
+                                              dtau, da2)
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    for name, got, leaf in zip(("k", "v", "W1", "W2"), (dk1 + dk2, dv1 + dv2, dW1, dW2_1 + dW2_2), leaves):
+        assert rel_err(got, leaf.grad) < TOL, name
+    if tau is not None:
+        assert rel_err(dtau, tl.grad[..., 0]) < TOL

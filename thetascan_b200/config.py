@@ -10,7 +10,7 @@ package executes that backend only (``"auto"`` resolves to it).
 
 Validation restates the reference's rules for the fields this package reads
 and raises ``NotImplementedError`` for configurations the GPU path does not
-cover yet (GN swiglu and two-step Jacobians, EMA decay gates, value anchors,
+cover yet (GN swiglu and depth > 1, EMA decay gates, value anchors,
 feature-space RoPE).
 """
 from __future__ import annotations
@@ -431,8 +431,6 @@ class ThetaScanConfig:
         if self.family == "gn":
             if self.gn.nonlinearity == "swiglu":
                 return "the GN swiglu nonlinearity is not built"
-            if self.gn.jacobian_steps != 1:
-                return "GN jacobian_steps=2 is not built"
             if self.depth != 1:
                 return "GN depth > 1 is not built"
             return None

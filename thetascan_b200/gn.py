@@ -239,7 +239,8 @@ def _hm_wgrad(gy, x):
     return part.view(B, H, S, o, i).sum(dim=(0, 2))
 
 
-def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, fake):
+def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, fake,
+                steps=1):
     """The GN core: ``y`` and the tensors its backward reads (a flat list, in
     the order _gn_backward takes them)."""
     B, H, T, d = q.shape
@@ -249,7 +250,13 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
     las = [None] + [log_alphas[j].float() for j in range(J)]
     stale = [False] + [mode == "stale"] * J
-    a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb = _write_forward(run, k, v, W1, W2, bf16=True)
+    a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb, g32 = _write_forward(run, k, v, W1, W2, bf16=True,
+                                                                           g32=steps == 2)
+    two = None
+    if steps == 2:
+        # the second Jacobian step (engine.py:323-339) and its streams
+        two = _write2_forward(run, k, v, W2, a_k, h_k, kk, lam, g32)
+        g = torch.cat([g, two["g2b"]], dim=-1)   # both g payloads in one stage-1 scan
     # stage 1, shared by all views (engine.py:475-500)
     a_q = _hm(W1, q)
     if read_norm_w1:
@@ -260,6 +267,10 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
         h0 = q.new_empty(0)
         R1, st1 = run.scan_fwd(q, k, g, False, las, stale)
     saved = [a_k, h_k, h_kb, s2, hh, kk, O, RS, lam, lamb, U, g, a_q, h0]
+    if two is not None:
+        saved += [g32] + [two[n] for n in _WRITE2_SAVED]
+        # the two g streams' reads add up (same query and keys)
+        R1 = [r[..., :m] + r[..., m:] for r in R1]
     saved += [x for piece in st1 for x in piece[3:]]
     ys = []
     # stage 2, one query per view (engine.py:500-528)
@@ -268,10 +279,15 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
         run.rows(_lib.TS_GN_FEATURES, [a_q, R1[s]], [hq], flags=int(read_norm_w1), bf16=hqb)
         base = _hm(W2, hq)
         (C,), st2 = run.scan_fwd(hqb, h_kb, lamb, bool(read_norm), [las[s]], [stale[s]])
+        saved += [hq, hqb] + [x for piece in st2 for x in piece[3:]]
+        if two is not None:
+            # the second step's lambda stream against its own keys h2
+            (C2,), st2b = run.scan_fwd(hqb, two["h2b"], two["lam2b"], False, [las[s]], [stale[s]])
+            C = C + C2
+            saved += [x for piece in st2b for x in piece[3:]]
         y = run.new(d)
         run.rows(_lib.TS_GN_OUT, [q, base, C], [y], flags=int(bool(read_norm)))
         ys.append(y)
-        saved += [hq, hqb] + [x for piece in st2 for x in piece[3:]]
     y = ys[0]
     if J and mode == "stale":
         # y - sum_j eta_j (y_stale_j - y_base), y_base the zero-memory read
@@ -295,7 +311,7 @@ def _take(saved, n):
 
 
 def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read_norm, read_norm_w1, mode, eps,
-                 fake):
+                 fake, steps=1):
     """Gradients of the GN core: q, k, v, W1, W2, tau, log_alphas, etas."""
     B, H, T, d = q.shape
     m = W1.shape[1]
@@ -306,17 +322,27 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     las = [None] + [log_alphas[j].float() for j in range(J)]
     stale = [False] + [mode == "stale"] * J
     (a_k, h_k, h_kb, s2, hh, kk, O, RS, lam, lamb, U, g, a_q, h0), rest = _take(saved, 14)
+    two = g32 = None
+    if steps == 2:
+        (g32,), rest = _take(rest, 1)
+        vals, rest = _take(rest, len(_WRITE2_SAVED))
+        two = dict(zip(_WRITE2_SAVED, vals))
     q1 = h0 if read_norm_w1 else q
     k1 = h_kb if read_norm_w1 else k
-    n1 = len(_scan_pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1]))
+    w1 = m * steps   # stage-1 payload: the g stream of each step
+    n1 = len(_scan_pieces(w1, bool(read_norm_w1), J + 1, q1.shape[-1]))
     flat1, rest = _take(rest, 2 * n1)
-    st1 = _pieces(m, bool(read_norm_w1), J + 1, q1.shape[-1], flat1)
+    st1 = _pieces(w1, bool(read_norm_w1), J + 1, q1.shape[-1], flat1)
     views = []
     for s in range(J + 1):
         (hq, hqb), rest = _take(rest, 2)
         n2 = len(_scan_pieces(d, bool(read_norm), 1, m))
         flat2, rest = _take(rest, 2 * n2)
-        views.append((hq, hqb, _pieces(d, bool(read_norm), 1, m, flat2)))
+        st2b = None
+        if steps == 2:
+            flat2b, rest = _take(rest, 2 * len(_scan_pieces(d, False, 1, m)))
+            st2b = _pieces(d, False, 1, m, flat2b)
+        views.append((hq, hqb, _pieces(d, bool(read_norm), 1, m, flat2), st2b))
     dy = dy.float().contiguous()
     # the view combination
     tau_grad = None if tau is None else torch.zeros(H, m, dtype=torch.float32, device=q.device)
@@ -344,8 +370,12 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     dlam = run.new(d, zero=True)
     da_q = run.new(m)
     R1 = [torch.cat([p[3][i] for p in st1], dim=-1) if len(st1) > 1 else st1[0][3][i] for i in range(J + 1)]
+    if steps == 2:
+        R1 = [r[..., :m] + r[..., m:] for r in R1]
+        dh2 = run.new(m, zero=True)
+        dlam2 = run.new(d, zero=True)
     dR1 = [run.new(R1[0].shape[-1]) for _ in range(J + 1)]
-    for s, (hq, hqb, st2) in enumerate(views):
+    for s, (hq, hqb, st2, st2b) in enumerate(views):
         C = st2[0][3][0] if len(st2) == 1 else torch.cat([p[3][0] for p in st2], dim=-1)
         if read_norm:
             dC = run.new(d + 1)
@@ -356,6 +386,13 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         dh_k += dhk_s
         dlam += dlam_s
         dla[s] += dla_s[0]
+        if st2b is not None:
+            dhq2, dh2_s, dlam2_s, dla2_s = run.scan_bwd([dC], hqb, two["h2b"], two["lam2b"], st2b, [las[s]],
+                                                        [stale[s]])
+            dhq = dhq + dhq2
+            dh2 += dh2_s
+            dlam2 += dlam2_s
+            dla[s] += dla2_s[0]
         dhq = dhq + _hm(W2t, dys[s])
         dW2 += _hm_wgrad(dys[s], hq)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, R1[s], dhq], [da_q, dR1[s]],
@@ -366,6 +403,8 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         dW2 += _hm_wgrad(dy_base, hb)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base)], [da_q, None], flags=2, dtau=tau_grad)
     # stage 1
+    if steps == 2:
+        dR1 = [torch.cat([r, r], dim=-1) for r in dR1]
     dq1, dk1, dg, dla1 = run.scan_bwd(dR1, q1, k1, g, st1, las, stale)
     dla += dla1
     dk = None
@@ -377,18 +416,31 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         dk = dk1
     dq += _hm(W1.transpose(1, 2), da_q)
     dW1 = _hm_wgrad(da_q, q)
+    da_extra = None
+    if steps == 2:
+        dg, dg2 = dg[..., :m].contiguous(), dg[..., m:].contiguous()
+        dk2, dv2, dW2_2, da_extra, dg_f, dh_f, dlam_f = _write2_backward(
+            run, k, v, W2, two, h_k, lam, g32, kk, dh2, dg2, dlam2, tau_grad)
+        dg = dg + dg_f
+        dh_k += dh_f
+        dlam += dlam_f
+        dW2 += dW2_2
+        dk = dk2 if dk is None else dk + dk2
     dk_w, dv, dW1_w, dW2_w = _write_backward(run, k, v, W1, W2, (a_k, h_k, s2, hh, kk, O, RS, lam, U),
-                                             dh_k, dg, dlam, tau_grad)
+                                             dh_k, dg, dlam, tau_grad, da_extra)
+    if steps == 2:
+        dv = dv + dv2
     dk = dk_w if dk is None else dk_w + dk
     return dq, dk, dv, dW1 + dW1_w, dW2 + dW2_w, tau_grad, dla[1:], deta
 
 
-def _write_forward(run, k, v, W1, W2, bf16=False):
+def _write_forward(run, k, v, W1, W2, bf16=False, g32=False):
     """The GN write (engine.py:161-340): ``a = W1 k`` and the row streams
     ``h, s2, hh, kk, O, RS, lam, U, g`` (h the keys, g and lam the payloads of
     the two read stages; the rest kept for the backward).  With ``bf16`` the
-    row kernels also write the scans' bf16 operands: g only in bf16, and
-    ``(h_bf16, lam_bf16)`` follow the tuple."""
+    row kernels also write the scans' bf16 operands: g in bf16 (and in f32
+    with ``g32``), and ``(h_bf16, lam_bf16, g_f32 or None)`` follow the
+    tuple."""
     m, d = run.m, run.d
     a_k = _hm(W1, k)
     h_k, s2, hh, kk = run.new(m), run.new(m), run.new(0), run.new(0)
@@ -400,17 +452,74 @@ def _write_forward(run, k, v, W1, W2, bf16=False):
     run.rows(_lib.TS_GN_WRITE_LAM, [v, k, O, RS, hh, kk], [lam], bf16=lamb)
     U = _hm(W2.transpose(1, 2), lam)
     if bf16:
-        g = run.new_bf16(m)
-        run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [None], bf16=g)
-        return a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb
+        g, gf = run.new_bf16(m), (run.new(m) if g32 else None)
+        run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [gf], bf16=g)
+        return a_k, h_k, s2, hh, kk, O, RS, lam, U, g, h_kb, lamb, gf
     g = run.new(m)
     run.rows(_lib.TS_GN_WRITE_G, [a_k, U], [g])
     return a_k, h_k, s2, hh, kk, O, RS, lam, U, g
 
 
-def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau):
+_WRITE2_SAVED = ("a2", "h2", "h2b", "s2b", "hh2", "O2", "RS2", "lam2", "lam2b", "U2", "hd")
+
+
+def _write2_forward(run, k, v, W2, a_k, h_k, kk, lam, g):
+    """The second Jacobian step (``write_iters == 2``, engine.py:323-339):
+    the block re-run at theta0 plus this token's first-step write
+    (engine.py:117-158 with ``delta``): a2 = a + g |k|^2, h2 = sigma(rms(a2) -
+    tau), O2 = W2 h2 + lam (h . h2), then the same damped solve for lam2 and
+    g2 = sigma'(p2) (W2^T lam2) / rms(a2).  The read adds the (k, g2) and
+    (h2, lam2) streams to the first step's."""
+    m, d = run.m, run.d
+    a2 = a_k + g * kk.unsqueeze(-1)
+    h2, s2b, hh2, kk2 = run.new(m), run.new(m), run.new(0), run.new(0)
+    h2b = run.new_bf16(m)
+    run.rows(_lib.TS_GN_WRITE_PRE, [a2, k], [h2, s2b, hh2, kk2], bf16=h2b)
+    hd = (h_k * h2).sum(-1, keepdim=True)
+    O2 = _hm(W2, h2) + lam * hd
+    RS2 = _hm(W2 * W2, s2b)
+    lam2, lam2b = run.new(d), run.new_bf16(d)
+    run.rows(_lib.TS_GN_WRITE_LAM, [v, k, O2, RS2, hh2, kk], [lam2], bf16=lam2b)
+    U2 = _hm(W2.transpose(1, 2), lam2)
+    g2b = run.new_bf16(m)
+    run.rows(_lib.TS_GN_WRITE_G, [a2, U2], [None], bf16=g2b)
+    return dict(a2=a2, h2=h2, h2b=h2b, s2b=s2b, hh2=hh2, O2=O2, RS2=RS2, lam2=lam2, lam2b=lam2b, U2=U2, hd=hd,
+                g2b=g2b)
+
+
+def _write2_backward(run, k, v, W2, two, h_k, lam, g, kk, dh2, dg2, dlam2, dtau):
+    """Backward of the second step from the gradients of its streams (h2,
+    g2, lam2): returns (d k, d v, d W2, d a2) of its own terms and the
+    gradients it hands to the first step's g, h and lam."""
+    m, d = run.m, run.d
+    W2t = W2.transpose(1, 2)
+    du2 = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_G_BWD, [dg2, two["a2"]], [du2])
+    dlam2W = _hm(W2, du2)
+    dr2, drowsq2, dk2, dhh2 = run.new(d), run.new(d), run.new(d), run.new(0)
+    run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam2, dlam2W, v, k, two["O2"], two["RS2"], two["hh2"], kk],
+             [dr2, drowsq2, dk2, dhh2])
+    h2 = two["h2"]
+    dW2 = _hm_wgrad(two["lam2"], du2) - _hm_wgrad(dr2, h2) + 2.0 * W2 * _hm_wgrad(drowsq2, two["s2b"])
+    # O2 = W2 h2 + lam (h . h2), and r2 = v - k - O2
+    dhd = -(dr2 * lam).sum(-1, keepdim=True)
+    dlam_first = -dr2 * two["hd"]
+    dh_first = dhd * h2
+    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq2)
+    dhO2 = _hm(W2t, dr2)
+    da2 = run.new(m)
+    run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh2 + dhd * h_k, dhO2, ds2, dhh2, dg2, two["U2"], two["a2"]], [da2],
+             dtau=dtau)
+    # a2 = a + g |k|^2
+    dg_first = da2 * kk.unsqueeze(-1)
+    dk2 = dk2 + 2.0 * (da2 * g).sum(-1, keepdim=True) * k
+    return dk2, dr2, dW2, da2, dg_first, dh_first, dlam_first
+
+
+def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau, da_extra=None):
     """Gradients of k, v, W1, W2 (and tau into ``dtau``) of the write from
-    those of its outputs h, g, lam."""
+    those of its outputs h, g, lam (and ``da_extra``, a gradient of a = W1 k
+    from elsewhere)."""
     a_k, h_k, s2, hh, kk, O, RS, lam, U = streams
     m, d = run.m, run.d
     W2t = W2.transpose(1, 2)
@@ -424,6 +533,8 @@ def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau):
     dhO = _hm(W2t, dv)
     da_k = run.new(m)
     run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh, dhO, ds2, dhh, dg, U, a_k], [da_k], dtau=dtau)
+    if da_extra is not None:
+        da_k = da_k + da_extra
     dk = dk_w + _hm(W1.transpose(1, 2), da_k)
     return dk, dv, _hm_wgrad(da_k, k), dW2
 
@@ -442,12 +553,14 @@ def _pieces(width, unit, n_retentions, dk, flat):
 
 
 def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_norm_w1=True, log_alphas=None,
-            etas=None, mode="fast", eps=1e-6):
+            etas=None, mode="fast", eps=1e-6, steps=1):
     """GN mixer core ``[B,H,T,d]`` f32 from ``q, k, v`` after RoPE / L2 norm.
 
     ``W1 [H,m,d]``, ``W2 [H,d,m]`` effective weights, ``tau [H,m,1]`` the learned
     threshold of ``relu2_threshold`` (or None), ``log_alphas``/``etas``
-    ``[J,H]`` for a bank.  Runs as the ``thetascan_b200::gn_core`` custom op
+    ``[J,H]`` for a bank, ``steps`` the Jacobian steps of the write (2: the
+    reference's ``write_iters == 2``, unnormalised reads only).  Runs as the
+    ``thetascan_b200::gn_core`` custom op
     (the row kernels of ``ts_b200_gn_rows``, cuBLAS for the per-head maps,
     the multi-view scan kernels for the reads)."""
     for x in (q, k, v):
@@ -455,11 +568,15 @@ def gn_core(q, k, v, W1, W2, tau=None, *, nonlin="relu2", read_norm=True, read_n
             raise RuntimeError("b200 backend requires CUDA tensors")
     if nonlin not in _NONLIN:
         raise NotImplementedError(f"b200 GN: nonlinearity {nonlin!r} is not built")
+    if steps not in (1, 2):
+        raise NotImplementedError(f"b200 GN: {steps} Jacobian steps")
+    if steps == 2 and (read_norm or read_norm_w1):
+        raise ValueError("GN feature-mass normalization requires jacobian_steps=1")
     J = 0 if log_alphas is None else log_alphas.shape[0]
     if J:
         _views(mode, J)
     from . import ops  # noqa: F401  (registers the operators)
     y, _ = torch.ops.thetascan_b200.gn_core_fwd(
         q.float().contiguous(), k.float().contiguous(), v.float().contiguous(), W1, W2, tau,
-        log_alphas, etas, nonlin, bool(read_norm), bool(read_norm_w1), mode if J else "sum", float(eps))
+        log_alphas, etas, nonlin, bool(read_norm), bool(read_norm_w1), mode if J else "sum", float(eps), int(steps))
     return y

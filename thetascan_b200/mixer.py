@@ -300,7 +300,7 @@ class ThetaScanCore(nn.Module):
                     read_norm=gn.read_normalization != "none",
                     read_norm_w1=gn.read_normalization == "both_feature_mass",
                     log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum",
-                    eps=eps)
+                    eps=eps, steps=gn.jacobian_steps)
         y = y.transpose(1, 2)
         if self.ogate is not None:
             g = tf32_linear(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)

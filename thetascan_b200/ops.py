@@ -468,31 +468,33 @@ torch.library.register_autograd(f"{LIB}::scan_views_stream_fwd", _stream_backwar
 @torch.library.custom_op(f"{LIB}::gn_core_fwd", mutates_args=())
 def gn_core_fwd(q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor, tau: Optional[Tensor],
                 log_alphas: Optional[Tensor], etas: Optional[Tensor], nonlin: str, read_norm: bool,
-                read_norm_w1: bool, mode: str, eps: float) -> tuple[Tensor, list[Tensor]]:
+                read_norm_w1: bool, mode: str, eps: float, steps: int) -> tuple[Tensor, list[Tensor]]:
     """GN core ``y [B,H,T,d]`` f32 from f32 post-RoPE/L2 ``q, k, v`` plus the
     intermediates of its backward (write streams, stage reads, scan states)."""
     from .gn import _gn_forward
     _require_cuda(q, k, v, W1, W2, tau, log_alphas, etas)
-    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, False)
+    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, False,
+                       steps)
 
 
 @gn_core_fwd.register_fake
-def _(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps):
+def _(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, steps):
     from .gn import _gn_forward
-    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, True)
+    return _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, True,
+                       steps)
 
 
 @torch.library.custom_op(f"{LIB}::gn_core_bwd", mutates_args=())
 def gn_core_bwd(dy: Tensor, q: Tensor, k: Tensor, v: Tensor, W1: Tensor, W2: Tensor, tau: Optional[Tensor],
                 log_alphas: Optional[Tensor], etas: Optional[Tensor], saved: list[Tensor], nonlin: str,
-                read_norm: bool, read_norm_w1: bool, mode: str,
-                eps: float) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+                read_norm: bool, read_norm_w1: bool, mode: str, eps: float,
+                steps: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
     """Gradients of q, k, v, W1, W2 (f32) and of tau ``[H,m]``, the bank's
     log-retentions and etas ``[J,H]`` (empty where the input is absent)."""
     from .gn import _gn_backward
     _require_cuda(dy, q, k, v, W1, W2, tau, log_alphas, etas)
     return _gn_outputs(_gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, list(saved), nonlin, read_norm,
-                                    read_norm_w1, mode, eps, False), q)
+                                    read_norm_w1, mode, eps, False, steps), q)
 
 
 def _gn_outputs(grads, q):
@@ -500,16 +502,16 @@ def _gn_outputs(grads, q):
 
 
 @gn_core_bwd.register_fake
-def _(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read_norm, read_norm_w1, mode, eps):
+def _(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read_norm, read_norm_w1, mode, eps, steps):
     from .gn import _gn_backward
     return _gn_outputs(_gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, list(saved), nonlin, read_norm,
-                                    read_norm_w1, mode, eps, True), q)
+                                    read_norm_w1, mode, eps, True, steps), q)
 
 
 def _gn_setup(ctx, inputs, output):
-    q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps = inputs
+    q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_norm_w1, mode, eps, steps = inputs
     y, saved = output
-    ctx.args = (nonlin, read_norm, read_norm_w1, mode, eps)
+    ctx.args = (nonlin, read_norm, read_norm_w1, mode, eps, steps)
     ctx.present = (tau is not None, log_alphas is not None, etas is not None)
     ctx.meta = [(t.dtype, t.shape) if t is not None else None for t in (q, k, v, W1, W2, tau, log_alphas, etas)]
     ctx.n_saved = len(saved)
@@ -532,7 +534,7 @@ def _gn_backward_fn(ctx, dy, dsaved):
     out = []
     for g_, meta in zip(grads, ctx.meta):
         out.append(None if meta is None else g_.to(meta[0]).reshape(meta[1]))
-    return (*out, None, None, None, None, None)
+    return (*out, None, None, None, None, None, None)
 
 
 torch.library.register_autograd(f"{LIB}::gn_core_fwd", _gn_backward_fn, setup_context=_gn_setup)
