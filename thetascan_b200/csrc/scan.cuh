@@ -39,6 +39,9 @@ struct ScanParams {
   int DvP;        // Dv rounded up to 16
   int NT, R;      // R: all slots; slots 0..RU-1 are the caller's, RU..R-1 auxiliary
   int RU;
+  // chain kernels: slots per CTA (blockIdx.y selects the group of slots
+  // [y * slot_group, ...)); 0 = all slots in one CTA
+  int slot_group;
   const __nv_bfloat16* q;
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;

@@ -26,6 +26,9 @@
 // reads, in the slot's operand buffer.  The slots are interleaved: slot r's
 // dSloc product runs while the epilogue works on slot r + 1.
 //
+// Where the (batch, head) CTAs would leave SMs idle, the slots are split
+// over several CTAs of the same (batch, head), as in the forward chain.
+//
 // Warp roles (160 threads): warp 0 lane 0 issues the copies and the MMAs;
 // warps 1-4 (one TMEM lane quadrant each) form operands and read G.  Every
 // wait is bounded; a wait that gives up records a device error, and the CTA
@@ -137,11 +140,14 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
   const int b = blockIdx.x / p.H, h = blockIdx.x % p.H;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int dvv = p.Dv - p.v_unit;
-  const BwdChainLayout L = bwd_chain_layout(p.DkM, p.Dv, p.v_unit, p.R);
+  // this CTA's slots: r0 .. r0 + nr - 1 (local index s = r - r0)
+  const int grp = p.slot_group > 0 ? p.slot_group : p.R;
+  const int r0 = blockIdx.y * grp, nr = min(grp, p.R - r0);
+  const BwdChainLayout L = bwd_chain_layout(p.DkM, p.Dv, p.v_unit, grp);
   const int mblocks = p.DkM / kTile;
   const int region = mblocks * p.DvP;                  // TMEM columns of one slot's G
-  const uint32_t t_x = static_cast<uint32_t>(p.R * region);   // scratch block (one M block) after the G blocks
-  const uint32_t ncols = bwd_chain_tmem_cols(p.R * region + p.DvP);
+  const uint32_t t_x = static_cast<uint32_t>(grp * region);   // scratch block (one M block) after the G blocks
+  const uint32_t ncols = bwd_chain_tmem_cols(grp * region + p.DvP);
   const int NT = p.NT;
   const int last_dla = g.dfinal != nullptr ? NT : NT - 1;   // tiles whose leaving state carries gradient
   auto local = [&](int n) { return n >= 1 || g.all_tiles; };
@@ -181,10 +187,10 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
       auto issue_raw = [&](int k) {
         const int n = NT - 1 - k;
         const uint32_t bytes = static_cast<uint32_t>(tile_len(p, n) * p.Dv * 2);
-        mbar_expect_tx(&sh.load_raw, bytes * p.R);
-        for (int r = 0; r < p.R; ++r) {
-          const __nv_bfloat16* src = g.dout[r] + ((static_cast<size_t>(b) * p.H + h) * p.T + n * kTile) * p.Dv;
-          bulk_load(base + L.off_raw + r * L.raw_bytes, src, bytes, &sh.load_raw);
+        mbar_expect_tx(&sh.load_raw, bytes * nr);
+        for (int s = 0; s < nr; ++s) {
+          const __nv_bfloat16* src = g.dout[r0 + s] + ((static_cast<size_t>(b) * p.H + h) * p.T + n * kTile) * p.Dv;
+          bulk_load(base + L.off_raw + s * L.raw_bytes, src, bytes, &sh.load_raw);
         }
       };
       const uint32_t id_v = idesc_bf16(kTile, 64 * L.vboxes, true, true);
@@ -219,8 +225,9 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
         const uint32_t qaddr = base + (k & 1) * L.q_bytes;
         ok = mbar_wait(&sh.load_q[k & 1], (k >> 1) & 1, kErrCopyTimeout);   // the tile's q landed
         if (!ok) break;
-        for (int r = 0; r < p.R && ok; ++r) {
-          const uint32_t op = base + L.off_op + r * L.op_bytes;
+        for (int s = 0; s < nr && ok; ++s) {
+          const int r = r0 + s;
+          const uint32_t op = base + L.off_op + s * L.op_bytes;
           if (want(r) && local(n)) {
             for (int mb = 0; mb < mblocks && ok; ++mb) {
               ok = mbar_wait(&sh.epi_x, nex & 1, kErrMmaTimeout);
@@ -233,17 +240,17 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
             }
             if (!ok || *(volatile int*)&sh.abort) break;
           }
-          ok = mbar_wait(&sh.epi_g[r], k & 1, kErrMmaTimeout);
+          ok = mbar_wait(&sh.epi_g[s], k & 1, kErrMmaTimeout);
           if (!ok || *(volatile int*)&sh.abort) break;
           tc_fence_after();
           if (local(n)) {
             for (int mb = 0; mb < mblocks; ++mb)
-              product(qaddr, tmem + static_cast<uint32_t>(r * region + mb * p.DvP), mb, op, true);
-            mma_commit(&sh.mma_g[r]);
-            ++ng[r];
+              product(qaddr, tmem + static_cast<uint32_t>(s * region + mb * p.DvP), mb, op, true);
+            mma_commit(&sh.mma_g[s]);
+            ++ng[s];
           }
           // every slot's raw rows are consumed once the last slot handed over
-          if (r == p.R - 1 && k + 1 < NT) {
+          if (s == nr - 1 && k + 1 < NT) {
             issue_raw(k + 1);
             ++raws;
           }
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
         if (!ok || *(volatile int*)&sh.abort) break;
         if (k + 2 < NT) {
           // this q stage is free once the tile's last product has read it
-          ok = mbar_wait(&sh.mma_g[p.R - 1], (ng[p.R - 1] - 1) & 1, kErrMmaTimeout);
+          ok = mbar_wait(&sh.mma_g[nr - 1], (ng[nr - 1] - 1) & 1, kErrMmaTimeout);
           if (!ok) break;
           issue_q(k + 2);
           last_q[k & 1] = k + 2;
@@ -262,8 +269,8 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
       for (int st = 0; st < 2; ++st)
         if (last_q[st] >= 0) mbar_wait(&sh.load_q[st], (last_q[st] >> 1) & 1, kErrCopyTimeout);
       mbar_wait(&sh.load_raw, (raws - 1) & 1, kErrCopyTimeout);
-      for (int r = 0; r < p.R; ++r)
-        if (ng[r] > 0) mbar_wait(&sh.mma_g[r], (ng[r] - 1) & 1, kErrMmaTimeout);
+      for (int s = 0; s < nr; ++s)
+        if (ng[s] > 0) mbar_wait(&sh.mma_g[s], (ng[s] - 1) & 1, kErrMmaTimeout);
       if (nx > 0) mbar_wait(&sh.mma_x, (nx - 1) & 1, kErrMmaTimeout);
     }
   } else {
@@ -274,8 +281,9 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
     int nx = 0;
     float acc[TS_MAX_RETENTIONS] = {0.f, 0.f, 0.f, 0.f};
     // G(NT-1): the gradient of the final state, or zero.
-    for (int r = 0; r < p.R; ++r)
+    for (int s = 0; s < nr; ++s)
       for (int mb = 0; mb < mblocks; ++mb) {
+        const int r = r0 + s;
         const int f = mb * kTile + lrow;
         for (int c = 0; c < p.DvP; c += 16) {
           float v[16];
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           for (int e = 0; e < 16; ++e)
             v[e] = (g.dfinal != nullptr && f < p.Dk && c + e < p.Dv)
                        ? __ldg(g.dfinal + boundary_index(p, b, h, r, f, c + e)) : 0.f;
-          tmem_st16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
+          tmem_st16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
         }
       }
     for (int k = 0; k < NT && ok; ++k) {
@@ -291,15 +299,16 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
       const int len = tile_len(p, n);
       ok = mbar_wait(&sh.load_raw, k & 1, kErrCopyTimeout);
       if (!ok) break;
-      for (int r = 0; r < p.R && ok; ++r) {
+      for (int s = 0; s < nr && ok; ++s) {
+        const int r = r0 + s;
         const bool decayed = p.la[r] != nullptr;
         const float la = head_la(p, r, h);
         const float c_row = decayed ? __expf(la * static_cast<float>(lrow + 1)) : 1.f;   // carry c(i), row i = lrow
-        const uint32_t raw_row = base + L.off_raw + r * L.raw_bytes + lrow * p.Dv * 2;
-        const uint32_t op = base + L.off_op + r * L.op_bytes;
+        const uint32_t raw_row = base + L.off_raw + s * L.raw_bytes + lrow * p.Dv * 2;
+        const uint32_t op = base + L.off_op + s * L.op_bytes;
         // G(n) of this slot is complete (and its operand buffer free) once the
         // previous tile's dSloc product of this slot is
-        if (k > 0) ok = mbar_wait(&sh.mma_g[r], (k - 1) & 1, kErrMmaTimeout);
+        if (k > 0) ok = mbar_wait(&sh.mma_g[s], (k - 1) & 1, kErrMmaTimeout);
         if (!ok || *(volatile int*)&sh.abort) {
           ok = false;
           break;
@@ -344,7 +353,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           for (int kk = 0; kk < kMaxDvP / 16; ++kk) {
             const int c = 16 * kk;
             if (c >= p.DvP) break;
-            const uint32_t ta = tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c);
+            const uint32_t ta = tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c);
             float v[16];
             tmem_ld16(ta, v);
             if (carry) {
@@ -390,22 +399,23 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row, 1.f);
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(&sh.epi_g[r]);
+        mbar_arrive(&sh.epi_g[s]);
       }
     }
     if (!ok) *(volatile int*)&sh.abort = 1;
     // G(-1): the gradient of the initial state, after tile 0's dSloc products.
     if (ok && g.dinit != nullptr) {
       if (local(0))
-        for (int r = 0; r < p.R && ok; ++r) ok = mbar_wait(&sh.mma_g[r], (NT - 1) & 1, kErrMmaTimeout);
+        for (int s = 0; s < nr && ok; ++s) ok = mbar_wait(&sh.mma_g[s], (NT - 1) & 1, kErrMmaTimeout);
       tc_fence_after();
       if (ok) {
-        for (int r = 0; r < p.R; ++r)
+        for (int s = 0; s < nr; ++s)
           for (int mb = 0; mb < mblocks; ++mb) {
+            const int r = r0 + s;
             const int f = mb * kTile + lrow;
             for (int c = 0; c < p.DvP; c += 16) {
               float v[16];
-              tmem_ld16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
+              tmem_ld16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
               if (f < p.Dk) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           }
       }
     }
-    for (int r = 0; r < p.R; ++r) {
+    for (int r = r0; r < r0 + nr; ++r) {
       if (!want(r)) continue;
       float v = acc[r];
 #pragma unroll
@@ -431,17 +441,22 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
 // ------------------------------------------------------------------ host launch
 
 size_t scan_bwd_chain_smem(const ScanParams& p) {
-  return static_cast<size_t>(bwd_chain_layout(p.DkM, p.Dv, p.v_unit, p.R).total) + 1024;
+  const int grp = p.slot_group > 0 ? p.slot_group : p.R;
+  return static_cast<size_t>(bwd_chain_layout(p.DkM, p.Dv, p.v_unit, grp).total) + 1024;
 }
+
+int chain_slot_group(const ScanParams& p);   // scan_chain.cu
 
 // Runs the reverse chain where it applies; returns 1 if it ran, 0 if the
 // caller should run the per-tile kernels and the HBM reverse prefix, or a
 // negative TS_ERR_* code.
-int launch_scan_bwd_chain(const ScanParams& p, const ScanGradParams& g, cudaStream_t s) {
+int launch_scan_bwd_chain(const ScanParams& pin, const ScanGradParams& g, cudaStream_t s) {
+  ScanParams p = pin;
   const int dvv = p.Dv - p.v_unit;
   if (p.any_stale || p.R != p.RU || g.zero_start_final || !g.store) return 0;
   if (dvv % 64 != 0 || p.DvP != dvv + (p.v_unit ? 16 : 0) || p.DvP > kTile || p.Dv % 2 != 0) return 0;
-  if (p.R * (p.DkM / kTile) * p.DvP + p.DvP > 512) return 0;
+  p.slot_group = chain_slot_group(p);
+  if (p.slot_group * (p.DkM / kTile) * p.DvP + p.DvP > 512) return 0;
   // raw dout rows by untiled bulk copies: 16-byte aligned starts and lengths
   const long long len_last = p.T - static_cast<long long>(p.NT - 1) * kTile;
   if ((static_cast<long long>(p.T) * p.Dv * 2) % 16 != 0 || (len_last * p.Dv * 2) % 16 != 0) return 0;
@@ -456,7 +471,7 @@ int launch_scan_bwd_chain(const ScanParams& p, const ScanGradParams& g, cudaStre
   const uint32_t box[4] = {64u, static_cast<uint32_t>(kTile), 1u, 1u};
   if (!make_tmap_bf16_sw128(&mq, p.q, 4, dims, strides, box)) return 0;
   cudaFuncSetAttribute(scan_bwd_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  scan_bwd_chain_kernel<<<p.B * p.H, kBwdChainThreads, smem, s>>>(p, g, mq);
+  scan_bwd_chain_kernel<<<dim3(p.B * p.H, ceil_div(p.R, p.slot_group)), kBwdChainThreads, smem, s>>>(p, g, mq);
   if (int e = check_launch("scan_bwd_chain_kernel")) return -e;
   return 1;
 }

@@ -17,7 +17,9 @@
 //
 // The slots are interleaved: slot r's update product of tile n runs while the
 // epilogue writes out slot r + 1, and the key and payload tiles run through a
-// two-stage load ring, so loads, products and the write-out overlap.  Warp
+// two-stage load ring, so loads, products and the write-out overlap.  Where
+// the (batch, head) CTAs would leave SMs idle, the slots are split over
+// several CTAs of the same (batch, head) (chain_slot_group).  Warp
 // roles (160 threads):
 //   warp 0, lane 0  TMA loads (128-byte-swizzled boxes, tensor maps of this
 //                   GPU's own memory, no multicast) and the tcgen05 MMA issue;
@@ -80,10 +82,13 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.H, h = blockIdx.x % p.H;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const ChainLayout L = chain_layout(p.DkM, (p.Dv - p.v_unit) / 64, p.v_unit, p.R);
+  // this CTA's slots: r0 .. r0 + nr - 1 (local index s = r - r0)
+  const int grp = p.slot_group > 0 ? p.slot_group : p.R;
+  const int r0 = blockIdx.y * grp, nr = min(grp, p.R - r0);
+  const ChainLayout L = chain_layout(p.DkM, (p.Dv - p.v_unit) / 64, p.v_unit, grp);
   const int mblocks = p.DkM / kTile;
   const int region = mblocks * p.DvP;          // TMEM columns of one slot's state
-  const uint32_t ncols = chain_tmem_cols(p.R * region);
+  const uint32_t ncols = chain_tmem_cols(grp * region);
   const int NT = p.NT;
 
   if (threadIdx.x == 0) {
@@ -126,13 +131,13 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       const uint32_t id_u = idesc_bf16(kTile, 16, true, true);
       for (int n = 0; n < NT && ok; ++n) {
         const uint32_t kaddr = base + (n & 1) * L.stage_bytes;
-        for (int r = 0; r < p.R && ok; ++r) {
-          ok = mbar_wait(&sh.epi[r], n & 1, kErrMmaTimeout);
+        for (int s = 0; s < nr && ok; ++s) {
+          ok = mbar_wait(&sh.epi[s], n & 1, kErrMmaTimeout);
           if (!ok || *(volatile int*)&sh.abort) break;
           tc_fence_after();
-          const uint32_t wv = base + L.off_wv + r * L.wv_bytes;
+          const uint32_t wv = base + L.off_wv + s * L.wv_bytes;
           for (int mb = 0; mb < mblocks; ++mb) {
-            const uint32_t d = tmem + static_cast<uint32_t>(r * region + mb * p.DvP);
+            const uint32_t d = tmem + static_cast<uint32_t>(s * region + mb * p.DvP);
 #pragma unroll 1
             for (int ks = 0; ks < kTile / 16; ++ks) {
               // A = k^T (features x tokens): MN-major, 64-feature boxes LBO apart
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
               }
             }
           }
-          mma_commit(&sh.mma[r]);
+          mma_commit(&sh.mma[s]);
           ++commits;
         }
         if (!ok || *(volatile int*)&sh.abort) break;
@@ -153,7 +158,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           // stage n & 1 is free once the tile's last product has read the key
           // tile (commits complete in issue order; the epilogue consumed the
           // payload tile before it handed over)
-          ok = mbar_wait(&sh.mma[p.R - 1], n & 1, kErrMmaTimeout);
+          ok = mbar_wait(&sh.mma[nr - 1], n & 1, kErrMmaTimeout);
           if (!ok) break;
           issue_load(n + 2);
           last_load[n & 1] = n + 2;
@@ -165,8 +170,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       for (int st = 0; st < 2; ++st)
         if (last_load[st] >= 0) mbar_wait(&sh.full[st], (last_load[st] >> 1) & 1, kErrCopyTimeout);
       if (commits > 0) {
-        const int tiles_done = (commits + p.R - 1) / p.R;   // the last tile reached, partly or fully
-        const int last_r = (commits - 1) % p.R;
+        const int tiles_done = (commits + nr - 1) / nr;   // the last tile reached, partly or fully
+        const int last_r = (commits - 1) % nr;
         mbar_wait(&sh.mma[last_r], (tiles_done - 1) & 1, kErrMmaTimeout);
       }
     }
@@ -176,8 +181,9 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     const int lrow = 32 * quad + lane;   // TMEM lane = token row of the payload tile = feature row of a state block
     bool ok = true;
     // S_in(0): the initial state, or zero.
-    for (int r = 0; r < p.R; ++r)
+    for (int s = 0; s < nr; ++s)
       for (int mb = 0; mb < mblocks; ++mb) {
+        const int r = r0 + s;
         const int f = mb * kTile + lrow;
         for (int c = 0; c < p.DvP; c += 16) {
           float v[16];
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           for (int e = 0; e < 16; ++e)
             v[e] = (p.init != nullptr && f < p.Dk && c + e < p.Dv)
                        ? __ldg(p.init + boundary_index(p, b, h, r, f, c + e)) : 0.f;
-          tmem_st16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
+          tmem_st16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
         }
       }
     for (int n = 0; n < NT && ok; ++n) {
@@ -193,12 +199,13 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       ok = mbar_wait(&sh.full[n & 1], (n >> 1) & 1, kErrCopyTimeout);
       if (!ok) break;
       const uint32_t vrow = base + (n & 1) * L.stage_bytes + L.k_bytes + lrow * kSwRow;
-      for (int r = 0; r < p.R && ok; ++r) {
+      for (int s = 0; s < nr && ok; ++s) {
+        const int r = r0 + s;
         const bool decayed = p.la[r] != nullptr;
         const float la = head_la(p, r, h);
         // S_in(n) of this slot is complete (and its payload buffer free) once
         // the previous tile's product of this slot is
-        if (n > 0) ok = mbar_wait(&sh.mma[r], (n - 1) & 1, kErrMmaTimeout);
+        if (n > 0) ok = mbar_wait(&sh.mma[s], (n - 1) & 1, kErrMmaTimeout);
         if (!ok || *(volatile int*)&sh.abort) {
           ok = false;
           break;
@@ -210,7 +217,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         // starting chunk (row % 8), so the 8 lanes of a shared-memory phase
         // touch 8 different bank groups.
         const float u = slot_key_weight(p, r, la, len, lrow);
-        const uint32_t wv = base + L.off_wv + r * L.wv_bytes;
+        const uint32_t wv = base + L.off_wv + s * L.wv_bytes;
         for (int i = 0; i < L.vboxes; ++i) {
           uint4 raw[8];
 #pragma unroll
@@ -242,7 +249,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           const int f = mb * kTile + lrow;
           const int f0 = f & ~7;
           for (int c = 0; c < p.DvP; c += 16) {
-            const uint32_t ta = tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c);
+            const uint32_t ta = tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c);
             float v[16];
             tmem_ld16(ta, v);
             if (p.store) {
@@ -269,21 +276,22 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&sh.epi[r]);
+        mbar_arrive(&sh.epi[s]);
       }
     }
     if (!ok) *(volatile int*)&sh.abort = 1;
     // The final state, after the last tile's updates.
     if (ok && p.final_state != nullptr) {
-      for (int r = 0; r < p.R && ok; ++r) ok = mbar_wait(&sh.mma[r], (NT - 1) & 1, kErrMmaTimeout);
+      for (int s = 0; s < nr && ok; ++s) ok = mbar_wait(&sh.mma[s], (NT - 1) & 1, kErrMmaTimeout);
       tc_fence_after();
       if (ok) {
-        for (int r = 0; r < p.R; ++r)
+        for (int s = 0; s < nr; ++s)
           for (int mb = 0; mb < mblocks; ++mb) {
+            const int r = r0 + s;
             const int f = mb * kTile + lrow;
             for (int c = 0; c < p.DvP; c += 16) {
               float v[16];
-              tmem_ld16(tmem_addr(tmem, 32 * quad, r * region + mb * p.DvP + c), v);
+              tmem_ld16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
               if (f < p.Dk) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
@@ -302,17 +310,31 @@ __global__ void __launch_bounds__(kChainThreads, 1)
 // ------------------------------------------------------------------ host launch
 
 size_t scan_chain_smem(const ScanParams& p) {
-  const ChainLayout L = chain_layout(p.DkM, (p.Dv - p.v_unit) / 64, p.v_unit, p.R);
+  const ChainLayout L = chain_layout(p.DkM, (p.Dv - p.v_unit) / 64, p.v_unit, p.slot_group > 0 ? p.slot_group : p.R);
   return static_cast<size_t>(L.total) + 1024;
+}
+
+// Slots per chain CTA.  The chains are sequential over tiles, so a CTA's time
+// is its slots' per-tile work: where the (batch, head) CTAs leave SMs idle,
+// the slots are split into groups, one CTA each, as long as the whole grid
+// still runs in one wave.
+int chain_slot_group(const ScanParams& p) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int units = max(1, p.B * p.H);
+  const int groups = max(1, min(p.R, sms / units));
+  return ceil_div(p.R, groups);
 }
 
 // The chain runs where it applies (see the file comment) and the tensor maps
 // of k and v can be expressed; returns 1 if it ran, 0 if the caller should
 // run the tile-parallel kernels, or a TS_ERR_* code.
-int launch_scan_chain(const ScanParams& p, cudaStream_t s) {
+int launch_scan_chain(const ScanParams& pin, cudaStream_t s) {
+  ScanParams p = pin;
   const int dvv = p.Dv - p.v_unit;
   if (p.any_stale || dvv % 64 != 0 || p.DvP != dvv + (p.v_unit ? 16 : 0)) return 0;
-  if (p.R * (p.DkM / kTile) * p.DvP > 512) return 0;
+  p.slot_group = chain_slot_group(p);
+  if (p.slot_group * (p.DkM / kTile) * p.DvP > 512) return 0;
   const size_t smem = scan_chain_smem(p);
   if (smem > 232448) return 0;
   CUtensorMap mk, mv;
@@ -326,7 +348,7 @@ int launch_scan_chain(const ScanParams& p, cudaStream_t s) {
   if (!make_tmap_bf16_sw128(&mk, p.k, 4, dims_k, strides_k, box)) return 0;
   if (!make_tmap_bf16_sw128(&mv, p.v, 4, dims_v, strides_v, box)) return 0;
   cudaFuncSetAttribute(scan_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  scan_chain_kernel<<<p.B * p.H, kChainThreads, smem, s>>>(p, mk, mv);
+  scan_chain_kernel<<<dim3(p.B * p.H, ceil_div(p.R, p.slot_group)), kChainThreads, smem, s>>>(p, mk, mv);
   if (int e = check_launch("scan_chain_kernel")) return -e;
   return 1;
 }
