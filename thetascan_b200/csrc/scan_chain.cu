@@ -20,12 +20,13 @@
 // two-stage load ring, so loads, products and the write-out overlap.  Where
 // the (batch, head) CTAs would leave SMs idle, the slots are split over
 // several CTAs of the same (batch, head) (chain_slot_group).  Warp
-// roles (160 threads):
+// roles (288 threads):
 //   warp 0, lane 0  TMA loads (128-byte-swizzled boxes, tensor maps of this
 //                   GPU's own memory, no multicast) and the tcgen05 MMA issue;
-//   warps 1-4       epilogue: one TMEM lane quadrant each (warp w reads lanes
-//                   32 (w % 4) ..): each slot's weighted payload tile, the
-//                   state write-out and the closing rescale.
+//   warps 1-8       epilogue, two warps per TMEM lane quadrant (warp w reads
+//                   lanes 32 (w % 4) ..), splitting each row's chunks: each
+//                   slot's weighted payload tile, the state write-out and the
+//                   closing rescale.
 // Every wait is bounded; a wait that gives up records a device error and the
 // CTA drains its own copies and MMAs in flight before it frees TMEM and exits.
 #include "capi_internal.h"
@@ -36,7 +37,10 @@ namespace ts {
 
 namespace {
 
-constexpr int kChainThreads = 160;
+// warp 0: loads and MMAs; warps 1-8: the epilogue, two warps per TMEM lane
+// quadrant, each taking every other 16-column chunk of a row
+constexpr int kChainEpiWarps = 8;
+constexpr int kChainThreads = 32 * (1 + kChainEpiWarps);
 
 struct ChainLayout {
   int kboxes, vboxes;       // 64-column boxes of a key tile (DkM / 64) and a payload tile
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     mbar_init(&sh.full[0], 1);
     mbar_init(&sh.full[1], 1);
     for (int r = 0; r < TS_MAX_RETENTIONS; ++r) {
-      mbar_init(&sh.epi[r], 4 * 32);
+      mbar_init(&sh.epi[r], kChainEpiWarps * 32);
       mbar_init(&sh.mma[r], 1);
     }
     sh.abort = 0;
@@ -178,14 +182,16 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   } else {
     // -------------------------------------------------------------------- epilogue
     const int quad = warp & 3;
+    const int half = (warp - 1) >> 2;    // which of the two warps of this lane quadrant
     const int lrow = 32 * quad + lane;   // TMEM lane = token row of the payload tile = feature row of a state block
+    const int nchunk = p.DvP / 16;       // 16-column chunks of a state block row
     bool ok = true;
     // S_in(0): the initial state, or zero.
     for (int s = 0; s < nr; ++s)
       for (int mb = 0; mb < mblocks; ++mb) {
         const int r = r0 + s;
         const int f = mb * kTile + lrow;
-        for (int c = 0; c < p.DvP; c += 16) {
+        for (int c = 16 * half; c < p.DvP; c += 32) {
           float v[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
@@ -219,19 +225,20 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         const float u = slot_key_weight(p, r, la, len, lrow);
         const uint32_t wv = base + L.off_wv + s * L.wv_bytes;
         for (int i = 0; i < L.vboxes; ++i) {
-          uint4 raw[8];
+          // this warp's four 16-byte chunks of the row (half 0: 0-3, half 1: 4-7)
+          uint4 raw[4];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) raw[c] = ld_shared_v4(vrow + i * kSwBox + ((c ^ (lrow & 7)) * 16));
+          for (int c = 0; c < 4; ++c) raw[c] = ld_shared_v4(vrow + i * kSwBox + (((4 * half + c) ^ (lrow & 7)) * 16));
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float f8[8];
             unpack8(raw[c], f8);
 #pragma unroll
             for (int e = 0; e < 8; ++e) f8[e] *= u;
-            st_shared_v4(wv + i * kSwBox + lrow * kSwRow + ((c ^ (lrow & 7)) * 16), pack8(f8));
+            st_shared_v4(wv + i * kSwBox + lrow * kSwRow + (((4 * half + c) ^ (lrow & 7)) * 16), pack8(f8));
           }
         }
-        if (p.v_unit) {
+        if (p.v_unit && half == 0) {
           // unit tile (core-matrix order, 128 rows x 16 columns): columns 0
           // (and 1) are u(j), the rest zero
           const float w1 = p.v_unit >= 2 ? u : 0.f;
@@ -248,7 +255,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
         for (int mb = 0; mb < mblocks; ++mb) {
           const int f = mb * kTile + lrow;
           const int f0 = f & ~7;
-          for (int c = 0; c < p.DvP; c += 16) {
+          for (int j = (mb * nchunk + half) & 1; j < nchunk; j += 2) {
+            const int c = 16 * j;
             const uint32_t ta = tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c);
             float v[16];
             tmem_ld16(ta, v);
@@ -258,14 +266,14 @@ __global__ void __launch_bounds__(kChainThreads, 1)
                 for (int e = 0; e < 16; ++e) st[static_cast<size_t>(c + e) * p.DkM + f] = v[e];
               }
 #pragma unroll
-              for (int half = 0; half < 2; ++half) {
+              for (int h8 = 0; h8 < 2; ++h8) {
                 float x[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = v[8 * half + e];
-                transpose8(x);   // lane l of the 8-group: column c + 8 half + l of features f0 .. f0 + 7
+                for (int e = 0; e < 8; ++e) x[e] = v[8 * h8 + e];
+                transpose8(x);   // lane l of the 8-group: column c + 8 h8 + l of features f0 .. f0 + 7
                 if (f0 < p.DkP)
                   *reinterpret_cast<uint4*>(img + static_cast<size_t>(f0 / 8) * p.DvP * 16 +
-                                            static_cast<size_t>(c + 8 * half + (lane & 7)) * 16) = pack8(x);
+                                            static_cast<size_t>(c + 8 * h8 + (lane & 7)) * 16) = pack8(x);
               }
             }
             if (decayed) {
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
           for (int mb = 0; mb < mblocks; ++mb) {
             const int r = r0 + s;
             const int f = mb * kTile + lrow;
-            for (int c = 0; c < p.DvP; c += 16) {
+            for (int c = 16 * half; c < p.DvP; c += 32) {
               float v[16];
               tmem_ld16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
               if (f < p.Dk) {
