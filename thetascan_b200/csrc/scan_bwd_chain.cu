@@ -29,8 +29,9 @@
 // Where the (batch, head) CTAs would leave SMs idle, the slots are split
 // over several CTAs of the same (batch, head), as in the forward chain.
 //
-// Warp roles (160 threads): warp 0 lane 0 issues the copies and the MMAs;
-// warps 1-4 (one TMEM lane quadrant each) form operands and read G.  Every
+// Warp roles (288 threads): warp 0 lane 0 issues the copies and the MMAs;
+// warps 1-8 (two per TMEM lane quadrant, each taking half of every row's
+// chunks) form operands and read G.  Every
 // wait is bounded; a wait that gives up records a device error, and the CTA
 // drains its copies and MMAs in flight before freeing TMEM.
 #include "capi_internal.h"
@@ -41,7 +42,10 @@ namespace ts {
 
 namespace {
 
-constexpr int kBwdChainThreads = 160;
+// warp 0: copies and MMAs; warps 1-8: the epilogue, two warps per TMEM lane
+// quadrant, each taking half of every row's chunks
+constexpr int kBwdEpiWarps = 8;
+constexpr int kBwdChainThreads = 32 * (1 + kBwdEpiWarps);
 
 struct BwdChainLayout {
   int qboxes, vboxes;
@@ -88,12 +92,15 @@ struct BwdChainShared {
 // multiplied by `times` and rounded again), into the swizzled boxes; the
 // remaining v_unit columns into the unit tile.  Rows past the tile's end are
 // zero.
+// `half` selects the 16-byte chunks 4 half .. 4 half + 3 of every box (the
+// unit tile belongs to half 0).
 __device__ __forceinline__ void build_row_operand(uint32_t op, uint32_t raw_row, int dvv, int v_unit, int vboxes,
                                                   uint32_t unit_off, int row, bool valid, float scale,
-                                                  float times) {
+                                                  float times, int half) {
   for (int i = 0; i < vboxes; ++i) {
 #pragma unroll
-    for (int c8 = 0; c8 < 8; ++c8) {
+    for (int cc = 0; cc < 4; ++cc) {
+      const int c8 = 4 * half + cc;
       float f[8];
       if (valid) {
 #pragma unroll
@@ -113,7 +120,7 @@ __device__ __forceinline__ void build_row_operand(uint32_t op, uint32_t raw_row,
       st_shared_v4(op + i * kSwBox + sw128_offset(row, c8), pack8(f));
     }
   }
-  if (v_unit) {
+  if (v_unit && half == 0) {
     float u[2] = {0.f, 0.f};
     if (valid) {
       uint32_t w;
@@ -157,10 +164,10 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
     mbar_init(&sh.load_q[0], 1);
     mbar_init(&sh.load_q[1], 1);
     mbar_init(&sh.load_raw, 1);
-    mbar_init(&sh.epi_x, 4 * 32);
+    mbar_init(&sh.epi_x, kBwdEpiWarps * 32);
     mbar_init(&sh.mma_x, 1);
     for (int r = 0; r < TS_MAX_RETENTIONS; ++r) {
-      mbar_init(&sh.epi_g[r], 4 * 32);
+      mbar_init(&sh.epi_g[r], kBwdEpiWarps * 32);
       mbar_init(&sh.mma_g[r], 1);
     }
     sh.abort = 0;
@@ -276,6 +283,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
   } else {
     // -------------------------------------------------------------------- epilogue
     const int quad = warp & 3;
+    const int half = (warp - 1) >> 2;    // which of the two warps of this lane quadrant
     const int lrow = 32 * quad + lane;   // token row of the operands, feature row of a G block
     bool ok = true;
     int nx = 0;
@@ -285,7 +293,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
       for (int mb = 0; mb < mblocks; ++mb) {
         const int r = r0 + s;
         const int f = mb * kTile + lrow;
-        for (int c = 0; c < p.DvP; c += 16) {
+        for (int c = 16 * half; c < p.DvP; c += 32) {
           float v[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
@@ -319,7 +327,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
         if (carry) {
           // (i+1) c(i) dout, from the bf16-rounded c(i) dout of dSloc's operand
           build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row,
-                            static_cast<float>(lrow + 1));
+                            static_cast<float>(lrow + 1), half);
           fence_async_smem();
           tc_fence_before();
           mbar_arrive(&sh.epi_x);
@@ -335,12 +343,18 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
         for (int mb = 0; mb < mblocks && ok; ++mb) {
           const int f = mb * kTile + lrow;
           const int f0 = f & ~7;
-          float sv[kMaxDvP];
+          // this warp's chunks of the row: kk = 2 i + par (every other chunk)
+          const int par = (mb * (p.DvP / 16) + half) & 1;
+          float sv[kMaxDvP / 2];
           if (carry || closing_term) {
-            // every column of this feature row in flight at once
+            // every column of this warp's chunks in flight at once
 #pragma unroll
-            for (int c = 0; c < kMaxDvP; ++c)
-              if (c < p.DvP) sv[c] = s_in[static_cast<size_t>(c) * p.DkM + f];
+            for (int i = 0; i < kMaxDvP / 32; ++i)
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int c = 16 * (2 * i + par) + e;
+                if (c < p.DvP) sv[16 * i + e] = s_in[static_cast<size_t>(c) * p.DkM + f];
+              }
           }
           if (carry) {
             ok = mbar_wait(&sh.mma_x, nx & 1, kErrMmaTimeout);
@@ -350,8 +364,8 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           }
           float part = 0.f;
 #pragma unroll
-          for (int kk = 0; kk < kMaxDvP / 16; ++kk) {
-            const int c = 16 * kk;
+          for (int i = 0; i < kMaxDvP / 32; ++i) {
+            const int c = 16 * (2 * i + par);
             if (c >= p.DvP) break;
             const uint32_t ta = tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c);
             float v[16];
@@ -360,24 +374,24 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
               float x[16];
               tmem_ld16(tmem_addr(tmem, 32 * quad, t_x + c), x);
 #pragma unroll
-              for (int e = 0; e < 16; ++e) part = fmaf(sv[c + e], x[e], part);
+              for (int e = 0; e < 16; ++e) part = fmaf(sv[16 * i + e], x[e], part);
             }
             if (closing_term) {
               float cg = 0.f;
 #pragma unroll
-              for (int e = 0; e < 16; ++e) cg = fmaf(sv[c + e], v[e], cg);
+              for (int e = 0; e < 16; ++e) cg = fmaf(sv[16 * i + e], v[e], cg);
               part = fmaf(kc, cg, part);
             }
             if (g.store) {
 #pragma unroll
-              for (int half = 0; half < 2; ++half) {
+              for (int h8 = 0; h8 < 2; ++h8) {
                 float x[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) x[e] = v[8 * half + e];
+                for (int e = 0; e < 8; ++e) x[e] = v[8 * h8 + e];
                 transpose8(x);
                 if (f0 < p.DkP)
                   *reinterpret_cast<uint4*>(img + static_cast<size_t>(f0 / 8) * p.DvP * 16 +
-                                            static_cast<size_t>(c + 8 * half + (lane & 7)) * 16) = pack8(x);
+                                            static_cast<size_t>(c + 8 * h8 + (lane & 7)) * 16) = pack8(x);
               }
             }
             if (decayed && local(n)) {
@@ -396,7 +410,8 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
         if (!ok) break;
         // dSloc(n)'s row operand c(i) dout (the carry products are done)
         if (local(n))
-          build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row, 1.f);
+          build_row_operand(op, raw_row, dvv, p.v_unit, L.vboxes, L.vboxes * kSwBox, lrow, lrow < len, c_row, 1.f,
+                            half);
         fence_async_smem();
         tc_fence_before();
         mbar_arrive(&sh.epi_g[s]);
@@ -413,7 +428,7 @@ __global__ void __launch_bounds__(kBwdChainThreads, 1)
           for (int mb = 0; mb < mblocks; ++mb) {
             const int r = r0 + s;
             const int f = mb * kTile + lrow;
-            for (int c = 0; c < p.DvP; c += 16) {
+            for (int c = 16 * half; c < p.DvP; c += 32) {
               float v[16];
               tmem_ld16(tmem_addr(tmem, 32 * quad, s * region + mb * p.DvP + c), v);
               if (f < p.Dk) {
