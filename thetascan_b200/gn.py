@@ -150,6 +150,7 @@ class _Run:
         self.m, self.nl, self.eps, self.fake = int(m), _NONLIN[nonlin], float(eps), fake
         self.like = q
         self.tau = None if tau is None else tau[..., 0].float().contiguous()   # [H, m]
+        self.tf32_wgrad = False   # weight-gradient products on TF32 (the core sets it)
 
     def new(self, width, zero=False, dtype=torch.float32):
         shape = (self.B, self.H, self.T) + ((width,) if width else ())
@@ -226,16 +227,24 @@ def _hm(W, x):
     return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
 
 
-def _hm_wgrad(gy, x):
+def _hm_wgrad(gy, x, tf32=False):
     """``sum_{b,t} gy[b,h,t] x[b,h,t]^T`` per head, ``[H,o,i]``: the token axis
-    cut into chunks that run as parallel batched products, summed after."""
+    cut into chunks that run as parallel batched products, summed after in
+    f32.  With ``tf32`` the products run on TF32 tensor cores (the GN core's
+    setting: a weight gradient sums ~10^5 products, so the operands' 10-bit
+    rounding averages out to ~1e-4 of it)."""
     B, H, T, i = x.shape
     o = gy.shape[-1]
     S = 1
     while T % (2 * S) == 0 and T // (2 * S) >= 512 and B * H * S < 512:
         S *= 2
-    part = torch.bmm(gy.contiguous().view(B * H * S, T // S, o).transpose(1, 2),
-                     x.contiguous().view(B * H * S, T // S, i))
+    saved = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32)
+    try:
+        part = torch.bmm(gy.contiguous().view(B * H * S, T // S, o).transpose(1, 2),
+                         x.contiguous().view(B * H * S, T // S, i))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = saved
     return part.view(B, H, S, o, i).sum(dim=(0, 2))
 
 
@@ -316,6 +325,7 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     B, H, T, d = q.shape
     m = W1.shape[1]
     run = _Run(q, m, tau, nonlin, eps, fake)
+    run.tf32_wgrad = True
     W1, W2 = W1.float().contiguous(), W2.float().contiguous()
     W2t = W2.transpose(1, 2)
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
@@ -394,13 +404,13 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
             dlam2 += dlam2_s
             dla[s] += dla2_s[0]
         dhq = dhq + _hm(W2t, dys[s])
-        dW2 += _hm_wgrad(dys[s], hq)
+        dW2 += _hm_wgrad(dys[s], hq, run.tf32_wgrad)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, R1[s], dhq], [da_q, dR1[s]],
                  flags=int(read_norm_w1) | (2 if s else 0), dtau=tau_grad)
     if dy_base is not None:
         hb = run.new(m)
         run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
-        dW2 += _hm_wgrad(dy_base, hb)
+        dW2 += _hm_wgrad(dy_base, hb, run.tf32_wgrad)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base)], [da_q, None], flags=2, dtau=tau_grad)
     # stage 1
     if steps == 2:
@@ -415,7 +425,7 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         dq += dq1
         dk = dk1
     dq += _hm(W1.transpose(1, 2), da_q)
-    dW1 = _hm_wgrad(da_q, q)
+    dW1 = _hm_wgrad(da_q, q, run.tf32_wgrad)
     da_extra = None
     if steps == 2:
         dg, dg2 = dg[..., :m].contiguous(), dg[..., m:].contiguous()
@@ -500,7 +510,9 @@ def _write2_backward(run, k, v, W2, two, h_k, lam, g, kk, dh2, dg2, dlam2, dtau)
     run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam2, dlam2W, v, k, two["O2"], two["RS2"], two["hh2"], kk],
              [dr2, drowsq2, dk2, dhh2])
     h2 = two["h2"]
-    dW2 = _hm_wgrad(two["lam2"], du2) - _hm_wgrad(dr2, h2) + 2.0 * W2 * _hm_wgrad(drowsq2, two["s2b"])
+    tf = run.tf32_wgrad
+    dW2 = (_hm_wgrad(two["lam2"], du2, tf) - _hm_wgrad(dr2, h2, tf)
+           + 2.0 * W2 * _hm_wgrad(drowsq2, two["s2b"], tf))
     # O2 = W2 h2 + lam (h . h2), and r2 = v - k - O2
     dhd = -(dr2 * lam).sum(-1, keepdim=True)
     dlam_first = -dr2 * two["hd"]
@@ -528,7 +540,8 @@ def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau, da_extra=Non
     dlamW = _hm(W2, du)
     dv, drowsq, dk_w, dhh = run.new(d), run.new(d), run.new(d), run.new(0)
     run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam, dlamW, v, k, O, RS, hh, kk], [dv, drowsq, dk_w, dhh])
-    dW2 = _hm_wgrad(lam, du) - _hm_wgrad(dv, h_k) + 2.0 * W2 * _hm_wgrad(drowsq, s2)
+    tf = run.tf32_wgrad
+    dW2 = _hm_wgrad(lam, du, tf) - _hm_wgrad(dv, h_k, tf) + 2.0 * W2 * _hm_wgrad(drowsq, s2, tf)
     ds2 = _hm((W2 * W2).transpose(1, 2), drowsq)
     dhO = _hm(W2t, dv)
     da_k = run.new(m)
@@ -536,7 +549,7 @@ def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau, da_extra=Non
     if da_extra is not None:
         da_k = da_k + da_extra
     dk = dk_w + _hm(W1.transpose(1, 2), da_k)
-    return dk, dv, _hm_wgrad(da_k, k), dW2
+    return dk, dv, _hm_wgrad(da_k, k, run.tf32_wgrad), dW2
 
 
 def _scan_pieces(width, unit, n_retentions, dk):
