@@ -217,6 +217,39 @@ GN_JAC2_CONFIGS = {
         rope=dict(mode="partial", fraction=0.5), B=2, T=96, dtype="float32"),
 }
 
+# GN nets the one-block row kernels do not cover: the swiglu activation and
+# depth > 1 (engine.py:117-175, 215-255), with one and two Jacobian steps,
+# each read normalisation and fast / stale banks; head_dim 64, ragged T.
+GN_DEEP_CONFIGS = {
+    "gn_swiglu_sum": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, family="gn",
+        gn=dict(nonlinearity="swiglu", read_normalization="none"),
+        rope=dict(mode="partial", fraction=0.5), B=2, T=96, dtype="float32"),
+    "gn_swiglu_jac2_bank": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, share_key_query=True, output_gate=False, family="gn",
+        gn=dict(nonlinearity="swiglu", jacobian_steps=2, read_normalization="none"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32"),
+    "gn_depth2_both_bank": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, depth=2, share_key_query=True, output_gate=False,
+        family="gn", gn=dict(nonlinearity="relu2", read_normalization="both_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), temporal=dict(mode="bank", retention_init=0.9),
+        B=1, T=160, dtype="float32"),
+    "gn_depth2_swiglu_stale": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, depth=2, family="gn",
+        gn=dict(nonlinearity="swiglu", read_normalization="none"),
+        temporal=dict(mode="bank", bank_mode="stale", retention_init=0.9), B=1, T=128, dtype="float32"),
+    "gn_depth3_threshold_w2_expanded": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, feature_expansion=2, depth=3, family="gn",
+        gn=dict(nonlinearity="relu2_threshold", read_normalization="w2_feature_mass"),
+        rope=dict(mode="partial", fraction=0.5), B=2, T=96, dtype="float32"),
+    "gn_depth2_silu_jac2_bank2": dict(
+        d_model=128, n_heads=2, memory_multiplier=2, depth=2, family="gn",
+        gn=dict(nonlinearity="silu", jacobian_steps=2, read_normalization="none"),
+        temporal=dict(mode="bank", recency_branches=2, retention_inits=(0.9, 0.99)),
+        B=1, T=128, dtype="float32"),
+}
+
 # Config-3 width (head_dim 128, m = 128, relu2, two-stage feature-mass read,
 # the plain sum view) at T = 1024; written to its own file, gn_c3_cases.pt.
 GN_C3_CONFIGS = {
@@ -417,8 +450,12 @@ def gn_jac2_cases():
     return gn_cases(GN_JAC2_CONFIGS)
 
 
+def gn_deep_cases():
+    return gn_cases(GN_DEEP_CONFIGS)
+
+
 GENERATORS = {"scan": scan_cases, "feature": feature_cases, "mixer": mixer_cases, "gn": gn_cases,
-              "gn_jac2": gn_jac2_cases,
+              "gn_jac2": gn_jac2_cases, "gn_deep": gn_deep_cases,
               "gn_c3": gn_c3_cases, "gn_tanh": gn_tanh_cases, "sparse": sparse_cases}
 
 

@@ -86,3 +86,36 @@ def test_gn_two_jacobian_steps_match_reference_fixture(dev, name):
     grads = dict(module._core.named_parameters())
     for n, want in case["grads"].items():
         assert rel_err(grads[n].grad, want) < JAC2_LOOSE.get((name, n), BF16_TOL), n
+
+
+DEEP_CASES = ["gn_swiglu_sum", "gn_swiglu_jac2_bank", "gn_depth2_both_bank", "gn_depth2_swiglu_stale",
+              "gn_depth3_threshold_w2_expanded", "gn_depth2_silu_jac2_bank2"]
+
+
+@pytest.mark.parametrize("name", DEEP_CASES)
+def test_gn_deep_and_swiglu_match_reference_fixture(dev, name):
+    """GN nets of depth 2 and 3 and the swiglu activation (``gn_deep``: the
+    per-token maps in f32, every read on the scan kernels), with one and two
+    Jacobian steps, each read normalisation, fast and stale banks, against
+    fixtures of the reference GN mixer: output, input gradient, every
+    parameter gradient."""
+    from thetascan_b200 import _lib
+    from thetascan_b200.config import ThetaScanConfig
+    from thetascan_b200.mixer import ThetaScan
+
+    case = torch.load(os.path.join(GOLDEN, "gn_deep_cases.pt"), weights_only=False)[name]
+    module = ThetaScan(ThetaScanConfig.from_dict(case["public_config"])).to(dev)
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    before = _lib.load().ts_b200_launch_count()
+    x = case["x"].float().to(dev).requires_grad_(True)
+    y = module(x)
+    (y.double() * case["out_weight"].to(dev)).sum().backward()
+    torch.cuda.synchronize()
+    assert _lib.load().ts_b200_launch_count() > before   # the reads ran on the library kernels
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    assert rel_err(y, case["y"]) < BF16_TOL
+    assert rel_err(x.grad, case["x_grad"]) < BF16_TOL
+    grads = dict(module._core.named_parameters())
+    for n, want in case["grads"].items():
+        assert rel_err(grads[n].grad, want) < BF16_TOL, n

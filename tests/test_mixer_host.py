@@ -58,8 +58,7 @@ def test_presets_and_unsupported_configs():
     ThetaScan(ThetaScanConfig.gn_reference_v0_1(d_model=256, n_heads=4))
     ThetaScan(ThetaScanConfig.gn_expanded_reference_v0_1(d_model=256, n_heads=4))
     from thetascan_b200.config import GNConfig
-    with pytest.raises(NotImplementedError):
-        ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn", gn=GNConfig(nonlinearity="swiglu")))
+    ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn", gn=GNConfig(nonlinearity="swiglu"), depth=2))
     ThetaScan(ThetaScanConfig.from_dict(_fixtures()["bspline_stale"]["public_config"]))
     from thetascan_b200.config import TemporalConfig
     ThetaScan(ThetaScanConfig(d_model=256, n_heads=4, family="gn",

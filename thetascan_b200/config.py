@@ -10,8 +10,7 @@ package executes that backend only (``"auto"`` resolves to it).
 
 Validation restates the reference's rules for the fields this package reads
 and raises ``NotImplementedError`` for configurations the GPU path does not
-cover yet (GN swiglu and depth > 1, EMA decay gates, value anchors,
-feature-space RoPE).
+cover (EMA decay gates, value anchors, feature-space RoPE).
 """
 from __future__ import annotations
 
@@ -429,10 +428,6 @@ class ThetaScanConfig:
         if self.rope.mode != "none" and self.rope.placement == "feature":
             return "feature-space RoPE is not built"
         if self.family == "gn":
-            if self.gn.nonlinearity == "swiglu":
-                return "the GN swiglu nonlinearity is not built"
-            if self.depth != 1:
-                return "GN depth > 1 is not built"
             return None
         k = self.kernel
         if k.value_representation == "value_anchors":

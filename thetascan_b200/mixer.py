@@ -193,27 +193,33 @@ class ThetaScanCore(nn.Module):
         else:
             self.proj_qkv = nn.Linear(D, 3 * H * d, bias=False)
         self.proj_out = nn.Linear(H * d, D, bias=False)
-        # Memory net theta0 (block.py:210-301).
+        # Memory net theta0 (block.py:210-301): one (W1, W2, Wg) per layer,
+        # drawn in the reference's order (every W1, every W2, every Wg).
+        L = cfg.depth
         projections = m // k.bspline_basis_count if kernel and k.feature_map == "projected_bspline" else m
-        self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, projections, d) / math.sqrt(d))])
-        self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, m))])
-        if not kernel and cfg.gn.nonlinearity == "relu2_threshold":
+        self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, projections, d) / math.sqrt(d)) for _ in range(L)])
+        self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, m)) for _ in range(L)])
+        if not kernel and cfg.gn.nonlinearity == "swiglu":
+            # swiglu gate branch, at the effective width (never expanded)
+            self.Wg = nn.ParameterList([nn.Parameter(torch.randn(H, m, d) / math.sqrt(d)) for _ in range(L)])
+        elif not kernel and cfg.gn.nonlinearity == "relu2_threshold":
             # GN learned threshold tau rides the Wg slot (block.py:231-235), zero-init
-            self.Wg = nn.ParameterList([nn.Parameter(torch.zeros(H, m, 1))])
+            self.Wg = nn.ParameterList([nn.Parameter(torch.zeros(H, m, 1)) for _ in range(L)])
         else:
             self.Wg = None
         self.register_buffer("_expansion_fingerprint", None)
         self._expanded = cfg.feature_expansion > 1
         if self._expanded:
             b = m // cfg.feature_expansion
-            self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, b, d) / math.sqrt(d))])
-            self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, b))])
-            self.register_buffer("_expand_w1_0", unit_row_map((1, m, b), key=cfg.expansion_key,
-                                                               role="w1-expand-layer-0"), persistent=False)
-            self.register_buffer("_expand_w2_0", unit_row_map((1, b, m), key=cfg.expansion_key,
-                                                               role="w2-expand-layer-0"), persistent=False)
+            self.W1 = nn.ParameterList([nn.Parameter(torch.randn(H, b, d) / math.sqrt(d)) for _ in range(L)])
+            self.W2 = nn.ParameterList([nn.Parameter(torch.zeros(H, d, b)) for _ in range(L)])
+            for layer in range(L):
+                self.register_buffer(f"_expand_w1_{layer}", unit_row_map(
+                    (1, m, b), key=cfg.expansion_key, role=f"w1-expand-layer-{layer}"), persistent=False)
+                self.register_buffer(f"_expand_w2_{layer}", unit_row_map(
+                    (1, b, m), key=cfg.expansion_key, role=f"w2-expand-layer-{layer}"), persistent=False)
             self._expansion_fingerprint = expansion_fingerprint(
-                key=cfg.expansion_key, effective=m, expansion=cfg.feature_expansion, depth=cfg.depth)
+                key=cfg.expansion_key, effective=m, expansion=cfg.feature_expansion, depth=L)
         self.vmlp_in = self.vmlp_out = None
         if k.value_representation == "value_mlp":
             vh = max(1, int(k.value_mlp_multiplier * d))
@@ -293,14 +299,25 @@ class ThetaScanCore(nn.Module):
             q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
-        W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
-        y = gn_core(q, k, v, W1, W2, None if self.Wg is None else self.Wg[0],
-                    nonlin="relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity,
-                    read_norm=gn.read_normalization != "none",
-                    read_norm_w1=gn.read_normalization == "both_feature_mass",
-                    log_alphas=log_alphas, etas=etas, mode=self.spec.mode if log_alphas is not None else "sum",
-                    eps=eps, steps=gn.jacobian_steps)
+        nonlin = "relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity
+        mode = self.spec.mode if log_alphas is not None else "sum"
+        if self.cfg.depth == 1 and nonlin != "swiglu":
+            W1, W2 = self.effective_weights()
+            y = gn_core(q, k, v, W1, W2, None if self.Wg is None else self.Wg[0], nonlin=nonlin,
+                        read_norm=gn.read_normalization != "none",
+                        read_norm_w1=gn.read_normalization == "both_feature_mass",
+                        log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps)
+        else:
+            # deeper nets and the swiglu activation (gn_deep: per-token maps
+            # in f32 PyTorch, every read on the scan kernels)
+            from .gn_deep import gn_deep
+            layers = [self.effective_weights(l) + (None if self.Wg is None else self.Wg[l],)
+                      for l in range(self.cfg.depth)]
+            y = gn_deep(q, k, v, layers, nonlin=nonlin, thresholded=gn.nonlinearity == "relu2_threshold",
+                        read_norm=gn.read_normalization != "none",
+                        read_norm_w1=gn.read_normalization == "both_feature_mass",
+                        log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps)
         y = y.transpose(1, 2)
         if self.ogate is not None:
             g = tf32_linear(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)
@@ -330,12 +347,12 @@ class ThetaScanCore(nn.Module):
             y = y * F.silu(F.linear(x, lin.weight, lin.bias).view(B, T, H, d))
         return F.linear(y.reshape(B, T, H * d), self.proj_out.weight)
 
-    def effective_weights(self):
-        """``U W1`` and ``W2 D`` (block.py:546-567)."""
-        W1, W2 = self.W1[0], self.W2[0]
+    def effective_weights(self, layer: int = 0):
+        """``U W1`` and ``W2 D`` of one layer (block.py:546-567)."""
+        W1, W2 = self.W1[layer], self.W2[layer]
         if self._expanded:
-            W1 = torch.matmul(self._expand_w1_0, W1)
-            W2 = torch.matmul(W2, self._expand_w2_0)
+            W1 = torch.matmul(getattr(self, f"_expand_w1_{layer}"), W1)
+            W2 = torch.matmul(W2, getattr(self, f"_expand_w2_{layer}"))
         return W1, W2
 
     def fade(self):
