@@ -335,8 +335,8 @@ typedef struct ts_feature_grad_args {
   const void* dy0_bf16;
   int64_t dy0_strides[3];
   /* 1: dw2 is f32 [H,m,d] (the transpose of W2's layout), accumulated with
-   * vector atomics; 0: [H,d,m].  When ts_feature_args.phi_q is given to the
-   * backward it is read as the forward's phi(q) for dw2 (else rebuilt). */
+   * vector atomics; 0: [H,d,m].  The backward rebuilds phi(q) for dw2 from
+   * q (ts_feature_args.phi_q is not read by it). */
   int dw2_transposed;
   float* drelative_threshold;  /* f32 [H], ACCUMULATED, or NULL (relative sparsity) */
   float* dsparse_blend;        /* f32 [H], ACCUMULATED, or NULL (relative_st_blend) */

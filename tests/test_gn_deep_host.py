@@ -1,7 +1,7 @@
 """Host algebra of the deep / swiglu GN core (``thetascan_b200.gn_deep``) on CPU.
 
 The core's per-token maps are PyTorch; its sequence reads go through the
-scan kernels.  Here the scan is replaced by the float64 oracle scan (the
+float32 scan kernels.  Here the scan is replaced by the float64 oracle scan (the
 checker, injected by the test only), so that the write, the per-layer reads,
 the view grouping and the bank blend are pinned on CPU against fixtures of
 the reference GN mixer itself (``tests/golden/gn_deep_cases.pt``): output,
@@ -33,19 +33,21 @@ def rel_err(got, want):
     return float((got - want).abs().max() / want.abs().max().clamp_min(1e-30))
 
 
-def oracle_views(q, k, v, append_unit, stale, retentions):
-    """float64 CPU stand-in for ``scan.scan_views_f32`` (same arguments and
-    results: f32 reads of every retention, ``[v | 1]`` with ``append_unit``,
-    the stale view as the plain sum minus the decayed read)."""
+def oracle_views(q, k, v, retentions, chunk=512, *, append_unit=False, stale=None):
+    """float64 CPU stand-in for ``scan.linattn_views`` (same arguments and
+    results: reads of every retention in the stream dtype, ``[v | 1]`` with
+    ``append_unit``, the stale view as the plain sum minus the decayed
+    read)."""
+    stale = stale or (False,) * len(retentions)
     if append_unit:
         v = torch.cat([v, v.new_ones(*v.shape[:3], 1)], dim=-1)
     rets = tuple(None if r is None else r.double() for r in retentions) + (None,)
     outs = oracle_scan.linattn_chunk_views(q.double(), k.double(), v.double(), rets, 64)
-    return tuple((outs[-1] - o if st else o).float() for o, st in zip(outs[:-1], stale))
+    return tuple((outs[-1] - o if st else o).to(q.dtype) for o, st in zip(outs[:-1], stale))
 
 
 def run_case(case, monkeypatch):
-    monkeypatch.setattr(gn_deep, "_scan", types.SimpleNamespace(scan_views_f32=oracle_views))
+    monkeypatch.setattr(gn_deep, "_scan", types.SimpleNamespace(linattn_views=oracle_views))
     cfg = ThetaScanConfig.from_dict(case["public_config"])
     module = ThetaScan(cfg)
     module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()

@@ -92,12 +92,19 @@ DEEP_CASES = ["gn_swiglu_sum", "gn_swiglu_jac2_bank", "gn_depth2_both_bank", "gn
               "gn_depth3_threshold_w2_expanded", "gn_depth2_silu_jac2_bank2"]
 
 
+# gn_deep runs float32 end to end (plain f32 projections, f32 scan kernels);
+# the fixtures' retention gradients move by 1-2% under a 2^-11 relative
+# perturbation of q and k alone, so TF32 or bf16 operands could not be told
+# apart from a wrong result here.
+DEEP_TOL = 2e-3
+
+
 @pytest.mark.parametrize("name", DEEP_CASES)
 def test_gn_deep_and_swiglu_match_reference_fixture(dev, name):
     """GN nets of depth 2 and 3 and the swiglu activation (``gn_deep``: the
-    per-token maps in f32, every read on the scan kernels), with one and two
-    Jacobian steps, each read normalisation, fast and stale banks, against
-    fixtures of the reference GN mixer: output, input gradient, every
+    per-token maps in f32, every read on the float32 scan kernels), with one
+    and two Jacobian steps, each read normalisation, fast and stale banks,
+    against fixtures of the reference GN mixer: output, input gradient, every
     parameter gradient."""
     from thetascan_b200 import _lib
     from thetascan_b200.config import ThetaScanConfig
@@ -114,8 +121,9 @@ def test_gn_deep_and_swiglu_match_reference_fixture(dev, name):
     torch.cuda.synchronize()
     assert _lib.load().ts_b200_launch_count() > before   # the reads ran on the library kernels
     assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
-    assert rel_err(y, case["y"]) < BF16_TOL
-    assert rel_err(x.grad, case["x_grad"]) < BF16_TOL
+    errs = {"y": rel_err(y, case["y"]), "x": rel_err(x.grad, case["x_grad"])}
     grads = dict(module._core.named_parameters())
     for n, want in case["grads"].items():
-        assert rel_err(grads[n].grad, want) < BF16_TOL, n
+        errs[n] = rel_err(grads[n].grad, want)
+    worst = max(errs, key=errs.get)
+    assert errs[worst] < DEEP_TOL, (worst, errs)

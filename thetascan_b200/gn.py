@@ -150,7 +150,7 @@ class _Run:
         self.m, self.nl, self.eps, self.fake = int(m), _NONLIN[nonlin], float(eps), fake
         self.like = q
         self.tau = None if tau is None else tau[..., 0].float().contiguous()   # [H, m]
-        self.tf32_wgrad = False   # weight-gradient products on TF32 (the core sets it)
+        self.tf32 = False   # per-head maps and weight-gradient products on TF32 (the core sets it)
 
     def new(self, width, zero=False, dtype=torch.float32):
         shape = (self.B, self.H, self.T) + ((width,) if width else ())
@@ -222,9 +222,18 @@ class _Run:
         return dq, dk, dp[0] if len(dp) == 1 else torch.cat(dp, dim=-1), dla
 
 
-def _hm(W, x):
-    """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (batched GEMM)."""
-    return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+def _hm(W, x, tf32=False):
+    """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (batched GEMM); with
+    ``tf32`` on TF32 tensor cores (10-bit operand mantissas, f32
+    accumulation)."""
+    if not tf32:
+        return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+    saved = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = saved
 
 
 def _hm_wgrad(gy, x, tf32=False):
@@ -255,6 +264,7 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
     B, H, T, d = q.shape
     m = W1.shape[1]
     run = _Run(q, m, tau, nonlin, eps, fake)
+    run.tf32 = True
     W1, W2 = W1.float().contiguous(), W2.float().contiguous()
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
     las = [None] + [log_alphas[j].float() for j in range(J)]
@@ -267,7 +277,7 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
         two = _write2_forward(run, k, v, W2, a_k, h_k, kk, lam, g32)
         g = torch.cat([g, two["g2b"]], dim=-1)   # both g payloads in one stage-1 scan
     # stage 1, shared by all views (engine.py:475-500)
-    a_q = _hm(W1, q)
+    a_q = _hm(W1, q, run.tf32)
     if read_norm_w1:
         h0 = run.new_bf16(m)
         run.rows(_lib.TS_GN_QUERY_PRE, [a_q], [None], bf16=h0)
@@ -286,7 +296,7 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
     for s in range(J + 1):
         hq, hqb = run.new(m), run.new_bf16(m)
         run.rows(_lib.TS_GN_FEATURES, [a_q, R1[s]], [hq], flags=int(read_norm_w1), bf16=hqb)
-        base = _hm(W2, hq)
+        base = _hm(W2, hq, run.tf32)
         (C,), st2 = run.scan_fwd(hqb, h_kb, lamb, bool(read_norm), [las[s]], [stale[s]])
         saved += [hq, hqb] + [x for piece in st2 for x in piece[3:]]
         if two is not None:
@@ -303,7 +313,7 @@ def _gn_forward(q, k, v, W1, W2, tau, log_alphas, etas, nonlin, read_norm, read_
         # (pre = W1 q, no memory term; block.py:697-718)
         hb = run.new(m)
         run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
-        y_base = q + _hm(W2, hb)
+        y_base = q + _hm(W2, hb, run.tf32)
         for j in range(J):
             y = y - etas[j].float().view(1, -1, 1, 1) * (ys[1 + j] - y_base)
         saved += ys + [y_base]
@@ -325,7 +335,7 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     B, H, T, d = q.shape
     m = W1.shape[1]
     run = _Run(q, m, tau, nonlin, eps, fake)
-    run.tf32_wgrad = True
+    run.tf32 = True
     W1, W2 = W1.float().contiguous(), W2.float().contiguous()
     W2t = W2.transpose(1, 2)
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
@@ -403,15 +413,15 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
             dh2 += dh2_s
             dlam2 += dlam2_s
             dla[s] += dla2_s[0]
-        dhq = dhq + _hm(W2t, dys[s])
-        dW2 += _hm_wgrad(dys[s], hq, run.tf32_wgrad)
+        dhq = dhq + _hm(W2t, dys[s], run.tf32)
+        dW2 += _hm_wgrad(dys[s], hq, run.tf32)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, R1[s], dhq], [da_q, dR1[s]],
                  flags=int(read_norm_w1) | (2 if s else 0), dtau=tau_grad)
     if dy_base is not None:
         hb = run.new(m)
         run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
-        dW2 += _hm_wgrad(dy_base, hb, run.tf32_wgrad)
-        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base)], [da_q, None], flags=2, dtau=tau_grad)
+        dW2 += _hm_wgrad(dy_base, hb, run.tf32)
+        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base, run.tf32)], [da_q, None], flags=2, dtau=tau_grad)
     # stage 1
     if steps == 2:
         dR1 = [torch.cat([r, r], dim=-1) for r in dR1]
@@ -424,8 +434,8 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     else:
         dq += dq1
         dk = dk1
-    dq += _hm(W1.transpose(1, 2), da_q)
-    dW1 = _hm_wgrad(da_q, q, run.tf32_wgrad)
+    dq += _hm(W1.transpose(1, 2), da_q, run.tf32)
+    dW1 = _hm_wgrad(da_q, q, run.tf32)
     da_extra = None
     if steps == 2:
         dg, dg2 = dg[..., :m].contiguous(), dg[..., m:].contiguous()
@@ -452,6 +462,9 @@ def _write_forward(run, k, v, W1, W2, bf16=False, g32=False):
     with ``g32``), and ``(h_bf16, lam_bf16, g_f32 or None)`` follow the
     tuple."""
     m, d = run.m, run.d
+    # The write's maps stay f32: the damped solve divides by them, and TF32
+    # operands here moved the log-retention gradient by ~0.4% of its largest
+    # entry (the read and backward maps run on TF32 without a visible shift).
     a_k = _hm(W1, k)
     h_k, s2, hh, kk = run.new(m), run.new(m), run.new(0), run.new(0)
     h_kb = run.new_bf16(m) if bf16 else None
@@ -505,20 +518,20 @@ def _write2_backward(run, k, v, W2, two, h_k, lam, g, kk, dh2, dg2, dlam2, dtau)
     W2t = W2.transpose(1, 2)
     du2 = run.new(m)
     run.rows(_lib.TS_GN_WRITE_G_BWD, [dg2, two["a2"]], [du2])
-    dlam2W = _hm(W2, du2)
+    dlam2W = _hm(W2, du2, run.tf32)
     dr2, drowsq2, dk2, dhh2 = run.new(d), run.new(d), run.new(d), run.new(0)
     run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam2, dlam2W, v, k, two["O2"], two["RS2"], two["hh2"], kk],
              [dr2, drowsq2, dk2, dhh2])
     h2 = two["h2"]
-    tf = run.tf32_wgrad
+    tf = run.tf32
     dW2 = (_hm_wgrad(two["lam2"], du2, tf) - _hm_wgrad(dr2, h2, tf)
            + 2.0 * W2 * _hm_wgrad(drowsq2, two["s2b"], tf))
     # O2 = W2 h2 + lam (h . h2), and r2 = v - k - O2
     dhd = -(dr2 * lam).sum(-1, keepdim=True)
     dlam_first = -dr2 * two["hd"]
     dh_first = dhd * h2
-    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq2)
-    dhO2 = _hm(W2t, dr2)
+    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq2, run.tf32)
+    dhO2 = _hm(W2t, dr2, run.tf32)
     da2 = run.new(m)
     run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh2 + dhd * h_k, dhO2, ds2, dhh2, dg2, two["U2"], two["a2"]], [da2],
              dtau=dtau)
@@ -537,19 +550,19 @@ def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau, da_extra=Non
     W2t = W2.transpose(1, 2)
     du = run.new(m)
     run.rows(_lib.TS_GN_WRITE_G_BWD, [dg, a_k], [du])
-    dlamW = _hm(W2, du)
+    dlamW = _hm(W2, du, run.tf32)
     dv, drowsq, dk_w, dhh = run.new(d), run.new(d), run.new(d), run.new(0)
     run.rows(_lib.TS_GN_WRITE_LAM_BWD, [dlam, dlamW, v, k, O, RS, hh, kk], [dv, drowsq, dk_w, dhh])
-    tf = run.tf32_wgrad
+    tf = run.tf32
     dW2 = _hm_wgrad(lam, du, tf) - _hm_wgrad(dv, h_k, tf) + 2.0 * W2 * _hm_wgrad(drowsq, s2, tf)
-    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq)
-    dhO = _hm(W2t, dv)
+    ds2 = _hm((W2 * W2).transpose(1, 2), drowsq, run.tf32)
+    dhO = _hm(W2t, dv, run.tf32)
     da_k = run.new(m)
     run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh, dhO, ds2, dhh, dg, U, a_k], [da_k], dtau=dtau)
     if da_extra is not None:
         da_k = da_k + da_extra
-    dk = dk_w + _hm(W1.transpose(1, 2), da_k)
-    return dk, dv, _hm_wgrad(da_k, k, run.tf32_wgrad), dW2
+    dk = dk_w + _hm(W1.transpose(1, 2), da_k, run.tf32)
+    return dk, dv, _hm_wgrad(da_k, k, run.tf32), dW2
 
 
 def _scan_pieces(width, unit, n_retentions, dk):

@@ -4,10 +4,13 @@ The row kernels of :mod:`thetascan_b200.gn` run a GN net of depth 1 with an
 elementwise activation.  This module runs every other GN net the reference
 accepts -- any depth, the two-branch swiglu activation, one or two Jacobian
 steps, all three read normalisations and every temporal view -- with the
-same sequence reads on the multi-view scan kernels
-(``thetascan_b200::scan_views_fwd``: bf16 operands on the tensor cores, f32
-reads, states and gradients) and the per-token maps as float32 PyTorch under
-autograd.
+sequence reads on the float32 multi-view scan kernels (custom op
+``thetascan_b200::scan_views_fwd`` with float32 streams: f32 operands, states,
+reads and gradients on the CUDA cores) and the per-token maps as float32
+PyTorch under autograd.  Deep and swiglu nets amplify the rounding of their
+scan operands: with bf16 operands the retention gradient of a swiglu net
+with two Jacobian steps moved by 1-6% of its largest entry under rounding
+perturbations alone, so these nets keep their streams in float32.
 
 Reference (src/thetascan/_core/ops/engine.py): the write is
 ``_forward_theta0`` / ``_block_forward`` (:117-175, residual
@@ -30,7 +33,7 @@ import torch
 import torch.nn.functional as F
 
 from . import scan as _scan
-from .gn import _scan_pieces, _views
+from .gn import _views
 
 _ACTS = ("relu2", "silu", "tanh", "swiglu")
 
@@ -172,13 +175,24 @@ class _Net:
         return la1, la2
 
 
+def _pieces(width, unit, dk):
+    """``(start, stop, unit)`` payload pieces within the float32 scan
+    kernels' shared-memory budget (payload plus unit column: 240 columns for
+    keys up to 128 wide, 120 beyond); the unit column rides the last piece."""
+    step = (240 if dk <= 128 else 120) - 1
+    if width + int(unit) <= step + 1:
+        return [(0, width, unit)]
+    return [(s, min(width, s + step), unit and min(width, s + step) >= width) for s in range(0, width, step)]
+
+
 def _reads(query, keys, payload, unit, retentions, stale):
     """Reads of one stream set through the views ``retentions`` (f32
-    ``[B,H,T,W(+1)]`` each), the payload cut into pieces within the scan
-    kernels' budgets."""
+    ``[B,H,T,W(+1)]`` each) on the float32 scan kernels, the payload cut into
+    pieces within their budgets."""
     parts = [[] for _ in retentions]
-    for start, stop, u in _scan_pieces(int(payload.shape[-1]), unit, len(retentions), int(query.shape[-1])):
-        outs = _scan.scan_views_f32(query, keys, payload[..., start:stop].contiguous(), int(u), stale, retentions)
+    for start, stop, u in _pieces(int(payload.shape[-1]), unit, int(query.shape[-1])):
+        outs = _scan.linattn_views(query, keys, payload[..., start:stop].contiguous(), tuple(retentions),
+                                   append_unit=bool(u), stale=tuple(stale))
         for i, o in enumerate(outs):
             parts[i].append(o)
     return [p[0] if len(p) == 1 else torch.cat(p, dim=-1) for p in parts]

@@ -269,10 +269,15 @@ class ThetaScanCore(nn.Module):
         rot, base = self._rot, self.cfg.rope.base
         gn = self.cfg.gn
         eps = 1e-6 if gn.damping is None else float(gn.damping)
+        # Deeper nets and swiglu (gn_deep) keep every product in plain f32:
+        # their retention gradients amplify a 2^-11 perturbation of q and k by
+        # ~40x, beyond what TF32 projections leave within tolerance.
+        deep = self.cfg.depth > 1 or gn.nonlinearity == "swiglu"
+        lin = F.linear if deep else tf32_linear
         if self.cfg.key_value_heads is None and not self.cfg.share_key_query:
             # fused projection, then RoPE + L2 of q and k in one row kernel
             from . import ops  # noqa: F401  (registers the operators)
-            qkv = tf32_linear(xf, self.proj_qkv.weight)
+            qkv = lin(xf, self.proj_qkv.weight)
             if rot:
                 cos, sin = _rope_tables(T, rot, float(base), str(x.device))
             else:
@@ -295,14 +300,15 @@ class ThetaScanCore(nn.Module):
                         _set_param(self, n, saved[n])
                 return q.contiguous(), k.contiguous(), v.contiguous()
 
-            q, k, v = per_token(qkv_fn, xf, *[params[n] for n in names])
+            ws = [params[n] for n in names]
+            q, k, v = qkv_fn(xf, *ws) if deep else per_token(qkv_fn, xf, *ws)
             q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         log_alphas, etas = self.fade()
         nonlin = "relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity
         mode = self.spec.mode if log_alphas is not None else "sum"
-        if self.cfg.depth == 1 and nonlin != "swiglu":
+        if not deep:
             W1, W2 = self.effective_weights()
             y = gn_core(q, k, v, W1, W2, None if self.Wg is None else self.Wg[0], nonlin=nonlin,
                         read_norm=gn.read_normalization != "none",
@@ -320,9 +326,9 @@ class ThetaScanCore(nn.Module):
                         log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps)
         y = y.transpose(1, 2)
         if self.ogate is not None:
-            g = tf32_linear(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)
+            g = lin(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)
             y = F.silu(g).view(B, T, H, d) * y
-        y = tf32_linear(y.reshape(B, T, H * d), self.proj_out.weight)
+        y = lin(y.reshape(B, T, H * d), self.proj_out.weight)
         return y.to(x.dtype)
 
     def _forward_f32(self, x, shard):
