@@ -18,7 +18,7 @@ import torch
 import torch.nn.functional as F
 
 from oracle import scan as oracle_scan
-from thetascan_b200 import gn_deep
+from thetascan_b200 import gn_deep, seqpar
 from thetascan_b200.config import ThetaScanConfig
 from thetascan_b200.mixer import ThetaScan, _l2, _rope
 
@@ -46,31 +46,43 @@ def oracle_views(q, k, v, retentions, chunk=512, *, append_unit=False, stale=Non
     return tuple((outs[-1] - o if st else o).to(q.dtype) for o, st in zip(outs[:-1], stale))
 
 
-def run_case(case, monkeypatch):
-    monkeypatch.setattr(gn_deep, "_scan", types.SimpleNamespace(linattn_views=oracle_views))
-    cfg = ThetaScanConfig.from_dict(case["public_config"])
-    module = ThetaScan(cfg)
-    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
-                            if not n.startswith("_expand_")})
-    core = module._core
+def _mixer(core, cfg, x, shard=None):
+    """The GN mixer's forward around ``gn_deep._core`` (float32 projections,
+    RoPE from the shard's first position, L2 norm, gate, out projection)."""
     gn = cfg.gn
-    x = case["x"].float().requires_grad_(True)
     B, T, _ = x.shape
     H, d = core.n_heads, core.head_dim
+    pos0 = 0 if shard is None else shard.rank * T
     q, k, v = core.project(x)
-    q, k = _l2(_rope(q, core._rot, cfg.rope.base)), _l2(_rope(k, core._rot, cfg.rope.base))
+    q, k = _l2(_rope(q, core._rot, cfg.rope.base, pos0)), _l2(_rope(k, core._rot, cfg.rope.base, pos0))
     log_alphas, etas = core.fade()
     layers = [core.effective_weights(l) + (None if core.Wg is None else core.Wg[l],) for l in range(cfg.depth)]
     y = gn_deep._core(q, k, v.contiguous(), layers,
                       "relu2" if gn.nonlinearity == "relu2_threshold" else gn.nonlinearity,
                       gn.nonlinearity == "relu2_threshold", gn.read_normalization != "none",
                       gn.read_normalization == "both_feature_mass", log_alphas, etas,
-                      core.spec.mode if log_alphas is not None else "sum", 1e-6, gn.jacobian_steps)
+                      core.spec.mode if log_alphas is not None else "sum", 1e-6, gn.jacobian_steps, shard)
     y = y.transpose(1, 2)
     if core.ogate is not None:
         lin = core.ogate.g.lin
         y = F.silu(F.linear(x, lin.weight, lin.bias)).view(B, T, H, d) * y
-    y = F.linear(y.reshape(B, T, H * d), core.proj_out.weight)
+    return F.linear(y.reshape(B, T, H * d), core.proj_out.weight)
+
+
+def run_case(case, monkeypatch, P=None):
+    monkeypatch.setattr(gn_deep, "_scan", types.SimpleNamespace(linattn_views=oracle_views))
+    cfg = ThetaScanConfig.from_dict(case["public_config"])
+    module = ThetaScan(cfg)
+    module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                            if not n.startswith("_expand_")})
+    x = case["x"].float().requires_grad_(True)
+    if P is None:
+        y = _mixer(module._core, cfg, x)
+    else:
+        runner = seqpar.SequentialShards(P)
+        L = x.shape[1] // P
+        y = torch.cat([_mixer(module._core, cfg, x[:, r * L:(r + 1) * L], runner.shard(r)) for r in range(P)],
+                      dim=1)
     (y.double() * case["out_weight"]).sum().backward()
     return module, x, y
 
@@ -83,6 +95,23 @@ def test_gn_deep_algebra_matches_reference_fixture(name, monkeypatch):
     assert rel_err(x.grad, case["x_grad"]) < TOL
     grads = dict(module._core.named_parameters())
     assert set(case["grads"]) <= set(grads)
+    for n, want in case["grads"].items():
+        assert rel_err(grads[n].grad, want) < TOL, n
+
+
+@pytest.mark.parametrize("name,P", [("gn_depth2_both_bank", 2), ("gn_depth2_swiglu_stale", 4),
+                                    ("gn_swiglu_jac2_bank", 2)])
+def test_gn_sequence_shards_match_reference_fixture(name, P, monkeypatch):
+    """The GN family on P sequence shards run one after another
+    (``SequentialShards``): every read of every layer enters with the earlier
+    shards' state (``seqpar.sharded_reads``; both stages' streams are
+    write-side), and the concatenated output and all gradients equal the
+    reference's unsharded fixture."""
+    case = torch.load(os.path.join(GOLDEN, "gn_deep_cases.pt"), weights_only=False)[name]
+    module, x, y = run_case(case, monkeypatch, P)
+    assert rel_err(y, case["y"]) < TOL
+    assert rel_err(x.grad, case["x_grad"]) < TOL
+    grads = dict(module._core.named_parameters())
     for n, want in case["grads"].items():
         assert rel_err(grads[n].grad, want) < TOL, n
 

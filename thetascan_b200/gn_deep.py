@@ -34,6 +34,7 @@ import torch.nn.functional as F
 
 from . import scan as _scan
 from .gn import _views
+from .seqpar import sharded_reads
 
 _ACTS = ("relu2", "silu", "tanh", "swiglu")
 
@@ -185,20 +186,26 @@ def _pieces(width, unit, dk):
     return [(s, min(width, s + step), unit and min(width, s + step) >= width) for s in range(0, width, step)]
 
 
-def _reads(query, keys, payload, unit, retentions, stale):
+def _reads(query, keys, payload, unit, retentions, stale, shard=None):
     """Reads of one stream set through the views ``retentions`` (f32
     ``[B,H,T,W(+1)]`` each) on the float32 scan kernels, the payload cut into
-    pieces within their budgets."""
+    pieces within their budgets; on a sequence shard each piece enters with
+    the earlier shards' state (:func:`thetascan_b200.seqpar.sharded_reads`)."""
     parts = [[] for _ in retentions]
     for start, stop, u in _pieces(int(payload.shape[-1]), unit, int(query.shape[-1])):
-        outs = _scan.linattn_views(query, keys, payload[..., start:stop].contiguous(), tuple(retentions),
-                                   append_unit=bool(u), stale=tuple(stale))
+        piece = payload[..., start:stop].contiguous()
+        if shard is None:
+            outs = _scan.linattn_views(query, keys, piece, tuple(retentions), append_unit=bool(u),
+                                       stale=tuple(stale))
+        else:
+            outs = sharded_reads(shard, _scan.linattn_views, query, keys, piece, tuple(retentions),
+                                 append_unit=bool(u), stale=tuple(stale))
         for i, o in enumerate(outs):
             parts[i].append(o)
     return [p[0] if len(p) == 1 else torch.cat(p, dim=-1) for p in parts]
 
 
-def _read(net, q, la1, la2, retentions, stale, read_norm, read_norm_w1, steps):
+def _read(net, q, la1, la2, retentions, stale, read_norm, read_norm_w1, steps, shard=None):
     """Every view's read ``f_theta_t(q_t)`` (engine.py:345-544)."""
     L, m, eps = net.L, net.m, net.eps
     V = len(retentions)
@@ -218,14 +225,14 @@ def _read(net, q, la1, la2, retentions, stale, read_norm, read_norm_w1, steps):
                 # pre-activation address [g | 1] (engine.py:475-506)
                 pre0 = net._threshold(_rms(a, eps)[0], Wg)
                 h0 = _act("relu2", pre0)
-                corr = _reads(h0, la2[l][0], la1[l][1], True, rets, flags)
+                corr = _reads(h0, la2[l][0], la1[l][1], True, rets, flags, shard)
                 pres = [a + c[..., :m] / (c[..., m:m + 1] + eps) for c in corr]
                 bs = [b] * len(idx)
             else:
                 pres, bs = [a] * len(idx), [b] * len(idx)
                 for it in range(steps):
                     keys, vals = la1[it * L + l]
-                    corr = _reads(x, keys, vals, False, rets, flags)
+                    corr = _reads(x, keys, vals, False, rets, flags, shard)
                     pres = [p + c[..., :m] for p, c in zip(pres, corr)]
                     if b is not None:
                         bs = [bb + c[..., m:] for bb, c in zip(bs, corr)]
@@ -233,13 +240,13 @@ def _read(net, q, la1, la2, retentions, stale, read_norm, read_norm_w1, steps):
                 h = net.features(pre, bb, Wg)[1]
                 base = _hm(W2, h)
                 if read_norm:
-                    c = _reads(h, la2[l][0], la2[l][1], True, [retentions[i]], [stale[i]])[0]
+                    c = _reads(h, la2[l][0], la2[l][1], True, [retentions[i]], [stale[i]], shard)[0]
                     mem = c[..., :-1] / (c[..., -1:] + eps)
                 else:
                     mem = None
                     for it in range(steps):
                         keys, vals = la2[it * L + l]
-                        c = _reads(h, keys, vals, False, [retentions[i]], [stale[i]])[0]
+                        c = _reads(h, keys, vals, False, [retentions[i]], [stale[i]], shard)[0]
                         mem = c if mem is None else mem + c
                 new[i] = x + net.s * (base + mem)
         xs = new
@@ -247,7 +254,7 @@ def _read(net, q, la1, la2, retentions, stale, read_norm, read_norm_w1, steps):
 
 
 def gn_deep(q, k, v, layers, *, nonlin="relu2", thresholded=False, read_norm=False, read_norm_w1=False,
-            log_alphas=None, etas=None, mode="fast", eps=1e-6, steps=1):
+            log_alphas=None, etas=None, mode="fast", eps=1e-6, steps=1, shard=None):
     """GN mixer core ``[B,H,T,d]`` f32 of a net of any depth.
 
     ``q, k, v`` after RoPE / L2 norm; ``layers`` the per-layer effective
@@ -255,7 +262,10 @@ def gn_deep(q, k, v, layers, *, nonlin="relu2", thresholded=False, read_norm=Fal
     ``[H,m,d]``, the learned threshold ``[H,m,1]`` (``thresholded``) or None;
     ``nonlin`` relu2 / silu / tanh / swiglu; ``log_alphas`` / ``etas``
     ``[J,H]`` a temporal bank (``mode`` fast or stale); ``steps`` the
-    Jacobian steps of the write.  Differentiable in every tensor argument."""
+    Jacobian steps of the write; ``shard`` (a
+    :class:`thetascan_b200.seqpar.SeqShard`) makes ``q, k, v`` one contiguous
+    slice of longer sequences, every read entering with the earlier slices'
+    state (one exchange per read).  Differentiable in every tensor argument."""
     for x in (q, k, v):
         if not x.is_cuda:
             raise RuntimeError("b200 backend requires CUDA tensors")
@@ -269,10 +279,11 @@ def gn_deep(q, k, v, layers, *, nonlin="relu2", thresholded=False, read_norm=Fal
     if J:
         _views(mode, J)
     return _core(q, k, v, layers, nonlin, thresholded, read_norm, read_norm_w1, log_alphas, etas, mode, eps,
-                 steps)
+                 steps, shard)
 
 
-def _core(q, k, v, layers, nonlin, thresholded, read_norm, read_norm_w1, log_alphas, etas, mode, eps, steps):
+def _core(q, k, v, layers, nonlin, thresholded, read_norm, read_norm_w1, log_alphas, etas, mode, eps, steps,
+          shard=None):
     """The GN core after the argument checks: write, reads of every view and
     the bank blend."""
     J = 0 if log_alphas is None else int(log_alphas.shape[0])
@@ -282,7 +293,7 @@ def _core(q, k, v, layers, nonlin, thresholded, read_norm, read_norm_w1, log_alp
     la1, la2 = net.write(k, v, steps)
     retentions = [None] + [log_alphas[j].float() for j in range(J)]
     stale = [False] + [mode == "stale"] * J
-    ys = _read(net, q, la1, la2, retentions, stale, bool(read_norm), bool(read_norm_w1), steps)
+    ys = _read(net, q, la1, la2, retentions, stale, bool(read_norm), bool(read_norm_w1), steps, shard)
     y = ys[0]
     if J and mode == "stale":
         # y - sum_j eta_j (y_stale_j - y_base); y_base reads an empty memory,

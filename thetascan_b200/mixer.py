@@ -113,11 +113,13 @@ def _rope_width(d: int, mode: str, frac: float) -> int:
     return max_rot if mode == "full" else min(max_rot, max(2, int(d * frac) // 2 * 2))
 
 
-def _rope(x: torch.Tensor, rot: int, base: float) -> torch.Tensor:
-    """Adjacent-pair rotation of the first ``rot`` channels with f32 phases (rope.py:57-72)."""
+def _rope(x: torch.Tensor, rot: int, base: float, pos0: int = 0) -> torch.Tensor:
+    """Adjacent-pair rotation of the first ``rot`` channels with f32 phases
+    (rope.py:57-72); ``pos0`` is the position of the first token."""
     if rot == 0:
         return x
-    cos, sin = _rope_tables(x.shape[2], rot, float(base), str(x.device))
+    cos, sin = _rope_tables(pos0 + x.shape[2], rot, float(base), str(x.device))
+    cos, sin = cos[pos0:], sin[pos0:]
     even, odd = x[..., 0:rot:2], x[..., 1:rot:2]
     rotated = torch.stack((even * cos - odd * sin, even * sin + odd * cos), dim=-1).flatten(-2)
     return torch.cat((rotated, x[..., rot:]), dim=-1)
@@ -257,8 +259,6 @@ class ThetaScanCore(nn.Module):
         and the GN core on the row kernels, every sequence read on the scan
         kernels (:mod:`thetascan_b200.gn`)."""
         from .gn import gn_core, per_token, tf32_linear
-        if shard is not None:
-            raise NotImplementedError("thetascan_b200: sequence shards of the GN family are not built")
         B, T, _ = x.shape
         H, d = self.n_heads, self.head_dim
         # The write's solve divides by ||k||^2-weighted terms and amplifies
@@ -272,14 +272,18 @@ class ThetaScanCore(nn.Module):
         # Deeper nets and swiglu (gn_deep) keep every product in plain f32:
         # their retention gradients amplify a 2^-11 perturbation of q and k by
         # ~40x, beyond what TF32 projections leave within tolerance.
-        deep = self.cfg.depth > 1 or gn.nonlinearity == "swiglu"
+        # Sequence shards take the same path, every read entering with the
+        # earlier shards' state.
+        deep = self.cfg.depth > 1 or gn.nonlinearity == "swiglu" or shard is not None
         lin = F.linear if deep else tf32_linear
+        pos0 = 0 if shard is None else shard.rank * T
         if self.cfg.key_value_heads is None and not self.cfg.share_key_query:
             # fused projection, then RoPE + L2 of q and k in one row kernel
             from . import ops  # noqa: F401  (registers the operators)
             qkv = lin(xf, self.proj_qkv.weight)
             if rot:
-                cos, sin = _rope_tables(T, rot, float(base), str(x.device))
+                cos, sin = _rope_tables(pos0 + T, rot, float(base), str(x.device))
+                cos, sin = cos[pos0:], sin[pos0:]
             else:
                 cos = sin = qkv.new_empty(0)
             q, k, v = torch.ops.thetascan_b200.gn_prep_fwd(qkv, cos, sin, rot, H, eps)
@@ -302,7 +306,7 @@ class ThetaScanCore(nn.Module):
 
             ws = [params[n] for n in names]
             q, k, v = qkv_fn(xf, *ws) if deep else per_token(qkv_fn, xf, *ws)
-            q, k = _l2(_rope(q, rot, base), eps), _l2(_rope(k, rot, base), eps)
+            q, k = _l2(_rope(q, rot, base, pos0), eps), _l2(_rope(k, rot, base, pos0), eps)
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         log_alphas, etas = self.fade()
@@ -315,15 +319,16 @@ class ThetaScanCore(nn.Module):
                         read_norm_w1=gn.read_normalization == "both_feature_mass",
                         log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps)
         else:
-            # deeper nets and the swiglu activation (gn_deep: per-token maps
-            # in f32 PyTorch, every read on the scan kernels)
+            # deeper nets, the swiglu activation and sequence shards (gn_deep:
+            # per-token maps in f32 PyTorch, every read on the scan kernels)
             from .gn_deep import gn_deep
             layers = [self.effective_weights(l) + (None if self.Wg is None else self.Wg[l],)
                       for l in range(self.cfg.depth)]
             y = gn_deep(q, k, v, layers, nonlin=nonlin, thresholded=gn.nonlinearity == "relu2_threshold",
                         read_norm=gn.read_normalization != "none",
                         read_norm_w1=gn.read_normalization == "both_feature_mass",
-                        log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps)
+                        log_alphas=log_alphas, etas=etas, mode=mode, eps=eps, steps=gn.jacobian_steps,
+                        shard=shard)
         y = y.transpose(1, 2)
         if self.ogate is not None:
             g = lin(xf, self.ogate.g.lin.weight, self.ogate.g.lin.bias)
@@ -333,25 +338,33 @@ class ThetaScanCore(nn.Module):
 
     def _forward_f32(self, x, shard):
         """Kernel family on a float32 input: float32 throughout, the sequence
-        reads on the float32 scan kernels (:mod:`thetascan_b200.precise`)."""
+        reads on the float32 scan kernels (:mod:`thetascan_b200.precise`); on
+        a sequence shard every read enters with the earlier shards' state."""
         from .precise import kernel_core_f32
-        if shard is not None:
-            raise NotImplementedError("thetascan_b200: sequence shards run bf16 streams; pass a bf16 input")
         B, T, _ = x.shape
         H, d = self.n_heads, self.head_dim
         rot, base = self._rot, self.cfg.rope.base
+        pos0 = 0 if shard is None else shard.rank * T
         q, k, v = self.project(x)
-        q, k = _l2(_rope(q, rot, base)), _l2(_rope(k, rot, base))
+        q, k = _l2(_rope(q, rot, base, pos0)), _l2(_rope(k, rot, base, pos0))
         if self.vmlp_in is not None:
             v = v + self.vmlp_out(F.silu(self.vmlp_in(v)))
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
-        y = kernel_core_f32(q, k, v.contiguous(), W1, W2, self.spec, log_alphas=log_alphas, etas=etas,
+        y = kernel_core_f32(q, k, v.contiguous(), W1, W2, self.spec, log_alphas=log_alphas, etas=etas, shard=shard,
                             **self.kernel_controls()).transpose(1, 2)
         if self.ogate is not None:
             lin = self.ogate.g.lin
             y = y * F.silu(F.linear(x, lin.weight, lin.bias).view(B, T, H, d))
         return F.linear(y.reshape(B, T, H * d), self.proj_out.weight)
+
+    def _fused_shards(self) -> bool:
+        """Whether sequence shards run the fused bf16 core (two scan stages
+        around one exchange, kernel.kernel_core_sharded): the fused q/k/v
+        projection, no value MLP, the key-mass read, the plain sum or a fast
+        bank, no relative sparsity."""
+        return (self.proj_qkv is not None and self.vmlp_in is None and self.spec.read == "key_mass"
+                and self.spec.mode != "stale" and self.spec.sparsity == "none")
 
     def effective_weights(self, layer: int = 0):
         """``U W1`` and ``W2 D`` of one layer (block.py:546-567)."""
@@ -434,6 +447,10 @@ class ThetaScanCore(nn.Module):
             return self._forward_gn(x, shard)
         if x.dtype == torch.float32:
             return self._forward_f32(x, shard)
+        if shard is not None and not self._fused_shards():
+            # sequence shards of the other views and reads: the float32 path,
+            # each scan entering with the earlier shards' state
+            return self._forward_f32(x.float(), shard).to(x.dtype)
         B, T, _ = x.shape
         H, d = self.n_heads, self.head_dim
         out_dtype = x.dtype
@@ -441,9 +458,6 @@ class ThetaScanCore(nn.Module):
         W1, W2 = self.effective_weights()
         log_alphas, etas = self.fade()
         if shard is not None:
-            if self.proj_qkv is None or self.vmlp_in is not None or self.spec.read != "key_mass":
-                raise NotImplementedError("sequence shards need the fused q/k/v projection without a value MLP "
-                                          "and the key-mass read")
             qkv = F.linear(xb, self.proj_qkv.weight.to(torch.bfloat16))
             pos0 = shard.rank * T
             cos = sin = None

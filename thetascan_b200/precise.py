@@ -26,6 +26,7 @@ import torch
 import torch.nn.functional as F
 
 from .scan import linattn_views
+from .seqpar import sharded_reads
 
 
 def _rmsnorm(a: torch.Tensor, eps: float) -> torch.Tensor:
@@ -107,20 +108,45 @@ def features(x, W1, spec, ctl) -> torch.Tensor:
     raise NotImplementedError(f"b200 float32 path: feature map {spec.kind!r}")
 
 
-def _mass(phi_k, retention, stale):
+def _views_fn(shard):
+    """The multi-view scan of this call: the float32 kernels over the whole
+    sequence, or, on a sequence shard, the shard's reads entering with the
+    earlier shards' state (payloads cut to the kernels' 256 columns with the
+    exchange's unit column)."""
+    if shard is None:
+        return linattn_views
+
+    def views(query, keys, payload, rets, append_unit=False, stale=None):
+        width = payload.shape[-1]
+        step = 128 if width + 1 > 256 else width
+        parts = []
+        for start in range(0, width, step):
+            unit = append_unit and start + step >= width
+            piece = payload[..., start:start + step].contiguous()
+            parts.append(sharded_reads(shard, linattn_views, query, keys, piece, rets, append_unit=unit,
+                                       stale=stale))
+        return [p[0] if len(p) == 1 else torch.cat(p, dim=-1) for p in zip(*parts)]
+
+    return views
+
+
+def _mass(phi_k, retention, stale, views=linattn_views):
     """Per-feature key mass of one view, ``sum_{j<=t} w(t-j) phi_k[j]``
     (view.mass_cum, interface.py:216-230, 278-279, 306-307), as a scan of
     ``phi_k`` with unit queries and keys."""
     one = phi_k.new_ones(*phi_k.shape[:3], 1)
-    return linattn_views(one, one, phi_k, (retention,), stale=(stale,))[0]
+    return views(one, one, phi_k, (retention,), stale=(stale,))[0]
 
 
 def kernel_core_f32(q, k, v, W1, W2, spec, *, threshold=None, score_bias=None, gain=None, spline_scale=None,
-                    log_alphas=None, etas=None, relative_threshold=None, sparse_blend=None):
+                    log_alphas=None, etas=None, relative_threshold=None, sparse_blend=None, shard=None):
     """``y = q + W2 phi(q) + blended normalized memory``, float32, ``[B,H,T,d]``.
 
     Same arguments as :func:`thetascan_b200.kernel.kernel_core` with float32
-    streams; ``log_alphas``/``etas`` are ``[J,H]`` for a bank."""
+    streams; ``log_alphas``/``etas`` are ``[J,H]`` for a bank.  ``shard`` (a
+    :class:`thetascan_b200.seqpar.SeqShard`) makes the streams one contiguous
+    slice of longer sequences: every view and read normalisation, each scan
+    entering with the earlier slices' state."""
     for x in (q, k, v):
         if not x.is_cuda:
             raise RuntimeError("b200 backend requires CUDA tensors")
@@ -137,16 +163,17 @@ def kernel_core_f32(q, k, v, W1, W2, spec, *, threshold=None, score_bias=None, g
     J = 0 if log_alphas is None else log_alphas.shape[0]
     rets = (None,) + tuple(log_alphas[j] for j in range(J))
     stale = (False,) + (spec.mode == "stale",) * J
+    views = _views_fn(shard)
     if spec.read == "key_mass":
-        reads = linattn_views(phi_q, phi_k, v, rets, append_unit=True, stale=stale)
+        reads = views(phi_q, phi_k, v, rets, append_unit=True, stale=stale)
         mems = [r[..., :-1] / (r[..., -1:] + eps) for r in reads]
     elif spec.read == "feature_mass":
         mems = []
         for ret, st in zip(rets, stale):
-            query = phi_q / (_mass(phi_k, ret, st) + eps)
-            mems.append(linattn_views(query, phi_k, v, (ret,), stale=(st,))[0])
+            query = phi_q / (_mass(phi_k, ret, st, views) + eps)
+            mems.append(views(query, phi_k, v, (ret,), stale=(st,))[0])
     elif spec.read == "none":
-        mems = list(linattn_views(phi_q, phi_k, v, rets, stale=stale))
+        mems = list(views(phi_q, phi_k, v, rets, stale=stale))
     else:
         raise ValueError(f"kernel_core: unknown read normalization {spec.read!r}")
     outs = [base + mem for mem in mems]

@@ -134,23 +134,77 @@ def exchange(shard: SeqShard, las: Sequence[torch.Tensor | None]):
     return between
 
 
+def sharded_reads(shard: SeqShard, scan, query, keys, payload, retentions, *, append_unit: bool = False,
+                  stale=None) -> list[torch.Tensor]:
+    """Reads of one shard of a sequence through several views, entering with
+    the state of the earlier shards: any stream set, any view.
+
+    ``scan`` has the signature of :func:`thetascan_b200.scan.linattn_views`
+    (the shard's own reads from a zero state); ``retentions`` / ``stale`` /
+    ``append_unit`` mean what they mean there.  A stale view (weights
+    ``1 - alpha^(t-i)``) is the plain read minus the decayed one, as the
+    reference forms it (FadeStale, interface.py:251-279), so the exchange
+    only ever carries plain and decayed states: one all-gather of
+    ``[B,H,R',Dk,Dv+1]`` totals per call, ``R'`` the distinct underlying
+    retentions."""
+    stale = tuple(bool(x) for x in stale) if stale is not None else (False,) * len(retentions)
+    base: list = []
+
+    def slot(r):
+        for i, b in enumerate(base):
+            if b is r:
+                return i
+        base.append(r)
+        return len(base) - 1
+
+    plan = [(slot(None), slot(r)) if st else (slot(r), None) for r, st in zip(retentions, stale)]
+    reads = list(scan(query, keys, payload, tuple(base), append_unit=True))
+    totals = shard.gather(shard_totals(keys, payload, base))
+    if shard.rank == 0:
+        tie = 0.0 * totals[0].sum()   # rank 0 still joins the gather's backward
+        reads[0] = reads[0] + tie.to(reads[0].dtype)
+    else:
+        S = entering_state(totals, base, query.shape[2], shard.rank)
+        reads = [r.to(S.dtype) for r in add_entering(reads, query, S, base)]
+    out = []
+    for a, b in plan:
+        o = reads[a] if b is None else reads[a] - reads[b]
+        out.append(o if append_unit else o[..., :-1])
+    return out
+
+
 class SequentialShards:
     """Runs the shards of one sequence one after another in this process:
     the stand-in for a process group when all shards share one device (tests,
-    single-GPU emulation).  Shard p sees the totals of shards < p computed
-    earlier in the same autograd graph; later totals are zeros it never
-    uses."""
+    single-GPU emulation).  The k-th exchange of shard p sees the k-th totals
+    of shards < p, computed earlier in the same autograd graph; later totals
+    are zeros it never uses."""
 
     def __init__(self, world: int):
         self.world = world
-        self.totals: list[torch.Tensor] = []
+        self.calls: list[list[torch.Tensor]] = []
+        self.next_rank = 0
+
+    @property
+    def totals(self) -> list[torch.Tensor]:
+        """The first exchange's totals, in rank order."""
+        return self.calls[0] if self.calls else []
 
     def shard(self, rank: int) -> SeqShard:
-        if rank != len(self.totals):
+        if rank != self.next_rank:
             raise ValueError("SequentialShards: run the shards in rank order")
+        self.next_rank += 1
+        count = [0]
 
         def gather(U):
-            self.totals.append(U)
-            return self.totals + [torch.zeros_like(U)] * (self.world - len(self.totals))
+            k = count[0]
+            count[0] += 1
+            if k == len(self.calls):
+                self.calls.append([])
+            got = self.calls[k]
+            if len(got) != rank:
+                raise ValueError("SequentialShards: every shard must exchange the same number of times, in order")
+            got.append(U)
+            return got + [torch.zeros_like(U)] * (self.world - len(got))
 
         return SeqShard(rank, self.world, gather)
