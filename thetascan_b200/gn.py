@@ -236,6 +236,21 @@ def _hm(W, x, tf32=False):
         torch.backends.cuda.matmul.allow_tf32 = saved
 
 
+def _hm_acc(base, W, x, tf32=False):
+    """``base + W[h] x[b,h,t]`` per head, the sum formed by the GEMM itself
+    (beta = 1: no separate elementwise pass over ``[B,H,T,o]``)."""
+    B, H, T, i = x.shape
+    o = W.shape[1]
+    Wt = W.transpose(-1, -2).unsqueeze(0).expand(B, H, i, o).reshape(B * H, i, o)
+    saved = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32)
+    try:
+        out = torch.baddbmm(base.contiguous().view(B * H, T, o), x.contiguous().view(B * H, T, i), Wt)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = saved
+    return out.view(B, H, T, o)
+
+
 def _hm_wgrad(gy, x, tf32=False):
     """``sum_{b,t} gy[b,h,t] x[b,h,t]^T`` per head, ``[H,o,i]``: the token axis
     cut into chunks that run as parallel batched products, summed after in
@@ -368,8 +383,8 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     tau_grad = None if tau is None else torch.zeros(H, m, dtype=torch.float32, device=q.device)
     dla = torch.zeros(J + 1, H, dtype=torch.float32, device=q.device)
     deta = None if J == 0 else torch.zeros(J, H, dtype=torch.float32, device=q.device)
-    # q enters every view and the zero-memory base with coefficients that sum to one
-    dq = dy.clone()
+    # q enters every view and the zero-memory base with coefficients that sum
+    # to one: its direct gradient is dy itself (added with the last product)
     dys = [dy]
     dy_base = None
     if J:
@@ -386,8 +401,7 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
             for j in range(J):
                 deta[j] = (dy * (ys[1 + j] - ys[0])).sum(dim=(0, 2, 3))
     dW2 = torch.zeros_like(W2)
-    dh_k = run.new(m, zero=True)
-    dlam = run.new(d, zero=True)
+    dh_k = dlam = None
     da_q = run.new(m)
     R1 = [torch.cat([p[3][i] for p in st1], dim=-1) if len(st1) > 1 else st1[0][3][i] for i in range(J + 1)]
     if steps == 2:
@@ -403,8 +417,8 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         else:
             dC = dys[s]
         dhq, dhk_s, dlam_s, dla_s = run.scan_bwd([dC], hqb, h_kb, lamb, st2, [las[s]], [stale[s]])
-        dh_k += dhk_s
-        dlam += dlam_s
+        dh_k = dhk_s if dh_k is None else dh_k + dhk_s
+        dlam = dlam_s if dlam is None else dlam + dlam_s
         dla[s] += dla_s[0]
         if st2b is not None:
             dhq2, dh2_s, dlam2_s, dla2_s = run.scan_bwd([dC], hqb, two["h2b"], two["lam2b"], st2b, [las[s]],
@@ -413,7 +427,7 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
             dh2 += dh2_s
             dlam2 += dlam2_s
             dla[s] += dla2_s[0]
-        dhq = dhq + _hm(W2t, dys[s], run.tf32)
+        dhq = _hm_acc(dhq, W2t, dys[s], run.tf32)
         dW2 += _hm_wgrad(dys[s], hq, run.tf32)
         run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, R1[s], dhq], [da_q, dR1[s]],
                  flags=int(read_norm_w1) | (2 if s else 0), dtau=tau_grad)
@@ -431,10 +445,10 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
     if read_norm_w1:
         dh_k += dk1
         run.rows(_lib.TS_GN_QUERY_PRE_BWD, [dq1, a_q], [da_q], flags=2, dtau=tau_grad)
+        dq = _hm_acc(dy, W1.transpose(1, 2), da_q, run.tf32)
     else:
-        dq += dq1
         dk = dk1
-    dq += _hm(W1.transpose(1, 2), da_q, run.tf32)
+        dq = _hm_acc(dy + dq1, W1.transpose(1, 2), da_q, run.tf32)
     dW1 = _hm_wgrad(da_q, q, run.tf32)
     da_extra = None
     if steps == 2:
@@ -561,7 +575,7 @@ def _write_backward(run, k, v, W1, W2, streams, dh, dg, dlam, dtau, da_extra=Non
     run.rows(_lib.TS_GN_WRITE_PRE_BWD, [dh, dhO, ds2, dhh, dg, U, a_k], [da_k], dtau=dtau)
     if da_extra is not None:
         da_k = da_k + da_extra
-    dk = dk_w + _hm(W1.transpose(1, 2), da_k, run.tf32)
+    dk = _hm_acc(dk_w, W1.transpose(1, 2), da_k, run.tf32)
     return dk, dv, _hm_wgrad(da_k, k, run.tf32), dW2
 
 
