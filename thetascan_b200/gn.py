@@ -225,11 +225,9 @@ class _Run:
 def _hm(W, x, tf32=False):
     """Per-head linear map ``y[b,h,t] = W[h] x[b,h,t]`` (batched GEMM); with
     ``tf32`` on TF32 tensor cores (10-bit operand mantissas, f32
-    accumulation)."""
-    if not tf32:
-        return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
+    accumulation), else in f32 whatever the global TF32 setting."""
     saved = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32)
     try:
         return torch.matmul(x, W.transpose(-1, -2).unsqueeze(0))
     finally:
