@@ -279,39 +279,6 @@ def _qkv_views(qkv, H, d):
     return q, k, v
 
 
-def _shard_total(phi_k, v, las):
-    """State a shard leaves behind from a zero start, per retention:
-    ``U_r = sum_t e^{la_r (L-1-t)} phi_k(t)^T [v_t | 1 | 1]`` (the key-mass
-    columns twice, as the scan kernels carry them), f32 ``[B,H,R,m,d+2]``:
-    one batched GEMM over all retentions (bf16 operands, f32 accumulation and
-    result) instead of a pass of the tile chain."""
-    B, H, L, m = phi_k.shape
-    d = v.shape[-1]
-    back = (L - 1) - torch.arange(L, device=phi_k.device, dtype=torch.float32)
-    vaug = torch.cat([v.float(), torch.ones(B, H, L, MASS_COLS, dtype=torch.float32, device=v.device)], dim=-1)
-    cols = [vaug if la is None else vaug * torch.exp(la.float().view(1, H, 1, 1) * back.view(1, 1, L, 1))
-            for la in las]
-    rhs = torch.cat(cols, dim=-1).to(torch.bfloat16).view(B * H, L, -1)
-    U = torch.bmm(phi_k.reshape(B * H, L, m).transpose(1, 2), rhs, out_dtype=torch.float32)
-    return U.view(B, H, m, len(las), d + MASS_COLS).permute(0, 1, 3, 2, 4).contiguous()
-
-
-def _entering_grad(phi_q, douts, las):
-    """Gradient of a shard's entering state from its own reads: a read t
-    carries ``e^{la_r (t+1)} phi_q(t) S_r``, so
-    ``dS_r = sum_t e^{la_r (t+1)} phi_q(t)^T dout_r(t)``, f32
-    ``[B,H,R,m,w]`` (one batched GEMM per retention)."""
-    B, H, L, m = phi_q.shape
-    ahead = torch.arange(1, L + 1, device=phi_q.device, dtype=torch.float32)
-    lhs = phi_q.reshape(B * H, L, m).transpose(1, 2)
-    out = []
-    for la, dout in zip(las, douts):
-        w = dout if la is None else \
-            (dout.float() * torch.exp(la.float().view(1, H, 1, 1) * ahead.view(1, 1, L, 1))).to(torch.bfloat16)
-        out.append(torch.bmm(lhs, w.reshape(B * H, L, -1), out_dtype=torch.float32).view(B, H, m, -1))
-    return torch.stack(out, dim=2)
-
-
 class _ShardScan:
     """What the two autograd stages of a sequence shard share: the scan
     workspaces (forward and backward), the slots and the entering state."""
@@ -350,12 +317,14 @@ class _ShardStageA(torch.autograd.Function):
         dev = q.device
         las = [None] + ([] if log_alphas is None else
                         [log_alphas[j].detach().to(torch.float32).contiguous() for j in range(log_alphas.shape[0])])
+        R = len(las)
         slots = [torch.empty(B, H, T, d + MASS_COLS, dtype=torch.float32, device=dev) for _ in las]
+        U = torch.empty(B, H, R, m, d + MASS_COLS, dtype=torch.float32, device=dev)
         sa = _build_args(phi_q, phi_k, v, las, slots, MASS_COLS)
         ws = _workspace(lib, lib.ts_b200_scan_workspace_bytes, sa, dev)
-        # the shard total goes out before the scan runs (the scan itself runs
-        # once, in the second half, from the entering state)
-        U = _shard_total(phi_k, v, las)
+        sa.workspace, sa.workspace_bytes = ws.data_ptr(), ws.numel()
+        sa.final_state, sa.stage = U.data_ptr(), 1
+        _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
         hold.ws, hold.slots, hold.las, hold.phi_q, hold.phi_k = ws, slots, las, phi_q, phi_k
         hold.dlas = [None] + [torch.zeros(H, dtype=torch.float32, device=dev) for _ in las[1:]]
         ctx.hold, ctx.spec, ctx.prologue, ctx.H, ctx.ctl = hold, spec, prologue, H, ctl
@@ -379,11 +348,9 @@ class _ShardStageA(torch.autograd.Function):
         dev = q.device
         dqkv = torch.empty_like(qkv)
         dq, dk, dv = _qkv_views(dqkv, H, d)
-        # the scan backward in one call: the shard's reads from its entering
-        # state S, with dU as the gradient of the state it leaves behind
+        # scan, second half: reverse prefix from dU, then dq / dk / dv
         sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
-        sa.init_state = hold.S.data_ptr()
-        gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
         sg = _lib.ScanGradArgs()
         m = hold.phi_q.shape[-1]
         dphi_q = torch.empty(B, H, T, m, dtype=torch.bfloat16, device=dev)
@@ -395,21 +362,14 @@ class _ShardStageA(torch.autograd.Function):
             sg.dlog_alpha[i] = _ptr(hold.dlas[i])
         sg.dq, sg.dk = dphi_q.data_ptr(), dphi_k.data_ptr()
         sg.grad_dtype = _lib.TS_DTYPE_BF16
-        sg.workspace, sg.workspace_bytes = gws.data_ptr(), gws.numel()
+        sg.workspace, sg.workspace_bytes = hold.gws.data_ptr(), hold.gws.numel()
         if dU is None:
             dU = torch.zeros(B, H, len(hold.las), m, d + MASS_COLS, dtype=torch.float32, device=dev)
         dU = dU.float().contiguous()
         sg.dfinal_state = _ptr(dU)
+        sg.stage = 2
         _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
-        del gws
-        # The kernels differentiate <dU, F> with F the state leaving the shard
-        # from S, F = U + e^{la L} S; the exchange sent U.  The one term of
-        # e^{la L} S that reaches an input is the log-retention's:
-        # L e^{la L} <dU, S>, removed here.
-        for r, la in enumerate(hold.las):
-            if la is not None:
-                spurious = (dU[:, :, r] * hold.S[:, :, r]).sum(dim=(0, 2, 3))
-                hold.dlas[r] -= float(T) * torch.exp(la * float(T)) * spurious
+        del hold.gws
         if dphi_q_out is not None:
             dphi_q = (dphi_q.float() + dphi_q_out.float()).to(torch.bfloat16)
         if dphi_k_out is not None:
@@ -456,7 +416,7 @@ class _ShardStageB(torch.autograd.Function):
         lib = _lib.load()
         hold.S = S.detach().float().contiguous()
         sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
-        sa.init_state = hold.S.data_ptr()
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
         _lib.check(lib.ts_b200_scan_fwd(ctypes.byref(sa), _stream()))
         B, H, T, d = y0.shape
         eta = None if etas is None else etas.detach().to(torch.float32).contiguous()
@@ -491,7 +451,19 @@ class _ShardStageB(torch.autograd.Function):
         deta = torch.zeros(n - 1, H, dtype=torch.float32, device=dev) if n > 1 else None
         ga.deta = _ptr(deta)
         _lib.check(lib.ts_b200_kread_bwd(ctypes.byref(ra), ctypes.byref(ga), _stream()))
-        dS = _entering_grad(hold.phi_q, hold.douts, hold.las)
+        sa = _build_args(hold.phi_q, hold.phi_k, v, hold.las, hold.slots, MASS_COLS, hold.ws)
+        sa.init_state, sa.stage = hold.S.data_ptr(), 2
+        hold.gws = _workspace(lib, lib.ts_b200_scan_bwd_workspace_bytes, sa, dev)
+        sg = _lib.ScanGradArgs()
+        for i in range(len(hold.las)):
+            sg.dout[i] = hold.douts[i].data_ptr()
+            sg.dlog_alpha[i] = _ptr(hold.dlas[i])
+        # dq / dk / dv are written by the second half (stage A's backward)
+        sg.grad_dtype = _lib.TS_DTYPE_BF16
+        sg.workspace, sg.workspace_bytes = hold.gws.data_ptr(), hold.gws.numel()
+        dS = torch.empty_like(hold.S)
+        sg.dinit_state, sg.stage = dS.data_ptr(), 1
+        _lib.check(lib.ts_b200_scan_bwd(ctypes.byref(sa), ctypes.byref(sg), _stream()))
         return None, dS, None, None, dy0, deta if ctx.has_eta else None
 
 
