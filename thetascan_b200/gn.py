@@ -433,7 +433,8 @@ def _gn_backward(dy, q, k, v, W1, W2, tau, log_alphas, etas, saved, nonlin, read
         hb = run.new(m)
         run.rows(_lib.TS_GN_FEATURES, [a_q, None], [hb])
         dW2 += _hm_wgrad(dy_base, hb, run.tf32)
-        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base, run.tf32)], [da_q, None], flags=2, dtau=tau_grad)
+        run.rows(_lib.TS_GN_FEATURES_BWD, [a_q, None, _hm(W2t, dy_base, run.tf32)], [da_q, None], flags=2,
+                 dtau=tau_grad)
     # stage 1
     if steps == 2:
         dR1 = [torch.cat([r, r], dim=-1) for r in dR1]

@@ -64,7 +64,8 @@ def _mixer(device: torch.device) -> None:
     torch.manual_seed(0)
     module = ThetaScan(cfg)
     with torch.no_grad():
-        module._core.W2[0].copy_(torch.randn(module._core.W2[0].shape, generator=torch.Generator().manual_seed(1)) * 0.2)
+        gen = torch.Generator().manual_seed(1)
+        module._core.W2[0].copy_(torch.randn(module._core.W2[0].shape, generator=gen) * 0.2)
     module = module.to(device)
     x = torch.randn(1, 160, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
     xg = x.to(device).requires_grad_(True)
