@@ -113,3 +113,59 @@ def test_sequential_shards_match_full_sequence():
         assert torch.allclose(o_got, o_ref, rtol=1e-10, atol=1e-10)
     for got, ref in zip(leaves, ref_grads):
         assert torch.allclose(got.grad, ref, rtol=1e-9, atol=1e-10)
+
+
+def _gn_worker(rank, port, out_dir, name):
+    """One rank of a two-rank GN mixer: its half of the sequence through the
+    deep / swiglu GN core, every read exchanging shard totals with the other
+    rank over the gloo group (several all-gathers per forward and their
+    backward collectives)."""
+    import sys
+    import types
+    sys.path.insert(0, os.path.dirname(__file__))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60))
+    try:
+        import test_gn_deep_host as host
+        from thetascan_b200 import gn_deep, seqpar
+        from thetascan_b200.config import ThetaScanConfig
+        from thetascan_b200.mixer import ThetaScan
+        gn_deep._scan = types.SimpleNamespace(linattn_views=host.oracle_views)
+        case = torch.load(os.path.join(host.GOLDEN, "gn_deep_cases.pt"), weights_only=False)[name]
+        cfg = ThetaScanConfig.from_dict(case["public_config"])
+        module = ThetaScan(cfg)
+        module.load_state_dict({"_core." + n: t.float() for n, t in case["params"].items()
+                                if not n.startswith("_expand_")})
+        L = case["x"].shape[1] // WORLD
+        sl = slice(rank * L, (rank + 1) * L)
+        x = case["x"][:, sl].float().clone().requires_grad_(True)
+        y = host._mixer(module._core, cfg, x, seqpar.nccl_shard())
+        (y.double() * case["out_weight"][:, sl]).sum().backward()
+        grads = {n: p.grad.clone() for n, p in module._core.named_parameters() if p.grad is not None}
+        for g in grads.values():
+            dist.all_reduce(g)
+        torch.save({"y": y.detach(), "x_grad": x.grad, "grads": grads}, os.path.join(out_dir, f"gn{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gn_shards_match_reference_fixture(tmp_path):
+    """A depth-2 swiglu GN mixer with a stale bank on two gloo ranks: the
+    concatenated outputs, the input gradient and the rank-summed parameter
+    gradients equal the reference's unsharded fixture (float32 per-token
+    maps, 1e-4)."""
+    name = "gn_depth2_swiglu_stale"
+    mp.spawn(_gn_worker, args=(_free_port(), str(tmp_path), name), nprocs=WORLD, join=True)
+    case = torch.load(os.path.join(os.path.dirname(__file__), "golden", "gn_deep_cases.pt"),
+                      weights_only=False)[name]
+    got = [torch.load(tmp_path / f"gn{r}.pt") for r in range(WORLD)]
+
+    def rel(a, b):
+        return float((a.double() - b.double()).abs().max() / b.double().abs().max())
+
+    assert rel(torch.cat([g["y"] for g in got], dim=1), case["y"]) < 1e-4
+    assert rel(torch.cat([g["x_grad"] for g in got], dim=1), case["x_grad"]) < 1e-4
+    for n, want in case["grads"].items():
+        assert rel(got[0]["grads"][n], want) < 1e-4, n
