@@ -155,6 +155,18 @@ def effective_weights(p, cfg):
     return W1, W2
 
 
+def layer_weights(p, cfg):
+    """Effective ``(W1, W2, Wg)`` of every block of a GN net (block.py:546-567)."""
+    out = []
+    for l in range(cfg.get("depth", 1)):
+        W1, W2 = p[f"W1.{l}"], p[f"W2.{l}"]
+        if cfg.get("feature_expansion", 1) > 1:
+            W1 = torch.matmul(p[f"_expand_w1_{l}"].to(W1.dtype), W1)
+            W2 = torch.matmul(W2, p[f"_expand_w2_{l}"].to(W2.dtype))
+        out.append((W1, W2, p.get(f"Wg.{l}")))
+    return out
+
+
 def feature_spec(p, cfg):
     """Kernel controls of block.py:408-456 as an oracle ``spec`` dict."""
     kind = cfg["kernel_kind"]
@@ -236,7 +248,15 @@ def mixer_forward(p, cfg, x, *, scan_fn=None):
     q, k = features.l2norm(q, eps), features.l2norm(k, eps)
     W1, W2 = effective_weights(p, cfg)
     log_alphas, etas = fade_parameters(p, cfg, x.dtype)
-    if cfg.get("write_rule", "kernel") == "gn":
+    if cfg.get("write_rule", "kernel") == "gn" and (cfg.get("depth", 1) > 1 or cfg["nonlin"] == "swiglu"
+                                                     or cfg.get("write_iters", 1) == 2):
+        from .gn import gn_core_net
+        y = gn_core_net(q, k, v, layer_weights(p, cfg), nonlin=cfg["nonlin"],
+                        learn_thresh=bool(cfg.get("learn_thresh")), read_norm=bool(cfg["read_norm"]),
+                        read_norm_w1=bool(cfg.get("read_norm_w1")), write_iters=cfg.get("write_iters", 1),
+                        log_alphas=log_alphas, etas=etas, mode=cfg.get("read_fade_mode", "fast"), eps=eps,
+                        chunk=cfg.get("scan_chunk", 512), scan_fn=scan_fn)
+    elif cfg.get("write_rule", "kernel") == "gn":
         from .gn import gn_core
         y = gn_core(q, k, v, W1, W2, p.get("Wg.0") if cfg.get("learn_thresh") else None,
                     nonlin=cfg["nonlin"], read_norm=bool(cfg["read_norm"]),

@@ -217,3 +217,32 @@ def test_sparse_mixer_oracle_matches_reference(name):
     assert rel(x.grad, case["x_grad"]) < 1e-6
     for n, g in case["grads"].items():
         assert rel(params[n].grad, g) < 1e-6, n
+
+
+@pytest.mark.parametrize("file,name", [("gn_deep_cases.pt", n) for n in (
+    "gn_swiglu_sum", "gn_swiglu_jac2_bank", "gn_depth2_both_bank", "gn_depth2_swiglu_stale",
+    "gn_depth3_threshold_w2_expanded", "gn_depth2_silu_jac2_bank2")] + [
+    ("gn_jac2_cases.pt", "gn_jac2_relu2_bank"), ("gn_jac2_cases.pt", "gn_jac2_threshold_sum")])
+def test_gn_net_oracle_matches_reference(file, name):
+    """The general GN net restatement (oracle/gn.py: depth > 1, swiglu, two
+    Jacobian steps) against the reference GN mixer's fixtures: output, input
+    gradient and every parameter gradient."""
+    case = _load(file)[name]
+    params = {n: t.to(torch.float64).clone().requires_grad_(t.is_floating_point() and not n.startswith("_"))
+              for n, t in case["params"].items()}
+    x = case["x"].to(torch.float64).clone().requires_grad_(True)
+    y = mixer.mixer_forward(params, dict(case["core"]), x)
+    (y * case["out_weight"].to(torch.float64)).sum().backward()
+
+    # float32 fixtures of float64 runs: the stored inputs are rounded, which
+    # these nets' solves amplify on small entries (up to 1e-3 of an entry,
+    # 1.5e-6 of a quantity's largest); the bound is on the largest entry
+    def rel(got, want):
+        want = want.to(torch.float64)
+        return float((got.detach() - want).abs().max() / want.abs().max())
+
+    tol = 1e-5
+    assert rel(y, case["y"]) < tol
+    assert rel(x.grad, case["x_grad"]) < tol
+    for n, g in case["grads"].items():
+        assert rel(params[n].grad, g) < tol, n
