@@ -10,7 +10,9 @@ reads and gradients on the CUDA cores) and the per-token maps as float32
 PyTorch under autograd.  Deep and swiglu nets amplify the rounding of their
 scan operands: with bf16 operands the retention gradient of a swiglu net
 with two Jacobian steps moved by 1-6% of its largest entry under rounding
-perturbations alone, so these nets keep their streams in float32.
+perturbations alone, so these nets keep their streams in float32 (and their
+per-token maps run in float32 under PyTorch's default matmul precision:
+``torch.backends.cuda.matmul.allow_tf32`` left off).
 
 Reference (src/thetascan/_core/ops/engine.py): the write is
 ``_forward_theta0`` / ``_block_forward`` (:117-175, residual
