@@ -65,3 +65,29 @@ def test_sequential_shards_keep_exchanges_apart():
     assert first[0] is a0 and second[0] is b0
     with pytest.raises(ValueError):
         runner.shard(3)
+
+
+def test_float32_shard_views_cut_wide_payloads(monkeypatch):
+    """The float32 kernel-family path's sharded reads (``precise._views_fn``)
+    cut payloads wider than the float32 scan kernels take (256 columns with
+    the exchange's unit column) into pieces; around the oracle scan, the
+    pieces of a 300-column payload with the unit column equal the whole
+    sequence's read."""
+    from thetascan_b200 import precise
+    monkeypatch.setattr(precise, "linattn_views", oracle_views)
+    g = torch.Generator().manual_seed(3)
+    B, H, T, P = 1, 2, 64, 2
+    q, k = (torch.rand(B, H, T, 1, generator=g, dtype=torch.float64) for _ in range(2))
+    v = torch.randn(B, H, T, 300, generator=g, dtype=torch.float64)
+    la = -torch.rand(H, generator=g, dtype=torch.float64) * 0.1
+    rets, stale = (None, la), (False, True)
+    want = oracle_views(q, k, v, rets, append_unit=True, stale=stale)
+    runner = seqpar.SequentialShards(P)
+    L = T // P
+    parts = [precise._views_fn(runner.shard(p))(q[:, :, p * L:(p + 1) * L], k[:, :, p * L:(p + 1) * L],
+                                               v[:, :, p * L:(p + 1) * L], rets, append_unit=True, stale=stale)
+             for p in range(P)]
+    for i, w in enumerate(want):
+        got = torch.cat([pt[i] for pt in parts], dim=2)
+        assert got.shape == w.shape
+        assert (got - w).abs().max() / w.abs().max() < 1e-10
